@@ -1,0 +1,337 @@
+#!/usr/bin/env python
+"""Decode-throughput benchmark of the B200 decode-step layer (one JSON line on rank 0).
+
+Workload (N=1): the full 48-layer Qwen3-30B-A3B shape (hidden 2048, 32/4 heads, head_dim 128,
+128 experts top-8, expert FFN 768, vocab 151936) with synthetic N(0, 0.02) weights in a
+Q4_K_M stand-in mix, all resident in HBM; batch-1 greedy decode after an 8192-token prefill
+of uniform-random token ids into the f16 paged KV cache. A step = one decode token.
+
+  value      device tok/s: K graph-replayed decode steps timed with CUDA events
+  e2e        tok/s through bt_forward with host token in / host logits out every step
+  roofline   the expert FFN (gate/up + down kernels) against the measured HBM copy peak
+  cpu_baseline  the CPU oracle decoding from the same weights and cache on the host cores
+
+N>1 (torchrun): replicas -- every rank runs the same batch-1 decode on its own GPU (weak
+scaling; no collective on the batch-1 path); rank 0 reports the sum of tok/s with the step
+time taken as the max over ranks.
+
+--impl reference: the reference's CPU implementation of the path is not buildable here (Rust,
+no toolchain; ggml absent), so this arm times the CPU oracle restatement (`kind: "port"`) on
+the same config with all host threads.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s (bs1, bs64) Qwen3-30B-A3B shape; expert-GEMV HBM GB/s vs peak"
+QWEN3_30B = dict(n_embd=2048, n_head=32, n_head_kv=4, head_dim=128, n_expert=128, n_expert_used=8, n_ff_exp=768,
+                 n_vocab=151936)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu: int):
+        self.gpu = gpu
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except OSError:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], [], set()
+        for ln in self.lines:
+            parts = [x.strip() for x in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"),
+                                 parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def expert_bytes(cfg):
+    """Algorithmic bytes of the expert FFN per token, averaged over layers: top-k experts x
+    (gate + up + down) in each layer's K-quant types."""
+    from bigtea_b200.gguf import tensor_nbytes
+
+    E, F, K = cfg.n_embd, cfg.n_ff_exp, cfg.n_expert_used
+    gu, dn = [], []
+    for t in cfg.layer_types:
+        gu.append(K * (tensor_nbytes(t[4], E * F) + tensor_nbytes(t[5], E * F)))
+        dn.append(K * tensor_nbytes(t[6], F * E))
+    return float(np.mean(gu)), float(np.mean(dn))
+
+
+def cpu_baseline_from_engine(engine, cache, cfg, ctx, n_tokens, threads, seed):
+    """Time the CPU oracle decoding n_tokens from the same weights (copied back from HBM)
+    and the same KV cache; the first token's logits are checked against the GPU's."""
+    from oracle import pyoracle as orc
+    import bigtea_b200 as bt
+    from bigtea_b200.gguf import tensor_nbytes
+
+    W = {}
+    for name, ty, ne, _ in cfg.tensor_specs():
+        n = 1
+        for d in ne:
+            n *= d
+        W[name] = (ty, ne, engine.tensor_bytes(name, tensor_nbytes(ty, n)))
+    model = orc.Model(cfg, W)
+    for il in range(cfg.n_layer):
+        k, v = cache.layer_bytes(il, 0, ctx)
+        model.write_kv_layer(il, k, v)
+    model.set_len(ctx)
+    orc.lib().or_set_threads(threads)
+    tok = int(np.random.default_rng(seed).integers(0, cfg.n_vocab))
+    t0 = time.perf_counter()
+    first = None
+    for i in range(n_tokens):
+        lg = model.forward([tok], model.len())
+        if first is None:
+            first = lg
+        tok = orc.argmax(lg)
+    dt = time.perf_counter() - t0
+    model.close()
+    return n_tokens / dt, first
+
+
+def run_ours(args, rank, world, local_rank):
+    import bigtea_b200 as bt
+
+    cfg = bt.config(args.config, max_positions=args.ctx + args.steps + args.warmup + args.steps // 4 + args.prof_steps + 64)
+    t_setup = time.perf_counter()
+    engine = bt.Engine.synthetic(cfg, seed=args.seed, device=local_rank)
+    cache = bt.KvCache(engine, max_positions=cfg.max_positions)
+    runner = bt.StreamingRunner(engine)
+    rng = np.random.default_rng(args.seed + 1)
+    prompt = rng.integers(0, cfg.n_vocab, args.ctx)
+    t0 = time.perf_counter()
+    logits = runner.forward_cached(cache, prompt, 0)
+    prefill_s = time.perf_counter() - t0
+    tok = int(np.argmax(logits))
+    # warm-up (also captures the step graph), then K timed graph replays
+    runner.generate_greedy(cache, [tok], args.warmup)
+    sync_ranks(world)
+    with ClockSampler(local_rank) as clk:
+        toks = runner.generate_greedy(cache, [tok], args.steps)
+        dev_ms = runner.last_device_ms()
+    ms = max_over_ranks(dev_ms, world)
+    value = world * args.steps / (ms / 1e3)
+
+    # e2e: bt_forward with a host token in and host logits out every step
+    e2e_steps = max(4, args.steps // 4)
+    sync_ranks(world)
+    t0 = time.perf_counter()
+    nxt = int(toks[-1, 0])
+    for _ in range(e2e_steps):
+        lg = runner.forward_cached(cache, [nxt], cache.len())
+        nxt = int(np.argmax(lg))
+    e2e_s = max_over_ranks(time.perf_counter() - t0, world)
+    e2e = world * e2e_steps / e2e_s
+
+    # per-kernel device times (serialised launches) for the roofline
+    prof = runner.profile_decode(cache, [nxt], args.prof_steps)
+    gu_bytes, dn_bytes = expert_bytes(cfg)
+    gu = prof.get("expert_gateup", (1, 0.0))
+    dn = prof.get("expert_down", (1, 0.0))
+    exp_ms = gu[1] / max(gu[0], 1) + dn[1] / max(dn[0], 1)
+    achieved = (gu_bytes + dn_bytes) / (exp_ms / 1e3) / 1e9 if exp_ms > 0 else None
+    peak, peak_kind = peaks()
+    per_step_launches = 1 + cfg.n_layer * 7 + 1 + 1
+
+    result = None
+    if rank == 0:
+        cpu = None
+        if not args.no_cpu:
+            threads = os.cpu_count() or 1
+            ctx_now = cache.len()
+            cpu_tps, _ = cpu_baseline_from_engine(engine, cache, cfg, args.ctx, args.cpu_tokens, threads, args.seed)
+            cpu = {"value": round(cpu_tps, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                   "sample": f"{args.cpu_tokens} greedy decode tokens of the same 48-layer model from the same "
+                             f"ctx-{args.ctx} KV cache (weights and cache copied back from HBM)"}
+            del ctx_now
+        kernel_table = {k: {"launches": v[0], "avg_us": round(1e3 * v[1] / max(v[0], 1), 2)} for k, v in prof.items()}
+        result = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4_K/q6_K weights, int8 dot, f32 accumulate",
+            "data": "synthetic (seeded N(0,0.02) weights, uniform-random token ids)",
+            "config": {"workload": f"{args.config}: Qwen3-30B-A3B shape, 48 layers, Q4_K_M stand-in, batch 1 "
+                                   f"greedy decode after a {args.ctx}-token prefill",
+                       "batch": 1, "context": args.ctx, "parallelism": "replicas" if world > 1 else "single GPU",
+                       "l2": "inputs larger than L2 (17 GB of weights per step)",
+                       "prefill_seconds": round(prefill_s, 2), "setup_seconds": round(time.perf_counter() - t_setup, 1)},
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * 7 + 1,
+                    "d2h_bytes_per_step": 4 * cfg.n_vocab + 4},
+            "gpu_launches": per_step_launches * args.steps,
+            "roofline": {"bound": "hbm", "kernel": "expert FFN (gate/up + down)",
+                         "achieved": round(achieved, 1) if achieved else None, "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4) if achieved else None, "peak_kind": peak_kind,
+                         "bytes_per_token_layer": gu_bytes + dn_bytes, "traffic": None},
+            "kernels_us": kernel_table,
+            "clocks": clk.summary(),
+            "cpu_baseline": cpu,
+        }
+    cache.close()
+    engine.close()
+    return result
+
+
+def run_reference(args, rank, world):
+    """The CPU restatement of the reference's decode path on the host cores, same config."""
+    if rank != 0:
+        return None
+    import bigtea_b200 as bt
+    from oracle import pyoracle as orc
+
+    cfg = bt.config(args.config, max_positions=args.ctx + args.steps + args.warmup + 8)
+    threads = os.cpu_count() or 1
+    W = bt.synth_model(cfg, seed=args.seed)
+    model = orc.Model(cfg, W)
+    # the decode cost does not depend on the cache contents: seeded f16 values stand in for
+    # the prefilled context
+    rng = np.random.default_rng(args.seed)
+    kw = cfg.n_head_kv * cfg.head_dim
+    for il in range(cfg.n_layer):
+        k = rng.standard_normal(args.ctx * kw).astype(np.float16)
+        v = rng.standard_normal(args.ctx * kw).astype(np.float16)
+        model.write_kv_layer(il, k, v)
+    model.set_len(args.ctx)
+    orc.lib().or_set_threads(threads)
+    tok = 1
+    for _ in range(args.warmup):
+        tok = orc.argmax(model.forward([tok], model.len()))
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        tok = orc.argmax(model.forward([tok], model.len()))
+    dt = time.perf_counter() - t0
+    tps = args.steps / dt
+    return {
+        "impl": "reference", "metric": METRIC, "value": round(tps, 3), "unit": "tok/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 2),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "q4_K/q6_K weights, int8 dot, f32 accumulate", "data": "synthetic",
+        "config": {"workload": f"{args.config}: Qwen3-30B-A3B shape, 48 layers, Q4_K_M stand-in, batch 1 greedy "
+                               f"decode at context {args.ctx}", "batch": 1, "context": args.ctx},
+        "cpu_baseline": {"value": round(tps, 3), "unit": "tok/s", "cores": threads, "kind": "port",
+                         "sample": f"{args.steps} decode tokens at context {args.ctx} (seeded f16 cache)"},
+        "e2e": {"value": round(tps, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+_dist = None
+
+
+def sync_ranks(world):
+    if world > 1:
+        import torch
+
+        torch.cuda.synchronize()
+        _dist.barrier()
+
+
+def max_over_ranks(x, world):
+    if world == 1:
+        return x
+    import torch
+
+    t = torch.tensor([float(x)], device="cuda")
+    _dist.all_reduce(t, op=_dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="cfg1")
+    ap.add_argument("--ctx", type=int, default=8192)
+    ap.add_argument("--seed", type=int, default=1234)
+    ap.add_argument("--prof-steps", type=int, default=4)
+    ap.add_argument("--cpu-tokens", type=int, default=3)
+    ap.add_argument("--no-cpu", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    global _dist
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600))
+        _dist = dist
+    if args.impl == "reference":
+        out = run_reference(args, rank, world)
+    else:
+        out = run_ours(args, rank, world, local_rank)
+    if world > 1:
+        _dist.barrier()
+        _dist.destroy_process_group()
+    if rank == 0 and out is not None:
+        print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,155 @@
+// bt_common.cuh -- arithmetic contract helpers and sm_100a PTX wrappers shared by the kernels.
+//
+// The arithmetic contract (exactly what the CPU oracle restates; every op is IEEE-754
+// binary32 round-to-nearest-even; the library is compiled with --fmad=false so a product
+// and a sum are never fused unless written as fmaf):
+//   C1 f32->f16 RNE (__float2half_rn); f16->f32 exact.
+//   C2 Q4_K value = (d*sc)*q - (dmin*m); Q6_K value = (d*sc)*q.
+//   C3 Q8_K activation: first signed max by |x|, iscale = -127/max, q = min(127, rint(iscale*x)),
+//      d = 1/iscale, bsums over 16.
+//   C4 K-quant row dot: exact int32 per superblock, then one float combination per superblock,
+//      summed in superblock order from 0.
+//   C5 P2: 32 lanes, lane l takes elements l, l+32, ... in order, xor butterfly 16,8,4,2,1.
+//   C6 RMSNorm y = (x * (1/sqrt(P2(x*x)/n + eps))) * w.
+//   C7 bt_exp: Cody-Waite ln2 reduction + degree-7 Taylor polynomial in Horner/fmaf form.
+//   C8 attention: chunks of 256 keys, per-chunk max/exp/sum/PV, chunks combined in order.
+//   C9 RoPE NeoX with a host-computed cos/sin table.
+#pragma once
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace bt {
+
+constexpr int WARP = 32;
+constexpr unsigned FULL = 0xffffffffu;
+
+// error bits a kernel ORs into the engine's device error word
+enum : int { ERR_WAIT_TIMEOUT = 1, ERR_BAD_INDEX = 2 };
+
+// ~1 s at the B200's 1.9 GHz SM clock: every spin on an mbarrier gives up after this
+constexpr long long WAIT_LIMIT_CYCLES = 2000000000LL;
+
+__device__ __forceinline__ float f16_round(float x) { return __half2float(__float2half_rn(x)); }
+
+__device__ __forceinline__ float pow2i(int n) { return __int_as_float((n + 127) << 23); }
+
+// C7. The same operation sequence as or_exp in the oracle.
+__device__ __forceinline__ float bt_exp(float x) {
+    if (!(x < 88.72283935546875f)) return (x != x) ? x : __int_as_float(0x7f800000);
+    if (x < -103.972084045410156f) return 0.0f;
+    float n = rintf(__fmul_rn(x, 1.44269502162933349609375f));
+    float r = fmaf(n, -0.693145751953125f, x);
+    r = fmaf(n, -1.428606765330187045e-06f, r);
+    float p = 1.98412698e-4f;
+    p = fmaf(p, r, 1.38888889e-3f);
+    p = fmaf(p, r, 8.33333333e-3f);
+    p = fmaf(p, r, 4.16666667e-2f);
+    p = fmaf(p, r, 1.66666667e-1f);
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    int ni = (int)n;
+    if (ni > 127) return __fmul_rn(__fmul_rn(p, pow2i(127)), pow2i(ni - 127));
+    if (ni < -126) return __fmul_rn(__fmul_rn(p, pow2i(ni + 64)), pow2i(-64));
+    return __fmul_rn(p, pow2i(ni));
+}
+
+__device__ __forceinline__ float bt_silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, bt_exp(-x))); }
+
+// f32::total_cmp as a signed integer key (core/arch/src/sample.rs:928-935 orders by it)
+__device__ __forceinline__ int total_key(float f) {
+    int b = __float_as_int(f);
+    return b ^ (int)(((unsigned)(b >> 31)) >> 1);
+}
+
+__device__ __forceinline__ float butterfly_sum(float v) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(FULL, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v = fmaxf(v, __shfl_xor_sync(FULL, v, o));
+    return v;
+}
+
+__device__ __forceinline__ int warp_sum_int(int v) {
+#pragma unroll
+    for (int o = 16; o >= 1; o >>= 1) v += __shfl_xor_sync(FULL, v, o);
+    return v;
+}
+
+// ---------------------------------------------------------------- PTX: PDL
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// ---------------------------------------------------------------- PTX: mbarrier + bulk copies
+__device__ __forceinline__ uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void fence_proxy_async() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Bounded wait: returns false (and sets ERR_WAIT_TIMEOUT) if the phase does not complete
+// within WAIT_LIMIT_CYCLES.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    long long t0 = clock64();
+    while (!mbar_try_wait(bar, parity)) {
+        if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+            if (err) atomicOr(err, ERR_WAIT_TIMEOUT);
+            return false;
+        }
+    }
+    return true;
+}
+
+// 1-D bulk copy global -> shared (TMA, no tensor map). dst/src 16-byte aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            smem_u32(dst)),
+        "l"(src), "r"(bytes), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 2-D tiled tensor copy global -> shared through a CUtensorMap (TMA). No multicast.
+__device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_u32(dst)),
+        "l"(tmap), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const void *tmap) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+}  // namespace bt

@@ -1,0 +1,1509 @@
+// engine.cu -- host runtime and C ABI of the decode-step layer (include/bigtea_decode.h).
+//
+// The engine owns the HBM-resident weights (GGUF bytes rearranged into the tiled layout of
+// kquant.cuh), the RoPE table, the per-step scratch and the CUDA graphs of the greedy loop.
+// bt_kv is the paged f16 KV pool. Reference interfaces: StreamingRunner::new / load_resident /
+// forward_cached (core/arch/src/stream.rs:586, 1793, 1933) and KvCache (core/arch/src/kv.rs).
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <string.h>
+
+#include <chrono>
+#include <map>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "../../include/bigtea_decode.h"
+#include "bt_common.cuh"
+#include "kernels.cuh"
+
+using namespace bt;
+
+// ------------------------------------------------------------------ errors
+static thread_local std::string g_err;
+static int fail(int code, const std::string &msg) {
+    g_err = msg;
+    return code;
+}
+#define CK(call)                                                                              \
+    do {                                                                                      \
+        cudaError_t e_ = (call);                                                              \
+        if (e_ != cudaSuccess) return fail(BT_ERR_CUDA, std::string(#call) + ": " + cudaGetErrorString(e_)); \
+    } while (0)
+
+extern "C" const char *bt_last_error(void) { return g_err.c_str(); }
+extern "C" int bt_abi_version(void) { return BT_ABI_VERSION; }
+
+// ------------------------------------------------------------------ device buffers
+struct DevBuf {
+    void *p = nullptr;
+    size_t n = 0;
+    DevBuf() = default;
+    DevBuf(const DevBuf &) = delete;
+    DevBuf &operator=(const DevBuf &) = delete;
+    DevBuf(DevBuf &&o) noexcept : p(o.p), n(o.n) {
+        o.p = nullptr;
+        o.n = 0;
+    }
+    DevBuf &operator=(DevBuf &&o) noexcept {
+        if (this != &o) {
+            if (p) cudaFree(p);
+            p = o.p;
+            n = o.n;
+            o.p = nullptr;
+            o.n = 0;
+        }
+        return *this;
+    }
+    ~DevBuf() {
+        if (p) cudaFree(p);
+    }
+    cudaError_t alloc(size_t bytes) {
+        if (p) cudaFree(p);
+        p = nullptr;
+        n = bytes;
+        return cudaMalloc(&p, bytes ? bytes : 16);
+    }
+    template <typename T> T *as() const { return reinterpret_cast<T *>(p); }
+};
+
+// A quantised matrix (or stack of per-expert matrices) in the tiled layout.
+struct QMat {
+    DevBuf buf;
+    DevBuf raw;  // GGUF bytes, kept only where a row gather needs them (token_embd)
+    int type = -1;
+    long long rows = 0, cols = 0, n_mats = 1;
+    TileGeom g{};
+    long long mat_bytes = 0;  // bytes of one expert's matrix
+};
+
+struct Layer {
+    DevBuf attn_norm, q_norm, k_norm, ffn_norm, gate_inp;
+    QMat q, k, v, o, gate, up, down;
+};
+
+struct GraphKey {
+    const void *kv;
+    std::vector<uint32_t> seqs;
+    bool operator<(const GraphKey &o) const { return kv != o.kv ? kv < o.kv : seqs < o.seqs; }
+};
+
+struct KernelTimer {
+    std::string name;
+    uint64_t launches = 0;
+    double ms = 0;
+};
+
+struct bt_engine {
+    bt_model_desc d{};
+    int device = 0;
+    int n_sm = 148;
+    cudaStream_t st = nullptr;
+    std::vector<Layer> L;
+    QMat embd, out;
+    DevBuf out_norm, rope;
+    // per-step scratch, sized for TB tokens and max_seqs outputs
+    int TB = 64;
+    int max_out = 0;
+    DevBuf x, ffn_in, fn, qkv, qbuf, att, rlog, rcnt, sel_ids, sel_w, act, part, acnt;
+    DevBuf dbg_ids, dbg_w;  // [n_layer][TB][K]
+    DevBuf tokens, seq_of, local_idx, pos_of, single, x_rows;
+    DevBuf st_seq, st_ntok, st_lrow, next_tok, gen_out, gen_count, logits;
+    DevBuf err;
+    int part_chunks = 0;
+    size_t gen_cap = 0;
+    uint64_t weight_bytes = 0;
+    bt_stats stats{};
+    std::map<GraphKey, cudaGraphExec_t> graphs;
+    cudaGraph_t graph_objs[64] = {};
+    int last_T = 0;
+    // profiling
+    bool timing = false;
+    std::map<std::string, KernelTimer> timers;
+    std::vector<std::pair<cudaEvent_t, cudaEvent_t>> ev_pool;
+    std::vector<std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>> ev_used;
+    double last_device_ms = 0;
+    bool pdl = true;
+};
+
+struct bt_kv {
+    bt_engine *e = nullptr;
+    uint32_t max_seqs = 0, max_positions = 0, block_tokens = 16;
+    int n_blocks = 0, max_blocks = 0;
+    DevBuf pool;                       // [n_layer][n_blocks][2][HK][16][D] f16
+    DevBuf bt_dev;                     // [max_seqs][max_blocks] int32
+    DevBuf dev_len;                    // [max_seqs] int32
+    DevBuf tmp;                        // export/import/shift staging
+    std::vector<int> table;            // host mirror of the block table
+    std::vector<int> free_blocks;
+    std::vector<std::vector<int>> pages;
+    std::vector<uint32_t> len;         // host mirror of the lengths
+    std::vector<std::vector<uint32_t>> layer_pos;  // positions held per layer (is_consistent)
+    CUtensorMap tmap;
+    bool table_dirty = true;
+};
+
+// ------------------------------------------------------------------ driver entry point for TMA maps
+typedef CUresult (*EncodeTiledFn)(CUtensorMap *, CUtensorMapDataType, cuuint32_t, void *, const cuuint64_t *,
+                                  const cuuint64_t *, const cuuint32_t *, const cuuint32_t *, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+static EncodeTiledFn get_encode_fn() {
+    static EncodeTiledFn fn = nullptr;
+    if (!fn) {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<EncodeTiledFn>(p);
+    }
+    return fn;
+}
+
+// ------------------------------------------------------------------ helpers
+static int pick_nst(size_t slot_bytes, size_t fixed_bytes) {
+    const size_t cap = 227 * 1024;
+    int nst = 4;
+    while (nst > 1 && fixed_bytes + (size_t)GEMV_WARPS * nst * slot_bytes > cap) nst--;
+    return nst;
+}
+
+static int grid_for(const bt_engine *e, long long units) {
+    long long g = units < e->n_sm ? units : e->n_sm;
+    return (int)(g < 1 ? 1 : g);
+}
+
+static void rope_table(const bt_model_desc &d, std::vector<float> &cs) {
+    // ggml_rope_cache_init's recurrence for NeoX with freq_scale 1, ext_factor 0, attn_factor 1
+    // (core/ggml/src/graph.rs:542-562 fixes those parameters for qwen3moe).
+    int n_rot = (int)d.n_rot;
+    cs.resize((size_t)d.max_positions * n_rot);
+    float theta_scale = powf(d.rope_freq_base, -2.0f / (float)n_rot);
+    for (uint32_t p = 0; p < d.max_positions; p++) {
+        float theta = (float)p;
+        float *row = cs.data() + (size_t)p * n_rot;
+        for (int i = 0; i < n_rot / 2; i++) {
+            row[2 * i] = cosf(theta);
+            row[2 * i + 1] = sinf(theta);
+            theta *= theta_scale;
+        }
+    }
+}
+
+static bool is_norm_name(const std::string &n) {
+    return n.find("_norm.weight") != std::string::npos;
+}
+
+// Upload one tensor (host or device source) into its resident form.
+static int ingest_qmat(bt_engine *e, QMat &m, int type, long long rows, long long cols, long long n_mats,
+                       const void *src, bool src_device, int rpt, bool keep_raw, DevBuf &staging) {
+    if (type != T_Q4_K && type != T_Q6_K)
+        return fail(BT_ERR_UNSUPPORTED, "quantised matrices must be Q4_K or Q6_K (got type " + std::to_string(type) + ")");
+    if (cols % 256) return fail(BT_ERR_UNSUPPORTED, "row length must be a multiple of 256");
+    if (cols / 256 > 32) return fail(BT_ERR_UNSUPPORTED, "rows longer than 8192 values are not supported");
+    m.type = type;
+    m.rows = rows;
+    m.cols = cols;
+    m.n_mats = n_mats;
+    m.g = tile_geom(type, rows, cols, rpt);
+    m.mat_bytes = m.g.n_tiles * (long long)m.g.tile_bytes;
+    size_t raw_bytes = (size_t)n_mats * rows * (cols / 256) * qk_block_bytes(type);
+    const uint8_t *dsrc = reinterpret_cast<const uint8_t *>(src);
+    if (!src_device) {
+        if (staging.n < raw_bytes) CK(staging.alloc(raw_bytes));
+        CK(cudaMemcpyAsync(staging.p, src, raw_bytes, cudaMemcpyHostToDevice, e->st));
+        dsrc = staging.as<uint8_t>();
+    }
+    CK(m.buf.alloc((size_t)m.mat_bytes * n_mats));
+    CK(launch_repack(type, dsrc, rows, cols, rpt, m.buf.as<uint8_t>(), n_mats, e->st));
+    if (keep_raw) {
+        CK(m.raw.alloc(raw_bytes));
+        CK(cudaMemcpyAsync(m.raw.p, dsrc, raw_bytes, cudaMemcpyDeviceToDevice, e->st));
+    }
+    CK(cudaStreamSynchronize(e->st));
+    e->weight_bytes += raw_bytes;
+    return BT_OK;
+}
+
+static int ingest_f32(bt_engine *e, DevBuf &b, const void *src, bool src_device, size_t n) {
+    CK(b.alloc(n * 4));
+    CK(cudaMemcpyAsync(b.p, src, n * 4, src_device ? cudaMemcpyDeviceToDevice : cudaMemcpyHostToDevice, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    e->weight_bytes += n * 4;
+    return BT_OK;
+}
+
+struct SrcTensor {
+    int type;
+    uint64_t ne[4];
+    int n_dims;
+    const void *data;
+    bool device;
+    uint64_t nbytes;
+};
+
+static uint64_t expected_bytes(int type, uint64_t n) {
+    switch (type) {
+    case T_F32: return n * 4;
+    case T_F16: return n * 2;
+    case T_Q4_K: return n / 256 * 144;
+    case T_Q6_K: return n / 256 * 210;
+    default: return 0;
+    }
+}
+
+static int validate_desc(const bt_model_desc *d) {
+    if (!d) return fail(BT_ERR_INVALID, "null model description");
+    if (d->n_layer == 0 || d->n_embd == 0 || d->n_head == 0 || d->n_head_kv == 0 || d->n_expert == 0 ||
+        d->n_expert_used == 0 || d->n_ff_exp == 0 || d->n_vocab == 0 || d->max_positions == 0)
+        return fail(BT_ERR_INVALID, "model description has a zero dimension");
+    if (d->head_dim != 128) return fail(BT_ERR_UNSUPPORTED, "head_dim must be 128");
+    if (d->n_rot != d->head_dim) return fail(BT_ERR_UNSUPPORTED, "partial rotary embeddings are not supported");
+    if (d->n_head % d->n_head_kv || (d->n_head / d->n_head_kv) > 8 || ((d->n_head / d->n_head_kv) & 1))
+        return fail(BT_ERR_UNSUPPORTED, "GQA group must be 2, 4, 6 or 8 query heads per KV head");
+    if (d->n_expert_used > (uint32_t)MAX_K || d->n_expert_used > d->n_expert)
+        return fail(BT_ERR_UNSUPPORTED, "n_expert_used must be at most 16 and at most n_expert");
+    if (d->n_expert > 512) return fail(BT_ERR_UNSUPPORTED, "n_expert must be at most 512");
+    if (d->n_embd % 256 || d->n_ff_exp % 256 || (d->n_head * d->head_dim) % 256)
+        return fail(BT_ERR_UNSUPPORTED, "n_embd, n_ff_exp and n_head*head_dim must be multiples of 256");
+    return BT_OK;
+}
+
+static int alloc_scratch(bt_engine *e) {
+    const bt_model_desc &d = e->d;
+    const int TB = e->TB, E = d.n_embd, QW = d.n_head * d.head_dim, KW = d.n_head_kv * d.head_dim;
+    const int K = d.n_expert_used, NE = d.n_expert, F = d.n_ff_exp, G = d.n_head / d.n_head_kv;
+    e->part_chunks = (int)((d.max_positions + ATTN_CHUNK - 1) / ATTN_CHUNK);
+    e->max_out = 256;
+    CK(e->x.alloc((size_t)TB * E * 4));
+    CK(e->ffn_in.alloc((size_t)TB * E * 4));
+    CK(e->fn.alloc((size_t)TB * E * 4));
+    CK(e->qkv.alloc((size_t)TB * (QW + 2 * KW) * 4));
+    CK(e->qbuf.alloc((size_t)TB * QW * 4));
+    CK(e->att.alloc((size_t)TB * QW * 4));
+    CK(e->rlog.alloc((size_t)TB * NE * 4));
+    CK(e->rcnt.alloc((size_t)TB * 4));
+    CK(cudaMemset(e->rcnt.p, 0, (size_t)TB * 4));
+    CK(e->sel_ids.alloc((size_t)TB * K * 4));
+    CK(e->sel_w.alloc((size_t)TB * K * 4));
+    CK(e->act.alloc((size_t)TB * K * F * 4));
+    CK(e->part.alloc((size_t)TB * d.n_head_kv * e->part_chunks * G * (d.head_dim + 2) * 4));
+    CK(e->acnt.alloc((size_t)TB * d.n_head_kv * 4));
+    CK(cudaMemset(e->acnt.p, 0, (size_t)TB * d.n_head_kv * 4));
+    CK(e->dbg_ids.alloc((size_t)d.n_layer * TB * K * 4));
+    CK(e->dbg_w.alloc((size_t)d.n_layer * TB * K * 4));
+    CK(e->tokens.alloc((size_t)TB * 4));
+    CK(e->seq_of.alloc((size_t)TB * 4));
+    CK(e->local_idx.alloc((size_t)TB * 4));
+    CK(e->pos_of.alloc((size_t)TB * 4));
+    CK(e->single.alloc((size_t)TB));
+    CK(e->x_rows.alloc((size_t)e->max_out * 4));
+    CK(e->st_seq.alloc((size_t)e->max_out * 4));
+    CK(e->st_ntok.alloc((size_t)e->max_out * 4));
+    CK(e->st_lrow.alloc((size_t)e->max_out * 4));
+    CK(e->next_tok.alloc((size_t)e->max_out * 4));
+    CK(e->gen_count.alloc((size_t)e->max_out * 4));
+    CK(e->logits.alloc((size_t)e->max_out * d.n_vocab * 4));
+    CK(e->err.alloc(4));
+    CK(cudaMemset(e->err.p, 0, 4));
+    return BT_OK;
+}
+
+static int finish_create(bt_engine *e) {
+    std::vector<float> cs;
+    rope_table(e->d, cs);
+    CK(e->rope.alloc(cs.size() * 4));
+    CK(cudaMemcpy(e->rope.p, cs.data(), cs.size() * 4, cudaMemcpyHostToDevice));
+    int r = alloc_scratch(e);
+    if (r) return r;
+    e->stats.weight_bytes = e->weight_bytes;
+    return BT_OK;
+}
+
+static int find_src(const std::map<std::string, SrcTensor> &m, const std::string &n, const SrcTensor **out) {
+    auto it = m.find(n);
+    if (it == m.end()) return fail(BT_ERR_MISSING_TENSOR, "missing tensor " + n);
+    *out = &it->second;
+    return BT_OK;
+}
+
+static int check_shape(const std::string &n, const SrcTensor *t, std::initializer_list<uint64_t> want) {
+    uint64_t n_el = 1;
+    int i = 0;
+    for (uint64_t w : want) {
+        if (i >= 4 || t->ne[i] != w)
+            return fail(BT_ERR_INVALID, "tensor " + n + " has an unexpected shape (dim " + std::to_string(i) + ")");
+        n_el *= w;
+        i++;
+    }
+    for (; i < 4; i++)
+        if (t->ne[i] > 1) return fail(BT_ERR_INVALID, "tensor " + n + " has extra dimensions");
+    uint64_t eb = expected_bytes(t->type, n_el);
+    if (eb == 0) return fail(BT_ERR_UNSUPPORTED, "tensor " + n + " has unsupported type " + std::to_string(t->type));
+    if (t->nbytes && t->nbytes != eb) return fail(BT_ERR_INVALID, "tensor " + n + " byte size does not match its shape");
+    return BT_OK;
+}
+
+static int build_engine(bt_engine *e, const std::map<std::string, SrcTensor> &src) {
+    const bt_model_desc &d = e->d;
+    const uint64_t E = d.n_embd, QW = d.n_head * d.head_dim, KW = d.n_head_kv * d.head_dim;
+    const uint64_t NE = d.n_expert, F = d.n_ff_exp, V = d.n_vocab, D = d.head_dim;
+    DevBuf staging;
+    const SrcTensor *t;
+    int r;
+#define NEED(name, ...)                                  \
+    if ((r = find_src(src, name, &t))) return r;         \
+    if ((r = check_shape(name, t, {__VA_ARGS__}))) return r;
+    NEED("token_embd.weight", E, V);
+    if ((r = ingest_qmat(e, e->embd, t->type, V, E, 1, t->data, t->device, default_rpt(E), true, staging))) return r;
+    NEED("output_norm.weight", E);
+    if (t->type != T_F32) return fail(BT_ERR_UNSUPPORTED, "norm weights must be F32");
+    if ((r = ingest_f32(e, e->out_norm, t->data, t->device, E))) return r;
+    {
+        const SrcTensor *o = nullptr;
+        auto it = src.find("output.weight");
+        o = it == src.end() ? nullptr : &it->second;
+        if (!o) {
+            NEED("token_embd.weight", E, V);
+            o = t;  // tied output head (stream.rs:2892-2896)
+        } else if ((r = check_shape("output.weight", o, {E, V}))) {
+            return r;
+        }
+        if ((r = ingest_qmat(e, e->out, o->type, V, E, 1, o->data, o->device, default_rpt(E), false, staging)))
+            return r;
+    }
+    e->L.resize(d.n_layer);
+    for (uint32_t il = 0; il < d.n_layer; il++) {
+        Layer &l = e->L[il];
+        std::string p = "blk." + std::to_string(il) + ".";
+        auto f32 = [&](const char *suffix, DevBuf &b, uint64_t n) -> int {
+            std::string nm = p + suffix;
+            const SrcTensor *tt;
+            int rr;
+            if ((rr = find_src(src, nm, &tt))) return rr;
+            if ((rr = check_shape(nm, tt, {n}))) return rr;
+            if (tt->type != T_F32) return fail(BT_ERR_UNSUPPORTED, nm + " must be F32");
+            return ingest_f32(e, b, tt->data, tt->device, n);
+        };
+        auto mat = [&](const char *suffix, QMat &m, uint64_t cols, uint64_t rows, uint64_t nm_, int rpt) -> int {
+            std::string nm = p + suffix;
+            const SrcTensor *tt;
+            int rr;
+            if ((rr = find_src(src, nm, &tt))) return rr;
+            if (nm_ > 1) {
+                if ((rr = check_shape(nm, tt, {cols, rows, nm_}))) return rr;
+            } else if ((rr = check_shape(nm, tt, {cols, rows}))) {
+                return rr;
+            }
+            return ingest_qmat(e, m, tt->type, rows, cols, nm_, tt->data, tt->device, rpt, false, staging);
+        };
+        if ((r = f32("attn_norm.weight", l.attn_norm, E))) return r;
+        if ((r = f32("attn_q_norm.weight", l.q_norm, D))) return r;
+        if ((r = f32("attn_k_norm.weight", l.k_norm, D))) return r;
+        if ((r = f32("ffn_norm.weight", l.ffn_norm, E))) return r;
+        {
+            std::string nm = p + "ffn_gate_inp.weight";
+            const SrcTensor *tt;
+            if ((r = find_src(src, nm, &tt))) return r;
+            if ((r = check_shape(nm, tt, {E, NE}))) return r;
+            if (tt->type != T_F32) return fail(BT_ERR_UNSUPPORTED, nm + " must be F32");
+            if ((r = ingest_f32(e, l.gate_inp, tt->data, tt->device, E * NE))) return r;
+        }
+        if ((r = mat("attn_q.weight", l.q, E, QW, 1, default_rpt(E)))) return r;
+        if ((r = mat("attn_k.weight", l.k, E, KW, 1, default_rpt(E)))) return r;
+        if ((r = mat("attn_v.weight", l.v, E, KW, 1, default_rpt(E)))) return r;
+        if ((r = mat("attn_output.weight", l.o, QW, E, 1, default_rpt(QW)))) return r;
+        if ((r = mat("ffn_gate_exps.weight", l.gate, E, F, NE, default_rpt(E)))) return r;
+        if ((r = mat("ffn_up_exps.weight", l.up, E, F, NE, default_rpt(E)))) return r;
+        if ((r = mat("ffn_down_exps.weight", l.down, F, E, NE, 1))) return r;
+        if (l.gate.g.tile_bytes != l.up.g.tile_bytes && l.gate.type == l.up.type)
+            return fail(BT_ERR_INVALID, "gate and up experts disagree in shape");
+    }
+#undef NEED
+    return finish_create(e);
+}
+
+static int engine_init_device(bt_engine *e, int device) {
+    e->device = device;
+    CK(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, device));
+    if (prop.major < 10) return fail(BT_ERR_UNSUPPORTED, "this build targets sm_100a (B200)");
+    e->n_sm = prop.multiProcessorCount;
+    CK(init_kernel_attributes());
+    CK(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking));
+    return BT_OK;
+}
+
+extern "C" int bt_engine_create(const bt_model_desc *desc, const bt_tensor_view *tensors, size_t n_tensors, int device,
+                                bt_engine **out) {
+    if (!out) return fail(BT_ERR_INVALID, "null output handle");
+    *out = nullptr;
+    int r = validate_desc(desc);
+    if (r) return r;
+    std::unique_ptr<bt_engine> e(new bt_engine());
+    e->d = *desc;
+    if (e->d.expert_workers == 0) e->d.expert_workers = 4;
+    if ((r = engine_init_device(e.get(), device))) return r;
+    std::map<std::string, SrcTensor> src;
+    for (size_t i = 0; i < n_tensors; i++) {
+        const bt_tensor_view &tv = tensors[i];
+        if (!tv.name || !tv.data) return fail(BT_ERR_INVALID, "tensor view with a null name or data");
+        SrcTensor s{};
+        s.type = (int)tv.type;
+        for (int k = 0; k < 4; k++) s.ne[k] = k < (int)tv.n_dims ? tv.ne[k] : 1;
+        s.n_dims = (int)tv.n_dims;
+        s.data = tv.data;
+        s.device = false;
+        s.nbytes = tv.nbytes;
+        src[tv.name] = s;
+    }
+    if ((r = build_engine(e.get(), src))) {
+        std::string keep = g_err;
+        bt_engine_destroy(e.release());
+        g_err = keep;
+        return r;
+    }
+    *out = e.release();
+    return BT_OK;
+}
+
+extern "C" int bt_engine_create_synthetic(const bt_model_desc *desc, const uint32_t *types, uint32_t embd_type,
+                                          uint32_t out_type, uint64_t seed, float sigma, int device,
+                                          bt_engine **out) {
+    if (!out || !types) return fail(BT_ERR_INVALID, "null argument");
+    *out = nullptr;
+    int r = validate_desc(desc);
+    if (r) return r;
+    std::unique_ptr<bt_engine> e(new bt_engine());
+    e->d = *desc;
+    if (e->d.expert_workers == 0) e->d.expert_workers = 4;
+    if ((r = engine_init_device(e.get(), device))) return r;
+    const bt_model_desc &d = e->d;
+    const uint64_t E = d.n_embd, QW = d.n_head * d.head_dim, KW = d.n_head_kv * d.head_dim;
+    const uint64_t NE = d.n_expert, F = d.n_ff_exp, V = d.n_vocab, D = d.head_dim;
+    // Generate every tensor on the device (synth_kernel), keep the raw bytes alive until the
+    // engine has ingested them. One buffer per tensor: peak memory is the raw model once.
+    std::vector<std::unique_ptr<DevBuf>> raws;
+    std::map<std::string, SrcTensor> src;
+    auto gen = [&](const std::string &name, int type, std::vector<uint64_t> ne) -> int {
+        uint64_t n = 1;
+        for (auto v : ne) n *= v;
+        uint64_t bytes = expected_bytes(type, n);
+        if (!bytes) return fail(BT_ERR_UNSUPPORTED, "synthetic tensor " + name + " has unsupported type");
+        std::unique_ptr<DevBuf> b(new DevBuf());
+        CK(b->alloc(bytes));
+        float mean = is_norm_name(name) ? 1.0f : 0.0f;
+        CK(launch_synth(type, synth_key(seed, name_id(name.c_str())), (long long)n, mean, synth_scale(sigma),
+                        b->as<uint8_t>(), e->st));
+        SrcTensor s{};
+        s.type = type;
+        for (int k = 0; k < 4; k++) s.ne[k] = k < (int)ne.size() ? ne[k] : 1;
+        s.n_dims = (int)ne.size();
+        s.data = b->p;
+        s.device = true;
+        s.nbytes = bytes;
+        src[name] = s;
+        raws.push_back(std::move(b));
+        return BT_OK;
+    };
+    if ((r = gen("token_embd.weight", (int)embd_type, {E, V}))) return r;
+    if ((r = gen("output_norm.weight", T_F32, {E}))) return r;
+    if ((r = gen("output.weight", (int)out_type, {E, V}))) return r;
+    for (uint32_t il = 0; il < d.n_layer; il++) {
+        std::string p = "blk." + std::to_string(il) + ".";
+        const uint32_t *ty = types + 7 * il;
+        if ((r = gen(p + "attn_norm.weight", T_F32, {E}))) return r;
+        if ((r = gen(p + "attn_q.weight", (int)ty[0], {E, QW}))) return r;
+        if ((r = gen(p + "attn_k.weight", (int)ty[1], {E, KW}))) return r;
+        if ((r = gen(p + "attn_v.weight", (int)ty[2], {E, KW}))) return r;
+        if ((r = gen(p + "attn_q_norm.weight", T_F32, {D}))) return r;
+        if ((r = gen(p + "attn_k_norm.weight", T_F32, {D}))) return r;
+        if ((r = gen(p + "attn_output.weight", (int)ty[3], {QW, E}))) return r;
+        if ((r = gen(p + "ffn_norm.weight", T_F32, {E}))) return r;
+        if ((r = gen(p + "ffn_gate_inp.weight", T_F32, {E, NE}))) return r;
+        if ((r = gen(p + "ffn_gate_exps.weight", (int)ty[4], {E, F, NE}))) return r;
+        if ((r = gen(p + "ffn_up_exps.weight", (int)ty[5], {E, F, NE}))) return r;
+        if ((r = gen(p + "ffn_down_exps.weight", (int)ty[6], {F, E, NE}))) return r;
+        // ingest this layer right away so the raw copies do not pile up
+        if (il == 0) continue;
+    }
+    CK(cudaStreamSynchronize(e->st));
+    if ((r = build_engine(e.get(), src))) {
+        std::string keep = g_err;
+        bt_engine_destroy(e.release());
+        g_err = keep;
+        return r;
+    }
+    *out = e.release();
+    return BT_OK;
+}
+
+extern "C" void bt_engine_destroy(bt_engine *e) {
+    if (!e) return;
+    cudaSetDevice(e->device);
+    if (e->st) cudaStreamSynchronize(e->st);
+    for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    for (auto &p : e->ev_pool) {
+        cudaEventDestroy(p.first);
+        cudaEventDestroy(p.second);
+    }
+    for (auto &p : e->ev_used) {
+        cudaEventDestroy(p.second.first);
+        cudaEventDestroy(p.second.second);
+    }
+    e->L.clear();
+    if (e->st) cudaStreamDestroy(e->st);
+    delete e;
+}
+
+extern "C" int bt_engine_stats(const bt_engine *e, bt_stats *out) {
+    if (!e || !out) return fail(BT_ERR_INVALID, "null argument");
+    *out = e->stats;
+    return BT_OK;
+}
+
+// ------------------------------------------------------------------ KV pool
+static int kv_build_tmap(bt_kv *kv) {
+    const bt_model_desc &d = kv->e->d;
+    EncodeTiledFn enc = get_encode_fn();
+    if (!enc) return fail(BT_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+    cuuint64_t rows = (cuuint64_t)d.n_layer * kv->n_blocks * 2 * d.n_head_kv * 16;
+    if (rows >= (1ull << 32)) return fail(BT_ERR_UNSUPPORTED, "KV pool too large for one tensor map");
+    cuuint64_t dims[2] = {d.head_dim, rows};
+    cuuint64_t strides[1] = {(cuuint64_t)d.head_dim * 2};
+    cuuint32_t box[2] = {64, 16};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(&kv->tmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, kv->pool.p, dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(BT_ERR_CUDA, "cuTensorMapEncodeTiled failed: " + std::to_string((int)r));
+    return BT_OK;
+}
+
+extern "C" int bt_kv_create(bt_engine *e, uint32_t kind, uint32_t max_seqs, uint32_t max_positions,
+                            uint32_t block_tokens, bt_kv **out) {
+    if (!e || !out) return fail(BT_ERR_INVALID, "null argument");
+    *out = nullptr;
+    if (kind != BT_KV_F16) return fail(BT_ERR_UNSUPPORTED, "only the f16 KV cache is on the device path");
+    if (block_tokens != 16) return fail(BT_ERR_UNSUPPORTED, "pages hold 16 positions");
+    if (max_seqs == 0 || max_positions == 0) return fail(BT_ERR_INVALID, "empty KV pool");
+    if (max_positions > e->d.max_positions)
+        return fail(BT_ERR_INVALID, "max_positions exceeds the model's RoPE table");
+    if (max_seqs > (uint32_t)e->max_out) return fail(BT_ERR_UNSUPPORTED, "at most 256 sequences per pool");
+    CK(cudaSetDevice(e->device));
+    std::unique_ptr<bt_kv> kv(new bt_kv());
+    kv->e = e;
+    kv->max_seqs = max_seqs;
+    kv->max_positions = max_positions;
+    kv->max_blocks = (int)((max_positions + 15) / 16);
+    kv->n_blocks = kv->max_blocks * (int)max_seqs;
+    const bt_model_desc &d = e->d;
+    size_t pool = (size_t)d.n_layer * kv->n_blocks * 2 * d.n_head_kv * 16 * d.head_dim * 2;
+    if (kv->pool.alloc(pool) != cudaSuccess) return fail(BT_ERR_OOM, "KV pool allocation failed");
+    CK(cudaMemset(kv->pool.p, 0, pool));
+    CK(kv->bt_dev.alloc((size_t)max_seqs * kv->max_blocks * 4));
+    CK(kv->dev_len.alloc((size_t)max_seqs * 4));
+    CK(cudaMemset(kv->dev_len.p, 0, (size_t)max_seqs * 4));
+    kv->table.assign((size_t)max_seqs * kv->max_blocks, 0);
+    for (int b = kv->n_blocks - 1; b >= 0; b--) kv->free_blocks.push_back(b);
+    kv->len.assign(max_seqs, 0);
+    kv->layer_pos.assign(max_seqs, std::vector<uint32_t>(d.n_layer, 0));
+    kv->pages.assign(max_seqs, std::vector<int>());
+    int r = kv_build_tmap(kv.get());
+    if (r) return r;
+    *out = kv.release();
+    return BT_OK;
+}
+
+extern "C" void bt_kv_destroy(bt_kv *kv) {
+    if (!kv) return;
+    cudaSetDevice(kv->e->device);
+    cudaStreamSynchronize(kv->e->st);
+    for (auto it = kv->e->graphs.begin(); it != kv->e->graphs.end();) {
+        if (it->first.kv == kv) {
+            cudaGraphExecDestroy(it->second);
+            it = kv->e->graphs.erase(it);
+        } else {
+            ++it;
+        }
+    }
+    delete kv;
+}
+
+// Page bookkeeping: pages[seq] lists the pool blocks holding positions [16*i, 16*i+16).
+static int kv_reserve(bt_kv *kv, uint32_t seq, uint32_t n_positions) {
+    size_t need = (n_positions + 15) / 16;
+    if (need > (size_t)kv->max_blocks) return fail(BT_ERR_KV, "sequence would exceed max_positions");
+    auto &pg = kv->pages[seq];
+    while (pg.size() < need) {
+        if (kv->free_blocks.empty()) return fail(BT_ERR_OOM, "KV pool has no free pages");
+        int b = kv->free_blocks.back();
+        kv->free_blocks.pop_back();
+        kv->table[(size_t)seq * kv->max_blocks + pg.size()] = b;
+        pg.push_back(b);
+        kv->table_dirty = true;
+    }
+    return BT_OK;
+}
+
+static void kv_release_beyond(bt_kv *kv, uint32_t seq, uint32_t n_positions) {
+    size_t keep = (n_positions + 15) / 16;
+    auto &pg = kv->pages[seq];
+    while (pg.size() > keep) {
+        kv->free_blocks.push_back(pg.back());
+        kv->table[(size_t)seq * kv->max_blocks + pg.size() - 1] = 0;
+        pg.pop_back();
+        kv->table_dirty = true;
+    }
+}
+
+static int kv_sync(bt_kv *kv) {
+    if (kv->table_dirty) {
+        CK(cudaMemcpyAsync(kv->bt_dev.p, kv->table.data(), kv->table.size() * 4, cudaMemcpyHostToDevice, kv->e->st));
+        kv->table_dirty = false;
+    }
+    return BT_OK;
+}
+
+static int kv_set_len(bt_kv *kv, uint32_t seq, uint32_t n) {
+    kv->len[seq] = n;
+    int v = (int)n;
+    CK(cudaMemcpyAsync(kv->dev_len.as<int>() + seq, &v, 4, cudaMemcpyHostToDevice, kv->e->st));
+    CK(cudaStreamSynchronize(kv->e->st));
+    return BT_OK;
+}
+
+static int kv_check_seq(const bt_kv *kv, uint32_t seq) {
+    if (!kv) return fail(BT_ERR_INVALID, "null KV handle");
+    if (seq >= kv->max_seqs) return fail(BT_ERR_INVALID, "sequence id out of range");
+    return BT_OK;
+}
+
+extern "C" int bt_kv_len(const bt_kv *kv, uint32_t seq, uint32_t *len) {
+    int r = kv_check_seq(kv, seq);
+    if (r) return r;
+    if (!len) return fail(BT_ERR_INVALID, "null output");
+    *len = kv->len[seq];
+    return BT_OK;
+}
+
+extern "C" int bt_kv_bytes(const bt_kv *kv, uint64_t *bytes) {
+    if (!kv || !bytes) return fail(BT_ERR_INVALID, "null argument");
+    // bytes held, as KvCache::bytes counts them: positions * per-position bytes, k and v, all layers
+    const bt_model_desc &d = kv->e->d;
+    uint64_t total = 0;
+    for (uint32_t s = 0; s < kv->max_seqs; s++)
+        for (uint32_t l = 0; l < d.n_layer; l++) total += (uint64_t)kv->layer_pos[s][l] * d.n_head_kv * d.head_dim * 2 * 2;
+    *bytes = total;
+    return BT_OK;
+}
+
+extern "C" int bt_kv_is_consistent(const bt_kv *kv, uint32_t seq, int *consistent) {
+    int r = kv_check_seq(kv, seq);
+    if (r) return r;
+    if (!consistent) return fail(BT_ERR_INVALID, "null output");
+    int ok = 1;
+    for (uint32_t l = 0; l < kv->e->d.n_layer; l++) ok &= kv->layer_pos[seq][l] == kv->len[seq];
+    *consistent = ok;
+    return BT_OK;
+}
+
+extern "C" int bt_kv_clear(bt_kv *kv, uint32_t seq) {
+    int r = kv_check_seq(kv, seq);
+    if (r) return r;
+    kv_release_beyond(kv, seq, 0);
+    for (auto &c : kv->layer_pos[seq]) c = 0;
+    return kv_set_len(kv, seq, 0);
+}
+
+extern "C" int bt_kv_truncate(bt_kv *kv, uint32_t seq, uint32_t n) {
+    int r = kv_check_seq(kv, seq);
+    if (r) return r;
+    if (n >= kv->len[seq]) return BT_OK;  // truncate_to keeps everything when n >= len (kv.rs:280-283)
+    kv_release_beyond(kv, seq, n);
+    for (auto &c : kv->layer_pos[seq]) c = c < n ? c : n;
+    return kv_set_len(kv, seq, n);
+}
+
+extern "C" int bt_kv_set_positions(bt_kv *kv, uint32_t seq, uint32_t n) {
+    int r = kv_check_seq(kv, seq);
+    if (r) return r;
+    if (n > kv->max_positions) return fail(BT_ERR_KV, "positions exceed the pool's max_positions");
+    if ((r = kv_reserve(kv, seq, n))) return r;
+    if ((r = kv_sync(kv))) return r;
+    return kv_set_len(kv, seq, n);
+}
+
+static int kv_tmp(bt_kv *kv, size_t bytes) {
+    if (kv->tmp.n < bytes) CK(kv->tmp.alloc(bytes));
+    return BT_OK;
+}
+
+extern "C" int bt_kv_shift_out(bt_kv *kv, uint32_t seq, uint32_t keep, uint32_t drop) {
+    int r = kv_check_seq(kv, seq);
+    if (r) return r;
+    uint32_t n = kv->len[seq];
+    if (drop == 0 || keep >= n) return BT_OK;  // kv.rs:314-317
+    if (drop > n - keep) drop = n - keep;
+    const bt_model_desc &d = kv->e->d;
+    const uint32_t tail = n - keep - drop;
+    const size_t per = (size_t)d.n_head_kv * d.head_dim;
+    if ((r = kv_sync(kv))) return r;
+    if (tail) {
+        if ((r = kv_tmp(kv, tail * per * 2 * 2))) return r;
+        __half *kb = kv->tmp.as<__half>(), *vb = kb + tail * per;
+        const int *row = kv->bt_dev.as<int>() + (size_t)seq * kv->max_blocks;
+        for (uint32_t l = 0; l < d.n_layer; l++) {
+            CK(launch_kv_copy(kv->pool.as<__half>(), row, (int)l, kv->n_blocks, d.n_head_kv, d.head_dim, keep + drop,
+                              tail, kb, vb, 0, kv->e->st));
+            CK(launch_kv_copy(kv->pool.as<__half>(), row, (int)l, kv->n_blocks, d.n_head_kv, d.head_dim, keep, tail, kb,
+                              vb, 1, kv->e->st));
+        }
+    }
+    CK(cudaStreamSynchronize(kv->e->st));
+    kv_release_beyond(kv, seq, n - drop);
+    for (auto &c : kv->layer_pos[seq]) c = c > drop ? c - drop : 0;
+    return kv_set_len(kv, seq, n - drop);
+}
+
+extern "C" int bt_kv_export_layer(const bt_kv *kvc, uint32_t seq, uint32_t layer, void *k_out, void *v_out,
+                                  uint64_t bytes) {
+    bt_kv *kv = const_cast<bt_kv *>(kvc);
+    int r = kv_check_seq(kv, seq);
+    if (r) return r;
+    const bt_model_desc &d = kv->e->d;
+    if (layer >= d.n_layer) return fail(BT_ERR_INVALID, "layer out of range");
+    const size_t step = (size_t)d.n_head_kv * d.head_dim * 2;
+    const uint32_t n = kv->layer_pos[seq][layer];
+    if (bytes != n * step) return fail(BT_ERR_KV, "export buffer must hold exactly the layer's positions");
+    if (!n) return BT_OK;
+    if (!k_out || !v_out) return fail(BT_ERR_INVALID, "null output buffer");
+    if ((r = kv_sync(kv))) return r;
+    if ((r = kv_tmp(kv, 2 * bytes))) return r;
+    __half *kb = kv->tmp.as<__half>(), *vb = kb + bytes / 2;
+    CK(launch_kv_copy(kv->pool.as<__half>(), kv->bt_dev.as<int>() + (size_t)seq * kv->max_blocks, (int)layer,
+                      kv->n_blocks, d.n_head_kv, d.head_dim, 0, (int)n, kb, vb, 0, kv->e->st));
+    CK(cudaMemcpyAsync(k_out, kb, bytes, cudaMemcpyDeviceToHost, kv->e->st));
+    CK(cudaMemcpyAsync(v_out, vb, bytes, cudaMemcpyDeviceToHost, kv->e->st));
+    CK(cudaStreamSynchronize(kv->e->st));
+    return BT_OK;
+}
+
+extern "C" int bt_kv_import_layer(bt_kv *kv, uint32_t seq, uint32_t layer, const void *k, const void *v,
+                                  uint64_t bytes) {
+    int r = kv_check_seq(kv, seq);
+    if (r) return r;
+    const bt_model_desc &d = kv->e->d;
+    const size_t step = (size_t)d.n_head_kv * d.head_dim * 2;
+    if (layer >= d.n_layer || bytes % step) return fail(BT_ERR_KV, "restore_layer needs whole positions");
+    const uint32_t n = (uint32_t)(bytes / step);
+    if (n > kv->max_positions) return fail(BT_ERR_KV, "restored layer exceeds max_positions");
+    if (n && (!k || !v)) return fail(BT_ERR_INVALID, "null input buffer");
+    uint32_t hold = n > kv->len[seq] ? n : kv->len[seq];
+    if ((r = kv_reserve(kv, seq, hold))) return r;
+    if ((r = kv_sync(kv))) return r;
+    if (n) {
+        if ((r = kv_tmp(kv, 2 * bytes))) return r;
+        __half *kb = kv->tmp.as<__half>(), *vb = kb + bytes / 2;
+        CK(cudaMemcpyAsync(kb, k, bytes, cudaMemcpyHostToDevice, kv->e->st));
+        CK(cudaMemcpyAsync(vb, v, bytes, cudaMemcpyHostToDevice, kv->e->st));
+        CK(launch_kv_copy(kv->pool.as<__half>(), kv->bt_dev.as<int>() + (size_t)seq * kv->max_blocks, (int)layer,
+                          kv->n_blocks, d.n_head_kv, d.head_dim, 0, (int)n, kb, vb, 1, kv->e->st));
+        CK(cudaStreamSynchronize(kv->e->st));
+    }
+    kv->layer_pos[seq][layer] = n;
+    return BT_OK;
+}
+
+// ------------------------------------------------------------------ one forward step
+struct StepPlan {
+    int T = 0;
+    std::vector<int> tokens, seq_of, local_idx;
+    std::vector<unsigned char> single;
+    std::vector<int> st_seq, st_ntok, st_lrow;
+    std::vector<int> x_rows;  // token index of each output row produced in this step
+    int out_first = 0;        // first output row
+};
+
+static void timer_begin(bt_engine *e, const char *name) {
+    if (!e->timing) return;
+    std::pair<cudaEvent_t, cudaEvent_t> ev;
+    if (!e->ev_pool.empty()) {
+        ev = e->ev_pool.back();
+        e->ev_pool.pop_back();
+    } else {
+        cudaEventCreate(&ev.first);
+        cudaEventCreate(&ev.second);
+    }
+    cudaEventRecord(ev.first, e->st);
+    e->ev_used.push_back({name, ev});
+}
+
+static void timer_end(bt_engine *e) {
+    if (!e->timing) return;
+    cudaEventRecord(e->ev_used.back().second.second, e->st);
+}
+
+static void timer_collect(bt_engine *e) {
+    for (auto &u : e->ev_used) {
+        float ms = 0;
+        cudaEventElapsedTime(&ms, u.second.first, u.second.second);
+        KernelTimer &k = e->timers[u.first];
+        k.name = u.first;
+        k.launches++;
+        k.ms += ms;
+        e->ev_pool.push_back(u.second);
+    }
+    e->ev_used.clear();
+}
+
+static GemvSeg make_seg(const QMat &m, int tile0, int out_off) {
+    GemvSeg s{};
+    s.w = m.buf.as<uint8_t>();
+    s.type = m.type;
+    s.nsb = m.g.nsb;
+    s.rpt = m.g.rpt;
+    s.S = m.g.S;
+    s.tile_bytes = m.g.tile_bytes;
+    s.rows = (int)m.rows;
+    s.n_tiles = (int)m.g.n_tiles;
+    s.tile0 = tile0;
+    s.out_off = out_off;
+    return s;
+}
+
+static cudaError_t run_gemv(bt_engine *e, const QMat *const *mats, const int *out_offs, int nseg, const float *x,
+                            long long x_stride, const int *x_rows, const float *norm_w, int K, int T, float *y,
+                            long long y_stride, const float *res, long long res_stride, const char *name) {
+    GemvArgs a{};
+    int tile0 = 0, slot = 0;
+    for (int i = 0; i < nseg; i++) {
+        a.seg[i] = make_seg(*mats[i], tile0, out_offs[i]);
+        tile0 += a.seg[i].n_tiles;
+        slot = a.seg[i].tile_bytes > slot ? a.seg[i].tile_bytes : slot;
+    }
+    a.nseg = nseg;
+    a.total_tiles = tile0;
+    a.x = x;
+    a.x_stride = x_stride;
+    a.x_rows = x_rows;
+    a.norm_w = norm_w;
+    a.eps = e->d.rms_eps;
+    a.K = K;
+    a.T = T;
+    a.y = y;
+    a.y_stride = y_stride;
+    a.res = res;
+    a.res_stride = res_stride;
+    a.err = e->err.as<int>();
+    a.slot_bytes = slot;
+    a.nst = 1;
+    size_t fixed = gemv_smem_bytes(a) - (size_t)GEMV_WARPS * slot;
+    a.nst = pick_nst(slot, fixed);
+    timer_begin(e, name);
+    cudaError_t r = launch_gemv(a, grid_for(e, tile0), e->st, e->pdl);
+    timer_end(e);
+    return r;
+}
+
+static int upload_plan(bt_engine *e, const StepPlan &p) {
+    cudaStream_t st = e->st;
+    CK(cudaMemcpyAsync(e->tokens.p, p.tokens.data(), p.T * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(e->seq_of.p, p.seq_of.data(), p.T * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(e->local_idx.p, p.local_idx.data(), p.T * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(e->single.p, p.single.data(), p.T, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(e->st_seq.p, p.st_seq.data(), p.st_seq.size() * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(e->st_ntok.p, p.st_ntok.data(), p.st_ntok.size() * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(e->st_lrow.p, p.st_lrow.data(), p.st_lrow.size() * 4, cudaMemcpyHostToDevice, st));
+    if (!p.x_rows.empty())
+        CK(cudaMemcpyAsync(e->x_rows.p, p.x_rows.data(), p.x_rows.size() * 4, cudaMemcpyHostToDevice, st));
+    // plan vectors are host locals of the caller: wait before they go out of scope
+    CK(cudaStreamSynchronize(st));
+    return BT_OK;
+}
+
+// All kernels of one step on e->st. Capturable: no host synchronisation inside.
+static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) {
+    const bt_model_desc &d = e->d;
+    const int T = p.T, E = d.n_embd, H = d.n_head, HK = d.n_head_kv, D = d.head_dim;
+    const int QW = H * D, KW = HK * D, K = d.n_expert_used, F = d.n_ff_exp, NE = d.n_expert;
+    const int G = H / HK;
+    cudaStream_t st = e->st;
+    const bool pdl = e->pdl;
+    int *err = e->err.as<int>();
+    {
+        EmbedArgs a{};
+        a.table = e->embd.raw.as<uint8_t>();
+        a.type = e->embd.type;
+        a.E = E;
+        a.V = d.n_vocab;
+        a.T = T;
+        a.tokens = e->tokens.as<int>();
+        a.seq_of = e->seq_of.as<int>();
+        a.local_idx = e->local_idx.as<int>();
+        a.dev_len = kv->dev_len.as<int>();
+        a.pos_of = e->pos_of.as<int>();
+        a.x = e->x.as<float>();
+        a.err = err;
+        timer_begin(e, "embed");
+        CK(launch_embed(a, st, pdl));
+        timer_end(e);
+    }
+    for (uint32_t il = 0; il < d.n_layer; il++) {
+        Layer &l = e->L[il];
+        for (int t0 = 0; t0 < T; t0 += MAX_T) {
+            int tg = T - t0 < MAX_T ? T - t0 : MAX_T;
+            const QMat *mats[3] = {&l.q, &l.k, &l.v};
+            int offs[3] = {0, QW, QW + KW};
+            CK(run_gemv(e, mats, offs, 3, e->x.as<float>() + (size_t)t0 * E, E, nullptr, l.attn_norm.as<float>(), E, tg,
+                        e->qkv.as<float>() + (size_t)t0 * (QW + 2 * KW), QW + 2 * KW, nullptr, 0, "qkv_gemv"));
+        }
+        {
+            QkvPostArgs a{};
+            a.qkv = e->qkv.as<float>();
+            a.qkv_stride = QW + 2 * KW;
+            a.q_norm = l.q_norm.as<float>();
+            a.k_norm = l.k_norm.as<float>();
+            a.eps = d.rms_eps;
+            a.rope = e->rope.as<float>();
+            a.n_rot = d.n_rot;
+            a.H = H;
+            a.HK = HK;
+            a.D = D;
+            a.T = T;
+            a.seq_of = e->seq_of.as<int>();
+            a.pos_of = e->pos_of.as<int>();
+            a.block_table = kv->bt_dev.as<int>();
+            a.max_blocks = kv->max_blocks;
+            a.layer = (int)il;
+            a.n_blocks = kv->n_blocks;
+            a.kv = kv->pool.as<__half>();
+            a.q_out = e->qbuf.as<float>();
+            timer_begin(e, "qkv_post");
+            CK(launch_qkv_post(a, st, pdl));
+            timer_end(e);
+        }
+        {
+            AttnArgs a{};
+            a.q = e->qbuf.as<float>();
+            a.H = H;
+            a.HK = HK;
+            a.D = D;
+            a.G = G;
+            a.T = T;
+            a.seq_of = e->seq_of.as<int>();
+            a.pos_of = e->pos_of.as<int>();
+            a.block_table = kv->bt_dev.as<int>();
+            a.max_blocks = kv->max_blocks;
+            a.layer = (int)il;
+            a.n_blocks = kv->n_blocks;
+            a.max_chunks = (int)((kv->max_positions + ATTN_CHUNK - 1) / ATTN_CHUNK);
+            a.scale = 1.0f / sqrtf((float)D);
+            a.part = e->part.as<float>();
+            a.cnt = e->acnt.as<int>();
+            a.out = e->att.as<float>();
+            a.err = err;
+            timer_begin(e, "attention");
+            CK(launch_attn(a, kv->tmap, st, pdl));
+            timer_end(e);
+        }
+        for (int t0 = 0; t0 < T; t0 += MAX_T) {
+            int tg = T - t0 < MAX_T ? T - t0 : MAX_T;
+            const QMat *mats[1] = {&l.o};
+            int offs[1] = {0};
+            CK(run_gemv(e, mats, offs, 1, e->att.as<float>() + (size_t)t0 * QW, QW, nullptr, nullptr, QW, tg,
+                        e->ffn_in.as<float>() + (size_t)t0 * E, E, e->x.as<float>() + (size_t)t0 * E, E, "attn_out_gemv"));
+        }
+        {
+            RouterArgs a{};
+            a.x = e->ffn_in.as<float>();
+            a.norm_w = l.ffn_norm.as<float>();
+            a.eps = d.rms_eps;
+            a.E = E;
+            a.Wr = l.gate_inp.as<float>();
+            a.NE = NE;
+            a.K = K;
+            a.T = T;
+            a.rows_per_cta = 8;
+            a.fn_out = e->fn.as<float>();
+            a.logits = e->rlog.as<float>();
+            a.cnt = e->rcnt.as<int>();
+            a.topk_ids = e->dbg_ids.as<int>() + (size_t)il * e->TB * K;
+            a.topk_w = e->dbg_w.as<float>() + (size_t)il * e->TB * K;
+            a.sel_ids = e->sel_ids.as<int>();
+            a.sel_w = e->sel_w.as<float>();
+            timer_begin(e, "router");
+            CK(launch_router(a, st, pdl));
+            timer_end(e);
+        }
+        for (int t0 = 0; t0 < T; t0 += MAX_T) {
+            int tg = T - t0 < MAX_T ? T - t0 : MAX_T;
+            ExpertArgs a{};
+            a.gate = l.gate.buf.as<uint8_t>();
+            a.up = l.up.buf.as<uint8_t>();
+            a.down = l.down.buf.as<uint8_t>();
+            a.gtype = l.gate.type;
+            a.utype = l.up.type;
+            a.dtype = l.down.type;
+            a.g_nsb = l.gate.g.nsb;
+            a.g_rpt = l.gate.g.rpt;
+            a.g_S = l.gate.g.S;
+            a.g_tile_bytes = l.gate.g.tile_bytes;
+            a.g_n_tiles = (int)l.gate.g.n_tiles;
+            a.u_tile_bytes = l.up.g.tile_bytes;
+            a.g_expert_bytes = l.gate.mat_bytes;
+            a.u_expert_bytes = l.up.mat_bytes;
+            a.d_expert_bytes = l.down.mat_bytes;
+            a.d_nsb = l.down.g.nsb;
+            a.d_tile_bytes = l.down.g.tile_bytes;
+            a.E = E;
+            a.F = F;
+            a.K = K;
+            a.T = tg;
+            a.workers = (int)d.expert_workers;
+            a.sel_ids = e->sel_ids.as<int>() + (size_t)t0 * K;
+            a.sel_w = e->sel_w.as<float>() + (size_t)t0 * K;
+            a.fn = e->fn.as<float>() + (size_t)t0 * E;
+            a.act = e->act.as<float>() + (size_t)t0 * K * F;
+            a.ffn_in = e->ffn_in.as<float>() + (size_t)t0 * E;
+            a.x_out = e->x.as<float>() + (size_t)t0 * E;
+            a.single = e->single.as<unsigned char>() + t0;
+            a.err = err;
+            a.slot_bytes = a.g_tile_bytes + a.u_tile_bytes;
+            a.nst = 1;
+            a.nst = pick_nst(a.slot_bytes, gateup_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes);
+            timer_begin(e, "expert_gateup");
+            CK(launch_gateup(a, grid_for(e, (long long)tg * K * a.g_n_tiles), st, pdl));
+            timer_end(e);
+            a.slot_bytes = K * a.d_tile_bytes;
+            a.nst = 1;
+            a.nst = pick_nst(a.slot_bytes, down_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes);
+            timer_begin(e, "expert_down");
+            CK(launch_down(a, grid_for(e, (long long)tg * E), st, pdl));
+            timer_end(e);
+        }
+    }
+    const int n_out = (int)p.x_rows.size();
+    for (int o0 = 0; o0 < n_out; o0 += MAX_T) {
+        int og = n_out - o0 < MAX_T ? n_out - o0 : MAX_T;
+        const QMat *mats[1] = {&e->out};
+        int offs[1] = {0};
+        CK(run_gemv(e, mats, offs, 1, e->x.as<float>(), E, e->x_rows.as<int>() + o0, e->out_norm.as<float>(), E, og,
+                    e->logits.as<float>() + (size_t)(p.out_first + o0) * d.n_vocab, d.n_vocab, nullptr, 0, "output_gemv"));
+    }
+    {
+        StepEndArgs a{};
+        a.logits = e->logits.as<float>();
+        a.V = d.n_vocab;
+        a.n_seqs = (int)p.st_seq.size();
+        a.n_out = greedy ? (int)p.st_seq.size() : e->max_out;
+        a.seq_ids = e->st_seq.as<int>();
+        a.n_tok = e->st_ntok.as<int>();
+        a.logit_row = e->st_lrow.as<int>();
+        a.dev_len = kv->dev_len.as<int>();
+        a.next_token = e->next_tok.as<int>();
+        a.tokens_buf = greedy ? e->tokens.as<int>() : nullptr;
+        a.gen_out = greedy ? e->gen_out.as<int>() : nullptr;
+        a.gen_count = e->gen_count.as<int>();
+        timer_begin(e, "step_end");
+        CK(launch_step_end(a, st, pdl));
+        timer_end(e);
+    }
+    return BT_OK;
+}
+
+static int check_err(bt_engine *e) {
+    int h = 0;
+    CK(cudaMemcpyAsync(&h, e->err.p, 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    if (h) {
+        CK(cudaMemsetAsync(e->err.p, 0, 4, e->st));
+        CK(cudaStreamSynchronize(e->st));
+        if (h & ERR_WAIT_TIMEOUT) return fail(BT_ERR_TIMEOUT, "a device wait ran out of time");
+        return fail(BT_ERR_INVALID, "a kernel rejected an index (token id out of range?)");
+    }
+    return BT_OK;
+}
+
+extern "C" int bt_forward(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const uint32_t *tokens,
+                          const uint32_t *n_tokens, const uint32_t *pos_start, uint32_t n_seqs, float *logits_out) {
+    if (!e || !kv || !seq_ids || !tokens || !n_tokens || !pos_start) return fail(BT_ERR_INVALID, "null argument");
+    if (kv->e != e) return fail(BT_ERR_INVALID, "KV pool belongs to another engine");
+    if (n_seqs == 0 || n_seqs > (uint32_t)e->max_out) return fail(BT_ERR_INVALID, "1..256 sequences per call");
+    CK(cudaSetDevice(e->device));
+    auto t0 = std::chrono::steady_clock::now();
+    std::vector<char> seen(kv->max_seqs, 0);
+    size_t total = 0;
+    for (uint32_t i = 0; i < n_seqs; i++) {
+        uint32_t s = seq_ids[i];
+        if (s >= kv->max_seqs) return fail(BT_ERR_INVALID, "sequence id out of range");
+        if (seen[s]) return fail(BT_ERR_INVALID, "a sequence appears twice in one call");
+        seen[s] = 1;
+        if (n_tokens[i] == 0) return fail(BT_ERR_INVALID, "a sequence has no tokens");
+        if (pos_start[i] != kv->len[s]) return fail(BT_ERR_KV, "pos_start must equal the sequence's cache length");
+        if ((uint64_t)kv->len[s] + n_tokens[i] > kv->max_positions)
+            return fail(BT_ERR_KV, "context would exceed max_positions");
+        total += n_tokens[i];
+    }
+    for (size_t i = 0; i < total; i++)
+        if (tokens[i] >= e->d.n_vocab) return fail(BT_ERR_INVALID, "token id out of range");
+    int r;
+    for (uint32_t i = 0; i < n_seqs; i++)
+        if ((r = kv_reserve(kv, seq_ids[i], kv->len[seq_ids[i]] + n_tokens[i]))) return r;
+    if ((r = kv_sync(kv))) return r;
+    // cut the concatenated tokens into steps of at most TB tokens
+    size_t g = 0;
+    uint32_t si = 0, ti = 0;  // current sequence, token within it
+    while (g < total) {
+        StepPlan p;
+        std::map<int, int> seq_slot;
+        while (p.T < e->TB && g < total) {
+            uint32_t s = seq_ids[si];
+            p.tokens.push_back((int)tokens[g]);
+            p.seq_of.push_back((int)s);
+            auto it = seq_slot.find((int)s);
+            int local = 0;
+            if (it == seq_slot.end()) {
+                seq_slot[(int)s] = (int)p.st_seq.size();
+                p.st_seq.push_back((int)s);
+                p.st_ntok.push_back(0);
+                p.st_lrow.push_back(-1);
+            } else {
+                local = p.st_ntok[it->second];
+            }
+            int slot = seq_slot[(int)s];
+            p.local_idx.push_back(local);
+            p.single.push_back(n_tokens[si] == 1 ? 1 : 0);
+            p.st_ntok[slot]++;
+            if (ti + 1 == n_tokens[si]) {  // the sequence's last token: its logits row is si
+                if (p.x_rows.empty()) p.out_first = (int)si;
+                p.st_lrow[slot] = (int)si;
+                p.x_rows.push_back(p.T);
+            }
+            p.T++;
+            g++;
+            ti++;
+            if (ti == n_tokens[si]) {
+                si++;
+                ti = 0;
+            }
+        }
+        if ((r = upload_plan(e, p))) return r;
+        if ((r = launch_step(e, kv, p, false))) return r;
+        e->last_T = p.T;
+    }
+    if ((r = check_err(e))) return r;
+    if (logits_out)
+        CK(cudaMemcpyAsync(logits_out, e->logits.p, (size_t)n_seqs * e->d.n_vocab * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    for (uint32_t i = 0; i < n_seqs; i++) {
+        uint32_t s = seq_ids[i];
+        kv->len[s] += n_tokens[i];
+        for (auto &c : kv->layer_pos[s]) c = kv->len[s];
+    }
+    e->stats.forward_calls++;
+    e->stats.tokens += total;
+    e->stats.forward_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    return BT_OK;
+}
+
+static int greedy_prepare(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const uint32_t *first_tokens,
+                          uint32_t n_seqs, uint32_t n_steps, StepPlan &p) {
+    if (!e || !kv || !seq_ids || !first_tokens) return fail(BT_ERR_INVALID, "null argument");
+    if (kv->e != e) return fail(BT_ERR_INVALID, "KV pool belongs to another engine");
+    if (n_seqs == 0 || n_seqs > (uint32_t)e->TB) return fail(BT_ERR_INVALID, "1..64 sequences per greedy batch");
+    CK(cudaSetDevice(e->device));
+    std::vector<char> seen(kv->max_seqs, 0);
+    for (uint32_t i = 0; i < n_seqs; i++) {
+        uint32_t s = seq_ids[i];
+        if (s >= kv->max_seqs || seen[s]) return fail(BT_ERR_INVALID, "bad or repeated sequence id");
+        seen[s] = 1;
+        if ((uint64_t)kv->len[s] + n_steps > kv->max_positions) return fail(BT_ERR_KV, "context would exceed max_positions");
+        if (first_tokens[i] >= e->d.n_vocab) return fail(BT_ERR_INVALID, "token id out of range");
+    }
+    int r;
+    for (uint32_t i = 0; i < n_seqs; i++)
+        if ((r = kv_reserve(kv, seq_ids[i], kv->len[seq_ids[i]] + n_steps))) return r;
+    if ((r = kv_sync(kv))) return r;
+    size_t need = (size_t)e->max_out * e->d.max_positions;
+    if (e->gen_out.n < need * 4) {
+        // the graphs hold the buffer's address: drop them before it moves
+        for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
+        e->graphs.clear();
+        CK(e->gen_out.alloc(need * 4));
+    }
+    CK(cudaMemsetAsync(e->gen_count.p, 0, (size_t)e->max_out * 4, e->st));
+    p.T = (int)n_seqs;
+    for (uint32_t i = 0; i < n_seqs; i++) {
+        p.tokens.push_back((int)first_tokens[i]);
+        p.seq_of.push_back((int)seq_ids[i]);
+        p.local_idx.push_back(0);
+        p.single.push_back(1);
+        p.st_seq.push_back((int)seq_ids[i]);
+        p.st_ntok.push_back(1);
+        p.st_lrow.push_back((int)i);
+        p.x_rows.push_back((int)i);
+    }
+    p.out_first = 0;
+    return upload_plan(e, p);
+}
+
+static int greedy_finish(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, uint32_t n_seqs, uint32_t n_steps,
+                         uint32_t *tokens_out, float *last_logits) {
+    int r = check_err(e);
+    if (r) return r;
+    if (tokens_out && n_steps)
+        CK(cudaMemcpyAsync(tokens_out, e->gen_out.p, (size_t)n_steps * n_seqs * 4, cudaMemcpyDeviceToHost, e->st));
+    if (last_logits && n_steps)
+        CK(cudaMemcpyAsync(last_logits, e->logits.p, (size_t)n_seqs * e->d.n_vocab * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    for (uint32_t i = 0; i < n_seqs; i++) {
+        uint32_t s = seq_ids[i];
+        kv->len[s] += n_steps;
+        for (auto &c : kv->layer_pos[s]) c = kv->len[s];
+    }
+    e->stats.tokens += (uint64_t)n_steps * n_seqs;
+    return BT_OK;
+}
+
+extern "C" int bt_generate_greedy(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const uint32_t *first_tokens,
+                                  uint32_t n_seqs, uint32_t n_steps, uint32_t *tokens_out, float *last_logits) {
+    auto t0 = std::chrono::steady_clock::now();
+    StepPlan p;
+    int r = greedy_prepare(e, kv, seq_ids, first_tokens, n_seqs, n_steps, p);
+    if (r) return r;
+    GraphKey key{kv, std::vector<uint32_t>(seq_ids, seq_ids + n_seqs)};
+    auto it = e->graphs.find(key);
+    if (it == e->graphs.end() && n_steps > 0) {
+        cudaGraph_t graph;
+        CK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+        int lr = launch_step(e, kv, p, true);
+        cudaError_t ce = cudaStreamEndCapture(e->st, &graph);
+        if (lr) return lr;
+        CK(ce);
+        cudaGraphExec_t exec;
+        ce = cudaGraphInstantiate(&exec, graph, 0);
+        cudaGraphDestroy(graph);
+        CK(ce);
+        it = e->graphs.emplace(key, exec).first;
+    }
+    cudaEvent_t a, b;
+    CK(cudaEventCreate(&a));
+    CK(cudaEventCreate(&b));
+    CK(cudaEventRecord(a, e->st));
+    for (uint32_t s = 0; s < n_steps; s++) CK(cudaGraphLaunch(it->second, e->st));
+    CK(cudaEventRecord(b, e->st));
+    CK(cudaEventSynchronize(b));
+    float ms = 0;
+    cudaEventElapsedTime(&ms, a, b);
+    cudaEventDestroy(a);
+    cudaEventDestroy(b);
+    e->last_device_ms = ms;
+    e->stats.graph_replays += n_steps;
+    r = greedy_finish(e, kv, seq_ids, n_seqs, n_steps, tokens_out, last_logits);
+    e->stats.forward_calls++;
+    e->stats.forward_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+    return r;
+}
+
+extern "C" int bt_last_device_ms(const bt_engine *e, double *ms) {
+    if (!e || !ms) return fail(BT_ERR_INVALID, "null argument");
+    *ms = e->last_device_ms;
+    return BT_OK;
+}
+
+extern "C" int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const uint32_t *first_tokens,
+                                 uint32_t n_seqs, uint32_t n_steps, bt_kernel_time *out, uint32_t max_out,
+                                 uint32_t *n_out) {
+    StepPlan p;
+    int r = greedy_prepare(e, kv, seq_ids, first_tokens, n_seqs, n_steps, p);
+    if (r) return r;
+    e->timers.clear();
+    e->timing = true;
+    bool pdl = e->pdl;
+    e->pdl = false;  // serialised launches: each event pair brackets one kernel
+    for (uint32_t s = 0; s < n_steps && !r; s++) {
+        r = launch_step(e, kv, p, true);
+        CK(cudaStreamSynchronize(e->st));
+        timer_collect(e);
+    }
+    e->timing = false;
+    e->pdl = pdl;
+    if (r) return r;
+    if ((r = greedy_finish(e, kv, seq_ids, n_seqs, n_steps, nullptr, nullptr))) return r;
+    uint32_t i = 0;
+    for (auto &kt : e->timers) {
+        if (i < max_out && out) {
+            memset(&out[i], 0, sizeof(bt_kernel_time));
+            strncpy(out[i].name, kt.first.c_str(), sizeof(out[i].name) - 1);
+            out[i].launches = kt.second.launches;
+            out[i].total_ms = kt.second.ms;
+        }
+        i++;
+    }
+    if (n_out) *n_out = i;
+    return BT_OK;
+}
+
+extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
+    if (!e || !name) return fail(BT_ERR_INVALID, "null argument");
+    if (!strcmp(name, "pdl")) {
+        e->pdl = value != 0;
+        for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
+        e->graphs.clear();
+        return BT_OK;
+    }
+    return fail(BT_ERR_INVALID, std::string("unknown option ") + name);
+}
+
+// ------------------------------------------------------------------ parity hooks
+extern "C" int bt_debug_topk(const bt_engine *e, uint32_t layer, uint32_t token, int32_t *ids, float *weights) {
+    if (!e || !ids || !weights) return fail(BT_ERR_INVALID, "null argument");
+    if (layer >= e->d.n_layer || (int)token >= e->last_T) return fail(BT_ERR_INVALID, "layer or token out of range");
+    const int K = e->d.n_expert_used;
+    size_t off = ((size_t)layer * e->TB + token) * K;
+    CK(cudaMemcpy(ids, e->dbg_ids.as<int>() + off, K * 4, cudaMemcpyDeviceToHost));
+    CK(cudaMemcpy(weights, e->dbg_w.as<float>() + off, K * 4, cudaMemcpyDeviceToHost));
+    return BT_OK;
+}
+
+extern "C" int bt_debug_hidden(const bt_engine *e, uint32_t token, float *out) {
+    if (!e || !out) return fail(BT_ERR_INVALID, "null argument");
+    if ((int)token >= e->last_T) return fail(BT_ERR_INVALID, "token out of range");
+    CK(cudaMemcpy(out, e->x.as<float>() + (size_t)token * e->d.n_embd, e->d.n_embd * 4, cudaMemcpyDeviceToHost));
+    return BT_OK;
+}
+
+extern "C" int bt_debug_dequant(uint32_t type, const void *bytes, uint64_t n, float *out) {
+    if (!bytes || !out) return fail(BT_ERR_INVALID, "null argument");
+    if (type != T_Q4_K && type != T_Q6_K) return fail(BT_ERR_UNSUPPORTED, "dequant hook covers Q4_K and Q6_K");
+    if (n % 256) return fail(BT_ERR_INVALID, "a partial K-quant block");  // lib.rs:258-264
+    if (n == 0) return BT_OK;
+    long long rows = (long long)(n / 256);
+    TileGeom g = tile_geom((int)type, rows, 256, 32);
+    DevBuf raw, tiled, y;
+    size_t rb = (size_t)rows * qk_block_bytes((int)type);
+    CK(raw.alloc(rb));
+    CK(tiled.alloc((size_t)g.n_tiles * g.tile_bytes));
+    CK(y.alloc(n * 4));
+    CK(cudaMemcpy(raw.p, bytes, rb, cudaMemcpyHostToDevice));
+    CK(launch_repack((int)type, raw.as<uint8_t>(), rows, 256, 32, tiled.as<uint8_t>(), 1, 0));
+    CK(launch_dequant_tiled((int)type, tiled.as<uint8_t>(), rows, 256, 32, y.as<float>(), 0));
+    CK(cudaMemcpy(out, y.p, n * 4, cudaMemcpyDeviceToHost));
+    return BT_OK;
+}
+
+extern "C" int bt_op_gemv(uint32_t type, const void *w_bytes, uint32_t rows, uint32_t cols, const float *x, uint32_t T,
+                          float *y) {
+    if (!w_bytes || !x || !y || !rows || !cols || !T) return fail(BT_ERR_INVALID, "bad argument");
+    bt_engine tmp;
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    cudaDeviceProp prop;
+    CK(cudaGetDeviceProperties(&prop, dev));
+    tmp.n_sm = prop.multiProcessorCount;
+    tmp.device = dev;
+    CK(init_kernel_attributes());
+    CK(cudaStreamCreateWithFlags(&tmp.st, cudaStreamNonBlocking));
+    tmp.pdl = false;
+    QMat m;
+    DevBuf staging, xd, yd;
+    int r = ingest_qmat(&tmp, m, (int)type, rows, cols, 1, w_bytes, false, default_rpt(cols), false, staging);
+    if (r) {
+        cudaStreamDestroy(tmp.st);
+        tmp.st = nullptr;
+        return r;
+    }
+    CK(tmp.err.alloc(4));
+    CK(cudaMemset(tmp.err.p, 0, 4));
+    CK(xd.alloc((size_t)T * cols * 4));
+    CK(yd.alloc((size_t)T * rows * 4));
+    CK(cudaMemcpy(xd.p, x, (size_t)T * cols * 4, cudaMemcpyHostToDevice));
+    for (uint32_t t0 = 0; t0 < T; t0 += MAX_T) {
+        int tg = T - t0 < (uint32_t)MAX_T ? (int)(T - t0) : MAX_T;
+        const QMat *mats[1] = {&m};
+        int offs[1] = {0};
+        CK(run_gemv(&tmp, mats, offs, 1, xd.as<float>() + (size_t)t0 * cols, cols, nullptr, nullptr, cols, tg,
+                    yd.as<float>() + (size_t)t0 * rows, rows, nullptr, 0, "gemv"));
+    }
+    CK(cudaStreamSynchronize(tmp.st));
+    r = check_err(&tmp);
+    CK(cudaMemcpy(y, yd.p, (size_t)T * rows * 4, cudaMemcpyDeviceToHost));
+    cudaStreamDestroy(tmp.st);
+    tmp.st = nullptr;
+    return r;
+}
+
+extern "C" int bt_engine_tensor_bytes(const bt_engine *ec, const char *name, void *host_out, uint64_t nbytes) {
+    bt_engine *e = const_cast<bt_engine *>(ec);
+    if (!e || !name || !host_out) return fail(BT_ERR_INVALID, "null argument");
+    CK(cudaSetDevice(e->device));
+    std::string n(name);
+    const QMat *m = nullptr;
+    const DevBuf *f = nullptr;
+    if (n == "token_embd.weight") m = &e->embd;
+    else if (n == "output.weight") m = &e->out;
+    else if (n == "output_norm.weight") f = &e->out_norm;
+    else if (n.rfind("blk.", 0) == 0) {
+        size_t dot = n.find('.', 4);
+        uint32_t il = (uint32_t)atoi(n.substr(4, dot - 4).c_str());
+        if (il >= e->d.n_layer) return fail(BT_ERR_MISSING_TENSOR, "no tensor " + n);
+        Layer &l = e->L[il];
+        std::string s = n.substr(dot + 1);
+        if (s == "attn_q.weight") m = &l.q;
+        else if (s == "attn_k.weight") m = &l.k;
+        else if (s == "attn_v.weight") m = &l.v;
+        else if (s == "attn_output.weight") m = &l.o;
+        else if (s == "ffn_gate_exps.weight") m = &l.gate;
+        else if (s == "ffn_up_exps.weight") m = &l.up;
+        else if (s == "ffn_down_exps.weight") m = &l.down;
+        else if (s == "attn_norm.weight") f = &l.attn_norm;
+        else if (s == "attn_q_norm.weight") f = &l.q_norm;
+        else if (s == "attn_k_norm.weight") f = &l.k_norm;
+        else if (s == "ffn_norm.weight") f = &l.ffn_norm;
+        else if (s == "ffn_gate_inp.weight") f = &l.gate_inp;
+    }
+    if (f) {
+        if (nbytes != f->n) return fail(BT_ERR_INVALID, "size mismatch for " + n);
+        CK(cudaMemcpy(host_out, f->p, nbytes, cudaMemcpyDeviceToHost));
+        return BT_OK;
+    }
+    if (!m) return fail(BT_ERR_MISSING_TENSOR, "no tensor " + n);
+    size_t raw = (size_t)m->n_mats * m->rows * (m->cols / 256) * qk_block_bytes(m->type);
+    if (nbytes != raw) return fail(BT_ERR_INVALID, "size mismatch for " + n);
+    DevBuf tmp;
+    CK(tmp.alloc(raw));
+    CK(launch_untile(m->type, m->buf.as<uint8_t>(), m->rows, m->cols, m->g.rpt, tmp.as<uint8_t>(), m->n_mats, e->st));
+    CK(cudaMemcpyAsync(host_out, tmp.p, raw, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    return BT_OK;
+}
+
+// ------------------------------------------------------------------ synthetic weights on the host
+extern "C" int bt_synth_tensor(uint32_t type, uint64_t rows, uint64_t cols, uint64_t seed, uint64_t tensor_id,
+                               float mean, float sigma, void *out) {
+    if (!out) return fail(BT_ERR_INVALID, "null output");
+    const uint64_t n = rows * cols;
+    const int t = (int)type;
+    if (t != T_F32 && t != T_F16 && t != T_Q4_K && t != T_Q6_K) return fail(BT_ERR_UNSUPPORTED, "unsupported type");
+    if ((t == T_Q4_K || t == T_Q6_K) && (cols % 256)) return fail(BT_ERR_INVALID, "K-quant rows must be whole blocks");
+    const uint64_t key = synth_key(seed, tensor_id);
+    const float scale = synth_scale(sigma);
+    const int eb = t == T_F32 ? 4 : (t == T_F16 ? 2 : 0);
+    const int bb = synth_block_bytes(t);
+    const long long nblk = (long long)((n + 255) / 256);
+    uint8_t *o = reinterpret_cast<uint8_t *>(out);
+#pragma omp parallel for schedule(static)
+    for (long long i = 0; i < nblk; i++) {
+        uint8_t blk[1024];
+        synth_block(t, key, (uint64_t)i * 256u, mean, scale, blk);
+        long long left = (long long)n - i * 256;
+        int nb = (eb && left < 256) ? (int)left * eb : bb;
+        memcpy(o + (eb ? i * 256 * eb : i * bb), blk, (size_t)nb);
+    }
+    return BT_OK;
+}
+
+extern "C" uint64_t bt_tensor_id(const char *name) { return name ? name_id(name) : 0; }

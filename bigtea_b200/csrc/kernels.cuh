@@ -1,0 +1,149 @@
+// kernels.cuh -- parameter blocks and launchers of the decode-layer kernels (sm_100a).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kquant.cuh"
+
+namespace bt {
+
+constexpr int MAX_T = 8;        // tokens one GEMV / expert launch carries in shared memory
+constexpr int MAX_K = 16;       // experts used per token
+constexpr int ATTN_CHUNK = 256; // attention keys per chunk (contract C8)
+constexpr int GEMV_WARPS = 8;
+
+struct GemvSeg {
+    const uint8_t *w;  // tiled weights
+    int type, nsb, rpt, S, tile_bytes;
+    int rows;
+    int n_tiles;
+    int tile0;    // first global unit of this segment
+    int out_off;  // column offset in y
+};
+
+struct GemvArgs {
+    GemvSeg seg[3];
+    int nseg, total_tiles;
+    const float *x;
+    long long x_stride;
+    const int *x_rows;     // optional row indirection for the activations
+    const float *norm_w;   // optional RMSNorm weight (C6) applied before quantising
+    float eps;
+    int K, T;
+    float *y;
+    long long y_stride;
+    const float *res;      // optional residual added to the output
+    long long res_stride;
+    int *err;
+    int slot_bytes, nst;
+};
+
+struct ExpertArgs {
+    const uint8_t *gate, *up, *down;
+    int gtype, utype, dtype;
+    int g_nsb, g_rpt, g_S, g_tile_bytes, g_n_tiles;
+    int u_tile_bytes;
+    long long g_expert_bytes, u_expert_bytes, d_expert_bytes;
+    int d_nsb, d_tile_bytes;
+    int E, F, K, T, workers;
+    const int *sel_ids;        // [T][K] ascending expert ids
+    const float *sel_w;        // [T][K] their renormalised weights
+    const float *fn;           // [T][E] post-norm activations (gate/up input)
+    float *act;                // [T][K][F] silu(gate)*up
+    const float *ffn_in;       // [T][E] residual
+    float *x_out;              // [T][E]
+    const unsigned char *single;  // [T] 1 = the token was a single-token step (paired order)
+    int *err;
+    int slot_bytes, nst;
+};
+
+struct RouterArgs {
+    const float *x, *norm_w;
+    float eps;
+    int E;
+    const float *Wr;
+    int NE, K, T, rows_per_cta;
+    float *fn_out, *logits;
+    int *cnt;
+    int *topk_ids;
+    float *topk_w;
+    int *sel_ids;
+    float *sel_w;
+};
+
+struct QkvPostArgs {
+    const float *qkv;
+    int qkv_stride;
+    const float *q_norm, *k_norm;
+    float eps;
+    const float *rope;
+    int n_rot, H, HK, D, T;
+    const int *seq_of, *pos_of, *block_table;
+    int max_blocks, layer, n_blocks;
+    __half *kv;
+    float *q_out;
+};
+
+struct AttnArgs {
+    const float *q;
+    int H, HK, D, G, T;
+    const int *seq_of, *pos_of, *block_table;
+    int max_blocks, layer, n_blocks, max_chunks;
+    float scale;
+    float *part;
+    int *cnt;
+    float *out;
+    int *err;
+};
+
+struct EmbedArgs {
+    const uint8_t *table;  // raw GGUF rows
+    int type, E, V, T;
+    const int *tokens, *seq_of, *local_idx;
+    const int *dev_len;
+    int *pos_of;
+    float *x;
+    int *err;
+};
+
+struct StepEndArgs {
+    const float *logits;  // [n_out][V]
+    int V, n_seqs, n_out;
+    const int *seq_ids, *n_tok;
+    const int *logit_row; // [n_seqs]: row of `logits` holding the sequence's last token, or -1
+    int *dev_len;
+    int *next_token;      // [n_out]
+    int *tokens_buf;      // if non-null: tokens_buf[row] = argmax (greedy feed-back)
+    int *gen_out;         // if non-null: gen_out[gen_count[row]*n_out + row] = argmax
+    int *gen_count;
+};
+
+cudaError_t init_kernel_attributes();
+
+// ---- launchers (all asynchronous on `st`; `pdl` enables programmatic dependent launch)
+size_t gemv_smem_bytes(const GemvArgs &a);
+cudaError_t launch_gemv(const GemvArgs &a, int grid, cudaStream_t st, bool pdl);
+size_t gateup_smem_bytes(const ExpertArgs &a);
+size_t down_smem_bytes(const ExpertArgs &a);
+cudaError_t launch_gateup(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
+cudaError_t launch_down(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
+cudaError_t launch_router(const RouterArgs &a, cudaStream_t st, bool pdl);
+cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl);
+size_t attn_smem_bytes(int G);
+cudaError_t launch_attn(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl);
+cudaError_t launch_embed(const EmbedArgs &a, cudaStream_t st, bool pdl);
+cudaError_t launch_step_end(const StepEndArgs &a, cudaStream_t st, bool pdl);
+
+cudaError_t launch_repack(int type, const uint8_t *src, long long rows, long long cols, int rpt, uint8_t *dst,
+                          long long n_mats, cudaStream_t st);
+cudaError_t launch_dequant_tiled(int type, const uint8_t *tiled, long long rows, long long cols, int rpt,
+                                 float *out, cudaStream_t st);
+cudaError_t launch_kv_copy(__half *pool, const int *table_row, int layer, int n_blocks, int HK, int D, int p0, int n,
+                           __half *kbuf, __half *vbuf, int to_pool, cudaStream_t st);
+cudaError_t launch_untile(int type, const uint8_t *tiled, long long rows, long long cols, int rpt, uint8_t *dst,
+                          long long n_mats, cudaStream_t st);
+cudaError_t launch_synth(int type, uint64_t key, long long n_elems, float mean, float scale, uint8_t *out,
+                         cudaStream_t st);
+
+}  // namespace bt

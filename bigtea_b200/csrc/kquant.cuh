@@ -1,0 +1,372 @@
+// kquant.cuh -- Q4_K / Q6_K block formats, the HBM tile layout, the seeded synthetic
+// quantiser and the per-slot integer dot products of the GEMV kernels.
+//
+// Block formats (ggml block_q4_K / block_q6_K; Chaos reads them at core/model/src/validate.rs:60-75
+// and sizes them at core/gguf/src/tensor.rs:30-32):
+//   Q4_K, 144 B / 256 values: f16 d, f16 dmin, 12 bytes of packed 6-bit scales and mins,
+//         128 bytes of 4-bit quants; value = (d*sc)*q - (dmin*m).
+//   Q6_K, 210 B / 256 values: 128 B low nibbles, 64 B high 2-bit pairs, 16 int8 scales,
+//         f16 d; value = (d*sc)*(q-32).
+//
+// HBM tile layout ("tiled-S"): a matrix of R rows x nsb superblocks is cut into tiles of
+// `rpt` rows; tile t holds the S = rpt*nsb superblocks of rows [t*rpt, t*rpt+rpt) as slots
+// s = (row - t*rpt)*nsb + b. A superblock's 16-byte chunk c lives at c*S*16 + s*16 inside
+// the tile, so one warp whose lane s reads chunk c touches S*16 contiguous bytes: every
+// 16-byte load of a superblock is coalesced across the warp. Q6_K's trailing f16 d (the
+// bytes after its 13 whole chunks) goes to a plane at 13*S*16 + s*2, padded to 16 bytes.
+// The permutation is lossless: a tile carries exactly the GGUF bytes of its rows.
+#pragma once
+#include <cuda_fp16.h>
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+namespace bt {
+
+enum : int { T_F32 = 0, T_F16 = 1, T_Q4_K = 12, T_Q6_K = 14 };
+
+__host__ __device__ inline int qk_block_bytes(int type) { return type == T_Q4_K ? 144 : (type == T_Q6_K ? 210 : 0); }
+__host__ __device__ inline int qk_chunks(int type) { return type == T_Q4_K ? 9 : 13; }
+
+struct TileGeom {
+    int type, nsb, rpt, S, tile_bytes;
+    long long n_tiles;
+    long long rows;
+};
+
+__host__ __device__ inline TileGeom tile_geom(int type, long long rows, long long cols, int rpt) {
+    TileGeom g;
+    g.type = type;
+    g.nsb = (int)(cols / 256);
+    g.rpt = rpt;
+    g.S = rpt * g.nsb;
+    g.rows = rows;
+    if (type == T_Q4_K) g.tile_bytes = 9 * g.S * 16;
+    else g.tile_bytes = 13 * g.S * 16 + ((g.S * 2 + 15) / 16) * 16;
+    g.n_tiles = (rows + rpt - 1) / rpt;
+    return g;
+}
+
+// the row count per tile a warp-wide GEMV uses: as many whole rows as fit in 32 slots
+__host__ __device__ inline int default_rpt(long long cols) {
+    int nsb = (int)(cols / 256);
+    return nsb > 0 && nsb <= 32 ? 32 / nsb : 0;
+}
+
+// ------------------------------------------------------------------ f16 on host and device
+__host__ __device__ inline uint16_t f32_to_f16_bits(float f) {
+#ifdef __CUDA_ARCH__
+    return __half_as_ushort(__float2half_rn(f));
+#else
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u, e8 = (x >> 23) & 0xffu, mant = x & 0x7fffffu;
+    if (e8 == 0xffu) return (uint16_t)(sign | 0x7c00u | (mant ? 0x200u : 0u));
+    int e = (int)e8 - 112;
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        mant |= 0x800000u;
+        int shift = 14 - e;
+        uint32_t h = mant >> shift, rem = mant & ((1u << shift) - 1u), mid = 1u << (shift - 1);
+        if (rem > mid || (rem == mid && (h & 1u))) h++;
+        return (uint16_t)(sign | h);
+    }
+    uint32_t h = sign | ((uint32_t)e << 10) | (mant >> 13), rem = mant & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;
+    return (uint16_t)h;
+#endif
+}
+
+__host__ __device__ inline float f16_bits_to_f32(uint16_t h) {
+#ifdef __CUDA_ARCH__
+    return __half2float(__ushort_as_half(h));
+#else
+    uint32_t sign = ((uint32_t)h & 0x8000u) << 16, e = ((uint32_t)h >> 10) & 0x1fu, m = (uint32_t)h & 0x3ffu, bits;
+    if (e == 0) {
+        if (m == 0) bits = sign;
+        else {
+            int sh = 0;
+            while (!(m & 0x400u)) { m <<= 1; sh++; }
+            bits = sign | ((uint32_t)(113 - sh) << 23) | ((m & 0x3ffu) << 13);
+        }
+    } else if (e == 31) bits = sign | 0x7f800000u | (m << 13);
+    else bits = sign | ((e + 112u) << 23) | (m << 13);
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+#endif
+}
+
+// ------------------------------------------------------------------ seeded synthetic values
+__host__ __device__ inline uint64_t splitmix64(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+// Irwin-Hall(4) approximation of N(mean, sigma): four 16-bit uniforms from one 64-bit hash.
+// Integer sum, one int->float conversion and two rounded float ops: the same bits on the
+// host and the device.
+__host__ __device__ inline float synth_value(uint64_t key, uint64_t idx, float mean, float scale) {
+    uint64_t h = splitmix64(key + idx * 0xD1B54A32D192ED03ull);
+    int s = (int)(h & 0xffffu) + (int)((h >> 16) & 0xffffu) + (int)((h >> 32) & 0xffffu) + (int)(h >> 48);
+    float z = (float)(s - 131070) * scale;
+    return mean + z;
+}
+
+__host__ __device__ inline uint64_t synth_key(uint64_t seed, uint64_t tensor_id) {
+    return splitmix64(seed ^ splitmix64(tensor_id));
+}
+
+// sigma * sqrt(3) / 65536: unit variance for the centred sum of four 16-bit uniforms
+__host__ __device__ inline float synth_scale(float sigma) { return sigma * 2.64296052e-05f; }
+
+__host__ __device__ inline int clampi(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+// A simple K-quant quantiser: per 32-value sub-block min/max, 6-bit scales and mins.
+__host__ __device__ inline void quant_q4k_block(const float *x, uint8_t *out) {
+    float scl[8], mns[8];
+    for (int j = 0; j < 8; j++) {
+        float mn = x[32 * j], mx = x[32 * j];
+        for (int l = 1; l < 32; l++) {
+            float v = x[32 * j + l];
+            mn = v < mn ? v : mn;
+            mx = v > mx ? v : mx;
+        }
+        if (mn > 0.0f) mn = 0.0f;
+        scl[j] = (mx - mn) / 15.0f;
+        mns[j] = -mn;
+    }
+    float ms = 0.0f, mm = 0.0f;
+    for (int j = 0; j < 8; j++) {
+        ms = scl[j] > ms ? scl[j] : ms;
+        mm = mns[j] > mm ? mns[j] : mm;
+    }
+    uint16_t dh = f32_to_f16_bits(ms / 63.0f), dmh = f32_to_f16_bits(mm / 63.0f);
+    float df = f16_bits_to_f32(dh), dmf = f16_bits_to_f32(dmh);
+    int sc[8], m[8];
+    for (int j = 0; j < 8; j++) {
+        sc[j] = df > 0.0f ? clampi((int)rintf(scl[j] / df), 0, 63) : 0;
+        m[j] = dmf > 0.0f ? clampi((int)rintf(mns[j] / dmf), 0, 63) : 0;
+    }
+    out[0] = (uint8_t)(dh & 0xff);
+    out[1] = (uint8_t)(dh >> 8);
+    out[2] = (uint8_t)(dmh & 0xff);
+    out[3] = (uint8_t)(dmh >> 8);
+    uint8_t *s = out + 4;
+    for (int j = 0; j < 4; j++) {
+        s[j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+        s[j + 4] = (uint8_t)((m[j] & 63) | ((m[j + 4] >> 4) << 6));
+        s[j + 8] = (uint8_t)((sc[j + 4] & 0xF) | ((m[j + 4] & 0xF) << 4));
+    }
+    uint8_t *qs = out + 16;
+    for (int g = 0; g < 4; g++) {
+        float d0 = df * (float)sc[2 * g], m0 = dmf * (float)m[2 * g];
+        float d1 = df * (float)sc[2 * g + 1], m1 = dmf * (float)m[2 * g + 1];
+        for (int l = 0; l < 32; l++) {
+            int q0 = d0 > 0.0f ? clampi((int)rintf((x[64 * g + l] + m0) / d0), 0, 15) : 0;
+            int q1 = d1 > 0.0f ? clampi((int)rintf((x[64 * g + 32 + l] + m1) / d1), 0, 15) : 0;
+            qs[32 * g + l] = (uint8_t)(q0 | (q1 << 4));
+        }
+    }
+}
+
+__host__ __device__ inline void quant_q6k_block(const float *x, uint8_t *out) {
+    float ds[16];
+    for (int s = 0; s < 16; s++) {
+        float amax = 0.0f, mx = 0.0f;
+        for (int i = 0; i < 16; i++) {
+            float v = x[16 * s + i], av = fabsf(v);
+            if (av > amax) {
+                amax = av;
+                mx = v;
+            }
+        }
+        ds[s] = amax == 0.0f ? 0.0f : mx / -32.0f;
+    }
+    float amax = 0.0f, smax = 0.0f;
+    for (int s = 0; s < 16; s++) {
+        float av = fabsf(ds[s]);
+        if (av > amax) {
+            amax = av;
+            smax = ds[s];
+        }
+    }
+    int L[256];
+    int8_t sc[16];
+    uint16_t dh = 0;
+    if (amax == 0.0f) {
+        for (int i = 0; i < 256; i++) L[i] = 32;
+        for (int s = 0; s < 16; s++) sc[s] = 0;
+    } else {
+        float iscale = -128.0f / smax;
+        dh = f32_to_f16_bits(1.0f / iscale);
+        float df = f16_bits_to_f32(dh);
+        for (int s = 0; s < 16; s++) {
+            sc[s] = (int8_t)clampi((int)rintf(iscale * ds[s]), -128, 127);
+            float den = df * (float)sc[s];
+            for (int i = 0; i < 16; i++) {
+                int q = den != 0.0f ? clampi((int)rintf(x[16 * s + i] / den), -32, 31) : 0;
+                L[16 * s + i] = q + 32;
+            }
+        }
+    }
+    uint8_t *ql = out, *qh = out + 128;
+    for (int n = 0; n < 2; n++)
+        for (int l = 0; l < 32; l++) {
+            int L1 = L[128 * n + l], L2 = L[128 * n + 32 + l], L3 = L[128 * n + 64 + l], L4 = L[128 * n + 96 + l];
+            ql[64 * n + l] = (uint8_t)((L1 & 0xF) | ((L3 & 0xF) << 4));
+            ql[64 * n + 32 + l] = (uint8_t)((L2 & 0xF) | ((L4 & 0xF) << 4));
+            qh[32 * n + l] = (uint8_t)((L1 >> 4) | ((L2 >> 4) << 2) | ((L3 >> 4) << 4) | ((L4 >> 4) << 6));
+        }
+    for (int s = 0; s < 16; s++) out[192 + s] = (uint8_t)sc[s];
+    out[208] = (uint8_t)(dh & 0xff);
+    out[209] = (uint8_t)(dh >> 8);
+}
+
+// One superblock (or, for F32/F16, 256 elements) of a synthetic tensor, element index base
+// `e0` in row-major order.
+__host__ __device__ inline void synth_block(int type, uint64_t key, uint64_t e0, float mean, float scale,
+                                            uint8_t *out) {
+    float x[256];
+    for (int i = 0; i < 256; i++) x[i] = synth_value(key, e0 + (uint64_t)i, mean, scale);
+    if (type == T_Q4_K) quant_q4k_block(x, out);
+    else if (type == T_Q6_K) quant_q6k_block(x, out);
+    else if (type == T_F32) memcpy(out, x, sizeof x);
+    else if (type == T_F16) {
+        for (int i = 0; i < 256; i++) {
+            uint16_t h = f32_to_f16_bits(x[i]);
+            out[2 * i] = (uint8_t)(h & 0xff);
+            out[2 * i + 1] = (uint8_t)(h >> 8);
+        }
+    }
+}
+
+__host__ __device__ inline int synth_block_bytes(int type) {
+    return type == T_Q4_K ? 144 : type == T_Q6_K ? 210 : type == T_F32 ? 1024 : 512;
+}
+
+// FNV-1a of a tensor name: the tensor id of the synthetic generator
+inline uint64_t name_id(const char *s) {
+    uint64_t h = 1469598103934665603ull;
+    while (*s) {
+        h ^= (uint8_t)*s++;
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+// ------------------------------------------------------------------ device-side decode
+#ifdef __CUDACC__
+
+// Q8_K activation block as staged in shared memory: 256 quants, scale, and the sums of the
+// 8 sub-blocks of 32 (what the Q4_K min term needs). 304 bytes = 19 x 16, so consecutive
+// blocks start in different 16-byte bank groups.
+struct __align__(16) ActBlock {
+    int8_t qs[256];
+    float d;
+    int pad[3];
+    int bs32[8];
+};
+static_assert(sizeof(ActBlock) == 304, "ActBlock layout");
+
+__device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+
+// C4 for one Q4_K superblock (slot s of a tile in shared memory) against one activation block.
+__device__ __forceinline__ float q4k_slot_dot(const uint8_t *tile, int S, int s, const ActBlock &a) {
+    const uint4 *base = reinterpret_cast<const uint4 *>(tile) + s;
+    uint4 h = base[0];
+    float dw = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffff)));
+    float dminw = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    // scales bytes 0..11 = h.y, h.z, h.w
+    uint32_t s03 = h.y, s47 = h.z, s811 = h.w;
+    int sc[8], mn[8];
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        sc[j] = (s03 >> (8 * j)) & 63;
+        mn[j] = (s47 >> (8 * j)) & 63;
+        int b8 = (s811 >> (8 * j)) & 0xff;
+        sc[j + 4] = (b8 & 0xF) | (((s03 >> (8 * j + 6)) & 3) << 4);
+        mn[j + 4] = (b8 >> 4) | (((s47 >> (8 * j + 6)) & 3) << 4);
+    }
+    const uint4 *aq = reinterpret_cast<const uint4 *>(a.qs);
+    int sumi = 0;
+#pragma unroll
+    for (int g = 0; g < 4; g++) {
+        uint4 w0 = base[(1 + 2 * g) * S];
+        uint4 w1 = base[(2 + 2 * g) * S];
+        uint4 al0 = aq[4 * g + 0], al1 = aq[4 * g + 1], ah0 = aq[4 * g + 2], ah1 = aq[4 * g + 3];
+        int dlo = 0, dhi = 0;
+        dlo = dp4a(w0.x & 0x0F0F0F0F, al0.x, dlo);
+        dlo = dp4a(w0.y & 0x0F0F0F0F, al0.y, dlo);
+        dlo = dp4a(w0.z & 0x0F0F0F0F, al0.z, dlo);
+        dlo = dp4a(w0.w & 0x0F0F0F0F, al0.w, dlo);
+        dlo = dp4a(w1.x & 0x0F0F0F0F, al1.x, dlo);
+        dlo = dp4a(w1.y & 0x0F0F0F0F, al1.y, dlo);
+        dlo = dp4a(w1.z & 0x0F0F0F0F, al1.z, dlo);
+        dlo = dp4a(w1.w & 0x0F0F0F0F, al1.w, dlo);
+        dhi = dp4a((w0.x >> 4) & 0x0F0F0F0F, ah0.x, dhi);
+        dhi = dp4a((w0.y >> 4) & 0x0F0F0F0F, ah0.y, dhi);
+        dhi = dp4a((w0.z >> 4) & 0x0F0F0F0F, ah0.z, dhi);
+        dhi = dp4a((w0.w >> 4) & 0x0F0F0F0F, ah0.w, dhi);
+        dhi = dp4a((w1.x >> 4) & 0x0F0F0F0F, ah1.x, dhi);
+        dhi = dp4a((w1.y >> 4) & 0x0F0F0F0F, ah1.y, dhi);
+        dhi = dp4a((w1.z >> 4) & 0x0F0F0F0F, ah1.z, dhi);
+        dhi = dp4a((w1.w >> 4) & 0x0F0F0F0F, ah1.w, dhi);
+        sumi += sc[2 * g] * dlo + sc[2 * g + 1] * dhi;
+    }
+    int summ = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) summ += mn[j] * a.bs32[j];
+    float t1 = __fmul_rn(dw, a.d);
+    float t2 = __fmul_rn(__int2float_rn(sumi), t1);
+    float t3 = __fmul_rn(dminw, a.d);
+    float t4 = __fmul_rn(__int2float_rn(summ), t3);
+    return __fsub_rn(t2, t4);
+}
+
+// C4 for one Q6_K superblock.
+__device__ __forceinline__ float q6k_slot_dot(const uint8_t *tile, int S, int s, const ActBlock &a) {
+    const uint4 *base = reinterpret_cast<const uint4 *>(tile) + s;
+    uint16_t dbits = *reinterpret_cast<const uint16_t *>(tile + 13 * S * 16 + 2 * s);
+    float dw = __half2float(__ushort_as_half(dbits));
+    uint4 scv = base[12 * S];
+    const int8_t *sc = reinterpret_cast<const int8_t *>(&scv);
+    const int *aw = reinterpret_cast<const int *>(a.qs);
+    int acc[16];
+#pragma unroll
+    for (int i = 0; i < 16; i++) acc[i] = 0;
+#pragma unroll
+    for (int n = 0; n < 2; n++) {
+        uint4 qa0 = base[(4 * n + 0) * S], qa1 = base[(4 * n + 1) * S];  // ql bytes 64n .. 64n+31
+        uint4 qb0 = base[(4 * n + 2) * S], qb1 = base[(4 * n + 3) * S];  // ql bytes 64n+32 .. 64n+63
+        uint4 hh0 = base[(8 + 2 * n) * S], hh1 = base[(9 + 2 * n) * S];  // qh bytes 32n .. 32n+31
+        uint32_t wa[8] = {qa0.x, qa0.y, qa0.z, qa0.w, qa1.x, qa1.y, qa1.z, qa1.w};
+        uint32_t wb[8] = {qb0.x, qb0.y, qb0.z, qb0.w, qb1.x, qb1.y, qb1.z, qb1.w};
+        uint32_t wh[8] = {hh0.x, hh0.y, hh0.z, hh0.w, hh1.x, hh1.y, hh1.z, hh1.w};
+#pragma unroll
+        for (int l4 = 0; l4 < 8; l4++) {
+            uint32_t h = wh[l4];
+            int q1 = (int)__vsub4((wa[l4] & 0x0F0F0F0F) | ((h & 0x03030303) << 4), 0x20202020);
+            int q2 = (int)__vsub4((wb[l4] & 0x0F0F0F0F) | (((h >> 2) & 0x03030303) << 4), 0x20202020);
+            int q3 = (int)__vsub4(((wa[l4] >> 4) & 0x0F0F0F0F) | (((h >> 4) & 0x03030303) << 4), 0x20202020);
+            int q4 = (int)__vsub4(((wb[l4] >> 4) & 0x0F0F0F0F) | (((h >> 6) & 0x03030303) << 4), 0x20202020);
+            int sub = 8 * n + (l4 >> 2);
+            int v0 = 128 * n + 4 * l4;  // value index of q1's first byte
+            acc[sub + 0] = dp4a(q1, aw[(v0 + 0) / 4], acc[sub + 0]);
+            acc[sub + 2] = dp4a(q2, aw[(v0 + 32) / 4], acc[sub + 2]);
+            acc[sub + 4] = dp4a(q3, aw[(v0 + 64) / 4], acc[sub + 4]);
+            acc[sub + 6] = dp4a(q4, aw[(v0 + 96) / 4], acc[sub + 6]);
+        }
+    }
+    int sumi = 0;
+#pragma unroll
+    for (int i = 0; i < 16; i++) sumi += (int)sc[i] * acc[i];
+    return __fmul_rn(__int2float_rn(sumi), __fmul_rn(dw, a.d));
+}
+
+#endif  // __CUDACC__
+
+}  // namespace bt

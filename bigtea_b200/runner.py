@@ -1,0 +1,226 @@
+"""Host-side mirror of the reference's decode interface over the C ABI.
+
+`StreamingRunner.forward_cached(cache, tokens, pos_start)` and `KvCache` keep the names,
+argument meaning and error behaviour of core/arch/src/stream.rs:1933-1975 and
+core/arch/src/kv.rs:114-338, so callers (and tests) read like the reference's. Everything
+runs on the GPU through libbigtea_decode.so; there is no host compute path.
+"""
+from __future__ import annotations
+
+import ctypes as C
+
+import numpy as np
+
+from . import _lib
+from ._lib import BtError, check, lib
+from .models import Qwen3MoeConfig, synth_model, tensor_views
+
+
+class Engine:
+    """StreamingRunner::new + load_resident: the model resident in HBM on one GPU."""
+
+    def __init__(self, cfg: Qwen3MoeConfig, tensors: dict | None = None, *, seed: int | None = None,
+                 sigma: float = 0.02, device: int = 0):
+        self.cfg = cfg
+        self.h = C.c_void_p()
+        d = cfg.desc()
+        if tensors is not None:
+            arr, _keep = tensor_views(tensors)
+            check(lib.bt_engine_create(C.byref(d), arr, len(tensors), device, C.byref(self.h)))
+        else:
+            if seed is None:
+                raise ValueError("give tensors or a synthetic seed")
+            types = cfg.flat_layer_types()
+            check(lib.bt_engine_create_synthetic(C.byref(d), _lib.ptr(types, C.c_uint32), cfg.embd_type,
+                                                 cfg.out_type, seed, sigma, device, C.byref(self.h)))
+
+    @classmethod
+    def synthetic(cls, cfg: Qwen3MoeConfig, seed: int, sigma: float = 0.02, device: int = 0) -> "Engine":
+        return cls(cfg, seed=seed, sigma=sigma, device=device)
+
+    def close(self):
+        if self.h:
+            lib.bt_engine_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def stats(self) -> dict:
+        s = _lib.Stats()
+        check(lib.bt_engine_stats(self.h, C.byref(s)))
+        return {k: getattr(s, k) for k, _ in s._fields_}
+
+    def tensor_bytes(self, name: str, nbytes: int) -> np.ndarray:
+        out = np.empty(nbytes, dtype=np.uint8)
+        check(lib.bt_engine_tensor_bytes(self.h, name.encode(), _lib.ptr(out), nbytes))
+        return out
+
+    def set_option(self, name: str, value: int):
+        check(lib.bt_set_option(self.h, name.encode(), int(value)))
+
+    def debug_topk(self, layer: int, token: int):
+        K = self.cfg.n_expert_used
+        ids = np.empty(K, np.int32)
+        w = np.empty(K, np.float32)
+        check(lib.bt_debug_topk(self.h, layer, token, _lib.ptr(ids, C.c_int32), _lib.ptr(w, C.c_float)))
+        return ids, w
+
+    def debug_hidden(self, token: int) -> np.ndarray:
+        out = np.empty(self.cfg.n_embd, np.float32)
+        check(lib.bt_debug_hidden(self.h, token, _lib.ptr(out, C.c_float)))
+        return out
+
+
+class KvCache:
+    """KvCache over a paged device pool. Sequence 0 is the reference's single cache; the
+    others serve batched decode. Byte layouts follow kv.rs: [pos][n_kv_heads*head_dim] f16."""
+
+    def __init__(self, engine: Engine, max_positions: int, max_seqs: int = 1):
+        self.engine = engine
+        self.h = C.c_void_p()
+        self.max_positions = max_positions
+        self.max_seqs = max_seqs
+        check(lib.bt_kv_create(engine.h, _lib.KV_F16, max_seqs, max_positions, 16, C.byref(self.h)))
+
+    def close(self):
+        if self.h:
+            lib.bt_kv_destroy(self.h)
+            self.h = C.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def per_position(self) -> int:
+        c = self.engine.cfg
+        return c.n_head_kv * c.head_dim
+
+    def len(self, seq: int = 0) -> int:
+        n = C.c_uint32()
+        check(lib.bt_kv_len(self.h, seq, C.byref(n)))
+        return n.value
+
+    def is_empty(self, seq: int = 0) -> bool:
+        return self.len(seq) == 0
+
+    def bytes(self) -> int:
+        n = C.c_uint64()
+        check(lib.bt_kv_bytes(self.h, C.byref(n)))
+        return n.value
+
+    def clear(self, seq: int = 0):
+        check(lib.bt_kv_clear(self.h, seq))
+
+    def truncate_to(self, n: int, seq: int = 0):
+        check(lib.bt_kv_truncate(self.h, seq, n))
+
+    def shift_out(self, keep: int, drop: int, seq: int = 0):
+        check(lib.bt_kv_shift_out(self.h, seq, keep, drop))
+
+    def set_positions(self, n: int, seq: int = 0):
+        check(lib.bt_kv_set_positions(self.h, seq, n))
+
+    def is_consistent(self, seq: int = 0) -> bool:
+        ok = C.c_int()
+        check(lib.bt_kv_is_consistent(self.h, seq, C.byref(ok)))
+        return bool(ok.value)
+
+    def _export(self, layer: int, seq: int, n_pos: int):
+        nb = n_pos * self.per_position * 2
+        k = np.empty(nb, np.uint8)
+        v = np.empty(nb, np.uint8)
+        check(lib.bt_kv_export_layer(self.h, seq, layer, _lib.ptr(k), _lib.ptr(v), nb))
+        return k, v
+
+    def keys(self, layer: int, seq: int = 0, n_pos: int | None = None) -> np.ndarray:
+        return self._export(layer, seq, self.len(seq) if n_pos is None else n_pos)[0]
+
+    def values(self, layer: int, seq: int = 0, n_pos: int | None = None) -> np.ndarray:
+        return self._export(layer, seq, self.len(seq) if n_pos is None else n_pos)[1]
+
+    def layer_bytes(self, layer: int, seq: int = 0, n_pos: int | None = None):
+        return self._export(layer, seq, self.len(seq) if n_pos is None else n_pos)
+
+    def restore_layer(self, layer: int, k: np.ndarray, v: np.ndarray, seq: int = 0):
+        k = np.ascontiguousarray(k).view(np.uint8)
+        v = np.ascontiguousarray(v).view(np.uint8)
+        if k.nbytes != v.nbytes:
+            raise BtError(_lib.BT_ERR_KV, "k and v differ in size")
+        check(lib.bt_kv_import_layer(self.h, seq, layer, _lib.ptr(k), _lib.ptr(v), k.nbytes))
+
+
+def _u32(a) -> np.ndarray:
+    return np.ascontiguousarray(np.asarray(a, dtype=np.uint32))
+
+
+class StreamingRunner:
+    """forward_cached over the device engine (stream.rs:1933-1975)."""
+
+    def __init__(self, engine: Engine):
+        self.engine = engine
+
+    def forward_cached(self, cache: KvCache, tokens, pos_start: int, seq: int = 0) -> np.ndarray:
+        """One step of `tokens` at `pos_start` for sequence `seq`: logits of the last position."""
+        return self.forward_batch(cache, [seq], [list(tokens)], [pos_start])[0]
+
+    def forward_batch(self, cache: KvCache, seqs, token_lists, pos_starts) -> np.ndarray:
+        V = self.engine.cfg.n_vocab
+        toks = _u32([t for tl in token_lists for t in tl])
+        n = _u32([len(tl) for tl in token_lists])
+        s = _u32(seqs)
+        ps = _u32(pos_starts)
+        out = np.empty((len(seqs), V), np.float32)
+        check(lib.bt_forward(self.engine.h, cache.h, _lib.ptr(s, C.c_uint32), _lib.ptr(toks, C.c_uint32),
+                             _lib.ptr(n, C.c_uint32), _lib.ptr(ps, C.c_uint32), len(seqs),
+                             _lib.ptr(out, C.c_float)))
+        return out
+
+    def generate_greedy(self, cache: KvCache, first_tokens, n_steps: int, seqs=None, want_logits: bool = False):
+        """The chaos-run temp-0 loop on the device; returns tokens [n_steps, n_seqs]."""
+        first = _u32(first_tokens)
+        seqs = _u32(range(len(first)) if seqs is None else seqs)
+        out = np.empty((n_steps, len(first)), np.uint32)
+        logits = np.empty((len(first), self.engine.cfg.n_vocab), np.float32) if want_logits else None
+        check(lib.bt_generate_greedy(self.engine.h, cache.h, _lib.ptr(seqs, C.c_uint32), _lib.ptr(first, C.c_uint32),
+                                     len(first), n_steps, _lib.ptr(out, C.c_uint32),
+                                     _lib.ptr(logits, C.c_float) if want_logits else None))
+        return (out, logits) if want_logits else out
+
+    def last_device_ms(self) -> float:
+        ms = C.c_double()
+        check(lib.bt_last_device_ms(self.engine.h, C.byref(ms)))
+        return ms.value
+
+    def profile_decode(self, cache: KvCache, first_tokens, n_steps: int, seqs=None) -> dict:
+        first = _u32(first_tokens)
+        seqs = _u32(range(len(first)) if seqs is None else seqs)
+        arr = (_lib.KernelTime * 32)()
+        n = C.c_uint32()
+        check(lib.bt_profile_decode(self.engine.h, cache.h, _lib.ptr(seqs, C.c_uint32), _lib.ptr(first, C.c_uint32),
+                                    len(first), n_steps, arr, 32, C.byref(n)))
+        return {arr[i].name.decode(): (arr[i].launches, arr[i].total_ms) for i in range(min(n.value, 32))}
+
+
+def dequantize(ggml_type: int, data: np.ndarray, n: int) -> np.ndarray:
+    """dequantize() (core/ggml/src/lib.rs:233-290) through the device kernels."""
+    out = np.empty(n, np.float32)
+    data = np.ascontiguousarray(data).view(np.uint8)
+    check(lib.bt_debug_dequant(ggml_type, _lib.ptr(data), n, _lib.ptr(out, C.c_float)))
+    return out
+
+
+def gemv(ggml_type: int, w: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+    """One quantised mul_mat on the device: y[t, r] = W[r, :] . x[t, :]."""
+    x = np.ascontiguousarray(np.atleast_2d(x), dtype=np.float32)
+    T = x.shape[0]
+    y = np.empty((T, rows), np.float32)
+    w = np.ascontiguousarray(w).view(np.uint8)
+    check(lib.bt_op_gemv(ggml_type, _lib.ptr(w), rows, cols, _lib.ptr(x, C.c_float), T, _lib.ptr(y, C.c_float)))
+    return y

@@ -1,0 +1,169 @@
+/*
+ * bigtea_decode.h -- C ABI of the B200 decode-step layer.
+ *
+ * Drop-in for the qwen3moe decode path of Chaos (aturzone/Bigtea). Every entry point
+ * names the reference interface it replaces (paths relative to the Chaos tree).
+ * Conventions: every call returns BT_OK (0) or a bt_status; on failure
+ * bt_last_error() holds a message for the calling thread. Nothing aborts. Handles are
+ * opaque; one engine is driven from one thread at a time (the reference's
+ * StreamingRunner is `&mut self`, core/arch/src/stream.rs:1933). Output buffers are
+ * caller-owned host memory unless a name says otherwise.
+ */
+#ifndef BIGTEA_DECODE_H
+#define BIGTEA_DECODE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BT_ABI_VERSION 1
+
+typedef enum {
+    BT_OK = 0,
+    BT_ERR_INVALID = 1,        /* bad argument, shape or state */
+    BT_ERR_CUDA = 2,           /* a CUDA runtime call failed */
+    BT_ERR_OOM = 3,            /* device or pinned-host allocation failed */
+    BT_ERR_MISSING_TENSOR = 4, /* ArchError::MissingTensor, core/arch/src/lib.rs */
+    BT_ERR_KV = 5,             /* KvError::WrongSize and capacity, core/arch/src/kv.rs:171-178 */
+    BT_ERR_TIMEOUT = 6,        /* a bounded device wait ran out; the context stays usable */
+    BT_ERR_UNSUPPORTED = 7     /* a tensor type or shape this build has no kernel for */
+} bt_status;
+
+/* ggml type ids (core/gguf/src/tensor.rs:18-57) accepted by this build */
+enum { BT_TYPE_F32 = 0, BT_TYPE_F16 = 1, BT_TYPE_Q4_K = 12, BT_TYPE_Q6_K = 14 };
+/* KvType (core/arch/src/kv.rs:44-55); only F16 is on the device path */
+enum { BT_KV_F16 = 1 };
+
+/* Qwen3Config fields the decode layer reads (core/arch/src/qwen3.rs:565-844). */
+typedef struct {
+    uint32_t n_layer, n_embd, n_head, n_head_kv, head_dim;
+    uint32_t n_expert, n_expert_used, n_ff_exp, n_vocab, n_rot;
+    float rms_eps, rope_freq_base;
+    /* CHAOS_EXPERT_WORKERS (stream.rs:1305-1312, default 4): fixes the order in which
+     * one position's expert outputs are summed. */
+    uint32_t expert_workers;
+    /* longest sequence the RoPE table covers (positions 0..max_positions-1) */
+    uint32_t max_positions;
+} bt_model_desc;
+
+/* One GGUF tensor as Model::read_tensor returns it (core/model/src/lib.rs:390-470):
+ * ggml dims (ne[0] innermost) and host bytes. The engine copies the bytes to HBM
+ * during bt_engine_create; the caller may free them afterwards. */
+typedef struct {
+    const char *name;
+    uint32_t type;
+    uint32_t n_dims;
+    uint64_t ne[4];
+    const void *data;
+    uint64_t nbytes;
+} bt_tensor_view;
+
+typedef struct bt_engine bt_engine;
+typedef struct bt_kv bt_kv;
+
+/* Phase timers, the device analogue of StreamStats (stream.rs:134-194). */
+typedef struct {
+    uint64_t forward_calls;
+    uint64_t tokens;
+    double forward_seconds;     /* host wall time inside bt_forward / bt_generate_greedy */
+    uint64_t weight_bytes;      /* bytes of weights resident in HBM */
+    uint64_t graph_replays;     /* decode steps served from a captured CUDA graph */
+} bt_stats;
+
+const char *bt_last_error(void);
+int bt_abi_version(void);
+
+/* StreamingRunner::new + load_resident (stream.rs:586, 1793-1876): upload every tensor
+ * (experts included: the model is HBM-resident) and build the kernels' layouts.
+ * `device` is a CUDA ordinal. */
+int bt_engine_create(const bt_model_desc *desc, const bt_tensor_view *tensors, size_t n_tensors,
+                     int device, bt_engine **out);
+/* Same engine with seeded synthetic weights generated on the device (N(0, sigma)
+ * quantised to each tensor's type; norms 1 + N(0, sigma)). `types` gives, per layer,
+ * the ggml types of attn_q, attn_k, attn_v, attn_output, ffn_gate_exps, ffn_up_exps,
+ * ffn_down_exps (7 entries per layer); token_embd and output use `embd_type`/`out_type`.
+ * The bytes are identical to bt_synth_tensor's for the same seed and tensor id. */
+int bt_engine_create_synthetic(const bt_model_desc *desc, const uint32_t *types, uint32_t embd_type,
+                               uint32_t out_type, uint64_t seed, float sigma, int device,
+                               bt_engine **out);
+void bt_engine_destroy(bt_engine *e);
+int bt_engine_stats(const bt_engine *e, bt_stats *out);
+/* copy a resident tensor's GGUF bytes back to the host (for a CPU check of synthetic weights) */
+int bt_engine_tensor_bytes(const bt_engine *e, const char *name, void *host_out, uint64_t nbytes);
+
+/* KvCache::with_type (kv.rs:114-160) as a paged device pool: `max_seqs` sequences of up to
+ * `max_positions` positions each, `block_tokens` (16) positions per page. */
+int bt_kv_create(bt_engine *e, uint32_t kind, uint32_t max_seqs, uint32_t max_positions,
+                 uint32_t block_tokens, bt_kv **out);
+void bt_kv_destroy(bt_kv *kv);
+int bt_kv_len(const bt_kv *kv, uint32_t seq, uint32_t *len);                 /* kv.rs:151-153 */
+int bt_kv_clear(bt_kv *kv, uint32_t seq);                                    /* kv.rs:232-238 */
+int bt_kv_truncate(bt_kv *kv, uint32_t seq, uint32_t n);                     /* kv.rs:280-292 */
+int bt_kv_shift_out(bt_kv *kv, uint32_t seq, uint32_t keep, uint32_t drop);  /* kv.rs:314-328 */
+int bt_kv_set_positions(bt_kv *kv, uint32_t seq, uint32_t n);                /* kv.rs:270-272 */
+int bt_kv_bytes(const bt_kv *kv, uint64_t *bytes);                          /* kv.rs:162-166 */
+int bt_kv_is_consistent(const bt_kv *kv, uint32_t seq, int *consistent);     /* kv.rs:330-338 */
+/* keys()/values() of one layer in the kv.rs byte layout ([pos][n_head_kv*head_dim] f16),
+ * `bytes` = positions * n_head_kv * head_dim * 2 for each of k and v (kv.rs:222-228). */
+int bt_kv_export_layer(const bt_kv *kv, uint32_t seq, uint32_t layer, void *k_out, void *v_out,
+                       uint64_t bytes);
+/* restore_layer (kv.rs:252-264): replaces the layer's positions with `bytes` of k and v. */
+int bt_kv_import_layer(bt_kv *kv, uint32_t seq, uint32_t layer, const void *k, const void *v,
+                       uint64_t bytes);
+
+/* StreamingRunner::forward_cached (stream.rs:1933-1975), batched over sequences.
+ * Sequence i appends n_tokens[i] tokens (tokens are concatenated in `tokens`) at
+ * pos_start[i], which must equal that sequence's cache length. Writes the logits of
+ * each sequence's last token to logits_out[i * n_vocab ...] (host). */
+int bt_forward(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const uint32_t *tokens,
+               const uint32_t *n_tokens, const uint32_t *pos_start, uint32_t n_seqs,
+               float *logits_out);
+/* The chaos-run greedy decode loop (cli/run/src/main.rs:3914-4070, temp 0, argmax of
+ * core/arch/src/sample.rs:928-935) run on the device: starting from `first_tokens`
+ * (one per sequence, not yet in the cache), runs n_steps single-token steps and writes
+ * the n_steps tokens each step produced to tokens_out[step * n_seqs + i]. The last
+ * step's logits go to last_logits (n_seqs * n_vocab, may be NULL). */
+int bt_generate_greedy(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const uint32_t *first_tokens,
+                       uint32_t n_seqs, uint32_t n_steps, uint32_t *tokens_out, float *last_logits);
+
+/* Device time (CUDA events on the engine stream) of the last bt_generate_greedy replay loop. */
+int bt_last_device_ms(const bt_engine *e, double *ms);
+
+/* StreamStats-style per-kernel timing (stream.rs:134-194): runs n_steps greedy steps with
+ * serialised launches, each bracketed by CUDA events; fills one entry per kernel kind. */
+typedef struct {
+    char name[32];
+    uint64_t launches;
+    double total_ms;
+} bt_kernel_time;
+int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const uint32_t *first_tokens,
+                      uint32_t n_seqs, uint32_t n_steps, bt_kernel_time *out, uint32_t max_out, uint32_t *n_out);
+/* Engine switches: "pdl" (programmatic dependent launch between the step's kernels, default 1). */
+int bt_set_option(bt_engine *e, const char *name, int value);
+
+/* ---- parity hooks: each runs one device kernel on host buffers ---- */
+/* dequantize() (core/ggml/src/lib.rs:233-290): n values of `type` through the device layout */
+int bt_debug_dequant(uint32_t type, const void *bytes, uint64_t n, float *out);
+/* route() result of the last bt_forward for one layer and token index (stream.rs:869-888):
+ * ids in descending probability, renormalised weights */
+int bt_debug_topk(const bt_engine *e, uint32_t layer, uint32_t token, int32_t *ids, float *weights);
+/* residual stream after the last layer, last bt_forward, token index `token` (n_embd floats) */
+int bt_debug_hidden(const bt_engine *e, uint32_t token, float *out);
+/* one quantised mul_mat (graph.rs:690): y[t][r] = W[r,:] . x[t,:] for T tokens */
+int bt_op_gemv(uint32_t type, const void *w_bytes, uint32_t rows, uint32_t cols, const float *x,
+               uint32_t T, float *y);
+
+/* ---- synthetic weights (seeded; same bytes on host and device) ---- */
+/* fill `out` (rows * row_bytes) with N(mean, sigma) values quantised to `type` */
+int bt_synth_tensor(uint32_t type, uint64_t rows, uint64_t cols, uint64_t seed, uint64_t tensor_id,
+                    float mean, float sigma, void *out);
+/* the tensor id bt_engine_create_synthetic uses for a tensor name (64-bit FNV-1a) */
+uint64_t bt_tensor_id(const char *name);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

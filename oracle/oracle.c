@@ -1,0 +1,798 @@
+/*
+ * oracle.c -- CPU restatement of the Chaos decode-step layer (TEST INFRASTRUCTURE).
+ *
+ * Loaded only by tests/, __graft_entry__.smoke() and bench.py's CPU legs. See
+ * oracle.h for what is restated from where. Build: oracle/Makefile (gcc, OpenMP,
+ * -ffp-contract=off so that no multiply-add is fused unless written as fmaf).
+ *
+ * ARITHMETIC CONTRACT (shared with bigtea_b200/csrc; every item is exact IEEE-754
+ * single precision with round-to-nearest-even unless stated):
+ *  C1 f16: f32->f16 rounds to nearest even, f16->f32 exact.
+ *  C2 dequant: Q4_K y = (d*sc)*q - (dmin*m); Q6_K y = (d*sc)*q  (gguf-py order).
+ *  C3 Q8_K activations: per 256 values, amax/first-occurrence signed max mx,
+ *     iscale = -127/mx, q = min(127, rint(iscale*x)), d = 1/iscale, bsums over 16.
+ *  C4 K-quant row dot: per superblock an exact int32 sum, then
+ *     Q4_K sb = (float)sumi*(dw*dx) - (float)summ*(dminw*dx), Q6_K sb = (float)sumi*(dw*dx);
+ *     row = ((0 + sb0) + sb1) + ... in superblock order.
+ *  C5 P2 reduction (norms, router dot, softmax sum): lane l of 32 accumulates elements
+ *     l, l+32, ... in order (fmaf for products), then an xor butterfly 16,8,4,2,1.
+ *  C6 RMSNorm: mean = P2(x*x)/n; s = 1/sqrt(mean+eps); y = (x*s)*w.
+ *  C7 exp: or_exp below (Cody-Waite reduction by ln2, degree-7 Taylor, Horner in fmaf).
+ *  C8 attention: q rounded to f16; s = fmaf-sequential dot over d, times scale;
+ *     keys in chunks of `chunk`; per chunk m = max s, p = exp(s-m), l = P3 sum (32-lane
+ *     butterflies per 32 keys, warps summed in order from 0), acc = fmaf-sequential p*v;
+ *     combine chunks in order: f = exp(m_c - M), L = fmaf(l_c,f,L), O = fmaf(acc_c,f,O),
+ *     out = O/L.
+ *  C9 RoPE: NeoX pairs (i, i+n_rot/2); theta_0 = pos, theta_{i+1} = theta_i*powf(base,-2/n_rot);
+ *     cos/sin from libm on the host (a table); x0' = x0*c - x1*s, x1' = x0*s + x1*c.
+ */
+#include "oracle.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+#ifdef _OPENMP
+#include <omp.h>
+#endif
+
+static __thread char g_err[512];
+static void set_err(const char *msg) { snprintf(g_err, sizeof g_err, "%s", msg); }
+const char *or_last_error(void) { return g_err; }
+
+int or_set_threads(int n) {
+#ifdef _OPENMP
+    if (n > 0) omp_set_num_threads(n);
+    return omp_get_max_threads();
+#else
+    (void)n;
+    return 1;
+#endif
+}
+
+/* ------------------------------------------------------------------ C1 f16 */
+uint16_t or_f32_to_f16(float f) {
+    uint32_t x;
+    memcpy(&x, &f, 4);
+    uint32_t sign = (x >> 16) & 0x8000u;
+    uint32_t e8 = (x >> 23) & 0xffu;
+    uint32_t mant = x & 0x7fffffu;
+    if (e8 == 0xffu) return (uint16_t)(sign | 0x7c00u | (mant ? 0x200u : 0u));
+    int e = (int)e8 - 127 + 15;
+    if (e >= 31) return (uint16_t)(sign | 0x7c00u);
+    if (e <= 0) {
+        if (e < -10) return (uint16_t)sign;
+        mant |= 0x800000u;
+        int shift = 14 - e;
+        uint32_t h = mant >> shift;
+        uint32_t rem = mant & ((1u << shift) - 1u);
+        uint32_t mid = 1u << (shift - 1);
+        if (rem > mid || (rem == mid && (h & 1u))) h++;
+        return (uint16_t)(sign | h);
+    }
+    uint32_t h = sign | ((uint32_t)e << 10) | (mant >> 13);
+    uint32_t rem = mant & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h++;
+    return (uint16_t)h;
+}
+
+float or_f16_to_f32(uint16_t h) {
+    uint32_t sign = ((uint32_t)h & 0x8000u) << 16;
+    uint32_t e = ((uint32_t)h >> 10) & 0x1fu;
+    uint32_t m = (uint32_t)h & 0x3ffu;
+    uint32_t bits;
+    if (e == 0) {
+        if (m == 0) {
+            bits = sign;
+        } else {
+            /* subnormal: renormalise */
+            int sh = 0;
+            while (!(m & 0x400u)) {
+                m <<= 1;
+                sh++;
+            }
+            m &= 0x3ffu;
+            bits = sign | ((uint32_t)(127 - 15 + 1 - sh) << 23) | (m << 13);
+        }
+    } else if (e == 31) {
+        bits = sign | 0x7f800000u | (m << 13);
+    } else {
+        bits = sign | ((e + 112u) << 23) | (m << 13);
+    }
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+/* ------------------------------------------------------------------ C7 exp */
+static float pow2i(int n) { /* 2^n for n in [-126, 127] */
+    uint32_t bits = (uint32_t)(n + 127) << 23;
+    float f;
+    memcpy(&f, &bits, 4);
+    return f;
+}
+
+float or_exp(float x) {
+    if (!(x < 88.72283935546875f)) return (x != x) ? x : INFINITY;
+    if (x < -103.972084045410156f) return 0.0f;
+    float n = rintf(x * 1.44269502162933349609375f);
+    float r = fmaf(n, -0.693145751953125f, x);
+    r = fmaf(n, -1.428606765330187045e-06f, r);
+    float p = 1.98412698e-4f; /* 1/5040 */
+    p = fmaf(p, r, 1.38888889e-3f); /* 1/720 */
+    p = fmaf(p, r, 8.33333333e-3f); /* 1/120 */
+    p = fmaf(p, r, 4.16666667e-2f); /* 1/24 */
+    p = fmaf(p, r, 1.66666667e-1f); /* 1/6 */
+    p = fmaf(p, r, 0.5f);
+    p = fmaf(p, r, 1.0f);
+    p = fmaf(p, r, 1.0f);
+    int ni = (int)n;
+    if (ni > 127) return (p * pow2i(127)) * pow2i(ni - 127);
+    if (ni < -126) return (p * pow2i(ni + 64)) * pow2i(-64);
+    return p * pow2i(ni);
+}
+
+float or_silu(float x) { return x / (1.0f + or_exp(-x)); }
+
+/* ------------------------------------------------------------------ formats */
+int64_t or_row_bytes(int type, int64_t n) {
+    switch (type) {
+    case OR_F32: return n * 4;
+    case OR_F16: return n * 2;
+    case OR_Q4_K: return (n % 256) ? -1 : n / 256 * 144;
+    case OR_Q6_K: return (n % 256) ? -1 : n / 256 * 210;
+    default: return -1;
+    }
+}
+
+static inline uint16_t rd16(const uint8_t *p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+/* get_scale_min_k4: 6-bit scale and min of sub-block j from the 12 packed bytes */
+static inline void q4k_scale_min(const uint8_t *s, int j, int *sc, int *m) {
+    if (j < 4) {
+        *sc = s[j] & 63;
+        *m = s[j + 4] & 63;
+    } else {
+        *sc = (s[j + 4] & 0xF) | ((s[j - 4] >> 6) << 4);
+        *m = (s[j + 4] >> 4) | ((s[j] >> 6) << 4);
+    }
+}
+
+static void dequant_q4k_block(const uint8_t *b, float *y) {
+    float d = or_f16_to_f32(rd16(b));
+    float dmin = or_f16_to_f32(rd16(b + 2));
+    const uint8_t *sc = b + 4, *qs = b + 16;
+    for (int g = 0; g < 4; g++) {
+        int s0, m0, s1, m1;
+        q4k_scale_min(sc, 2 * g, &s0, &m0);
+        q4k_scale_min(sc, 2 * g + 1, &s1, &m1);
+        float d0 = d * (float)s0, mm0 = dmin * (float)m0;
+        float d1 = d * (float)s1, mm1 = dmin * (float)m1;
+        for (int l = 0; l < 32; l++) {
+            y[64 * g + l] = d0 * (float)(qs[32 * g + l] & 0xF) - mm0;
+            y[64 * g + 32 + l] = d1 * (float)(qs[32 * g + l] >> 4) - mm1;
+        }
+    }
+}
+
+/* Q6_K value i of a block as a signed 6-bit integer in [-32, 31] */
+static inline int q6k_value(const uint8_t *b, int i) {
+    const uint8_t *ql = b, *qh = b + 128;
+    int n = i / 128, r = i % 128, quad = r / 32, l = r % 32;
+    int lo;
+    if (quad == 0) lo = ql[64 * n + l] & 0xF;
+    else if (quad == 1) lo = ql[64 * n + 32 + l] & 0xF;
+    else if (quad == 2) lo = ql[64 * n + l] >> 4;
+    else lo = ql[64 * n + 32 + l] >> 4;
+    int hi = (qh[32 * n + l] >> (2 * quad)) & 3;
+    return (lo | (hi << 4)) - 32;
+}
+
+static void dequant_q6k_block(const uint8_t *b, float *y) {
+    float d = or_f16_to_f32(rd16(b + 208));
+    const int8_t *sc = (const int8_t *)(b + 192);
+    for (int i = 0; i < 256; i++) y[i] = (d * (float)sc[i / 16]) * (float)q6k_value(b, i);
+}
+
+int or_dequant(int type, const void *src, int64_t n, float *dst) {
+    const uint8_t *s = (const uint8_t *)src;
+    switch (type) {
+    case OR_F32: memcpy(dst, src, (size_t)n * 4); return 0;
+    case OR_F16:
+        for (int64_t i = 0; i < n; i++) dst[i] = or_f16_to_f32(rd16(s + 2 * i));
+        return 0;
+    case OR_Q4_K:
+        if (n % 256) return -1;
+        for (int64_t b = 0; b < n / 256; b++) dequant_q4k_block(s + 144 * b, dst + 256 * b);
+        return 0;
+    case OR_Q6_K:
+        if (n % 256) return -1;
+        for (int64_t b = 0; b < n / 256; b++) dequant_q6k_block(s + 210 * b, dst + 256 * b);
+        return 0;
+    default: return -1;
+    }
+}
+
+/* ------------------------------------------------------------------ C3 Q8_K */
+void or_quantize_q8k(const float *x, int64_t n, or_block_q8k *y) {
+    for (int64_t b = 0; b < n / 256; b++) {
+        const float *xb = x + 256 * b;
+        or_block_q8k *yb = y + b;
+        float amax = 0.0f, mx = 0.0f;
+        for (int j = 0; j < 256; j++) {
+            float ax = fabsf(xb[j]);
+            if (ax > amax) {
+                amax = ax;
+                mx = xb[j];
+            }
+        }
+        if (amax == 0.0f) {
+            yb->d = 0.0f;
+            memset(yb->qs, 0, 256);
+            memset(yb->bsums, 0, sizeof yb->bsums);
+            continue;
+        }
+        float iscale = -127.0f / mx;
+        for (int j = 0; j < 256; j++) {
+            int v = (int)rintf(iscale * xb[j]);
+            yb->qs[j] = (int8_t)(v > 127 ? 127 : v);
+        }
+        for (int j = 0; j < 16; j++) {
+            int s = 0;
+            for (int i = 0; i < 16; i++) s += yb->qs[16 * j + i];
+            yb->bsums[j] = (int16_t)s;
+        }
+        yb->d = 1.0f / iscale;
+    }
+}
+
+/* ------------------------------------------------------------------ C4 dots */
+static float dot_q4k_row(const uint8_t *row, const or_block_q8k *a, int nsb) {
+    float acc = 0.0f;
+    for (int b = 0; b < nsb; b++) {
+        const uint8_t *blk = row + 144 * b;
+        const or_block_q8k *ab = a + b;
+        float dw = or_f16_to_f32(rd16(blk)), dminw = or_f16_to_f32(rd16(blk + 2));
+        const uint8_t *sc = blk + 4, *qs = blk + 16;
+        int32_t sumi = 0, summ = 0;
+        for (int g = 0; g < 4; g++) {
+            int s0, m0, s1, m1;
+            q4k_scale_min(sc, 2 * g, &s0, &m0);
+            q4k_scale_min(sc, 2 * g + 1, &s1, &m1);
+            int32_t dlo = 0, dhi = 0;
+            for (int l = 0; l < 32; l++) {
+                dlo += (qs[32 * g + l] & 0xF) * ab->qs[64 * g + l];
+                dhi += (qs[32 * g + l] >> 4) * ab->qs[64 * g + 32 + l];
+            }
+            sumi += s0 * dlo + s1 * dhi;
+            summ += m0 * (ab->bsums[4 * g] + ab->bsums[4 * g + 1]);
+            summ += m1 * (ab->bsums[4 * g + 2] + ab->bsums[4 * g + 3]);
+        }
+        float t1 = dw * ab->d;
+        float t2 = (float)sumi * t1;
+        float t3 = dminw * ab->d;
+        float t4 = (float)summ * t3;
+        acc = acc + (t2 - t4);
+    }
+    return acc;
+}
+
+static float dot_q6k_row(const uint8_t *row, const or_block_q8k *a, int nsb) {
+    float acc = 0.0f;
+    for (int b = 0; b < nsb; b++) {
+        const uint8_t *blk = row + 210 * b;
+        const or_block_q8k *ab = a + b;
+        const int8_t *sc = (const int8_t *)(blk + 192);
+        float dw = or_f16_to_f32(rd16(blk + 208));
+        int32_t sumi = 0;
+        for (int s = 0; s < 16; s++) {
+            int32_t d = 0;
+            for (int i = 0; i < 16; i++) d += q6k_value(blk, 16 * s + i) * ab->qs[16 * s + i];
+            sumi += sc[s] * d;
+        }
+        acc = acc + (float)sumi * (dw * ab->d);
+    }
+    return acc;
+}
+
+static void butterfly32(float v[32]) {
+    for (int o = 16; o >= 1; o >>= 1) {
+        float t[32];
+        for (int l = 0; l < 32; l++) t[l] = v[l] + v[l ^ o];
+        memcpy(v, t, sizeof t);
+    }
+}
+
+float or_dot_p2(const float *a, const float *b, int n) {
+    float lane[32];
+    for (int l = 0; l < 32; l++) {
+        float acc = 0.0f;
+        for (int i = l; i < n; i += 32) acc = fmaf(a[i], b[i], acc);
+        lane[l] = acc;
+    }
+    butterfly32(lane);
+    return lane[0];
+}
+
+float or_sumsq_p2(const float *x, int n) { return or_dot_p2(x, x, n); }
+
+static float sum_p2(const float *x, int n) {
+    float lane[32];
+    for (int l = 0; l < 32; l++) {
+        float acc = 0.0f;
+        for (int i = l; i < n; i += 32) acc = acc + x[i];
+        lane[l] = acc;
+    }
+    butterfly32(lane);
+    return lane[0];
+}
+
+int or_gemv(int type, const void *W, int64_t rows, int64_t cols, const float *x, float *y) {
+    const uint8_t *w = (const uint8_t *)W;
+    if (type == OR_F32) {
+#pragma omp parallel for schedule(static)
+        for (int64_t r = 0; r < rows; r++) y[r] = or_dot_p2((const float *)(w + r * cols * 4), x, (int)cols);
+        return 0;
+    }
+    if ((type != OR_Q4_K && type != OR_Q6_K) || cols % 256) return -1;
+    int nsb = (int)(cols / 256);
+    or_block_q8k *a = (or_block_q8k *)malloc(sizeof(or_block_q8k) * (size_t)nsb);
+    or_quantize_q8k(x, cols, a);
+    int64_t rb = or_row_bytes(type, cols);
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++)
+        y[r] = (type == OR_Q4_K) ? dot_q4k_row(w + r * rb, a, nsb) : dot_q6k_row(w + r * rb, a, nsb);
+    free(a);
+    return 0;
+}
+
+/* ------------------------------------------------------------------ C6 norm */
+void or_rmsnorm(const float *x, const float *w, int n, float eps, float *y) {
+    float mean = or_sumsq_p2(x, n) / (float)n;
+    float s = 1.0f / sqrtf(mean + eps);
+    for (int i = 0; i < n; i++) y[i] = (x[i] * s) * w[i];
+}
+
+/* ------------------------------------------------------------------ C9 rope */
+void or_rope_table(int n_pos, int n_rot, float base, float *cs) {
+    float theta_scale = powf(base, -2.0f / (float)n_rot);
+    for (int p = 0; p < n_pos; p++) {
+        float theta = (float)p;
+        float *row = cs + (size_t)p * n_rot;
+        for (int i = 0; i < n_rot / 2; i++) {
+            row[2 * i] = cosf(theta);
+            row[2 * i + 1] = sinf(theta);
+            theta *= theta_scale;
+        }
+    }
+}
+
+void or_rope_neox(float *x, int n_rot, const float *cs) {
+    int h = n_rot / 2;
+    for (int i = 0; i < h; i++) {
+        float c = cs[2 * i], s = cs[2 * i + 1];
+        float x0 = x[i], x1 = x[i + h];
+        float a = x0 * c, b = x1 * s, e = x0 * s, f = x1 * c;
+        x[i] = a - b;
+        x[i + h] = e + f;
+    }
+}
+
+/* ------------------------------------------------------------------ router */
+void or_softmax(const float *logits, int n, float *probs) {
+    float m = -INFINITY;
+    for (int i = 0; i < n; i++) m = logits[i] > m ? logits[i] : m;
+    for (int i = 0; i < n; i++) probs[i] = or_exp(logits[i] - m);
+    float s = sum_p2(probs, n);
+    float inv = 1.0f / s;
+    for (int i = 0; i < n; i++) probs[i] = probs[i] * inv;
+}
+
+/* f32::total_cmp as a signed integer key */
+static inline int32_t total_key(float f) {
+    int32_t b;
+    memcpy(&b, &f, 4);
+    b ^= (int32_t)(((uint32_t)(b >> 31)) >> 1);
+    return b;
+}
+
+void or_route(const float *probs, int n, int k, int32_t *ids, float *weights) {
+    /* stable sort descending by total_cmp == rank by (key desc, index asc) */
+    int taken = 0;
+    int32_t *order = (int32_t *)malloc(sizeof(int32_t) * (size_t)n);
+    for (int i = 0; i < n; i++) order[i] = i;
+    for (int i = 1; i < n; i++) { /* insertion sort: stable */
+        int32_t v = order[i];
+        int j = i - 1;
+        while (j >= 0 && total_key(probs[order[j]]) < total_key(probs[v])) {
+            order[j + 1] = order[j];
+            j--;
+        }
+        order[j + 1] = v;
+    }
+    if (k > n) k = n;
+    float total = 0.0f;
+    for (int i = 0; i < k; i++) {
+        ids[i] = order[i];
+        weights[i] = probs[order[i]];
+        total = total + weights[i];
+        taken++;
+    }
+    if (total > 0.0f)
+        for (int i = 0; i < taken; i++) weights[i] = weights[i] / total;
+    free(order);
+}
+
+uint32_t or_argmax(const float *logits, int64_t n) {
+    if (n <= 0) return 0;
+    int64_t best = 0;
+    int32_t bk = total_key(logits[0]);
+    for (int64_t i = 1; i < n; i++) {
+        int32_t k = total_key(logits[i]);
+        if (k >= bk) { /* max_by keeps the last of equal maxima */
+            bk = k;
+            best = i;
+        }
+    }
+    return (uint32_t)best;
+}
+
+/* ------------------------------------------------------------------ C8 attention */
+void or_attn_head(const float *q, const uint16_t *k, const uint16_t *v, int64_t ld, int nk,
+                  int head_dim, float scale, int chunk, float *out) {
+    float qf[512];
+    for (int d = 0; d < head_dim; d++) qf[d] = or_f16_to_f32(or_f32_to_f16(q[d]));
+    int nc = (nk + chunk - 1) / chunk;
+    float *mc = (float *)malloc(sizeof(float) * (size_t)nc);
+    float *lc = (float *)malloc(sizeof(float) * (size_t)nc);
+    float *ac = (float *)calloc((size_t)nc * head_dim, sizeof(float));
+    float *s = (float *)malloc(sizeof(float) * (size_t)chunk);
+    float *p = (float *)malloc(sizeof(float) * (size_t)chunk);
+    for (int c = 0; c < nc; c++) {
+        int base = c * chunk, cnt = nk - base < chunk ? nk - base : chunk;
+        float m = -INFINITY;
+        for (int j = 0; j < cnt; j++) {
+            const uint16_t *kr = k + (int64_t)(base + j) * ld;
+            float acc = 0.0f;
+            for (int d = 0; d < head_dim; d++) acc = fmaf(qf[d], or_f16_to_f32(kr[d]), acc);
+            s[j] = acc * scale;
+            m = s[j] > m ? s[j] : m;
+        }
+        for (int j = 0; j < chunk; j++) p[j] = j < cnt ? or_exp(s[j] - m) : 0.0f;
+        float l = 0.0f;
+        for (int w = 0; w < chunk / 32; w++) {
+            float lane[32];
+            memcpy(lane, p + 32 * w, sizeof lane);
+            butterfly32(lane);
+            l = l + lane[0];
+        }
+        float *a = ac + (size_t)c * head_dim;
+        for (int j = 0; j < cnt; j++) {
+            const uint16_t *vr = v + (int64_t)(base + j) * ld;
+            for (int d = 0; d < head_dim; d++) a[d] = fmaf(p[j], or_f16_to_f32(vr[d]), a[d]);
+        }
+        mc[c] = m;
+        lc[c] = l;
+    }
+    float M = -INFINITY;
+    for (int c = 0; c < nc; c++) M = mc[c] > M ? mc[c] : M;
+    float L = 0.0f;
+    for (int d = 0; d < head_dim; d++) out[d] = 0.0f;
+    for (int c = 0; c < nc; c++) {
+        float f = or_exp(mc[c] - M);
+        L = fmaf(lc[c], f, L);
+        for (int d = 0; d < head_dim; d++) out[d] = fmaf(ac[(size_t)c * head_dim + d], f, out[d]);
+    }
+    for (int d = 0; d < head_dim; d++) out[d] = out[d] / L;
+    free(mc);
+    free(lc);
+    free(ac);
+    free(s);
+    free(p);
+}
+
+/* ------------------------------------------------------------------ model */
+typedef struct {
+    int type;
+    int64_t ne[4];
+    const uint8_t *data;
+} tref;
+
+typedef struct {
+    tref attn_norm, q, k, v, q_norm, k_norm, o, ffn_norm, gate_inp, gate, up, down;
+} layer_w;
+
+struct or_model {
+    or_config c;
+    tref embd, out_norm, out;
+    layer_w *L;
+    float *rope; /* [max_positions][n_rot] */
+    /* debug captures of the last forward */
+    int dbg_tokens;
+    int32_t *dbg_ids;   /* [n_layer][T][k] */
+    float *dbg_w;       /* [n_layer][T][k] */
+    float *dbg_hidden;  /* [T][E] */
+};
+
+struct or_kv {
+    const or_model *m;
+    int len;
+    int kvw;
+    uint16_t **k, **v; /* per layer [max_positions][kvw] */
+};
+
+static int find_tensor(const or_tensor *ts, int n, const char *name, tref *out, int required) {
+    for (int i = 0; i < n; i++) {
+        if (strcmp(ts[i].name, name) == 0) {
+            out->type = ts[i].type;
+            memcpy(out->ne, ts[i].ne, sizeof out->ne);
+            out->data = (const uint8_t *)ts[i].data;
+            return 0;
+        }
+    }
+    out->data = NULL;
+    if (required) {
+        char msg[256];
+        snprintf(msg, sizeof msg, "missing tensor %s", name);
+        set_err(msg);
+        return -1;
+    }
+    return 0;
+}
+
+or_model *or_model_new(const or_config *cfg, const or_tensor *ts, int n) {
+    or_model *m = (or_model *)calloc(1, sizeof(or_model));
+    m->c = *cfg;
+    if (m->c.expert_workers <= 0) m->c.expert_workers = 4;
+    if (m->c.attn_chunk <= 0) m->c.attn_chunk = 256;
+    if (m->c.n_rot <= 0) m->c.n_rot = m->c.head_dim;
+    int bad = 0;
+    bad |= find_tensor(ts, n, "token_embd.weight", &m->embd, 1);
+    bad |= find_tensor(ts, n, "output_norm.weight", &m->out_norm, 1);
+    find_tensor(ts, n, "output.weight", &m->out, 0);
+    if (!m->out.data) m->out = m->embd;
+    m->L = (layer_w *)calloc((size_t)cfg->n_layer, sizeof(layer_w));
+    char nm[128];
+#define GETW(field, suffix)                                              \
+    snprintf(nm, sizeof nm, "blk.%d.%s", il, suffix);                    \
+    bad |= find_tensor(ts, n, nm, &m->L[il].field, 1);
+    for (int il = 0; il < cfg->n_layer; il++) {
+        GETW(attn_norm, "attn_norm.weight");
+        GETW(q, "attn_q.weight");
+        GETW(k, "attn_k.weight");
+        GETW(v, "attn_v.weight");
+        GETW(q_norm, "attn_q_norm.weight");
+        GETW(k_norm, "attn_k_norm.weight");
+        GETW(o, "attn_output.weight");
+        GETW(ffn_norm, "ffn_norm.weight");
+        GETW(gate_inp, "ffn_gate_inp.weight");
+        GETW(gate, "ffn_gate_exps.weight");
+        GETW(up, "ffn_up_exps.weight");
+        GETW(down, "ffn_down_exps.weight");
+    }
+#undef GETW
+    if (bad) {
+        or_model_free(m);
+        return NULL;
+    }
+    m->rope = (float *)malloc(sizeof(float) * (size_t)m->c.max_positions * m->c.n_rot);
+    or_rope_table(m->c.max_positions, m->c.n_rot, m->c.rope_base, m->rope);
+    return m;
+}
+
+void or_model_free(or_model *m) {
+    if (!m) return;
+    free(m->L);
+    free(m->rope);
+    free(m->dbg_ids);
+    free(m->dbg_w);
+    free(m->dbg_hidden);
+    free(m);
+}
+
+or_kv *or_kv_new(const or_model *m) {
+    or_kv *kv = (or_kv *)calloc(1, sizeof(or_kv));
+    kv->m = m;
+    kv->kvw = m->c.n_head_kv * m->c.head_dim;
+    kv->k = (uint16_t **)calloc((size_t)m->c.n_layer, sizeof(uint16_t *));
+    kv->v = (uint16_t **)calloc((size_t)m->c.n_layer, sizeof(uint16_t *));
+    for (int l = 0; l < m->c.n_layer; l++) {
+        kv->k[l] = (uint16_t *)calloc((size_t)m->c.max_positions * kv->kvw, 2);
+        kv->v[l] = (uint16_t *)calloc((size_t)m->c.max_positions * kv->kvw, 2);
+    }
+    return kv;
+}
+
+void or_kv_free(or_kv *kv) {
+    if (!kv) return;
+    for (int l = 0; l < kv->m->c.n_layer; l++) {
+        free(kv->k[l]);
+        free(kv->v[l]);
+    }
+    free(kv->k);
+    free(kv->v);
+    free(kv);
+}
+
+int or_kv_len(const or_kv *kv) { return kv->len; }
+void or_kv_set_len(or_kv *kv, int n) { kv->len = n; }
+
+void or_kv_read(const or_kv *kv, int layer, int n_pos, uint16_t *k, uint16_t *v) {
+    memcpy(k, kv->k[layer], (size_t)n_pos * kv->kvw * 2);
+    memcpy(v, kv->v[layer], (size_t)n_pos * kv->kvw * 2);
+}
+
+void or_kv_write(or_kv *kv, int layer, int n_pos, const uint16_t *k, const uint16_t *v) {
+    memcpy(kv->k[layer], k, (size_t)n_pos * kv->kvw * 2);
+    memcpy(kv->v[layer], v, (size_t)n_pos * kv->kvw * 2);
+}
+
+static const uint8_t *expert_slice(const tref *t, int e, int64_t rows, int64_t cols) {
+    return t->data + (int64_t)e * rows * or_row_bytes(t->type, cols);
+}
+
+int or_forward(or_model *m, or_kv *kv, const int32_t *tokens, int T, int pos_start, float *logits) {
+    const or_config *c = &m->c;
+    const int E = c->n_embd, H = c->n_head, HK = c->n_head_kv, D = c->head_dim;
+    const int NE = c->n_expert, K = c->n_expert_used, F = c->n_ff_exp;
+    const int QW = H * D, KW = HK * D;
+    if (T <= 0) { set_err("no tokens"); return -1; }
+    if (pos_start != kv->len) { set_err("pos_start must equal the cache length"); return -1; }
+    if (pos_start + T > c->max_positions) { set_err("context exceeds max_positions"); return -1; }
+    for (int t = 0; t < T; t++)
+        if (tokens[t] < 0 || tokens[t] >= c->n_vocab) { set_err("token id out of range"); return -1; }
+
+    free(m->dbg_ids);
+    free(m->dbg_w);
+    free(m->dbg_hidden);
+    m->dbg_tokens = T;
+    m->dbg_ids = (int32_t *)calloc((size_t)c->n_layer * T * K, sizeof(int32_t));
+    m->dbg_w = (float *)calloc((size_t)c->n_layer * T * K, sizeof(float));
+    m->dbg_hidden = (float *)calloc((size_t)T * E, sizeof(float));
+
+    float *x = (float *)malloc(sizeof(float) * (size_t)T * E);
+    float *xn = (float *)malloc(sizeof(float) * (size_t)T * E);
+    float *q = (float *)malloc(sizeof(float) * (size_t)T * QW);
+    float *kk = (float *)malloc(sizeof(float) * (size_t)T * KW);
+    float *vv = (float *)malloc(sizeof(float) * (size_t)T * KW);
+    float *att = (float *)malloc(sizeof(float) * (size_t)T * QW);
+    float *ao = (float *)malloc(sizeof(float) * (size_t)T * E);
+    float *ffin = (float *)malloc(sizeof(float) * (size_t)T * E);
+    float *rl = (float *)malloc(sizeof(float) * (size_t)NE);
+    float *pr = (float *)malloc(sizeof(float) * (size_t)NE);
+    float *g = (float *)malloc(sizeof(float) * (size_t)F);
+    float *u = (float *)malloc(sizeof(float) * (size_t)F);
+    float *o = (float *)malloc(sizeof(float) * (size_t)E);
+    float *eo = (float *)malloc(sizeof(float) * (size_t)K * E);
+    float *sum = (float *)malloc(sizeof(float) * (size_t)E);
+    float *tot = (float *)malloc(sizeof(float) * (size_t)E);
+    int32_t ids[64];
+    float wts[64];
+
+    /* embedding: get_rows dequantises the token's row (stream.rs:2192-2231) */
+    int64_t erb = or_row_bytes(m->embd.type, E);
+    for (int t = 0; t < T; t++) or_dequant(m->embd.type, m->embd.data + (int64_t)tokens[t] * erb, E, x + (size_t)t * E);
+
+    const float scale = 1.0f / sqrtf((float)D);
+    for (int il = 0; il < c->n_layer; il++) {
+        const layer_w *w = &m->L[il];
+        /* phase 1: attn norm, q/k/v, q/k head norms, rope (stream.rs:2265-2474) */
+        for (int t = 0; t < T; t++) {
+            float *xt = x + (size_t)t * E, *xnt = xn + (size_t)t * E;
+            or_rmsnorm(xt, (const float *)w->attn_norm.data, E, c->rms_eps, xnt);
+            or_gemv(w->q.type, w->q.data, QW, E, xnt, q + (size_t)t * QW);
+            or_gemv(w->k.type, w->k.data, KW, E, xnt, kk + (size_t)t * KW);
+            or_gemv(w->v.type, w->v.data, KW, E, xnt, vv + (size_t)t * KW);
+            const float *cs = m->rope + (size_t)(pos_start + t) * c->n_rot;
+            for (int h = 0; h < H; h++) {
+                float *qh = q + (size_t)t * QW + h * D;
+                or_rmsnorm(qh, (const float *)w->q_norm.data, D, c->rms_eps, qh);
+                or_rope_neox(qh, c->n_rot, cs);
+            }
+            for (int h = 0; h < HK; h++) {
+                float *kh = kk + (size_t)t * KW + h * D;
+                or_rmsnorm(kh, (const float *)w->k_norm.data, D, c->rms_eps, kh);
+                or_rope_neox(kh, c->n_rot, cs);
+            }
+            /* KvCache::push: f32 -> f16 (kv.rs:184-192) */
+            uint16_t *kd = kv->k[il] + (size_t)(pos_start + t) * KW;
+            uint16_t *vd = kv->v[il] + (size_t)(pos_start + t) * KW;
+            for (int i = 0; i < KW; i++) {
+                kd[i] = or_f32_to_f16(kk[(size_t)t * KW + i]);
+                vd[i] = or_f32_to_f16(vv[(size_t)t * KW + i]);
+            }
+        }
+        /* phase 2: attention over the history, causal (stream.rs:2554-2703) */
+#pragma omp parallel for collapse(2) schedule(dynamic)
+        for (int t = 0; t < T; t++)
+            for (int h = 0; h < H; h++) {
+                int g2 = h / (H / HK);
+                or_attn_head(q + (size_t)t * QW + h * D, kv->k[il] + g2 * D, kv->v[il] + g2 * D, KW,
+                             pos_start + t + 1, D, scale, c->attn_chunk, att + (size_t)t * QW + h * D);
+            }
+        for (int t = 0; t < T; t++) {
+            or_gemv(w->o.type, w->o.data, E, QW, att + (size_t)t * QW, ao + (size_t)t * E);
+            for (int i = 0; i < E; i++) ffin[(size_t)t * E + i] = x[(size_t)t * E + i] + ao[(size_t)t * E + i];
+        }
+        /* phase 3: ffn norm, router, softmax (stream.rs:2784-2831) and experts */
+        for (int t = 0; t < T; t++) {
+            float *fi = ffin + (size_t)t * E, *fn = xn + (size_t)t * E;
+            or_rmsnorm(fi, (const float *)w->ffn_norm.data, E, c->rms_eps, fn);
+            or_gemv(OR_F32, w->gate_inp.data, NE, E, fn, rl);
+            or_softmax(rl, NE, pr);
+            or_route(pr, NE, K, ids, wts);
+            memcpy(m->dbg_ids + ((size_t)il * T + t) * K, ids, sizeof(int32_t) * K);
+            memcpy(m->dbg_w + ((size_t)il * T + t) * K, wts, sizeof(float) * K);
+            /* ascending expert order (BTreeMap in expert_ffn_block, stream.rs:916-926) */
+            int32_t sid[64];
+            float sw[64];
+            for (int i = 0; i < K; i++) {
+                sid[i] = ids[i];
+                sw[i] = wts[i];
+            }
+            for (int i = 1; i < K; i++)
+                for (int j = i; j > 0 && sid[j - 1] > sid[j]; j--) {
+                    int32_t ti = sid[j];
+                    sid[j] = sid[j - 1];
+                    sid[j - 1] = ti;
+                    float tw = sw[j];
+                    sw[j] = sw[j - 1];
+                    sw[j - 1] = tw;
+                }
+            for (int i = 0; i < K; i++) {
+                int e = sid[i];
+                or_gemv(w->gate.type, expert_slice(&w->gate, e, F, E), F, E, fn, g);
+                or_gemv(w->up.type, expert_slice(&w->up, e, F, E), F, E, fn, u);
+                for (int j = 0; j < F; j++) g[j] = or_silu(g[j]) * u[j];
+                or_gemv(w->down.type, expert_slice(&w->down, e, E, F), E, F, g, o);
+                for (int j = 0; j < E; j++) eo[(size_t)i * E + j] = o[j] * sw[i];
+            }
+            if (T == 1) {
+                /* expert_ffn_single: chunks of ceil(K/workers), each summed in order by
+                 * ggml_add, then partials added to a zero vector (stream.rs:1232-1284) */
+                int workers = c->expert_workers < K ? c->expert_workers : K;
+                if (workers < 1) workers = 1;
+                int chunk = (K + workers - 1) / workers;
+                for (int j = 0; j < E; j++) sum[j] = 0.0f;
+                for (int s0 = 0; s0 < K; s0 += chunk) {
+                    for (int j = 0; j < E; j++) tot[j] = eo[(size_t)s0 * E + j];
+                    for (int i = s0 + 1; i < K && i < s0 + chunk; i++)
+                        for (int j = 0; j < E; j++) tot[j] = tot[j] + eo[(size_t)i * E + j];
+                    if (workers <= 1) memcpy(sum, tot, sizeof(float) * E);
+                    else
+                        for (int j = 0; j < E; j++) sum[j] = sum[j] + tot[j];
+                }
+            } else {
+                /* expert_ffn_block: accum[t] += w * out, ascending experts (stream.rs:1051-1058) */
+                for (int j = 0; j < E; j++) sum[j] = 0.0f;
+                for (int i = 0; i < K; i++)
+                    for (int j = 0; j < E; j++) sum[j] = sum[j] + eo[(size_t)i * E + j];
+            }
+            for (int j = 0; j < E; j++) x[(size_t)t * E + j] = fi[j] + sum[j];
+        }
+    }
+    kv->len += T;
+    memcpy(m->dbg_hidden, x, sizeof(float) * (size_t)T * E);
+
+    /* output head on the last position (stream.rs:2853-2914) */
+    or_rmsnorm(x + (size_t)(T - 1) * E, (const float *)m->out_norm.data, E, c->rms_eps, xn);
+    or_gemv(m->out.type, m->out.data, c->n_vocab, E, xn, logits);
+
+    free(x); free(xn); free(q); free(kk); free(vv); free(att); free(ao); free(ffin);
+    free(rl); free(pr); free(g); free(u); free(o); free(eo); free(sum); free(tot);
+    return 0;
+}
+
+int or_debug_topk(const or_model *m, int layer, int t, int32_t *ids, float *weights) {
+    if (!m->dbg_ids || t >= m->dbg_tokens || layer >= m->c.n_layer) return -1;
+    int K = m->c.n_expert_used;
+    memcpy(ids, m->dbg_ids + ((size_t)layer * m->dbg_tokens + t) * K, sizeof(int32_t) * K);
+    memcpy(weights, m->dbg_w + ((size_t)layer * m->dbg_tokens + t) * K, sizeof(float) * K);
+    return 0;
+}
+
+int or_debug_hidden(const or_model *m, int t, float *out) {
+    if (!m->dbg_hidden || t >= m->dbg_tokens) return -1;
+    memcpy(out, m->dbg_hidden + (size_t)t * m->c.n_embd, sizeof(float) * m->c.n_embd);
+    return 0;
+}

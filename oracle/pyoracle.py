@@ -1,0 +1,266 @@
+"""ctypes wrapper of oracle/liboracle.so -- the CPU parity checker (TEST INFRASTRUCTURE).
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU legs import this module; the product
+(bigtea_b200) never does. `build()` compiles the library with oracle/Makefile.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB = os.path.join(HERE, "liboracle.so")
+
+OR_F32, OR_F16, OR_Q4_K, OR_Q6_K = 0, 1, 12, 14
+
+
+class Q8KBlock(C.Structure):
+    _fields_ = [("d", C.c_float), ("qs", C.c_int8 * 256), ("bsums", C.c_int16 * 16)]
+
+
+class Config(C.Structure):
+    _fields_ = [(n, C.c_int) for n in ("n_layer", "n_embd", "n_head", "n_head_kv", "head_dim", "n_expert",
+                                        "n_expert_used", "n_ff_exp", "n_vocab", "n_rot")] + \
+               [("rms_eps", C.c_float), ("rope_base", C.c_float), ("expert_workers", C.c_int),
+                ("attn_chunk", C.c_int), ("max_positions", C.c_int)]
+
+
+class Tensor(C.Structure):
+    _fields_ = [("name", C.c_char_p), ("type", C.c_int), ("ne", C.c_int64 * 4), ("data", C.c_void_p)]
+
+
+def build() -> str:
+    src = [os.path.join(HERE, f) for f in ("oracle.c", "oracle.h", "Makefile")]
+    if not os.path.exists(LIB) or any(os.path.getmtime(s) > os.path.getmtime(LIB) for s in src):
+        subprocess.run(["make", "-s", "-C", HERE], check=True)
+    return LIB
+
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is None:
+        build()
+        L = C.CDLL(LIB)
+        P, F, I = C.c_void_p, C.POINTER(C.c_float), C.c_int
+        sig = {
+            "or_f32_to_f16": (C.c_uint16, [C.c_float]),
+            "or_f16_to_f32": (C.c_float, [C.c_uint16]),
+            "or_exp": (C.c_float, [C.c_float]),
+            "or_silu": (C.c_float, [C.c_float]),
+            "or_row_bytes": (C.c_int64, [I, C.c_int64]),
+            "or_dequant": (I, [I, P, C.c_int64, F]),
+            "or_quantize_q8k": (None, [F, C.c_int64, C.POINTER(Q8KBlock)]),
+            "or_gemv": (I, [I, P, C.c_int64, C.c_int64, F, F]),
+            "or_rmsnorm": (None, [F, F, I, C.c_float, F]),
+            "or_rope_table": (None, [I, I, C.c_float, F]),
+            "or_softmax": (None, [F, I, F]),
+            "or_route": (None, [F, I, I, C.POINTER(C.c_int32), F]),
+            "or_attn_head": (None, [F, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), C.c_int64, I, I, C.c_float, I, F]),
+            "or_argmax": (C.c_uint32, [F, C.c_int64]),
+            "or_model_new": (P, [C.POINTER(Config), C.POINTER(Tensor), I]),
+            "or_model_free": (None, [P]),
+            "or_last_error": (C.c_char_p, []),
+            "or_kv_new": (P, [P]),
+            "or_kv_free": (None, [P]),
+            "or_kv_len": (I, [P]),
+            "or_kv_set_len": (None, [P, I]),
+            "or_kv_read": (None, [P, I, I, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16)]),
+            "or_kv_write": (None, [P, I, I, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16)]),
+            "or_forward": (I, [P, P, C.POINTER(C.c_int32), I, I, F]),
+            "or_debug_topk": (I, [P, I, I, C.POINTER(C.c_int32), F]),
+            "or_debug_hidden": (I, [P, I, F]),
+            "or_set_threads": (I, [I]),
+        }
+        for n, (r, a) in sig.items():
+            fn = getattr(L, n)
+            fn.restype = r
+            fn.argtypes = a
+        _lib = L
+    return _lib
+
+
+def _f(a):
+    return a.ctypes.data_as(C.POINTER(C.c_float))
+
+
+def dequant(ggml_type: int, data: np.ndarray, n: int) -> np.ndarray:
+    out = np.empty(n, np.float32)
+    data = np.ascontiguousarray(data).view(np.uint8)
+    if lib().or_dequant(ggml_type, data.ctypes.data_as(C.c_void_p), n, _f(out)):
+        raise ValueError("or_dequant rejected the input")
+    return out
+
+
+def quantize_q8k(x: np.ndarray):
+    x = np.ascontiguousarray(x, np.float32)
+    nb = x.size // 256
+    blocks = (Q8KBlock * nb)()
+    lib().or_quantize_q8k(_f(x), x.size, blocks)
+    d = np.array([b.d for b in blocks], np.float32)
+    qs = np.array([list(b.qs) for b in blocks], np.int8)
+    bs = np.array([list(b.bsums) for b in blocks], np.int16)
+    return d, qs, bs
+
+
+def gemv(ggml_type: int, w: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(np.atleast_2d(x), np.float32)
+    w = np.ascontiguousarray(w).view(np.uint8)
+    y = np.empty((x.shape[0], rows), np.float32)
+    for t in range(x.shape[0]):
+        xt = np.ascontiguousarray(x[t])
+        yt = np.empty(rows, np.float32)
+        if lib().or_gemv(ggml_type, w.ctypes.data_as(C.c_void_p), rows, cols, _f(xt), _f(yt)):
+            raise ValueError("or_gemv rejected the input")
+        y[t] = yt
+    return y
+
+
+def exp(x: float) -> float:
+    return lib().or_exp(x)
+
+
+def f32_to_f16(x: float) -> int:
+    return lib().or_f32_to_f16(x)
+
+
+def softmax(x) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    lib().or_softmax(_f(x), x.size, _f(out))
+    return out
+
+
+def route(probs, k):
+    p = np.ascontiguousarray(probs, np.float32)
+    ids = np.empty(k, np.int32)
+    w = np.empty(k, np.float32)
+    lib().or_route(_f(p), p.size, k, ids.ctypes.data_as(C.POINTER(C.c_int32)), _f(w))
+    return ids, w
+
+
+def argmax(logits) -> int:
+    x = np.ascontiguousarray(logits, np.float32)
+    return int(lib().or_argmax(_f(x), x.size))
+
+
+def rmsnorm(x, w, eps):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    lib().or_rmsnorm(_f(x), _f(w), x.size, eps, _f(out))
+    return out
+
+
+def rope_table(n_pos, n_rot, base):
+    out = np.empty((n_pos, n_rot), np.float32)
+    lib().or_rope_table(n_pos, n_rot, base, _f(out))
+    return out
+
+
+def attn_head(q, k16, v16, nk, scale, chunk=256):
+    """one query head over f16 keys/values [nk, head_dim] (uint16 bit patterns)"""
+    q = np.ascontiguousarray(q, np.float32)
+    k16 = np.ascontiguousarray(k16, np.uint16)
+    v16 = np.ascontiguousarray(v16, np.uint16)
+    out = np.empty(q.size, np.float32)
+    u16 = C.POINTER(C.c_uint16)
+    lib().or_attn_head(_f(q), k16.ctypes.data_as(u16), v16.ctypes.data_as(u16), k16.shape[1], nk, q.size, scale,
+                       chunk, _f(out))
+    return out
+
+
+class Model:
+    """The whole qwen3moe decode path on the CPU: forward_cached over a contiguous f16 cache."""
+
+    def __init__(self, cfg, tensors: dict):
+        c = Config(cfg.n_layer, cfg.n_embd, cfg.n_head, cfg.n_head_kv, cfg.head_dim, cfg.n_expert,
+                   cfg.n_expert_used, cfg.n_ff_exp, cfg.n_vocab, cfg.head_dim, cfg.rms_eps, cfg.rope_freq_base,
+                   cfg.expert_workers, 256, cfg.max_positions)
+        self.cfg = cfg
+        self._keep = []
+        arr = (Tensor * len(tensors))()
+        for i, (name, (ty, ne, data)) in enumerate(tensors.items()):
+            nb = name.encode()
+            data = np.ascontiguousarray(data)
+            self._keep += [nb, data]
+            arr[i].name = nb
+            arr[i].type = ty
+            for j in range(4):
+                arr[i].ne[j] = ne[j] if j < len(ne) else 1
+            arr[i].data = data.ctypes.data_as(C.c_void_p)
+        self._arr = arr
+        self.h = lib().or_model_new(C.byref(c), arr, len(tensors))
+        if not self.h:
+            raise ValueError(lib().or_last_error().decode())
+        self.kv = lib().or_kv_new(self.h)
+
+    def close(self):
+        if self.h:
+            lib().or_kv_free(self.kv)
+            lib().or_model_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, tokens, pos_start: int) -> np.ndarray:
+        t = np.ascontiguousarray(tokens, np.int32)
+        out = np.empty(self.cfg.n_vocab, np.float32)
+        if lib().or_forward(self.h, self.kv, t.ctypes.data_as(C.POINTER(C.c_int32)), t.size, pos_start, _f(out)):
+            raise ValueError(lib().or_last_error().decode())
+        return out
+
+    def len(self) -> int:
+        return lib().or_kv_len(self.kv)
+
+    def set_len(self, n: int):
+        lib().or_kv_set_len(self.kv, n)
+
+    def kv_layer(self, layer: int, n_pos: int | None = None):
+        n = self.len() if n_pos is None else n_pos
+        kw = self.cfg.n_head_kv * self.cfg.head_dim
+        k = np.empty(n * kw, np.uint16)
+        v = np.empty(n * kw, np.uint16)
+        u16 = C.POINTER(C.c_uint16)
+        lib().or_kv_read(self.kv, layer, n, k.ctypes.data_as(u16), v.ctypes.data_as(u16))
+        return k, v
+
+    def write_kv_layer(self, layer: int, k: np.ndarray, v: np.ndarray):
+        kw = self.cfg.n_head_kv * self.cfg.head_dim
+        k = np.ascontiguousarray(k).view(np.uint16)
+        v = np.ascontiguousarray(v).view(np.uint16)
+        u16 = C.POINTER(C.c_uint16)
+        lib().or_kv_write(self.kv, layer, k.size // kw, k.ctypes.data_as(u16), v.ctypes.data_as(u16))
+
+    def topk(self, layer: int, t: int):
+        K = self.cfg.n_expert_used
+        ids = np.empty(K, np.int32)
+        w = np.empty(K, np.float32)
+        if lib().or_debug_topk(self.h, layer, t, ids.ctypes.data_as(C.POINTER(C.c_int32)), _f(w)):
+            raise ValueError("no top-k capture")
+        return ids, w
+
+    def hidden(self, t: int) -> np.ndarray:
+        out = np.empty(self.cfg.n_embd, np.float32)
+        if lib().or_debug_hidden(self.h, t, _f(out)):
+            raise ValueError("no hidden capture")
+        return out
+
+    def greedy(self, first_token: int, n_steps: int) -> list:
+        """the chaos-run temp-0 loop: feed the argmax back n_steps times"""
+        toks = []
+        tok = first_token
+        for _ in range(n_steps):
+            logits = self.forward([tok], self.len())
+            tok = argmax(logits)
+            toks.append(tok)
+        return toks

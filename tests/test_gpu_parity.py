@@ -1,0 +1,255 @@
+"""GPU parity: every kernel of the decode layer against the CPU oracle, through the C ABI.
+
+The bar: K-quant dequant, KV-cache bytes and top-k expert ids bit-exact; logits within 1e-2
+max-abs after the final norm (the tolerance the path's specification states) -- and, because
+both sides implement one arithmetic contract, bit-exact as well, which is asserted too.
+"""
+import numpy as np
+import pytest
+
+import bigtea_b200 as bt
+from bigtea_b200 import _lib
+from oracle import pyoracle as orc
+from tests.conftest import bits
+
+pytestmark = pytest.mark.gpu
+
+LOGIT_TOL = 1e-2
+
+
+def assert_logits(got, want):
+    assert np.abs(got - want).max() <= LOGIT_TOL
+    assert np.array_equal(bits(got), bits(want))
+
+
+# ------------------------------------------------------------------ dequant
+def test_dequant_bit_exact_on_golden(golden):
+    for ty, key in ((_lib.TYPE_Q4_K, "q4k"), (_lib.TYPE_Q6_K, "q6k")):
+        b = golden[key + "_bytes"].reshape(-1)
+        want = golden[key + "_values"]
+        assert np.array_equal(bits(bt.dequantize(ty, b, want.size)), bits(want))
+
+
+@pytest.mark.parametrize("ty", [_lib.TYPE_Q4_K, _lib.TYPE_Q6_K])
+def test_dequant_bit_exact_on_synthetic(ty):
+    w = bt.models.synth_tensor("deq.weight", ty, (2048, 97), 0.0, seed=4)
+    n = 2048 * 97
+    assert np.array_equal(bits(bt.dequantize(ty, w, n)), bits(orc.dequant(ty, w, n)))
+
+
+# ------------------------------------------------------------------ GEMV
+@pytest.mark.parametrize("ty", [_lib.TYPE_Q4_K, _lib.TYPE_Q6_K])
+@pytest.mark.parametrize("rows,cols,T", [(37, 256, 1), (768, 2048, 1), (2048, 768, 3), (2048, 4096, 8),
+                                          (130, 512, 9), (1, 2048, 2)])
+def test_gemv_bit_exact(ty, rows, cols, T):
+    w = bt.models.synth_tensor(f"gemv.{rows}.{cols}", ty, (cols, rows), 0.0, seed=rows + cols)
+    x = np.random.default_rng(rows).standard_normal((T, cols)).astype(np.float32)
+    x[0, :256] = 0.0  # an all-zero activation block (d = 0)
+    got = bt.gemv(ty, w, rows, cols, x)
+    want = orc.gemv(ty, w, rows, cols, x)
+    assert np.array_equal(bits(got), bits(want))
+
+
+# ------------------------------------------------------------------ whole forward
+@pytest.fixture(scope="module")
+def tiny_engine(tiny_cfg, tiny_weights):
+    e = bt.Engine(tiny_cfg, tiny_weights)
+    yield e
+    e.close()
+
+
+def compare_kv(cache, model, cfg, seq=0):
+    n = cache.len(seq)
+    assert n == model.len()
+    for il in range(cfg.n_layer):
+        k, v = cache.layer_bytes(il, seq)
+        ko, vo = model.kv_layer(il)
+        assert np.array_equal(k, ko.view(np.uint8)), f"layer {il} keys"
+        assert np.array_equal(v, vo.view(np.uint8)), f"layer {il} values"
+
+
+def test_forward_prefill_and_decode_match_oracle(tiny_cfg, tiny_weights, tiny_engine):
+    cfg = tiny_cfg
+    rng = np.random.default_rng(21)
+    prompt = rng.integers(0, cfg.n_vocab, 20)
+    model = orc.Model(cfg, tiny_weights)
+    cache = bt.KvCache(tiny_engine, max_positions=512)
+    runner = bt.StreamingRunner(tiny_engine)
+    got = runner.forward_cached(cache, prompt, 0)
+    want = model.forward(prompt, 0)
+    assert_logits(got, want)
+    for il in range(cfg.n_layer):
+        for t in (0, 7, 19):
+            gi, gw = tiny_engine.debug_topk(il, t)
+            oi, ow = model.topk(il, t)
+            assert np.array_equal(gi, oi) and np.array_equal(bits(gw), bits(ow))
+    assert np.array_equal(bits(tiny_engine.debug_hidden(19)), bits(model.hidden(19)))
+    compare_kv(cache, model, cfg)
+    tok = int(np.argmax(want))
+    for step in range(6):
+        got = runner.forward_cached(cache, [tok], cache.len())
+        want = model.forward([tok], model.len())
+        assert_logits(got, want)
+        gi, _ = tiny_engine.debug_topk(1, 0)
+        oi, _ = model.topk(1, 0)
+        assert np.array_equal(gi, oi)
+        tok = orc.argmax(want)
+    compare_kv(cache, model, cfg)
+    assert cache.is_consistent()
+
+
+def test_long_context_uses_several_attention_chunks(tiny_cfg, tiny_weights, tiny_engine):
+    cfg = tiny_cfg
+    prompt = np.random.default_rng(22).integers(0, cfg.n_vocab, 600)
+    model = orc.Model(cfg, tiny_weights)
+    cache = bt.KvCache(tiny_engine, max_positions=1024)
+    runner = bt.StreamingRunner(tiny_engine)
+    assert_logits(runner.forward_cached(cache, prompt, 0), model.forward(prompt, 0))
+    tok = 5
+    for _ in range(3):
+        assert_logits(runner.forward_cached(cache, [tok], cache.len()), model.forward([tok], model.len()))
+        tok = (tok * 7 + 3) % cfg.n_vocab
+    compare_kv(cache, model, cfg)
+
+
+def test_greedy_graph_loop_matches_oracle(tiny_cfg, tiny_weights, tiny_engine):
+    cfg = tiny_cfg
+    prompt = np.random.default_rng(23).integers(0, cfg.n_vocab, 17)
+    model = orc.Model(cfg, tiny_weights)
+    cache = bt.KvCache(tiny_engine, max_positions=512)
+    runner = bt.StreamingRunner(tiny_engine)
+    first = orc.argmax(model.forward(prompt, 0))
+    runner.forward_cached(cache, prompt, 0)
+    toks, logits = runner.generate_greedy(cache, [first], 12, want_logits=True)
+    want = model.greedy(first, 12)
+    assert list(toks[:, 0]) == want
+    compare_kv(cache, model, cfg)
+    # the last step's logits are the oracle's for the same position
+    last = model.forward([want[-1]], model.len())
+    nxt = runner.forward_cached(cache, [want[-1]], cache.len())
+    assert_logits(nxt, last)
+
+
+def test_batched_sequences_match_single_sequence_runs(tiny_cfg, tiny_weights, tiny_engine):
+    cfg = tiny_cfg
+    rng = np.random.default_rng(24)
+    prompts = [rng.integers(0, cfg.n_vocab, n) for n in (5, 1, 12)]
+    cache = bt.KvCache(tiny_engine, max_positions=256, max_seqs=4)
+    runner = bt.StreamingRunner(tiny_engine)
+    got = runner.forward_batch(cache, [2, 0, 3], prompts, [0, 0, 0])
+    for i, p in enumerate(prompts):
+        model = orc.Model(cfg, tiny_weights)
+        assert_logits(got[i], model.forward(p, 0))
+    # one decode step for all three, then against the oracle continued per sequence
+    nxt = [int(np.argmax(g)) for g in got]
+    got2 = runner.forward_batch(cache, [2, 0, 3], [[t] for t in nxt], [5, 1, 12])
+    for i, (p, s) in enumerate(zip(prompts, [2, 0, 3])):
+        model = orc.Model(cfg, tiny_weights)
+        model.forward(p, 0)
+        assert_logits(got2[i], model.forward([nxt[i]], len(p)))
+        compare_kv(cache, model, cfg, seq=s)
+
+
+def test_batched_greedy_matches_per_sequence_oracle(tiny_cfg, tiny_weights, tiny_engine):
+    cfg = tiny_cfg
+    rng = np.random.default_rng(25)
+    prompts = [rng.integers(0, cfg.n_vocab, n) for n in (3, 9)]
+    cache = bt.KvCache(tiny_engine, max_positions=128, max_seqs=2)
+    runner = bt.StreamingRunner(tiny_engine)
+    lg = runner.forward_batch(cache, [0, 1], prompts, [0, 0])
+    first = [orc.argmax(x) for x in lg]
+    toks = runner.generate_greedy(cache, first, 8, seqs=[0, 1])
+    for i, p in enumerate(prompts):
+        model = orc.Model(cfg, tiny_weights)
+        model.forward(p, 0)
+        assert list(toks[:, i]) == model.greedy(first[i], 8)
+
+
+# ------------------------------------------------------------------ KvCache semantics on the device pool (kv.rs tests)
+def test_kv_truncate_shift_and_restore(tiny_cfg, tiny_weights, tiny_engine):
+    cfg = tiny_cfg
+    rng = np.random.default_rng(26)
+    prompt = rng.integers(0, cfg.n_vocab, 40)
+    cache = bt.KvCache(tiny_engine, max_positions=256)
+    runner = bt.StreamingRunner(tiny_engine)
+    runner.forward_cached(cache, prompt, 0)
+    k0, v0 = cache.layer_bytes(0)
+    per = cfg.n_head_kv * cfg.head_dim * 2
+    # shift_out(keep=4, drop=10): positions 0..3 stay, 14.. slide down to 4..
+    cache.shift_out(4, 10)
+    assert cache.len() == 30 and cache.is_consistent()
+    k1, v1 = cache.layer_bytes(0)
+    assert np.array_equal(k1[:4 * per], k0[:4 * per])
+    assert np.array_equal(k1[4 * per:], k0[14 * per:])
+    assert np.array_equal(v1[4 * per:], v0[14 * per:])
+    # a decode step over the shifted cache equals the oracle given the same cache
+    model = orc.Model(cfg, tiny_weights)
+    for il in range(cfg.n_layer):
+        k, v = cache.layer_bytes(il)
+        model.write_kv_layer(il, k, v)
+    model.set_len(30)
+    assert_logits(runner.forward_cached(cache, [11], 30), model.forward([11], 30))
+    # shifting more than there is clamps; shifting nothing is a no-op
+    cache.shift_out(28, 100)
+    assert cache.len() == 28
+    before = cache.keys(0)
+    cache.shift_out(0, 0)
+    cache.shift_out(50, 3)
+    assert np.array_equal(cache.keys(0), before)
+    # truncate_to keeps a prefix; a larger n is a no-op
+    cache.truncate_to(10)
+    assert cache.len() == 10 and np.array_equal(cache.keys(0), before[:10 * per])
+    cache.truncate_to(99)
+    assert cache.len() == 10
+    # restore_layer + set_positions (the prompt cache path); a ragged length is refused
+    for il in range(cfg.n_layer):
+        cache.restore_layer(il, *(x[:10 * per] for x in model.kv_layer(il, 10)))
+    cache.set_positions(10)
+    assert cache.is_consistent()
+    with pytest.raises(bt.BtError):
+        cache.restore_layer(0, np.zeros(per + 2, np.uint8), np.zeros(per + 2, np.uint8))
+    cache.clear()
+    assert cache.is_empty() and cache.bytes() == 0
+
+
+def test_errors_leave_the_engine_usable(tiny_cfg, tiny_weights, tiny_engine):
+    cfg = tiny_cfg
+    cache = bt.KvCache(tiny_engine, max_positions=64)
+    runner = bt.StreamingRunner(tiny_engine)
+    with pytest.raises(bt.BtError) as e:
+        runner.forward_cached(cache, [cfg.n_vocab + 5], 0)
+    assert e.value.status == _lib.BT_ERR_INVALID
+    with pytest.raises(bt.BtError) as e:
+        runner.forward_cached(cache, [1, 2], 3)
+    assert e.value.status == _lib.BT_ERR_KV
+    with pytest.raises(bt.BtError):
+        runner.forward_cached(cache, list(range(65)), 0)
+    model = orc.Model(cfg, tiny_weights)
+    assert_logits(runner.forward_cached(cache, [1, 2, 3], 0), model.forward([1, 2, 3], 0))
+
+
+# ------------------------------------------------------------------ the reference's CPU-runnable workload
+def test_cfg0_prefill_128_then_64_greedy_steps():
+    """qwen3moe, 2 layers at Qwen3-30B-A3B dims, Q4_K weights with Q6_K embedding/output:
+    128-token prefill of uniform-random ids, then 64 greedy steps (the reference's cfg0)."""
+    cfg = bt.config("cfg0")
+    W = bt.synth_model(cfg, seed=2024)
+    prompt = np.random.default_rng(2024).integers(0, cfg.n_vocab, 128)
+    model = orc.Model(cfg, W)
+    want0 = model.forward(prompt, 0)
+    e = bt.Engine(cfg, W)
+    try:
+        cache = bt.KvCache(e, max_positions=256)
+        runner = bt.StreamingRunner(e)
+        got0 = runner.forward_cached(cache, prompt, 0)
+        assert_logits(got0, want0)
+        for il in range(cfg.n_layer):
+            for t in (0, 64, 127):
+                assert np.array_equal(e.debug_topk(il, t)[0], model.topk(il, t)[0])
+        first = orc.argmax(want0)
+        toks = runner.generate_greedy(cache, [first], 64)
+        want = model.greedy(first, 64)
+        assert list(toks[:, 0]) == want
+        compare_kv(cache, model, cfg)
+    finally:
+        e.close()
