@@ -152,17 +152,30 @@ def cpu_baseline_from_engine(engine, cache, cfg, ctx, n_tokens, threads, seed):
 def run_ours(args, rank, world, local_rank):
     import bigtea_b200 as bt
 
-    cfg = bt.config(args.config, max_positions=args.ctx + args.steps + args.warmup + args.steps // 4 + args.prof_steps + 64)
+    over = {"max_positions": args.ctx + args.steps + args.warmup + args.steps // 4 + args.prof_steps + 64}
+    if args.layers:
+        over["n_layer"] = args.layers
+        over["layer_types"] = bt.config(args.config).layer_types[:args.layers]
+    cfg = bt.config(args.config, **over)
     t_setup = time.perf_counter()
     engine = bt.Engine.synthetic(cfg, seed=args.seed, device=local_rank)
     cache = bt.KvCache(engine, max_positions=cfg.max_positions)
     runner = bt.StreamingRunner(engine)
     rng = np.random.default_rng(args.seed + 1)
-    prompt = rng.integers(0, cfg.n_vocab, args.ctx)
     t0 = time.perf_counter()
-    logits = runner.forward_cached(cache, prompt, 0)
+    if args.fill == "prefill":
+        prompt = rng.integers(0, cfg.n_vocab, args.ctx)
+        logits = runner.forward_cached(cache, prompt, 0)
+        tok = int(np.argmax(logits))
+    else:  # seeded f16 values: the decode cost does not depend on the cache contents
+        kw = cfg.n_head_kv * cfg.head_dim
+        for il in range(cfg.n_layer):
+            k = rng.standard_normal(args.ctx * kw).astype(np.float16)
+            v = rng.standard_normal(args.ctx * kw).astype(np.float16)
+            cache.restore_layer(il, k, v)
+        cache.set_positions(args.ctx)
+        tok = int(rng.integers(0, cfg.n_vocab))
     prefill_s = time.perf_counter() - t0
-    tok = int(np.argmax(logits))
     # warm-up (also captures the step graph), then K timed graph replays
     runner.generate_greedy(cache, [tok], args.warmup)
     sync_ranks(world)
@@ -184,7 +197,7 @@ def run_ours(args, rank, world, local_rank):
     e2e = world * e2e_steps / e2e_s
 
     # per-kernel device times (serialised launches) for the roofline
-    prof = runner.profile_decode(cache, [nxt], args.prof_steps)
+    prof = runner.profile_decode(cache, [nxt], args.prof_steps) if args.prof_steps else {}
     gu_bytes, dn_bytes = expert_bytes(cfg)
     gu = prof.get("expert_gateup", (1, 0.0))
     dn = prof.get("expert_down", (1, 0.0))
@@ -210,8 +223,9 @@ def run_ours(args, rank, world, local_rank):
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q4_K/q6_K weights, int8 dot, f32 accumulate",
             "data": "synthetic (seeded N(0,0.02) weights, uniform-random token ids)",
-            "config": {"workload": f"{args.config}: Qwen3-30B-A3B shape, 48 layers, Q4_K_M stand-in, batch 1 "
-                                   f"greedy decode after a {args.ctx}-token prefill",
+            "config": {"workload": f"{args.config}: Qwen3-30B-A3B shape, {cfg.n_layer} layers, Q4_K_M stand-in, "
+                                   f"batch 1 greedy decode after a {args.ctx}-token "
+                                   + ("prefill" if args.fill == "prefill" else "seeded cache fill"),
                        "batch": 1, "context": args.ctx, "parallelism": "replicas" if world > 1 else "single GPU",
                        "l2": "inputs larger than L2 (17 GB of weights per step)",
                        "prefill_seconds": round(prefill_s, 2), "setup_seconds": round(time.perf_counter() - t_setup, 1)},
@@ -306,6 +320,9 @@ def main():
     ap.add_argument("--prof-steps", type=int, default=4)
     ap.add_argument("--cpu-tokens", type=int, default=3)
     ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--fill", default="prefill", choices=["prefill", "random"],
+                    help="build the context by a real prefill, or fill the cache with seeded f16 values")
+    ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling runs)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

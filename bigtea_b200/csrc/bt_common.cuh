@@ -80,6 +80,58 @@ __device__ __forceinline__ int warp_sum_int(int v) {
     return v;
 }
 
+// C5 over n elements (lane l: l, l+32, ... in order). Loads are issued 16 at a time ahead of
+// the in-order fmaf chain, so the chain waits on one load latency per 16 elements.
+__device__ __forceinline__ float warp_sumsq_p2(const float *__restrict__ x, int n, int lane) {
+    float acc = 0.0f;
+    int i = lane;
+    for (; i + 32 * 15 < n; i += 32 * 16) {
+        float v[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) v[k] = x[i + 32 * k];
+#pragma unroll
+        for (int k = 0; k < 16; k++) acc = fmaf(v[k], v[k], acc);
+    }
+    for (; i < n; i += 32) acc = fmaf(x[i], x[i], acc);
+    return butterfly_sum(acc);
+}
+
+// C5 dot of a (global, streamed once) and b (any memory).
+__device__ __forceinline__ float warp_dot_p2(const float *__restrict__ a, const float *__restrict__ b, int n, int lane) {
+    float acc = 0.0f;
+    int i = lane;
+    for (; i + 32 * 15 < n; i += 32 * 16) {
+        float va[16], vb[16];
+#pragma unroll
+        for (int k = 0; k < 16; k++) {
+            va[k] = __ldg(a + i + 32 * k);
+            vb[k] = b[i + 32 * k];
+        }
+#pragma unroll
+        for (int k = 0; k < 16; k++) acc = fmaf(va[k], vb[k], acc);
+    }
+    for (; i < n; i += 32) acc = fmaf(__ldg(a + i), b[i], acc);
+    return butterfly_sum(acc);
+}
+
+// Start pulling [p, p+bytes) from HBM into L2 without waiting (TMA bulk prefetch).
+// p 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void prefetch_l2(const void *p, uint32_t bytes) {
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// Prefetch a large range in pieces of at most 1 MiB, spread over the calling threads.
+__device__ __forceinline__ void prefetch_l2_range(const void *p, unsigned long long bytes, int tid, int nthreads) {
+    const unsigned long long piece = 1ull << 20;
+    const char *c = reinterpret_cast<const char *>(p);
+    unsigned long long n = (bytes + piece - 1) / piece;
+    for (unsigned long long k = tid; k < n; k += nthreads) {
+        unsigned long long off = k * piece;
+        unsigned long long len = bytes - off < piece ? bytes - off : piece;
+        prefetch_l2(c + off, (uint32_t)(len & ~15ull));
+    }
+}
+
 // ---------------------------------------------------------------- PTX: PDL
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }

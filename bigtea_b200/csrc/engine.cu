@@ -110,7 +110,7 @@ struct bt_engine {
     DevBuf x, ffn_in, fn, qkv, qbuf, att, rlog, rcnt, sel_ids, sel_w, act, part, acnt;
     DevBuf dbg_ids, dbg_w;  // [n_layer][TB][K]
     DevBuf tokens, seq_of, local_idx, pos_of, single, x_rows;
-    DevBuf st_seq, st_ntok, st_lrow, next_tok, gen_out, gen_count, logits;
+    DevBuf st_seq, st_ntok, st_lrow, next_tok, gen_out, gen_count, logits, amax;
     DevBuf err;
     int part_chunks = 0;
     size_t gen_cap = 0;
@@ -118,7 +118,8 @@ struct bt_engine {
     bt_stats stats{};
     std::map<GraphKey, cudaGraphExec_t> graphs;
     cudaGraph_t graph_objs[64] = {};
-    int last_T = 0;
+    int last_T = 0;        // tokens in the last step of the last bt_forward
+    size_t last_first = 0; // index (in that call's token list) of the step's first token
     // profiling
     bool timing = false;
     std::map<std::string, KernelTimer> timers;
@@ -126,6 +127,7 @@ struct bt_engine {
     std::vector<std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>> ev_used;
     double last_device_ms = 0;
     bool pdl = true;
+    bool prefetch = true;
 };
 
 struct bt_kv {
@@ -163,7 +165,8 @@ static EncodeTiledFn get_encode_fn() {
 
 // ------------------------------------------------------------------ helpers
 static int pick_nst(size_t slot_bytes, size_t fixed_bytes) {
-    const size_t cap = 227 * 1024;
+    static size_t cap = 0;
+    if (!cap) cap = (size_t)max_dynamic_smem();
     int nst = 4;
     while (nst > 1 && fixed_bytes + (size_t)GEMV_WARPS * nst * slot_bytes > cap) nst--;
     return nst;
@@ -288,7 +291,7 @@ static int alloc_scratch(bt_engine *e) {
     CK(e->sel_ids.alloc((size_t)TB * K * 4));
     CK(e->sel_w.alloc((size_t)TB * K * 4));
     CK(e->act.alloc((size_t)TB * K * F * 4));
-    CK(e->part.alloc((size_t)TB * d.n_head_kv * e->part_chunks * G * (d.head_dim + 2) * 4));
+    CK(e->part.alloc((size_t)TB * d.n_head_kv * e->part_chunks * G * (d.head_dim + 4) * 4));
     CK(e->acnt.alloc((size_t)TB * d.n_head_kv * 4));
     CK(cudaMemset(e->acnt.p, 0, (size_t)TB * d.n_head_kv * 4));
     CK(e->dbg_ids.alloc((size_t)d.n_layer * TB * K * 4));
@@ -305,6 +308,8 @@ static int alloc_scratch(bt_engine *e) {
     CK(e->next_tok.alloc((size_t)e->max_out * 4));
     CK(e->gen_count.alloc((size_t)e->max_out * 4));
     CK(e->logits.alloc((size_t)e->max_out * d.n_vocab * 4));
+    CK(e->amax.alloc((size_t)e->max_out * 8));
+    CK(cudaMemset(e->amax.p, 0, (size_t)e->max_out * 8));
     CK(e->err.alloc(4));
     CK(cudaMemset(e->err.p, 0, 4));
     return BT_OK;
@@ -776,8 +781,10 @@ extern "C" int bt_kv_export_layer(const bt_kv *kvc, uint32_t seq, uint32_t layer
     const bt_model_desc &d = kv->e->d;
     if (layer >= d.n_layer) return fail(BT_ERR_INVALID, "layer out of range");
     const size_t step = (size_t)d.n_head_kv * d.head_dim * 2;
-    const uint32_t n = kv->layer_pos[seq][layer];
-    if (bytes != n * step) return fail(BT_ERR_KV, "export buffer must hold exactly the layer's positions");
+    const uint32_t held = kv->layer_pos[seq][layer];
+    if (bytes % step || bytes > held * step)
+        return fail(BT_ERR_KV, "export size must be whole positions, at most the layer's");
+    const uint32_t n = (uint32_t)(bytes / step);
     if (!n) return BT_OK;
     if (!k_out || !v_out) return fail(BT_ERR_INVALID, "null output buffer");
     if ((r = kv_sync(kv))) return r;
@@ -876,8 +883,11 @@ static GemvSeg make_seg(const QMat &m, int tile0, int out_off) {
 
 static cudaError_t run_gemv(bt_engine *e, const QMat *const *mats, const int *out_offs, int nseg, const float *x,
                             long long x_stride, const int *x_rows, const float *norm_w, int K, int T, float *y,
-                            long long y_stride, const float *res, long long res_stride, const char *name) {
+                            long long y_stride, const float *res, long long res_stride, const char *name,
+                            unsigned long long *amax = nullptr, const PrefetchSpec *pf = nullptr) {
     GemvArgs a{};
+    a.amax = amax;
+    if (pf) a.pf = *pf;
     int tile0 = 0, slot = 0;
     for (int i = 0; i < nseg; i++) {
         a.seg[i] = make_seg(*mats[i], tile0, out_offs[i]);
@@ -953,12 +963,32 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
     }
     for (uint32_t il = 0; il < d.n_layer; il++) {
         Layer &l = e->L[il];
+        // while q/k/v run: pull this layer's KV pages, attn_output and router weights into L2
+        PrefetchSpec pf_qkv{};
+        pf_qkv.ptr[0] = l.o.buf.p;
+        pf_qkv.bytes[0] = l.o.buf.n;
+        pf_qkv.ptr[1] = l.gate_inp.p;
+        pf_qkv.bytes[1] = l.gate_inp.n;
+        pf_qkv.n = e->prefetch ? 2 : 0;
+        if (e->prefetch && T <= MAX_T) {
+            pf_qkv.kv = kv->pool.as<__half>();
+            pf_qkv.block_table = kv->bt_dev.as<int>();
+            pf_qkv.seq_of = e->seq_of.as<int>();
+            pf_qkv.pos_of = e->pos_of.as<int>();
+            pf_qkv.max_blocks = kv->max_blocks;
+            pf_qkv.layer = (int)il;
+            pf_qkv.n_blocks = kv->n_blocks;
+            pf_qkv.HK = HK;
+            pf_qkv.D = D;
+            pf_qkv.T = T;
+        }
         for (int t0 = 0; t0 < T; t0 += MAX_T) {
             int tg = T - t0 < MAX_T ? T - t0 : MAX_T;
             const QMat *mats[3] = {&l.q, &l.k, &l.v};
             int offs[3] = {0, QW, QW + KW};
             CK(run_gemv(e, mats, offs, 3, e->x.as<float>() + (size_t)t0 * E, E, nullptr, l.attn_norm.as<float>(), E, tg,
-                        e->qkv.as<float>() + (size_t)t0 * (QW + 2 * KW), QW + 2 * KW, nullptr, 0, "qkv_gemv"));
+                        e->qkv.as<float>() + (size_t)t0 * (QW + 2 * KW), QW + 2 * KW, nullptr, 0, "qkv_gemv", nullptr,
+                        t0 == 0 ? &pf_qkv : nullptr));
         }
         {
             QkvPostArgs a{};
@@ -1071,6 +1101,21 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.x_out = e->x.as<float>() + (size_t)t0 * E;
             a.single = e->single.as<unsigned char>() + t0;
             a.err = err;
+            if (e->prefetch && t0 == 0 && il + 1 < d.n_layer) {  // the next layer's q/k/v weights
+                const Layer &n = e->L[il + 1];
+                a.pf.ptr[0] = n.q.buf.p;
+                a.pf.bytes[0] = n.q.buf.n;
+                a.pf.ptr[1] = n.k.buf.p;
+                a.pf.bytes[1] = n.k.buf.n;
+                a.pf.ptr[2] = n.v.buf.p;
+                a.pf.bytes[2] = n.v.buf.n;
+                a.pf.n = 3;
+            } else if (e->prefetch && t0 == 0) {  // the output head
+                a.pf.ptr[0] = e->out.buf.p;
+                a.pf.bytes[0] = e->out.buf.n < (64ull << 20) ? e->out.buf.n : (64ull << 20);
+                a.pf.n = 1;
+            }
+            a.prefetch_down = e->prefetch ? 1 : 0;
             a.slot_bytes = a.g_tile_bytes + a.u_tile_bytes;
             a.nst = 1;
             a.nst = pick_nst(a.slot_bytes, gateup_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes);
@@ -1080,6 +1125,8 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.slot_bytes = K * a.d_tile_bytes;
             a.nst = 1;
             a.nst = pick_nst(a.slot_bytes, down_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes);
+            a.pf = PrefetchSpec{};
+            a.prefetch_down = 0;
             timer_begin(e, "expert_down");
             CK(launch_down(a, grid_for(e, (long long)tg * E), st, pdl));
             timer_end(e);
@@ -1091,7 +1138,8 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
         const QMat *mats[1] = {&e->out};
         int offs[1] = {0};
         CK(run_gemv(e, mats, offs, 1, e->x.as<float>(), E, e->x_rows.as<int>() + o0, e->out_norm.as<float>(), E, og,
-                    e->logits.as<float>() + (size_t)(p.out_first + o0) * d.n_vocab, d.n_vocab, nullptr, 0, "output_gemv"));
+                    e->logits.as<float>() + (size_t)(p.out_first + o0) * d.n_vocab, d.n_vocab, nullptr, 0, "output_gemv",
+                    e->amax.as<unsigned long long>() + p.out_first + o0));
     }
     {
         StepEndArgs a{};
@@ -1102,6 +1150,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
         a.seq_ids = e->st_seq.as<int>();
         a.n_tok = e->st_ntok.as<int>();
         a.logit_row = e->st_lrow.as<int>();
+        a.amax = e->amax.as<unsigned long long>();
         a.dev_len = kv->dev_len.as<int>();
         a.next_token = e->next_tok.as<int>();
         a.tokens_buf = greedy ? e->tokens.as<int>() : nullptr;
@@ -1193,6 +1242,7 @@ extern "C" int bt_forward(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, cons
         if ((r = upload_plan(e, p))) return r;
         if ((r = launch_step(e, kv, p, false))) return r;
         e->last_T = p.T;
+        e->last_first = g - p.T;
     }
     if ((r = check_err(e))) return r;
     if (logits_out)
@@ -1265,6 +1315,8 @@ static int greedy_finish(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, uint3
         for (auto &c : kv->layer_pos[s]) c = kv->len[s];
     }
     e->stats.tokens += (uint64_t)n_steps * n_seqs;
+    e->last_T = (int)n_seqs;
+    e->last_first = 0;
     return BT_OK;
 }
 
@@ -1349,6 +1401,12 @@ extern "C" int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_id
 
 extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
     if (!e || !name) return fail(BT_ERR_INVALID, "null argument");
+    if (!strcmp(name, "prefetch")) {
+        e->prefetch = value != 0;
+        for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
+        e->graphs.clear();
+        return BT_OK;
+    }
     if (!strcmp(name, "pdl")) {
         e->pdl = value != 0;
         for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
@@ -1361,9 +1419,11 @@ extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
 // ------------------------------------------------------------------ parity hooks
 extern "C" int bt_debug_topk(const bt_engine *e, uint32_t layer, uint32_t token, int32_t *ids, float *weights) {
     if (!e || !ids || !weights) return fail(BT_ERR_INVALID, "null argument");
-    if (layer >= e->d.n_layer || (int)token >= e->last_T) return fail(BT_ERR_INVALID, "layer or token out of range");
+    if (layer >= e->d.n_layer) return fail(BT_ERR_INVALID, "layer out of range");
+    if (token < e->last_first || token >= e->last_first + e->last_T)
+        return fail(BT_ERR_INVALID, "token is not in the last step of the last forward (the last 64 tokens)");
     const int K = e->d.n_expert_used;
-    size_t off = ((size_t)layer * e->TB + token) * K;
+    size_t off = ((size_t)layer * e->TB + (token - e->last_first)) * K;
     CK(cudaMemcpy(ids, e->dbg_ids.as<int>() + off, K * 4, cudaMemcpyDeviceToHost));
     CK(cudaMemcpy(weights, e->dbg_w.as<float>() + off, K * 4, cudaMemcpyDeviceToHost));
     return BT_OK;
@@ -1371,8 +1431,9 @@ extern "C" int bt_debug_topk(const bt_engine *e, uint32_t layer, uint32_t token,
 
 extern "C" int bt_debug_hidden(const bt_engine *e, uint32_t token, float *out) {
     if (!e || !out) return fail(BT_ERR_INVALID, "null argument");
-    if ((int)token >= e->last_T) return fail(BT_ERR_INVALID, "token out of range");
-    CK(cudaMemcpy(out, e->x.as<float>() + (size_t)token * e->d.n_embd, e->d.n_embd * 4, cudaMemcpyDeviceToHost));
+    if (token < e->last_first || token >= e->last_first + e->last_T)
+        return fail(BT_ERR_INVALID, "token is not in the last step of the last forward (the last 64 tokens)");
+    CK(cudaMemcpy(out, e->x.as<float>() + (size_t)(token - e->last_first) * e->d.n_embd, e->d.n_embd * 4, cudaMemcpyDeviceToHost));
     return BT_OK;
 }
 

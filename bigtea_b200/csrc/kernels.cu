@@ -127,6 +127,47 @@ __global__ void synth_kernel(int type, uint64_t key, long long n_elems, float me
     }
 }
 
+// ====================================================================== L2 prefetch of upcoming inputs
+// Pieces of 64 KB go round-robin over the CTAs first (then over a CTA's threads), so every
+// SM's TMA unit carries a share of the traffic.
+constexpr unsigned long long PREFETCH_PIECE = 64ull << 10;
+
+__device__ __forceinline__ bool prefetch_owner(unsigned long long k) {
+    return (int)(k % gridDim.x) == (int)blockIdx.x && (int)((k / gridDim.x) % blockDim.x) == (int)threadIdx.x;
+}
+
+__device__ void prefetch_ranges_spread(const void *const *ptrs, const unsigned long long *bytes, int n,
+                                       unsigned long long &k) {
+    for (int i = 0; i < n; i++) {
+        const char *c = reinterpret_cast<const char *>(ptrs[i]);
+        const unsigned long long np = (bytes[i] + PREFETCH_PIECE - 1) / PREFETCH_PIECE;
+        for (unsigned long long q = 0; q < np; q++, k++) {
+            if (!prefetch_owner(k)) continue;
+            const unsigned long long off = q * PREFETCH_PIECE;
+            const unsigned long long len = bytes[i] - off < PREFETCH_PIECE ? bytes[i] - off : PREFETCH_PIECE;
+            prefetch_l2(c + off, (uint32_t)(len & ~15ull));
+        }
+    }
+}
+
+__device__ void run_prefetch(const PrefetchSpec &pf) {
+    unsigned long long k = 0;
+    prefetch_ranges_spread(pf.ptr, pf.bytes, pf.n, k);
+    if (pf.kv) {
+        const unsigned long long page = 2ull * pf.HK * 16 * pf.D * 2;  // K and V of one page, contiguous
+        for (int t = 0; t < pf.T; t++) {
+            const int np = pf.pos_of[t] / 16 + 1;
+            const int seq = pf.seq_of[t];
+            for (int pg = 0; pg < np; pg++, k++) {
+                if (!prefetch_owner(k)) continue;
+                const int blk = pf.block_table[seq * pf.max_blocks + pg];
+                const unsigned long long row = (((unsigned long long)pf.layer * pf.n_blocks + blk) * 2) * pf.HK * 16;
+                prefetch_l2(pf.kv + row * pf.D, (uint32_t)page);
+            }
+        }
+    }
+}
+
 // ====================================================================== activation staging
 // C3 over one 256-value block held 8 values per lane (lane l: elements 8l..8l+7).
 __device__ __forceinline__ void quantize_block_warp(const float v[8], ActBlock *dst, int lane) {
@@ -186,9 +227,7 @@ __device__ void stage_activations(const float *x, long long x_stride, const int 
     if (norm_w) {
         for (int t = warp; t < T; t += NWARP) {
             const float *xt = x + (long long)(x_rows ? x_rows[t] : t) * x_stride;
-            float acc = 0.0f;
-            for (int i = lane; i < K; i += 32) acc = fmaf(xt[i], xt[i], acc);
-            acc = butterfly_sum(acc);
+            float acc = warp_sumsq_p2(xt, K, lane);
             if (lane == 0) normS[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)K), eps)));
         }
         __syncthreads();
@@ -257,10 +296,14 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_kernel(const __grid_consta
         for (int i = 0; i < p.nst && i < nmine; i++) issue(i);
 
     pdl_wait();
+    run_prefetch(p.pf);
     stage_activations<NWARP>(p.x, p.x_stride, p.x_rows, p.norm_w, p.eps, p.K, p.T, act, normS);
     __syncthreads();
     pdl_trigger();
 
+    unsigned long long best[MAX_T];
+#pragma unroll
+    for (int t = 0; t < MAX_T; t++) best[t] = 0ull;
     int j = 0;
     for (; j < nmine; j++) {
         const int slot = j % p.nst;
@@ -289,6 +332,13 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_kernel(const __grid_consta
                 float r = acc;
                 if (p.res) r = __fadd_rn(p.res[t * p.res_stride + sg.out_off + row], acc);
                 p.y[t * p.y_stride + sg.out_off + row] = r;
+                if (p.amax) {
+                    unsigned long long key = ((unsigned long long)((unsigned)total_key(r) ^ 0x80000000u) << 32) |
+                                             (unsigned)(sg.out_off + row);
+#pragma unroll
+                    for (int tt = 0; tt < MAX_T; tt++)
+                        if (tt == t && key > best[tt]) best[tt] = key;
+                }
             }
         }
         __syncwarp();
@@ -299,6 +349,27 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_kernel(const __grid_consta
     }
     if (j < nmine) {  // a wait ran out: let any copy still in flight land (bounded) before exiting
         for (int k = j; k < nmine && k < j + p.nst; k++) mbar_wait(&mybar[k % p.nst], (k / p.nst) & 1, nullptr);
+    }
+    if (p.amax) {  // argmax of the rows this CTA wrote: one 64-bit atomicMax per token
+        __shared__ unsigned long long s_best[MAX_T][NWARP];
+        for (int t = 0; t < p.T; t++) {
+            unsigned long long b = best[0];
+#pragma unroll
+            for (int tt = 1; tt < MAX_T; tt++)
+                if (tt == t) b = best[tt];
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) {
+                unsigned long long ob = __shfl_xor_sync(FULL, b, o);
+                b = ob > b ? ob : b;
+            }
+            if (lane == 0) s_best[t][warp] = b;
+        }
+        __syncthreads();
+        if (threadIdx.x < p.T) {
+            unsigned long long b = 0;
+            for (int w = 0; w < NWARP; w++) b = s_best[threadIdx.x][w] > b ? s_best[threadIdx.x][w] : b;
+            atomicMax(p.amax + threadIdx.x, b);
+        }
     }
 }
 
@@ -353,6 +424,15 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gateup_kernel(const __grid_cons
     }
     __syncwarp();
     pdl_wait();  // expert ids come from the router
+    run_prefetch(p.pf);
+    if (p.prefetch_down) {  // the down weights of the selected experts, for the next kernel
+        unsigned long long k = 1ull << 40;  // a fresh round-robin start
+        for (int q = 0; q < p.T * p.K; q++) {
+            const void *ptr = p.down + p.sel_ids[q] * p.d_expert_bytes;
+            const unsigned long long nb = (unsigned long long)p.d_expert_bytes;
+            prefetch_ranges_spread(&ptr, &nb, 1, k);
+        }
+    }
 
     auto issue = [&](int j) {
         long long u = u0 + warp + (long long)j * NWARP;
@@ -436,6 +516,7 @@ __global__ void __launch_bounds__(NWARP * 32, 1) down_kernel(const __grid_consta
     }
     __syncwarp();
     pdl_wait();
+    run_prefetch(p.pf);
 
     auto issue = [&](int j) {
         long long u = u0 + warp + (long long)j * NWARP;
@@ -528,10 +609,14 @@ cudaError_t launch_down(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl
 }
 
 // ====================================================================== router
-// grid (ceil(NE/rows_per_cta), T), 128 threads. Each CTA normalises the token (C6), computes
-// its rows of the F32 router (C5); the last CTA of a token (atomic ticket) runs soft_max_ext
-// and route(): stable descending order by total_cmp, top-K, renormalised over the selection.
+// grid (ceil(NE/4), T), 128 threads: each CTA normalises the token (C6) into shared memory and
+// warp w computes router row blockIdx.x*4+w (C5). The token's last CTA (atomic ticket) runs
+// soft_max_ext and route(): stable descending order by total_cmp, top-K, renormalised over
+// the selection.
+constexpr int ROUTER_ROWS = 4;
+
 __global__ void __launch_bounds__(128) router_kernel(const __grid_constant__ RouterArgs p) {
+    extern __shared__ float s_y[];  // [E] normalised activations
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int t = blockIdx.y;
     __shared__ float s_norm;
@@ -542,23 +627,19 @@ __global__ void __launch_bounds__(128) router_kernel(const __grid_constant__ Rou
     pdl_wait();
     const float *x = p.x + (long long)t * p.E;
     if (warp == 0) {
-        float acc = 0.0f;
-        for (int i = lane; i < p.E; i += 32) acc = fmaf(x[i], x[i], acc);
-        acc = butterfly_sum(acc);
+        float acc = warp_sumsq_p2(x, p.E, lane);
         if (lane == 0) s_norm = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)p.E), p.eps)));
     }
     __syncthreads();
     pdl_trigger();
     const float s = s_norm;
+    for (int i = threadIdx.x; i < p.E; i += blockDim.x) s_y[i] = __fmul_rn(__fmul_rn(x[i], s), p.norm_w[i]);
+    __syncthreads();
     if (blockIdx.x == 0)
-        for (int i = threadIdx.x; i < p.E; i += blockDim.x)
-            p.fn_out[(long long)t * p.E + i] = __fmul_rn(__fmul_rn(x[i], s), p.norm_w[i]);
-    const int r0 = blockIdx.x * p.rows_per_cta;
-    for (int r = r0 + warp; r < r0 + p.rows_per_cta && r < p.NE; r += 4) {
-        const float *wr = p.Wr + (long long)r * p.E;
-        float acc = 0.0f;
-        for (int i = lane; i < p.E; i += 32) acc = fmaf(wr[i], __fmul_rn(__fmul_rn(x[i], s), p.norm_w[i]), acc);
-        acc = butterfly_sum(acc);
+        for (int i = threadIdx.x; i < p.E; i += blockDim.x) p.fn_out[(long long)t * p.E + i] = s_y[i];
+    const int r = blockIdx.x * ROUTER_ROWS + warp;
+    if (r < p.NE) {
+        float acc = warp_dot_p2(p.Wr + (long long)r * p.E, s_y, p.E, lane);
         if (lane == 0) p.logits[(long long)t * p.NE + r] = acc;
     }
     __threadfence();
@@ -567,62 +648,67 @@ __global__ void __launch_bounds__(128) router_kernel(const __grid_constant__ Rou
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    if (warp != 0) return;
-    const float *lg = p.logits + (long long)t * p.NE;
-    float m = -__int_as_float(0x7f800000);
-    for (int i = lane; i < p.NE; i += 32) m = fmaxf(m, __ldcg(lg + i));
-    m = warp_max(m);
-    float acc = 0.0f;
-    for (int i = lane; i < p.NE; i += 32) {
-        float e = bt_exp(__fsub_rn(__ldcg(lg + i), m));
-        s_prob[i] = e;
-        acc = __fadd_rn(acc, e);
-    }
-    acc = butterfly_sum(acc);
-    const float inv = __fdiv_rn(1.0f, acc);
-    for (int i = lane; i < p.NE; i += 32) s_prob[i] = __fmul_rn(s_prob[i], inv);
-    __syncwarp();
-    for (int i = lane; i < p.NE; i += 32) {
-        int ki = total_key(s_prob[i]);
-        int rank = 0;
-        for (int jj = 0; jj < p.NE; jj++) {
-            int kj = total_key(s_prob[jj]);
-            rank += (kj > ki) || (kj == ki && jj < i);
+    if (warp == 0) {
+        const float *lg = p.logits + (long long)t * p.NE;
+        float m = -__int_as_float(0x7f800000);
+        for (int i = lane; i < p.NE; i += 32) {
+            float v = __ldcg(lg + i);
+            s_prob[i] = v;
+            m = fmaxf(m, v);
         }
-        if (rank < p.K) {
-            s_rank_id[rank] = i;
-            s_rank_p[rank] = s_prob[i];
+        m = warp_max(m);
+        float acc = 0.0f;
+        for (int i = lane; i < p.NE; i += 32) {
+            float e = bt_exp(__fsub_rn(s_prob[i], m));
+            s_prob[i] = e;
+            acc = __fadd_rn(acc, e);
         }
-    }
-    __syncwarp();
-    if (lane == 0) {
-        float total = 0.0f;
-        for (int r = 0; r < p.K; r++) total = __fadd_rn(total, s_rank_p[r]);
-        int ids[MAX_K];
-        float ws[MAX_K];
-        for (int r = 0; r < p.K; r++) {
-            float w = total > 0.0f ? __fdiv_rn(s_rank_p[r], total) : s_rank_p[r];
-            ids[r] = s_rank_id[r];
-            ws[r] = w;
-            p.topk_ids[t * p.K + r] = ids[r];
-            p.topk_w[t * p.K + r] = w;
-        }
-        for (int a = 1; a < p.K; a++)
-            for (int b = a; b > 0 && ids[b - 1] > ids[b]; b--) {
-                int ti = ids[b]; ids[b] = ids[b - 1]; ids[b - 1] = ti;
-                float tw = ws[b]; ws[b] = ws[b - 1]; ws[b - 1] = tw;
+        acc = butterfly_sum(acc);
+        const float inv = __fdiv_rn(1.0f, acc);
+        for (int i = lane; i < p.NE; i += 32) s_prob[i] = __fmul_rn(s_prob[i], inv);
+        __syncwarp();
+        for (int i = lane; i < p.NE; i += 32) {
+            int ki = total_key(s_prob[i]);
+            int rank = 0;
+            for (int jj = 0; jj < p.NE; jj++) {
+                int kj = total_key(s_prob[jj]);
+                rank += (kj > ki) || (kj == ki && jj < i);
             }
-        for (int r = 0; r < p.K; r++) {
-            p.sel_ids[t * p.K + r] = ids[r];
-            p.sel_w[t * p.K + r] = ws[r];
+            if (rank < p.K) {
+                s_rank_id[rank] = i;
+                s_rank_p[rank] = s_prob[i];
+            }
         }
-        p.cnt[t] = 0;
+        __syncwarp();
+        if (lane == 0) {
+            float total = 0.0f;
+            for (int q = 0; q < p.K; q++) total = __fadd_rn(total, s_rank_p[q]);
+            int ids[MAX_K];
+            float ws[MAX_K];
+            for (int q = 0; q < p.K; q++) {
+                float w = total > 0.0f ? __fdiv_rn(s_rank_p[q], total) : s_rank_p[q];
+                ids[q] = s_rank_id[q];
+                ws[q] = w;
+                p.topk_ids[t * p.K + q] = ids[q];
+                p.topk_w[t * p.K + q] = w;
+            }
+            for (int a = 1; a < p.K; a++)
+                for (int b = a; b > 0 && ids[b - 1] > ids[b]; b--) {
+                    int ti = ids[b]; ids[b] = ids[b - 1]; ids[b - 1] = ti;
+                    float tw = ws[b]; ws[b] = ws[b - 1]; ws[b - 1] = tw;
+                }
+            for (int q = 0; q < p.K; q++) {
+                p.sel_ids[t * p.K + q] = ids[q];
+                p.sel_w[t * p.K + q] = ws[q];
+            }
+            p.cnt[t] = 0;
+        }
     }
 }
 
 cudaError_t launch_router(const RouterArgs &a, cudaStream_t st, bool pdl) {
-    dim3 grid((a.NE + a.rows_per_cta - 1) / a.rows_per_cta, a.T);
-    return launch_ex(router_kernel, grid, dim3(128), 0, st, pdl, a);
+    dim3 grid((a.NE + ROUTER_ROWS - 1) / ROUTER_ROWS, a.T);
+    return launch_ex(router_kernel, grid, dim3(128), (size_t)a.E * 4, st, pdl, a);
 }
 
 // ====================================================================== q/k norm, RoPE, KV append
@@ -697,26 +783,44 @@ cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl) {
 
 // ====================================================================== attention
 // grid (max_chunks, HK, T), 256 threads, one CTA per (token, kv head, chunk of 256 keys).
-// K and V pages are fetched with 2-D TMA (128-byte swizzle, box 64 x 16) into shared memory;
-// thread j owns key j for the scores, thread (d, head group) owns an output column for P*V.
-// A chunk writes (m, l, acc) to scratch; the last chunk of a (token, head) combines (C8).
+// K and V pages arrive by 2-D TMA (128-byte swizzle, box 64 x 16) in shared memory. Scores:
+// thread (hh, kp) owns keys kp and kp+128 for heads [hh*G/2, hh*G/2+G/2), each a sequential
+// fmaf dot over d. P*V: thread (hq, d) owns column d for heads [hq*G/2, hq*G/2+G/2), a
+// sequential fmaf over the chunk's keys. A chunk writes (m, l, acc) to scratch; the last
+// chunk of a (token, kv head) combines them in chunk order (C8).
 constexpr int ATTN_THREADS = 256;
+constexpr int ATTN_PART_ROW = 132;  // floats per (chunk, head) partial: acc[128], m, l, 2 pad (16-byte rows)
 
-size_t attn_smem_bytes(int G) {
-    return 4 * 32768 + (size_t)128 * G * 4 + (size_t)ATTN_CHUNK * G * 4 + 8 * 8 * 4 * 2 + 64 + 1024;
+size_t attn_smem_bytes(int G, int max_chunks) {
+    (void)max_chunks;  // the combine reuses the K tile region
+    return 4 * 32768 + (size_t)128 * G * 4 + (size_t)ATTN_CHUNK * G * 4 + 2 * 8 * 8 * 4 + 64 + 1024;
 }
 
+template <int N>
+__device__ __forceinline__ void lds_vec(float (&dst)[N], const float *src) {
+    if constexpr (N == 4) {
+        float4 v = *reinterpret_cast<const float4 *>(src);
+        dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+    } else if constexpr (N == 2) {
+        float2 v = *reinterpret_cast<const float2 *>(src);
+        dst[0] = v.x; dst[1] = v.y;
+    } else {
+#pragma unroll
+        for (int k = 0; k < N; k++) dst[k] = src[k];
+    }
+}
+
+template <int G>
 __global__ void __launch_bounds__(ATTN_THREADS, 1)
     attn_kernel(const __grid_constant__ AttnArgs p, const __grid_constant__ CUtensorMap tmap) {
+    constexpr int D = 128, HPT = G / 2;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t *Kr[2] = {smem, smem + 32768};
-    uint8_t *Vr[2] = {smem + 65536, smem + 98304};
-    const int G = p.G, D = 128;
-    float *qs = reinterpret_cast<float *>(smem + 131072);          // [D][G]
-    float *ps = qs + D * G;                                        // [256][G]
-    float *red = ps + ATTN_CHUNK * G;                              // [8][8]
-    float *red2 = red + 64;                                        // [8][8]
+    uint8_t *const K0 = smem, *const K1 = smem + 32768, *const V0 = smem + 65536, *const V1 = smem + 98304;
+    float *qs = reinterpret_cast<float *>(smem + 131072);  // [D][G]
+    float *ps = qs + D * G;                                // [256][G]
+    float *red = ps + ATTN_CHUNK * G;                      // [8 warps][8]
+    float *red2 = red + 64;                                // [8 key groups][8]
     uint64_t *bar = reinterpret_cast<uint64_t *>(red2 + 64);
     __shared__ int s_last;
     __shared__ float s_m[8], s_l[8];
@@ -745,10 +849,10 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
             int blk = p.block_table[seq * p.max_blocks + (base >> 4) + pg];
             int rowK = (int)(((((long long)p.layer * p.n_blocks + blk) * 2 + 0) * p.HK + g) * 16);
             int rowV = rowK + p.HK * 16;
-            tma_load_2d(Kr[0] + pg * 2048, &tmap, 0, rowK, bar);
-            tma_load_2d(Kr[1] + pg * 2048, &tmap, 64, rowK, bar);
-            tma_load_2d(Vr[0] + pg * 2048, &tmap, 0, rowV, bar);
-            tma_load_2d(Vr[1] + pg * 2048, &tmap, 64, rowV, bar);
+            tma_load_2d(K0 + pg * 2048, &tmap, 0, rowK, bar);
+            tma_load_2d(K1 + pg * 2048, &tmap, 64, rowK, bar);
+            tma_load_2d(V0 + pg * 2048, &tmap, 0, rowV, bar);
+            tma_load_2d(V1 + pg * 2048, &tmap, 64, rowV, bar);
         }
     }
     pdl_trigger();
@@ -762,51 +866,65 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         if (tid == 0) mbar_wait(bar, 0, nullptr);
         return;
     }
-    // scores: thread j owns key j (sequential fmaf over d, C8)
-    const int j = tid;
-    const bool valid = j < cnt;
-    float s[8];
+
+    // ---- scores: keys kp and kp+128, heads hh*HPT .. +HPT
+    const int hh = tid >> 7, kp = tid & 127;
+    const bool v0 = kp < cnt, v1 = kp + 128 < cnt;
+    float s0[HPT], s1[HPT];
 #pragma unroll
-    for (int h = 0; h < 8; h++) s[h] = 0.0f;
-    if (valid) {
-#pragma unroll 1
+    for (int h = 0; h < HPT; h++) s0[h] = s1[h] = 0.0f;
+    {
+        const int ka = kp, kb = kp + 128;
+#pragma unroll 2
         for (int c16 = 0; c16 < 16; c16++) {
-            const uint8_t *kr = Kr[c16 >> 3] + j * 128 + ((((c16 & 7) ^ (j & 7))) << 4);
-            uint4 kv = *reinterpret_cast<const uint4 *>(kr);
-            const __half *hk = reinterpret_cast<const __half *>(&kv);
+            const uint8_t *kr = (c16 < 8) ? K0 : K1;
+            const int cc = c16 & 7;
+            uint4 wa = *reinterpret_cast<const uint4 *>(kr + ka * 128 + ((cc ^ (ka & 7)) << 4));
+            uint4 wb = *reinterpret_cast<const uint4 *>(kr + kb * 128 + ((cc ^ (kb & 7)) << 4));
+            const __half *ha = reinterpret_cast<const __half *>(&wa);
+            const __half *hb = reinterpret_cast<const __half *>(&wb);
 #pragma unroll
             for (int e = 0; e < 8; e++) {
-                float kf = __half2float(hk[e]);
-                const float *qd = qs + (c16 * 8 + e) * G;
+                const float fa = __half2float(ha[e]), fb = __half2float(hb[e]);
+                float q[HPT];
+                lds_vec<HPT>(q, qs + (c16 * 8 + e) * G + hh * HPT);
 #pragma unroll
-                for (int h = 0; h < 8; h++)
-                    if (h < G) s[h] = fmaf(qd[h], kf, s[h]);
+                for (int h = 0; h < HPT; h++) {
+                    s0[h] = fmaf(q[h], fa, s0[h]);
+                    s1[h] = fmaf(q[h], fb, s1[h]);
+                }
             }
         }
     }
+    const float NEG_INF = -__int_as_float(0x7f800000);
 #pragma unroll
-    for (int h = 0; h < 8; h++) s[h] = valid ? __fmul_rn(s[h], p.scale) : -__int_as_float(0x7f800000);
-    // per-head chunk max
-#pragma unroll
-    for (int h = 0; h < 8; h++) {
-        float m = warp_max(s[h]);
+    for (int h = 0; h < HPT; h++) {
+        s0[h] = v0 ? __fmul_rn(s0[h], p.scale) : NEG_INF;
+        s1[h] = v1 ? __fmul_rn(s1[h], p.scale) : NEG_INF;
+        float m = warp_max(fmaxf(s0[h], s1[h]));
         if (lane == 0) red[warp * 8 + h] = m;
     }
     __syncthreads();
-    if (tid < G) {
-        float m = red[tid];
-        for (int w = 1; w < 8; w++) m = fmaxf(m, red[w * 8 + tid]);
+    if (tid < G) {  // head tid lives in warps (tid / HPT) * 4 .. +3, slot tid % HPT
+        const int w0 = (tid / HPT) * 4, slot = tid % HPT;
+        float m = red[w0 * 8 + slot];
+        for (int w = 1; w < 4; w++) m = fmaxf(m, red[(w0 + w) * 8 + slot]);
         s_m[tid] = m;
     }
     __syncthreads();
-    // probabilities and the P3 sum
+    // ---- probabilities and the P3 sum: warp (hh, q) holds key groups q and q+4
 #pragma unroll
-    for (int h = 0; h < 8; h++) {
-        if (h < G) {
-            float pr = valid ? bt_exp(__fsub_rn(s[h], s_m[h])) : 0.0f;
-            ps[j * G + h] = pr;
-            float ws = butterfly_sum(pr);
-            if (lane == 0) red2[warp * 8 + h] = ws;
+    for (int h = 0; h < HPT; h++) {
+        const int head = hh * HPT + h;
+        const float m = s_m[head];
+        const float p0 = v0 ? bt_exp(__fsub_rn(s0[h], m)) : 0.0f;
+        const float p1 = v1 ? bt_exp(__fsub_rn(s1[h], m)) : 0.0f;
+        ps[kp * G + head] = p0;
+        ps[(kp + 128) * G + head] = p1;
+        const float w0 = butterfly_sum(p0), w1 = butterfly_sum(p1);
+        if (lane == 0) {
+            red2[(warp & 3) * 8 + head] = w0;
+            red2[((warp & 3) + 4) * 8 + head] = w1;
         }
     }
     __syncthreads();
@@ -815,42 +933,54 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         for (int w = 0; w < 8; w++) l = __fadd_rn(l, red2[w * 8 + tid]);
         s_l[tid] = l;
     }
-    // P*V: thread owns column d for heads [hq*G/2, hq*G/2 + G/2)
-    const int d = tid & 127, hq = tid >> 7, hpt = G / 2;
-    float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-    {
-        const uint8_t *vreg = Vr[d >> 6];
-        const int cc = (d & 63) >> 3, within = (d & 7) * 2;
-        for (int jj = 0; jj < cnt; jj++) {
-            const __half hv = *reinterpret_cast<const __half *>(vreg + jj * 128 + (((cc ^ (jj & 7))) << 4) + within);
-            const float vf = __half2float(hv);
-            const float *pj = ps + jj * G + hq * hpt;
+    // ---- P*V: column d, heads hq*HPT .. +HPT
+    const int d = tid & 127, hq = tid >> 7;
+    float acc[HPT];
 #pragma unroll
-            for (int h = 0; h < 4; h++)
-                if (h < hpt) acc[h] = fmaf(pj[h], vf, acc[h]);
+    for (int h = 0; h < HPT; h++) acc[h] = 0.0f;
+    {
+        const int cc = (d & 63) >> 3;
+        const uint8_t *vcol = ((d < 64) ? V0 : V1) + (d & 7) * 2;
+        int off[8];
+#pragma unroll
+        for (int k = 0; k < 8; k++) off[k] = k * 128 + ((cc ^ k) << 4);
+        for (int j0 = 0; j0 < cnt; j0 += 8) {
+            const uint8_t *vb = vcol + j0 * 128;
+            const float *pb = ps + j0 * G + hq * HPT;
+#pragma unroll
+            for (int k = 0; k < 8; k++) {
+                if (j0 + k < cnt) {
+                    const float vf = __half2float(*reinterpret_cast<const __half *>(vb + off[k]));
+                    float pj[HPT];
+                    lds_vec<HPT>(pj, pb + k * G);
+#pragma unroll
+                    for (int h = 0; h < HPT; h++) acc[h] = fmaf(pj[h], vf, acc[h]);
+                }
+            }
         }
     }
     __syncthreads();
     const int QW = p.H * D;
     if (nc == 1) {
-        for (int h = 0; h < hpt; h++) {
-            int hh = hq * hpt + h;
-            float M = s_m[hh];
-            float f = bt_exp(__fsub_rn(s_m[hh], M));
-            float L = fmaf(s_l[hh], f, 0.0f);
-            float O = fmaf(acc[h], f, 0.0f);
-            p.out[(long long)t * QW + (g * G + hh) * D + d] = __fdiv_rn(O, L);
+#pragma unroll
+        for (int h = 0; h < HPT; h++) {
+            const int head = hq * HPT + h;
+            const float f = bt_exp(__fsub_rn(s_m[head], s_m[head]));
+            const float L = fmaf(s_l[head], f, 0.0f);
+            const float O = fmaf(acc[h], f, 0.0f);
+            p.out[(long long)t * QW + (g * G + head) * D + d] = __fdiv_rn(O, L);
         }
         return;
     }
-    const long long pbase = (((long long)t * p.HK + g) * p.max_chunks) * G * (D + 2);
-    for (int h = 0; h < hpt; h++) {
-        int hh = hq * hpt + h;
-        float *pp = p.part + pbase + ((long long)c * G + hh) * (D + 2);
+    const long long pbase = (((long long)t * p.HK + g) * p.max_chunks) * G * ATTN_PART_ROW;
+#pragma unroll
+    for (int h = 0; h < HPT; h++) {
+        const int head = hq * HPT + h;
+        float *pp = p.part + pbase + ((long long)c * G + head) * ATTN_PART_ROW;
         pp[d] = acc[h];
         if (d == 0) {
-            pp[D] = s_m[hh];
-            pp[D + 1] = s_l[hh];
+            pp[D] = s_m[head];
+            pp[D + 1] = s_l[head];
         }
     }
     __threadfence();
@@ -859,35 +989,88 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    for (int h = 0; h < hpt; h++) {
-        int hh = hq * hpt + h;
-        float M = -__int_as_float(0x7f800000);
-        for (int cc = 0; cc < nc; cc++) M = fmaxf(M, __ldcg(p.part + pbase + ((long long)cc * G + hh) * (D + 2) + D));
-        float L = 0.0f, O = 0.0f;
+    // ---- combine (the last chunk's CTA): per-chunk m and l, then the acc rows in chunk
+    // order, streamed into shared memory as 1-D TMA slices of SL chunks
+    float *cm = reinterpret_cast<float *>(V0);  // [nc][G]  (the V tile is no longer needed)
+    float *cl = cm + nc * G;                    // [nc][G]
+    float *cf = cl + nc * G;                    // [nc][G]
+    for (int i = tid; i < nc * G; i += ATTN_THREADS) {
+        const float *pp = p.part + pbase + (long long)i * ATTN_PART_ROW;
+        cm[i] = __ldcg(pp + D);
+        cl[i] = __ldcg(pp + D + 1);
+    }
+    __syncthreads();
+    if (tid < G) {
+        float M = NEG_INF;
+        for (int cc = 0; cc < nc; cc++) M = fmaxf(M, cm[cc * G + tid]);
+        float L = 0.0f;
         for (int cc = 0; cc < nc; cc++) {
-            const float *pp = p.part + pbase + ((long long)cc * G + hh) * (D + 2);
-            float f = bt_exp(__fsub_rn(__ldcg(pp + D), M));
-            L = fmaf(__ldcg(pp + D + 1), f, L);
-            O = fmaf(__ldcg(pp + d), f, O);
+            const float f = bt_exp(__fsub_rn(cm[cc * G + tid], M));
+            cf[cc * G + tid] = f;
+            L = fmaf(cl[cc * G + tid], f, L);
         }
-        p.out[(long long)t * QW + (g * G + hh) * D + d] = __fdiv_rn(O, L);
+        s_l[tid] = L;
+    }
+    constexpr int ROWB = ATTN_PART_ROW * 4;
+    constexpr int SL = 65536 / (G * ROWB);  // chunks per slice in the 64 KB K tile region
+    float O[HPT];
+#pragma unroll
+    for (int h = 0; h < HPT; h++) O[h] = 0.0f;
+    uint32_t phase = 1;  // phase 0 of `bar` was the K/V load
+    const float *slice = reinterpret_cast<const float *>(K0);
+    for (int c0 = 0; c0 < nc; c0 += SL) {
+        const int n = nc - c0 < SL ? nc - c0 : SL;
+        __syncthreads();  // the previous slice (and the K tile) are no longer read
+        if (tid == 0) {
+            asm volatile("fence.proxy.async;" ::: "memory");
+            mbar_arrive_expect_tx(bar, (uint32_t)(n * G * ROWB));
+            bulk_g2s(K0, p.part + pbase + (long long)c0 * G * ATTN_PART_ROW, (uint32_t)(n * G * ROWB), bar);
+        }
+        const bool ok = mbar_wait(bar, phase, p.err);
+        phase ^= 1;
+        if (__syncthreads_or(!ok)) {
+            if (tid == 0) mbar_wait(bar, phase ^ 1, nullptr);
+            return;
+        }
+        for (int cc = 0; cc < n; cc++) {
+#pragma unroll
+            for (int h = 0; h < HPT; h++) {
+                const int head = hq * HPT + h;
+                O[h] = fmaf(slice[(cc * G + head) * ATTN_PART_ROW + d], cf[(c0 + cc) * G + head], O[h]);
+            }
+        }
+    }
+#pragma unroll
+    for (int h = 0; h < HPT; h++) {
+        const int head = hq * HPT + h;
+        p.out[(long long)t * QW + (g * G + head) * D + d] = __fdiv_rn(O[h], s_l[head]);
     }
     if (tid == 0) p.cnt[t * p.HK + g] = 0;
 }
 
-cudaError_t launch_attn(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl) {
-    size_t smem = attn_smem_bytes(a.G);
+template <int G>
+static cudaError_t launch_attn_g(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.max_chunks, a.HK, a.T);
     cfg.blockDim = dim3(ATTN_THREADS);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = attn_smem_bytes(G, a.max_chunks);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, attn_kernel, a, tmap);
+    return cudaLaunchKernelEx(&cfg, attn_kernel<G>, a, tmap);
+}
+
+cudaError_t launch_attn(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl) {
+    switch (a.G) {
+    case 2: return launch_attn_g<2>(a, tmap, st, pdl);
+    case 4: return launch_attn_g<4>(a, tmap, st, pdl);
+    case 6: return launch_attn_g<6>(a, tmap, st, pdl);
+    case 8: return launch_attn_g<8>(a, tmap, st, pdl);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 // ====================================================================== embedding and step end
@@ -940,78 +1123,59 @@ cudaError_t launch_embed(const EmbedArgs &a, cudaStream_t st, bool pdl) {
     return launch_ex(embed_kernel, dim3(a.T), dim3(256), 0, st, pdl, a);
 }
 
-// grid (n_seqs), 1024 threads: argmax with total_cmp, last maximum wins (sample.rs:928-935);
-// then advance the sequence's device length (advance_by) and, for the greedy loop, feed the
-// token back. CTA s handles sequence s of the step; logit_row[s] < 0 means no logits.
-__global__ void __launch_bounds__(1024) step_end_kernel(const __grid_constant__ StepEndArgs p) {
+// grid (n_seqs), 32 threads: the argmax of each sequence's logits was folded by the output
+// GEMV into a 64-bit (total_cmp key, row) maximum -- the last maximum wins, as max_by does
+// (sample.rs:928-935). Read it, reset the slot for the next step, advance the sequence's
+// device length (advance_by) and, for the greedy loop, feed the token back.
+__global__ void __launch_bounds__(32) step_end_kernel(const __grid_constant__ StepEndArgs p) {
     const int s = blockIdx.x;
-    __shared__ int s_key[32], s_idx[32];
     pdl_wait();
     pdl_trigger();
+    if (threadIdx.x != 0) return;
     const int lrow = p.logit_row ? p.logit_row[s] : -1;
-    int bk = -2147483647 - 1, bi = -1;
+    p.dev_len[p.seq_ids[s]] += p.n_tok[s];
     if (lrow >= 0) {
-        const float *lg = p.logits + (long long)lrow * p.V;
-        for (int i = threadIdx.x; i < p.V; i += blockDim.x) {
-            int k = total_key(lg[i]);
-            if (k >= bk) {
-                bk = k;
-                bi = i;
-            }
-        }
-#pragma unroll
-        for (int o = 16; o >= 1; o >>= 1) {
-            int ok = __shfl_xor_sync(FULL, bk, o), oi = __shfl_xor_sync(FULL, bi, o);
-            if (ok > bk || (ok == bk && oi > bi)) {
-                bk = ok;
-                bi = oi;
-            }
-        }
-        if ((threadIdx.x & 31) == 0) {
-            s_key[threadIdx.x >> 5] = bk;
-            s_idx[threadIdx.x >> 5] = bi;
-        }
-        __syncthreads();
-        if (threadIdx.x < 32) {
-            int nw = blockDim.x >> 5;
-            bk = threadIdx.x < nw ? s_key[threadIdx.x] : (-2147483647 - 1);
-            bi = threadIdx.x < nw ? s_idx[threadIdx.x] : -1;
-#pragma unroll
-            for (int o = 16; o >= 1; o >>= 1) {
-                int ok = __shfl_xor_sync(FULL, bk, o), oi = __shfl_xor_sync(FULL, bi, o);
-                if (ok > bk || (ok == bk && oi > bi)) {
-                    bk = ok;
-                    bi = oi;
-                }
-            }
-        }
-    }
-    if (threadIdx.x == 0) {
-        p.dev_len[p.seq_ids[s]] += p.n_tok[s];
-        if (lrow >= 0) {
-            p.next_token[lrow] = bi;
-            if (p.tokens_buf) p.tokens_buf[lrow] = bi;
-            if (p.gen_out) {
-                int k = p.gen_count[lrow]++;
-                p.gen_out[(long long)k * p.n_out + lrow] = bi;
-            }
+        const unsigned long long packed = p.amax[lrow];
+        p.amax[lrow] = 0ull;
+        const int bi = (int)(packed & 0xffffffffull);
+        p.next_token[lrow] = bi;
+        if (p.tokens_buf) p.tokens_buf[lrow] = bi;
+        if (p.gen_out) {
+            int k = p.gen_count[lrow]++;
+            p.gen_out[(long long)k * p.n_out + lrow] = bi;
         }
     }
 }
 
 cudaError_t launch_step_end(const StepEndArgs &a, cudaStream_t st, bool pdl) {
-    return launch_ex(step_end_kernel, dim3(a.n_seqs), dim3(1024), 0, st, pdl, a);
+    return launch_ex(step_end_kernel, dim3(a.n_seqs), dim3(32), 0, st, pdl, a);
 }
 
 // Large dynamic shared memory must be enabled per kernel and per device before the first
 // launch (and outside any stream capture): the engine calls this when it binds a device.
 cudaError_t init_kernel_attributes() {
-    const int cap = 227 * 1024;
+    int dev = 0, optin = 0;
     cudaError_t e;
-    if ((e = cudaFuncSetAttribute(gemv_kernel<GEMV_WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap))) return e;
-    if ((e = cudaFuncSetAttribute(gateup_kernel<GEMV_WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap))) return e;
-    if ((e = cudaFuncSetAttribute(down_kernel<GEMV_WARPS>, cudaFuncAttributeMaxDynamicSharedMemorySize, cap))) return e;
-    return cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, cap);
+    if ((e = cudaGetDevice(&dev))) return e;
+    if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
+    const void *kerns[] = {(const void *)gemv_kernel<GEMV_WARPS>, (const void *)gateup_kernel<GEMV_WARPS>,
+                           (const void *)down_kernel<GEMV_WARPS>, (const void *)attn_kernel<2>,
+                           (const void *)attn_kernel<4>,          (const void *)attn_kernel<6>,
+                           (const void *)attn_kernel<8>};
+    for (const void *k : kerns) {
+        cudaFuncAttributes fa;
+        if ((e = cudaFuncGetAttributes(&fa, k))) return e;
+        int dyn = optin - (int)fa.sharedSizeBytes;
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn))) return e;
+    }
+    return cudaSuccess;
+}
+
+int max_dynamic_smem() {
+    int dev = 0, optin = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    return optin - 2048;  // headroom for the kernels' static shared memory
 }
 
 // ====================================================================== one-off launchers

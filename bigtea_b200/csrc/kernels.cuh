@@ -13,6 +13,18 @@ constexpr int MAX_K = 16;       // experts used per token
 constexpr int ATTN_CHUNK = 256; // attention keys per chunk (contract C8)
 constexpr int GEMV_WARPS = 8;
 
+// Ranges to start pulling into L2 while a kernel runs (the next kernels' inputs), and
+// optionally one layer's KV pages of the step's sequences.
+struct PrefetchSpec {
+    const void *ptr[4];
+    unsigned long long bytes[4];
+    int n;
+    // KV pages of `layer` for every token's sequence (positions 0..pos_of[t])
+    const __half *kv;
+    const int *block_table, *seq_of, *pos_of;
+    int max_blocks, layer, n_blocks, HK, D, T;
+};
+
 struct GemvSeg {
     const uint8_t *w;  // tiled weights
     int type, nsb, rpt, S, tile_bytes;
@@ -37,6 +49,8 @@ struct GemvArgs {
     long long res_stride;
     int *err;
     int slot_bytes, nst;
+    unsigned long long *amax;  // optional: per token, max of (total_cmp key, row) over the output
+    PrefetchSpec pf;
 };
 
 struct ExpertArgs {
@@ -56,6 +70,8 @@ struct ExpertArgs {
     const unsigned char *single;  // [T] 1 = the token was a single-token step (paired order)
     int *err;
     int slot_bytes, nst;
+    PrefetchSpec pf;
+    int prefetch_down;  // gate/up: pull the selected experts' down weights into L2
 };
 
 struct RouterArgs {
@@ -112,6 +128,7 @@ struct StepEndArgs {
     int V, n_seqs, n_out;
     const int *seq_ids, *n_tok;
     const int *logit_row; // [n_seqs]: row of `logits` holding the sequence's last token, or -1
+    unsigned long long *amax;  // [n_out] argmax packed by the output GEMV; read and reset here
     int *dev_len;
     int *next_token;      // [n_out]
     int *tokens_buf;      // if non-null: tokens_buf[row] = argmax (greedy feed-back)
@@ -120,6 +137,7 @@ struct StepEndArgs {
 };
 
 cudaError_t init_kernel_attributes();
+int max_dynamic_smem();  // per-block dynamic shared memory the ring sizing may use
 
 // ---- launchers (all asynchronous on `st`; `pdl` enables programmatic dependent launch)
 size_t gemv_smem_bytes(const GemvArgs &a);
@@ -130,7 +148,7 @@ cudaError_t launch_gateup(const ExpertArgs &a, int grid, cudaStream_t st, bool p
 cudaError_t launch_down(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_router(const RouterArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl);
-size_t attn_smem_bytes(int G);
+size_t attn_smem_bytes(int G, int max_chunks);
 cudaError_t launch_attn(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl);
 cudaError_t launch_embed(const EmbedArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_step_end(const StepEndArgs &a, cudaStream_t st, bool pdl);

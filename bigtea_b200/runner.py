@@ -8,6 +8,7 @@ runs on the GPU through libbigtea_decode.so; there is no host compute path.
 from __future__ import annotations
 
 import ctypes as C
+import weakref
 
 import numpy as np
 
@@ -23,6 +24,7 @@ class Engine:
                  sigma: float = 0.02, device: int = 0):
         self.cfg = cfg
         self.h = C.c_void_p()
+        self._caches = weakref.WeakSet()
         d = cfg.desc()
         if tensors is not None:
             arr, _keep = tensor_views(tensors)
@@ -39,6 +41,9 @@ class Engine:
         return cls(cfg, seed=seed, sigma=sigma, device=device)
 
     def close(self):
+        # a KV pool belongs to its engine: release the pools first
+        for c in list(self._caches):
+            c.close()
         if self.h:
             lib.bt_engine_destroy(self.h)
             self.h = C.c_void_p()
@@ -85,11 +90,12 @@ class KvCache:
         self.max_positions = max_positions
         self.max_seqs = max_seqs
         check(lib.bt_kv_create(engine.h, _lib.KV_F16, max_seqs, max_positions, 16, C.byref(self.h)))
+        engine._caches.add(self)
 
     def close(self):
-        if self.h:
+        if self.h and self.engine.h:
             lib.bt_kv_destroy(self.h)
-            self.h = C.c_void_p()
+        self.h = C.c_void_p()
 
     def __del__(self):
         try:

@@ -89,6 +89,7 @@ int bt_engine_create(const bt_model_desc *desc, const bt_tensor_view *tensors, s
 int bt_engine_create_synthetic(const bt_model_desc *desc, const uint32_t *types, uint32_t embd_type,
                                uint32_t out_type, uint64_t seed, float sigma, int device,
                                bt_engine **out);
+/* Destroy every bt_kv of the engine before the engine itself. */
 void bt_engine_destroy(bt_engine *e);
 int bt_engine_stats(const bt_engine *e, bt_stats *out);
 /* copy a resident tensor's GGUF bytes back to the host (for a CPU check of synthetic weights) */
@@ -106,8 +107,9 @@ int bt_kv_shift_out(bt_kv *kv, uint32_t seq, uint32_t keep, uint32_t drop);  /* 
 int bt_kv_set_positions(bt_kv *kv, uint32_t seq, uint32_t n);                /* kv.rs:270-272 */
 int bt_kv_bytes(const bt_kv *kv, uint64_t *bytes);                          /* kv.rs:162-166 */
 int bt_kv_is_consistent(const bt_kv *kv, uint32_t seq, int *consistent);     /* kv.rs:330-338 */
-/* keys()/values() of one layer in the kv.rs byte layout ([pos][n_head_kv*head_dim] f16),
- * `bytes` = positions * n_head_kv * head_dim * 2 for each of k and v (kv.rs:222-228). */
+/* keys()/values() of one layer in the kv.rs byte layout ([pos][n_head_kv*head_dim] f16)
+ * (kv.rs:222-228): the first bytes / (n_head_kv*head_dim*2) positions, into k_out and v_out
+ * of `bytes` each; `bytes` must be whole positions and at most what the layer holds. */
 int bt_kv_export_layer(const bt_kv *kv, uint32_t seq, uint32_t layer, void *k_out, void *v_out,
                        uint64_t bytes);
 /* restore_layer (kv.rs:252-264): replaces the layer's positions with `bytes` of k and v. */
@@ -141,16 +143,18 @@ typedef struct {
 } bt_kernel_time;
 int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const uint32_t *first_tokens,
                       uint32_t n_seqs, uint32_t n_steps, bt_kernel_time *out, uint32_t max_out, uint32_t *n_out);
-/* Engine switches: "pdl" (programmatic dependent launch between the step's kernels, default 1). */
+/* Engine switches: "pdl" (programmatic dependent launch between the step's kernels, default 1),
+ * "prefetch" (L2 bulk prefetch of the next kernels' weights and KV pages, default 1). */
 int bt_set_option(bt_engine *e, const char *name, int value);
 
 /* ---- parity hooks: each runs one device kernel on host buffers ---- */
 /* dequantize() (core/ggml/src/lib.rs:233-290): n values of `type` through the device layout */
 int bt_debug_dequant(uint32_t type, const void *bytes, uint64_t n, float *out);
-/* route() result of the last bt_forward for one layer and token index (stream.rs:869-888):
- * ids in descending probability, renormalised weights */
+/* route() result for one layer and token (stream.rs:869-888): ids in descending probability,
+ * renormalised weights. `token` indexes the token list of the last bt_forward; only its last
+ * step (its last 64 tokens) is kept. After bt_generate_greedy, token i is sequence i's last step. */
 int bt_debug_topk(const bt_engine *e, uint32_t layer, uint32_t token, int32_t *ids, float *weights);
-/* residual stream after the last layer, last bt_forward, token index `token` (n_embd floats) */
+/* residual stream after the last layer for `token`, indexed as for bt_debug_topk (n_embd floats) */
 int bt_debug_hidden(const bt_engine *e, uint32_t token, float *out);
 /* one quantised mul_mat (graph.rs:690): y[t][r] = W[r,:] . x[t,:] for T tokens */
 int bt_op_gemv(uint32_t type, const void *w_bytes, uint32_t rows, uint32_t cols, const float *x,

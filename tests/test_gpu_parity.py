@@ -244,8 +244,12 @@ def test_cfg0_prefill_128_then_64_greedy_steps():
         got0 = runner.forward_cached(cache, prompt, 0)
         assert_logits(got0, want0)
         for il in range(cfg.n_layer):
-            for t in (0, 64, 127):
-                assert np.array_equal(e.debug_topk(il, t)[0], model.topk(il, t)[0])
+            for t in (64, 100, 127):  # the debug hooks keep the last 64-token step
+                gi, gw = e.debug_topk(il, t)
+                oi, ow = model.topk(il, t)
+                assert np.array_equal(gi, oi) and np.array_equal(bits(gw), bits(ow))
+        with pytest.raises(bt.BtError):
+            e.debug_topk(0, 3)
         first = orc.argmax(want0)
         toks = runner.generate_greedy(cache, [first], 64)
         want = model.greedy(first, 64)
