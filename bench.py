@@ -159,6 +159,10 @@ def run_ours(args, rank, world, local_rank):
     cfg = bt.config(args.config, **over)
     t_setup = time.perf_counter()
     engine = bt.Engine.synthetic(cfg, seed=args.seed, device=local_rank)
+    if args.prefetch:
+        engine.set_option("prefetch", 1)
+    if args.no_pdl:
+        engine.set_option("pdl", 0)
     cache = bt.KvCache(engine, max_positions=cfg.max_positions)
     runner = bt.StreamingRunner(engine)
     rng = np.random.default_rng(args.seed + 1)
@@ -323,6 +327,8 @@ def main():
     ap.add_argument("--fill", default="prefill", choices=["prefill", "random"],
                     help="build the context by a real prefill, or fill the cache with seeded f16 values")
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling runs)")
+    ap.add_argument("--prefetch", action="store_true", help="enable the L2 bulk prefetch of upcoming inputs")
+    ap.add_argument("--no-pdl", action="store_true", help="disable programmatic dependent launch")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -12,7 +12,7 @@
 //   C5 P2: 32 lanes, lane l takes elements l, l+32, ... in order, xor butterfly 16,8,4,2,1.
 //   C6 RMSNorm y = (x * (1/sqrt(P2(x*x)/n + eps))) * w.
 //   C7 bt_exp: Cody-Waite ln2 reduction + degree-7 Taylor polynomial in Horner/fmaf form.
-//   C8 attention: chunks of 256 keys, per-chunk max/exp/sum/PV, chunks combined in order.
+//   C8 attention: chunks of 128 keys, per-chunk max/exp/sum/PV, chunks combined in order.
 //   C9 RoPE NeoX with a host-computed cos/sin table.
 #pragma once
 #include <cuda_fp16.h>
@@ -80,17 +80,17 @@ __device__ __forceinline__ int warp_sum_int(int v) {
     return v;
 }
 
-// C5 over n elements (lane l: l, l+32, ... in order). Loads are issued 16 at a time ahead of
-// the in-order fmaf chain, so the chain waits on one load latency per 16 elements.
+// C5 over n elements (lane l: l, l+32, ... in order). Loads are issued 32 at a time ahead of
+// the in-order fmaf chain, so the chain waits on one load latency per 32 elements.
 __device__ __forceinline__ float warp_sumsq_p2(const float *__restrict__ x, int n, int lane) {
     float acc = 0.0f;
     int i = lane;
-    for (; i + 32 * 15 < n; i += 32 * 16) {
-        float v[16];
+    for (; i + 32 * 31 < n; i += 32 * 32) {
+        float v[32];
 #pragma unroll
-        for (int k = 0; k < 16; k++) v[k] = x[i + 32 * k];
+        for (int k = 0; k < 32; k++) v[k] = x[i + 32 * k];
 #pragma unroll
-        for (int k = 0; k < 16; k++) acc = fmaf(v[k], v[k], acc);
+        for (int k = 0; k < 32; k++) acc = fmaf(v[k], v[k], acc);
     }
     for (; i < n; i += 32) acc = fmaf(x[i], x[i], acc);
     return butterfly_sum(acc);
@@ -100,15 +100,15 @@ __device__ __forceinline__ float warp_sumsq_p2(const float *__restrict__ x, int 
 __device__ __forceinline__ float warp_dot_p2(const float *__restrict__ a, const float *__restrict__ b, int n, int lane) {
     float acc = 0.0f;
     int i = lane;
-    for (; i + 32 * 15 < n; i += 32 * 16) {
-        float va[16], vb[16];
+    for (; i + 32 * 31 < n; i += 32 * 32) {
+        float va[32], vb[32];
 #pragma unroll
-        for (int k = 0; k < 16; k++) {
+        for (int k = 0; k < 32; k++) {
             va[k] = __ldg(a + i + 32 * k);
             vb[k] = b[i + 32 * k];
         }
 #pragma unroll
-        for (int k = 0; k < 16; k++) acc = fmaf(va[k], vb[k], acc);
+        for (int k = 0; k < 32; k++) acc = fmaf(va[k], vb[k], acc);
     }
     for (; i < n; i += 32) acc = fmaf(__ldg(a + i), b[i], acc);
     return butterfly_sum(acc);

@@ -127,7 +127,9 @@ struct bt_engine {
     std::vector<std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>> ev_used;
     double last_device_ms = 0;
     bool pdl = true;
-    bool prefetch = true;
+    // L2 bulk prefetch of the next kernels' inputs: measured slower (the issuing CTAs wait on
+    // their prefetches), so off unless asked for
+    bool prefetch = false;
 };
 
 struct bt_kv {
@@ -164,10 +166,15 @@ static EncodeTiledFn get_encode_fn() {
 }
 
 // ------------------------------------------------------------------ helpers
+// Ring depth per warp: at most 3 slots and about 110 KB per CTA, so that the CTAs of the next
+// kernel (programmatic dependent launch) fit beside a running CTA on the same SM.
 static int pick_nst(size_t slot_bytes, size_t fixed_bytes) {
     static size_t cap = 0;
-    if (!cap) cap = (size_t)max_dynamic_smem();
-    int nst = 4;
+    if (!cap) {
+        cap = (size_t)max_dynamic_smem();
+        if (cap > 110 * 1024) cap = 110 * 1024;
+    }
+    int nst = 3;
     while (nst > 1 && fixed_bytes + (size_t)GEMV_WARPS * nst * slot_bytes > cap) nst--;
     return nst;
 }

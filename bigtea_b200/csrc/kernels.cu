@@ -466,19 +466,24 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gateup_kernel(const __grid_cons
         const bool active = lane < p.g_S;
         const int rit = active ? lane / nsb : 0, b = active ? lane % nsb : 0;
         const int row = tile * p.g_rpt + rit;
-        float vg = 0.0f, vu = 0.0f;
-        if (active) {
-            const ActBlock &ab = act[t * nsb + b];
-            vg = p.gtype == T_Q4_K ? q4k_slot_dot(gt, p.g_S, lane, ab) : q6k_slot_dot(gt, p.g_S, lane, ab);
-            vu = p.utype == T_Q4_K ? q4k_slot_dot(ut, p.g_S, lane, ab) : q6k_slot_dot(ut, p.g_S, lane, ab);
+        float rowv[2];
+#pragma unroll 1
+        for (int which = 0; which < 2; which++) {  // gate, then up: one copy of the dot code
+            const uint8_t *tl = which ? ut : gt;
+            const int ty = which ? p.utype : p.gtype;
+            float v = 0.0f;
+            if (active) {
+                const ActBlock &ab = act[t * nsb + b];
+                v = ty == T_Q4_K ? q4k_slot_dot(tl, p.g_S, lane, ab) : q6k_slot_dot(tl, p.g_S, lane, ab);
+            }
+            float r = 0.0f;
+            for (int b2 = 0; b2 < nsb; b2++) {
+                int srcl = rit * nsb + b2;
+                r = __fadd_rn(r, __shfl_sync(FULL, v, srcl < 32 ? srcl : 31));
+            }
+            rowv[which] = r;
         }
-        float ag = 0.0f, au = 0.0f;
-        for (int b2 = 0; b2 < nsb; b2++) {
-            int srcl = rit * nsb + b2;
-            srcl = srcl < 32 ? srcl : 31;
-            ag = __fadd_rn(ag, __shfl_sync(FULL, vg, srcl));
-            au = __fadd_rn(au, __shfl_sync(FULL, vu, srcl));
-        }
+        const float ag = rowv[0], au = rowv[1];
         if (active && b == 0 && row < p.F) p.act[tk * p.F + row] = __fmul_rn(bt_silu(ag), au);
         __syncwarp();
         if (lane == 0 && j + p.nst < nmine) {
@@ -782,18 +787,19 @@ cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl) {
 }
 
 // ====================================================================== attention
-// grid (max_chunks, HK, T), 256 threads, one CTA per (token, kv head, chunk of 256 keys).
-// K and V pages arrive by 2-D TMA (128-byte swizzle, box 64 x 16) in shared memory. Scores:
-// thread (hh, kp) owns keys kp and kp+128 for heads [hh*G/2, hh*G/2+G/2), each a sequential
-// fmaf dot over d. P*V: thread (hq, d) owns column d for heads [hq*G/2, hq*G/2+G/2), a
-// sequential fmaf over the chunk's keys. A chunk writes (m, l, acc) to scratch; the last
-// chunk of a (token, kv head) combines them in chunk order (C8).
+// grid (max_chunks, HK, T), 256 threads, one CTA per (token, kv head, chunk of 128 keys);
+// about 73 KB of shared memory, so two or three CTAs share an SM. K and V pages arrive by
+// 2-D TMA (128-byte swizzle, box 64 x 16). Scores: thread (hh, k) owns key k for heads
+// [hh*G/2, hh*G/2+G/2), a sequential fmaf dot over d. P*V: thread (hq, d) owns column d for
+// heads [hq*G/2, hq*G/2+G/2), a sequential fmaf over the chunk's keys. A chunk that is the
+// whole context finalises its heads; otherwise it writes (acc, m, l) to scratch and
+// attn_combine_kernel merges the chunks in order (C8).
 constexpr int ATTN_THREADS = 256;
-constexpr int ATTN_PART_ROW = 132;  // floats per (chunk, head) partial: acc[128], m, l, 2 pad (16-byte rows)
+constexpr int ATTN_PART_ROW = 132;  // floats per (chunk, head) partial: acc[128], m, l, 2 pad
 
 size_t attn_smem_bytes(int G, int max_chunks) {
-    (void)max_chunks;  // the combine reuses the K tile region
-    return 4 * 32768 + (size_t)128 * G * 4 + (size_t)ATTN_CHUNK * G * 4 + 2 * 8 * 8 * 4 + 64 + 1024;
+    (void)max_chunks;
+    return 4 * 16384 + (size_t)128 * G * 4 + (size_t)ATTN_CHUNK * G * 4 + 2 * 8 * 8 * 4 + 64 + 1024;
 }
 
 template <int N>
@@ -811,31 +817,30 @@ __device__ __forceinline__ void lds_vec(float (&dst)[N], const float *src) {
 }
 
 template <int G>
-__global__ void __launch_bounds__(ATTN_THREADS, 1)
+__global__ void __launch_bounds__(ATTN_THREADS, 2)
     attn_kernel(const __grid_constant__ AttnArgs p, const __grid_constant__ CUtensorMap tmap) {
-    constexpr int D = 128, HPT = G / 2;
+    constexpr int D = 128, HPT = G / 2, CH = ATTN_CHUNK;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
-    uint8_t *const K0 = smem, *const K1 = smem + 32768, *const V0 = smem + 65536, *const V1 = smem + 98304;
-    float *qs = reinterpret_cast<float *>(smem + 131072);  // [D][G]
-    float *ps = qs + D * G;                                // [256][G]
-    float *red = ps + ATTN_CHUNK * G;                      // [8 warps][8]
-    float *red2 = red + 64;                                // [8 key groups][8]
+    uint8_t *const K0 = smem, *const K1 = smem + 16384, *const V0 = smem + 32768, *const V1 = smem + 49152;
+    float *qs = reinterpret_cast<float *>(smem + 65536);  // [D][G]
+    float *ps = qs + D * G;                               // [CH][G]
+    float *red = ps + CH * G;                             // [8 warps][8]
+    float *red2 = red + 64;                               // [4 key groups][8]
     uint64_t *bar = reinterpret_cast<uint64_t *>(red2 + 64);
-    __shared__ int s_last;
     __shared__ float s_m[8], s_l[8];
 
     const int c = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     pdl_wait();
     const int seq = p.seq_of[t], pos = p.pos_of[t];
-    const int nk = pos + 1, nc = (nk + ATTN_CHUNK - 1) / ATTN_CHUNK;
+    const int nk = pos + 1, nc = (nk + CH - 1) / CH;
     if (c >= nc) {
         pdl_trigger();
         return;
     }
-    const int base = c * ATTN_CHUNK;
-    const int cnt = nk - base < ATTN_CHUNK ? nk - base : ATTN_CHUNK;
+    const int base = c * CH;
+    const int cnt = nk - base < CH ? nk - base : CH;
     const int npages = (cnt + 15) / 16;
     if (tid == 0) {
         mbar_init(bar, 1);
@@ -867,41 +872,31 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         return;
     }
 
-    // ---- scores: keys kp and kp+128, heads hh*HPT .. +HPT
-    const int hh = tid >> 7, kp = tid & 127;
-    const bool v0 = kp < cnt, v1 = kp + 128 < cnt;
-    float s0[HPT], s1[HPT];
+    // ---- scores: key k, heads hh*HPT .. +HPT
+    const int hh = tid >> 7, k = tid & 127;
+    const bool valid = k < cnt;
+    float sc[HPT];
 #pragma unroll
-    for (int h = 0; h < HPT; h++) s0[h] = s1[h] = 0.0f;
-    {
-        const int ka = kp, kb = kp + 128;
+    for (int h = 0; h < HPT; h++) sc[h] = 0.0f;
 #pragma unroll 2
-        for (int c16 = 0; c16 < 16; c16++) {
-            const uint8_t *kr = (c16 < 8) ? K0 : K1;
-            const int cc = c16 & 7;
-            uint4 wa = *reinterpret_cast<const uint4 *>(kr + ka * 128 + ((cc ^ (ka & 7)) << 4));
-            uint4 wb = *reinterpret_cast<const uint4 *>(kr + kb * 128 + ((cc ^ (kb & 7)) << 4));
-            const __half *ha = reinterpret_cast<const __half *>(&wa);
-            const __half *hb = reinterpret_cast<const __half *>(&wb);
+    for (int c16 = 0; c16 < 16; c16++) {
+        const uint8_t *kr = (c16 < 8) ? K0 : K1;
+        uint4 w = *reinterpret_cast<const uint4 *>(kr + k * 128 + (((c16 & 7) ^ (k & 7)) << 4));
+        const __half *hk = reinterpret_cast<const __half *>(&w);
 #pragma unroll
-            for (int e = 0; e < 8; e++) {
-                const float fa = __half2float(ha[e]), fb = __half2float(hb[e]);
-                float q[HPT];
-                lds_vec<HPT>(q, qs + (c16 * 8 + e) * G + hh * HPT);
+        for (int e = 0; e < 8; e++) {
+            const float kf = __half2float(hk[e]);
+            float q[HPT];
+            lds_vec<HPT>(q, qs + (c16 * 8 + e) * G + hh * HPT);
 #pragma unroll
-                for (int h = 0; h < HPT; h++) {
-                    s0[h] = fmaf(q[h], fa, s0[h]);
-                    s1[h] = fmaf(q[h], fb, s1[h]);
-                }
-            }
+            for (int h = 0; h < HPT; h++) sc[h] = fmaf(q[h], kf, sc[h]);
         }
     }
     const float NEG_INF = -__int_as_float(0x7f800000);
 #pragma unroll
     for (int h = 0; h < HPT; h++) {
-        s0[h] = v0 ? __fmul_rn(s0[h], p.scale) : NEG_INF;
-        s1[h] = v1 ? __fmul_rn(s1[h], p.scale) : NEG_INF;
-        float m = warp_max(fmaxf(s0[h], s1[h]));
+        sc[h] = valid ? __fmul_rn(sc[h], p.scale) : NEG_INF;
+        float m = warp_max(sc[h]);
         if (lane == 0) red[warp * 8 + h] = m;
     }
     __syncthreads();
@@ -912,25 +907,19 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         s_m[tid] = m;
     }
     __syncthreads();
-    // ---- probabilities and the P3 sum: warp (hh, q) holds key groups q and q+4
+    // ---- probabilities and the P3 sum: warp (hh, q) holds key group q
 #pragma unroll
     for (int h = 0; h < HPT; h++) {
         const int head = hh * HPT + h;
-        const float m = s_m[head];
-        const float p0 = v0 ? bt_exp(__fsub_rn(s0[h], m)) : 0.0f;
-        const float p1 = v1 ? bt_exp(__fsub_rn(s1[h], m)) : 0.0f;
-        ps[kp * G + head] = p0;
-        ps[(kp + 128) * G + head] = p1;
-        const float w0 = butterfly_sum(p0), w1 = butterfly_sum(p1);
-        if (lane == 0) {
-            red2[(warp & 3) * 8 + head] = w0;
-            red2[((warp & 3) + 4) * 8 + head] = w1;
-        }
+        const float pr = valid ? bt_exp(__fsub_rn(sc[h], s_m[head])) : 0.0f;
+        ps[k * G + head] = pr;
+        const float ws = butterfly_sum(pr);
+        if (lane == 0) red2[(warp & 3) * 8 + head] = ws;
     }
     __syncthreads();
     if (tid < G) {
         float l = 0.0f;
-        for (int w = 0; w < 8; w++) l = __fadd_rn(l, red2[w * 8 + tid]);
+        for (int w = 0; w < CH / 32; w++) l = __fadd_rn(l, red2[w * 8 + tid]);
         s_l[tid] = l;
     }
     // ---- P*V: column d, heads hq*HPT .. +HPT
@@ -943,16 +932,16 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
         const uint8_t *vcol = ((d < 64) ? V0 : V1) + (d & 7) * 2;
         int off[8];
 #pragma unroll
-        for (int k = 0; k < 8; k++) off[k] = k * 128 + ((cc ^ k) << 4);
+        for (int kk = 0; kk < 8; kk++) off[kk] = kk * 128 + ((cc ^ kk) << 4);
         for (int j0 = 0; j0 < cnt; j0 += 8) {
             const uint8_t *vb = vcol + j0 * 128;
             const float *pb = ps + j0 * G + hq * HPT;
 #pragma unroll
-            for (int k = 0; k < 8; k++) {
-                if (j0 + k < cnt) {
-                    const float vf = __half2float(*reinterpret_cast<const __half *>(vb + off[k]));
+            for (int kk = 0; kk < 8; kk++) {
+                if (j0 + kk < cnt) {
+                    const float vf = __half2float(*reinterpret_cast<const __half *>(vb + off[kk]));
                     float pj[HPT];
-                    lds_vec<HPT>(pj, pb + k * G);
+                    lds_vec<HPT>(pj, pb + kk * G);
 #pragma unroll
                     for (int h = 0; h < HPT; h++) acc[h] = fmaf(pj[h], vf, acc[h]);
                 }
@@ -983,69 +972,55 @@ __global__ void __launch_bounds__(ATTN_THREADS, 1)
             pp[D + 1] = s_l[head];
         }
     }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&p.cnt[t * p.HK + g], 1) == nc - 1);
-    __syncthreads();
-    if (!s_last) return;
-    __threadfence();
-    // ---- combine (the last chunk's CTA): per-chunk m and l, then the acc rows in chunk
-    // order, streamed into shared memory as 1-D TMA slices of SL chunks
-    float *cm = reinterpret_cast<float *>(V0);  // [nc][G]  (the V tile is no longer needed)
-    float *cl = cm + nc * G;                    // [nc][G]
-    float *cf = cl + nc * G;                    // [nc][G]
-    for (int i = tid; i < nc * G; i += ATTN_THREADS) {
-        const float *pp = p.part + pbase + (long long)i * ATTN_PART_ROW;
-        cm[i] = __ldcg(pp + D);
-        cl[i] = __ldcg(pp + D + 1);
+}
+
+// grid (H, T), 128 threads: merges the chunk partials of one query head in chunk order
+// (C8): M = max m_c, f_c = exp(m_c - M), L = fmaf(l_c, f_c, L), O = fmaf(acc_c, f_c, O).
+__global__ void __launch_bounds__(128) attn_combine_kernel(const __grid_constant__ AttnArgs p) {
+    extern __shared__ float cbuf[];  // m[nc], l[nc], f[nc]
+    __shared__ float s_M, s_L;
+    const int hd = blockIdx.x, t = blockIdx.y, d = threadIdx.x;
+    pdl_wait();
+    pdl_trigger();
+    const int pos = p.pos_of[t];
+    const int nc = (pos + 1 + ATTN_CHUNK - 1) / ATTN_CHUNK;
+    if (nc == 1) return;  // the attention kernel finalised this token
+    const int G = p.G, g = hd / G, h = hd % G, D = 128;
+    const float *part = p.part + (((long long)t * p.HK + g) * p.max_chunks) * G * ATTN_PART_ROW + (long long)h * ATTN_PART_ROW;
+    const long long cstride = (long long)G * ATTN_PART_ROW;
+    float *cm = cbuf, *cl = cbuf + nc, *cf = cbuf + 2 * nc;
+    for (int c = d; c < nc; c += blockDim.x) {
+        cm[c] = part[c * cstride + D];
+        cl[c] = part[c * cstride + D + 1];
     }
     __syncthreads();
-    if (tid < G) {
-        float M = NEG_INF;
-        for (int cc = 0; cc < nc; cc++) M = fmaxf(M, cm[cc * G + tid]);
+    if (d < 32) {  // M (order-free)
+        float m = -__int_as_float(0x7f800000);
+        for (int c = d; c < nc; c += 32) m = fmaxf(m, cm[c]);
+        m = warp_max(m);
+        if (d == 0) s_M = m;
+    }
+    __syncthreads();
+    for (int c = d; c < nc; c += blockDim.x) cf[c] = bt_exp(__fsub_rn(cm[c], s_M));
+    __syncthreads();
+    if (d == 0) {
         float L = 0.0f;
-        for (int cc = 0; cc < nc; cc++) {
-            const float f = bt_exp(__fsub_rn(cm[cc * G + tid], M));
-            cf[cc * G + tid] = f;
-            L = fmaf(cl[cc * G + tid], f, L);
-        }
-        s_l[tid] = L;
+        for (int c = 0; c < nc; c++) L = fmaf(cl[c], cf[c], L);
+        s_L = L;
     }
-    constexpr int ROWB = ATTN_PART_ROW * 4;
-    constexpr int SL = 65536 / (G * ROWB);  // chunks per slice in the 64 KB K tile region
-    float O[HPT];
+    float O = 0.0f;
+    const float *pa = part + d;
+    int c = 0;
+    for (; c + 16 <= nc; c += 16) {
+        float a[16];
 #pragma unroll
-    for (int h = 0; h < HPT; h++) O[h] = 0.0f;
-    uint32_t phase = 1;  // phase 0 of `bar` was the K/V load
-    const float *slice = reinterpret_cast<const float *>(K0);
-    for (int c0 = 0; c0 < nc; c0 += SL) {
-        const int n = nc - c0 < SL ? nc - c0 : SL;
-        __syncthreads();  // the previous slice (and the K tile) are no longer read
-        if (tid == 0) {
-            asm volatile("fence.proxy.async;" ::: "memory");
-            mbar_arrive_expect_tx(bar, (uint32_t)(n * G * ROWB));
-            bulk_g2s(K0, p.part + pbase + (long long)c0 * G * ATTN_PART_ROW, (uint32_t)(n * G * ROWB), bar);
-        }
-        const bool ok = mbar_wait(bar, phase, p.err);
-        phase ^= 1;
-        if (__syncthreads_or(!ok)) {
-            if (tid == 0) mbar_wait(bar, phase ^ 1, nullptr);
-            return;
-        }
-        for (int cc = 0; cc < n; cc++) {
+        for (int k = 0; k < 16; k++) a[k] = pa[(long long)(c + k) * cstride];
 #pragma unroll
-            for (int h = 0; h < HPT; h++) {
-                const int head = hq * HPT + h;
-                O[h] = fmaf(slice[(cc * G + head) * ATTN_PART_ROW + d], cf[(c0 + cc) * G + head], O[h]);
-            }
-        }
+        for (int k = 0; k < 16; k++) O = fmaf(a[k], cf[c + k], O);
     }
-#pragma unroll
-    for (int h = 0; h < HPT; h++) {
-        const int head = hq * HPT + h;
-        p.out[(long long)t * QW + (g * G + head) * D + d] = __fdiv_rn(O[h], s_l[head]);
-    }
-    if (tid == 0) p.cnt[t * p.HK + g] = 0;
+    for (; c < nc; c++) O = fmaf(pa[(long long)c * cstride], cf[c], O);
+    __syncthreads();
+    p.out[(long long)t * p.H * D + hd * D + d] = __fdiv_rn(O, s_L);
 }
 
 template <int G>
@@ -1064,13 +1039,16 @@ static cudaError_t launch_attn_g(const AttnArgs &a, const CUtensorMap &tmap, cud
 }
 
 cudaError_t launch_attn(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl) {
+    cudaError_t e;
     switch (a.G) {
-    case 2: return launch_attn_g<2>(a, tmap, st, pdl);
-    case 4: return launch_attn_g<4>(a, tmap, st, pdl);
-    case 6: return launch_attn_g<6>(a, tmap, st, pdl);
-    case 8: return launch_attn_g<8>(a, tmap, st, pdl);
+    case 2: e = launch_attn_g<2>(a, tmap, st, pdl); break;
+    case 4: e = launch_attn_g<4>(a, tmap, st, pdl); break;
+    case 6: e = launch_attn_g<6>(a, tmap, st, pdl); break;
+    case 8: e = launch_attn_g<8>(a, tmap, st, pdl); break;
     default: return cudaErrorInvalidValue;
     }
+    if (e != cudaSuccess) return e;
+    return launch_ex(attn_combine_kernel, dim3(a.H, a.T), dim3(128), (size_t)3 * a.max_chunks * 4, st, pdl, a);
 }
 
 // ====================================================================== embedding and step end

@@ -10,7 +10,7 @@ namespace bt {
 
 constexpr int MAX_T = 8;        // tokens one GEMV / expert launch carries in shared memory
 constexpr int MAX_K = 16;       // experts used per token
-constexpr int ATTN_CHUNK = 256; // attention keys per chunk (contract C8)
+constexpr int ATTN_CHUNK = 128; // attention keys per chunk (contract C8)
 constexpr int GEMV_WARPS = 8;
 
 // Ranges to start pulling into L2 while a kernel runs (the next kernels' inputs), and

@@ -275,29 +275,36 @@ static_assert(sizeof(ActBlock) == 304, "ActBlock layout");
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 
 // C4 for one Q4_K superblock (slot s of a tile in shared memory) against one activation block.
+// The four 64-value groups run as a rolled loop: the same instructions serve every group, which
+// keeps the kernels' code small (each warp runs it only a few times per launch, from a cold
+// instruction cache).
 __device__ __forceinline__ float q4k_slot_dot(const uint8_t *tile, int S, int s, const ActBlock &a) {
     const uint4 *base = reinterpret_cast<const uint4 *>(tile) + s;
-    uint4 h = base[0];
-    float dw = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffff)));
-    float dminw = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
-    // scales bytes 0..11 = h.y, h.z, h.w
-    uint32_t s03 = h.y, s47 = h.z, s811 = h.w;
-    int sc[8], mn[8];
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-        sc[j] = (s03 >> (8 * j)) & 63;
-        mn[j] = (s47 >> (8 * j)) & 63;
-        int b8 = (s811 >> (8 * j)) & 0xff;
-        sc[j + 4] = (b8 & 0xF) | (((s03 >> (8 * j + 6)) & 3) << 4);
-        mn[j + 4] = (b8 >> 4) | (((s47 >> (8 * j + 6)) & 3) << 4);
-    }
+    const uint4 h = base[0];
+    const float dw = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffff)));
+    const float dminw = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    const uint32_t s03 = h.y, s47 = h.z, s811 = h.w;  // the 12 packed scale bytes
     const uint4 *aq = reinterpret_cast<const uint4 *>(a.qs);
-    int sumi = 0;
-#pragma unroll
+    int sumi = 0, summ = 0;
+#pragma unroll 1
     for (int g = 0; g < 4; g++) {
-        uint4 w0 = base[(1 + 2 * g) * S];
-        uint4 w1 = base[(2 + 2 * g) * S];
-        uint4 al0 = aq[4 * g + 0], al1 = aq[4 * g + 1], ah0 = aq[4 * g + 2], ah1 = aq[4 * g + 3];
+        // sub-blocks 2g and 2g+1: 6-bit scale and min (get_scale_min_k4)
+        int sc0, m0, sc1, m1;
+        if (g < 2) {
+            sc0 = (s03 >> (16 * g)) & 63;
+            m0 = (s47 >> (16 * g)) & 63;
+            sc1 = (s03 >> (16 * g + 8)) & 63;
+            m1 = (s47 >> (16 * g + 8)) & 63;
+        } else {
+            const int j0 = 2 * g - 4;  // byte index within s811 for sub-block 2g
+            const int b0 = (s811 >> (8 * j0)) & 0xff, b1 = (s811 >> (8 * j0 + 8)) & 0xff;
+            sc0 = (b0 & 0xF) | (((s03 >> (8 * j0 + 6)) & 3) << 4);
+            m0 = (b0 >> 4) | (((s47 >> (8 * j0 + 6)) & 3) << 4);
+            sc1 = (b1 & 0xF) | (((s03 >> (8 * j0 + 14)) & 3) << 4);
+            m1 = (b1 >> 4) | (((s47 >> (8 * j0 + 14)) & 3) << 4);
+        }
+        const uint4 w0 = base[(1 + 2 * g) * S], w1 = base[(2 + 2 * g) * S];
+        const uint4 al0 = aq[4 * g + 0], al1 = aq[4 * g + 1], ah0 = aq[4 * g + 2], ah1 = aq[4 * g + 3];
         int dlo = 0, dhi = 0;
         dlo = dp4a(w0.x & 0x0F0F0F0F, al0.x, dlo);
         dlo = dp4a(w0.y & 0x0F0F0F0F, al0.y, dlo);
@@ -315,55 +322,52 @@ __device__ __forceinline__ float q4k_slot_dot(const uint8_t *tile, int S, int s,
         dhi = dp4a((w1.y >> 4) & 0x0F0F0F0F, ah1.y, dhi);
         dhi = dp4a((w1.z >> 4) & 0x0F0F0F0F, ah1.z, dhi);
         dhi = dp4a((w1.w >> 4) & 0x0F0F0F0F, ah1.w, dhi);
-        sumi += sc[2 * g] * dlo + sc[2 * g + 1] * dhi;
+        sumi += sc0 * dlo + sc1 * dhi;
+        summ += m0 * a.bs32[2 * g] + m1 * a.bs32[2 * g + 1];
     }
-    int summ = 0;
-#pragma unroll
-    for (int j = 0; j < 8; j++) summ += mn[j] * a.bs32[j];
-    float t1 = __fmul_rn(dw, a.d);
-    float t2 = __fmul_rn(__int2float_rn(sumi), t1);
-    float t3 = __fmul_rn(dminw, a.d);
-    float t4 = __fmul_rn(__int2float_rn(summ), t3);
+    const float t1 = __fmul_rn(dw, a.d);
+    const float t2 = __fmul_rn(__int2float_rn(sumi), t1);
+    const float t3 = __fmul_rn(dminw, a.d);
+    const float t4 = __fmul_rn(__int2float_rn(summ), t3);
     return __fsub_rn(t2, t4);
 }
 
-// C4 for one Q6_K superblock.
+// C4 for one Q6_K superblock. Integer identity: sum over 16-value sub-blocks s of
+// sc[s] * dot_s equals the sum over the 4-value dp4a groups of sc[sub(group)] * dp4a(group).
 __device__ __forceinline__ float q6k_slot_dot(const uint8_t *tile, int S, int s, const ActBlock &a) {
     const uint4 *base = reinterpret_cast<const uint4 *>(tile) + s;
-    uint16_t dbits = *reinterpret_cast<const uint16_t *>(tile + 13 * S * 16 + 2 * s);
-    float dw = __half2float(__ushort_as_half(dbits));
-    uint4 scv = base[12 * S];
-    const int8_t *sc = reinterpret_cast<const int8_t *>(&scv);
+    const uint16_t dbits = *reinterpret_cast<const uint16_t *>(tile + 13 * S * 16 + 2 * s);
+    const float dw = __half2float(__ushort_as_half(dbits));
+    const uint4 scv = base[12 * S];
     const int *aw = reinterpret_cast<const int *>(a.qs);
-    int acc[16];
-#pragma unroll
-    for (int i = 0; i < 16; i++) acc[i] = 0;
-#pragma unroll
+    int sumi = 0;
+#pragma unroll 1
     for (int n = 0; n < 2; n++) {
-        uint4 qa0 = base[(4 * n + 0) * S], qa1 = base[(4 * n + 1) * S];  // ql bytes 64n .. 64n+31
-        uint4 qb0 = base[(4 * n + 2) * S], qb1 = base[(4 * n + 3) * S];  // ql bytes 64n+32 .. 64n+63
-        uint4 hh0 = base[(8 + 2 * n) * S], hh1 = base[(9 + 2 * n) * S];  // qh bytes 32n .. 32n+31
-        uint32_t wa[8] = {qa0.x, qa0.y, qa0.z, qa0.w, qa1.x, qa1.y, qa1.z, qa1.w};
-        uint32_t wb[8] = {qb0.x, qb0.y, qb0.z, qb0.w, qb1.x, qb1.y, qb1.z, qb1.w};
-        uint32_t wh[8] = {hh0.x, hh0.y, hh0.z, hh0.w, hh1.x, hh1.y, hh1.z, hh1.w};
+        const uint32_t wlo = n ? scv.z : scv.x;  // int8 scales of sub-blocks 8n .. 8n+3
+        const uint32_t whi = n ? scv.w : scv.y;  // 8n+4 .. 8n+7
+        const uint4 qa0 = base[(4 * n + 0) * S], qa1 = base[(4 * n + 1) * S];  // ql bytes 64n .. 64n+31
+        const uint4 qb0 = base[(4 * n + 2) * S], qb1 = base[(4 * n + 3) * S];  // ql bytes 64n+32 .. 64n+63
+        const uint4 hh0 = base[(8 + 2 * n) * S], hh1 = base[(9 + 2 * n) * S];  // qh bytes 32n .. 32n+31
+        const uint32_t wa[8] = {qa0.x, qa0.y, qa0.z, qa0.w, qa1.x, qa1.y, qa1.z, qa1.w};
+        const uint32_t wb[8] = {qb0.x, qb0.y, qb0.z, qb0.w, qb1.x, qb1.y, qb1.z, qb1.w};
+        const uint32_t wh[8] = {hh0.x, hh0.y, hh0.z, hh0.w, hh1.x, hh1.y, hh1.z, hh1.w};
+        const int *an = aw + 32 * n;  // activation words of values 128n ..
 #pragma unroll
         for (int l4 = 0; l4 < 8; l4++) {
-            uint32_t h = wh[l4];
-            int q1 = (int)__vsub4((wa[l4] & 0x0F0F0F0F) | ((h & 0x03030303) << 4), 0x20202020);
-            int q2 = (int)__vsub4((wb[l4] & 0x0F0F0F0F) | (((h >> 2) & 0x03030303) << 4), 0x20202020);
-            int q3 = (int)__vsub4(((wa[l4] >> 4) & 0x0F0F0F0F) | (((h >> 4) & 0x03030303) << 4), 0x20202020);
-            int q4 = (int)__vsub4(((wb[l4] >> 4) & 0x0F0F0F0F) | (((h >> 6) & 0x03030303) << 4), 0x20202020);
-            int sub = 8 * n + (l4 >> 2);
-            int v0 = 128 * n + 4 * l4;  // value index of q1's first byte
-            acc[sub + 0] = dp4a(q1, aw[(v0 + 0) / 4], acc[sub + 0]);
-            acc[sub + 2] = dp4a(q2, aw[(v0 + 32) / 4], acc[sub + 2]);
-            acc[sub + 4] = dp4a(q3, aw[(v0 + 64) / 4], acc[sub + 4]);
-            acc[sub + 6] = dp4a(q4, aw[(v0 + 96) / 4], acc[sub + 6]);
+            const uint32_t h = wh[l4];
+            const int q1 = (int)__vsub4((wa[l4] & 0x0F0F0F0F) | ((h & 0x03030303) << 4), 0x20202020);
+            const int q2 = (int)__vsub4((wb[l4] & 0x0F0F0F0F) | (((h >> 2) & 0x03030303) << 4), 0x20202020);
+            const int q3 = (int)__vsub4(((wa[l4] >> 4) & 0x0F0F0F0F) | (((h >> 4) & 0x03030303) << 4), 0x20202020);
+            const int q4 = (int)__vsub4(((wb[l4] >> 4) & 0x0F0F0F0F) | (((h >> 6) & 0x03030303) << 4), 0x20202020);
+            const int j = l4 >> 2;  // sub-blocks 8n + j, +2, +4, +6
+            const int s1 = (int)(signed char)((j == 0 ? wlo : wlo >> 8) & 0xff);
+            const int s2 = (int)(signed char)(((j == 0 ? wlo >> 16 : wlo >> 24)) & 0xff);
+            const int s3 = (int)(signed char)((j == 0 ? whi : whi >> 8) & 0xff);
+            const int s4 = (int)(signed char)(((j == 0 ? whi >> 16 : whi >> 24)) & 0xff);
+            sumi += s1 * dp4a(q1, an[l4], 0) + s2 * dp4a(q2, an[8 + l4], 0) + s3 * dp4a(q3, an[16 + l4], 0) +
+                    s4 * dp4a(q4, an[24 + l4], 0);
         }
     }
-    int sumi = 0;
-#pragma unroll
-    for (int i = 0; i < 16; i++) sumi += (int)sc[i] * acc[i];
     return __fmul_rn(__int2float_rn(sumi), __fmul_rn(dw, a.d));
 }
 

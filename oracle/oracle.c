@@ -19,7 +19,7 @@
  *  C6 RMSNorm: mean = P2(x*x)/n; s = 1/sqrt(mean+eps); y = (x*s)*w.
  *  C7 exp: or_exp below (Cody-Waite reduction by ln2, degree-7 Taylor, Horner in fmaf).
  *  C8 attention: q rounded to f16; s = fmaf-sequential dot over d, times scale;
- *     keys in chunks of `chunk`; per chunk m = max s, p = exp(s-m), l = P3 sum (32-lane
+ *     keys in chunks of `chunk` (128); per chunk m = max s, p = exp(s-m), l = P3 sum (32-lane
  *     butterflies per 32 keys, warps summed in order from 0), acc = fmaf-sequential p*v;
  *     combine chunks in order: f = exp(m_c - M), L = fmaf(l_c,f,L), O = fmaf(acc_c,f,O),
  *     out = O/L.
@@ -544,7 +544,7 @@ or_model *or_model_new(const or_config *cfg, const or_tensor *ts, int n) {
     or_model *m = (or_model *)calloc(1, sizeof(or_model));
     m->c = *cfg;
     if (m->c.expert_workers <= 0) m->c.expert_workers = 4;
-    if (m->c.attn_chunk <= 0) m->c.attn_chunk = 256;
+    if (m->c.attn_chunk <= 0) m->c.attn_chunk = 128;
     if (m->c.n_rot <= 0) m->c.n_rot = m->c.head_dim;
     int bad = 0;
     bad |= find_tensor(ts, n, "token_embd.weight", &m->embd, 1);

@@ -79,7 +79,7 @@ typedef struct {
     int n_rot;
     float rms_eps, rope_base;
     int expert_workers; /* reference default 4 (stream.rs:1305-1312) */
-    int attn_chunk;     /* attention contract chunk, 256 */
+    int attn_chunk;     /* attention contract chunk, 128 */
     int max_positions;  /* RoPE table / KV capacity */
 } or_config;
 

@@ -15,6 +15,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB = os.path.join(HERE, "liboracle.so")
 
 OR_F32, OR_F16, OR_Q4_K, OR_Q6_K = 0, 1, 12, 14
+ATTN_CHUNK = 128  # keys per attention chunk in the arithmetic contract (C8)
 
 
 class Q8KBlock(C.Structure):
@@ -163,7 +164,7 @@ def rope_table(n_pos, n_rot, base):
     return out
 
 
-def attn_head(q, k16, v16, nk, scale, chunk=256):
+def attn_head(q, k16, v16, nk, scale, chunk=128):
     """one query head over f16 keys/values [nk, head_dim] (uint16 bit patterns)"""
     q = np.ascontiguousarray(q, np.float32)
     k16 = np.ascontiguousarray(k16, np.uint16)
@@ -181,7 +182,7 @@ class Model:
     def __init__(self, cfg, tensors: dict):
         c = Config(cfg.n_layer, cfg.n_embd, cfg.n_head, cfg.n_head_kv, cfg.head_dim, cfg.n_expert,
                    cfg.n_expert_used, cfg.n_ff_exp, cfg.n_vocab, cfg.head_dim, cfg.rms_eps, cfg.rope_freq_base,
-                   cfg.expert_workers, 256, cfg.max_positions)
+                   cfg.expert_workers, ATTN_CHUNK, cfg.max_positions)
         self.cfg = cfg
         self._keep = []
         arr = (Tensor * len(tensors))()
