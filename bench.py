@@ -203,8 +203,10 @@ def run_ours(args, rank, world, local_rank):
     # per-kernel device times (serialised launches) for the roofline
     prof = runner.profile_decode(cache, [nxt], args.prof_steps) if args.prof_steps else {}
     gu_bytes, dn_bytes = expert_bytes(cfg)
-    gu = prof.get("expert_gateup", (1, 0.0))
-    dn = prof.get("expert_down", (1, 0.0))
+    # per-phase kernels: the expert kernels' times; the persistent step: its gate/up and down
+    # phases (slowest CTA, from the in-kernel timeline)
+    gu = prof.get("expert_gateup", prof.get("ph5_gateup_work", (1, 0.0)))
+    dn = prof.get("expert_down", prof.get("ph6_down_work", (1, 0.0)))
     exp_ms = gu[1] / max(gu[0], 1) + dn[1] / max(dn[0], 1)
     achieved = (gu_bytes + dn_bytes) / (exp_ms / 1e3) / 1e9 if exp_ms > 0 else None
     peak, peak_kind = peaks()

@@ -18,6 +18,7 @@
 #include "../../include/bigtea_decode.h"
 #include "bt_common.cuh"
 #include "kernels.cuh"
+#include "step_kernel.cuh"
 
 using namespace bt;
 
@@ -127,6 +128,12 @@ struct bt_engine {
     std::vector<std::pair<std::string, std::pair<cudaEvent_t, cudaEvent_t>>> ev_used;
     double last_device_ms = 0;
     bool pdl = true;
+    bool mega = true;      // run single-token steps of up to STEP_MAX_T sequences as one persistent kernel
+    DevBuf layer_dev;      // LayerDev[n_layer] for the persistent kernel
+    QMatDev out_dev{};
+    DevBuf gbar;           // grid barrier words of the persistent kernel
+    DevBuf trace;          // persistent-kernel timeline (profiling only)
+    bool tracing = false;
     // L2 bulk prefetch of the next kernels' inputs: measured slower (the issuing CTAs wait on
     // their prefetches), so off unless asked for
     bool prefetch = false;
@@ -322,7 +329,43 @@ static int alloc_scratch(bt_engine *e) {
     return BT_OK;
 }
 
+static QMatDev qmat_dev(const QMat &m) {
+    QMatDev d{};
+    d.w = m.buf.as<uint8_t>();
+    d.type = m.type;
+    d.nsb = m.g.nsb;
+    d.rpt = m.g.rpt;
+    d.S = m.g.S;
+    d.tile_bytes = m.g.tile_bytes;
+    d.rows = (int)m.rows;
+    d.n_tiles = (int)m.g.n_tiles;
+    d.mat_bytes = m.mat_bytes;
+    return d;
+}
+
 static int finish_create(bt_engine *e) {
+    std::vector<LayerDev> ld(e->d.n_layer);
+    for (uint32_t il = 0; il < e->d.n_layer; il++) {
+        Layer &l = e->L[il];
+        LayerDev &x = ld[il];
+        x.attn_norm = l.attn_norm.as<float>();
+        x.q_norm = l.q_norm.as<float>();
+        x.k_norm = l.k_norm.as<float>();
+        x.ffn_norm = l.ffn_norm.as<float>();
+        x.gate_inp = l.gate_inp.as<float>();
+        x.q = qmat_dev(l.q);
+        x.k = qmat_dev(l.k);
+        x.v = qmat_dev(l.v);
+        x.o = qmat_dev(l.o);
+        x.gate = qmat_dev(l.gate);
+        x.up = qmat_dev(l.up);
+        x.down = qmat_dev(l.down);
+    }
+    CK(e->layer_dev.alloc(ld.size() * sizeof(LayerDev)));
+    CK(cudaMemcpy(e->layer_dev.p, ld.data(), ld.size() * sizeof(LayerDev), cudaMemcpyHostToDevice));
+    e->out_dev = qmat_dev(e->out);
+    CK(e->gbar.alloc(64));
+    CK(cudaMemset(e->gbar.p, 0, 64));
     std::vector<float> cs;
     rope_table(e->d, cs);
     CK(e->rope.alloc(cs.size() * 4));
@@ -444,6 +487,7 @@ static int engine_init_device(bt_engine *e, int device) {
     if (prop.major < 10) return fail(BT_ERR_UNSUPPORTED, "this build targets sm_100a (B200)");
     e->n_sm = prop.multiProcessorCount;
     CK(init_kernel_attributes());
+    CK(init_step_kernel_attributes());
     CK(cudaStreamCreateWithFlags(&e->st, cudaStreamNonBlocking));
     return BT_OK;
 }
@@ -941,8 +985,89 @@ static int upload_plan(bt_engine *e, const StepPlan &p) {
     return BT_OK;
 }
 
+// Can this step run as one persistent kernel? Single-token steps of up to STEP_MAX_T
+// sequences whose activations fit the kernel's shared memory.
+static bool step_eligible(const bt_engine *e, const bt_kv *kv, const StepPlan &p) {
+    if (!e->mega || p.T > STEP_MAX_T || p.out_first != 0 || (int)p.x_rows.size() != p.T) return false;
+    for (int t = 0; t < p.T; t++)
+        if (!p.single[t] || p.local_idx[t] != 0 || p.x_rows[t] != t || p.st_lrow[t] != t) return false;
+    if ((int)p.st_seq.size() != p.T) return false;
+    const bt_model_desc &d = e->d;
+    const int nsbE = d.n_embd / 256, nsbQ = d.n_head * d.head_dim / 256, nsbF = d.n_ff_exp / 256;
+    int blocks = nsbE > nsbQ ? nsbE : nsbQ;
+    blocks = (int)d.n_expert_used * nsbF > blocks ? (int)d.n_expert_used * nsbF : blocks;
+    if ((size_t)p.T * blocks * sizeof(ActBlock) > (size_t)STEP_ACT_BYTES) return false;
+    if ((long long)e->L[0].gate.g.nsb * 1 > 32 || 32 / nsbF < 1) return false;
+    const int max_chunks = (int)((kv->max_positions + ATTN_CHUNK - 1) / ATTN_CHUNK);
+    if (3 * max_chunks * 4 > STEP_CBUF_BYTES || d.n_expert > 512) return false;
+    if ((long long)d.n_expert_used * e->L[0].down.g.tile_bytes > STEP_REGION_BYTES / 8) return false;
+    return true;
+}
+
+static int launch_persistent_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) {
+    const bt_model_desc &d = e->d;
+    StepArgs a{};
+    a.layers = e->layer_dev.as<LayerDev>();
+    a.n_layer = (int)d.n_layer;
+    a.out = e->out_dev;
+    a.out_norm = e->out_norm.as<float>();
+    a.embd = e->embd.raw.as<uint8_t>();
+    a.embd_type = e->embd.type;
+    a.E = d.n_embd;
+    a.H = d.n_head;
+    a.HK = d.n_head_kv;
+    a.D = d.head_dim;
+    a.G = d.n_head / d.n_head_kv;
+    a.NE = d.n_expert;
+    a.K = d.n_expert_used;
+    a.F = d.n_ff_exp;
+    a.V = d.n_vocab;
+    a.workers = (int)d.expert_workers;
+    a.n_rot = d.n_rot;
+    a.eps = d.rms_eps;
+    a.scale = 1.0f / sqrtf((float)d.head_dim);
+    a.rope = e->rope.as<float>();
+    a.T = p.T;
+    a.tokens = e->tokens.as<int>();
+    a.seq_of = e->seq_of.as<int>();
+    a.pos_of = e->pos_of.as<int>();
+    a.dev_len = kv->dev_len.as<int>();
+    a.kv = kv->pool.as<__half>();
+    a.block_table = kv->bt_dev.as<int>();
+    a.max_blocks = kv->max_blocks;
+    a.n_blocks = kv->n_blocks;
+    a.max_chunks = (int)((kv->max_positions + ATTN_CHUNK - 1) / ATTN_CHUNK);
+    a.x = e->x.as<float>();
+    a.ffn_in = e->ffn_in.as<float>();
+    a.qkv = e->qkv.as<float>();
+    a.att = e->att.as<float>();
+    a.part = e->part.as<float>();
+    a.rlog = e->rlog.as<float>();
+    a.act = e->act.as<float>();
+    a.dbg_ids = e->dbg_ids.as<int>();
+    a.dbg_w = e->dbg_w.as<float>();
+    a.TB = e->TB;
+    a.logits = e->logits.as<float>();
+    a.amax = e->amax.as<unsigned long long>();
+    a.next_token = e->next_tok.as<int>();
+    a.tokens_buf = greedy ? e->tokens.as<int>() : nullptr;
+    a.gen_out = greedy ? e->gen_out.as<int>() : nullptr;
+    a.gen_count = e->gen_count.as<int>();
+    a.n_out = p.T;
+    a.bar = e->gbar.as<unsigned>();
+    a.err = e->err.as<int>();
+    a.trace = e->tracing ? e->trace.as<unsigned long long>() : nullptr;
+    // the barrier's arrival count starts from zero even if an earlier launch stopped early
+    CK(cudaMemsetAsync(e->gbar.p, 0, 8, e->st));
+    timer_begin(e, "decode_step");
+    CK(launch_decode_step(a, kv->tmap, e->n_sm, e->st));
+    timer_end(e);
+    return BT_OK;
+}
+
 // All kernels of one step on e->st. Capturable: no host synchronisation inside.
 static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) {
+    if (step_eligible(e, kv, p)) return launch_persistent_step(e, kv, p, greedy);
     const bt_model_desc &d = e->d;
     const int T = p.T, E = d.n_embd, H = d.n_head, HK = d.n_head_kv, D = d.head_dim;
     const int QW = H * D, KW = HK * D, K = d.n_expert_used, F = d.n_ff_exp, NE = d.n_expert;
@@ -1392,6 +1517,84 @@ extern "C" int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_id
     e->pdl = pdl;
     if (r) return r;
     if ((r = greedy_finish(e, kv, seq_ids, n_seqs, n_steps, nullptr, nullptr))) return r;
+    if (e->mega && (int)n_seqs <= STEP_MAX_T && n_steps > 0) {
+        // one more step with the in-kernel timeline: per phase, the slowest CTA's work and the
+        // barrier's release latency, averaged over layers
+        const int grid = e->n_sm, L = (int)e->d.n_layer;
+        const size_t rows = (size_t)(L + 1) * STEP_PHASES + 1;
+        CK(e->trace.alloc(rows * (grid + 1) * 8));
+        CK(cudaMemset(e->trace.p, 0, rows * (grid + 1) * 8));
+        StepPlan q;
+        if ((r = greedy_prepare(e, kv, seq_ids, first_tokens, n_seqs, 1, q))) return r;
+        e->tracing = true;
+        r = launch_step(e, kv, q, true);
+        e->tracing = false;
+        if (r) return r;
+        CK(cudaStreamSynchronize(e->st));
+        if ((r = greedy_finish(e, kv, seq_ids, n_seqs, 1, nullptr, nullptr))) return r;
+        std::vector<unsigned long long> tr(rows * (grid + 1));
+        CK(cudaMemcpy(tr.data(), e->trace.p, tr.size() * 8, cudaMemcpyDeviceToHost));
+        const char *names[8] = {"ph0_qkv", "ph1_attn", "ph2_combine", "ph3_attn_out", "ph4_router",
+                                "ph5_gateup", "ph6_down", "ph7_unused"};
+        // points inside phases: slowest CTA, measured from the departure of the barrier before
+        const char *pnames[8] = {"pt_qkv_staged", "pt_attn_item1", "pt_o_staged", "pt_router_staged",
+                                 "pt_gateup_routed", "pt_gateup_units", "pt_down_staged", "pt_unused"};
+        const int point_after[8] = {-1, 0, 2, 3, -1, 4, 5, -1};  // barrier whose departure starts each point
+        // cycle counters inside phases (max over warps, then over CTAs), as microseconds at the
+        // SM clock the device reports
+        int clk_khz = 0;
+        cudaDeviceGetAttribute(&clk_khz, cudaDevAttrClockRate, e->device);
+        const char *cnames[6] = {"cyc_qkv_wait", "cyc_qkv_compute", "cyc_down_wait", "cyc_down_compute",
+                                 "cyc_gateup_wait", "cyc_gateup_compute"};
+        for (int l = 0; l < L; l++)
+            for (int k = 7; k <= 12; k++) {
+                const unsigned long long *row = tr.data() + ((size_t)l * STEP_PHASES + 8 + k) * (grid + 1);
+                unsigned long long mx = 0;
+                for (int c = 0; c < grid; c++) mx = row[c] > mx ? row[c] : mx;
+                KernelTimer &w = e->timers[cnames[k - 7]];
+                w.launches++;
+                w.ms += clk_khz ? (double)mx / (double)clk_khz : 0.0;
+            }
+        for (int l = 0; l < L; l++) {
+            for (int k = 0; k < 7; k++) {
+                const unsigned long long *row = tr.data() + ((size_t)l * STEP_PHASES + 8 + k) * (grid + 1);
+                unsigned long long mx = 0;
+                for (int c = 0; c < grid; c++) mx = row[c] > mx ? row[c] : mx;
+                if (!mx) continue;
+                unsigned long long start;
+                if (point_after[k] >= 0) {
+                    const unsigned long long *b = tr.data() + ((size_t)l * STEP_PHASES + point_after[k]) * (grid + 1);
+                    start = b[grid];
+                    if (k == 2 && !start) start = tr[((size_t)l * STEP_PHASES + 1) * (grid + 1) + grid];
+                } else if (k == 0) {
+                    start = l == 0 ? tr[(rows - 1) * (grid + 1)] : tr[((size_t)(l - 1) * STEP_PHASES + 6) * (grid + 1) + grid];
+                } else {  // k == 4: from the router barrier
+                    start = tr[((size_t)l * STEP_PHASES + 4) * (grid + 1) + grid];
+                }
+                if (!start || mx < start) continue;
+                KernelTimer &w = e->timers[pnames[k]];
+                w.launches++;
+                w.ms += (double)(mx - start) * 1e-6;
+            }
+        }
+        unsigned long long prev = tr[(rows - 1) * (grid + 1)];  // kernel start (CTA 0)
+        for (int l = 0; l <= L; l++) {
+            for (int ph = 0; ph < 8; ph++) {
+                const unsigned long long *row = tr.data() + ((size_t)l * STEP_PHASES + ph) * (grid + 1);
+                if (!row[grid]) continue;  // this barrier did not run (no combine, or past the head)
+                unsigned long long mx = 0;
+                for (int c = 0; c < grid; c++) mx = row[c] > mx ? row[c] : mx;
+                std::string base = l == L ? std::string("ph_head") : std::string(names[ph]);
+                KernelTimer &w = e->timers[base + "_work"];
+                w.launches++;
+                w.ms += (double)(mx - prev) * 1e-6;
+                KernelTimer &b = e->timers[base + "_barrier"];
+                b.launches++;
+                b.ms += (double)(row[grid] - mx) * 1e-6;
+                prev = row[grid];
+            }
+        }
+    }
     uint32_t i = 0;
     for (auto &kt : e->timers) {
         if (i < max_out && out) {
@@ -1410,6 +1613,12 @@ extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
     if (!e || !name) return fail(BT_ERR_INVALID, "null argument");
     if (!strcmp(name, "prefetch")) {
         e->prefetch = value != 0;
+        for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
+        e->graphs.clear();
+        return BT_OK;
+    }
+    if (!strcmp(name, "persistent")) {
+        e->mega = value != 0;
         for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
         e->graphs.clear();
         return BT_OK;

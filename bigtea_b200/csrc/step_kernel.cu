@@ -1,0 +1,1068 @@
+// step_kernel.cu -- the persistent decode step for sm_100a.
+//
+// One cooperative kernel (one CTA per SM) runs every layer of a single-token decode step
+// for up to STEP_MAX_T sequences: embedding, then per layer the phases
+//   QKV (RMSNorm + q/k/v GEMV) | ATTN (q/k head norm, RoPE, f16 KV append, split-K flash
+//   decode) | COMBINE (chunk merge) | O (attn_output GEMV + residual) | ROUTER (ffn RMSNorm,
+//   F32 router rows) | GATEUP (soft_max + route() in every CTA, expert gate/up GEMV, SiLU)
+//   | DOWN (expert down GEMV, the reference's expert sum, residual)
+// and finally the output head with a fused argmax and the step's bookkeeping.
+// Phases are separated by a grid barrier with a bounded wait. Weights never depend on the
+// previous phase, so each phase's first tiles are requested by 1-D TMA into the warps' rings
+// before the barrier that precedes it; the attention K/V pages of a CTA's first chunk are
+// requested the same way. The arithmetic is the contract of bt_common.cuh, operation for
+// operation the same as the per-phase kernels of kernels.cu (the tests compare both paths
+// with the CPU oracle bit for bit).
+//
+// Reference call sites: core/arch/src/stream.rs forward_cached_inner 2106-2915 (per layer:
+// 2265-2474 q/k/v, 2545-2552 KvCache::push, 2554-2703 attention, 2723-2726 residual,
+// 2784-2831 router, 869-888 route, 1084-1289 experts, 2841-2843 residual, 2853-2914 head).
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+#include "bt_common.cuh"
+#include "kernels.cuh"
+#include "stage.cuh"
+#include "step_kernel.cuh"
+
+namespace bt {
+
+constexpr int STEP_THREADS = 256, STEP_WARPS = 8;
+constexpr int RING_SLOTS = 4;
+constexpr int PART_ROW = 132;  // floats per (chunk, head) partial: acc[128], m, l, pad
+
+// ------------------------------------------------------------------ shared memory map
+struct StepSmem {
+    uint8_t *region;     // rings (GEMV phases) or K/V tiles (attention), STEP_REGION_BYTES
+    ActBlock *act;       // activations, STEP_ACT_BYTES
+    uint64_t *ring_bar;  // [warp][RING_SLOTS]
+    uint64_t *attn_bar;
+    float *normS;        // [STEP_MAX_T]
+    float *misc;         // 64 floats
+    int *sel_ids;        // [STEP_MAX_T][MAX_K]
+    float *sel_w;        // [STEP_MAX_T][MAX_K]
+    int *pos;            // [STEP_MAX_T]
+    float *cbuf;         // combine scratch: 3 * max_chunks floats
+};
+
+// ------------------------------------------------------------------ grid barrier
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
+    unsigned v;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Sense by generation: the last CTA to arrive resets the count and advances the generation.
+// The wait is bounded; a timeout sets the engine's error word, after which every CTA leaves
+// at its next barrier.
+__device__ __forceinline__ unsigned long long global_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ bool grid_sync(unsigned *bar, int *err, unsigned long long *trace_row = nullptr) {
+    __syncthreads();
+    if (threadIdx.x == 0 && trace_row) trace_row[blockIdx.x] = global_ns();
+    if (threadIdx.x == 0) {
+        const unsigned gen = ld_acquire_gpu(bar + 1);
+        __threadfence();
+        const unsigned arrived = atomicAdd(bar, 1u);
+        if (arrived == gridDim.x - 1) {
+            atomicExch(bar, 0u);
+            __threadfence();
+            atomicAdd(bar + 1, 1u);
+        } else {
+            const long long t0 = clock64();
+            while (ld_acquire_gpu(bar + 1) == gen) {
+                if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+                    atomicOr(err, ERR_WAIT_TIMEOUT);
+                    break;
+                }
+            }
+        }
+        __threadfence();
+        if (trace_row && blockIdx.x == 0) trace_row[gridDim.x] = global_ns();
+    }
+    __syncthreads();
+    return *reinterpret_cast<volatile int *>(err) == 0;
+}
+
+// ------------------------------------------------------------------ per-warp TMA ring
+// A warp streams its units through `nst` slots of `slot_bytes` in its share of the region.
+// Every lane keeps the same counters; lane 0 issues the copies.
+struct WarpRing {
+    uint8_t *base;
+    uint64_t *bars;
+    uint32_t par;  // next parity to wait for, one bit per slot
+    int nst, slot_bytes, issued, done;
+
+    __device__ void configure(int sbytes) {
+        slot_bytes = sbytes;
+        nst = (STEP_REGION_BYTES / STEP_WARPS) / sbytes;
+        nst = nst > RING_SLOTS ? RING_SLOTS : nst;
+        issued = done = 0;
+    }
+    __device__ uint8_t *slot_ptr(int j) const { return base + (size_t)(j % nst) * slot_bytes; }
+    __device__ uint64_t *slot_bar(int j) const { return bars + (j % nst); }
+    __device__ bool can_issue() const { return issued - done < nst; }
+    // wait for unit j (== done); false if the bounded wait ran out
+    __device__ bool wait(int j, int *err) {
+        const int s = j % nst;
+        const bool ok = __all_sync(FULL, mbar_wait(bars + s, (par >> s) & 1u, err));
+        par ^= 1u << s;
+        return ok;
+    }
+};
+
+// ------------------------------------------------------------------ unit ranges
+__device__ __forceinline__ void cta_range(long long total, long long &u0, long long &u1) {
+    u0 = (long long)blockIdx.x * total / gridDim.x;
+    u1 = (long long)(blockIdx.x + 1) * total / gridDim.x;
+}
+__device__ __forceinline__ int warp_units(long long u0, long long u1, int warp) {
+    return (u1 - u0 > warp) ? (int)((u1 - u0 - warp + STEP_WARPS - 1) / STEP_WARPS) : 0;
+}
+
+// ------------------------------------------------------------------ GEMV phases
+// A "segment list" GEMV over tiles (q|k|v, attn_output, output head).
+struct SegList {
+    const QMatDev *m[3];
+    int out_off[3];
+    int n;
+    int tile0[3];
+    int total;
+};
+
+__device__ __forceinline__ SegList make_segs(const QMatDev *a, int oa, const QMatDev *b, int ob, const QMatDev *c,
+                                              int oc) {
+    SegList s;
+    s.n = 0;
+    s.total = 0;
+    const QMatDev *ms[3] = {a, b, c};
+    int os[3] = {oa, ob, oc};
+    for (int i = 0; i < 3; i++) {
+        if (!ms[i]) continue;
+        s.m[s.n] = ms[i];
+        s.out_off[s.n] = os[i];
+        s.tile0[s.n] = s.total;
+        s.total += ms[i]->n_tiles;
+        s.n++;
+    }
+    return s;
+}
+
+__device__ __forceinline__ int seg_of(const SegList &s, long long u) {
+    int si = 0;
+    if (s.n > 1 && u >= s.tile0[1]) si = 1;
+    if (s.n > 2 && u >= s.tile0[2]) si = 2;
+    return si;
+}
+
+__device__ __forceinline__ int seglist_max_tile(const SegList &s) {
+    int m = 0;
+    for (int i = 0; i < s.n; i++) m = s.m[i]->tile_bytes > m ? s.m[i]->tile_bytes : m;
+    return m;
+}
+
+__device__ void gemv_issue(WarpRing &r, const SegList &s, long long u0, int warp, int lane) {
+    const int j = r.issued;
+    if (lane == 0) {
+        const long long u = u0 + warp + (long long)j * STEP_WARPS;
+        const QMatDev &m = *s.m[seg_of(s, u)];
+        const uint8_t *src = m.w + (u - s.tile0[seg_of(s, u)]) * (long long)m.tile_bytes;
+        fence_proxy_async();
+        mbar_arrive_expect_tx(r.slot_bar(j), m.tile_bytes);
+        bulk_g2s(r.slot_ptr(j), src, m.tile_bytes, r.slot_bar(j));
+    }
+    r.issued++;
+}
+
+__device__ void gemv_preissue(WarpRing &r, const SegList &s, int warp, int lane) {
+    long long u0, u1;
+    cta_range(s.total, u0, u1);
+    const int n = warp_units(u0, u1, warp);
+    r.configure(seglist_max_tile(s));
+    while (r.issued < n && r.can_issue()) gemv_issue(r, s, u0, warp, lane);
+}
+
+// Consume every unit of this warp; y[t*ys + off + row] = acc (+ res[t*rs + off + row]);
+// `amax` folds an argmax over the written rows (output head).
+__device__ bool gemv_run(WarpRing &r, const SegList &s, const ActBlock *act, int nsbK, int T, float *y, long long ys,
+                         const float *res, long long rs, unsigned long long *amax, int *err, int warp, int lane,
+                         unsigned long long *cyc = nullptr) {
+    long long cw = 0, cc0 = clock64();
+    long long u0, u1;
+    cta_range(s.total, u0, u1);
+    const int n = warp_units(u0, u1, warp);
+    unsigned long long best[STEP_MAX_T];
+#pragma unroll
+    for (int t = 0; t < STEP_MAX_T; t++) best[t] = 0ull;
+    bool ok = true;
+    for (int j = 0; j < n; j++) {
+        while (r.issued < n && r.can_issue()) gemv_issue(r, s, u0, warp, lane);
+        const long long w0 = clock64();
+        if (!r.wait(j, err)) {
+            ok = false;
+            break;
+        }
+        cw += clock64() - w0;
+        const long long u = u0 + warp + (long long)j * STEP_WARPS;
+        const int si = seg_of(s, u);
+        const QMatDev &m = *s.m[si];
+        const uint8_t *tile = r.slot_ptr(j);
+        const long long tl = u - s.tile0[si];
+        const bool active = lane < m.S;
+        const int rit = active ? lane / m.nsb : 0, b = active ? lane % m.nsb : 0;
+        const long long row = tl * m.rpt + rit;
+        const bool writer = active && b == 0 && row < m.rows;
+        for (int t = 0; t < T; t++) {
+            float v = 0.0f;
+            if (active) {
+                const ActBlock &ab = act[t * nsbK + b];
+                v = (m.type == T_Q4_K) ? q4k_slot_dot(tile, m.S, lane, ab) : q6k_slot_dot(tile, m.S, lane, ab);
+            }
+            float acc = 0.0f;
+            for (int b2 = 0; b2 < m.nsb; b2++) {
+                const int srcl = rit * m.nsb + b2;
+                acc = __fadd_rn(acc, __shfl_sync(FULL, v, srcl < 32 ? srcl : 31));
+            }
+            if (writer) {
+                const long long o = s.out_off[si] + row;
+                float val = acc;
+                if (res) val = __fadd_rn(res[t * rs + o], acc);
+                y[t * ys + o] = val;
+                if (amax) {
+                    const unsigned long long key =
+                        ((unsigned long long)((unsigned)total_key(val) ^ 0x80000000u) << 32) | (unsigned)o;
+#pragma unroll
+                    for (int tt = 0; tt < STEP_MAX_T; tt++)
+                        if (tt == t && key > best[tt]) best[tt] = key;
+                }
+            }
+        }
+        __syncwarp();
+        r.done++;
+    }
+    if (cyc && lane == 0) {
+        atomicMax(cyc, (unsigned long long)cw);
+        atomicMax(cyc + 1, (unsigned long long)(clock64() - cc0 - cw));
+    }
+    if (amax) {
+        for (int t = 0; t < T; t++) {
+            unsigned long long bv = best[0];
+#pragma unroll
+            for (int tt = 1; tt < STEP_MAX_T; tt++)
+                if (tt == t) bv = best[tt];
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) {
+                const unsigned long long ob = __shfl_xor_sync(FULL, bv, o);
+                bv = ob > bv ? ob : bv;
+            }
+            if (lane == 0 && bv) atomicMax(amax + t, bv);
+        }
+    }
+    return ok;
+}
+
+// ------------------------------------------------------------------ expert phases
+__device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, long long u0, int warp,
+                             int lane) {
+    const int j = r.issued;
+    if (lane == 0) {
+        const long long u = u0 + warp + (long long)j * STEP_WARPS;
+        const int tile = (int)(u % L.gate.n_tiles);
+        const int tk = (int)(u / L.gate.n_tiles);
+        const int e = sm.sel_ids[(tk / K) * MAX_K + tk % K];
+        uint8_t *dst = r.slot_ptr(j);
+        fence_proxy_async();
+        mbar_arrive_expect_tx(r.slot_bar(j), L.gate.tile_bytes + L.up.tile_bytes);
+        bulk_g2s(dst, L.gate.w + e * L.gate.mat_bytes + (long long)tile * L.gate.tile_bytes, L.gate.tile_bytes,
+                 r.slot_bar(j));
+        bulk_g2s(dst + L.gate.tile_bytes, L.up.w + e * L.up.mat_bytes + (long long)tile * L.up.tile_bytes,
+                 L.up.tile_bytes, r.slot_bar(j));
+    }
+    r.issued++;
+}
+
+__device__ void down_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int E, long long u0, int warp,
+                           int lane) {
+    const int j = r.issued;
+    if (lane == 0) {
+        const long long u = u0 + warp + (long long)j * STEP_WARPS;
+        const int row = (int)(u % E), t = (int)(u / E);
+        uint8_t *dst = r.slot_ptr(j);
+        fence_proxy_async();
+        mbar_arrive_expect_tx(r.slot_bar(j), K * L.down.tile_bytes);
+        for (int k = 0; k < K; k++) {
+            const int e = sm.sel_ids[t * MAX_K + k];
+            bulk_g2s(dst + k * L.down.tile_bytes, L.down.w + e * L.down.mat_bytes + (long long)row * L.down.tile_bytes,
+                     L.down.tile_bytes, r.slot_bar(j));
+        }
+    }
+    r.issued++;
+}
+
+// ------------------------------------------------------------------ attention item helpers
+struct AttnItem {
+    int t, g, c;
+};
+
+// item i of the step's attention work: tokens in order, kv heads, chunks
+__device__ __forceinline__ bool attn_item(const StepArgs &p, const int *pos, long long i, AttnItem &it) {
+    for (int t = 0; t < p.T; t++) {
+        const int nc = (pos[t] + 1 + ATTN_CHUNK - 1) / ATTN_CHUNK;
+        const long long cnt = (long long)p.HK * nc;
+        if (i < cnt) {
+            it.t = t;
+            it.g = (int)(i / nc);
+            it.c = (int)(i % nc);
+            return true;
+        }
+        i -= cnt;
+    }
+    return false;
+}
+
+__device__ __forceinline__ long long attn_items(const StepArgs &p, const int *pos) {
+    long long n = 0;
+    for (int t = 0; t < p.T; t++) n += (long long)p.HK * ((pos[t] + 1 + ATTN_CHUNK - 1) / ATTN_CHUNK);
+    return n;
+}
+
+// the TMA loads of one item's K and V pages into the region (thread 0)
+__device__ void attn_issue(const StepArgs &p, const CUtensorMap *tmap, const StepSmem &sm, const AttnItem &it,
+                           int layer) {
+    const int seq = p.seq_of[it.t];
+    const int nk = sm.pos[it.t] + 1, base = it.c * ATTN_CHUNK;
+    const int cnt = nk - base < ATTN_CHUNK ? nk - base : ATTN_CHUNK;
+    const int npages = (cnt + 15) / 16;
+    uint8_t *K0 = sm.region, *K1 = K0 + 16384, *V0 = K0 + 32768, *V1 = K0 + 49152;
+    fence_proxy_async();
+    mbar_arrive_expect_tx(sm.attn_bar, npages * 8192);
+    for (int pg = 0; pg < npages; pg++) {
+        const int blk = p.block_table[seq * p.max_blocks + (base >> 4) + pg];
+        const int rowK = (int)(((((long long)layer * p.n_blocks + blk) * 2 + 0) * p.HK + it.g) * 16);
+        const int rowV = rowK + p.HK * 16;
+        tma_load_2d(K0 + pg * 2048, tmap, 0, rowK, sm.attn_bar);
+        tma_load_2d(K1 + pg * 2048, tmap, 64, rowK, sm.attn_bar);
+        tma_load_2d(V0 + pg * 2048, tmap, 0, rowV, sm.attn_bar);
+        tma_load_2d(V1 + pg * 2048, tmap, 64, rowV, sm.attn_bar);
+    }
+}
+
+// q/k head RMSNorm (C5/C6) and NeoX RoPE (C9) of one head held 4 values per lane
+// (lane l: l, l+32, l+64, l+96).
+__device__ __forceinline__ void head_norm_rope(float v[4], const float *w, const float *cs, float eps, int lane) {
+    float acc = 0.0f;
+#pragma unroll
+    for (int i = 0; i < 4; i++) acc = fmaf(v[i], v[i], acc);
+    acc = butterfly_sum(acc);
+    const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, 128.0f), eps)));
+#pragma unroll
+    for (int i = 0; i < 4; i++) v[i] = __fmul_rn(__fmul_rn(v[i], s), w[lane + 32 * i]);
+#pragma unroll
+    for (int i = 0; i < 2; i++) {
+        const int d = lane + 32 * i;
+        const float c = cs[2 * d], sn = cs[2 * d + 1];
+        const float x0 = v[i], x1 = v[i + 2];
+        const float a = __fmul_rn(x0, c), b = __fmul_rn(x1, sn), e = __fmul_rn(x0, sn), f = __fmul_rn(x1, c);
+        v[i] = __fsub_rn(a, b);
+        v[i + 2] = __fadd_rn(e, f);
+    }
+}
+
+template <int N>
+__device__ __forceinline__ void lds_n(float (&dst)[N], const float *src) {
+    if constexpr (N == 4) {
+        float4 v = *reinterpret_cast<const float4 *>(src);
+        dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+    } else if constexpr (N == 2) {
+        float2 v = *reinterpret_cast<const float2 *>(src);
+        dst[0] = v.x; dst[1] = v.y;
+    } else {
+#pragma unroll
+        for (int k = 0; k < N; k++) dst[k] = src[k];
+    }
+}
+
+// One attention item (C8): the K/V tiles are in flight (attn_issue); stages q, appends the new
+// key and value if this is the token's last chunk, then scores, softmax and P*V.
+template <int G>
+__device__ bool attn_run(const StepArgs &p, const LayerDev &L, const StepSmem &sm, const AttnItem &it, int layer,
+                         uint32_t &apar) {
+    constexpr int D = 128, HPT = G / 2, CH = ATTN_CHUNK;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint8_t *K0 = sm.region, *K1 = K0 + 16384, *V0 = K0 + 32768, *V1 = K0 + 49152;
+    float *qs = reinterpret_cast<float *>(sm.region + 65536);  // [D][G]
+    float *ps = qs + D * G;                                    // [CH][G]
+    float *red = ps + CH * G;                                  // [8][8]
+    float *red2 = red + 64;                                    // [4][8]
+    float *s_m = red2 + 32, *s_l = s_m + 8;
+    __half *kvnew = reinterpret_cast<__half *>(s_l + 8);       // [2][128] the appended key and value
+    const int t = it.t, g = it.g, c = it.c;
+    const int pos = sm.pos[t], nk = pos + 1, nc = (nk + CH - 1) / CH;
+    const int base = c * CH, cnt = nk - base < CH ? nk - base : CH;
+    const bool last = c == nc - 1;
+    const float *qkv = p.qkv + (long long)t * (p.H * D + 2 * p.HK * D);
+    const float *cs = p.rope + (long long)pos * p.n_rot;
+    // q heads g*G .. g*G+G-1: warp w < G stages head w; a warp G (or 0 when G == 8) the new k/v
+    if (warp < G) {
+        float v[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) v[i] = qkv[(g * G + warp) * D + lane + 32 * i];
+        head_norm_rope(v, L.q_norm, cs, p.eps, lane);
+#pragma unroll
+        for (int i = 0; i < 4; i++) qs[(lane + 32 * i) * G + warp] = f16_round(v[i]);
+    }
+    if (last && warp == (G < 8 ? G : 0)) {
+        // KvCache::push of this token's head g: k normed and roped, v as is, both to f16
+        float kk[4], vv[4];
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            kk[i] = qkv[p.H * D + g * D + lane + 32 * i];
+            vv[i] = qkv[p.H * D + p.HK * D + g * D + lane + 32 * i];
+        }
+        head_norm_rope(kk, L.k_norm, cs, p.eps, lane);
+        const int seq = p.seq_of[t];
+        const int blk = p.block_table[seq * p.max_blocks + pos / 16];
+        const long long rowK = ((((long long)layer * p.n_blocks + blk) * 2 + 0) * p.HK + g) * 16 + pos % 16;
+        const long long rowV = rowK + (long long)p.HK * 16;
+#pragma unroll
+        for (int i = 0; i < 4; i++) {
+            const __half hk = __float2half_rn(kk[i]), hv = __float2half_rn(vv[i]);
+            p.kv[rowK * D + lane + 32 * i] = hk;
+            p.kv[rowV * D + lane + 32 * i] = hv;
+            kvnew[lane + 32 * i] = hk;
+            kvnew[128 + lane + 32 * i] = hv;
+        }
+    }
+    __syncthreads();
+    const bool landed = mbar_wait(sm.attn_bar, apar, p.err);
+    apar ^= 1u;
+    if (__syncthreads_or(!landed)) return false;
+    if (last) {  // the new position's row of the tiles is the value just computed
+        const int r = pos - base;
+        if (tid < 32) {
+            const int d0 = tid * 4;  // 4 halves per thread: K then V
+            for (int e = 0; e < 4; e++) {
+                const int d = d0 + e;
+                const int cc = (d & 63) >> 3;
+                uint8_t *kt = (d < 64 ? K0 : K1) + r * 128 + ((cc ^ (r & 7)) << 4) + (d & 7) * 2;
+                uint8_t *vt = (d < 64 ? V0 : V1) + r * 128 + ((cc ^ (r & 7)) << 4) + (d & 7) * 2;
+                *reinterpret_cast<__half *>(kt) = kvnew[d];
+                *reinterpret_cast<__half *>(vt) = kvnew[128 + d];
+            }
+        }
+        __syncthreads();
+    }
+    // ---- scores: key k, heads hh*HPT .. +HPT
+    const int hh = tid >> 7, k = tid & 127;
+    const bool valid = k < cnt;
+    float sc[HPT];
+#pragma unroll
+    for (int h = 0; h < HPT; h++) sc[h] = 0.0f;
+#pragma unroll 2
+    for (int c16 = 0; c16 < 16; c16++) {
+        const uint8_t *kr = (c16 < 8) ? K0 : K1;
+        const uint4 w = *reinterpret_cast<const uint4 *>(kr + k * 128 + (((c16 & 7) ^ (k & 7)) << 4));
+        const __half *hk = reinterpret_cast<const __half *>(&w);
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+            const float kf = __half2float(hk[e]);
+            float q[HPT];
+            lds_n<HPT>(q, qs + (c16 * 8 + e) * G + hh * HPT);
+#pragma unroll
+            for (int h = 0; h < HPT; h++) sc[h] = fmaf(q[h], kf, sc[h]);
+        }
+    }
+    const float NEG_INF = -__int_as_float(0x7f800000);
+#pragma unroll
+    for (int h = 0; h < HPT; h++) {
+        sc[h] = valid ? __fmul_rn(sc[h], p.scale) : NEG_INF;
+        const float m = warp_max(sc[h]);
+        if (lane == 0) red[warp * 8 + h] = m;
+    }
+    __syncthreads();
+    if (tid < G) {
+        const int w0 = (tid / HPT) * 4, slot = tid % HPT;
+        float m = red[w0 * 8 + slot];
+        for (int w = 1; w < 4; w++) m = fmaxf(m, red[(w0 + w) * 8 + slot]);
+        s_m[tid] = m;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < HPT; h++) {
+        const int head = hh * HPT + h;
+        const float pr = valid ? bt_exp(__fsub_rn(sc[h], s_m[head])) : 0.0f;
+        ps[k * G + head] = pr;
+        const float ws = butterfly_sum(pr);
+        if (lane == 0) red2[(warp & 3) * 8 + head] = ws;
+    }
+    __syncthreads();
+    if (tid < G) {
+        float l = 0.0f;
+        for (int w = 0; w < CH / 32; w++) l = __fadd_rn(l, red2[w * 8 + tid]);
+        s_l[tid] = l;
+    }
+    // ---- P*V: column d, heads hq*HPT .. +HPT
+    const int d = tid & 127, hq = tid >> 7;
+    float acc[HPT];
+#pragma unroll
+    for (int h = 0; h < HPT; h++) acc[h] = 0.0f;
+    {
+        const int cc = (d & 63) >> 3;
+        const uint8_t *vcol = ((d < 64) ? V0 : V1) + (d & 7) * 2;
+        int off[8];
+#pragma unroll
+        for (int kk = 0; kk < 8; kk++) off[kk] = kk * 128 + ((cc ^ kk) << 4);
+        for (int j0 = 0; j0 < cnt; j0 += 8) {
+            const uint8_t *vb = vcol + j0 * 128;
+            const float *pb = ps + j0 * G + hq * HPT;
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) {
+                if (j0 + kk < cnt) {
+                    const float vf = __half2float(*reinterpret_cast<const __half *>(vb + off[kk]));
+                    float pj[HPT];
+                    lds_n<HPT>(pj, pb + kk * G);
+#pragma unroll
+                    for (int h = 0; h < HPT; h++) acc[h] = fmaf(pj[h], vf, acc[h]);
+                }
+            }
+        }
+    }
+    __syncthreads();
+    const int QW = p.H * D;
+    if (nc == 1) {
+#pragma unroll
+        for (int h = 0; h < HPT; h++) {
+            const int head = hq * HPT + h;
+            const float f = bt_exp(__fsub_rn(s_m[head], s_m[head]));
+            const float Lh = fmaf(s_l[head], f, 0.0f);
+            const float O = fmaf(acc[h], f, 0.0f);
+            p.att[(long long)t * QW + (g * G + head) * D + d] = __fdiv_rn(O, Lh);
+        }
+    } else {
+        const long long pbase = (((long long)t * p.HK + g) * p.max_chunks) * G * PART_ROW;
+#pragma unroll
+        for (int h = 0; h < HPT; h++) {
+            const int head = hq * HPT + h;
+            float *pp = p.part + pbase + ((long long)c * G + head) * PART_ROW;
+            pp[d] = acc[h];
+            if (d == 0) {
+                pp[D] = s_m[head];
+                pp[D + 1] = s_l[head];
+            }
+        }
+    }
+    __syncthreads();  // the tiles are free for the next item
+    return true;
+}
+
+// ------------------------------------------------------------------ the kernel
+template <int G>
+__global__ void __launch_bounds__(STEP_THREADS, 1)
+    decode_step_kernel(const __grid_constant__ StepArgs p, const __grid_constant__ CUtensorMap tmap) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    StepSmem sm;
+    sm.ring_bar = reinterpret_cast<uint64_t *>(smem);                      // 8 x 4 x 8 B
+    sm.attn_bar = sm.ring_bar + STEP_WARPS * RING_SLOTS;
+    sm.normS = reinterpret_cast<float *>(smem + 512);
+    sm.misc = sm.normS + STEP_MAX_T;
+    sm.pos = reinterpret_cast<int *>(sm.misc + 64);
+    sm.region = smem + 1024;
+    sm.act = reinterpret_cast<ActBlock *>(sm.region + STEP_REGION_BYTES);
+    sm.sel_ids = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(sm.act) + STEP_ACT_BYTES);
+    sm.sel_w = reinterpret_cast<float *>(sm.sel_ids + STEP_MAX_T * MAX_K);
+    sm.cbuf = sm.sel_w + STEP_MAX_T * MAX_K;
+
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int T = p.T, E = p.E, QW = p.H * 128, KW = p.HK * 128, K = p.K, F = p.F;
+    auto TR = [&](int layer, int ph) -> unsigned long long * {
+        return p.trace ? p.trace + ((long long)layer * STEP_PHASES + ph) * (gridDim.x + 1) : nullptr;
+    };
+    // a point inside a phase: this CTA's time when all its threads got there
+    unsigned long long *cycv = reinterpret_cast<unsigned long long *>(sm.cbuf + STEP_CBUF_BYTES / 4 - 64);  // [16]
+    auto CYC_RESET = [&]() {
+        if (p.trace) {
+            __syncthreads();
+            if (tid < 16) cycv[tid] = 0ull;
+            __syncthreads();
+        }
+    };
+    auto CYC_WRITE = [&](int layer, int k, int idx) {  // slot k <- cycles idx (max over warps)
+        if (!p.trace) return;
+        __syncthreads();
+        if (tid == 0) p.trace[((long long)layer * STEP_PHASES + 8 + k) * (gridDim.x + 1) + blockIdx.x] = cycv[idx];
+    };
+    auto POINT = [&](int layer, int k) {
+        if (!p.trace) return;
+        __syncthreads();
+        if (tid == 0) p.trace[((long long)layer * STEP_PHASES + 8 + k) * (gridDim.x + 1) + blockIdx.x] = global_ns();
+    };
+    if (p.trace && tid == 0 && blockIdx.x == 0) p.trace[((long long)(p.n_layer + 1) * STEP_PHASES) * (gridDim.x + 1)] = global_ns();
+    const int nsbE = E / 256, nsbQ = QW / 256, nsbF = F / 256;
+
+    WarpRing ring;
+    ring.base = sm.region + (size_t)warp * (STEP_REGION_BYTES / STEP_WARPS);
+    ring.bars = sm.ring_bar + warp * RING_SLOTS;
+    ring.par = 0;
+    ring.configure(4096);
+    if (lane == 0) {
+        for (int i = 0; i < RING_SLOTS; i++) mbar_init(ring.bars + i, 1);
+    }
+    if (tid == 0) mbar_init(sm.attn_bar, 1);
+    if (tid < T) sm.pos[tid] = p.dev_len[p.seq_of[tid]];
+    fence_mbar_init();
+    __syncthreads();
+    uint32_t apar = 0;
+    if (tid == 0) prefetch_tmap(&tmap);
+
+    // ---- embedding rows (get_rows) for every token, into the region, then layer 0 reads them
+    float *x0 = reinterpret_cast<float *>(sm.region);  // [T][E] f32, 16-byte aligned
+    {
+        const int bb = qk_block_bytes(p.embd_type);
+        for (int i = tid; i < T * E; i += STEP_THREADS) {
+            const int t = i / E, e = i % E;
+            const int tok = p.tokens[t];
+            const bool okt = tok >= 0 && tok < p.V;
+            const uint8_t *blk = p.embd + ((long long)(okt ? tok : 0) * nsbE + e / 256) * bb;
+            const int v = e % 256;
+            float yv;
+            if (p.embd_type == T_Q4_K) {
+                const float dd = f16_bits_to_f32((uint16_t)(blk[0] | (blk[1] << 8)));
+                const float dmin = f16_bits_to_f32((uint16_t)(blk[2] | (blk[3] << 8)));
+                const uint8_t *scb = blk + 4, *qs = blk + 16;
+                const int j = v / 32, gi = v / 64, hi = j & 1, l = v % 32;
+                int scj, mj;
+                if (j < 4) {
+                    scj = scb[j] & 63;
+                    mj = scb[j + 4] & 63;
+                } else {
+                    scj = (scb[j + 4] & 0xF) | ((scb[j - 4] >> 6) << 4);
+                    mj = (scb[j + 4] >> 4) | ((scb[j] >> 6) << 4);
+                }
+                const int q = hi ? (qs[32 * gi + l] >> 4) : (qs[32 * gi + l] & 0xF);
+                yv = __fsub_rn(__fmul_rn(__fmul_rn(dd, (float)scj), (float)q), __fmul_rn(dmin, (float)mj));
+            } else {
+                const float dd = f16_bits_to_f32((uint16_t)(blk[208] | (blk[209] << 8)));
+                const int8_t *scb = reinterpret_cast<const int8_t *>(blk + 192);
+                const int n = v / 128, r = v % 128, quad = r / 32, l = r % 32;
+                const int lo = quad == 0 ? (blk[64 * n + l] & 0xF)
+                                         : quad == 1 ? (blk[64 * n + 32 + l] & 0xF)
+                                                     : quad == 2 ? (blk[64 * n + l] >> 4) : (blk[64 * n + 32 + l] >> 4);
+                const int hi2 = (blk[128 + 32 * n + l] >> (2 * quad)) & 3;
+                yv = __fmul_rn(__fmul_rn(dd, (float)scb[v / 16]), (float)((lo | (hi2 << 4)) - 32));
+            }
+            yv = okt ? yv : 0.0f;
+            x0[i] = yv;
+            if (blockIdx.x == 0) p.x[i] = yv;
+            if (!okt && e == 0) atomicOr(p.err, ERR_BAD_INDEX);
+        }
+        if (blockIdx.x == 0 && tid < T) p.pos_of[tid] = sm.pos[tid];
+        __syncthreads();
+    }
+
+    for (int il = 0; il < p.n_layer; il++) {
+        const LayerDev &L = p.layers[il];
+        // ================= QKV
+        const SegList sq = make_segs(&L.q, 0, &L.k, QW, &L.v, QW + KW);
+        {
+            const float *xs = il == 0 ? x0 : p.x;
+            stage_activations<STEP_WARPS>(xs, E, nullptr, L.attn_norm, p.eps, E, T, sm.act, sm.normS);
+            __syncthreads();
+            POINT(il, 0);
+            if (il == 0) gemv_preissue(ring, sq, warp, lane);  // the region held the embedding rows
+            CYC_RESET();
+            if (!gemv_run(ring, sq, sm.act, nsbE, T, p.qkv, QW + 2 * KW, nullptr, 0, nullptr, p.err, warp, lane,
+                          p.trace ? cycv : nullptr))
+                return;
+            CYC_WRITE(il, 7, 0);
+            CYC_WRITE(il, 8, 1);
+        }
+        // the first attention item's K/V pages, requested before the barrier
+        long long it0 = blockIdx.x;
+        const long long n_items = attn_items(p, sm.pos);
+        __syncthreads();
+        if (tid == 0 && it0 < n_items) {
+            AttnItem it;
+            attn_item(p, sm.pos, it0, it);
+            attn_issue(p, &tmap, sm, it, il);
+        }
+        if (!grid_sync(p.bar, p.err, TR(il, 0))) return;
+        // ================= ATTN
+        for (long long i = it0; i < n_items; i += gridDim.x) {
+            AttnItem it;
+            attn_item(p, sm.pos, i, it);
+            if (i != it0) {
+                if (tid == 0) attn_issue(p, &tmap, sm, it, il);
+            }
+            if (!attn_run<G>(p, L, sm, it, il, apar)) return;
+            if (i == it0) POINT(il, 1);
+        }
+        // attn_output tiles are static: request this CTA's first ones now
+        const SegList so = make_segs(&L.o, 0, nullptr, 0, nullptr, 0);
+        __syncthreads();
+        gemv_preissue(ring, so, warp, lane);
+        if (!grid_sync(p.bar, p.err, TR(il, 1))) return;
+        // ================= COMBINE (tokens whose context spans several chunks)
+        {
+            int multi = 0;
+            for (int t = 0; t < T; t++) multi += (sm.pos[t] + 1 > ATTN_CHUNK);
+            if (multi) {
+                const long long n_ci = (long long)T * p.H;
+                for (long long ci = blockIdx.x; ci < n_ci; ci += gridDim.x) {
+                    const int t = (int)(ci / p.H), hd = (int)(ci % p.H);
+                    const int nc = (sm.pos[t] + 1 + ATTN_CHUNK - 1) / ATTN_CHUNK;
+                    if (nc == 1) continue;
+                    const int g = hd / G, h = hd % G;
+                    const float *part =
+                        p.part + (((long long)t * p.HK + g) * p.max_chunks) * G * PART_ROW + (long long)h * PART_ROW;
+                    const long long cstride = (long long)G * PART_ROW;
+                    float *cm = sm.cbuf, *cl = cm + nc, *cf = cl + nc;
+                    for (int cc = tid; cc < nc; cc += STEP_THREADS) {
+                        cm[cc] = __ldcg(part + cc * cstride + 128);
+                        cl[cc] = __ldcg(part + cc * cstride + 129);
+                    }
+                    __syncthreads();
+                    if (warp == 0) {
+                        float m = -__int_as_float(0x7f800000);
+                        for (int cc = lane; cc < nc; cc += 32) m = fmaxf(m, cm[cc]);
+                        m = warp_max(m);
+                        if (lane == 0) sm.misc[0] = m;
+                    }
+                    __syncthreads();
+                    for (int cc = tid; cc < nc; cc += STEP_THREADS) cf[cc] = bt_exp(__fsub_rn(cm[cc], sm.misc[0]));
+                    __syncthreads();
+                    if (tid == 0) {
+                        float Lh = 0.0f;
+                        for (int cc = 0; cc < nc; cc++) Lh = fmaf(cl[cc], cf[cc], Lh);
+                        sm.misc[1] = Lh;
+                    }
+                    __syncthreads();
+                    if (tid < 128) {
+                        float O = 0.0f;
+                        const float *pa = part + tid;
+                        int cc = 0;
+                        for (; cc + 16 <= nc; cc += 16) {
+                            float a[16];
+#pragma unroll
+                            for (int kk = 0; kk < 16; kk++) a[kk] = __ldcg(pa + (long long)(cc + kk) * cstride);
+#pragma unroll
+                            for (int kk = 0; kk < 16; kk++) O = fmaf(a[kk], cf[cc + kk], O);
+                        }
+                        for (; cc < nc; cc++) O = fmaf(__ldcg(pa + (long long)cc * cstride), cf[cc], O);
+                        p.att[(long long)t * QW + hd * 128 + tid] = __fdiv_rn(O, sm.misc[1]);
+                    }
+                    __syncthreads();
+                }
+                if (!grid_sync(p.bar, p.err, TR(il, 2))) return;
+            }
+        }
+        // ================= O: ffn_in = x + W_o * att
+        stage_activations<STEP_WARPS>(p.att, QW, nullptr, nullptr, 0.0f, QW, T, sm.act, nullptr);
+        __syncthreads();
+        POINT(il, 2);
+        if (!gemv_run(ring, so, sm.act, nsbQ, T, p.ffn_in, E, p.x, E, nullptr, p.err, warp, lane)) return;
+        if (!grid_sync(p.bar, p.err, TR(il, 3))) return;
+        // ================= ROUTER: ffn RMSNorm (staged for the experts too) and router rows
+        stage_activations<STEP_WARPS>(p.ffn_in, E, nullptr, L.ffn_norm, p.eps, E, T, sm.act, sm.normS);
+        __syncthreads();
+        POINT(il, 3);
+        {
+            // router row r is computed by warp (r / gridDim.x) of CTA r % gridDim.x
+            for (int r = blockIdx.x + warp * gridDim.x; r < p.NE; r += STEP_WARPS * gridDim.x) {
+                const float *wr = L.gate_inp + (long long)r * E;
+                for (int t = 0; t < T; t++) {
+                    const float *xt = p.ffn_in + (long long)t * E;
+                    const float s = sm.normS[t];
+                    float acc = 0.0f;
+                    int i = lane;
+                    for (; i + 32 * 15 < E; i += 32 * 16) {
+                        float wv[16], yv[16];
+#pragma unroll
+                        for (int kk = 0; kk < 16; kk++) {
+                            wv[kk] = __ldg(wr + i + 32 * kk);
+                            yv[kk] = __fmul_rn(__fmul_rn(xt[i + 32 * kk], s), L.ffn_norm[i + 32 * kk]);
+                        }
+#pragma unroll
+                        for (int kk = 0; kk < 16; kk++) acc = fmaf(wv[kk], yv[kk], acc);
+                    }
+                    for (; i < E; i += 32) acc = fmaf(__ldg(wr + i), __fmul_rn(__fmul_rn(xt[i], s), L.ffn_norm[i]), acc);
+                    acc = butterfly_sum(acc);
+                    if (lane == 0) p.rlog[(long long)t * p.NE + r] = acc;
+                }
+            }
+        }
+        if (!grid_sync(p.bar, p.err, TR(il, 4))) return;
+        // ================= GATEUP: soft_max + route() in every CTA, then the experts
+        if (warp < T) {  // warp t routes token t (C5, C7; stable descending by total_cmp)
+            const int t = warp;
+            float *prob = sm.cbuf + t * 512;  // NE <= 512
+            const float *lg = p.rlog + (long long)t * p.NE;
+            float m = -__int_as_float(0x7f800000);
+            for (int i = lane; i < p.NE; i += 32) {
+                const float v = __ldcg(lg + i);
+                prob[i] = v;
+                m = fmaxf(m, v);
+            }
+            m = warp_max(m);
+            float acc = 0.0f;
+            for (int i = lane; i < p.NE; i += 32) {
+                const float e = bt_exp(__fsub_rn(prob[i], m));
+                prob[i] = e;
+                acc = __fadd_rn(acc, e);
+            }
+            acc = butterfly_sum(acc);
+            const float inv = __fdiv_rn(1.0f, acc);
+            for (int i = lane; i < p.NE; i += 32) prob[i] = __fmul_rn(prob[i], inv);
+            __syncwarp();
+            for (int i = lane; i < p.NE; i += 32) {
+                const int ki = total_key(prob[i]);
+                int rank = 0;
+                for (int jj = 0; jj < p.NE; jj++) {
+                    const int kj = total_key(prob[jj]);
+                    rank += (kj > ki) || (kj == ki && jj < i);
+                }
+                if (rank < K) sm.sel_ids[t * MAX_K + rank] = i;  // temporarily by rank
+            }
+            __syncwarp();
+            if (lane == 0) {
+                float total = 0.0f;
+                int ids[MAX_K];
+                float ws[MAX_K];
+                for (int q = 0; q < K; q++) {
+                    ids[q] = sm.sel_ids[t * MAX_K + q];
+                    ws[q] = prob[ids[q]];
+                    total = __fadd_rn(total, ws[q]);
+                }
+                for (int q = 0; q < K; q++) {
+                    ws[q] = total > 0.0f ? __fdiv_rn(ws[q], total) : ws[q];
+                    if (blockIdx.x == 0) {
+                        p.dbg_ids[((long long)il * p.TB + t) * K + q] = ids[q];
+                        p.dbg_w[((long long)il * p.TB + t) * K + q] = ws[q];
+                    }
+                }
+                for (int a = 1; a < K; a++)
+                    for (int b = a; b > 0 && ids[b - 1] > ids[b]; b--) {
+                        const int ti = ids[b];
+                        ids[b] = ids[b - 1];
+                        ids[b - 1] = ti;
+                        const float tw = ws[b];
+                        ws[b] = ws[b - 1];
+                        ws[b - 1] = tw;
+                    }
+                for (int q = 0; q < K; q++) {
+                    sm.sel_ids[t * MAX_K + q] = ids[q];
+                    sm.sel_w[t * MAX_K + q] = ws[q];
+                }
+            }
+        }
+        __syncthreads();
+        POINT(il, 4);
+        {
+            const long long total = (long long)T * K * L.gate.n_tiles;
+            long long u0, u1;
+            cta_range(total, u0, u1);
+            const int n = warp_units(u0, u1, warp);
+            ring.configure(L.gate.tile_bytes + L.up.tile_bytes);
+            const int nsb = L.gate.nsb;
+            CYC_RESET();
+            long long gcw = 0, gc0 = clock64();
+            for (int j = 0; j < n; j++) {
+                while (ring.issued < n && ring.can_issue()) gateup_issue(ring, L, sm, K, u0, warp, lane);
+                const long long w0 = clock64();
+                if (!ring.wait(j, p.err)) return;
+                gcw += clock64() - w0;
+                const long long u = u0 + warp + (long long)j * STEP_WARPS;
+                const int tile = (int)(u % L.gate.n_tiles);
+                const long long tk = u / L.gate.n_tiles;
+                const int t = (int)(tk / K);
+                const uint8_t *gt = ring.slot_ptr(j), *ut = gt + L.gate.tile_bytes;
+                const bool active = lane < L.gate.S;
+                const int rit = active ? lane / nsb : 0, b = active ? lane % nsb : 0;
+                const int row = tile * L.gate.rpt + rit;
+                float rowv[2];
+#pragma unroll 1
+                for (int which = 0; which < 2; which++) {
+                    const uint8_t *tl = which ? ut : gt;
+                    const int ty = which ? L.up.type : L.gate.type;
+                    float v = 0.0f;
+                    if (active) {
+                        const ActBlock &ab = sm.act[t * nsbE + b];
+                        v = ty == T_Q4_K ? q4k_slot_dot(tl, L.gate.S, lane, ab) : q6k_slot_dot(tl, L.gate.S, lane, ab);
+                    }
+                    float rr = 0.0f;
+                    for (int b2 = 0; b2 < nsb; b2++) {
+                        const int srcl = rit * nsb + b2;
+                        rr = __fadd_rn(rr, __shfl_sync(FULL, v, srcl < 32 ? srcl : 31));
+                    }
+                    rowv[which] = rr;
+                }
+                if (active && b == 0 && row < F) p.act[tk * F + row] = __fmul_rn(bt_silu(rowv[0]), rowv[1]);
+                __syncwarp();
+                ring.done++;
+            }
+            if (p.trace && lane == 0) {
+                atomicMax(cycv + 4, (unsigned long long)gcw);
+                atomicMax(cycv + 5, (unsigned long long)(clock64() - gc0 - gcw));
+            }
+            CYC_WRITE(il, 11, 4);
+            CYC_WRITE(il, 12, 5);
+            POINT(il, 5);
+            // the down rows of this CTA: request the first ones before the barrier
+            const long long dtotal = (long long)T * E;
+            long long d0, d1;
+            cta_range(dtotal, d0, d1);
+            const int dn = warp_units(d0, d1, warp);
+            ring.configure(K * L.down.tile_bytes);
+            while (ring.issued < dn && ring.can_issue()) down_issue(ring, L, sm, K, E, d0, warp, lane);
+        }
+        if (!grid_sync(p.bar, p.err, TR(il, 5))) return;
+        // ================= DOWN: the experts' down rows, their sum in the reference's order, residual
+        stage_activations<STEP_WARPS>(p.act, F, nullptr, nullptr, 0.0f, F, T * K, sm.act, nullptr);
+        __syncthreads();
+        POINT(il, 6);
+        {
+            const long long total = (long long)T * E;
+            long long u0, u1;
+            cta_range(total, u0, u1);
+            const int n = warp_units(u0, u1, warp);
+            const int nsb = nsbF, epp = 32 / nsb;
+            float *wv = sm.cbuf + STEP_MAX_T * 512 + warp * MAX_K;  // this warp's expert row values
+            CYC_RESET();
+            long long dcw = 0, dc0 = clock64();
+            for (int j = 0; j < n; j++) {
+                while (ring.issued < n && ring.can_issue()) down_issue(ring, L, sm, K, E, u0, warp, lane);
+                const long long w0 = clock64();
+                if (!ring.wait(j, p.err)) return;
+                dcw += clock64() - w0;
+                const long long u = u0 + warp + (long long)j * STEP_WARPS;
+                const int row = (int)(u % E), t = (int)(u / E);
+                const uint8_t *base = ring.slot_ptr(j);
+                const int kk = lane / nsb, b = lane % nsb;
+                for (int k0 = 0; k0 < K; k0 += epp) {
+                    const int k = k0 + kk;
+                    const bool valid = kk < epp && k < K;
+                    float v = 0.0f;
+                    if (valid) {
+                        const ActBlock &ab = sm.act[(t * K + k) * nsb + b];
+                        const uint8_t *tile = base + k * L.down.tile_bytes;
+                        v = L.down.type == T_Q4_K ? q4k_slot_dot(tile, nsb, b, ab) : q6k_slot_dot(tile, nsb, b, ab);
+                    }
+                    float acc = 0.0f;
+                    for (int b2 = 0; b2 < nsb; b2++) {
+                        const int srcl = kk * nsb + b2;
+                        acc = __fadd_rn(acc, __shfl_sync(FULL, v, srcl < 32 ? srcl : 31));
+                    }
+                    if (valid && b == 0) wv[k] = acc;
+                }
+                __syncwarp();
+                if (lane == 0) {
+                    // expert_ffn_single order: chunks of ceil(K/workers) summed by ggml_add, partials
+                    // added to a zero vector (stream.rs:1232-1284)
+                    const float *w = sm.sel_w + t * MAX_K;
+                    int workers = p.workers < K ? p.workers : K;
+                    if (workers < 1) workers = 1;
+                    const int chunk = (K + workers - 1) / workers;
+                    float sum = 0.0f;
+                    for (int s0 = 0; s0 < K; s0 += chunk) {
+                        float tot = __fmul_rn(wv[s0], w[s0]);
+                        for (int q = s0 + 1; q < K && q < s0 + chunk; q++) tot = __fadd_rn(tot, __fmul_rn(wv[q], w[q]));
+                        sum = workers <= 1 ? tot : __fadd_rn(sum, tot);
+                    }
+                    p.x[(long long)t * E + row] = __fadd_rn(p.ffn_in[(long long)t * E + row], sum);
+                }
+                __syncwarp();
+                ring.done++;
+            }
+            if (p.trace && lane == 0) {
+                atomicMax(cycv + 2, (unsigned long long)dcw);
+                atomicMax(cycv + 3, (unsigned long long)(clock64() - dc0 - dcw));
+            }
+            CYC_WRITE(il, 9, 2);
+            CYC_WRITE(il, 10, 3);
+        }
+        // the next layer's q/k/v tiles (or the output head's) are static: request them now
+        if (il + 1 < p.n_layer) {
+            const LayerDev &Ln = p.layers[il + 1];
+            const SegList sqn = make_segs(&Ln.q, 0, &Ln.k, QW, &Ln.v, QW + KW);
+            gemv_preissue(ring, sqn, warp, lane);
+        } else {
+            const SegList sout = make_segs(&p.out, 0, nullptr, 0, nullptr, 0);
+            gemv_preissue(ring, sout, warp, lane);
+        }
+        if (!grid_sync(p.bar, p.err, TR(il, 6))) return;
+    }
+    // ================= output head with the fused argmax
+    {
+        const SegList sout = make_segs(&p.out, 0, nullptr, 0, nullptr, 0);
+        stage_activations<STEP_WARPS>(p.x, E, nullptr, p.out_norm, p.eps, E, T, sm.act, sm.normS);
+        __syncthreads();
+        if (!gemv_run(ring, sout, sm.act, nsbE, T, p.logits, p.V, nullptr, 0, p.amax, p.err, warp, lane)) return;
+    }
+    if (!grid_sync(p.bar, p.err, TR(p.n_layer, 0))) return;
+    // ================= step end: argmax out, lengths advance, greedy feed-back
+    if (blockIdx.x == 0 && tid < T) {
+        const int t = tid;
+        const unsigned long long packed = p.amax[t];
+        p.amax[t] = 0ull;
+        const int bi = (int)(packed & 0xffffffffull);
+        p.next_token[t] = bi;
+        if (p.tokens_buf) p.tokens_buf[t] = bi;
+        if (p.gen_out) {
+            const int k = p.gen_count[t]++;
+            p.gen_out[(long long)k * p.n_out + t] = bi;
+        }
+        p.dev_len[p.seq_of[t]] += 1;
+    }
+}
+
+size_t step_smem_bytes(int max_chunks) {
+    (void)max_chunks;
+    return 1024 + 1024 + STEP_REGION_BYTES + STEP_ACT_BYTES + (size_t)STEP_MAX_T * MAX_K * 8 + STEP_CBUF_BYTES;
+}
+
+cudaError_t init_step_kernel_attributes() {
+    int dev = 0, optin = 0;
+    cudaError_t e;
+    if ((e = cudaGetDevice(&dev))) return e;
+    if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
+    const void *kerns[] = {(const void *)decode_step_kernel<2>, (const void *)decode_step_kernel<4>,
+                           (const void *)decode_step_kernel<6>, (const void *)decode_step_kernel<8>};
+    for (const void *k : kerns) {
+        cudaFuncAttributes fa;
+        if ((e = cudaFuncGetAttributes(&fa, k))) return e;
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes)))
+            return e;
+    }
+    return cudaSuccess;
+}
+
+template <int G>
+static cudaError_t launch_step_g(const StepArgs &a, const CUtensorMap &tmap, int grid, cudaStream_t st) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(STEP_THREADS);
+    cfg.dynamicSmemBytes = step_smem_bytes(a.max_chunks);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeCooperative;
+    attr[0].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, decode_step_kernel<G>, a, tmap);
+}
+
+cudaError_t launch_decode_step(const StepArgs &a, const CUtensorMap &tmap, int grid, cudaStream_t st) {
+    switch (a.G) {
+    case 2: return launch_step_g<2>(a, tmap, grid, st);
+    case 4: return launch_step_g<4>(a, tmap, grid, st);
+    case 6: return launch_step_g<6>(a, tmap, grid, st);
+    case 8: return launch_step_g<8>(a, tmap, grid, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace bt

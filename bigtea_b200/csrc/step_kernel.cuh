@@ -1,0 +1,64 @@
+// step_kernel.cuh -- parameters of the persistent decode-step kernel (step_kernel.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace bt {
+
+constexpr int STEP_MAX_T = 4;                    // sequences one persistent step carries
+constexpr int STEP_REGION_BYTES = 150 * 1024;    // rings / attention tiles
+constexpr int STEP_ACT_BYTES = 32 * 1024;        // Q8_K activation blocks
+constexpr int STEP_CBUF_BYTES = 16 * 1024;       // router probabilities, combine scratch, expert values
+
+// A quantised matrix in the tiled layout, as the device reads it.
+struct QMatDev {
+    const uint8_t *w;
+    int type, nsb, rpt, S, tile_bytes, rows, n_tiles;
+    long long mat_bytes;  // one expert's matrix
+};
+
+struct LayerDev {
+    const float *attn_norm, *q_norm, *k_norm, *ffn_norm, *gate_inp;
+    QMatDev q, k, v, o, gate, up, down;
+};
+
+struct StepArgs {
+    const LayerDev *layers;
+    int n_layer;
+    QMatDev out;
+    const float *out_norm;
+    const uint8_t *embd;
+    int embd_type;
+    int E, H, HK, D, G, NE, K, F, V, workers, n_rot;
+    float eps, scale;
+    const float *rope;
+    int T;
+    const int *tokens, *seq_of;
+    int *pos_of, *dev_len;
+    __half *kv;
+    const int *block_table;
+    int max_blocks, n_blocks, max_chunks;
+    float *x, *ffn_in, *qkv, *att, *part, *rlog, *act;
+    int *dbg_ids;
+    float *dbg_w;
+    int TB;
+    float *logits;
+    unsigned long long *amax;
+    int *next_token, *tokens_buf, *gen_out, *gen_count;
+    int n_out;
+    unsigned *bar;  // [2] grid barrier: arrivals, generation
+    int *err;
+    // optional timeline: per barrier, every CTA's arrival time and CTA 0's departure time
+    // (%globaltimer ns), rows of gridDim.x + 1 at trace[(layer * STEP_PHASES + phase) * (grid + 1)]
+    unsigned long long *trace;
+};
+
+constexpr int STEP_PHASES = 24;  // timeline slots per layer: 8 barriers, then 16 points inside phases
+
+size_t step_smem_bytes(int max_chunks);
+cudaError_t init_step_kernel_attributes();
+cudaError_t launch_decode_step(const StepArgs &a, const CUtensorMap &tmap, int grid, cudaStream_t st);
+
+}  // namespace bt

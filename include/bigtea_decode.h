@@ -144,7 +144,9 @@ typedef struct {
 int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const uint32_t *first_tokens,
                       uint32_t n_seqs, uint32_t n_steps, bt_kernel_time *out, uint32_t max_out, uint32_t *n_out);
 /* Engine switches: "pdl" (programmatic dependent launch between the step's kernels, default 1),
- * "prefetch" (L2 bulk prefetch of the next kernels' weights and KV pages, default 0). */
+ * "prefetch" (L2 bulk prefetch of the next kernels' weights and KV pages, default 0),
+ * "persistent" (run single-token steps of up to 4 sequences as one cooperative kernel that
+ * holds every SM for the whole step, default 1; 0 = one kernel per phase). */
 int bt_set_option(bt_engine *e, const char *name, int value);
 
 /* ---- parity hooks: each runs one device kernel on host buffers ---- */

@@ -257,3 +257,29 @@ def test_cfg0_prefill_128_then_64_greedy_steps():
         compare_kv(cache, model, cfg)
     finally:
         e.close()
+
+
+# ------------------------------------------------------------------ the persistent step against the per-phase kernels
+def test_persistent_and_per_phase_steps_agree(tiny_cfg, tiny_weights):
+    """Single-token steps run as one cooperative kernel by default; the per-phase kernels
+    are the other implementation of the same contract. Both must equal the oracle."""
+    cfg = tiny_cfg
+    prompt = np.random.default_rng(31).integers(0, cfg.n_vocab, 300)  # three attention chunks
+    runs = {}
+    for persistent in (1, 0):
+        e = bt.Engine(cfg, tiny_weights)
+        e.set_option("persistent", persistent)
+        cache = bt.KvCache(e, max_positions=512, max_seqs=3)
+        runner = bt.StreamingRunner(e)
+        runner.forward_batch(cache, [0, 2], [prompt, prompt[:50]], [0, 0])
+        toks = runner.generate_greedy(cache, [7, 9], 5, seqs=[0, 2])
+        lg = runner.forward_batch(cache, [0, 2], [[11], [12]], [305, 55])
+        runs[persistent] = (toks, lg, [cache.layer_bytes(il, 0) for il in range(cfg.n_layer)])
+        e.close()
+    assert np.array_equal(runs[0][0], runs[1][0])
+    assert np.array_equal(bits(runs[0][1]), bits(runs[1][1]))
+    for a, b in zip(runs[0][2], runs[1][2]):
+        assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
+    model = orc.Model(cfg, tiny_weights)
+    model.forward(prompt, 0)
+    assert list(runs[1][0][:, 0]) == model.greedy(7, 5)
