@@ -1001,6 +1001,15 @@ static bool step_eligible(const bt_engine *e, const bt_kv *kv, const StepPlan &p
     const int max_chunks = (int)((kv->max_positions + ATTN_CHUNK - 1) / ATTN_CHUNK);
     if (3 * max_chunks * 4 > STEP_CBUF_BYTES || d.n_expert > 512) return false;
     if ((long long)d.n_expert_used * e->L[0].down.g.tile_bytes > STEP_REGION_BYTES / 8) return false;
+    // router: rows of a CTA plus the normalised rows in the region, probabilities and keys in cbuf
+    if (d.n_expert % 4 != 0 || (int)d.n_expert > STEP_ROUTER_ROWS * e->n_sm) return false;
+    if ((size_t)(STEP_ROUTER_ROWS + p.T) * d.n_embd * 4 > (size_t)STEP_REGION_BYTES) return false;
+    if ((size_t)d.n_embd * 4 > (size_t)STEP_CBUF_BYTES || (size_t)2 * p.T * d.n_expert * 4 > (size_t)STEP_CBUF_BYTES)
+        return false;
+    // residual rows one CTA prefetches: the down rows and the attn_output tiles' rows
+    if ((long long)p.T * d.n_embd / e->n_sm + 1 > STEP_RES) return false;
+    const long long o_tiles = e->L[0].o.g.n_tiles;
+    if ((long long)p.T * ((o_tiles + e->n_sm - 1) / e->n_sm + 1) * e->L[0].o.g.rpt > STEP_RES) return false;
     return true;
 }
 
@@ -1544,10 +1553,11 @@ extern "C" int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_id
         // SM clock the device reports
         int clk_khz = 0;
         cudaDeviceGetAttribute(&clk_khz, cudaDevAttrClockRate, e->device);
-        const char *cnames[6] = {"cyc_qkv_wait", "cyc_qkv_compute", "cyc_down_wait", "cyc_down_compute",
-                                 "cyc_gateup_wait", "cyc_gateup_compute"};
-        for (int l = 0; l < L; l++)
-            for (int k = 7; k <= 12; k++) {
+        const char *cnames[8] = {"cyc_qkv_wait",    "cyc_qkv_compute",    "cyc_down_wait", "cyc_down_compute",
+                                 "cyc_gateup_wait", "cyc_gateup_compute", "cyc_head_wait", "cyc_head_compute"};
+        for (int l = 0; l <= L; l++)
+            for (int k = 7; k <= 14; k++) {
+                if ((l == L) != (k >= 13)) continue;  // the head's counters sit in the row after the layers
                 const unsigned long long *row = tr.data() + ((size_t)l * STEP_PHASES + 8 + k) * (grid + 1);
                 unsigned long long mx = 0;
                 for (int c = 0; c < grid; c++) mx = row[c] > mx ? row[c] : mx;
@@ -1573,6 +1583,21 @@ extern "C" int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_id
                 }
                 if (!start || mx < start) continue;
                 KernelTimer &w = e->timers[pnames[k]];
+                w.launches++;
+                w.ms += (double)(mx - start) * 1e-6;
+            }
+        }
+        // points inside a CTA's first attention item, from the departure of the barrier before it
+        const char *anames[6] = {"pta_q_staged", "pta_tiles_landed", "pta_scores_max", "pta_softmax", "pta_pv",
+                                 "pta_done"};
+        for (int l = 0; l < L; l++) {
+            const unsigned long long start = tr[((size_t)l * STEP_PHASES + 0) * (grid + 1) + grid];
+            for (int k = 0; k < 6; k++) {
+                const unsigned long long *row = tr.data() + ((size_t)l * STEP_PHASES + 8 + 16 + k) * (grid + 1);
+                unsigned long long mx = 0;
+                for (int c = 0; c < grid; c++) mx = row[c] > mx ? row[c] : mx;
+                if (!start || mx < start) continue;
+                KernelTimer &w = e->timers[anames[k]];
                 w.launches++;
                 w.ms += (double)(mx - start) * 1e-6;
             }

@@ -261,50 +261,49 @@ inline uint64_t name_id(const char *s) {
 // ------------------------------------------------------------------ device-side decode
 #ifdef __CUDACC__
 
-// Q8_K activation block as staged in shared memory: 256 quants, scale, and the sums of the
-// 8 sub-blocks of 32 (what the Q4_K min term needs). 304 bytes = 19 x 16, so consecutive
-// blocks start in different 16-byte bank groups.
+// Q8_K activation block as staged in shared memory: 256 quants, scale, the sums of the 8
+// sub-blocks of 32 (the Q4_K min term) and of the 16 sub-blocks of 16 (the Q6_K offset term).
+// 336 bytes = 21 x 16, so 8 consecutive blocks start in 8 different 16-byte bank groups.
 struct __align__(16) ActBlock {
     int8_t qs[256];
     float d;
     int pad[3];
     int bs32[8];
+    int16_t bs16[16];
 };
-static_assert(sizeof(ActBlock) == 304, "ActBlock layout");
+static_assert(sizeof(ActBlock) == 336, "ActBlock layout");
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
+// unsigned bytes of a times signed bytes of b, accumulated into c
+__device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
+    int d;
+    asm("dp4a.u32.s32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+    return d;
+}
+__device__ __forceinline__ int byte_u(uint32_t w, int k) { return (int)((w >> (8 * k)) & 0xffu); }
+__device__ __forceinline__ int byte_s(uint32_t w, int k) { return (int)(int8_t)((w >> (8 * k)) & 0xffu); }
+__device__ __forceinline__ int comp(const int4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
 
-// C4 for one Q4_K superblock (slot s of a tile in shared memory) against one activation block.
-// The four 64-value groups run as a rolled loop: the same instructions serve every group, which
-// keeps the kernels' code small (each warp runs it only a few times per launch, from a cold
-// instruction cache).
+// C4 for one Q4_K superblock (slot s of a tile in shared memory) against one activation block:
+// sumi = sum_j sc_j * (q . a over sub-block j), summ = sum_j m_j * bs32_j (integers, so the
+// grouping below gives the same values as any other order), then
+// (float)sumi * (d * d_a) - (float)summ * (dmin * d_a). High nibbles enter the dot unshifted
+// (unsigned x signed dp4a) and the exact multiple of 16 is shifted out afterwards.
 __device__ __forceinline__ float q4k_slot_dot(const uint8_t *tile, int S, int s, const ActBlock &a) {
     const uint4 *base = reinterpret_cast<const uint4 *>(tile) + s;
     const uint4 h = base[0];
     const float dw = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffff)));
     const float dminw = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
-    const uint32_t s03 = h.y, s47 = h.z, s811 = h.w;  // the 12 packed scale bytes
-    const uint4 *aq = reinterpret_cast<const uint4 *>(a.qs);
-    int sumi = 0, summ = 0;
-#pragma unroll 1
+    const uint32_t s03 = h.y, s47 = h.z, s811 = h.w;  // the 12 packed scale bytes (get_scale_min_k4)
+    const uint32_t sc_lo = s03 & 0x3F3F3F3Fu, m_lo = s47 & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (s811 & 0x0F0F0F0Fu) | ((s03 >> 2) & 0x30303030u);
+    const uint32_t m_hi = ((s811 >> 4) & 0x0F0F0F0Fu) | ((s47 >> 2) & 0x30303030u);
+    const int4 *aq = reinterpret_cast<const int4 *>(a.qs);
+    int dot[8];
+#pragma unroll
     for (int g = 0; g < 4; g++) {
-        // sub-blocks 2g and 2g+1: 6-bit scale and min (get_scale_min_k4)
-        int sc0, m0, sc1, m1;
-        if (g < 2) {
-            sc0 = (s03 >> (16 * g)) & 63;
-            m0 = (s47 >> (16 * g)) & 63;
-            sc1 = (s03 >> (16 * g + 8)) & 63;
-            m1 = (s47 >> (16 * g + 8)) & 63;
-        } else {
-            const int j0 = 2 * g - 4;  // byte index within s811 for sub-block 2g
-            const int b0 = (s811 >> (8 * j0)) & 0xff, b1 = (s811 >> (8 * j0 + 8)) & 0xff;
-            sc0 = (b0 & 0xF) | (((s03 >> (8 * j0 + 6)) & 3) << 4);
-            m0 = (b0 >> 4) | (((s47 >> (8 * j0 + 6)) & 3) << 4);
-            sc1 = (b1 & 0xF) | (((s03 >> (8 * j0 + 14)) & 3) << 4);
-            m1 = (b1 >> 4) | (((s47 >> (8 * j0 + 14)) & 3) << 4);
-        }
         const uint4 w0 = base[(1 + 2 * g) * S], w1 = base[(2 + 2 * g) * S];
-        const uint4 al0 = aq[4 * g + 0], al1 = aq[4 * g + 1], ah0 = aq[4 * g + 2], ah1 = aq[4 * g + 3];
+        const int4 al0 = aq[4 * g + 0], al1 = aq[4 * g + 1], ah0 = aq[4 * g + 2], ah1 = aq[4 * g + 3];
         int dlo = 0, dhi = 0;
         dlo = dp4a(w0.x & 0x0F0F0F0F, al0.x, dlo);
         dlo = dp4a(w0.y & 0x0F0F0F0F, al0.y, dlo);
@@ -314,16 +313,26 @@ __device__ __forceinline__ float q4k_slot_dot(const uint8_t *tile, int S, int s,
         dlo = dp4a(w1.y & 0x0F0F0F0F, al1.y, dlo);
         dlo = dp4a(w1.z & 0x0F0F0F0F, al1.z, dlo);
         dlo = dp4a(w1.w & 0x0F0F0F0F, al1.w, dlo);
-        dhi = dp4a((w0.x >> 4) & 0x0F0F0F0F, ah0.x, dhi);
-        dhi = dp4a((w0.y >> 4) & 0x0F0F0F0F, ah0.y, dhi);
-        dhi = dp4a((w0.z >> 4) & 0x0F0F0F0F, ah0.z, dhi);
-        dhi = dp4a((w0.w >> 4) & 0x0F0F0F0F, ah0.w, dhi);
-        dhi = dp4a((w1.x >> 4) & 0x0F0F0F0F, ah1.x, dhi);
-        dhi = dp4a((w1.y >> 4) & 0x0F0F0F0F, ah1.y, dhi);
-        dhi = dp4a((w1.z >> 4) & 0x0F0F0F0F, ah1.z, dhi);
-        dhi = dp4a((w1.w >> 4) & 0x0F0F0F0F, ah1.w, dhi);
-        sumi += sc0 * dlo + sc1 * dhi;
-        summ += m0 * a.bs32[2 * g] + m1 * a.bs32[2 * g + 1];
+        dhi = dp4a_us(w0.x & 0xF0F0F0F0u, ah0.x, dhi);
+        dhi = dp4a_us(w0.y & 0xF0F0F0F0u, ah0.y, dhi);
+        dhi = dp4a_us(w0.z & 0xF0F0F0F0u, ah0.z, dhi);
+        dhi = dp4a_us(w0.w & 0xF0F0F0F0u, ah0.w, dhi);
+        dhi = dp4a_us(w1.x & 0xF0F0F0F0u, ah1.x, dhi);
+        dhi = dp4a_us(w1.y & 0xF0F0F0F0u, ah1.y, dhi);
+        dhi = dp4a_us(w1.z & 0xF0F0F0F0u, ah1.z, dhi);
+        dhi = dp4a_us(w1.w & 0xF0F0F0F0u, ah1.w, dhi);
+        dot[2 * g] = dlo;
+        dot[2 * g + 1] = dhi >> 4;
+    }
+    const int4 b0 = *reinterpret_cast<const int4 *>(a.bs32), b1 = *reinterpret_cast<const int4 *>(a.bs32 + 4);
+    const int bs[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    int sumi = 0, summ = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int sc = j < 4 ? byte_u(sc_lo, j) : byte_u(sc_hi, j - 4);
+        const int m = j < 4 ? byte_u(m_lo, j) : byte_u(m_hi, j - 4);
+        sumi += sc * dot[j];
+        summ += m * bs[j];
     }
     const float t1 = __fmul_rn(dw, a.d);
     const float t2 = __fmul_rn(__int2float_rn(sumi), t1);
@@ -332,40 +341,55 @@ __device__ __forceinline__ float q4k_slot_dot(const uint8_t *tile, int S, int s,
     return __fsub_rn(t2, t4);
 }
 
-// C4 for one Q6_K superblock. Integer identity: sum over 16-value sub-blocks s of
-// sc[s] * dot_s equals the sum over the 4-value dp4a groups of sc[sub(group)] * dp4a(group).
+// C4 for one Q6_K superblock: sumi = sum over the 16 sub-blocks of sc * (q - 32) . a, computed
+// as sc * (u . a - 32 * bs16) with u = q + 32 in [0, 63] (unsigned x signed dp4a; integers, so
+// equal to the per-value form), then (float)sumi * (d * d_a). Value v of the superblock:
+// n = v / 128, quad = (v % 128) / 32, l = v % 32; low nibble from ql[64n + 32 * (quad & 1) + l]
+// (high nibble when quad >= 2), two high bits from qh[32n + l] >> 2 * quad; sub-block v / 16.
 __device__ __forceinline__ float q6k_slot_dot(const uint8_t *tile, int S, int s, const ActBlock &a) {
     const uint4 *base = reinterpret_cast<const uint4 *>(tile) + s;
     const uint16_t dbits = *reinterpret_cast<const uint16_t *>(tile + 13 * S * 16 + 2 * s);
     const float dw = __half2float(__ushort_as_half(dbits));
-    const uint4 scv = base[12 * S];
-    const int *aw = reinterpret_cast<const int *>(a.qs);
+    const uint4 scv = base[12 * S];  // the 16 int8 sub-block scales
+    const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+    const int4 *aq = reinterpret_cast<const int4 *>(a.qs);
+    const int4 bq0 = *reinterpret_cast<const int4 *>(a.bs16), bq1 = *reinterpret_cast<const int4 *>(a.bs16 + 8);
+    const uint32_t bsw[8] = {(uint32_t)bq0.x, (uint32_t)bq0.y, (uint32_t)bq0.z, (uint32_t)bq0.w,
+                             (uint32_t)bq1.x, (uint32_t)bq1.y, (uint32_t)bq1.z, (uint32_t)bq1.w};
     int sumi = 0;
-#pragma unroll 1
+#pragma unroll
     for (int n = 0; n < 2; n++) {
-        const uint32_t wlo = n ? scv.z : scv.x;  // int8 scales of sub-blocks 8n .. 8n+3
-        const uint32_t whi = n ? scv.w : scv.y;  // 8n+4 .. 8n+7
         const uint4 qa0 = base[(4 * n + 0) * S], qa1 = base[(4 * n + 1) * S];  // ql bytes 64n .. 64n+31
         const uint4 qb0 = base[(4 * n + 2) * S], qb1 = base[(4 * n + 3) * S];  // ql bytes 64n+32 .. 64n+63
         const uint4 hh0 = base[(8 + 2 * n) * S], hh1 = base[(9 + 2 * n) * S];  // qh bytes 32n .. 32n+31
         const uint32_t wa[8] = {qa0.x, qa0.y, qa0.z, qa0.w, qa1.x, qa1.y, qa1.z, qa1.w};
         const uint32_t wb[8] = {qb0.x, qb0.y, qb0.z, qb0.w, qb1.x, qb1.y, qb1.z, qb1.w};
         const uint32_t wh[8] = {hh0.x, hh0.y, hh0.z, hh0.w, hh1.x, hh1.y, hh1.z, hh1.w};
-        const int *an = aw + 32 * n;  // activation words of values 128n ..
 #pragma unroll
-        for (int l4 = 0; l4 < 8; l4++) {
-            const uint32_t h = wh[l4];
-            const int q1 = (int)__vsub4((wa[l4] & 0x0F0F0F0F) | ((h & 0x03030303) << 4), 0x20202020);
-            const int q2 = (int)__vsub4((wb[l4] & 0x0F0F0F0F) | (((h >> 2) & 0x03030303) << 4), 0x20202020);
-            const int q3 = (int)__vsub4(((wa[l4] >> 4) & 0x0F0F0F0F) | (((h >> 4) & 0x03030303) << 4), 0x20202020);
-            const int q4 = (int)__vsub4(((wb[l4] >> 4) & 0x0F0F0F0F) | (((h >> 6) & 0x03030303) << 4), 0x20202020);
-            const int j = l4 >> 2;  // sub-blocks 8n + j, +2, +4, +6
-            const int s1 = (int)(signed char)((j == 0 ? wlo : wlo >> 8) & 0xff);
-            const int s2 = (int)(signed char)(((j == 0 ? wlo >> 16 : wlo >> 24)) & 0xff);
-            const int s3 = (int)(signed char)((j == 0 ? whi : whi >> 8) & 0xff);
-            const int s4 = (int)(signed char)(((j == 0 ? whi >> 16 : whi >> 24)) & 0xff);
-            sumi += s1 * dp4a(q1, an[l4], 0) + s2 * dp4a(q2, an[8 + l4], 0) + s3 * dp4a(q3, an[16 + l4], 0) +
-                    s4 * dp4a(q4, an[24 + l4], 0);
+        for (int hf = 0; hf < 2; hf++) {  // l = 16 hf .. 16 hf + 15: sub-blocks 8n + 2 quad + hf
+            const int4 A0 = aq[8 * n + 0 + hf], A1 = aq[8 * n + 2 + hf], A2 = aq[8 * n + 4 + hf], A3 = aq[8 * n + 6 + hf];
+            int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int l4 = 4 * hf + i;
+                const uint32_t hq = wh[l4];
+                const uint32_t u1 = (wa[l4] & 0x0F0F0F0Fu) | ((hq << 4) & 0x30303030u);
+                const uint32_t u2 = (wb[l4] & 0x0F0F0F0Fu) | ((hq << 2) & 0x30303030u);
+                const uint32_t u3 = ((wa[l4] >> 4) & 0x0F0F0F0Fu) | (hq & 0x30303030u);
+                const uint32_t u4 = ((wb[l4] >> 4) & 0x0F0F0F0Fu) | ((hq >> 2) & 0x30303030u);
+                acc0 = dp4a_us(u1, comp(A0, i), acc0);
+                acc1 = dp4a_us(u2, comp(A1, i), acc1);
+                acc2 = dp4a_us(u3, comp(A2, i), acc2);
+                acc3 = dp4a_us(u4, comp(A3, i), acc3);
+            }
+            const int accs[4] = {acc0, acc1, acc2, acc3};
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const int sub = 8 * n + 2 * q + hf;
+                const int sc = byte_s(scw[sub >> 2], sub & 3);
+                const int bs = (int)(int16_t)((bsw[sub >> 1] >> (16 * (sub & 1))) & 0xffffu);
+                sumi += sc * (accs[q] - 32 * bs);
+            }
         }
     }
     return __fmul_rn(__int2float_rn(sumi), __fmul_rn(dw, a.d));

@@ -53,6 +53,7 @@ __device__ __forceinline__ void quantize_block_warp(const float v[8], ActBlock *
     int s16 = s8 + __shfl_xor_sync(FULL, s8, 1);
     int s32 = s16 + __shfl_xor_sync(FULL, s16, 2);
     if ((lane & 3) == 0) dst->bs32[lane >> 2] = s32;
+    if ((lane & 1) == 0) dst->bs16[lane >> 1] = (int16_t)s16;
     if (lane == 0) dst->d = d;
 }
 

@@ -7,12 +7,20 @@
 //   F32 router rows) | GATEUP (soft_max + route() in every CTA, expert gate/up GEMV, SiLU)
 //   | DOWN (expert down GEMV, the reference's expert sum, residual)
 // and finally the output head with a fused argmax and the step's bookkeeping.
-// Phases are separated by a grid barrier with a bounded wait. Weights never depend on the
-// previous phase, so each phase's first tiles are requested by 1-D TMA into the warps' rings
-// before the barrier that precedes it; the attention K/V pages of a CTA's first chunk are
-// requested the same way. The arithmetic is the contract of bt_common.cuh, operation for
-// operation the same as the per-phase kernels of kernels.cu (the tests compare both paths
-// with the CPU oracle bit for bit).
+//
+// At batch 1 a layer moves ~40 MB in a few microseconds, so the step is bound by global round
+// trips more than by bandwidth, and the kernel is organised around them:
+//  * phases are separated by a one-counter grid barrier (release-add, relaxed polls, one
+//    acquire fence; bounded);
+//  * whatever is static in a phase is requested before the barrier that precedes it: weight
+//    tiles into the warps' TMA rings, the K/V pages of a CTA's first attention item, the
+//    router rows, the norm vector of the next staging (into shared memory), and the residual
+//    rows a CTA adds (into registers, stored to shared memory after the barrier);
+//  * the layer descriptors are read into shared memory one layer ahead;
+//  * activation staging issues all its loads before the first use (one L2 round trip);
+//  * attention items double-buffer their K/V tiles.
+// The arithmetic is the contract of bt_common.cuh, operation for operation the same as the
+// per-phase kernels of kernels.cu (the tests compare both paths with the CPU oracle bit for bit).
 //
 // Reference call sites: core/arch/src/stream.rs forward_cached_inner 2106-2915 (per layer:
 // 2265-2474 q/k/v, 2545-2552 KvCache::push, 2554-2703 attention, 2723-2726 residual,
@@ -29,59 +37,67 @@ namespace bt {
 
 constexpr int STEP_THREADS = 256, STEP_WARPS = 8;
 constexpr int RING_SLOTS = 4;
-constexpr int PART_ROW = 132;  // floats per (chunk, head) partial: acc[128], m, l, pad
+constexpr int PART_ROW = 132;    // floats per (chunk, head) partial: acc[128], m, l, pad
+constexpr int ATTN_BUF = 65536;  // one attention item's K and V tiles (128 keys x 128 dims x f16 x 2)
+constexpr int LD_WORDS = sizeof(LayerDev) / 4;
+static_assert(sizeof(LayerDev) % 4 == 0 && sizeof(LayerDev) <= 384, "layer descriptor size");
+static_assert(2 * ATTN_BUF + 9216 <= STEP_REGION_BYTES, "attention tiles and scratch fit the region");
+static_assert(STEP_RES == STEP_THREADS, "one residual value per thread");
 
 // ------------------------------------------------------------------ shared memory map
 struct StepSmem {
-    uint8_t *region;     // rings (GEMV phases) or K/V tiles (attention), STEP_REGION_BYTES
+    uint8_t *region;     // rings (GEMV phases), K/V tiles (attention) or router rows, STEP_REGION_BYTES
     ActBlock *act;       // activations, STEP_ACT_BYTES
     uint64_t *ring_bar;  // [warp][RING_SLOTS]
-    uint64_t *attn_bar;
+    uint64_t *attn_bar;  // [2] one per attention tile buffer
+    uint64_t *aux_bar;   // [2] 0: router rows, 1: norm vector
     float *normS;        // [STEP_MAX_T]
     float *misc;         // 64 floats
+    int *pos;            // [STEP_MAX_T]
+    LayerDev *ldesc;     // [2] this layer's and the next layer's descriptors
+    QMatDev *outd;       // the output head's descriptor
     int *sel_ids;        // [STEP_MAX_T][MAX_K]
     float *sel_w;        // [STEP_MAX_T][MAX_K]
-    int *pos;            // [STEP_MAX_T]
-    float *cbuf;         // combine scratch: 3 * max_chunks floats
+    float *wv;           // [STEP_WARPS][MAX_K] expert row values of the down phase
+    float *cbuf;         // norm vector / router probabilities / combine scratch, STEP_CBUF_BYTES
+    float *res;          // [STEP_RES] residual values of this CTA's output rows
 };
 
 // ------------------------------------------------------------------ grid barrier
-__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
+__device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned *p) {
     unsigned v;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
-// Sense by generation: the last CTA to arrive resets the count and advances the generation.
-// The wait is bounded; a timeout sets the engine's error word, after which every CTA leaves
-// at its next barrier.
 __device__ __forceinline__ unsigned long long global_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
 
-__device__ bool grid_sync(unsigned *bar, int *err, unsigned long long *trace_row = nullptr) {
+// One monotonic arrival counter, zeroed before each launch: barrier n of a launch completes
+// when the counter reaches n * gridDim.x. Thread 0 arrives with a release-add after the CTA's
+// __syncthreads and waits with relaxed polls followed by one acquire fence. The wait is
+// bounded: a timeout sets the engine's error word, after which every CTA leaves at its next
+// barrier.
+__device__ bool grid_sync(unsigned *bar, unsigned &epoch, int *err, unsigned long long *trace_row = nullptr) {
     __syncthreads();
-    if (threadIdx.x == 0 && trace_row) trace_row[blockIdx.x] = global_ns();
+    epoch += 1;
     if (threadIdx.x == 0) {
-        const unsigned gen = ld_acquire_gpu(bar + 1);
-        __threadfence();
-        const unsigned arrived = atomicAdd(bar, 1u);
-        if (arrived == gridDim.x - 1) {
-            atomicExch(bar, 0u);
-            __threadfence();
-            atomicAdd(bar + 1, 1u);
-        } else {
+        if (trace_row) trace_row[blockIdx.x] = global_ns();
+        const unsigned target = epoch * gridDim.x;
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(bar), "r"(1u) : "memory");
+        if (ld_relaxed_gpu(bar) < target) {
             const long long t0 = clock64();
-            while (ld_acquire_gpu(bar + 1) == gen) {
+            while (ld_relaxed_gpu(bar) < target) {
                 if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
                     atomicOr(err, ERR_WAIT_TIMEOUT);
                     break;
                 }
             }
         }
-        __threadfence();
+        asm volatile("fence.acq_rel.gpu;" ::: "memory");
         if (trace_row && blockIdx.x == 0) trace_row[gridDim.x] = global_ns();
     }
     __syncthreads();
@@ -97,11 +113,16 @@ struct WarpRing {
     uint32_t par;  // next parity to wait for, one bit per slot
     int nst, slot_bytes, issued, done;
 
+    // A phase's first use of the ring: the region may hold values written by the generic proxy
+    // (attention's appended row, normalised router inputs, embedding rows), so the issuing lane
+    // orders those before its bulk copies. Within a phase a slot is only read before it is
+    // refilled, and the warp's own __syncwarp orders that.
     __device__ void configure(int sbytes) {
         slot_bytes = sbytes;
         nst = (STEP_REGION_BYTES / STEP_WARPS) / sbytes;
         nst = nst > RING_SLOTS ? RING_SLOTS : nst;
         issued = done = 0;
+        if ((threadIdx.x & 31) == 0) fence_proxy_async();
     }
     __device__ uint8_t *slot_ptr(int j) const { return base + (size_t)(j % nst) * slot_bytes; }
     __device__ uint64_t *slot_bar(int j) const { return bars + (j % nst); }
@@ -122,6 +143,114 @@ __device__ __forceinline__ void cta_range(long long total, long long &u0, long l
 }
 __device__ __forceinline__ int warp_units(long long u0, long long u1, int warp) {
     return (u1 - u0 > warp) ? (int)((u1 - u0 - warp + STEP_WARPS - 1) / STEP_WARPS) : 0;
+}
+
+// ------------------------------------------------------------------ shared code
+// The step runs each phase once per layer and the whole layer's code does not fit the
+// instruction caches, so every instruction a phase executes is fetched again from L2 in the
+// next layer. Code that several phases run is therefore kept in one non-inlined copy: the
+// K-quant slot dots, the Q8_K block quantiser, the staging and the GEMV consumer.
+__device__ __noinline__ float dot_q4k(uint32_t tile_s, int S, int s, uint32_t act_s) {
+    const uint8_t *tile = reinterpret_cast<const uint8_t *>(__cvta_shared_to_generic(tile_s));
+    const ActBlock *a = reinterpret_cast<const ActBlock *>(__cvta_shared_to_generic(act_s));
+    return q4k_slot_dot(tile, S, s, *a);
+}
+__device__ __noinline__ float dot_q6k(uint32_t tile_s, int S, int s, uint32_t act_s) {
+    const uint8_t *tile = reinterpret_cast<const uint8_t *>(__cvta_shared_to_generic(tile_s));
+    const ActBlock *a = reinterpret_cast<const ActBlock *>(__cvta_shared_to_generic(act_s));
+    return q6k_slot_dot(tile, S, s, *a);
+}
+// slot s of a tile (tile_s, S slots) against the activation block at act_s
+__device__ __forceinline__ float slot_dot(bool q4, const uint8_t *tile, int S, int s, const ActBlock *act) {
+    return q4 ? dot_q4k(smem_u32(tile), S, s, smem_u32(act)) : dot_q6k(smem_u32(tile), S, s, smem_u32(act));
+}
+
+struct F8 {
+    float v[8];
+};
+__device__ __noinline__ void quantize_block_nl(F8 x, uint32_t dst_s, int lane) {
+    quantize_block_warp(x.v, reinterpret_cast<ActBlock *>(__cvta_shared_to_generic(dst_s)), lane);
+}
+
+// ------------------------------------------------------------------ activation staging
+__device__ __forceinline__ float4 ld_f4(const float *p, bool global) {
+    return global ? __ldcg(reinterpret_cast<const float4 *>(p)) : *reinterpret_cast<const float4 *>(p);
+}
+__device__ __forceinline__ float ld_f(const float *p, bool global) { return global ? __ldcg(p) : *p; }
+
+// Stage T rows of K values (row stride xs) as Q8_K blocks (C3), in waves of STAGE_B blocks per
+// warp. Every load of the first wave is issued before the first use; with `norm` the warps t < T
+// load row t lane-strided for the C5 sum of squares (C6) in the same round trip, and the norm
+// weights come from `norm_s` (shared memory). `yout` (shared memory, [T][K], optional) receives
+// the normalised values. Rows written by other CTAs are read with L1-bypassing loads.
+constexpr int STAGE_B = 3;
+__device__ __noinline__ void step_stage(const float *x, long long xs, int K, int T, const float *norm_s, float eps,
+                                        ActBlock *act, float *normS, float *yout) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const bool gl = __isGlobal(x), norm = norm_s != nullptr;
+    const int nsb = K >> 8, nblk = T * nsb;
+    F8 v[STAGE_B];
+    auto load_wave = [&](int w0) {
+#pragma unroll
+        for (int i = 0; i < STAGE_B; i++) {
+            const int blk = w0 + warp + i * STEP_WARPS;
+            if (blk < nblk) {
+                const int t = blk / nsb, b = blk - t * nsb;
+                const float *src = x + t * xs + b * 256 + lane * 8;
+                const float4 a0 = ld_f4(src, gl), a1 = ld_f4(src + 4, gl);
+                v[i].v[0] = a0.x; v[i].v[1] = a0.y; v[i].v[2] = a0.z; v[i].v[3] = a0.w;
+                v[i].v[4] = a1.x; v[i].v[5] = a1.y; v[i].v[6] = a1.z; v[i].v[7] = a1.w;
+            }
+        }
+    };
+    load_wave(0);
+    if (norm) {
+        if (warp < T) {
+            const float *xt = x + (long long)warp * xs;
+            float acc = 0.0f;
+            int i = lane;
+            for (; i + 32 * 63 < K; i += 32 * 64) {
+                float r[64];
+#pragma unroll
+                for (int k = 0; k < 64; k++) r[k] = ld_f(xt + i + 32 * k, gl);
+#pragma unroll
+                for (int k = 0; k < 64; k++) acc = fmaf(r[k], r[k], acc);
+            }
+            for (; i < K; i += 32) {
+                const float r = ld_f(xt + i, gl);
+                acc = fmaf(r, r, acc);
+            }
+            acc = butterfly_sum(acc);
+            if (lane == 0) normS[warp] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)K), eps)));
+        }
+        __syncthreads();
+    }
+    for (int w0 = 0;;) {
+#pragma unroll
+        for (int i = 0; i < STAGE_B; i++) {
+            const int blk = w0 + warp + i * STEP_WARPS;
+            if (blk < nblk) {
+                if (norm) {
+                    const int t = blk / nsb, b = blk - t * nsb;
+                    const float s = normS[t];
+                    const float4 n0 = *reinterpret_cast<const float4 *>(norm_s + b * 256 + lane * 8);
+                    const float4 n1 = *reinterpret_cast<const float4 *>(norm_s + b * 256 + lane * 8 + 4);
+                    const float wn[8] = {n0.x, n0.y, n0.z, n0.w, n1.x, n1.y, n1.z, n1.w};
+#pragma unroll
+                    for (int k = 0; k < 8; k++) v[i].v[k] = __fmul_rn(__fmul_rn(v[i].v[k], s), wn[k]);
+                    if (yout) {
+                        float4 *d = reinterpret_cast<float4 *>(yout + t * K + b * 256 + lane * 8);
+                        d[0] = make_float4(v[i].v[0], v[i].v[1], v[i].v[2], v[i].v[3]);
+                        d[1] = make_float4(v[i].v[4], v[i].v[5], v[i].v[6], v[i].v[7]);
+                    }
+                }
+                quantize_block_nl(v[i], smem_u32(act + blk), lane);
+            }
+        }
+        w0 += STAGE_B * STEP_WARPS;
+        if (w0 >= nblk) break;
+        load_wave(w0);
+    }
 }
 
 // ------------------------------------------------------------------ GEMV phases
@@ -169,11 +298,11 @@ __device__ void gemv_issue(WarpRing &r, const SegList &s, long long u0, int warp
     const int j = r.issued;
     if (lane == 0) {
         const long long u = u0 + warp + (long long)j * STEP_WARPS;
-        const QMatDev &m = *s.m[seg_of(s, u)];
-        const uint8_t *src = m.w + (u - s.tile0[seg_of(s, u)]) * (long long)m.tile_bytes;
-        fence_proxy_async();
+        const int si = seg_of(s, u);
+        const QMatDev &m = *s.m[si];
+        const uint8_t *src = m.w + (u - s.tile0[si]) * (long long)m.tile_bytes;
         mbar_arrive_expect_tx(r.slot_bar(j), m.tile_bytes);
-        bulk_g2s(r.slot_ptr(j), src, m.tile_bytes, r.slot_bar(j));
+        bulk_g2s_hint(r.slot_ptr(j), src, m.tile_bytes, r.slot_bar(j), l2_evict_first_policy());
     }
     r.issued++;
 }
@@ -186,15 +315,29 @@ __device__ void gemv_preissue(WarpRing &r, const SegList &s, int warp, int lane)
     while (r.issued < n && r.can_issue()) gemv_issue(r, s, u0, warp, lane);
 }
 
-// Consume every unit of this warp; y[t*ys + off + row] = acc (+ res[t*rs + off + row]);
-// `amax` folds an argmax over the written rows (output head).
-__device__ bool gemv_run(WarpRing &r, const SegList &s, const ActBlock *act, int nsbK, int T, float *y, long long ys,
-                         const float *res, long long rs, unsigned long long *amax, int *err, int warp, int lane,
-                         unsigned long long *cyc = nullptr) {
+// Consume every unit of this warp; y[t*ys + off + row] = acc, plus the residual
+// res[t*res_ld + off + row - res_row0] (shared memory) when res is given; `amax` folds an argmax
+// over the written rows (output head). The segments' parameters are read once into registers.
+__device__ __forceinline__ bool gemv_run(WarpRing &r, const SegList &s, const ActBlock *act, int nsbK, int T,
+                                         float *y, long long ys, const float *res, int res_row0, int res_ld,
+                                         unsigned long long *amax, int *err, int warp, int lane,
+                                         unsigned long long *cyc = nullptr) {
     long long cw = 0, cc0 = clock64();
     long long u0, u1;
     cta_range(s.total, u0, u1);
     const int n = warp_units(u0, u1, warp);
+    int sS[3], snsb[3], srpt[3], srows[3], soff[3];
+    bool sq4[3];
+#pragma unroll
+    for (int i = 0; i < 3; i++) {
+        const QMatDev &m = *s.m[i < s.n ? i : 0];
+        sS[i] = m.S;
+        snsb[i] = m.nsb;
+        srpt[i] = m.rpt;
+        srows[i] = m.rows;
+        sq4[i] = m.type == T_Q4_K;
+        soff[i] = s.out_off[i < s.n ? i : 0];
+    }
     unsigned long long best[STEP_MAX_T];
 #pragma unroll
     for (int t = 0; t < STEP_MAX_T; t++) best[t] = 0ull;
@@ -209,28 +352,30 @@ __device__ bool gemv_run(WarpRing &r, const SegList &s, const ActBlock *act, int
         cw += clock64() - w0;
         const long long u = u0 + warp + (long long)j * STEP_WARPS;
         const int si = seg_of(s, u);
-        const QMatDev &m = *s.m[si];
+        const int mS = si == 0 ? sS[0] : si == 1 ? sS[1] : sS[2];
+        const int mnsb = si == 0 ? snsb[0] : si == 1 ? snsb[1] : snsb[2];
+        const int mrpt = si == 0 ? srpt[0] : si == 1 ? srpt[1] : srpt[2];
+        const int mrows = si == 0 ? srows[0] : si == 1 ? srows[1] : srows[2];
+        const int off = si == 0 ? soff[0] : si == 1 ? soff[1] : soff[2];
+        const bool q4 = si == 0 ? sq4[0] : si == 1 ? sq4[1] : sq4[2];
         const uint8_t *tile = r.slot_ptr(j);
         const long long tl = u - s.tile0[si];
-        const bool active = lane < m.S;
-        const int rit = active ? lane / m.nsb : 0, b = active ? lane % m.nsb : 0;
-        const long long row = tl * m.rpt + rit;
-        const bool writer = active && b == 0 && row < m.rows;
+        const bool active = lane < mS;
+        const int rit = active ? lane / mnsb : 0, b = active ? lane - rit * mnsb : 0;
+        const long long row = tl * mrpt + rit;
+        const bool writer = active && b == 0 && row < mrows;
         for (int t = 0; t < T; t++) {
             float v = 0.0f;
-            if (active) {
-                const ActBlock &ab = act[t * nsbK + b];
-                v = (m.type == T_Q4_K) ? q4k_slot_dot(tile, m.S, lane, ab) : q6k_slot_dot(tile, m.S, lane, ab);
-            }
+            if (active) v = slot_dot(q4, tile, mS, lane, act + t * nsbK + b);
             float acc = 0.0f;
-            for (int b2 = 0; b2 < m.nsb; b2++) {
-                const int srcl = rit * m.nsb + b2;
+            for (int b2 = 0; b2 < mnsb; b2++) {
+                const int srcl = rit * mnsb + b2;
                 acc = __fadd_rn(acc, __shfl_sync(FULL, v, srcl < 32 ? srcl : 31));
             }
             if (writer) {
-                const long long o = s.out_off[si] + row;
+                const long long o = off + row;
                 float val = acc;
-                if (res) val = __fadd_rn(res[t * rs + o], acc);
+                if (res) val = __fadd_rn(res[t * res_ld + (int)(o - res_row0)], acc);
                 y[t * ys + o] = val;
                 if (amax) {
                     const unsigned long long key =
@@ -275,12 +420,12 @@ __device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm,
         const int tk = (int)(u / L.gate.n_tiles);
         const int e = sm.sel_ids[(tk / K) * MAX_K + tk % K];
         uint8_t *dst = r.slot_ptr(j);
-        fence_proxy_async();
+        const uint64_t pol = l2_evict_first_policy();
         mbar_arrive_expect_tx(r.slot_bar(j), L.gate.tile_bytes + L.up.tile_bytes);
-        bulk_g2s(dst, L.gate.w + e * L.gate.mat_bytes + (long long)tile * L.gate.tile_bytes, L.gate.tile_bytes,
-                 r.slot_bar(j));
-        bulk_g2s(dst + L.gate.tile_bytes, L.up.w + e * L.up.mat_bytes + (long long)tile * L.up.tile_bytes,
-                 L.up.tile_bytes, r.slot_bar(j));
+        bulk_g2s_hint(dst, L.gate.w + e * L.gate.mat_bytes + (long long)tile * L.gate.tile_bytes, L.gate.tile_bytes,
+                      r.slot_bar(j), pol);
+        bulk_g2s_hint(dst + L.gate.tile_bytes, L.up.w + e * L.up.mat_bytes + (long long)tile * L.up.tile_bytes,
+                      L.up.tile_bytes, r.slot_bar(j), pol);
     }
     r.issued++;
 }
@@ -292,12 +437,13 @@ __device__ void down_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, i
         const long long u = u0 + warp + (long long)j * STEP_WARPS;
         const int row = (int)(u % E), t = (int)(u / E);
         uint8_t *dst = r.slot_ptr(j);
-        fence_proxy_async();
+        const uint64_t pol = l2_evict_first_policy();
         mbar_arrive_expect_tx(r.slot_bar(j), K * L.down.tile_bytes);
         for (int k = 0; k < K; k++) {
             const int e = sm.sel_ids[t * MAX_K + k];
-            bulk_g2s(dst + k * L.down.tile_bytes, L.down.w + e * L.down.mat_bytes + (long long)row * L.down.tile_bytes,
-                     L.down.tile_bytes, r.slot_bar(j));
+            bulk_g2s_hint(dst + k * L.down.tile_bytes,
+                          L.down.w + e * L.down.mat_bytes + (long long)row * L.down.tile_bytes, L.down.tile_bytes,
+                          r.slot_bar(j), pol);
         }
     }
     r.issued++;
@@ -330,41 +476,43 @@ __device__ __forceinline__ long long attn_items(const StepArgs &p, const int *po
     return n;
 }
 
-// the TMA loads of one item's K and V pages into the region (thread 0)
+// the TMA loads of one item's K and V pages into tile buffer `buf` (thread 0)
 __device__ void attn_issue(const StepArgs &p, const CUtensorMap *tmap, const StepSmem &sm, const AttnItem &it,
-                           int layer) {
+                           int layer, int buf) {
     const int seq = p.seq_of[it.t];
     const int nk = sm.pos[it.t] + 1, base = it.c * ATTN_CHUNK;
     const int cnt = nk - base < ATTN_CHUNK ? nk - base : ATTN_CHUNK;
     const int npages = (cnt + 15) / 16;
-    uint8_t *K0 = sm.region, *K1 = K0 + 16384, *V0 = K0 + 32768, *V1 = K0 + 49152;
+    uint8_t *K0 = sm.region + buf * ATTN_BUF, *K1 = K0 + 16384, *V0 = K0 + 32768, *V1 = K0 + 49152;
+    uint64_t *bar = sm.attn_bar + buf;
+    const uint64_t pol = l2_evict_first_policy();
     fence_proxy_async();
-    mbar_arrive_expect_tx(sm.attn_bar, npages * 8192);
+    mbar_arrive_expect_tx(bar, npages * 8192);
     for (int pg = 0; pg < npages; pg++) {
         const int blk = p.block_table[seq * p.max_blocks + (base >> 4) + pg];
         const int rowK = (int)(((((long long)layer * p.n_blocks + blk) * 2 + 0) * p.HK + it.g) * 16);
         const int rowV = rowK + p.HK * 16;
-        tma_load_2d(K0 + pg * 2048, tmap, 0, rowK, sm.attn_bar);
-        tma_load_2d(K1 + pg * 2048, tmap, 64, rowK, sm.attn_bar);
-        tma_load_2d(V0 + pg * 2048, tmap, 0, rowV, sm.attn_bar);
-        tma_load_2d(V1 + pg * 2048, tmap, 64, rowV, sm.attn_bar);
+        tma_load_2d_hint(K0 + pg * 2048, tmap, 0, rowK, bar, pol);
+        tma_load_2d_hint(K1 + pg * 2048, tmap, 64, rowK, bar, pol);
+        tma_load_2d_hint(V0 + pg * 2048, tmap, 0, rowV, bar, pol);
+        tma_load_2d_hint(V1 + pg * 2048, tmap, 64, rowV, bar, pol);
     }
 }
 
 // q/k head RMSNorm (C5/C6) and NeoX RoPE (C9) of one head held 4 values per lane
-// (lane l: l, l+32, l+64, l+96).
-__device__ __forceinline__ void head_norm_rope(float v[4], const float *w, const float *cs, float eps, int lane) {
+// (lane l: dims l, l+32, l+64, l+96); w holds this lane's norm weights for those dims and cs the
+// cos/sin pairs of dims l and l+32.
+__device__ __forceinline__ void head_norm_rope(float v[4], const float w[4], const float cs[4], float eps) {
     float acc = 0.0f;
 #pragma unroll
     for (int i = 0; i < 4; i++) acc = fmaf(v[i], v[i], acc);
     acc = butterfly_sum(acc);
     const float s = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, 128.0f), eps)));
 #pragma unroll
-    for (int i = 0; i < 4; i++) v[i] = __fmul_rn(__fmul_rn(v[i], s), w[lane + 32 * i]);
+    for (int i = 0; i < 4; i++) v[i] = __fmul_rn(__fmul_rn(v[i], s), w[i]);
 #pragma unroll
     for (int i = 0; i < 2; i++) {
-        const int d = lane + 32 * i;
-        const float c = cs[2 * d], sn = cs[2 * d + 1];
+        const float c = cs[2 * i], sn = cs[2 * i + 1];
         const float x0 = v[i], x1 = v[i + 2];
         const float a = __fmul_rn(x0, c), b = __fmul_rn(x1, sn), e = __fmul_rn(x0, sn), f = __fmul_rn(x1, c);
         v[i] = __fsub_rn(a, b);
@@ -386,32 +534,45 @@ __device__ __forceinline__ void lds_n(float (&dst)[N], const float *src) {
     }
 }
 
-// One attention item (C8): the K/V tiles are in flight (attn_issue); stages q, appends the new
-// key and value if this is the token's last chunk, then scores, softmax and P*V.
+// One attention item (C8): the K/V tiles are in flight into buffer `buf` (attn_issue); stages q,
+// appends the new key and value if this is the token's last chunk, then scores, softmax and P*V.
 template <int G>
 __device__ bool attn_run(const StepArgs &p, const LayerDev &L, const StepSmem &sm, const AttnItem &it, int layer,
-                         uint32_t &apar) {
+                         int buf, uint32_t &apar, unsigned long long *tp) {
+    // tp (traced steps, first item): this CTA's time at points 0..5 of the item, row stride tps
+    const long long tps = gridDim.x + 1;
+    auto PT = [&](int i) {
+        if (tp && threadIdx.x == 0) tp[i * tps + blockIdx.x] = global_ns();
+    };
     constexpr int D = 128, HPT = G / 2, CH = ATTN_CHUNK;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint8_t *K0 = sm.region, *K1 = K0 + 16384, *V0 = K0 + 32768, *V1 = K0 + 49152;
-    float *qs = reinterpret_cast<float *>(sm.region + 65536);  // [D][G]
-    float *ps = qs + D * G;                                    // [CH][G]
-    float *red = ps + CH * G;                                  // [8][8]
-    float *red2 = red + 64;                                    // [4][8]
+    uint8_t *K0 = sm.region + buf * ATTN_BUF, *K1 = K0 + 16384, *V0 = K0 + 32768, *V1 = K0 + 49152;
+    float *qs = reinterpret_cast<float *>(sm.region + 2 * ATTN_BUF);  // [D][G]
+    float *ps = qs + D * G;                                            // [CH][G]
+    float *red = ps + CH * G;                                          // [8][8]
+    float *red2 = red + 64;                                            // [4][8]
     float *s_m = red2 + 32, *s_l = s_m + 8;
-    __half *kvnew = reinterpret_cast<__half *>(s_l + 8);       // [2][128] the appended key and value
+    __half *kvnew = reinterpret_cast<__half *>(s_l + 8);  // [2][128] the appended key and value
     const int t = it.t, g = it.g, c = it.c;
     const int pos = sm.pos[t], nk = pos + 1, nc = (nk + CH - 1) / CH;
     const int base = c * CH, cnt = nk - base < CH ? nk - base : CH;
     const bool last = c == nc - 1;
     const float *qkv = p.qkv + (long long)t * (p.H * D + 2 * p.HK * D);
-    const float *cs = p.rope + (long long)pos * p.n_rot;
+    float cs[4], wn[4];
+    {
+        const float2 *csrow = reinterpret_cast<const float2 *>(p.rope + (long long)pos * p.n_rot);
+        const float2 c0 = __ldg(csrow + lane), c1 = __ldg(csrow + lane + 32);
+        cs[0] = c0.x; cs[1] = c0.y; cs[2] = c1.x; cs[3] = c1.y;
+    }
     // q heads g*G .. g*G+G-1: warp w < G stages head w; a warp G (or 0 when G == 8) the new k/v
     if (warp < G) {
         float v[4];
 #pragma unroll
-        for (int i = 0; i < 4; i++) v[i] = qkv[(g * G + warp) * D + lane + 32 * i];
-        head_norm_rope(v, L.q_norm, cs, p.eps, lane);
+        for (int i = 0; i < 4; i++) {
+            v[i] = __ldcg(qkv + (g * G + warp) * D + lane + 32 * i);
+            wn[i] = __ldg(L.q_norm + lane + 32 * i);
+        }
+        head_norm_rope(v, wn, cs, p.eps);
 #pragma unroll
         for (int i = 0; i < 4; i++) qs[(lane + 32 * i) * G + warp] = f16_round(v[i]);
     }
@@ -420,10 +581,11 @@ __device__ bool attn_run(const StepArgs &p, const LayerDev &L, const StepSmem &s
         float kk[4], vv[4];
 #pragma unroll
         for (int i = 0; i < 4; i++) {
-            kk[i] = qkv[p.H * D + g * D + lane + 32 * i];
-            vv[i] = qkv[p.H * D + p.HK * D + g * D + lane + 32 * i];
+            kk[i] = __ldcg(qkv + p.H * D + g * D + lane + 32 * i);
+            vv[i] = __ldcg(qkv + p.H * D + p.HK * D + g * D + lane + 32 * i);
+            wn[i] = __ldg(L.k_norm + lane + 32 * i);
         }
-        head_norm_rope(kk, L.k_norm, cs, p.eps, lane);
+        head_norm_rope(kk, wn, cs, p.eps);
         const int seq = p.seq_of[t];
         const int blk = p.block_table[seq * p.max_blocks + pos / 16];
         const long long rowK = ((((long long)layer * p.n_blocks + blk) * 2 + 0) * p.HK + g) * 16 + pos % 16;
@@ -438,9 +600,11 @@ __device__ bool attn_run(const StepArgs &p, const LayerDev &L, const StepSmem &s
         }
     }
     __syncthreads();
-    const bool landed = mbar_wait(sm.attn_bar, apar, p.err);
-    apar ^= 1u;
+    PT(0);
+    const bool landed = mbar_wait(sm.attn_bar + buf, (apar >> buf) & 1u, p.err);
+    apar ^= 1u << buf;
     if (__syncthreads_or(!landed)) return false;
+    PT(1);
     if (last) {  // the new position's row of the tiles is the value just computed
         const int r = pos - base;
         if (tid < 32) {
@@ -491,6 +655,7 @@ __device__ bool attn_run(const StepArgs &p, const LayerDev &L, const StepSmem &s
         s_m[tid] = m;
     }
     __syncthreads();
+    PT(2);
 #pragma unroll
     for (int h = 0; h < HPT; h++) {
         const int head = hh * HPT + h;
@@ -500,6 +665,7 @@ __device__ bool attn_run(const StepArgs &p, const LayerDev &L, const StepSmem &s
         if (lane == 0) red2[(warp & 3) * 8 + head] = ws;
     }
     __syncthreads();
+    PT(3);
     if (tid < G) {
         float l = 0.0f;
         for (int w = 0; w < CH / 32; w++) l = __fadd_rn(l, red2[w * 8 + tid]);
@@ -532,6 +698,7 @@ __device__ bool attn_run(const StepArgs &p, const LayerDev &L, const StepSmem &s
         }
     }
     __syncthreads();
+    PT(4);
     const int QW = p.H * D;
     if (nc == 1) {
 #pragma unroll
@@ -556,7 +723,51 @@ __device__ bool attn_run(const StepArgs &p, const LayerDev &L, const StepSmem &s
         }
     }
     __syncthreads();  // the tiles are free for the next item
+    PT(5);
     return true;
+}
+
+// One head's merge of its chunk partials (C8): M = max m_c, f_c = exp(m_c - M),
+// L = sum_c l_c f_c and O = sum_c acc_c f_c in chunk order, out = O / L. Threads < 128 load their
+// dimension's partials (64 chunks at a time) in the same round trip as the m/l loads of threads
+// >= 128.
+__device__ void combine_head(const float *part, long long cstride, int nc, float *out, float *cbuf, float *misc) {
+    const int tid = threadIdx.x;
+    float *cm = cbuf, *cl = cm + nc, *cf = cl + nc;
+    constexpr int B = 64;
+    float a[B];
+    float O = 0.0f;
+    for (int c0 = 0; c0 < nc; c0 += B) {
+        if (tid < 128) {
+#pragma unroll
+            for (int kk = 0; kk < B; kk++)
+                a[kk] = c0 + kk < nc ? __ldcg(part + (long long)(c0 + kk) * cstride + tid) : 0.0f;
+        }
+        if (c0 == 0) {
+            for (int cc = tid - 128; tid >= 128 && cc < nc; cc += STEP_THREADS - 128) {
+                cm[cc] = __ldcg(part + cc * cstride + 128);
+                cl[cc] = __ldcg(part + cc * cstride + 129);
+            }
+            __syncthreads();
+            float M = -__int_as_float(0x7f800000);
+            for (int cc = 0; cc < nc; cc++) M = fmaxf(M, cm[cc]);
+            for (int cc = tid; cc < nc; cc += STEP_THREADS) cf[cc] = bt_exp(__fsub_rn(cm[cc], M));
+            __syncthreads();
+        }
+        if (tid < 128) {
+#pragma unroll
+            for (int kk = 0; kk < B; kk++)
+                if (c0 + kk < nc) O = fmaf(a[kk], cf[c0 + kk], O);
+        }
+    }
+    if (tid == 128) {
+        float Lh = 0.0f;
+        for (int cc = 0; cc < nc; cc++) Lh = fmaf(cl[cc], cf[cc], Lh);
+        misc[1] = Lh;
+    }
+    __syncthreads();
+    if (tid < 128) out[tid] = __fdiv_rn(O, misc[1]);
+    __syncthreads();
 }
 
 // ------------------------------------------------------------------ the kernel
@@ -566,24 +777,30 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     StepSmem sm;
-    sm.ring_bar = reinterpret_cast<uint64_t *>(smem);                      // 8 x 4 x 8 B
+    sm.ring_bar = reinterpret_cast<uint64_t *>(smem);  // 8 x 4 x 8 B
     sm.attn_bar = sm.ring_bar + STEP_WARPS * RING_SLOTS;
+    sm.aux_bar = sm.attn_bar + 2;
     sm.normS = reinterpret_cast<float *>(smem + 512);
     sm.misc = sm.normS + STEP_MAX_T;
     sm.pos = reinterpret_cast<int *>(sm.misc + 64);
-    sm.region = smem + 1024;
+    sm.ldesc = reinterpret_cast<LayerDev *>(smem + 1024);
+    sm.outd = reinterpret_cast<QMatDev *>(smem + 1024 + 2 * sizeof(LayerDev));
+    sm.region = smem + 2048;
     sm.act = reinterpret_cast<ActBlock *>(sm.region + STEP_REGION_BYTES);
     sm.sel_ids = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(sm.act) + STEP_ACT_BYTES);
     sm.sel_w = reinterpret_cast<float *>(sm.sel_ids + STEP_MAX_T * MAX_K);
-    sm.cbuf = sm.sel_w + STEP_MAX_T * MAX_K;
+    sm.wv = sm.sel_w + STEP_MAX_T * MAX_K;
+    sm.cbuf = sm.wv + STEP_WARPS * MAX_K;
+    sm.res = sm.cbuf + STEP_CBUF_BYTES / 4;
 
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int T = p.T, E = p.E, QW = p.H * 128, KW = p.HK * 128, K = p.K, F = p.F;
+    unsigned epoch = 0;
     auto TR = [&](int layer, int ph) -> unsigned long long * {
         return p.trace ? p.trace + ((long long)layer * STEP_PHASES + ph) * (gridDim.x + 1) : nullptr;
     };
-    // a point inside a phase: this CTA's time when all its threads got there
-    unsigned long long *cycv = reinterpret_cast<unsigned long long *>(sm.cbuf + STEP_CBUF_BYTES / 4 - 64);  // [16]
+    // cycle counters of the traced step (max over warps), slots 8 + k of the layer's rows
+    unsigned long long *cycv = reinterpret_cast<unsigned long long *>(sm.misc + 32);  // [16]
     auto CYC_RESET = [&]() {
         if (p.trace) {
             __syncthreads();
@@ -596,12 +813,14 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         __syncthreads();
         if (tid == 0) p.trace[((long long)layer * STEP_PHASES + 8 + k) * (gridDim.x + 1) + blockIdx.x] = cycv[idx];
     };
+    // a point inside a phase: this CTA's time when all its threads got there
     auto POINT = [&](int layer, int k) {
         if (!p.trace) return;
         __syncthreads();
         if (tid == 0) p.trace[((long long)layer * STEP_PHASES + 8 + k) * (gridDim.x + 1) + blockIdx.x] = global_ns();
     };
-    if (p.trace && tid == 0 && blockIdx.x == 0) p.trace[((long long)(p.n_layer + 1) * STEP_PHASES) * (gridDim.x + 1)] = global_ns();
+    if (p.trace && tid == 0 && blockIdx.x == 0)
+        p.trace[((long long)(p.n_layer + 1) * STEP_PHASES) * (gridDim.x + 1)] = global_ns();
     const int nsbE = E / 256, nsbQ = QW / 256, nsbF = F / 256;
 
     WarpRing ring;
@@ -612,12 +831,27 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
     if (lane == 0) {
         for (int i = 0; i < RING_SLOTS; i++) mbar_init(ring.bars + i, 1);
     }
-    if (tid == 0) mbar_init(sm.attn_bar, 1);
+    if (tid < 4) mbar_init(sm.attn_bar + tid, 1);  // attn_bar[0..1] and aux_bar[0..1]
     if (tid < T) sm.pos[tid] = p.dev_len[p.seq_of[tid]];
+    if (tid < LD_WORDS)
+        reinterpret_cast<uint32_t *>(sm.ldesc)[tid] = __ldg(reinterpret_cast<const uint32_t *>(p.layers) + tid);
+    if (tid == 0) *sm.outd = p.out;
     fence_mbar_init();
     __syncthreads();
-    uint32_t apar = 0;
-    if (tid == 0) prefetch_tmap(&tmap);
+    uint32_t apar = 0, xpar = 0;  // next parities of attn_bar[0..1] and aux_bar[0..1]
+    if (tid == 0) {
+        prefetch_tmap(&tmap);
+        // layer 0's attn_norm for the first staging
+        fence_proxy_async();
+        mbar_arrive_expect_tx(sm.aux_bar + 1, E * 4);
+        bulk_g2s(sm.cbuf, sm.ldesc[0].attn_norm, E * 4, sm.aux_bar + 1);
+    }
+    // wait for aux copy i (all threads); false if the bounded wait ran out anywhere in the CTA
+    auto wait_aux = [&](int i) -> bool {
+        const bool ok = mbar_wait(sm.aux_bar + i, (xpar >> i) & 1u, p.err);
+        xpar ^= 1u << i;
+        return !__syncthreads_or(!ok);
+    };
 
     // ---- embedding rows (get_rows) for every token, into the region, then layer 0 reads them
     float *x0 = reinterpret_cast<float *>(sm.region);  // [T][E] f32, 16-byte aligned
@@ -663,49 +897,84 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         if (blockIdx.x == 0 && tid < T) p.pos_of[tid] = sm.pos[tid];
         __syncthreads();
     }
+    // the rope rows of this step's positions, towards L2
+    if (tid < T) prefetch_l2(p.rope + (long long)sm.pos[tid] * p.n_rot, p.n_rot * 4);
 
     for (int il = 0; il < p.n_layer; il++) {
-        const LayerDev &L = p.layers[il];
+        const LayerDev &L = sm.ldesc[il & 1];
+        const bool has_next = il + 1 < p.n_layer;
+        // the next layer's descriptor: loaded now, stored to shared memory after the attention
+        uint32_t ld_next = 0;
+        if (has_next && tid < LD_WORDS) ld_next = __ldg(reinterpret_cast<const uint32_t *>(p.layers + il + 1) + tid);
         // ================= QKV
         const SegList sq = make_segs(&L.q, 0, &L.k, QW, &L.v, QW + KW);
         {
             const float *xs = il == 0 ? x0 : p.x;
-            stage_activations<STEP_WARPS>(xs, E, nullptr, L.attn_norm, p.eps, E, T, sm.act, sm.normS);
+            if (!wait_aux(1)) return;  // attn_norm in cbuf
+            step_stage(xs, E, E, T, sm.cbuf, p.eps, sm.act, sm.normS, nullptr);
             __syncthreads();
             POINT(il, 0);
             if (il == 0) gemv_preissue(ring, sq, warp, lane);  // the region held the embedding rows
             CYC_RESET();
-            if (!gemv_run(ring, sq, sm.act, nsbE, T, p.qkv, QW + 2 * KW, nullptr, 0, nullptr, p.err, warp, lane,
+            if (!gemv_run(ring, sq, sm.act, nsbE, T, p.qkv, QW + 2 * KW, nullptr, 0, 0, nullptr, p.err, warp, lane,
                           p.trace ? cycv : nullptr))
                 return;
             CYC_WRITE(il, 7, 0);
             CYC_WRITE(il, 8, 1);
         }
         // the first attention item's K/V pages, requested before the barrier
-        long long it0 = blockIdx.x;
+        const long long it0 = blockIdx.x;
         const long long n_items = attn_items(p, sm.pos);
         __syncthreads();
         if (tid == 0 && it0 < n_items) {
             AttnItem it;
             attn_item(p, sm.pos, it0, it);
-            attn_issue(p, &tmap, sm, it, il);
+            attn_issue(p, &tmap, sm, it, il, 0);
         }
-        if (!grid_sync(p.bar, p.err, TR(il, 0))) return;
-        // ================= ATTN
-        for (long long i = it0; i < n_items; i += gridDim.x) {
-            AttnItem it;
-            attn_item(p, sm.pos, i, it);
-            if (i != it0) {
-                if (tid == 0) attn_issue(p, &tmap, sm, it, il);
+        if (!grid_sync(p.bar, epoch, p.err, TR(il, 0))) return;
+        // ================= ATTN: items it0, it0 + grid, ...; item k uses tile buffer k & 1 and
+        // requests item k + 1 into the other buffer before its own work
+        {
+            int k = 0;
+            for (long long i = it0; i < n_items; i += gridDim.x, k++) {
+                AttnItem it;
+                attn_item(p, sm.pos, i, it);
+                if (tid == 0 && i + gridDim.x < n_items) {
+                    AttnItem nx;
+                    attn_item(p, sm.pos, i + gridDim.x, nx);
+                    attn_issue(p, &tmap, sm, nx, il, (k + 1) & 1);
+                }
+                unsigned long long *tp =
+                    (p.trace && k == 0) ? p.trace + ((long long)il * STEP_PHASES + 8 + 16) * (gridDim.x + 1) : nullptr;
+                if (!attn_run<G>(p, L, sm, it, il, k & 1, apar, tp)) return;
+                if (k == 0) POINT(il, 1);
             }
-            if (!attn_run<G>(p, L, sm, it, il, apar)) return;
-            if (i == it0) POINT(il, 1);
         }
-        // attn_output tiles are static: request this CTA's first ones now
+        if (has_next && tid < LD_WORDS) reinterpret_cast<uint32_t *>(sm.ldesc + ((il + 1) & 1))[tid] = ld_next;
+        // attn_output tiles are static: request this CTA's first ones now. Its residual rows (x)
+        // are final since the last barrier of the previous layer.
         const SegList so = make_segs(&L.o, 0, nullptr, 0, nullptr, 0);
+        long long o0, o1;
+        cta_range(so.total, o0, o1);
+        const int orow0 = (int)(o0 * L.o.rpt);
+        int orows = (int)(o1 * L.o.rpt) - orow0;
+        orows = orow0 + orows > E ? E - orow0 : orows;
+        orows = orows < 1 ? 1 : orows;
+        float res_pre = 0.0f;
+        if (tid < T * orows && orow0 + tid % orows < E)
+            res_pre = __ldcg(p.x + (long long)(tid / orows) * E + orow0 + tid % orows);
         __syncthreads();
         gemv_preissue(ring, so, warp, lane);
-        if (!grid_sync(p.bar, p.err, TR(il, 1))) return;
+        if (!grid_sync(p.bar, epoch, p.err, TR(il, 1))) return;
+        if (tid < T * orows) sm.res[tid] = res_pre;
+        // the next layer's small vectors, towards L2
+        if (has_next && blockIdx.x < 3) {
+            const LayerDev &Ln = sm.ldesc[(il + 1) & 1];
+            const float *v = blockIdx.x == 0 ? Ln.attn_norm : blockIdx.x == 1 ? Ln.ffn_norm : Ln.q_norm;
+            const int nb = blockIdx.x == 2 ? 128 * 4 : E * 4;
+            if (tid * 128 < nb) prefetch_l2(reinterpret_cast<const uint8_t *>(v) + tid * 128, 128);
+            if (blockIdx.x == 2 && tid < 4) prefetch_l2(reinterpret_cast<const uint8_t *>(Ln.k_norm) + tid * 128, 128);
+        }
         // ================= COMBINE (tokens whose context spans several chunks)
         {
             int multi = 0;
@@ -719,147 +988,118 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                     const int g = hd / G, h = hd % G;
                     const float *part =
                         p.part + (((long long)t * p.HK + g) * p.max_chunks) * G * PART_ROW + (long long)h * PART_ROW;
-                    const long long cstride = (long long)G * PART_ROW;
-                    float *cm = sm.cbuf, *cl = cm + nc, *cf = cl + nc;
-                    for (int cc = tid; cc < nc; cc += STEP_THREADS) {
-                        cm[cc] = __ldcg(part + cc * cstride + 128);
-                        cl[cc] = __ldcg(part + cc * cstride + 129);
-                    }
-                    __syncthreads();
-                    if (warp == 0) {
-                        float m = -__int_as_float(0x7f800000);
-                        for (int cc = lane; cc < nc; cc += 32) m = fmaxf(m, cm[cc]);
-                        m = warp_max(m);
-                        if (lane == 0) sm.misc[0] = m;
-                    }
-                    __syncthreads();
-                    for (int cc = tid; cc < nc; cc += STEP_THREADS) cf[cc] = bt_exp(__fsub_rn(cm[cc], sm.misc[0]));
-                    __syncthreads();
-                    if (tid == 0) {
-                        float Lh = 0.0f;
-                        for (int cc = 0; cc < nc; cc++) Lh = fmaf(cl[cc], cf[cc], Lh);
-                        sm.misc[1] = Lh;
-                    }
-                    __syncthreads();
-                    if (tid < 128) {
-                        float O = 0.0f;
-                        const float *pa = part + tid;
-                        int cc = 0;
-                        for (; cc + 16 <= nc; cc += 16) {
-                            float a[16];
-#pragma unroll
-                            for (int kk = 0; kk < 16; kk++) a[kk] = __ldcg(pa + (long long)(cc + kk) * cstride);
-#pragma unroll
-                            for (int kk = 0; kk < 16; kk++) O = fmaf(a[kk], cf[cc + kk], O);
-                        }
-                        for (; cc < nc; cc++) O = fmaf(__ldcg(pa + (long long)cc * cstride), cf[cc], O);
-                        p.att[(long long)t * QW + hd * 128 + tid] = __fdiv_rn(O, sm.misc[1]);
-                    }
-                    __syncthreads();
+                    combine_head(part, (long long)G * PART_ROW, nc, p.att + (long long)t * QW + hd * 128, sm.cbuf,
+                                 sm.misc);
                 }
-                if (!grid_sync(p.bar, p.err, TR(il, 2))) return;
+                if (!grid_sync(p.bar, epoch, p.err, TR(il, 2))) return;
             }
         }
         // ================= O: ffn_in = x + W_o * att
-        stage_activations<STEP_WARPS>(p.att, QW, nullptr, nullptr, 0.0f, QW, T, sm.act, nullptr);
+        step_stage(p.att, QW, QW, T, nullptr, 0.0f, sm.act, nullptr, nullptr);
         __syncthreads();
         POINT(il, 2);
-        if (!gemv_run(ring, so, sm.act, nsbQ, T, p.ffn_in, E, p.x, E, nullptr, p.err, warp, lane)) return;
-        if (!grid_sync(p.bar, p.err, TR(il, 3))) return;
+        if (!gemv_run(ring, so, sm.act, nsbQ, T, p.ffn_in, E, sm.res, orow0, orows, nullptr, p.err, warp, lane))
+            return;
+        // this CTA's router rows and the ffn norm vector, requested before the barrier
+        const int nrr = (int)blockIdx.x < p.NE ? (p.NE - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
+        float *rrows = reinterpret_cast<float *>(sm.region);
+        float *ynorm = rrows + STEP_ROUTER_ROWS * E;
+        __syncthreads();
+        if (tid == 0) {
+            fence_proxy_async();
+            mbar_arrive_expect_tx(sm.aux_bar + 0, nrr * E * 4);
+            for (int k = 0; k < nrr; k++)
+                bulk_g2s_hint(rrows + k * E, L.gate_inp + (long long)(blockIdx.x + k * gridDim.x) * E, E * 4,
+                              sm.aux_bar + 0, l2_evict_first_policy());
+            mbar_arrive_expect_tx(sm.aux_bar + 1, E * 4);
+            bulk_g2s(sm.cbuf, L.ffn_norm, E * 4, sm.aux_bar + 1);
+        }
+        if (!grid_sync(p.bar, epoch, p.err, TR(il, 3))) return;
         // ================= ROUTER: ffn RMSNorm (staged for the experts too) and router rows
-        stage_activations<STEP_WARPS>(p.ffn_in, E, nullptr, L.ffn_norm, p.eps, E, T, sm.act, sm.normS);
-        __syncthreads();
+        if (!wait_aux(1)) return;
+        step_stage(p.ffn_in, E, E, T, sm.cbuf, p.eps, sm.act, sm.normS, ynorm);
+        if (!wait_aux(0)) return;  // its __syncthreads also completes ynorm
         POINT(il, 3);
-        {
-            // router row r is computed by warp (r / gridDim.x) of CTA r % gridDim.x
-            for (int r = blockIdx.x + warp * gridDim.x; r < p.NE; r += STEP_WARPS * gridDim.x) {
-                const float *wr = L.gate_inp + (long long)r * E;
-                for (int t = 0; t < T; t++) {
-                    const float *xt = p.ffn_in + (long long)t * E;
-                    const float s = sm.normS[t];
-                    float acc = 0.0f;
-                    int i = lane;
-                    for (; i + 32 * 15 < E; i += 32 * 16) {
-                        float wv[16], yv[16];
-#pragma unroll
-                        for (int kk = 0; kk < 16; kk++) {
-                            wv[kk] = __ldg(wr + i + 32 * kk);
-                            yv[kk] = __fmul_rn(__fmul_rn(xt[i + 32 * kk], s), L.ffn_norm[i + 32 * kk]);
-                        }
-#pragma unroll
-                        for (int kk = 0; kk < 16; kk++) acc = fmaf(wv[kk], yv[kk], acc);
-                    }
-                    for (; i < E; i += 32) acc = fmaf(__ldg(wr + i), __fmul_rn(__fmul_rn(xt[i], s), L.ffn_norm[i]), acc);
-                    acc = butterfly_sum(acc);
-                    if (lane == 0) p.rlog[(long long)t * p.NE + r] = acc;
-                }
-            }
-        }
-        if (!grid_sync(p.bar, p.err, TR(il, 4))) return;
-        // ================= GATEUP: soft_max + route() in every CTA, then the experts
-        if (warp < T) {  // warp t routes token t (C5, C7; stable descending by total_cmp)
-            const int t = warp;
-            float *prob = sm.cbuf + t * 512;  // NE <= 512
-            const float *lg = p.rlog + (long long)t * p.NE;
-            float m = -__int_as_float(0x7f800000);
-            for (int i = lane; i < p.NE; i += 32) {
-                const float v = __ldcg(lg + i);
-                prob[i] = v;
-                m = fmaxf(m, v);
-            }
-            m = warp_max(m);
+        for (int q = warp; q < nrr * T; q += STEP_WARPS) {  // (router row k, token t) per warp, C5
+            const int k = q / T, t = q % T;
+            const float *wr = rrows + k * E, *yt = ynorm + t * E;
             float acc = 0.0f;
-            for (int i = lane; i < p.NE; i += 32) {
-                const float e = bt_exp(__fsub_rn(prob[i], m));
-                prob[i] = e;
-                acc = __fadd_rn(acc, e);
-            }
+#pragma unroll 8
+            for (int i = lane; i < E; i += 32) acc = fmaf(wr[i], yt[i], acc);
             acc = butterfly_sum(acc);
-            const float inv = __fdiv_rn(1.0f, acc);
-            for (int i = lane; i < p.NE; i += 32) prob[i] = __fmul_rn(prob[i], inv);
-            __syncwarp();
-            for (int i = lane; i < p.NE; i += 32) {
-                const int ki = total_key(prob[i]);
-                int rank = 0;
-                for (int jj = 0; jj < p.NE; jj++) {
-                    const int kj = total_key(prob[jj]);
-                    rank += (kj > ki) || (kj == ki && jj < i);
-                }
-                if (rank < K) sm.sel_ids[t * MAX_K + rank] = i;  // temporarily by rank
-            }
-            __syncwarp();
-            if (lane == 0) {
-                float total = 0.0f;
-                int ids[MAX_K];
-                float ws[MAX_K];
-                for (int q = 0; q < K; q++) {
-                    ids[q] = sm.sel_ids[t * MAX_K + q];
-                    ws[q] = prob[ids[q]];
-                    total = __fadd_rn(total, ws[q]);
-                }
-                for (int q = 0; q < K; q++) {
-                    ws[q] = total > 0.0f ? __fdiv_rn(ws[q], total) : ws[q];
-                    if (blockIdx.x == 0) {
-                        p.dbg_ids[((long long)il * p.TB + t) * K + q] = ids[q];
-                        p.dbg_w[((long long)il * p.TB + t) * K + q] = ws[q];
-                    }
-                }
-                for (int a = 1; a < K; a++)
-                    for (int b = a; b > 0 && ids[b - 1] > ids[b]; b--) {
-                        const int ti = ids[b];
-                        ids[b] = ids[b - 1];
-                        ids[b - 1] = ti;
-                        const float tw = ws[b];
-                        ws[b] = ws[b - 1];
-                        ws[b - 1] = tw;
-                    }
-                for (int q = 0; q < K; q++) {
-                    sm.sel_ids[t * MAX_K + q] = ids[q];
-                    sm.sel_w[t * MAX_K + q] = ws[q];
-                }
-            }
+            if (lane == 0) p.rlog[(long long)t * p.NE + blockIdx.x + k * gridDim.x] = acc;
         }
-        __syncthreads();
+        const long long dtotal = (long long)T * E;
+        long long d0, d1;
+        cta_range(dtotal, d0, d1);
+        if (!grid_sync(p.bar, epoch, p.err, TR(il, 4))) return;
+        // ================= GATEUP: soft_max + route() in every CTA (C5, C7; stable descending
+        // by total_cmp, top K, renormalised), then the experts
+        {
+            const int NE = p.NE;
+            float *prob = sm.cbuf;                                  // [T][NE]
+            int *keys = reinterpret_cast<int *>(sm.cbuf + T * NE);  // [T][NE]
+            for (int i = tid; i < T * NE; i += STEP_THREADS) prob[i] = __ldcg(p.rlog + i);
+            __syncthreads();
+            if (warp < T) {
+                float *pr = prob + warp * NE;
+                float m = -__int_as_float(0x7f800000);
+                for (int i = lane; i < NE; i += 32) m = fmaxf(m, pr[i]);
+                m = warp_max(m);
+                float acc = 0.0f;
+                for (int i = lane; i < NE; i += 32) {
+                    const float e = bt_exp(__fsub_rn(pr[i], m));
+                    pr[i] = e;
+                    acc = __fadd_rn(acc, e);
+                }
+                acc = butterfly_sum(acc);
+                const float inv = __fdiv_rn(1.0f, acc);
+                for (int i = lane; i < NE; i += 32) {
+                    const float v = __fmul_rn(pr[i], inv);
+                    pr[i] = v;
+                    keys[warp * NE + i] = total_key(v);
+                }
+            }
+            __syncthreads();
+            for (int i = tid; i < T * NE; i += STEP_THREADS) {  // rank of every expert, one per thread
+                const int t = i / NE, li = i - t * NE;
+                const int ki = keys[i];
+                const int4 *kr = reinterpret_cast<const int4 *>(keys + t * NE);
+                int rank = 0;
+#pragma unroll 4
+                for (int j4 = 0; j4 < NE / 4; j4++) {
+                    const int4 kk = kr[j4];
+                    const int j = 4 * j4;
+                    rank += (kk.x > ki) | ((kk.x == ki) & (j < li));
+                    rank += (kk.y > ki) | ((kk.y == ki) & (j + 1 < li));
+                    rank += (kk.z > ki) | ((kk.z == ki) & (j + 2 < li));
+                    rank += (kk.w > ki) | ((kk.w == ki) & (j + 3 < li));
+                }
+                if (rank < K) sm.sel_ids[t * MAX_K + rank] = li;  // by rank for now
+            }
+            __syncthreads();
+            if (warp < T) {  // token t = warp: lane q holds the expert of rank q
+                const int t = warp;
+                const bool has = lane < K;
+                const int id = has ? sm.sel_ids[t * MAX_K + lane] : 0x7fffffff;
+                float w = has ? prob[t * NE + id] : 0.0f;
+                float total = 0.0f;  // in rank order
+                for (int q = 0; q < K; q++) total = __fadd_rn(total, __shfl_sync(FULL, w, q));
+                w = total > 0.0f ? __fdiv_rn(w, total) : w;
+                if (has && blockIdx.x == 0) {
+                    p.dbg_ids[((long long)il * p.TB + t) * K + lane] = id;
+                    p.dbg_w[((long long)il * p.TB + t) * K + lane] = w;
+                }
+                int slot = 0;  // ascending expert ids (distinct)
+                for (int q = 0; q < K; q++) slot += __shfl_sync(FULL, id, q) < id;
+                __syncwarp();
+                if (has) {
+                    sm.sel_ids[t * MAX_K + slot] = id;
+                    sm.sel_w[t * MAX_K + slot] = w;
+                }
+            }
+            __syncthreads();
+        }
         POINT(il, 4);
         {
             const long long total = (long long)T * K * L.gate.n_tiles;
@@ -867,7 +1107,10 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             cta_range(total, u0, u1);
             const int n = warp_units(u0, u1, warp);
             ring.configure(L.gate.tile_bytes + L.up.tile_bytes);
-            const int nsb = L.gate.nsb;
+            const int nsb = L.gate.nsb, gS = L.gate.S, grpt = L.gate.rpt, gnt = L.gate.n_tiles;
+            const bool gq4 = L.gate.type == T_Q4_K, uq4 = L.up.type == T_Q4_K;
+            const int gtb = L.gate.tile_bytes;
+            while (ring.issued < n && ring.can_issue()) gateup_issue(ring, L, sm, K, u0, warp, lane);
             CYC_RESET();
             long long gcw = 0, gc0 = clock64();
             for (int j = 0; j < n; j++) {
@@ -876,22 +1119,22 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                 if (!ring.wait(j, p.err)) return;
                 gcw += clock64() - w0;
                 const long long u = u0 + warp + (long long)j * STEP_WARPS;
-                const int tile = (int)(u % L.gate.n_tiles);
-                const long long tk = u / L.gate.n_tiles;
+                const int tile = (int)(u % gnt);
+                const long long tk = u / gnt;
                 const int t = (int)(tk / K);
-                const uint8_t *gt = ring.slot_ptr(j), *ut = gt + L.gate.tile_bytes;
-                const bool active = lane < L.gate.S;
-                const int rit = active ? lane / nsb : 0, b = active ? lane % nsb : 0;
-                const int row = tile * L.gate.rpt + rit;
+                const uint8_t *gt = ring.slot_ptr(j), *ut = gt + gtb;
+                const bool active = lane < gS;
+                const int rit = active ? lane / nsb : 0, b = active ? lane - rit * nsb : 0;
+                const int row = tile * grpt + rit;
                 float rowv[2];
 #pragma unroll 1
                 for (int which = 0; which < 2; which++) {
                     const uint8_t *tl = which ? ut : gt;
-                    const int ty = which ? L.up.type : L.gate.type;
+                    const bool q4 = which ? uq4 : gq4;
                     float v = 0.0f;
                     if (active) {
                         const ActBlock &ab = sm.act[t * nsbE + b];
-                        v = ty == T_Q4_K ? q4k_slot_dot(tl, L.gate.S, lane, ab) : q6k_slot_dot(tl, L.gate.S, lane, ab);
+                        v = slot_dot(q4, tl, gS, lane, &ab);
                     }
                     float rr = 0.0f;
                     for (int b2 = 0; b2 < nsb; b2++) {
@@ -912,44 +1155,47 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             CYC_WRITE(il, 12, 5);
             POINT(il, 5);
             // the down rows of this CTA: request the first ones before the barrier
-            const long long dtotal = (long long)T * E;
-            long long d0, d1;
-            cta_range(dtotal, d0, d1);
             const int dn = warp_units(d0, d1, warp);
             ring.configure(K * L.down.tile_bytes);
             while (ring.issued < dn && ring.can_issue()) down_issue(ring, L, sm, K, E, d0, warp, lane);
         }
-        if (!grid_sync(p.bar, p.err, TR(il, 5))) return;
+        // the down phase's residual rows (ffn_in, final since the O barrier)
+        float dres_pre = 0.0f;
+        if (tid < d1 - d0) dres_pre = __ldcg(p.ffn_in + d0 + tid);
+        if (!grid_sync(p.bar, epoch, p.err, TR(il, 5))) return;
+        if (tid < d1 - d0) sm.res[tid] = dres_pre;
         // ================= DOWN: the experts' down rows, their sum in the reference's order, residual
-        stage_activations<STEP_WARPS>(p.act, F, nullptr, nullptr, 0.0f, F, T * K, sm.act, nullptr);
+        step_stage(p.act, F, F, T * K, nullptr, 0.0f, sm.act, nullptr, nullptr);
         __syncthreads();
         POINT(il, 6);
         {
-            const long long total = (long long)T * E;
-            long long u0, u1;
-            cta_range(total, u0, u1);
-            const int n = warp_units(u0, u1, warp);
+            const int n = warp_units(d0, d1, warp);
             const int nsb = nsbF, epp = 32 / nsb;
-            float *wv = sm.cbuf + STEP_MAX_T * 512 + warp * MAX_K;  // this warp's expert row values
+            const int dtb = L.down.tile_bytes;
+            const bool dq4 = L.down.type == T_Q4_K;
+            float *wv = sm.wv + warp * MAX_K;  // this warp's expert row values
+            int workers = p.workers < K ? p.workers : K;
+            if (workers < 1) workers = 1;
+            const int wchunk = (K + workers - 1) / workers;
             CYC_RESET();
             long long dcw = 0, dc0 = clock64();
             for (int j = 0; j < n; j++) {
-                while (ring.issued < n && ring.can_issue()) down_issue(ring, L, sm, K, E, u0, warp, lane);
+                while (ring.issued < n && ring.can_issue()) down_issue(ring, L, sm, K, E, d0, warp, lane);
                 const long long w0 = clock64();
                 if (!ring.wait(j, p.err)) return;
                 dcw += clock64() - w0;
-                const long long u = u0 + warp + (long long)j * STEP_WARPS;
-                const int row = (int)(u % E), t = (int)(u / E);
+                const long long u = d0 + warp + (long long)j * STEP_WARPS;
+                const int t = (int)(u / E);
                 const uint8_t *base = ring.slot_ptr(j);
-                const int kk = lane / nsb, b = lane % nsb;
+                const int kk = lane / nsb, b = lane - kk * nsb;
                 for (int k0 = 0; k0 < K; k0 += epp) {
                     const int k = k0 + kk;
                     const bool valid = kk < epp && k < K;
                     float v = 0.0f;
                     if (valid) {
                         const ActBlock &ab = sm.act[(t * K + k) * nsb + b];
-                        const uint8_t *tile = base + k * L.down.tile_bytes;
-                        v = L.down.type == T_Q4_K ? q4k_slot_dot(tile, nsb, b, ab) : q6k_slot_dot(tile, nsb, b, ab);
+                        const uint8_t *tile = base + k * dtb;
+                        v = slot_dot(dq4, tile, nsb, b, &ab);
                     }
                     float acc = 0.0f;
                     for (int b2 = 0; b2 < nsb; b2++) {
@@ -963,16 +1209,13 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                     // expert_ffn_single order: chunks of ceil(K/workers) summed by ggml_add, partials
                     // added to a zero vector (stream.rs:1232-1284)
                     const float *w = sm.sel_w + t * MAX_K;
-                    int workers = p.workers < K ? p.workers : K;
-                    if (workers < 1) workers = 1;
-                    const int chunk = (K + workers - 1) / workers;
                     float sum = 0.0f;
-                    for (int s0 = 0; s0 < K; s0 += chunk) {
+                    for (int s0 = 0; s0 < K; s0 += wchunk) {
                         float tot = __fmul_rn(wv[s0], w[s0]);
-                        for (int q = s0 + 1; q < K && q < s0 + chunk; q++) tot = __fadd_rn(tot, __fmul_rn(wv[q], w[q]));
+                        for (int q = s0 + 1; q < K && q < s0 + wchunk; q++) tot = __fadd_rn(tot, __fmul_rn(wv[q], w[q]));
                         sum = workers <= 1 ? tot : __fadd_rn(sum, tot);
                     }
-                    p.x[(long long)t * E + row] = __fadd_rn(p.ffn_in[(long long)t * E + row], sum);
+                    p.x[u] = __fadd_rn(sm.res[(int)(u - d0)], sum);
                 }
                 __syncwarp();
                 ring.done++;
@@ -984,25 +1227,39 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             CYC_WRITE(il, 9, 2);
             CYC_WRITE(il, 10, 3);
         }
-        // the next layer's q/k/v tiles (or the output head's) are static: request them now
-        if (il + 1 < p.n_layer) {
-            const LayerDev &Ln = p.layers[il + 1];
+        // the next layer's q/k/v tiles (or the output head's) and its norm vector are static:
+        // request them now
+        __syncthreads();
+        if (tid == 0) {
+            const float *nv = has_next ? sm.ldesc[(il + 1) & 1].attn_norm : p.out_norm;
+            fence_proxy_async();
+            mbar_arrive_expect_tx(sm.aux_bar + 1, E * 4);
+            bulk_g2s(sm.cbuf, nv, E * 4, sm.aux_bar + 1);
+        }
+        if (has_next) {
+            const LayerDev &Ln = sm.ldesc[(il + 1) & 1];
             const SegList sqn = make_segs(&Ln.q, 0, &Ln.k, QW, &Ln.v, QW + KW);
             gemv_preissue(ring, sqn, warp, lane);
         } else {
-            const SegList sout = make_segs(&p.out, 0, nullptr, 0, nullptr, 0);
+            const SegList sout = make_segs(sm.outd, 0, nullptr, 0, nullptr, 0);
             gemv_preissue(ring, sout, warp, lane);
         }
-        if (!grid_sync(p.bar, p.err, TR(il, 6))) return;
+        if (!grid_sync(p.bar, epoch, p.err, TR(il, 6))) return;
     }
     // ================= output head with the fused argmax
     {
-        const SegList sout = make_segs(&p.out, 0, nullptr, 0, nullptr, 0);
-        stage_activations<STEP_WARPS>(p.x, E, nullptr, p.out_norm, p.eps, E, T, sm.act, sm.normS);
+        const SegList sout = make_segs(sm.outd, 0, nullptr, 0, nullptr, 0);
+        if (!wait_aux(1)) return;  // out_norm in cbuf
+        step_stage(p.x, E, E, T, sm.cbuf, p.eps, sm.act, sm.normS, nullptr);
         __syncthreads();
-        if (!gemv_run(ring, sout, sm.act, nsbE, T, p.logits, p.V, nullptr, 0, p.amax, p.err, warp, lane)) return;
+        CYC_RESET();
+        if (!gemv_run(ring, sout, sm.act, nsbE, T, p.logits, p.V, nullptr, 0, 0, p.amax, p.err, warp, lane,
+                      p.trace ? cycv : nullptr))
+            return;
+        CYC_WRITE(p.n_layer, 13, 0);
+        CYC_WRITE(p.n_layer, 14, 1);
     }
-    if (!grid_sync(p.bar, p.err, TR(p.n_layer, 0))) return;
+    if (!grid_sync(p.bar, epoch, p.err, TR(p.n_layer, 0))) return;
     // ================= step end: argmax out, lengths advance, greedy feed-back
     if (blockIdx.x == 0 && tid < T) {
         const int t = tid;
@@ -1021,7 +1278,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
 
 size_t step_smem_bytes(int max_chunks) {
     (void)max_chunks;
-    return 1024 + 1024 + STEP_REGION_BYTES + STEP_ACT_BYTES + (size_t)STEP_MAX_T * MAX_K * 8 + STEP_CBUF_BYTES;
+    return 1024 + 2048 + STEP_REGION_BYTES + STEP_ACT_BYTES + (size_t)STEP_MAX_T * MAX_K * 8 +
+           (size_t)STEP_WARPS * MAX_K * 4 + STEP_CBUF_BYTES + (size_t)STEP_RES * 4;
 }
 
 cudaError_t init_step_kernel_attributes() {

@@ -10,7 +10,9 @@ namespace bt {
 constexpr int STEP_MAX_T = 4;                    // sequences one persistent step carries
 constexpr int STEP_REGION_BYTES = 150 * 1024;    // rings / attention tiles
 constexpr int STEP_ACT_BYTES = 32 * 1024;        // Q8_K activation blocks
-constexpr int STEP_CBUF_BYTES = 16 * 1024;       // router probabilities, combine scratch, expert values
+constexpr int STEP_CBUF_BYTES = 16 * 1024;       // norm vector, router probabilities, combine scratch
+constexpr int STEP_ROUTER_ROWS = 4;              // router rows one CTA computes
+constexpr int STEP_RES = 256;                    // residual values one CTA prefetches for a phase
 
 // A quantised matrix in the tiled layout, as the device reads it.
 struct QMatDev {
@@ -19,6 +21,8 @@ struct QMatDev {
     long long mat_bytes;  // one expert's matrix
 };
 
+// One layer's tensors as the device reads them; the persistent kernel copies it into shared
+// memory word by word.
 struct LayerDev {
     const float *attn_norm, *q_norm, *k_norm, *ffn_norm, *gate_inp;
     QMatDev q, k, v, o, gate, up, down;
@@ -48,14 +52,14 @@ struct StepArgs {
     unsigned long long *amax;
     int *next_token, *tokens_buf, *gen_out, *gen_count;
     int n_out;
-    unsigned *bar;  // [2] grid barrier: arrivals, generation
+    unsigned *bar;  // grid barrier arrival counter, zeroed before each launch
     int *err;
     // optional timeline: per barrier, every CTA's arrival time and CTA 0's departure time
     // (%globaltimer ns), rows of gridDim.x + 1 at trace[(layer * STEP_PHASES + phase) * (grid + 1)]
     unsigned long long *trace;
 };
 
-constexpr int STEP_PHASES = 24;  // timeline slots per layer: 8 barriers, then 16 points inside phases
+constexpr int STEP_PHASES = 32;  // timeline slots per layer: 8 barriers, then 24 points inside phases
 
 size_t step_smem_bytes(int max_chunks);
 cudaError_t init_step_kernel_attributes();

@@ -207,11 +207,12 @@ class StreamingRunner:
     def profile_decode(self, cache: KvCache, first_tokens, n_steps: int, seqs=None) -> dict:
         first = _u32(first_tokens)
         seqs = _u32(range(len(first)) if seqs is None else seqs)
-        arr = (_lib.KernelTime * 32)()
+        cap = 128
+        arr = (_lib.KernelTime * cap)()
         n = C.c_uint32()
         check(lib.bt_profile_decode(self.engine.h, cache.h, _lib.ptr(seqs, C.c_uint32), _lib.ptr(first, C.c_uint32),
-                                    len(first), n_steps, arr, 32, C.byref(n)))
-        return {arr[i].name.decode(): (arr[i].launches, arr[i].total_ms) for i in range(min(n.value, 32))}
+                                    len(first), n_steps, arr, cap, C.byref(n)))
+        return {arr[i].name.decode(): (arr[i].launches, arr[i].total_ms) for i in range(min(n.value, cap))}
 
 
 def dequantize(ggml_type: int, data: np.ndarray, n: int) -> np.ndarray:
