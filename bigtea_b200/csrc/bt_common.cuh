@@ -54,6 +54,22 @@ __device__ __forceinline__ float bt_exp(float x) {
     return __fmul_rn(p, pow2i(ni));
 }
 
+// f16 x f16 + f32 with one rounding (sm_100 mixed-precision fma on the FMA pipe). Equal to
+// fmaf((float)a, (float)b, c): the product of two f16 values is exact in f32.
+__device__ __forceinline__ float fma_f16(uint16_t a, uint16_t b, float c) {
+    float d;
+    asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));
+    return d;
+}
+// f16 -> f32 on the FMA pipe: a + (-0) is exact for every value, signed zeros included.
+__device__ __forceinline__ float h2f_fma(uint16_t a) {
+    float d;
+    asm("add.rn.f32.f16 %0, %1, %2;" : "=f"(d) : "h"(a), "f"(-0.0f));
+    return d;
+}
+__device__ __forceinline__ uint16_t lo16(uint32_t w) { return (uint16_t)(w & 0xffffu); }
+__device__ __forceinline__ uint16_t hi16(uint32_t w) { return (uint16_t)(w >> 16); }
+
 __device__ __forceinline__ float bt_silu(float x) { return __fdiv_rn(x, __fadd_rn(1.0f, bt_exp(-x))); }
 
 // f32::total_cmp as a signed integer key (core/arch/src/sample.rs:928-935 orders by it)

@@ -41,7 +41,6 @@ constexpr int PART_ROW = 132;    // floats per (chunk, head) partial: acc[128], 
 constexpr int ATTN_BUF = 65536;  // one attention item's K and V tiles (128 keys x 128 dims x f16 x 2)
 constexpr int LD_WORDS = sizeof(LayerDev) / 4;
 static_assert(sizeof(LayerDev) % 4 == 0 && sizeof(LayerDev) <= 384, "layer descriptor size");
-static_assert(2 * ATTN_BUF + 9216 <= STEP_REGION_BYTES, "attention tiles and scratch fit the region");
 static_assert(STEP_RES == STEP_THREADS, "one residual value per thread");
 
 // ------------------------------------------------------------------ shared memory map
@@ -54,6 +53,7 @@ struct StepSmem {
     float *normS;        // [STEP_MAX_T]
     float *misc;         // 64 floats
     int *pos;            // [STEP_MAX_T]
+    int *blkn;           // [STEP_MAX_T] the cache block of each token's new position
     LayerDev *ldesc;     // [2] this layer's and the next layer's descriptors
     QMatDev *outd;       // the output head's descriptor
     int *sel_ids;        // [STEP_MAX_T][MAX_K]
@@ -520,6 +520,47 @@ __device__ __forceinline__ void head_norm_rope(float v[4], const float w[4], con
     }
 }
 
+// ------------------------------------------------------------------ attention
+// Each half of the CTA (128 threads, warps 4h .. 4h+3, named barrier 1 + h) runs one attention
+// item at a time with its own K/V tile buffer and scratch, so a CTA's first two items run
+// concurrently.
+constexpr int ATTN_SCRATCH = 8192;  // per half: q (D x G f16), p (CH x G f32), reductions, new k/v
+static_assert(2 * ATTN_BUF + 2 * ATTN_SCRATCH <= STEP_REGION_BYTES, "attention tiles and scratch fit the region");
+
+__device__ __forceinline__ void half_sync(int h) { asm volatile("bar.sync %0, 128;" ::"r"(1 + h) : "memory"); }
+__device__ __forceinline__ bool half_sync_or(int h, bool v) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.s32 p, %1, 0;\n\tbar.red.or.pred q, %2, 128, p;\n\tselp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((int)v), "r"(1 + h)
+        : "memory");
+    return r != 0;
+}
+
+// a0 += lo(q) * k, a1 += hi(q) * k with k the low (KHI false) or high half of kw (C8 terms)
+template <bool KHI>
+__device__ __forceinline__ void fma_qk(uint32_t qw, uint32_t kw, float &a0, float &a1) {
+    if constexpr (KHI)
+        asm("{\n\t.reg .b16 ql, qh, kl, kh;\n\tmov.b32 {ql, qh}, %2;\n\tmov.b32 {kl, kh}, %3;\n\t"
+            "fma.rn.f32.f16 %0, ql, kh, %0;\n\tfma.rn.f32.f16 %1, qh, kh, %1;\n\t}"
+            : "+f"(a0), "+f"(a1)
+            : "r"(qw), "r"(kw));
+    else
+        asm("{\n\t.reg .b16 ql, qh, kl, kh;\n\tmov.b32 {ql, qh}, %2;\n\tmov.b32 {kl, kh}, %3;\n\t"
+            "fma.rn.f32.f16 %0, ql, kl, %0;\n\tfma.rn.f32.f16 %1, qh, kl, %1;\n\t}"
+            : "+f"(a0), "+f"(a1)
+            : "r"(qw), "r"(kw));
+}
+// both halves of w as exact f32 values (FMA pipe)
+__device__ __forceinline__ float2 h2f2_fma(uint32_t w) {
+    float2 r;
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tadd.rn.f32.f16 %0, l, %3;\n\tadd.rn.f32.f16 %1, h, %3;\n\t}"
+        : "=f"(r.x), "=f"(r.y)
+        : "r"(w), "f"(-0.0f));
+    return r;
+}
+
 template <int N>
 __device__ __forceinline__ void lds_n(float (&dst)[N], const float *src) {
     if constexpr (N == 4) {
@@ -533,77 +574,93 @@ __device__ __forceinline__ void lds_n(float (&dst)[N], const float *src) {
         for (int k = 0; k < N; k++) dst[k] = src[k];
     }
 }
+template <int N>
+__device__ __forceinline__ void ldw_n(uint32_t (&dst)[N], const uint32_t *src) {
+    if constexpr (N == 4) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(src);
+        dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
+    } else if constexpr (N == 2) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(src);
+        dst[0] = v.x; dst[1] = v.y;
+    } else {
+#pragma unroll
+        for (int k = 0; k < N; k++) dst[k] = src[k];
+    }
+}
 
-// One attention item (C8): the K/V tiles are in flight into buffer `buf` (attn_issue); stages q,
-// appends the new key and value if this is the token's last chunk, then scores, softmax and P*V.
+// One attention item (C8) on half `hf` of the CTA: the K/V tiles are in flight into buffer hf
+// (attn_issue). Stages q (f16), appends the new key and value if this is the token's last
+// chunk, then scores (thread = key, all G heads, dims in order), the chunk max, exp and P3 sum
+// (32-key butterflies, the 4 warp sums in order) and P*V (thread = 2 dims x G/2 heads, keys in
+// order).
 template <int G>
-__device__ bool attn_run(const StepArgs &p, const LayerDev &L, const StepSmem &sm, const AttnItem &it, int layer,
-                         int buf, uint32_t &apar, unsigned long long *tp) {
-    // tp (traced steps, first item): this CTA's time at points 0..5 of the item, row stride tps
+__device__ bool attn_half(const StepArgs &p, const LayerDev &L, const StepSmem &sm, const AttnItem &it, int layer,
+                          int hf, uint32_t &apar, unsigned long long *tp) {
+    constexpr int D = 128, HPT = G / 2, CH = ATTN_CHUNK, QWORDS = G / 2;
+    const int tid = threadIdx.x & 127, warp = tid >> 5, lane = tid & 31;
     const long long tps = gridDim.x + 1;
     auto PT = [&](int i) {
-        if (tp && threadIdx.x == 0) tp[i * tps + blockIdx.x] = global_ns();
+        if (tp && tid == 0) tp[i * tps + blockIdx.x] = global_ns();
     };
-    constexpr int D = 128, HPT = G / 2, CH = ATTN_CHUNK;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint8_t *K0 = sm.region + buf * ATTN_BUF, *K1 = K0 + 16384, *V0 = K0 + 32768, *V1 = K0 + 49152;
-    float *qs = reinterpret_cast<float *>(sm.region + 2 * ATTN_BUF);  // [D][G]
-    float *ps = qs + D * G;                                            // [CH][G]
-    float *red = ps + CH * G;                                          // [8][8]
-    float *red2 = red + 64;                                            // [4][8]
+    uint8_t *K0 = sm.region + hf * ATTN_BUF, *K1 = K0 + 16384, *V0 = K0 + 32768, *V1 = K0 + 49152;
+    uint8_t *scr = sm.region + 2 * ATTN_BUF + hf * ATTN_SCRATCH;
+    uint16_t *qs = reinterpret_cast<uint16_t *>(scr);           // [D][G] f16 bits
+    float *ps = reinterpret_cast<float *>(scr + D * G * 2);     // [CH][G]
+    float *red = ps + CH * G;                                   // [4][8]
+    float *red2 = red + 32;                                     // [4][8]
     float *s_m = red2 + 32, *s_l = s_m + 8;
-    __half *kvnew = reinterpret_cast<__half *>(s_l + 8);  // [2][128] the appended key and value
+    __half *kvnew = reinterpret_cast<__half *>(s_l + 8);        // [2][128] the appended key and value
     const int t = it.t, g = it.g, c = it.c;
     const int pos = sm.pos[t], nk = pos + 1, nc = (nk + CH - 1) / CH;
     const int base = c * CH, cnt = nk - base < CH ? nk - base : CH;
     const bool last = c == nc - 1;
     const float *qkv = p.qkv + (long long)t * (p.H * D + 2 * p.HK * D);
-    float cs[4], wn[4];
+    float cs[4];
     {
         const float2 *csrow = reinterpret_cast<const float2 *>(p.rope + (long long)pos * p.n_rot);
         const float2 c0 = __ldg(csrow + lane), c1 = __ldg(csrow + lane + 32);
         cs[0] = c0.x; cs[1] = c0.y; cs[2] = c1.x; cs[3] = c1.y;
     }
-    // q heads g*G .. g*G+G-1: warp w < G stages head w; a warp G (or 0 when G == 8) the new k/v
-    if (warp < G) {
-        float v[4];
+    // units: the G q heads, then (last chunk) the new key/value; warp w takes units w, w+4, ...
+    const int units = G + (last ? 1 : 0);
+    for (int u = warp; u < units; u += 4) {
+        float v[4], wn[4];
+        if (u < G) {
 #pragma unroll
-        for (int i = 0; i < 4; i++) {
-            v[i] = __ldcg(qkv + (g * G + warp) * D + lane + 32 * i);
-            wn[i] = __ldg(L.q_norm + lane + 32 * i);
+            for (int i = 0; i < 4; i++) {
+                v[i] = __ldcg(qkv + (g * G + u) * D + lane + 32 * i);
+                wn[i] = __ldg(L.q_norm + lane + 32 * i);
+            }
+            head_norm_rope(v, wn, cs, p.eps);
+#pragma unroll
+            for (int i = 0; i < 4; i++) qs[(lane + 32 * i) * G + u] = __half_as_ushort(__float2half_rn(v[i]));
+        } else {
+            // KvCache::push of this token's head g: k normed and roped, v as is, both to f16
+            float vv[4];
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                v[i] = __ldcg(qkv + p.H * D + g * D + lane + 32 * i);
+                vv[i] = __ldcg(qkv + p.H * D + p.HK * D + g * D + lane + 32 * i);
+                wn[i] = __ldg(L.k_norm + lane + 32 * i);
+            }
+            head_norm_rope(v, wn, cs, p.eps);
+            const long long rowK = ((((long long)layer * p.n_blocks + sm.blkn[t]) * 2 + 0) * p.HK + g) * 16 + pos % 16;
+            const long long rowV = rowK + (long long)p.HK * 16;
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const __half hk = __float2half_rn(v[i]), hv = __float2half_rn(vv[i]);
+                p.kv[rowK * D + lane + 32 * i] = hk;
+                p.kv[rowV * D + lane + 32 * i] = hv;
+                kvnew[lane + 32 * i] = hk;
+                kvnew[128 + lane + 32 * i] = hv;
+            }
         }
-        head_norm_rope(v, wn, cs, p.eps);
-#pragma unroll
-        for (int i = 0; i < 4; i++) qs[(lane + 32 * i) * G + warp] = f16_round(v[i]);
     }
-    if (last && warp == (G < 8 ? G : 0)) {
-        // KvCache::push of this token's head g: k normed and roped, v as is, both to f16
-        float kk[4], vv[4];
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            kk[i] = __ldcg(qkv + p.H * D + g * D + lane + 32 * i);
-            vv[i] = __ldcg(qkv + p.H * D + p.HK * D + g * D + lane + 32 * i);
-            wn[i] = __ldg(L.k_norm + lane + 32 * i);
-        }
-        head_norm_rope(kk, wn, cs, p.eps);
-        const int seq = p.seq_of[t];
-        const int blk = p.block_table[seq * p.max_blocks + pos / 16];
-        const long long rowK = ((((long long)layer * p.n_blocks + blk) * 2 + 0) * p.HK + g) * 16 + pos % 16;
-        const long long rowV = rowK + (long long)p.HK * 16;
-#pragma unroll
-        for (int i = 0; i < 4; i++) {
-            const __half hk = __float2half_rn(kk[i]), hv = __float2half_rn(vv[i]);
-            p.kv[rowK * D + lane + 32 * i] = hk;
-            p.kv[rowV * D + lane + 32 * i] = hv;
-            kvnew[lane + 32 * i] = hk;
-            kvnew[128 + lane + 32 * i] = hv;
-        }
-    }
-    __syncthreads();
+    half_sync(hf);
     PT(0);
-    const bool landed = mbar_wait(sm.attn_bar + buf, (apar >> buf) & 1u, p.err);
-    apar ^= 1u << buf;
-    if (__syncthreads_or(!landed)) return false;
+    const bool landed = mbar_wait(sm.attn_bar + hf, (apar >> hf) & 1u, p.err);
+    apar ^= 1u << hf;
+    if (half_sync_or(hf, !landed)) return false;
     PT(1);
     if (last) {  // the new position's row of the tiles is the value just computed
         const int r = pos - base;
@@ -618,96 +675,116 @@ __device__ bool attn_run(const StepArgs &p, const LayerDev &L, const StepSmem &s
                 *reinterpret_cast<__half *>(vt) = kvnew[128 + d];
             }
         }
-        __syncthreads();
+        half_sync(hf);
     }
-    // ---- scores: key k, heads hh*HPT .. +HPT
-    const int hh = tid >> 7, k = tid & 127;
+    // ---- scores: thread = key k, all G heads (pairs of heads per q word)
+    const int k = tid;
     const bool valid = k < cnt;
-    float sc[HPT];
+    float sc[G];
 #pragma unroll
-    for (int h = 0; h < HPT; h++) sc[h] = 0.0f;
+    for (int h = 0; h < G; h++) sc[h] = 0.0f;
+    {
+        const uint8_t *krow = K0 + k * 128;
+        const int ksw = k & 7;
+        const uint32_t *qw = reinterpret_cast<const uint32_t *>(qs);
 #pragma unroll 2
-    for (int c16 = 0; c16 < 16; c16++) {
-        const uint8_t *kr = (c16 < 8) ? K0 : K1;
-        const uint4 w = *reinterpret_cast<const uint4 *>(kr + k * 128 + (((c16 & 7) ^ (k & 7)) << 4));
-        const __half *hk = reinterpret_cast<const __half *>(&w);
+        for (int c16 = 0; c16 < 16; c16++) {
+            const uint4 w = *reinterpret_cast<const uint4 *>((c16 < 8 ? krow : krow + 16384) + (((c16 & 7) ^ ksw) << 4));
+            const uint32_t kw[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            const float kf = __half2float(hk[e]);
-            float q[HPT];
-            lds_n<HPT>(q, qs + (c16 * 8 + e) * G + hh * HPT);
+            for (int e = 0; e < 8; e++) {
+                uint32_t q[QWORDS];
+                ldw_n<QWORDS>(q, qw + (c16 * 8 + e) * QWORDS);
 #pragma unroll
-            for (int h = 0; h < HPT; h++) sc[h] = fmaf(q[h], kf, sc[h]);
+                for (int j = 0; j < QWORDS; j++) {
+                    if (e & 1)
+                        fma_qk<true>(q[j], kw[e >> 1], sc[2 * j], sc[2 * j + 1]);
+                    else
+                        fma_qk<false>(q[j], kw[e >> 1], sc[2 * j], sc[2 * j + 1]);
+                }
+            }
         }
     }
     const float NEG_INF = -__int_as_float(0x7f800000);
 #pragma unroll
-    for (int h = 0; h < HPT; h++) {
+    for (int h = 0; h < G; h++) {
         sc[h] = valid ? __fmul_rn(sc[h], p.scale) : NEG_INF;
         const float m = warp_max(sc[h]);
         if (lane == 0) red[warp * 8 + h] = m;
     }
-    __syncthreads();
+    half_sync(hf);
     if (tid < G) {
-        const int w0 = (tid / HPT) * 4, slot = tid % HPT;
-        float m = red[w0 * 8 + slot];
-        for (int w = 1; w < 4; w++) m = fmaxf(m, red[(w0 + w) * 8 + slot]);
+        float m = red[tid];
+        for (int w = 1; w < 4; w++) m = fmaxf(m, red[w * 8 + tid]);
         s_m[tid] = m;
     }
-    __syncthreads();
+    half_sync(hf);
     PT(2);
 #pragma unroll
-    for (int h = 0; h < HPT; h++) {
-        const int head = hh * HPT + h;
-        const float pr = valid ? bt_exp(__fsub_rn(sc[h], s_m[head])) : 0.0f;
-        ps[k * G + head] = pr;
+    for (int h = 0; h < G; h++) {
+        const float pr = valid ? bt_exp(__fsub_rn(sc[h], s_m[h])) : 0.0f;
+        sc[h] = pr;
         const float ws = butterfly_sum(pr);
-        if (lane == 0) red2[(warp & 3) * 8 + head] = ws;
+        if (lane == 0) red2[warp * 8 + h] = ws;
     }
-    __syncthreads();
+    if constexpr (G % 4 == 0) {
+        float4 *prow = reinterpret_cast<float4 *>(ps + k * G);
+#pragma unroll
+        for (int h4 = 0; h4 < G / 4; h4++) prow[h4] = make_float4(sc[4 * h4], sc[4 * h4 + 1], sc[4 * h4 + 2], sc[4 * h4 + 3]);
+    } else {
+#pragma unroll
+        for (int h = 0; h < G; h++) ps[k * G + h] = sc[h];
+    }
+    half_sync(hf);
     PT(3);
     if (tid < G) {
         float l = 0.0f;
         for (int w = 0; w < CH / 32; w++) l = __fadd_rn(l, red2[w * 8 + tid]);
         s_l[tid] = l;
     }
-    // ---- P*V: column d, heads hq*HPT .. +HPT
-    const int d = tid & 127, hq = tid >> 7;
-    float acc[HPT];
+    // ---- P*V: thread = dims 2dp, 2dp+1 and heads hq*HPT .. +HPT
+    const int dp = tid & 63, hq = tid >> 6;
+    float acc0[HPT], acc1[HPT];
 #pragma unroll
-    for (int h = 0; h < HPT; h++) acc[h] = 0.0f;
+    for (int h = 0; h < HPT; h++) acc0[h] = acc1[h] = 0.0f;
     {
-        const int cc = (d & 63) >> 3;
+        const int d = 2 * dp, cc = (d & 63) >> 3;
         const uint8_t *vcol = ((d < 64) ? V0 : V1) + (d & 7) * 2;
         int off[8];
 #pragma unroll
         for (int kk = 0; kk < 8; kk++) off[kk] = kk * 128 + ((cc ^ kk) << 4);
+        const float *pb0 = ps + hq * HPT;
         for (int j0 = 0; j0 < cnt; j0 += 8) {
             const uint8_t *vb = vcol + j0 * 128;
-            const float *pb = ps + j0 * G + hq * HPT;
+            const float *pb = pb0 + j0 * G;
 #pragma unroll
             for (int kk = 0; kk < 8; kk++) {
                 if (j0 + kk < cnt) {
-                    const float vf = __half2float(*reinterpret_cast<const __half *>(vb + off[kk]));
+                    const float2 vf = h2f2_fma(*reinterpret_cast<const uint32_t *>(vb + off[kk]));
                     float pj[HPT];
                     lds_n<HPT>(pj, pb + kk * G);
 #pragma unroll
-                    for (int h = 0; h < HPT; h++) acc[h] = fmaf(pj[h], vf, acc[h]);
+                    for (int h = 0; h < HPT; h++) {
+                        acc0[h] = fmaf(pj[h], vf.x, acc0[h]);
+                        acc1[h] = fmaf(pj[h], vf.y, acc1[h]);
+                    }
                 }
             }
         }
     }
-    __syncthreads();
+    half_sync(hf);
     PT(4);
     const int QW = p.H * D;
+    const int d = 2 * dp;
     if (nc == 1) {
 #pragma unroll
         for (int h = 0; h < HPT; h++) {
             const int head = hq * HPT + h;
             const float f = bt_exp(__fsub_rn(s_m[head], s_m[head]));
             const float Lh = fmaf(s_l[head], f, 0.0f);
-            const float O = fmaf(acc[h], f, 0.0f);
-            p.att[(long long)t * QW + (g * G + head) * D + d] = __fdiv_rn(O, Lh);
+            float *o = p.att + (long long)t * QW + (g * G + head) * D + d;
+            o[0] = __fdiv_rn(fmaf(acc0[h], f, 0.0f), Lh);
+            o[1] = __fdiv_rn(fmaf(acc1[h], f, 0.0f), Lh);
         }
     } else {
         const long long pbase = (((long long)t * p.HK + g) * p.max_chunks) * G * PART_ROW;
@@ -715,14 +792,14 @@ __device__ bool attn_run(const StepArgs &p, const LayerDev &L, const StepSmem &s
         for (int h = 0; h < HPT; h++) {
             const int head = hq * HPT + h;
             float *pp = p.part + pbase + ((long long)c * G + head) * PART_ROW;
-            pp[d] = acc[h];
-            if (d == 0) {
+            *reinterpret_cast<float2 *>(pp + d) = make_float2(acc0[h], acc1[h]);
+            if (dp == 0) {
                 pp[D] = s_m[head];
                 pp[D + 1] = s_l[head];
             }
         }
     }
-    __syncthreads();  // the tiles are free for the next item
+    half_sync(hf);  // the tiles and scratch are free for this half's next item
     PT(5);
     return true;
 }
@@ -783,6 +860,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
     sm.normS = reinterpret_cast<float *>(smem + 512);
     sm.misc = sm.normS + STEP_MAX_T;
     sm.pos = reinterpret_cast<int *>(sm.misc + 64);
+    sm.blkn = sm.pos + STEP_MAX_T;
     sm.ldesc = reinterpret_cast<LayerDev *>(smem + 1024);
     sm.outd = reinterpret_cast<QMatDev *>(smem + 1024 + 2 * sizeof(LayerDev));
     sm.region = smem + 2048;
@@ -832,7 +910,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         for (int i = 0; i < RING_SLOTS; i++) mbar_init(ring.bars + i, 1);
     }
     if (tid < 4) mbar_init(sm.attn_bar + tid, 1);  // attn_bar[0..1] and aux_bar[0..1]
-    if (tid < T) sm.pos[tid] = p.dev_len[p.seq_of[tid]];
+    if (tid < T) {
+        const int seq = p.seq_of[tid], ps = p.dev_len[seq];
+        sm.pos[tid] = ps;
+        sm.blkn[tid] = p.block_table[seq * p.max_blocks + ps / 16];
+    }
     if (tid < LD_WORDS)
         reinterpret_cast<uint32_t *>(sm.ldesc)[tid] = __ldg(reinterpret_cast<const uint32_t *>(p.layers) + tid);
     if (tid == 0) *sm.outd = p.out;
@@ -922,33 +1004,38 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             CYC_WRITE(il, 7, 0);
             CYC_WRITE(il, 8, 1);
         }
-        // the first attention item's K/V pages, requested before the barrier
+        // the K/V pages of this CTA's first two attention items, requested before the barrier
         const long long it0 = blockIdx.x;
         const long long n_items = attn_items(p, sm.pos);
         __syncthreads();
-        if (tid == 0 && it0 < n_items) {
-            AttnItem it;
-            attn_item(p, sm.pos, it0, it);
-            attn_issue(p, &tmap, sm, it, il, 0);
-        }
-        if (!grid_sync(p.bar, epoch, p.err, TR(il, 0))) return;
-        // ================= ATTN: items it0, it0 + grid, ...; item k uses tile buffer k & 1 and
-        // requests item k + 1 into the other buffer before its own work
-        {
-            int k = 0;
-            for (long long i = it0; i < n_items; i += gridDim.x, k++) {
+        if (tid == 0) {
+            for (int k = 0; k < 2; k++) {
+                const long long i = it0 + (long long)k * gridDim.x;
+                if (i >= n_items) break;
                 AttnItem it;
                 attn_item(p, sm.pos, i, it);
-                if (tid == 0 && i + gridDim.x < n_items) {
-                    AttnItem nx;
-                    attn_item(p, sm.pos, i + gridDim.x, nx);
-                    attn_issue(p, &tmap, sm, nx, il, (k + 1) & 1);
-                }
+                attn_issue(p, &tmap, sm, it, il, k);
+            }
+        }
+        if (!grid_sync(p.bar, epoch, p.err, TR(il, 0))) return;
+        // ================= ATTN: items it0 + k * grid; half hf of the CTA runs k = hf, hf + 2, ...
+        {
+            const int hf = warp >> 2;
+            bool ok = true;
+            for (long long k = hf;; k += 2) {
+                const long long i = it0 + k * gridDim.x;
+                if (i >= n_items) break;
+                AttnItem it;
+                attn_item(p, sm.pos, i, it);
+                if (k >= 2 && (tid & 127) == 0) attn_issue(p, &tmap, sm, it, il, hf);
                 unsigned long long *tp =
                     (p.trace && k == 0) ? p.trace + ((long long)il * STEP_PHASES + 8 + 16) * (gridDim.x + 1) : nullptr;
-                if (!attn_run<G>(p, L, sm, it, il, k & 1, apar, tp)) return;
-                if (k == 0) POINT(il, 1);
+                if (!attn_half<G>(p, L, sm, it, il, hf, apar, tp)) {
+                    ok = false;
+                    break;
+                }
             }
+            if (__syncthreads_or(!ok)) return;
         }
         if (has_next && tid < LD_WORDS) reinterpret_cast<uint32_t *>(sm.ldesc + ((il + 1) & 1))[tid] = ld_next;
         // attn_output tiles are static: request this CTA's first ones now. Its residual rows (x)
