@@ -90,6 +90,8 @@ SIGNATURES = {
     "bt_debug_topk": (C.c_int, [_P, C.c_uint32, C.c_uint32, _I32P, _F32P]),
     "bt_debug_hidden": (C.c_int, [_P, C.c_uint32, _F32P]),
     "bt_op_gemv": (C.c_int, [C.c_uint32, _P, C.c_uint32, C.c_uint32, _F32P, C.c_uint32, _F32P]),
+    # device pointers and a cudaStream_t, passed as integers
+    "bt_op_gemv_noalloc": (C.c_int, [C.c_uint32, _P, C.c_uint32, C.c_uint32, _P, C.c_uint32, _P, _P]),
     "bt_synth_tensor": (C.c_int, [C.c_uint32, C.c_uint64, C.c_uint64, C.c_uint64, C.c_uint64, C.c_float,
                                   C.c_float, _P]),
     "bt_tensor_id": (C.c_uint64, [C.c_char_p]),

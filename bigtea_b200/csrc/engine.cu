@@ -12,6 +12,7 @@
 #include <chrono>
 #include <map>
 #include <memory>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -1809,3 +1810,94 @@ extern "C" int bt_synth_tensor(uint32_t type, uint64_t rows, uint64_t cols, uint
 }
 
 extern "C" uint64_t bt_tensor_id(const char *name) { return name ? name_id(name) : 0; }
+
+// ------------------------------------------------------------------ allocation-free GEMV
+// bt_op_gemv on caller-owned device buffers, with no allocation of any kind: the tiled copy of
+// the weights and the error word live in a file-scope device array reserved when the module
+// loads. Layout of the array: [0, 256) the error word (zeroed by every call on its stream),
+// [256, BT_NOALLOC_SCRATCH_BYTES) the tiled matrix. One array per device, so calls on one
+// device must not overlap.
+static __device__ __align__(256) uint8_t g_noalloc_scratch[BT_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+constexpr int NOALLOC_MAX_DEVICES = 64;
+struct NoallocDevice {
+    uint8_t *scratch = nullptr;
+    int n_sm = 0;
+    bool ready = false;
+};
+NoallocDevice g_noalloc[NOALLOC_MAX_DEVICES];
+std::mutex g_noalloc_mu;
+}  // namespace
+
+extern "C" int bt_op_gemv_noalloc(uint32_t type, const void *w_dev, uint32_t rows, uint32_t cols, const float *x_dev,
+                                  uint32_t T, float *y_dev, void *stream) {
+    if (!w_dev || !x_dev || !y_dev || !rows || !cols || !T) return fail(BT_ERR_INVALID, "bad argument");
+    if (type != T_Q4_K && type != T_Q6_K)
+        return fail(BT_ERR_UNSUPPORTED, "bt_op_gemv_noalloc: the matrix must be Q4_K or Q6_K");
+    if (cols % 256 || cols / 256 > 32)
+        return fail(BT_ERR_UNSUPPORTED, "bt_op_gemv_noalloc: row length must be a multiple of 256 up to 8192");
+    const int rpt = default_rpt(cols);
+    const TileGeom g = tile_geom((int)type, rows, cols, rpt);
+    const unsigned long long need = 256ull + (unsigned long long)g.n_tiles * (unsigned long long)g.tile_bytes;
+    if (need > BT_NOALLOC_SCRATCH_BYTES)
+        return fail(BT_ERR_INVALID, "bt_op_gemv_noalloc: the tiled matrix needs " + std::to_string(need) +
+                                        " bytes of scratch; the static scratch holds " +
+                                        std::to_string(BT_NOALLOC_SCRATCH_BYTES) + " (BT_NOALLOC_SCRATCH_BYTES)");
+    int dev = 0;
+    CK(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= NOALLOC_MAX_DEVICES) return fail(BT_ERR_INVALID, "bt_op_gemv_noalloc: device ordinal too large");
+    NoallocDevice *nd = &g_noalloc[dev];
+    {
+        // one-time set-up on this device (the device is current): the scratch's address and the
+        // kernels' shared-memory limits
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        if (!nd->ready) {
+            void *p = nullptr;
+            CK(cudaGetSymbolAddress(&p, g_noalloc_scratch));
+            CK(init_kernel_attributes());
+            CK(cudaDeviceGetAttribute(&nd->n_sm, cudaDevAttrMultiProcessorCount, dev));
+            nd->scratch = reinterpret_cast<uint8_t *>(p);
+            nd->ready = true;
+        }
+    }
+    cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+    int *err = reinterpret_cast<int *>(nd->scratch);
+    uint8_t *tiled = nd->scratch + 256;
+    CK(cudaMemsetAsync(err, 0, sizeof(int), st));
+    CK(launch_repack((int)type, reinterpret_cast<const uint8_t *>(w_dev), rows, cols, rpt, tiled, 1, st));
+    GemvArgs a{};
+    a.seg[0].w = tiled;
+    a.seg[0].type = (int)type;
+    a.seg[0].nsb = g.nsb;
+    a.seg[0].rpt = g.rpt;
+    a.seg[0].S = g.S;
+    a.seg[0].tile_bytes = g.tile_bytes;
+    a.seg[0].rows = (int)rows;
+    a.seg[0].n_tiles = (int)g.n_tiles;
+    a.seg[0].tile0 = 0;
+    a.seg[0].out_off = 0;
+    a.nseg = 1;
+    a.total_tiles = (int)g.n_tiles;
+    a.x_stride = cols;
+    a.K = (int)cols;
+    a.y_stride = rows;
+    a.err = err;
+    a.slot_bytes = g.tile_bytes;
+    const int grid = g.n_tiles < nd->n_sm ? (int)g.n_tiles : nd->n_sm;
+    for (uint32_t t0 = 0; t0 < T; t0 += MAX_T) {
+        a.T = T - t0 < (uint32_t)MAX_T ? (int)(T - t0) : MAX_T;
+        a.x = x_dev + (size_t)t0 * cols;
+        a.y = y_dev + (size_t)t0 * rows;
+        a.nst = 1;
+        const size_t fixed = gemv_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes;
+        a.nst = pick_nst((size_t)a.slot_bytes, fixed);
+        CK(launch_gemv(a, grid, st, false));
+    }
+    int h_err = 0;
+    CK(cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st));
+    CK(cudaStreamSynchronize(st));
+    if (h_err & ERR_WAIT_TIMEOUT) return fail(BT_ERR_TIMEOUT, "bt_op_gemv_noalloc: a bounded device wait ran out");
+    if (h_err) return fail(BT_ERR_INVALID, "bt_op_gemv_noalloc: device error word " + std::to_string(h_err));
+    return BT_OK;
+}

@@ -162,6 +162,28 @@ int bt_debug_hidden(const bt_engine *e, uint32_t token, float *out);
 int bt_op_gemv(uint32_t type, const void *w_bytes, uint32_t rows, uint32_t cols, const float *x,
                uint32_t T, float *y);
 
+/* ---- allocation-free GEMV (no counterpart in the reference) ----
+ * bt_op_gemv on caller-owned DEVICE buffers that allocates nothing: no cudaMalloc, cudaFree,
+ * stream or event creation, and no allocating library call. It is for callers that cannot
+ * allocate inside a step: cudaMalloc and cudaFree synchronise the whole device, and they fail
+ * once the engine's weights and KV pool have reserved HBM, so a serving loop that owns the
+ * device's memory and overlaps work on several streams needs a call that only uses memory
+ * reserved up front. Its scratch is one file-scope device array of BT_NOALLOC_SCRATCH_BYTES
+ * per device, reserved when the library loads: a 256-byte header holding the error word (the
+ * call zeroes it on `stream` before its kernels; nothing else must start at zero) and the
+ * tiled copy of W. A matrix whose tiled copy does not fit (rows * cols/256 * block bytes >
+ * BT_NOALLOC_SCRATCH_BYTES - 256; e.g. the 151936 x 2048 Q6_K output head) is rejected with
+ * BT_ERR_INVALID before anything runs. Calls on one device share the scratch, so overlapping
+ * calls (other threads, or other streams without ordering) race: serialise them. The first
+ * call on a device does that device's set-up (the scratch's address, the kernels' shared-memory
+ * limits) with the device current; make it before any stream capture. The call waits for
+ * `stream` (a cudaStream_t, NULL for the legacy default stream) before it returns.
+ * w_dev: rows x cols GGUF bytes (Q4_K or Q6_K, row-major); x_dev: T x cols f32; y_dev: T x rows
+ * f32, y[t][r] = W[r,:] . x[t,:] with the same arithmetic as bt_op_gemv. */
+#define BT_NOALLOC_SCRATCH_BYTES (16u << 20)
+int bt_op_gemv_noalloc(uint32_t type, const void *w_dev, uint32_t rows, uint32_t cols, const float *x_dev, uint32_t T,
+                       float *y_dev, void *stream);
+
 /* ---- synthetic weights (seeded; same bytes on host and device) ---- */
 /* fill `out` (rows * row_bytes) with N(mean, sigma) values quantised to `type` */
 int bt_synth_tensor(uint32_t type, uint64_t rows, uint64_t cols, uint64_t seed, uint64_t tensor_id,
