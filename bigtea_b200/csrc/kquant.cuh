@@ -18,6 +18,7 @@
 #pragma once
 #include <cuda_fp16.h>
 #include <math.h>
+#include <stddef.h>
 #include <stdint.h>
 #include <string.h>
 
@@ -272,6 +273,8 @@ struct __align__(16) ActBlock {
     int16_t bs16[16];
 };
 static_assert(sizeof(ActBlock) == 336, "ActBlock layout");
+static_assert(offsetof(ActBlock, d) == 256 && offsetof(ActBlock, bs32) == 272 && offsetof(ActBlock, bs16) == 304,
+              "ActBlock field offsets");
 
 __device__ __forceinline__ int dp4a(int a, int b, int c) { return __dp4a(a, b, c); }
 // unsigned bytes of a times signed bytes of b, accumulated into c
@@ -282,28 +285,48 @@ __device__ __forceinline__ int dp4a_us(uint32_t a, int b, int c) {
 }
 __device__ __forceinline__ int byte_u(uint32_t w, int k) { return (int)((w >> (8 * k)) & 0xffu); }
 __device__ __forceinline__ int byte_s(uint32_t w, int k) { return (int)(int8_t)((w >> (8 * k)) & 0xffu); }
-__device__ __forceinline__ int comp(const int4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
 
-// C4 for one Q4_K superblock (slot s of a tile in shared memory) against one activation block:
-// sumi = sum_j sc_j * (q . a over sub-block j), summ = sum_j m_j * bs32_j (integers, so the
-// grouping below gives the same values as any other order), then
+// Shared-memory loads at 32-bit shared-window addresses. The dots below take such addresses,
+// so a non-inlined copy of them still reads shared memory with shared loads. The "memory"
+// clobber keeps them after the waits that make the data valid.
+__device__ __forceinline__ uint4 lds_u4(uint32_t a) {
+    uint4 v;
+    asm volatile("ld.shared.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ float lds_f32(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a) : "memory");
+    return v;
+}
+__device__ __forceinline__ uint16_t lds_u16(uint32_t a) {
+    unsigned short v;
+    asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a) : "memory");
+    return v;
+}
+// ActBlock field offsets, for the address-based dots
+constexpr uint32_t ACT_D = 256, ACT_BS32 = 272, ACT_BS16 = 304;
+
+// C4 for one Q4_K superblock (slot s of a tile at shared address tile_s, S slots) against the
+// activation block at act_s: sumi = sum_j sc_j * (q . a over sub-block j), summ = sum_j m_j *
+// bs32_j (integers, so the grouping below gives the same values as any other order), then
 // (float)sumi * (d * d_a) - (float)summ * (dmin * d_a). High nibbles enter the dot unshifted
 // (unsigned x signed dp4a) and the exact multiple of 16 is shifted out afterwards.
-__device__ __forceinline__ float q4k_slot_dot(const uint8_t *tile, int S, int s, const ActBlock &a) {
-    const uint4 *base = reinterpret_cast<const uint4 *>(tile) + s;
-    const uint4 h = base[0];
+__device__ __forceinline__ float q4k_dot_s(uint32_t tile_s, int S, int s, uint32_t act_s) {
+    const uint32_t base = tile_s + (uint32_t)s * 16u, cstride = (uint32_t)S * 16u;
+    const uint4 h = lds_u4(base);
     const float dw = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffff)));
     const float dminw = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
     const uint32_t s03 = h.y, s47 = h.z, s811 = h.w;  // the 12 packed scale bytes (get_scale_min_k4)
     const uint32_t sc_lo = s03 & 0x3F3F3F3Fu, m_lo = s47 & 0x3F3F3F3Fu;
     const uint32_t sc_hi = (s811 & 0x0F0F0F0Fu) | ((s03 >> 2) & 0x30303030u);
     const uint32_t m_hi = ((s811 >> 4) & 0x0F0F0F0Fu) | ((s47 >> 2) & 0x30303030u);
-    const int4 *aq = reinterpret_cast<const int4 *>(a.qs);
     int dot[8];
 #pragma unroll
     for (int g = 0; g < 4; g++) {
-        const uint4 w0 = base[(1 + 2 * g) * S], w1 = base[(2 + 2 * g) * S];
-        const int4 al0 = aq[4 * g + 0], al1 = aq[4 * g + 1], ah0 = aq[4 * g + 2], ah1 = aq[4 * g + 3];
+        const uint4 w0 = lds_u4(base + (1 + 2 * g) * cstride), w1 = lds_u4(base + (2 + 2 * g) * cstride);
+        const uint4 al0 = lds_u4(act_s + 64 * g), al1 = lds_u4(act_s + 64 * g + 16);
+        const uint4 ah0 = lds_u4(act_s + 64 * g + 32), ah1 = lds_u4(act_s + 64 * g + 48);
         int dlo = 0, dhi = 0;
         dlo = dp4a(w0.x & 0x0F0F0F0F, al0.x, dlo);
         dlo = dp4a(w0.y & 0x0F0F0F0F, al0.y, dlo);
@@ -324,8 +347,8 @@ __device__ __forceinline__ float q4k_slot_dot(const uint8_t *tile, int S, int s,
         dot[2 * g] = dlo;
         dot[2 * g + 1] = dhi >> 4;
     }
-    const int4 b0 = *reinterpret_cast<const int4 *>(a.bs32), b1 = *reinterpret_cast<const int4 *>(a.bs32 + 4);
-    const int bs[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+    const uint4 b0 = lds_u4(act_s + ACT_BS32), b1 = lds_u4(act_s + ACT_BS32 + 16);
+    const int bs[8] = {(int)b0.x, (int)b0.y, (int)b0.z, (int)b0.w, (int)b1.x, (int)b1.y, (int)b1.z, (int)b1.w};
     int sumi = 0, summ = 0;
 #pragma unroll
     for (int j = 0; j < 8; j++) {
@@ -334,9 +357,10 @@ __device__ __forceinline__ float q4k_slot_dot(const uint8_t *tile, int S, int s,
         sumi += sc * dot[j];
         summ += m * bs[j];
     }
-    const float t1 = __fmul_rn(dw, a.d);
+    const float da = lds_f32(act_s + ACT_D);
+    const float t1 = __fmul_rn(dw, da);
     const float t2 = __fmul_rn(__int2float_rn(sumi), t1);
-    const float t3 = __fmul_rn(dminw, a.d);
+    const float t3 = __fmul_rn(dminw, da);
     const float t4 = __fmul_rn(__int2float_rn(summ), t3);
     return __fsub_rn(t2, t4);
 }
@@ -346,28 +370,30 @@ __device__ __forceinline__ float q4k_slot_dot(const uint8_t *tile, int S, int s,
 // equal to the per-value form), then (float)sumi * (d * d_a). Value v of the superblock:
 // n = v / 128, quad = (v % 128) / 32, l = v % 32; low nibble from ql[64n + 32 * (quad & 1) + l]
 // (high nibble when quad >= 2), two high bits from qh[32n + l] >> 2 * quad; sub-block v / 16.
-__device__ __forceinline__ float q6k_slot_dot(const uint8_t *tile, int S, int s, const ActBlock &a) {
-    const uint4 *base = reinterpret_cast<const uint4 *>(tile) + s;
-    const uint16_t dbits = *reinterpret_cast<const uint16_t *>(tile + 13 * S * 16 + 2 * s);
+// In the tile: chunks 0-7 ql, 8-11 qh, 12 the scales, and d in a plane after chunk row 12.
+__device__ __forceinline__ float q6k_dot_s(uint32_t tile_s, int S, int s, uint32_t act_s) {
+    const uint32_t base = tile_s + (uint32_t)s * 16u, cstride = (uint32_t)S * 16u;
+    const uint16_t dbits = lds_u16(tile_s + 13u * cstride + 2u * (uint32_t)s);
     const float dw = __half2float(__ushort_as_half(dbits));
-    const uint4 scv = base[12 * S];  // the 16 int8 sub-block scales
+    const uint4 scv = lds_u4(base + 12u * cstride);  // the 16 int8 sub-block scales
     const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
-    const int4 *aq = reinterpret_cast<const int4 *>(a.qs);
-    const int4 bq0 = *reinterpret_cast<const int4 *>(a.bs16), bq1 = *reinterpret_cast<const int4 *>(a.bs16 + 8);
-    const uint32_t bsw[8] = {(uint32_t)bq0.x, (uint32_t)bq0.y, (uint32_t)bq0.z, (uint32_t)bq0.w,
-                             (uint32_t)bq1.x, (uint32_t)bq1.y, (uint32_t)bq1.z, (uint32_t)bq1.w};
+    const uint4 bq0 = lds_u4(act_s + ACT_BS16), bq1 = lds_u4(act_s + ACT_BS16 + 16);
+    const uint32_t bsw[8] = {bq0.x, bq0.y, bq0.z, bq0.w, bq1.x, bq1.y, bq1.z, bq1.w};
     int sumi = 0;
 #pragma unroll
     for (int n = 0; n < 2; n++) {
-        const uint4 qa0 = base[(4 * n + 0) * S], qa1 = base[(4 * n + 1) * S];  // ql bytes 64n .. 64n+31
-        const uint4 qb0 = base[(4 * n + 2) * S], qb1 = base[(4 * n + 3) * S];  // ql bytes 64n+32 .. 64n+63
-        const uint4 hh0 = base[(8 + 2 * n) * S], hh1 = base[(9 + 2 * n) * S];  // qh bytes 32n .. 32n+31
+        const uint4 qa0 = lds_u4(base + (4 * n + 0) * cstride), qa1 = lds_u4(base + (4 * n + 1) * cstride);
+        const uint4 qb0 = lds_u4(base + (4 * n + 2) * cstride), qb1 = lds_u4(base + (4 * n + 3) * cstride);
+        const uint4 hh0 = lds_u4(base + (8 + 2 * n) * cstride), hh1 = lds_u4(base + (9 + 2 * n) * cstride);
         const uint32_t wa[8] = {qa0.x, qa0.y, qa0.z, qa0.w, qa1.x, qa1.y, qa1.z, qa1.w};
         const uint32_t wb[8] = {qb0.x, qb0.y, qb0.z, qb0.w, qb1.x, qb1.y, qb1.z, qb1.w};
         const uint32_t wh[8] = {hh0.x, hh0.y, hh0.z, hh0.w, hh1.x, hh1.y, hh1.z, hh1.w};
 #pragma unroll
         for (int hf = 0; hf < 2; hf++) {  // l = 16 hf .. 16 hf + 15: sub-blocks 8n + 2 quad + hf
-            const int4 A0 = aq[8 * n + 0 + hf], A1 = aq[8 * n + 2 + hf], A2 = aq[8 * n + 4 + hf], A3 = aq[8 * n + 6 + hf];
+            const uint4 A0 = lds_u4(act_s + 16 * (8 * n + 0 + hf)), A1 = lds_u4(act_s + 16 * (8 * n + 2 + hf));
+            const uint4 A2 = lds_u4(act_s + 16 * (8 * n + 4 + hf)), A3 = lds_u4(act_s + 16 * (8 * n + 6 + hf));
+            const uint32_t a0[4] = {A0.x, A0.y, A0.z, A0.w}, a1[4] = {A1.x, A1.y, A1.z, A1.w};
+            const uint32_t a2[4] = {A2.x, A2.y, A2.z, A2.w}, a3[4] = {A3.x, A3.y, A3.z, A3.w};
             int acc0 = 0, acc1 = 0, acc2 = 0, acc3 = 0;
 #pragma unroll
             for (int i = 0; i < 4; i++) {
@@ -377,10 +403,10 @@ __device__ __forceinline__ float q6k_slot_dot(const uint8_t *tile, int S, int s,
                 const uint32_t u2 = (wb[l4] & 0x0F0F0F0Fu) | ((hq << 2) & 0x30303030u);
                 const uint32_t u3 = ((wa[l4] >> 4) & 0x0F0F0F0Fu) | (hq & 0x30303030u);
                 const uint32_t u4 = ((wb[l4] >> 4) & 0x0F0F0F0Fu) | ((hq >> 2) & 0x30303030u);
-                acc0 = dp4a_us(u1, comp(A0, i), acc0);
-                acc1 = dp4a_us(u2, comp(A1, i), acc1);
-                acc2 = dp4a_us(u3, comp(A2, i), acc2);
-                acc3 = dp4a_us(u4, comp(A3, i), acc3);
+                acc0 = dp4a_us(u1, (int)a0[i], acc0);
+                acc1 = dp4a_us(u2, (int)a1[i], acc1);
+                acc2 = dp4a_us(u3, (int)a2[i], acc2);
+                acc3 = dp4a_us(u4, (int)a3[i], acc3);
             }
             const int accs[4] = {acc0, acc1, acc2, acc3};
 #pragma unroll
@@ -392,7 +418,15 @@ __device__ __forceinline__ float q6k_slot_dot(const uint8_t *tile, int S, int s,
             }
         }
     }
-    return __fmul_rn(__int2float_rn(sumi), __fmul_rn(dw, a.d));
+    return __fmul_rn(__int2float_rn(sumi), __fmul_rn(dw, lds_f32(act_s + ACT_D)));
+}
+
+// The same dots on generic pointers into shared memory.
+__device__ __forceinline__ float q4k_slot_dot(const uint8_t *tile, int S, int s, const ActBlock &a) {
+    return q4k_dot_s((uint32_t)__cvta_generic_to_shared(tile), S, s, (uint32_t)__cvta_generic_to_shared(&a));
+}
+__device__ __forceinline__ float q6k_slot_dot(const uint8_t *tile, int S, int s, const ActBlock &a) {
+    return q6k_dot_s((uint32_t)__cvta_generic_to_shared(tile), S, s, (uint32_t)__cvta_generic_to_shared(&a));
 }
 
 #endif  // __CUDACC__

@@ -54,6 +54,8 @@ struct StepSmem {
     float *misc;         // 64 floats
     int *pos;            // [STEP_MAX_T]
     int *blkn;           // [STEP_MAX_T] the cache block of each token's new position
+    int *seq;            // [STEP_MAX_T] each token's sequence
+    int *iblk;           // [2][ATTN_CHUNK / 16] page ids of this CTA's first two attention items
     LayerDev *ldesc;     // [2] this layer's and the next layer's descriptors
     QMatDev *outd;       // the output head's descriptor
     int *sel_ids;        // [STEP_MAX_T][MAX_K]
@@ -114,15 +116,15 @@ struct WarpRing {
     int nst, slot_bytes, issued, done;
 
     // A phase's first use of the ring: the region may hold values written by the generic proxy
-    // (attention's appended row, normalised router inputs, embedding rows), so the issuing lane
-    // orders those before its bulk copies. Within a phase a slot is only read before it is
+    // (attention's appended row, normalised router inputs, embedding rows), so the issuing lanes
+    // order those before their bulk copies. Within a phase a slot is only read before it is
     // refilled, and the warp's own __syncwarp orders that.
     __device__ void configure(int sbytes) {
         slot_bytes = sbytes;
         nst = (STEP_REGION_BYTES / STEP_WARPS) / sbytes;
         nst = nst > RING_SLOTS ? RING_SLOTS : nst;
         issued = done = 0;
-        if ((threadIdx.x & 31) == 0) fence_proxy_async();
+        fence_proxy_async();
     }
     __device__ uint8_t *slot_ptr(int j) const { return base + (size_t)(j % nst) * slot_bytes; }
     __device__ uint64_t *slot_bar(int j) const { return bars + (j % nst); }
@@ -147,20 +149,17 @@ __device__ __forceinline__ int warp_units(long long u0, long long u1, int warp) 
 
 // ------------------------------------------------------------------ shared code
 // The step runs each phase once per layer and the whole layer's code does not fit the
-// instruction caches, so every instruction a phase executes is fetched again from L2 in the
-// next layer. Code that several phases run is therefore kept in one non-inlined copy: the
-// K-quant slot dots, the Q8_K block quantiser, the staging and the GEMV consumer.
+// instruction caches, so every instruction a phase executes is fetched again in the next
+// layer. Code that several phases run is therefore kept in one non-inlined copy: the K-quant
+// slot dots (their loads are explicit shared-memory loads at 32-bit addresses), the Q8_K block
+// quantiser and the staging.
 __device__ __noinline__ float dot_q4k(uint32_t tile_s, int S, int s, uint32_t act_s) {
-    const uint8_t *tile = reinterpret_cast<const uint8_t *>(__cvta_shared_to_generic(tile_s));
-    const ActBlock *a = reinterpret_cast<const ActBlock *>(__cvta_shared_to_generic(act_s));
-    return q4k_slot_dot(tile, S, s, *a);
+    return q4k_dot_s(tile_s, S, s, act_s);
 }
 __device__ __noinline__ float dot_q6k(uint32_t tile_s, int S, int s, uint32_t act_s) {
-    const uint8_t *tile = reinterpret_cast<const uint8_t *>(__cvta_shared_to_generic(tile_s));
-    const ActBlock *a = reinterpret_cast<const ActBlock *>(__cvta_shared_to_generic(act_s));
-    return q6k_slot_dot(tile, S, s, *a);
+    return q6k_dot_s(tile_s, S, s, act_s);
 }
-// slot s of a tile (tile_s, S slots) against the activation block at act_s
+// slot s of a tile (tile, S slots) against the activation block at act
 __device__ __forceinline__ float slot_dot(bool q4, const uint8_t *tile, int S, int s, const ActBlock *act) {
     return q4 ? dot_q4k(smem_u32(tile), S, s, smem_u32(act)) : dot_q6k(smem_u32(tile), S, s, smem_u32(act));
 }
@@ -414,37 +413,36 @@ __device__ __forceinline__ bool gemv_run(WarpRing &r, const SegList &s, const Ac
 __device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, long long u0, int warp,
                              int lane) {
     const int j = r.issued;
-    if (lane == 0) {
-        const long long u = u0 + warp + (long long)j * STEP_WARPS;
-        const int tile = (int)(u % L.gate.n_tiles);
-        const int tk = (int)(u / L.gate.n_tiles);
-        const int e = sm.sel_ids[(tk / K) * MAX_K + tk % K];
-        uint8_t *dst = r.slot_ptr(j);
-        const uint64_t pol = l2_evict_first_policy();
-        mbar_arrive_expect_tx(r.slot_bar(j), L.gate.tile_bytes + L.up.tile_bytes);
-        bulk_g2s_hint(dst, L.gate.w + e * L.gate.mat_bytes + (long long)tile * L.gate.tile_bytes, L.gate.tile_bytes,
-                      r.slot_bar(j), pol);
-        bulk_g2s_hint(dst + L.gate.tile_bytes, L.up.w + e * L.up.mat_bytes + (long long)tile * L.up.tile_bytes,
-                      L.up.tile_bytes, r.slot_bar(j), pol);
+    const long long u = u0 + warp + (long long)j * STEP_WARPS;
+    const int tile = (int)(u % L.gate.n_tiles);
+    const int tk = (int)(u / L.gate.n_tiles);
+    const int e = sm.sel_ids[(tk / K) * MAX_K + tk % K];
+    uint8_t *dst = r.slot_ptr(j);
+    if (lane == 0) mbar_arrive_expect_tx(r.slot_bar(j), L.gate.tile_bytes + L.up.tile_bytes);
+    __syncwarp();
+    if (lane < 2) {  // lane 0 the gate tile, lane 1 the up tile
+        const QMatDev &m = lane ? L.up : L.gate;
+        bulk_g2s_hint(dst + lane * L.gate.tile_bytes, m.w + e * m.mat_bytes + (long long)tile * m.tile_bytes,
+                      m.tile_bytes, r.slot_bar(j), l2_evict_first_policy());
     }
     r.issued++;
 }
 
+// one unit of the down phase: output row `row` of token t from every selected expert (lane k
+// issues expert k's row)
 __device__ void down_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int E, long long u0, int warp,
                            int lane) {
     const int j = r.issued;
-    if (lane == 0) {
-        const long long u = u0 + warp + (long long)j * STEP_WARPS;
-        const int row = (int)(u % E), t = (int)(u / E);
-        uint8_t *dst = r.slot_ptr(j);
-        const uint64_t pol = l2_evict_first_policy();
-        mbar_arrive_expect_tx(r.slot_bar(j), K * L.down.tile_bytes);
-        for (int k = 0; k < K; k++) {
-            const int e = sm.sel_ids[t * MAX_K + k];
-            bulk_g2s_hint(dst + k * L.down.tile_bytes,
-                          L.down.w + e * L.down.mat_bytes + (long long)row * L.down.tile_bytes, L.down.tile_bytes,
-                          r.slot_bar(j), pol);
-        }
+    const long long u = u0 + warp + (long long)j * STEP_WARPS;
+    const int row = (int)(u % E), t = (int)(u / E);
+    uint8_t *dst = r.slot_ptr(j);
+    if (lane == 0) mbar_arrive_expect_tx(r.slot_bar(j), K * L.down.tile_bytes);
+    __syncwarp();
+    if (lane < K) {
+        const int e = sm.sel_ids[t * MAX_K + lane];
+        bulk_g2s_hint(dst + lane * L.down.tile_bytes,
+                      L.down.w + e * L.down.mat_bytes + (long long)row * L.down.tile_bytes, L.down.tile_bytes,
+                      r.slot_bar(j), l2_evict_first_policy());
     }
     r.issued++;
 }
@@ -476,22 +474,24 @@ __device__ __forceinline__ long long attn_items(const StepArgs &p, const int *po
     return n;
 }
 
-// the TMA loads of one item's K and V pages into tile buffer `buf` (thread 0)
-__device__ void attn_issue(const StepArgs &p, const CUtensorMap *tmap, const StepSmem &sm, const AttnItem &it,
-                           int layer, int buf) {
-    const int seq = p.seq_of[it.t];
+// The TMA loads of one item's K and V pages into tile buffer `buf`, issued by one warp (lane l
+// takes pages l, l+32, ...). `blk_s` holds the item's page ids in shared memory (a CTA's first
+// two items, staged once per step), or is null and the ids come from the block table.
+__device__ void attn_issue_warp(const StepArgs &p, const CUtensorMap *tmap, const StepSmem &sm, const AttnItem &it,
+                                int layer, int buf, const int *blk_s, int lane) {
     const int nk = sm.pos[it.t] + 1, base = it.c * ATTN_CHUNK;
     const int cnt = nk - base < ATTN_CHUNK ? nk - base : ATTN_CHUNK;
     const int npages = (cnt + 15) / 16;
     uint8_t *K0 = sm.region + buf * ATTN_BUF, *K1 = K0 + 16384, *V0 = K0 + 32768, *V1 = K0 + 49152;
     uint64_t *bar = sm.attn_bar + buf;
+    if (lane == 0) mbar_arrive_expect_tx(bar, npages * 8192);
+    __syncwarp();
     const uint64_t pol = l2_evict_first_policy();
-    fence_proxy_async();
-    mbar_arrive_expect_tx(bar, npages * 8192);
-    for (int pg = 0; pg < npages; pg++) {
-        const int blk = p.block_table[seq * p.max_blocks + (base >> 4) + pg];
+    for (int pg = lane; pg < npages; pg += 32) {
+        const int blk = blk_s ? blk_s[pg] : p.block_table[sm.seq[it.t] * p.max_blocks + (base >> 4) + pg];
         const int rowK = (int)(((((long long)layer * p.n_blocks + blk) * 2 + 0) * p.HK + it.g) * 16);
         const int rowV = rowK + p.HK * 16;
+        fence_proxy_async();
         tma_load_2d_hint(K0 + pg * 2048, tmap, 0, rowK, bar, pol);
         tma_load_2d_hint(K1 + pg * 2048, tmap, 64, rowK, bar, pol);
         tma_load_2d_hint(V0 + pg * 2048, tmap, 0, rowV, bar, pol);
@@ -861,6 +861,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
     sm.misc = sm.normS + STEP_MAX_T;
     sm.pos = reinterpret_cast<int *>(sm.misc + 64);
     sm.blkn = sm.pos + STEP_MAX_T;
+    sm.seq = sm.blkn + STEP_MAX_T;
+    sm.iblk = sm.seq + STEP_MAX_T;
     sm.ldesc = reinterpret_cast<LayerDev *>(smem + 1024);
     sm.outd = reinterpret_cast<QMatDev *>(smem + 1024 + 2 * sizeof(LayerDev));
     sm.region = smem + 2048;
@@ -913,6 +915,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
     if (tid < T) {
         const int seq = p.seq_of[tid], ps = p.dev_len[seq];
         sm.pos[tid] = ps;
+        sm.seq[tid] = seq;
         sm.blkn[tid] = p.block_table[seq * p.max_blocks + ps / 16];
     }
     if (tid < LD_WORDS)
@@ -921,6 +924,23 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
     fence_mbar_init();
     __syncthreads();
     uint32_t apar = 0, xpar = 0;  // next parities of attn_bar[0..1] and aux_bar[0..1]
+    {
+        // the page ids of this CTA's first two attention items: the same in every layer
+        constexpr int PPI = ATTN_CHUNK / 16;
+        const long long n_it = attn_items(p, sm.pos);
+        if (tid < 2 * PPI) {
+            const int k = tid / PPI, pg = tid % PPI;
+            const long long i = blockIdx.x + (long long)k * gridDim.x;
+            int blk = 0;
+            if (i < n_it) {
+                AttnItem it;
+                attn_item(p, sm.pos, i, it);
+                const int nk = sm.pos[it.t] + 1, base = it.c * ATTN_CHUNK;
+                if (base + pg * 16 < nk) blk = p.block_table[sm.seq[it.t] * p.max_blocks + (base >> 4) + pg];
+            }
+            sm.iblk[tid] = blk;
+        }
+    }
     if (tid == 0) {
         prefetch_tmap(&tmap);
         // layer 0's attn_norm for the first staging
@@ -1008,13 +1028,12 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         const long long it0 = blockIdx.x;
         const long long n_items = attn_items(p, sm.pos);
         __syncthreads();
-        if (tid == 0) {
-            for (int k = 0; k < 2; k++) {
-                const long long i = it0 + (long long)k * gridDim.x;
-                if (i >= n_items) break;
+        if (warp < 2) {  // warp k issues item k's pages
+            const long long i = it0 + (long long)warp * gridDim.x;
+            if (i < n_items) {
                 AttnItem it;
                 attn_item(p, sm.pos, i, it);
-                attn_issue(p, &tmap, sm, it, il, k);
+                attn_issue_warp(p, &tmap, sm, it, il, warp, sm.iblk + warp * (ATTN_CHUNK / 16), lane);
             }
         }
         if (!grid_sync(p.bar, epoch, p.err, TR(il, 0))) return;
@@ -1027,7 +1046,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                 if (i >= n_items) break;
                 AttnItem it;
                 attn_item(p, sm.pos, i, it);
-                if (k >= 2 && (tid & 127) == 0) attn_issue(p, &tmap, sm, it, il, hf);
+                if (k >= 2 && (tid & 127) < 32) attn_issue_warp(p, &tmap, sm, it, il, hf, nullptr, lane);
                 unsigned long long *tp =
                     (p.trace && k == 0) ? p.trace + ((long long)il * STEP_PHASES + 8 + 16) * (gridDim.x + 1) : nullptr;
                 if (!attn_half<G>(p, L, sm, it, il, hf, apar, tp)) {
