@@ -83,7 +83,7 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // __syncthreads and waits with relaxed polls followed by one acquire fence. The wait is
 // bounded: a timeout sets the engine's error word, after which every CTA leaves at its next
 // barrier.
-__device__ bool grid_sync(unsigned *bar, unsigned &epoch, int *err, unsigned long long *trace_row = nullptr) {
+__device__ __noinline__ bool grid_sync(unsigned *bar, unsigned &epoch, int *err, unsigned long long *trace_row = nullptr) {
     __syncthreads();
     epoch += 1;
     if (threadIdx.x == 0) {
@@ -139,11 +139,13 @@ struct WarpRing {
 };
 
 // ------------------------------------------------------------------ unit ranges
-__device__ __forceinline__ void cta_range(long long total, long long &u0, long long &u1) {
-    u0 = (long long)blockIdx.x * total / gridDim.x;
-    u1 = (long long)(blockIdx.x + 1) * total / gridDim.x;
+// 32-bit unit arithmetic: unit counts stay far below 2^32 / gridDim.x (a 64-bit division is a
+// long instruction sequence, and these run per unit)
+__device__ __forceinline__ void cta_range(int total, int &u0, int &u1) {
+    u0 = (int)((unsigned)blockIdx.x * (unsigned)total / gridDim.x);
+    u1 = (int)((unsigned)(blockIdx.x + 1) * (unsigned)total / gridDim.x);
 }
-__device__ __forceinline__ int warp_units(long long u0, long long u1, int warp) {
+__device__ __forceinline__ int warp_units(int u0, int u1, int warp) {
     return (u1 - u0 > warp) ? (int)((u1 - u0 - warp + STEP_WARPS - 1) / STEP_WARPS) : 0;
 }
 
@@ -280,7 +282,7 @@ __device__ __forceinline__ SegList make_segs(const QMatDev *a, int oa, const QMa
     return s;
 }
 
-__device__ __forceinline__ int seg_of(const SegList &s, long long u) {
+__device__ __forceinline__ int seg_of(const SegList &s, int u) {
     int si = 0;
     if (s.n > 1 && u >= s.tile0[1]) si = 1;
     if (s.n > 2 && u >= s.tile0[2]) si = 2;
@@ -293,10 +295,10 @@ __device__ __forceinline__ int seglist_max_tile(const SegList &s) {
     return m;
 }
 
-__device__ void gemv_issue(WarpRing &r, const SegList &s, long long u0, int warp, int lane) {
+__device__ void gemv_issue(WarpRing &r, const SegList &s, int u0, int warp, int lane) {
     const int j = r.issued;
     if (lane == 0) {
-        const long long u = u0 + warp + (long long)j * STEP_WARPS;
+        const int u = u0 + warp + j * STEP_WARPS;
         const int si = seg_of(s, u);
         const QMatDev &m = *s.m[si];
         const uint8_t *src = m.w + (u - s.tile0[si]) * (long long)m.tile_bytes;
@@ -307,7 +309,7 @@ __device__ void gemv_issue(WarpRing &r, const SegList &s, long long u0, int warp
 }
 
 __device__ void gemv_preissue(WarpRing &r, const SegList &s, int warp, int lane) {
-    long long u0, u1;
+    int u0, u1;
     cta_range(s.total, u0, u1);
     const int n = warp_units(u0, u1, warp);
     r.configure(seglist_max_tile(s));
@@ -322,7 +324,7 @@ __device__ __forceinline__ bool gemv_run(WarpRing &r, const SegList &s, const Ac
                                          unsigned long long *amax, int *err, int warp, int lane,
                                          unsigned long long *cyc = nullptr) {
     long long cw = 0, cc0 = clock64();
-    long long u0, u1;
+    int u0, u1;
     cta_range(s.total, u0, u1);
     const int n = warp_units(u0, u1, warp);
     int sS[3], snsb[3], srpt[3], srows[3], soff[3];
@@ -349,7 +351,7 @@ __device__ __forceinline__ bool gemv_run(WarpRing &r, const SegList &s, const Ac
             break;
         }
         cw += clock64() - w0;
-        const long long u = u0 + warp + (long long)j * STEP_WARPS;
+        const int u = u0 + warp + j * STEP_WARPS;
         const int si = seg_of(s, u);
         const int mS = si == 0 ? sS[0] : si == 1 ? sS[1] : sS[2];
         const int mnsb = si == 0 ? snsb[0] : si == 1 ? snsb[1] : snsb[2];
@@ -358,10 +360,10 @@ __device__ __forceinline__ bool gemv_run(WarpRing &r, const SegList &s, const Ac
         const int off = si == 0 ? soff[0] : si == 1 ? soff[1] : soff[2];
         const bool q4 = si == 0 ? sq4[0] : si == 1 ? sq4[1] : sq4[2];
         const uint8_t *tile = r.slot_ptr(j);
-        const long long tl = u - s.tile0[si];
+        const int tl = u - s.tile0[si];
         const bool active = lane < mS;
         const int rit = active ? lane / mnsb : 0, b = active ? lane - rit * mnsb : 0;
-        const long long row = tl * mrpt + rit;
+        const int row = tl * mrpt + rit;
         const bool writer = active && b == 0 && row < mrows;
         for (int t = 0; t < T; t++) {
             float v = 0.0f;
@@ -372,9 +374,9 @@ __device__ __forceinline__ bool gemv_run(WarpRing &r, const SegList &s, const Ac
                 acc = __fadd_rn(acc, __shfl_sync(FULL, v, srcl < 32 ? srcl : 31));
             }
             if (writer) {
-                const long long o = off + row;
+                const int o = off + row;
                 float val = acc;
-                if (res) val = __fadd_rn(res[t * res_ld + (int)(o - res_row0)], acc);
+                if (res) val = __fadd_rn(res[t * res_ld + (o - res_row0)], acc);
                 y[t * ys + o] = val;
                 if (amax) {
                     const unsigned long long key =
@@ -410,12 +412,11 @@ __device__ __forceinline__ bool gemv_run(WarpRing &r, const SegList &s, const Ac
 }
 
 // ------------------------------------------------------------------ expert phases
-__device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, long long u0, int warp,
+__device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int u0, int warp,
                              int lane) {
     const int j = r.issued;
-    const long long u = u0 + warp + (long long)j * STEP_WARPS;
-    const int tile = (int)(u % L.gate.n_tiles);
-    const int tk = (int)(u / L.gate.n_tiles);
+    const int u = u0 + warp + j * STEP_WARPS;
+    const int tk = u / L.gate.n_tiles, tile = u - tk * L.gate.n_tiles;
     const int e = sm.sel_ids[(tk / K) * MAX_K + tk % K];
     uint8_t *dst = r.slot_ptr(j);
     if (lane == 0) mbar_arrive_expect_tx(r.slot_bar(j), L.gate.tile_bytes + L.up.tile_bytes);
@@ -430,11 +431,11 @@ __device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm,
 
 // one unit of the down phase: output row `row` of token t from every selected expert (lane k
 // issues expert k's row)
-__device__ void down_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int E, long long u0, int warp,
+__device__ void down_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int E, int u0, int warp,
                            int lane) {
     const int j = r.issued;
-    const long long u = u0 + warp + (long long)j * STEP_WARPS;
-    const int row = (int)(u % E), t = (int)(u / E);
+    const int u = u0 + warp + j * STEP_WARPS;
+    const int t = u / E, row = u - t * E;
     uint8_t *dst = r.slot_ptr(j);
     if (lane == 0) mbar_arrive_expect_tx(r.slot_bar(j), K * L.down.tile_bytes);
     __syncwarp();
@@ -453,14 +454,14 @@ struct AttnItem {
 };
 
 // item i of the step's attention work: tokens in order, kv heads, chunks
-__device__ __forceinline__ bool attn_item(const StepArgs &p, const int *pos, long long i, AttnItem &it) {
+__device__ __forceinline__ bool attn_item(const StepArgs &p, const int *pos, int i, AttnItem &it) {
     for (int t = 0; t < p.T; t++) {
-        const int nc = (pos[t] + 1 + ATTN_CHUNK - 1) / ATTN_CHUNK;
-        const long long cnt = (long long)p.HK * nc;
+        const int nc = (pos[t] + ATTN_CHUNK) / ATTN_CHUNK;
+        const int cnt = p.HK * nc;
         if (i < cnt) {
             it.t = t;
-            it.g = (int)(i / nc);
-            it.c = (int)(i % nc);
+            it.g = i / nc;
+            it.c = i - it.g * nc;
             return true;
         }
         i -= cnt;
@@ -468,9 +469,9 @@ __device__ __forceinline__ bool attn_item(const StepArgs &p, const int *pos, lon
     return false;
 }
 
-__device__ __forceinline__ long long attn_items(const StepArgs &p, const int *pos) {
-    long long n = 0;
-    for (int t = 0; t < p.T; t++) n += (long long)p.HK * ((pos[t] + 1 + ATTN_CHUNK - 1) / ATTN_CHUNK);
+__device__ __forceinline__ int attn_items(const StepArgs &p, const int *pos) {
+    int n = 0;
+    for (int t = 0; t < p.T; t++) n += p.HK * ((pos[t] + ATTN_CHUNK) / ATTN_CHUNK);
     return n;
 }
 
@@ -805,39 +806,41 @@ __device__ bool attn_half(const StepArgs &p, const LayerDev &L, const StepSmem &
 }
 
 // One head's merge of its chunk partials (C8): M = max m_c, f_c = exp(m_c - M),
-// L = sum_c l_c f_c and O = sum_c acc_c f_c in chunk order, out = O / L. Threads < 128 load their
-// dimension's partials (64 chunks at a time) in the same round trip as the m/l loads of threads
-// >= 128.
-__device__ void combine_head(const float *part, long long cstride, int nc, float *out, float *cbuf, float *misc) {
+// L = sum_c l_c f_c and O = sum_c acc_c f_c in chunk order, out = O / L. Threads < 128 load
+// their dimension's first 64 partials in the same round trip as the m/l loads of threads >= 128.
+__device__ void combine_head(const float *part, int cstride, int nc, float *out, float *cbuf, float *misc) {
     const int tid = threadIdx.x;
     float *cm = cbuf, *cl = cm + nc, *cf = cl + nc;
     constexpr int B = 64;
+    const float *pd = part + tid;
     float a[B];
-    float O = 0.0f;
-    for (int c0 = 0; c0 < nc; c0 += B) {
-        if (tid < 128) {
+    auto load = [&](int c0) {
 #pragma unroll
-            for (int kk = 0; kk < B; kk++)
-                a[kk] = c0 + kk < nc ? __ldcg(part + (long long)(c0 + kk) * cstride + tid) : 0.0f;
+        for (int kk = 0; kk < B; kk++) a[kk] = c0 + kk < nc ? __ldcg(pd + (c0 + kk) * cstride) : 0.0f;
+    };
+    if (tid < 128) {
+        load(0);
+    } else {
+        for (int cc = tid - 128; cc < nc; cc += STEP_THREADS - 128) {
+            cm[cc] = __ldcg(part + cc * cstride + 128);
+            cl[cc] = __ldcg(part + cc * cstride + 129);
         }
-        if (c0 == 0) {
-            for (int cc = tid - 128; tid >= 128 && cc < nc; cc += STEP_THREADS - 128) {
-                cm[cc] = __ldcg(part + cc * cstride + 128);
-                cl[cc] = __ldcg(part + cc * cstride + 129);
-            }
-            __syncthreads();
-            float M = -__int_as_float(0x7f800000);
-            for (int cc = 0; cc < nc; cc++) M = fmaxf(M, cm[cc]);
-            for (int cc = tid; cc < nc; cc += STEP_THREADS) cf[cc] = bt_exp(__fsub_rn(cm[cc], M));
-            __syncthreads();
-        }
-        if (tid < 128) {
+    }
+    __syncthreads();
+    float M = -__int_as_float(0x7f800000);
+    for (int cc = 0; cc < nc; cc++) M = fmaxf(M, cm[cc]);
+    for (int cc = tid; cc < nc; cc += STEP_THREADS) cf[cc] = bt_exp(__fsub_rn(cm[cc], M));
+    __syncthreads();
+    float O = 0.0f;
+    if (tid < 128) {
+#pragma unroll 1
+        for (int c0 = 0; c0 < nc; c0 += B) {
+            if (c0) load(c0);
 #pragma unroll
             for (int kk = 0; kk < B; kk++)
                 if (c0 + kk < nc) O = fmaf(a[kk], cf[c0 + kk], O);
         }
-    }
-    if (tid == 128) {
+    } else if (tid == 128) {
         float Lh = 0.0f;
         for (int cc = 0; cc < nc; cc++) Lh = fmaf(cl[cc], cf[cc], Lh);
         misc[1] = Lh;
@@ -927,10 +930,10 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
     {
         // the page ids of this CTA's first two attention items: the same in every layer
         constexpr int PPI = ATTN_CHUNK / 16;
-        const long long n_it = attn_items(p, sm.pos);
+        const int n_it = attn_items(p, sm.pos);
         if (tid < 2 * PPI) {
             const int k = tid / PPI, pg = tid % PPI;
-            const long long i = blockIdx.x + (long long)k * gridDim.x;
+            const int i = blockIdx.x + k * gridDim.x;
             int blk = 0;
             if (i < n_it) {
                 AttnItem it;
@@ -1025,11 +1028,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             CYC_WRITE(il, 8, 1);
         }
         // the K/V pages of this CTA's first two attention items, requested before the barrier
-        const long long it0 = blockIdx.x;
-        const long long n_items = attn_items(p, sm.pos);
+        const int it0 = blockIdx.x;
+        const int n_items = attn_items(p, sm.pos);
         __syncthreads();
         if (warp < 2) {  // warp k issues item k's pages
-            const long long i = it0 + (long long)warp * gridDim.x;
+            const int i = it0 + warp * gridDim.x;
             if (i < n_items) {
                 AttnItem it;
                 attn_item(p, sm.pos, i, it);
@@ -1041,8 +1044,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         {
             const int hf = warp >> 2;
             bool ok = true;
-            for (long long k = hf;; k += 2) {
-                const long long i = it0 + k * gridDim.x;
+            for (int k = hf;; k += 2) {
+                const int i = it0 + k * gridDim.x;
                 if (i >= n_items) break;
                 AttnItem it;
                 attn_item(p, sm.pos, i, it);
@@ -1060,7 +1063,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         // attn_output tiles are static: request this CTA's first ones now. Its residual rows (x)
         // are final since the last barrier of the previous layer.
         const SegList so = make_segs(&L.o, 0, nullptr, 0, nullptr, 0);
-        long long o0, o1;
+        int o0, o1;
         cta_range(so.total, o0, o1);
         const int orow0 = (int)(o0 * L.o.rpt);
         int orows = (int)(o1 * L.o.rpt) - orow0;
@@ -1086,15 +1089,15 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             int multi = 0;
             for (int t = 0; t < T; t++) multi += (sm.pos[t] + 1 > ATTN_CHUNK);
             if (multi) {
-                const long long n_ci = (long long)T * p.H;
-                for (long long ci = blockIdx.x; ci < n_ci; ci += gridDim.x) {
-                    const int t = (int)(ci / p.H), hd = (int)(ci % p.H);
+                const int n_ci = T * p.H;
+                for (int ci = blockIdx.x; ci < n_ci; ci += gridDim.x) {
+                    const int t = ci / p.H, hd = ci - t * p.H;
                     const int nc = (sm.pos[t] + 1 + ATTN_CHUNK - 1) / ATTN_CHUNK;
                     if (nc == 1) continue;
                     const int g = hd / G, h = hd % G;
                     const float *part =
                         p.part + (((long long)t * p.HK + g) * p.max_chunks) * G * PART_ROW + (long long)h * PART_ROW;
-                    combine_head(part, (long long)G * PART_ROW, nc, p.att + (long long)t * QW + hd * 128, sm.cbuf,
+                    combine_head(part, G * PART_ROW, nc, p.att + (long long)t * QW + hd * 128, sm.cbuf,
                                  sm.misc);
                 }
                 if (!grid_sync(p.bar, epoch, p.err, TR(il, 2))) return;
@@ -1135,9 +1138,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             acc = butterfly_sum(acc);
             if (lane == 0) p.rlog[(long long)t * p.NE + blockIdx.x + k * gridDim.x] = acc;
         }
-        const long long dtotal = (long long)T * E;
-        long long d0, d1;
-        cta_range(dtotal, d0, d1);
+        int d0, d1;
+        cta_range(T * E, d0, d1);
         if (!grid_sync(p.bar, epoch, p.err, TR(il, 4))) return;
         // ================= GATEUP: soft_max + route() in every CTA (C5, C7; stable descending
         // by total_cmp, top K, renormalised), then the experts
@@ -1208,9 +1210,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         }
         POINT(il, 4);
         {
-            const long long total = (long long)T * K * L.gate.n_tiles;
-            long long u0, u1;
-            cta_range(total, u0, u1);
+            int u0, u1;
+            cta_range(T * K * L.gate.n_tiles, u0, u1);
             const int n = warp_units(u0, u1, warp);
             ring.configure(L.gate.tile_bytes + L.up.tile_bytes);
             const int nsb = L.gate.nsb, gS = L.gate.S, grpt = L.gate.rpt, gnt = L.gate.n_tiles;
@@ -1224,10 +1225,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                 const long long w0 = clock64();
                 if (!ring.wait(j, p.err)) return;
                 gcw += clock64() - w0;
-                const long long u = u0 + warp + (long long)j * STEP_WARPS;
-                const int tile = (int)(u % gnt);
-                const long long tk = u / gnt;
-                const int t = (int)(tk / K);
+                const int u = u0 + warp + j * STEP_WARPS;
+                const int tk = u / gnt, tile = u - tk * gnt;
+                const int t = tk / K;
                 const uint8_t *gt = ring.slot_ptr(j), *ut = gt + gtb;
                 const bool active = lane < gS;
                 const int rit = active ? lane / nsb : 0, b = active ? lane - rit * nsb : 0;
@@ -1249,7 +1249,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                     }
                     rowv[which] = rr;
                 }
-                if (active && b == 0 && row < F) p.act[tk * F + row] = __fmul_rn(bt_silu(rowv[0]), rowv[1]);
+                if (active && b == 0 && row < F) p.act[(long long)tk * F + row] = __fmul_rn(bt_silu(rowv[0]), rowv[1]);
                 __syncwarp();
                 ring.done++;
             }
@@ -1290,8 +1290,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                 const long long w0 = clock64();
                 if (!ring.wait(j, p.err)) return;
                 dcw += clock64() - w0;
-                const long long u = d0 + warp + (long long)j * STEP_WARPS;
-                const int t = (int)(u / E);
+                const int u = d0 + warp + j * STEP_WARPS;
+                const int t = u / E;
                 const uint8_t *base = ring.slot_ptr(j);
                 const int kk = lane / nsb, b = lane - kk * nsb;
                 for (int k0 = 0; k0 < K; k0 += epp) {
@@ -1321,7 +1321,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                         for (int q = s0 + 1; q < K && q < s0 + wchunk; q++) tot = __fadd_rn(tot, __fmul_rn(wv[q], w[q]));
                         sum = workers <= 1 ? tot : __fadd_rn(sum, tot);
                     }
-                    p.x[u] = __fadd_rn(sm.res[(int)(u - d0)], sum);
+                    p.x[u] = __fadd_rn(sm.res[u - d0], sum);
                 }
                 __syncwarp();
                 ring.done++;
