@@ -152,7 +152,8 @@ def cpu_baseline_from_engine(engine, cache, cfg, ctx, n_tokens, threads, seed):
 def run_ours(args, rank, world, local_rank):
     import bigtea_b200 as bt
 
-    over = {"max_positions": args.ctx + args.steps + args.warmup + args.steps // 4 + args.prof_steps + 64}
+    longest = max(args.ctx, args.ctx2_max if args.batch2 else 0)
+    over = {"max_positions": longest + 2 * (args.steps + args.warmup) + args.steps // 4 + args.prof_steps + 64}
     if args.layers:
         over["n_layer"] = args.layers
         over["layer_types"] = bt.config(args.config).layer_types[:args.layers]
@@ -203,6 +204,42 @@ def run_ours(args, rank, world, local_rank):
     # per-kernel device times (serialised launches) for the roofline
     prof = runner.profile_decode(cache, [nxt], args.prof_steps) if args.prof_steps else {}
     gu_bytes, dn_bytes = expert_bytes(cfg)
+    persistent = "decode_step" in prof
+
+    # the batched workload: batch2 concurrent sequences, per-sequence contexts seeded uniform in
+    # [ctx2_min, ctx2_max], paged f16 KV
+    batched = None
+    if args.batch2:
+        B = args.batch2
+        rng2 = np.random.default_rng(args.seed + 2)
+        ctxs = rng2.integers(args.ctx2_min, args.ctx2_max + 1, B)
+        cache2 = bt.KvCache(engine, max_positions=int(ctxs.max()) + 2 * (args.steps + args.warmup) + 8,
+                            max_seqs=B)
+        # seeded f16 values in every cached position (a zero-filled pool is not a fair workload:
+        # pages that hold only zeros can cost the memory system almost nothing to read); one
+        # random buffer per layer, its prefixes shared by the sequences
+        kw = cfg.n_head_kv * cfg.head_dim
+        cmax = int(ctxs.max())
+        for il in range(cfg.n_layer):
+            k = rng2.standard_normal(cmax * kw).astype(np.float16)
+            v = rng2.standard_normal(cmax * kw).astype(np.float16)
+            for sq, c in enumerate(ctxs):
+                cache2.restore_layer(il, k[:int(c) * kw], v[:int(c) * kw], seq=sq)
+        for sq, c in enumerate(ctxs):
+            cache2.set_positions(int(c), sq)
+        first2 = rng2.integers(0, cfg.n_vocab, B)
+        runner.generate_greedy(cache2, first2, args.warmup)
+        sync_ranks(world)
+        runner.generate_greedy(cache2, first2, args.steps)
+        ms2 = max_over_ranks(runner.last_device_ms(), world)
+        batched = {"value": round(world * B * args.steps / (ms2 / 1e3), 1), "unit": "tok/s", "batch": B,
+                   "ms_per_step": round(ms2 / args.steps, 3),
+                   "context": f"per sequence, seeded uniform in [{args.ctx2_min}, {args.ctx2_max}], "
+                              f"mean {float(ctxs.mean()):.0f}",
+                   "kv": "paged f16, 16-token blocks, seeded random contents",
+                   "routing": "the synthetic router (no Zipf popularity bias)",
+                   "path": "per-phase kernels (single-token steps of more than 4 sequences)"}
+        cache2.close()
     # per-phase kernels: the expert kernels' times; the persistent step: its gate/up and down
     # phases (slowest CTA, from the in-kernel timeline)
     gu = prof.get("expert_gateup", prof.get("ph5_gateup_work", (1, 0.0)))
@@ -210,7 +247,7 @@ def run_ours(args, rank, world, local_rank):
     exp_ms = gu[1] / max(gu[0], 1) + dn[1] / max(dn[0], 1)
     achieved = (gu_bytes + dn_bytes) / (exp_ms / 1e3) / 1e9 if exp_ms > 0 else None
     peak, peak_kind = peaks()
-    per_step_launches = 1 + cfg.n_layer * 7 + 1 + 1
+    per_step_launches = 1 if persistent else 1 + cfg.n_layer * 7 + 1 + 1
 
     result = None
     if rank == 0:
@@ -233,7 +270,8 @@ def run_ours(args, rank, world, local_rank):
                                    f"batch 1 greedy decode after a {args.ctx}-token "
                                    + ("prefill" if args.fill == "prefill" else "seeded cache fill"),
                        "batch": 1, "context": args.ctx, "parallelism": "replicas" if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2 (17 GB of weights per step)",
+                       "l2": "inputs larger than L2: about 2.6 GB of weights and KV read per step "
+                             "(17 GB of weights resident)",
                        "prefill_seconds": round(prefill_s, 2), "setup_seconds": round(time.perf_counter() - t_setup, 1)},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * 7 + 1,
                     "d2h_bytes_per_step": 4 * cfg.n_vocab + 4},
@@ -243,6 +281,7 @@ def run_ours(args, rank, world, local_rank):
                          "frac": round(achieved / peak, 4) if achieved else None, "peak_kind": peak_kind,
                          "bytes_per_token_layer": gu_bytes + dn_bytes, "traffic": None},
             "kernels_us": kernel_table,
+            "batched": batched,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
@@ -331,6 +370,9 @@ def main():
     ap.add_argument("--layers", type=int, default=0, help="override the layer count (profiling runs)")
     ap.add_argument("--prefetch", action="store_true", help="enable the L2 bulk prefetch of upcoming inputs")
     ap.add_argument("--no-pdl", action="store_true", help="disable programmatic dependent launch")
+    ap.add_argument("--batch2", type=int, default=64, help="sequences of the batched workload (0 skips it)")
+    ap.add_argument("--ctx2-min", type=int, default=512)
+    ap.add_argument("--ctx2-max", type=int, default=16384)
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

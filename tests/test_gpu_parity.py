@@ -283,3 +283,38 @@ def test_persistent_and_per_phase_steps_agree(tiny_cfg, tiny_weights):
     model = orc.Model(cfg, tiny_weights)
     model.forward(prompt, 0)
     assert list(runs[1][0][:, 0]) == model.greedy(7, 5)
+
+
+@pytest.mark.parametrize("persistent,ctxs", [(1, (2900, 450, 1700)), (0, (2900, 450, 1700, 3000, 300, 1290))])
+def test_long_context_batched_step_matches_oracle(tiny_cfg, tiny_weights, persistent, ctxs):
+    """One single-token step of several sequences whose cached contexts span many attention
+    chunks (seeded cache contents): the step's logits and its KV append against the oracle run
+    per sequence. Three sequences run as the persistent kernel, six as the per-phase kernels."""
+    cfg = bt.config("tiny", max_positions=4096)
+    rng = np.random.default_rng(41 + persistent)
+    kw = cfg.n_head_kv * cfg.head_dim
+    e = bt.Engine(cfg, tiny_weights)
+    e.set_option("persistent", persistent)
+    cache = bt.KvCache(e, max_positions=4096, max_seqs=len(ctxs))
+    kv = []
+    for s, n in enumerate(ctxs):
+        layers = []
+        for il in range(cfg.n_layer):
+            k = (0.5 * rng.standard_normal(n * kw)).astype(np.float16)
+            v = rng.standard_normal(n * kw).astype(np.float16)
+            cache.restore_layer(il, k, v, seq=s)
+            layers.append((k, v))
+        cache.set_positions(n, s)
+        kv.append(layers)
+    toks = [int(t) for t in rng.integers(0, cfg.n_vocab, len(ctxs))]
+    runner = bt.StreamingRunner(e)
+    got = runner.forward_batch(cache, list(range(len(ctxs))), [[t] for t in toks], list(ctxs))
+    for s, n in enumerate(ctxs):
+        model = orc.Model(cfg, tiny_weights)
+        for il in range(cfg.n_layer):
+            model.write_kv_layer(il, kv[s][il][0], kv[s][il][1])
+        model.set_len(n)
+        assert_logits(got[s], model.forward([toks[s]], n))
+        compare_kv(cache, model, cfg, seq=s)
+    cache.close()
+    e.close()
