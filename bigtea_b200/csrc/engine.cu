@@ -110,6 +110,7 @@ struct bt_engine {
     int TB = 64;
     int max_out = 0;
     DevBuf x, ffn_in, fn, qkv, qbuf, att, rlog, rcnt, sel_ids, sel_w, act, part, acnt;
+    DevBuf g_count, g_off, g_list, g_active, g_nactive, dpart;  // grouped experts of batched steps
     DevBuf dbg_ids, dbg_w;  // [n_layer][TB][K]
     DevBuf tokens, seq_of, local_idx, pos_of, single, x_rows;
     DevBuf st_seq, st_ntok, st_lrow, next_tok, gen_out, gen_count, logits, amax;
@@ -185,6 +186,26 @@ static int pick_nst(size_t slot_bytes, size_t fixed_bytes) {
     int nst = 3;
     while (nst > 1 && fixed_bytes + (size_t)GEMV_WARPS * nst * slot_bytes > cap) nst--;
     return nst;
+}
+
+// the same choice with an explicit cap on the CTA's shared memory (the batched kernels use all of it)
+static int pick_nst_cap(size_t slot_bytes, size_t fixed_bytes, size_t cap) {
+    int nst = 3;
+    while (nst > 1 && fixed_bytes + (size_t)GEMV_WARPS * nst * slot_bytes > cap) nst--;
+    return nst;
+}
+
+// Tokens one GEMV launch carries in a step of T > MAX_T tokens: as many as fit beside a two-slot
+// ring in the CTA's shared memory, split evenly (the weights are read once per launch).
+static int gemv_chunk(int T, int K, int slot_bytes) {
+    if (T <= MAX_T) return MAX_T;
+    const size_t cap = (size_t)max_dynamic_smem();
+    const size_t ring = (size_t)GEMV_WARPS * 2 * slot_bytes;
+    const size_t per = (size_t)(K / 256) * sizeof(ActBlock);
+    long long n = cap > 1024 + 128 + ring ? (long long)((cap - 1024 - 128 - ring) / per) : MAX_T;
+    if (n < MAX_T) n = MAX_T;
+    const int chunks = (int)((T + n - 1) / n);
+    return (T + chunks - 1) / chunks;
 }
 
 static int grid_for(const bt_engine *e, long long units) {
@@ -308,6 +329,12 @@ static int alloc_scratch(bt_engine *e) {
     CK(e->act.alloc((size_t)TB * K * F * 4));
     CK(e->part.alloc((size_t)TB * d.n_head_kv * e->part_chunks * G * (d.head_dim + 4) * 4));
     CK(e->acnt.alloc((size_t)TB * d.n_head_kv * 4));
+    CK(e->g_count.alloc((size_t)NE * 4));
+    CK(e->g_off.alloc((size_t)NE * 4));
+    CK(e->g_list.alloc((size_t)TB * K * 4));
+    CK(e->g_active.alloc((size_t)NE * 4));
+    CK(e->g_nactive.alloc(4));
+    CK(e->dpart.alloc((size_t)TB * K * E * 4));
     CK(cudaMemset(e->acnt.p, 0, (size_t)TB * d.n_head_kv * 4));
     CK(e->dbg_ids.alloc((size_t)d.n_layer * TB * K * 4));
     CK(e->dbg_w.alloc((size_t)d.n_layer * TB * K * 4));
@@ -963,7 +990,7 @@ static cudaError_t run_gemv(bt_engine *e, const QMat *const *mats, const int *ou
     a.slot_bytes = slot;
     a.nst = 1;
     size_t fixed = gemv_smem_bytes(a) - (size_t)GEMV_WARPS * slot;
-    a.nst = pick_nst(slot, fixed);
+    a.nst = T > MAX_T ? pick_nst_cap(slot, fixed, (size_t)max_dynamic_smem()) : pick_nst(slot, fixed);
     timer_begin(e, name);
     cudaError_t r = launch_gemv(a, grid_for(e, tile0), e->st, e->pdl);
     timer_end(e);
@@ -1124,8 +1151,11 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             pf_qkv.D = D;
             pf_qkv.T = T;
         }
-        for (int t0 = 0; t0 < T; t0 += MAX_T) {
-            int tg = T - t0 < MAX_T ? T - t0 : MAX_T;
+        int qslot = l.q.g.tile_bytes > l.k.g.tile_bytes ? l.q.g.tile_bytes : l.k.g.tile_bytes;
+        qslot = l.v.g.tile_bytes > qslot ? l.v.g.tile_bytes : qslot;
+        const int qchunk = gemv_chunk(T, E, qslot);
+        for (int t0 = 0; t0 < T; t0 += qchunk) {
+            int tg = T - t0 < qchunk ? T - t0 : qchunk;
             const QMat *mats[3] = {&l.q, &l.k, &l.v};
             int offs[3] = {0, QW, QW + KW};
             CK(run_gemv(e, mats, offs, 3, e->x.as<float>() + (size_t)t0 * E, E, nullptr, l.attn_norm.as<float>(), E, tg,
@@ -1181,8 +1211,9 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             CK(launch_attn(a, kv->tmap, st, pdl));
             timer_end(e);
         }
-        for (int t0 = 0; t0 < T; t0 += MAX_T) {
-            int tg = T - t0 < MAX_T ? T - t0 : MAX_T;
+        const int ochunk = gemv_chunk(T, QW, l.o.g.tile_bytes);
+        for (int t0 = 0; t0 < T; t0 += ochunk) {
+            int tg = T - t0 < ochunk ? T - t0 : ochunk;
             const QMat *mats[1] = {&l.o};
             int offs[1] = {0};
             CK(run_gemv(e, mats, offs, 1, e->att.as<float>() + (size_t)t0 * QW, QW, nullptr, nullptr, QW, tg,
@@ -1210,7 +1241,75 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             CK(launch_router(a, st, pdl));
             timer_end(e);
         }
-        for (int t0 = 0; t0 < T; t0 += MAX_T) {
+        if (T > MAX_T) {  // grouped: each selected expert's weights once per step
+            GroupArgs ga{};
+            ga.sel_ids = e->sel_ids.as<int>();
+            ga.T = T;
+            ga.K = K;
+            ga.NE = NE;
+            ga.g_count = e->g_count.as<int>();
+            ga.g_off = e->g_off.as<int>();
+            ga.g_list = e->g_list.as<int>();
+            ga.g_active = e->g_active.as<int>();
+            ga.g_nactive = e->g_nactive.as<int>();
+            timer_begin(e, "expert_group");
+            CK(launch_group(ga, st, pdl));
+            timer_end(e);
+            ExpertArgs a{};
+            a.gate = l.gate.buf.as<uint8_t>();
+            a.up = l.up.buf.as<uint8_t>();
+            a.down = l.down.buf.as<uint8_t>();
+            a.gtype = l.gate.type;
+            a.utype = l.up.type;
+            a.dtype = l.down.type;
+            a.g_nsb = l.gate.g.nsb;
+            a.g_rpt = l.gate.g.rpt;
+            a.g_S = l.gate.g.S;
+            a.g_tile_bytes = l.gate.g.tile_bytes;
+            a.g_n_tiles = (int)l.gate.g.n_tiles;
+            a.u_tile_bytes = l.up.g.tile_bytes;
+            a.g_expert_bytes = l.gate.mat_bytes;
+            a.u_expert_bytes = l.up.mat_bytes;
+            a.d_expert_bytes = l.down.mat_bytes;
+            a.d_nsb = l.down.g.nsb;
+            a.d_tile_bytes = l.down.g.tile_bytes;
+            a.E = E;
+            a.F = F;
+            a.K = K;
+            a.T = T;
+            a.workers = (int)d.expert_workers;
+            a.sel_ids = e->sel_ids.as<int>();
+            a.sel_w = e->sel_w.as<float>();
+            a.fn = e->fn.as<float>();
+            a.act = e->act.as<float>();
+            a.ffn_in = e->ffn_in.as<float>();
+            a.x_out = e->x.as<float>();
+            a.single = e->single.as<unsigned char>();
+            a.err = err;
+            a.g_count = ga.g_count;
+            a.g_off = ga.g_off;
+            a.g_list = ga.g_list;
+            a.g_active = ga.g_active;
+            a.g_nactive = ga.g_nactive;
+            a.dpart = e->dpart.as<float>();
+            const size_t cap = (size_t)max_dynamic_smem();
+            a.slot_bytes = a.g_tile_bytes + a.u_tile_bytes;
+            a.nst = 1;
+            a.nst = pick_nst_cap(a.slot_bytes, gateup_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
+            timer_begin(e, "expert_gateup");
+            CK(launch_gateup_grouped(a, e->n_sm, st, pdl));
+            timer_end(e);
+            a.slot_bytes = down_group_rows(a) * a.d_tile_bytes;
+            a.nst = 1;
+            a.nst = pick_nst_cap(a.slot_bytes, down_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
+            timer_begin(e, "expert_down");
+            CK(launch_down_grouped(a, e->n_sm, st, pdl));
+            timer_end(e);
+            timer_begin(e, "expert_combine");
+            CK(launch_down_combine(a, st, pdl));
+            timer_end(e);
+        }
+        for (int t0 = 0; T <= MAX_T && t0 < T; t0 += MAX_T) {
             int tg = T - t0 < MAX_T ? T - t0 : MAX_T;
             ExpertArgs a{};
             a.gate = l.gate.buf.as<uint8_t>();

@@ -532,6 +532,315 @@ cudaError_t launch_down(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl
     return launch_ex(down_kernel<GEMV_WARPS>, dim3(grid), dim3(GEMV_WARPS * 32), down_smem_bytes(a), st, pdl, a);
 }
 
+// ====================================================================== grouped experts (batched steps)
+// With many tokens in a step, the per-(token, expert) units above read an expert's weights once
+// for every token that selected it. The grouped kernels read each selected expert's weights
+// once per step: units are (expert, tile), and a CTA stages the activations of that expert's
+// tokens (GROUP_MAXM at a time). The arithmetic per (token, expert, row) is unchanged.
+
+// One CTA: per expert, the (token, slot) indices tk = t*K + k that selected it, ascending.
+__global__ void __launch_bounds__(256) group_kernel(const __grid_constant__ GroupArgs p) {
+    extern __shared__ int gsm[];
+    const int n = p.T * p.K, tid = threadIdx.x;
+    int *sel = gsm, *cnt = sel + n, *off = cnt + p.NE;
+    pdl_wait();  // the selections come from the router
+    for (int i = tid; i < n; i += blockDim.x) sel[i] = p.sel_ids[i];
+    __syncthreads();
+    for (int e = tid; e < p.NE; e += blockDim.x) {
+        int c = 0;
+        for (int i = 0; i < n; i++) c += sel[i] == e;
+        cnt[e] = c;
+    }
+    __syncthreads();
+    if (tid == 0) {
+        int na = 0, o = 0;
+        for (int e = 0; e < p.NE; e++) {
+            off[e] = o;
+            o += cnt[e];
+            if (cnt[e]) p.g_active[na++] = e;
+        }
+        *p.g_nactive = na;
+    }
+    __syncthreads();
+    for (int e = tid; e < p.NE; e += blockDim.x) {
+        int o = off[e];
+        for (int i = 0; i < n; i++)
+            if (sel[i] == e) p.g_list[o++] = i;
+        p.g_count[e] = cnt[e];
+        p.g_off[e] = off[e];
+    }
+    pdl_trigger();
+}
+
+// A warp's ring across the chunks of a grouped kernel: copy g goes to slot g % nst and its
+// wait uses parity (g / nst) & 1; `issued` and `done` count copies over the whole launch.
+struct GroupRing {
+    uint8_t *base;
+    uint64_t *bars;
+    int nst, slot_bytes, issued, done;
+};
+
+// gate/up, grouped: unit = (selected expert a, tile); the CTA's units are a contiguous range in
+// (a, tile) order, so it walks at most a few experts and stages each one's tokens once.
+template <int NWARP>
+__global__ void __launch_bounds__(NWARP * 32, 1) gateup_grouped_kernel(const __grid_constant__ ExpertArgs p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int *rows_s = reinterpret_cast<int *>(smem + 512);  // [GROUP_MAXM] token of each staged row
+    int *tk_s = rows_s + GROUP_MAXM;                     // [GROUP_MAXM] its (token, slot) index
+    ActBlock *act = reinterpret_cast<ActBlock *>(smem + 1024);
+    const int nsb = p.g_nsb, nt = p.g_n_tiles;
+    const size_t act_bytes = (size_t)GROUP_MAXM * nsb * sizeof(ActBlock);
+    GroupRing r;
+    r.nst = p.nst;
+    r.slot_bytes = p.slot_bytes;
+    r.base = smem + 1024 + ((act_bytes + 127) & ~(size_t)127) + (size_t)warp * p.nst * p.slot_bytes;
+    r.bars = reinterpret_cast<uint64_t *>(smem) + warp * p.nst;
+    r.issued = r.done = 0;
+    if (lane == 0) {
+        for (int i = 0; i < p.nst; i++) mbar_init(&r.bars[i], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    pdl_wait();  // the groups come from group_kernel, the activations from the router
+    const int total = *p.g_nactive * nt;
+    const int u0 = (int)((unsigned)blockIdx.x * (unsigned)total / gridDim.x);
+    const int u1 = (int)((unsigned)(blockIdx.x + 1) * (unsigned)total / gridDim.x);
+    pdl_trigger();
+    bool ok = true;
+    for (int a = nt ? u0 / nt : 0; ok && a * nt < u1; a++) {
+        const int e = p.g_active[a], m = p.g_count[e], off = p.g_off[e];
+        const int lo = (u0 > a * nt ? u0 : a * nt) - a * nt;
+        const int hi = (u1 < (a + 1) * nt ? u1 : (a + 1) * nt) - a * nt;
+        const int ntw = hi - lo > warp ? (hi - lo - warp + NWARP - 1) / NWARP : 0;
+        for (int c0 = 0; ok && c0 < m; c0 += GROUP_MAXM) {
+            const int mc = m - c0 < GROUP_MAXM ? m - c0 : GROUP_MAXM;
+            __syncthreads();  // the previous chunk's activations are no longer read
+            if (tid < mc) {
+                const int tk = p.g_list[off + c0 + tid];
+                tk_s[tid] = tk;
+                rows_s[tid] = tk / p.K;
+            }
+            const int base = r.done;  // this warp's j-th tile of the chunk is copy base + j
+            auto issue = [&](int j) {
+                const int tile = lo + warp + j * NWARP, slot = (base + j) % r.nst;
+                uint8_t *dst = r.base + (size_t)slot * r.slot_bytes;
+                mbar_arrive_expect_tx(&r.bars[slot], p.g_tile_bytes + p.u_tile_bytes);
+                bulk_g2s(dst, p.gate + e * p.g_expert_bytes + (long long)tile * p.g_tile_bytes, p.g_tile_bytes,
+                         &r.bars[slot]);
+                bulk_g2s(dst + p.g_tile_bytes, p.up + e * p.u_expert_bytes + (long long)tile * p.u_tile_bytes,
+                         p.u_tile_bytes, &r.bars[slot]);
+            };
+            if (lane == 0) {
+                fence_proxy_async();
+                while (r.issued - base < ntw && r.issued - r.done < r.nst) {
+                    issue(r.issued - base);
+                    r.issued++;
+                }
+            }
+            r.issued = __shfl_sync(FULL, r.issued, 0);
+            __syncthreads();  // rows_s, tk_s
+            stage_activations<NWARP>(p.fn, p.E, rows_s, nullptr, 0.0f, p.E, mc, act, nullptr);
+            __syncthreads();
+            for (int j = 0; j < ntw; j++) {
+                const int g = base + j, slot = g % r.nst;
+                if (!__all_sync(FULL, mbar_wait(&r.bars[slot], (g / r.nst) & 1, p.err))) {
+                    ok = false;
+                    break;
+                }
+                r.done = g + 1;
+                const int tile = lo + warp + j * NWARP;
+                const uint8_t *gt = r.base + (size_t)slot * r.slot_bytes, *ut = gt + p.g_tile_bytes;
+                const bool active = lane < p.g_S;
+                const int rit = active ? lane / nsb : 0, b = active ? lane - rit * nsb : 0;
+                const int row = tile * p.g_rpt + rit;
+#pragma unroll 1
+                for (int i = 0; i < mc; i++) {
+                    float rowv[2];
+#pragma unroll 1
+                    for (int which = 0; which < 2; which++) {
+                        const uint8_t *tl = which ? ut : gt;
+                        const int ty = which ? p.utype : p.gtype;
+                        float v = 0.0f;
+                        if (active) {
+                            const ActBlock &ab = act[i * nsb + b];
+                            v = ty == T_Q4_K ? q4k_slot_dot(tl, p.g_S, lane, ab) : q6k_slot_dot(tl, p.g_S, lane, ab);
+                        }
+                        float rr = 0.0f;
+                        for (int b2 = 0; b2 < nsb; b2++) {
+                            const int srcl = rit * nsb + b2;
+                            rr = __fadd_rn(rr, __shfl_sync(FULL, v, srcl < 32 ? srcl : 31));
+                        }
+                        rowv[which] = rr;
+                    }
+                    if (active && b == 0 && row < p.F)
+                        p.act[(long long)tk_s[i] * p.F + row] = __fmul_rn(bt_silu(rowv[0]), rowv[1]);
+                }
+                __syncwarp();
+                if (lane == 0 && r.issued - base < ntw) {
+                    fence_proxy_async();
+                    issue(r.issued - base);
+                    r.issued++;
+                }
+                r.issued = __shfl_sync(FULL, r.issued, 0);
+            }
+            if (__syncthreads_or(!ok)) ok = false;
+        }
+    }
+    if (!ok && lane == 0)  // a wait ran out: let this warp's copies in flight land (bounded) before exiting
+        for (int g = r.done; g < r.issued; g++) mbar_wait(&r.bars[g % r.nst], (g / r.nst) & 1, nullptr);
+}
+
+// down, grouped: unit = (selected expert a, group of RG = 32 / nsb output rows): one copy of RG
+// consecutive row tiles; lane l decodes slot l % nsb of row l / nsb. Each (token, slot)'s row
+// values go to dpart; down_combine_kernel adds them in the reference's order.
+template <int NWARP>
+__global__ void __launch_bounds__(NWARP * 32, 1) down_grouped_kernel(const __grid_constant__ ExpertArgs p) {
+    extern __shared__ __align__(1024) uint8_t smem[];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    int *tk_s = reinterpret_cast<int *>(smem + 512);  // [GROUP_MAXM] (token, slot) index = act row
+    ActBlock *act = reinterpret_cast<ActBlock *>(smem + 1024);
+    const int nsb = p.d_nsb, RG = 32 / nsb, ng = (p.E + RG - 1) / RG;
+    const size_t act_bytes = (size_t)GROUP_MAXM * nsb * sizeof(ActBlock);
+    GroupRing r;
+    r.nst = p.nst;
+    r.slot_bytes = p.slot_bytes;
+    r.base = smem + 1024 + ((act_bytes + 127) & ~(size_t)127) + (size_t)warp * p.nst * p.slot_bytes;
+    r.bars = reinterpret_cast<uint64_t *>(smem) + warp * p.nst;
+    r.issued = r.done = 0;
+    if (lane == 0) {
+        for (int i = 0; i < p.nst; i++) mbar_init(&r.bars[i], 1);
+        fence_mbar_init();
+    }
+    __syncwarp();
+    pdl_wait();
+    const int total = *p.g_nactive * ng;
+    const int u0 = (int)((unsigned)blockIdx.x * (unsigned)total / gridDim.x);
+    const int u1 = (int)((unsigned)(blockIdx.x + 1) * (unsigned)total / gridDim.x);
+    pdl_trigger();
+    bool ok = true;
+    for (int a = ng ? u0 / ng : 0; ok && a * ng < u1; a++) {
+        const int e = p.g_active[a], m = p.g_count[e], off = p.g_off[e];
+        const int lo = (u0 > a * ng ? u0 : a * ng) - a * ng;
+        const int hi = (u1 < (a + 1) * ng ? u1 : (a + 1) * ng) - a * ng;
+        const int nuw = hi - lo > warp ? (hi - lo - warp + NWARP - 1) / NWARP : 0;
+        for (int c0 = 0; ok && c0 < m; c0 += GROUP_MAXM) {
+            const int mc = m - c0 < GROUP_MAXM ? m - c0 : GROUP_MAXM;
+            __syncthreads();
+            if (tid < mc) tk_s[tid] = p.g_list[off + c0 + tid];
+            const int base = r.done;
+            auto issue = [&](int j) {
+                const int gr = lo + warp + j * NWARP, slot = (base + j) % r.nst;
+                const int r0 = gr * RG, nr = p.E - r0 < RG ? p.E - r0 : RG;
+                mbar_arrive_expect_tx(&r.bars[slot], nr * p.d_tile_bytes);
+                bulk_g2s(r.base + (size_t)slot * r.slot_bytes, p.down + e * p.d_expert_bytes + (long long)r0 * p.d_tile_bytes,
+                         nr * p.d_tile_bytes, &r.bars[slot]);
+            };
+            if (lane == 0) {
+                fence_proxy_async();
+                while (r.issued - base < nuw && r.issued - r.done < r.nst) {
+                    issue(r.issued - base);
+                    r.issued++;
+                }
+            }
+            r.issued = __shfl_sync(FULL, r.issued, 0);
+            __syncthreads();  // tk_s
+            stage_activations<NWARP>(p.act, p.F, tk_s, nullptr, 0.0f, p.F, mc, act, nullptr);
+            __syncthreads();
+            for (int j = 0; j < nuw; j++) {
+                const int g = base + j, slot = g % r.nst;
+                if (!__all_sync(FULL, mbar_wait(&r.bars[slot], (g / r.nst) & 1, p.err))) {
+                    ok = false;
+                    break;
+                }
+                r.done = g + 1;
+                const int gr = lo + warp + j * NWARP, r0 = gr * RG;
+                const int nr = p.E - r0 < RG ? p.E - r0 : RG;
+                const bool active = lane < nr * nsb;
+                const int rr = active ? lane / nsb : 0, b = active ? lane - rr * nsb : 0;
+                const uint8_t *tile = r.base + (size_t)slot * r.slot_bytes + (size_t)rr * p.d_tile_bytes;
+#pragma unroll 1
+                for (int i = 0; i < mc; i++) {
+                    float v = 0.0f;
+                    if (active) {
+                        const ActBlock &ab = act[i * nsb + b];
+                        v = p.dtype == T_Q4_K ? q4k_slot_dot(tile, nsb, b, ab) : q6k_slot_dot(tile, nsb, b, ab);
+                    }
+                    float acc = 0.0f;
+                    for (int b2 = 0; b2 < nsb; b2++) {
+                        const int srcl = rr * nsb + b2;
+                        acc = __fadd_rn(acc, __shfl_sync(FULL, v, srcl < 32 ? srcl : 31));
+                    }
+                    if (active && b == 0) p.dpart[(long long)tk_s[i] * p.E + r0 + rr] = acc;
+                }
+                __syncwarp();
+                if (lane == 0 && r.issued - base < nuw) {
+                    fence_proxy_async();
+                    issue(r.issued - base);
+                    r.issued++;
+                }
+                r.issued = __shfl_sync(FULL, r.issued, 0);
+            }
+            if (__syncthreads_or(!ok)) ok = false;
+        }
+    }
+    if (!ok && lane == 0)
+        for (int g = r.done; g < r.issued; g++) mbar_wait(&r.bars[g % r.nst], (g / r.nst) & 1, nullptr);
+}
+
+// grid T: x = ffn_in + the K expert rows scaled by their weights and summed in the reference's
+// order (the single-token pairs of expert_ffn_single, or the block path's sequential sum).
+__global__ void __launch_bounds__(256) down_combine_kernel(const __grid_constant__ ExpertArgs p) {
+    const int t = blockIdx.x;
+    pdl_wait();
+    const float *w = p.sel_w + t * p.K;
+    for (int row = threadIdx.x; row < p.E; row += blockDim.x) {
+        float o[MAX_K];
+        for (int k = 0; k < p.K; k++) o[k] = p.dpart[((long long)t * p.K + k) * p.E + row];
+        float sum = 0.0f;
+        if (p.single[t]) {
+            int workers = p.workers < p.K ? p.workers : p.K;
+            if (workers < 1) workers = 1;
+            const int chunk = (p.K + workers - 1) / workers;
+            for (int s0 = 0; s0 < p.K; s0 += chunk) {
+                float tot = __fmul_rn(o[s0], w[s0]);
+                for (int i = s0 + 1; i < p.K && i < s0 + chunk; i++) tot = __fadd_rn(tot, __fmul_rn(o[i], w[i]));
+                sum = workers <= 1 ? tot : __fadd_rn(sum, tot);
+            }
+        } else {
+            for (int i = 0; i < p.K; i++) sum = __fadd_rn(sum, __fmul_rn(o[i], w[i]));
+        }
+        p.x_out[(long long)t * p.E + row] = __fadd_rn(p.ffn_in[(long long)t * p.E + row], sum);
+    }
+    pdl_trigger();
+}
+
+size_t gateup_grouped_smem_bytes(const ExpertArgs &a) {
+    size_t act = (size_t)GROUP_MAXM * a.g_nsb * sizeof(ActBlock);
+    return 1024 + ((act + 127) & ~(size_t)127) + (size_t)GEMV_WARPS * a.nst * a.slot_bytes;
+}
+size_t down_grouped_smem_bytes(const ExpertArgs &a) {
+    size_t act = (size_t)GROUP_MAXM * a.d_nsb * sizeof(ActBlock);
+    return 1024 + ((act + 127) & ~(size_t)127) + (size_t)GEMV_WARPS * a.nst * a.slot_bytes;
+}
+int down_group_rows(const ExpertArgs &a) { return 32 / a.d_nsb; }
+
+cudaError_t launch_group(const GroupArgs &a, cudaStream_t st, bool pdl) {
+    const size_t smem = ((size_t)a.T * a.K + 2 * (size_t)a.NE + 1) * 4;
+    return launch_ex(group_kernel, dim3(1), dim3(256), smem, st, pdl, a);
+}
+cudaError_t launch_gateup_grouped(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl) {
+    return launch_ex(gateup_grouped_kernel<GEMV_WARPS>, dim3(grid), dim3(GEMV_WARPS * 32), gateup_grouped_smem_bytes(a),
+                     st, pdl, a);
+}
+cudaError_t launch_down_grouped(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl) {
+    return launch_ex(down_grouped_kernel<GEMV_WARPS>, dim3(grid), dim3(GEMV_WARPS * 32), down_grouped_smem_bytes(a), st,
+                     pdl, a);
+}
+cudaError_t launch_down_combine(const ExpertArgs &a, cudaStream_t st, bool pdl) {
+    return launch_ex(down_combine_kernel, dim3(a.T), dim3(256), 0, st, pdl, a);
+}
+
 // ====================================================================== router
 // grid (ceil(NE/4), T), 128 threads: each CTA normalises the token (C6) into shared memory and
 // warp w computes router row blockIdx.x*4+w (C5). The token's last CTA (atomic ticket) runs
@@ -735,6 +1044,21 @@ __device__ __forceinline__ void lds_vec(float (&dst)[N], const float *src) {
     }
 }
 
+// N f16 values (bit patterns) from shared memory
+template <int N>
+__device__ __forceinline__ void lds_half(uint16_t (&dst)[N], const uint16_t *src) {
+    if constexpr (N == 4) {
+        const uint2 v = *reinterpret_cast<const uint2 *>(src);
+        dst[0] = lo16(v.x); dst[1] = hi16(v.x); dst[2] = lo16(v.y); dst[3] = hi16(v.y);
+    } else if constexpr (N == 2) {
+        const uint32_t v = *reinterpret_cast<const uint32_t *>(src);
+        dst[0] = lo16(v); dst[1] = hi16(v);
+    } else {
+#pragma unroll
+        for (int k = 0; k < N; k++) dst[k] = src[k];
+    }
+}
+
 template <int G>
 __global__ void __launch_bounds__(ATTN_THREADS, 2)
     attn_kernel(const __grid_constant__ AttnArgs p, const __grid_constant__ CUtensorMap tmap) {
@@ -742,8 +1066,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2)
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *const K0 = smem, *const K1 = smem + 16384, *const V0 = smem + 32768, *const V1 = smem + 49152;
-    float *qs = reinterpret_cast<float *>(smem + 65536);  // [D][G]
-    float *ps = qs + D * G;                               // [CH][G]
+    uint16_t *qs = reinterpret_cast<uint16_t *>(smem + 65536);  // [D][G] q rounded to f16 (bits)
+    float *ps = reinterpret_cast<float *>(smem + 65536 + D * G * 4);  // [CH][G]
     float *red = ps + CH * G;                             // [8 warps][8]
     float *red2 = red + 64;                               // [4 key groups][8]
     uint64_t *bar = reinterpret_cast<uint64_t *>(red2 + 64);
@@ -782,7 +1106,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2)
     pdl_trigger();
     for (int i = tid; i < D * G; i += ATTN_THREADS) {
         int h = i / D, d = i % D;
-        qs[d * G + h] = f16_round(p.q[(long long)t * p.H * D + (g * G + h) * D + d]);
+        qs[d * G + h] = __half_as_ushort(__float2half_rn(p.q[(long long)t * p.H * D + (g * G + h) * D + d]));
     }
     __syncthreads();
     const bool landed = mbar_wait(bar, 0, p.err);
@@ -800,15 +1124,15 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2)
 #pragma unroll 2
     for (int c16 = 0; c16 < 16; c16++) {
         const uint8_t *kr = (c16 < 8) ? K0 : K1;
-        uint4 w = *reinterpret_cast<const uint4 *>(kr + k * 128 + (((c16 & 7) ^ (k & 7)) << 4));
-        const __half *hk = reinterpret_cast<const __half *>(&w);
+        const uint4 w = *reinterpret_cast<const uint4 *>(kr + k * 128 + (((c16 & 7) ^ (k & 7)) << 4));
+        const uint32_t kw[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
         for (int e = 0; e < 8; e++) {
-            const float kf = __half2float(hk[e]);
-            float q[HPT];
-            lds_vec<HPT>(q, qs + (c16 * 8 + e) * G + hh * HPT);
+            const uint16_t kh = (e & 1) ? hi16(kw[e >> 1]) : lo16(kw[e >> 1]);
+            uint16_t q[HPT];
+            lds_half<HPT>(q, qs + (c16 * 8 + e) * G + hh * HPT);
 #pragma unroll
-            for (int h = 0; h < HPT; h++) sc[h] = fmaf(q[h], kf, sc[h]);
+            for (int h = 0; h < HPT; h++) sc[h] = fma_f16(q[h], kh, sc[h]);  // = fmaf((float)q, (float)k, sc)
         }
     }
     const float NEG_INF = -__int_as_float(0x7f800000);
@@ -858,7 +1182,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2)
 #pragma unroll
             for (int kk = 0; kk < 8; kk++) {
                 if (j0 + kk < cnt) {
-                    const float vf = __half2float(*reinterpret_cast<const __half *>(vb + off[kk]));
+                    const float vf = h2f_fma(*reinterpret_cast<const uint16_t *>(vb + off[kk]));
                     float pj[HPT];
                     lds_vec<HPT>(pj, pb + kk * G);
 #pragma unroll
@@ -1056,7 +1380,9 @@ cudaError_t init_kernel_attributes() {
     if ((e = cudaGetDevice(&dev))) return e;
     if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
     const void *kerns[] = {(const void *)gemv_kernel<GEMV_WARPS>, (const void *)gateup_kernel<GEMV_WARPS>,
-                           (const void *)down_kernel<GEMV_WARPS>, (const void *)attn_kernel<2>,
+                           (const void *)down_kernel<GEMV_WARPS>, (const void *)gateup_grouped_kernel<GEMV_WARPS>,
+                           (const void *)down_grouped_kernel<GEMV_WARPS>, (const void *)group_kernel,
+                           (const void *)attn_kernel<2>,
                            (const void *)attn_kernel<4>,          (const void *)attn_kernel<6>,
                            (const void *)attn_kernel<8>};
     for (const void *k : kerns) {

@@ -72,7 +72,20 @@ struct ExpertArgs {
     int slot_bytes, nst;
     PrefetchSpec pf;
     int prefetch_down;  // gate/up: pull the selected experts' down weights into L2
+    // grouped form (batched steps): the tokens of each selected expert, from group_kernel
+    const int *g_count, *g_off, *g_list, *g_active, *g_nactive;
+    float *dpart;  // [T][K][E] each (token, expert slot)'s down rows before the expert sum
 };
+
+// Tokens grouped by expert for the batched expert kernels: for every expert e, the (token,
+// slot) indices tk = t*K + k that selected it, in ascending tk; the experts with at least one
+// token in ascending id order.
+struct GroupArgs {
+    const int *sel_ids;  // [T][K]
+    int T, K, NE;
+    int *g_count, *g_off, *g_list, *g_active, *g_nactive;
+};
+constexpr int GROUP_MAXM = 16;  // tokens of one expert whose activations a CTA stages at a time
 
 struct RouterArgs {
     const float *x, *norm_w;
@@ -147,6 +160,13 @@ size_t down_smem_bytes(const ExpertArgs &a);
 cudaError_t launch_gateup(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_down(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_router(const RouterArgs &a, cudaStream_t st, bool pdl);
+cudaError_t launch_group(const GroupArgs &a, cudaStream_t st, bool pdl);
+size_t gateup_grouped_smem_bytes(const ExpertArgs &a);
+size_t down_grouped_smem_bytes(const ExpertArgs &a);
+int down_group_rows(const ExpertArgs &a);  // output rows of one grouped down unit
+cudaError_t launch_gateup_grouped(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
+cudaError_t launch_down_grouped(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
+cudaError_t launch_down_combine(const ExpertArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl);
 size_t attn_smem_bytes(int G, int max_chunks);
 cudaError_t launch_attn(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl);

@@ -285,11 +285,16 @@ def test_persistent_and_per_phase_steps_agree(tiny_cfg, tiny_weights):
     assert list(runs[1][0][:, 0]) == model.greedy(7, 5)
 
 
-@pytest.mark.parametrize("persistent,ctxs", [(1, (2900, 450, 1700)), (0, (2900, 450, 1700, 3000, 300, 1290))])
+@pytest.mark.parametrize("persistent,ctxs", [
+    (1, (2900, 450, 1700)),
+    (0, (2900, 450, 1700, 3000, 300, 1290)),
+    (0, tuple(int(c) for c in np.random.default_rng(5).integers(130, 2200, 40))),
+])
 def test_long_context_batched_step_matches_oracle(tiny_cfg, tiny_weights, persistent, ctxs):
     """One single-token step of several sequences whose cached contexts span many attention
     chunks (seeded cache contents): the step's logits and its KV append against the oracle run
-    per sequence. Three sequences run as the persistent kernel, six as the per-phase kernels."""
+    per sequence. Three sequences run as the persistent kernel, six as the per-phase kernels,
+    forty as the per-phase kernels with the experts grouped (more than 8 tokens in the step)."""
     cfg = bt.config("tiny", max_positions=4096)
     rng = np.random.default_rng(41 + persistent)
     kw = cfg.n_head_kv * cfg.head_dim
