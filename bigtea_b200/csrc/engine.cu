@@ -200,7 +200,7 @@ static int pick_nst_cap(size_t slot_bytes, size_t fixed_bytes, size_t cap) {
 static int gemv_chunk(int T, int K, int slot_bytes) {
     if (T <= MAX_T) return MAX_T;
     const size_t cap = (size_t)max_dynamic_smem();
-    const size_t ring = (size_t)GEMV_WARPS * 2 * slot_bytes;
+    const size_t ring = (size_t)GEMV_WARPS * 2 * slot_bytes + (size_t)GEMV_WARPS * RED_WARP_FLOATS * 4;
     const size_t per = (size_t)(K / 256) * sizeof(ActBlock);
     long long n = cap > 1024 + 128 + ring ? (long long)((cap - 1024 - 128 - ring) / per) : MAX_T;
     if (n < MAX_T) n = MAX_T;

@@ -170,6 +170,9 @@ __device__ void run_prefetch(const PrefetchSpec &pf) {
 }
 
 // ====================================================================== GEMV
+// Per-warp scratch of the row reductions (RED_STRIDE, RED_WARP_FLOATS in kernels.cuh): 8 tokens
+// x 32 lanes, rows padded to 33 floats so that the lanes reading one superblock index of
+// different tokens hit different banks.
 // Persistent-style: the grid covers the SMs; CTA c owns a contiguous range of tiles; each
 // warp streams its tiles through a private ring of `nst` shared-memory slots with 1-D TMA
 // bulk copies (weights do not depend on the previous kernel, so the first slots are
@@ -186,6 +189,7 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_kernel(const __grid_consta
     uint8_t *ring = smem + 1024 + ((act_bytes + 127) & ~(size_t)127);
     uint8_t *myring = ring + (size_t)warp * p.nst * p.slot_bytes;
     uint64_t *mybar = bars + warp * p.nst;
+    float *red = reinterpret_cast<float *>(ring + (size_t)NWARP * p.nst * p.slot_bytes) + warp * RED_WARP_FLOATS;
 
     const long long u0 = (long long)blockIdx.x * p.total_tiles / gridDim.x;
     const long long u1 = (long long)(blockIdx.x + 1) * p.total_tiles / gridDim.x;
@@ -232,33 +236,41 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_kernel(const __grid_consta
         const uint8_t *tile = myring + (size_t)slot * p.slot_bytes;
         const long long tl = u - sg.tile0;
         const bool active = lane < sg.S;
-        const int rit = active ? lane / sg.nsb : 0, b = active ? lane % sg.nsb : 0;
-        const long long row = tl * sg.rpt + rit;
-        const bool writer = active && b == 0 && row < sg.rows;
-        for (int t = 0; t < p.T; t++) {
-            float v = 0.0f;
-            if (active) {
-                const ActBlock &ab = act[t * nsbK + b];
-                v = (sg.type == T_Q4_K) ? q4k_slot_dot(tile, sg.S, lane, ab) : q6k_slot_dot(tile, sg.S, lane, ab);
+        const int b = active ? lane % sg.nsb : 0;
+        // 8 tokens at a time: every lane's superblock partial to shared memory, then one lane
+        // per (row, token) adds the row's nsb partials in superblock order (C4)
+        for (int t0 = 0; t0 < p.T; t0 += 8) {
+            const int tn = p.T - t0 < 8 ? p.T - t0 : 8;
+            for (int i = 0; i < tn; i++) {
+                float v = 0.0f;
+                if (active) {
+                    const ActBlock &ab = act[(t0 + i) * nsbK + b];
+                    v = (sg.type == T_Q4_K) ? q4k_slot_dot(tile, sg.S, lane, ab) : q6k_slot_dot(tile, sg.S, lane, ab);
+                }
+                red[i * RED_STRIDE + lane] = v;
             }
-            float acc = 0.0f;
-            for (int b2 = 0; b2 < sg.nsb; b2++) {
-                int srcl = rit * sg.nsb + b2;
-                float o = __shfl_sync(FULL, v, srcl < 32 ? srcl : 31);
-                acc = __fadd_rn(acc, o);
-            }
-            if (writer) {
-                float r = acc;
-                if (p.res) r = __fadd_rn(p.res[t * p.res_stride + sg.out_off + row], acc);
-                p.y[t * p.y_stride + sg.out_off + row] = r;
-                if (p.amax) {
-                    unsigned long long key = ((unsigned long long)((unsigned)total_key(r) ^ 0x80000000u) << 32) |
-                                             (unsigned)(sg.out_off + row);
+            __syncwarp();
+            for (int q = lane; q < sg.rpt * 8; q += 32) {
+                const int rr = q >> 3, i = q & 7;
+                const long long rrow = tl * sg.rpt + rr;
+                if (i < tn && rrow < sg.rows) {
+                    const float *rv = red + i * RED_STRIDE + rr * sg.nsb;
+                    float acc = 0.0f;
+                    for (int b2 = 0; b2 < sg.nsb; b2++) acc = __fadd_rn(acc, rv[b2]);
+                    const int t = t0 + i;
+                    float r = acc;
+                    if (p.res) r = __fadd_rn(p.res[t * p.res_stride + sg.out_off + rrow], acc);
+                    p.y[t * p.y_stride + sg.out_off + rrow] = r;
+                    if (p.amax) {
+                        unsigned long long key = ((unsigned long long)((unsigned)total_key(r) ^ 0x80000000u) << 32) |
+                                                 (unsigned)(sg.out_off + rrow);
 #pragma unroll
-                    for (int tt = 0; tt < MAX_T; tt++)
-                        if (tt == t && key > best[tt]) best[tt] = key;
+                        for (int tt = 0; tt < MAX_T; tt++)
+                            if (tt == t && key > best[tt]) best[tt] = key;
+                    }
                 }
             }
+            __syncwarp();
         }
         __syncwarp();
         if (lane == 0 && j + p.nst < nmine) {
@@ -294,7 +306,8 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_kernel(const __grid_consta
 
 size_t gemv_smem_bytes(const GemvArgs &a) {
     size_t act = (size_t)a.T * (a.K / 256) * sizeof(ActBlock);
-    return 1024 + ((act + 127) & ~(size_t)127) + (size_t)GEMV_WARPS * a.nst * a.slot_bytes;
+    return 1024 + ((act + 127) & ~(size_t)127) + (size_t)GEMV_WARPS * a.nst * a.slot_bytes +
+           (size_t)GEMV_WARPS * RED_WARP_FLOATS * 4;
 }
 
 template <typename Kern, typename Arg>
@@ -597,6 +610,8 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gateup_grouped_kernel(const __g
     r.base = smem + 1024 + ((act_bytes + 127) & ~(size_t)127) + (size_t)warp * p.nst * p.slot_bytes;
     r.bars = reinterpret_cast<uint64_t *>(smem) + warp * p.nst;
     r.issued = r.done = 0;
+    float *red = reinterpret_cast<float *>(smem + 1024 + ((act_bytes + 127) & ~(size_t)127) +
+                                           (size_t)NWARP * p.nst * p.slot_bytes) + warp * 2 * RED_WARP_FLOATS;
     if (lane == 0) {
         for (int i = 0; i < p.nst; i++) mbar_init(&r.bars[i], 1);
         fence_mbar_init();
@@ -652,29 +667,38 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gateup_grouped_kernel(const __g
                 const int tile = lo + warp + j * NWARP;
                 const uint8_t *gt = r.base + (size_t)slot * r.slot_bytes, *ut = gt + p.g_tile_bytes;
                 const bool active = lane < p.g_S;
-                const int rit = active ? lane / nsb : 0, b = active ? lane - rit * nsb : 0;
-                const int row = tile * p.g_rpt + rit;
+                const int b = active ? lane % nsb : 0;
+                for (int t0 = 0; t0 < mc; t0 += 8) {  // 8 tokens at a time, reduced as in gemv_kernel
+                    const int tn = mc - t0 < 8 ? mc - t0 : 8;
 #pragma unroll 1
-                for (int i = 0; i < mc; i++) {
-                    float rowv[2];
+                    for (int i = 0; i < tn; i++) {
 #pragma unroll 1
-                    for (int which = 0; which < 2; which++) {
-                        const uint8_t *tl = which ? ut : gt;
-                        const int ty = which ? p.utype : p.gtype;
-                        float v = 0.0f;
-                        if (active) {
-                            const ActBlock &ab = act[i * nsb + b];
-                            v = ty == T_Q4_K ? q4k_slot_dot(tl, p.g_S, lane, ab) : q6k_slot_dot(tl, p.g_S, lane, ab);
+                        for (int which = 0; which < 2; which++) {
+                            const uint8_t *tl = which ? ut : gt;
+                            const int ty = which ? p.utype : p.gtype;
+                            float v = 0.0f;
+                            if (active) {
+                                const ActBlock &ab = act[(t0 + i) * nsb + b];
+                                v = ty == T_Q4_K ? q4k_slot_dot(tl, p.g_S, lane, ab) : q6k_slot_dot(tl, p.g_S, lane, ab);
+                            }
+                            red[which * RED_WARP_FLOATS + i * RED_STRIDE + lane] = v;
                         }
-                        float rr = 0.0f;
-                        for (int b2 = 0; b2 < nsb; b2++) {
-                            const int srcl = rit * nsb + b2;
-                            rr = __fadd_rn(rr, __shfl_sync(FULL, v, srcl < 32 ? srcl : 31));
-                        }
-                        rowv[which] = rr;
                     }
-                    if (active && b == 0 && row < p.F)
-                        p.act[(long long)tk_s[i] * p.F + row] = __fmul_rn(bt_silu(rowv[0]), rowv[1]);
+                    __syncwarp();
+                    for (int q = lane; q < p.g_rpt * 8; q += 32) {
+                        const int rr = q >> 3, i = q & 7, rrow = tile * p.g_rpt + rr;
+                        if (i < tn && rrow < p.F) {
+                            const float *gv = red + i * RED_STRIDE + rr * nsb;
+                            const float *uv = gv + RED_WARP_FLOATS;
+                            float ag = 0.0f, au = 0.0f;
+                            for (int b2 = 0; b2 < nsb; b2++) {
+                                ag = __fadd_rn(ag, gv[b2]);
+                                au = __fadd_rn(au, uv[b2]);
+                            }
+                            p.act[(long long)tk_s[t0 + i] * p.F + rrow] = __fmul_rn(bt_silu(ag), au);
+                        }
+                    }
+                    __syncwarp();
                 }
                 __syncwarp();
                 if (lane == 0 && r.issued - base < ntw) {
@@ -817,7 +841,8 @@ __global__ void __launch_bounds__(256) down_combine_kernel(const __grid_constant
 
 size_t gateup_grouped_smem_bytes(const ExpertArgs &a) {
     size_t act = (size_t)GROUP_MAXM * a.g_nsb * sizeof(ActBlock);
-    return 1024 + ((act + 127) & ~(size_t)127) + (size_t)GEMV_WARPS * a.nst * a.slot_bytes;
+    return 1024 + ((act + 127) & ~(size_t)127) + (size_t)GEMV_WARPS * a.nst * a.slot_bytes +
+           (size_t)GEMV_WARPS * 2 * RED_WARP_FLOATS * 4;
 }
 size_t down_grouped_smem_bytes(const ExpertArgs &a) {
     size_t act = (size_t)GROUP_MAXM * a.d_nsb * sizeof(ActBlock);
@@ -1022,12 +1047,12 @@ cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl) {
 // heads [hq*G/2, hq*G/2+G/2), a sequential fmaf over the chunk's keys. A chunk that is the
 // whole context finalises its heads; otherwise it writes (acc, m, l) to scratch and
 // attn_combine_kernel merges the chunks in order (C8).
-constexpr int ATTN_THREADS = 256;
+constexpr int ATTN_THREADS = 128;
 constexpr int ATTN_PART_ROW = 132;  // floats per (chunk, head) partial: acc[128], m, l, 2 pad
 
 size_t attn_smem_bytes(int G, int max_chunks) {
     (void)max_chunks;
-    return 4 * 16384 + (size_t)128 * G * 4 + (size_t)ATTN_CHUNK * G * 4 + 2 * 8 * 8 * 4 + 64 + 1024;
+    return 65536 + (size_t)128 * G * 2 + (size_t)ATTN_CHUNK * G * 4 + (32 + 32 + 8 + 8) * 4 + 16 + 1024;
 }
 
 template <int N>
@@ -1044,34 +1069,62 @@ __device__ __forceinline__ void lds_vec(float (&dst)[N], const float *src) {
     }
 }
 
-// N f16 values (bit patterns) from shared memory
+
+// a0 += lo(q) * k, a1 += hi(q) * k with k the low (KHI false) or high half of kw (C8 terms)
+template <bool KHI>
+__device__ __forceinline__ void fma_qk(uint32_t qw, uint32_t kw, float &a0, float &a1) {
+    if constexpr (KHI)
+        asm("{\n\t.reg .b16 ql, qh, kl, kh;\n\tmov.b32 {ql, qh}, %2;\n\tmov.b32 {kl, kh}, %3;\n\t"
+            "fma.rn.f32.f16 %0, ql, kh, %0;\n\tfma.rn.f32.f16 %1, qh, kh, %1;\n\t}"
+            : "+f"(a0), "+f"(a1)
+            : "r"(qw), "r"(kw));
+    else
+        asm("{\n\t.reg .b16 ql, qh, kl, kh;\n\tmov.b32 {ql, qh}, %2;\n\tmov.b32 {kl, kh}, %3;\n\t"
+            "fma.rn.f32.f16 %0, ql, kl, %0;\n\tfma.rn.f32.f16 %1, qh, kl, %1;\n\t}"
+            : "+f"(a0), "+f"(a1)
+            : "r"(qw), "r"(kw));
+}
+// both halves of w as exact f32 values (FMA pipe)
+__device__ __forceinline__ float2 h2f2_fma(uint32_t w) {
+    float2 r;
+    asm("{\n\t.reg .b16 l, h;\n\tmov.b32 {l, h}, %2;\n\tadd.rn.f32.f16 %0, l, %3;\n\tadd.rn.f32.f16 %1, h, %3;\n\t}"
+        : "=f"(r.x), "=f"(r.y)
+        : "r"(w), "f"(-0.0f));
+    return r;
+}
 template <int N>
-__device__ __forceinline__ void lds_half(uint16_t (&dst)[N], const uint16_t *src) {
+__device__ __forceinline__ void ldw_n(uint32_t (&dst)[N], const uint32_t *src) {
     if constexpr (N == 4) {
-        const uint2 v = *reinterpret_cast<const uint2 *>(src);
-        dst[0] = lo16(v.x); dst[1] = hi16(v.x); dst[2] = lo16(v.y); dst[3] = hi16(v.y);
+        const uint4 v = *reinterpret_cast<const uint4 *>(src);
+        dst[0] = v.x; dst[1] = v.y; dst[2] = v.z; dst[3] = v.w;
     } else if constexpr (N == 2) {
-        const uint32_t v = *reinterpret_cast<const uint32_t *>(src);
-        dst[0] = lo16(v); dst[1] = hi16(v);
+        const uint2 v = *reinterpret_cast<const uint2 *>(src);
+        dst[0] = v.x; dst[1] = v.y;
     } else {
 #pragma unroll
         for (int k = 0; k < N; k++) dst[k] = src[k];
     }
 }
 
+// One CTA of 128 threads per (chunk c, kv head g, token t): the chunk's K/V pages by TMA (one
+// lane per page), q rounded to f16 in shared memory, then
+//   scores: thread = key, all G heads, dims in order (C8: q.k as f16 x f16 + f32 fmas);
+//   chunk max, exp and the P3 sum (32-key butterflies, the 4 warp sums in order);
+//   P*V: thread = dims 2dp, 2dp+1 and heads hq*G/2 .. +G/2, keys in order;
+// and writes the chunk's partial (acc, m, l), or the output when the context is one chunk.
 template <int G>
-__global__ void __launch_bounds__(ATTN_THREADS, 2)
+__global__ void __launch_bounds__(ATTN_THREADS, 3)
     attn_kernel(const __grid_constant__ AttnArgs p, const __grid_constant__ CUtensorMap tmap) {
-    constexpr int D = 128, HPT = G / 2, CH = ATTN_CHUNK;
+    constexpr int D = 128, HPT = G / 2, CH = ATTN_CHUNK, QWORDS = G / 2;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
     uint8_t *const K0 = smem, *const K1 = smem + 16384, *const V0 = smem + 32768, *const V1 = smem + 49152;
-    uint16_t *qs = reinterpret_cast<uint16_t *>(smem + 65536);  // [D][G] q rounded to f16 (bits)
-    float *ps = reinterpret_cast<float *>(smem + 65536 + D * G * 4);  // [CH][G]
-    float *red = ps + CH * G;                             // [8 warps][8]
-    float *red2 = red + 64;                               // [4 key groups][8]
-    uint64_t *bar = reinterpret_cast<uint64_t *>(red2 + 64);
-    __shared__ float s_m[8], s_l[8];
+    uint16_t *qs = reinterpret_cast<uint16_t *>(smem + 65536);        // [D][G] f16 bits
+    float *ps = reinterpret_cast<float *>(smem + 65536 + D * G * 2);  // [CH][G]
+    float *red = ps + CH * G;                                         // [4][8]
+    float *red2 = red + 32;                                           // [4][8]
+    float *s_m = red2 + 32, *s_l = s_m + 8;
+    uint64_t *bar = reinterpret_cast<uint64_t *>(s_l + 8);
 
     const int c = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -1090,13 +1143,16 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2)
         fence_mbar_init();
     }
     __syncthreads();
-    if (tid == 0) {
-        prefetch_tmap(&tmap);
-        mbar_arrive_expect_tx(bar, npages * 8192);
-        for (int pg = 0; pg < npages; pg++) {
-            int blk = p.block_table[seq * p.max_blocks + (base >> 4) + pg];
-            int rowK = (int)(((((long long)p.layer * p.n_blocks + blk) * 2 + 0) * p.HK + g) * 16);
-            int rowV = rowK + p.HK * 16;
+    if (warp == 0) {
+        if (lane == 0) {
+            prefetch_tmap(&tmap);
+            mbar_arrive_expect_tx(bar, npages * 8192);
+        }
+        __syncwarp();
+        for (int pg = lane; pg < npages; pg += 32) {
+            const int blk = p.block_table[seq * p.max_blocks + (base >> 4) + pg];
+            const int rowK = (int)(((((long long)p.layer * p.n_blocks + blk) * 2 + 0) * p.HK + g) * 16);
+            const int rowV = rowK + p.HK * 16;
             tma_load_2d(K0 + pg * 2048, &tmap, 0, rowK, bar);
             tma_load_2d(K1 + pg * 2048, &tmap, 64, rowK, bar);
             tma_load_2d(V0 + pg * 2048, &tmap, 0, rowV, bar);
@@ -1105,7 +1161,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2)
     }
     pdl_trigger();
     for (int i = tid; i < D * G; i += ATTN_THREADS) {
-        int h = i / D, d = i % D;
+        const int h = i / D, d = i % D;
         qs[d * G + h] = __half_as_ushort(__float2half_rn(p.q[(long long)t * p.H * D + (g * G + h) * D + d]));
     }
     __syncthreads();
@@ -1115,49 +1171,62 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2)
         return;
     }
 
-    // ---- scores: key k, heads hh*HPT .. +HPT
-    const int hh = tid >> 7, k = tid & 127;
+    // ---- scores
+    const int k = tid;
     const bool valid = k < cnt;
-    float sc[HPT];
+    float sc[G];
 #pragma unroll
-    for (int h = 0; h < HPT; h++) sc[h] = 0.0f;
+    for (int h = 0; h < G; h++) sc[h] = 0.0f;
+    {
+        const uint8_t *krow = K0 + k * 128;
+        const int ksw = k & 7;
+        const uint32_t *qw = reinterpret_cast<const uint32_t *>(qs);
 #pragma unroll 2
-    for (int c16 = 0; c16 < 16; c16++) {
-        const uint8_t *kr = (c16 < 8) ? K0 : K1;
-        const uint4 w = *reinterpret_cast<const uint4 *>(kr + k * 128 + (((c16 & 7) ^ (k & 7)) << 4));
-        const uint32_t kw[4] = {w.x, w.y, w.z, w.w};
+        for (int c16 = 0; c16 < 16; c16++) {
+            const uint4 w = *reinterpret_cast<const uint4 *>((c16 < 8 ? krow : krow + 16384) + (((c16 & 7) ^ ksw) << 4));
+            const uint32_t kw[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-        for (int e = 0; e < 8; e++) {
-            const uint16_t kh = (e & 1) ? hi16(kw[e >> 1]) : lo16(kw[e >> 1]);
-            uint16_t q[HPT];
-            lds_half<HPT>(q, qs + (c16 * 8 + e) * G + hh * HPT);
+            for (int e = 0; e < 8; e++) {
+                uint32_t q[QWORDS];
+                ldw_n<QWORDS>(q, qw + (c16 * 8 + e) * QWORDS);
 #pragma unroll
-            for (int h = 0; h < HPT; h++) sc[h] = fma_f16(q[h], kh, sc[h]);  // = fmaf((float)q, (float)k, sc)
+                for (int j = 0; j < QWORDS; j++) {
+                    if (e & 1)
+                        fma_qk<true>(q[j], kw[e >> 1], sc[2 * j], sc[2 * j + 1]);
+                    else
+                        fma_qk<false>(q[j], kw[e >> 1], sc[2 * j], sc[2 * j + 1]);
+                }
+            }
         }
     }
     const float NEG_INF = -__int_as_float(0x7f800000);
 #pragma unroll
-    for (int h = 0; h < HPT; h++) {
+    for (int h = 0; h < G; h++) {
         sc[h] = valid ? __fmul_rn(sc[h], p.scale) : NEG_INF;
-        float m = warp_max(sc[h]);
+        const float m = warp_max(sc[h]);
         if (lane == 0) red[warp * 8 + h] = m;
     }
     __syncthreads();
-    if (tid < G) {  // head tid lives in warps (tid / HPT) * 4 .. +3, slot tid % HPT
-        const int w0 = (tid / HPT) * 4, slot = tid % HPT;
-        float m = red[w0 * 8 + slot];
-        for (int w = 1; w < 4; w++) m = fmaxf(m, red[(w0 + w) * 8 + slot]);
+    if (tid < G) {
+        float m = red[tid];
+        for (int w = 1; w < 4; w++) m = fmaxf(m, red[w * 8 + tid]);
         s_m[tid] = m;
     }
     __syncthreads();
-    // ---- probabilities and the P3 sum: warp (hh, q) holds key group q
 #pragma unroll
-    for (int h = 0; h < HPT; h++) {
-        const int head = hh * HPT + h;
-        const float pr = valid ? bt_exp(__fsub_rn(sc[h], s_m[head])) : 0.0f;
-        ps[k * G + head] = pr;
+    for (int h = 0; h < G; h++) {
+        const float pr = valid ? bt_exp(__fsub_rn(sc[h], s_m[h])) : 0.0f;
+        sc[h] = pr;
         const float ws = butterfly_sum(pr);
-        if (lane == 0) red2[(warp & 3) * 8 + head] = ws;
+        if (lane == 0) red2[warp * 8 + h] = ws;
+    }
+    if constexpr (G % 4 == 0) {
+        float4 *prow = reinterpret_cast<float4 *>(ps + k * G);
+#pragma unroll
+        for (int h4 = 0; h4 < G / 4; h4++) prow[h4] = make_float4(sc[4 * h4], sc[4 * h4 + 1], sc[4 * h4 + 2], sc[4 * h4 + 3]);
+    } else {
+#pragma unroll
+        for (int h = 0; h < G; h++) ps[k * G + h] = sc[h];
     }
     __syncthreads();
     if (tid < G) {
@@ -1165,42 +1234,47 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2)
         for (int w = 0; w < CH / 32; w++) l = __fadd_rn(l, red2[w * 8 + tid]);
         s_l[tid] = l;
     }
-    // ---- P*V: column d, heads hq*HPT .. +HPT
-    const int d = tid & 127, hq = tid >> 7;
-    float acc[HPT];
+    // ---- P*V
+    const int dp = tid & 63, hq = tid >> 6;
+    float acc0[HPT], acc1[HPT];
 #pragma unroll
-    for (int h = 0; h < HPT; h++) acc[h] = 0.0f;
+    for (int h = 0; h < HPT; h++) acc0[h] = acc1[h] = 0.0f;
     {
-        const int cc = (d & 63) >> 3;
+        const int d = 2 * dp, cc = (d & 63) >> 3;
         const uint8_t *vcol = ((d < 64) ? V0 : V1) + (d & 7) * 2;
         int off[8];
 #pragma unroll
         for (int kk = 0; kk < 8; kk++) off[kk] = kk * 128 + ((cc ^ kk) << 4);
+        const float *pb0 = ps + hq * HPT;
         for (int j0 = 0; j0 < cnt; j0 += 8) {
             const uint8_t *vb = vcol + j0 * 128;
-            const float *pb = ps + j0 * G + hq * HPT;
+            const float *pb = pb0 + j0 * G;
 #pragma unroll
             for (int kk = 0; kk < 8; kk++) {
                 if (j0 + kk < cnt) {
-                    const float vf = h2f_fma(*reinterpret_cast<const uint16_t *>(vb + off[kk]));
+                    const float2 vf = h2f2_fma(*reinterpret_cast<const uint32_t *>(vb + off[kk]));
                     float pj[HPT];
                     lds_vec<HPT>(pj, pb + kk * G);
 #pragma unroll
-                    for (int h = 0; h < HPT; h++) acc[h] = fmaf(pj[h], vf, acc[h]);
+                    for (int h = 0; h < HPT; h++) {
+                        acc0[h] = fmaf(pj[h], vf.x, acc0[h]);
+                        acc1[h] = fmaf(pj[h], vf.y, acc1[h]);
+                    }
                 }
             }
         }
     }
     __syncthreads();
-    const int QW = p.H * D;
+    const int QW = p.H * D, d = 2 * dp;
     if (nc == 1) {
 #pragma unroll
         for (int h = 0; h < HPT; h++) {
             const int head = hq * HPT + h;
             const float f = bt_exp(__fsub_rn(s_m[head], s_m[head]));
             const float L = fmaf(s_l[head], f, 0.0f);
-            const float O = fmaf(acc[h], f, 0.0f);
-            p.out[(long long)t * QW + (g * G + head) * D + d] = __fdiv_rn(O, L);
+            float *o = p.out + (long long)t * QW + (g * G + head) * D + d;
+            o[0] = __fdiv_rn(fmaf(acc0[h], f, 0.0f), L);
+            o[1] = __fdiv_rn(fmaf(acc1[h], f, 0.0f), L);
         }
         return;
     }
@@ -1209,8 +1283,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, 2)
     for (int h = 0; h < HPT; h++) {
         const int head = hq * HPT + h;
         float *pp = p.part + pbase + ((long long)c * G + head) * ATTN_PART_ROW;
-        pp[d] = acc[h];
-        if (d == 0) {
+        *reinterpret_cast<float2 *>(pp + d) = make_float2(acc0[h], acc1[h]);
+        if (dp == 0) {
             pp[D] = s_m[head];
             pp[D + 1] = s_l[head];
         }

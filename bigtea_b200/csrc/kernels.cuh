@@ -12,6 +12,8 @@ constexpr int MAX_T = 8;        // tokens one GEMV / expert launch carries in sh
 constexpr int MAX_K = 16;       // experts used per token
 constexpr int ATTN_CHUNK = 128; // attention keys per chunk (contract C8)
 constexpr int GEMV_WARPS = 8;
+// per-warp scratch of the row reductions: 8 tokens x 32 lanes, rows padded to 33 floats
+constexpr int RED_STRIDE = 33, RED_WARP_FLOATS = 8 * RED_STRIDE;
 
 // Ranges to start pulling into L2 while a kernel runs (the next kernels' inputs), and
 // optionally one layer's KV pages of the step's sequences.
