@@ -13,7 +13,9 @@ of uniform-random token ids into the f16 paged KV cache. A step = one decode tok
 
 N>1 (torchrun): replicas -- every rank runs the same batch-1 decode on its own GPU (weak
 scaling; no collective on the batch-1 path); rank 0 reports the sum of tok/s with the step
-time taken as the max over ranks.
+time taken as the max over ranks. The batched workload then runs expert parallel: each rank
+holds its own batch of sequences and computes 1/N of the experts for every rank's tokens, the
+rows exchanged over NCCL (weak scaling: global batch = N x batch).
 
 --impl reference: the reference's CPU implementation of the path is not buildable here (Rust,
 no toolchain; ggml absent), so this arm times the CPU oracle restatement (`kind: "port"`) on
@@ -228,6 +230,9 @@ def run_ours(args, rank, world, local_rank):
         for sq, c in enumerate(ctxs):
             cache2.set_positions(int(c), sq)
         first2 = rng2.integers(0, cfg.n_vocab, B)
+        if world > 1:
+            # expert parallelism: each rank computes NE/world experts for every rank's tokens
+            engine.enable_ep_torch()
         runner.generate_greedy(cache2, first2, args.warmup)
         sync_ranks(world)
         runner.generate_greedy(cache2, first2, args.steps)
@@ -238,7 +243,10 @@ def run_ours(args, rank, world, local_rank):
                               f"mean {float(ctxs.mean()):.0f}",
                    "kv": "paged f16, 16-token blocks, seeded random contents",
                    "routing": "the synthetic router (no Zipf popularity bias)",
-                   "path": "per-phase kernels (single-token steps of more than 4 sequences)"}
+                   "path": "per-phase kernels (single-token steps of more than 4 sequences)",
+                   "parallelism": (f"expert parallel over {world} GPUs: {B} sequences per rank, experts split "
+                                   f"{cfg.n_expert // world} per rank, rows exchanged by NCCL send/recv"
+                                   if world > 1 else "single GPU")}
         cache2.close()
     # per-phase kernels: the expert kernels' times; the persistent step: its gate/up and down
     # phases (slowest CTA, from the in-kernel timeline)

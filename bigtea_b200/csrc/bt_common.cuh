@@ -207,7 +207,7 @@ __device__ __forceinline__ void bulk_g2s(void *dst, const void *src, uint32_t by
         : "memory");
 }
 
-// 2-D tiled tensor copy global -> shared through a CUtensorMap (TMA). No multicast.
+// 2-D tiled tensor copy global -> shared through a CUtensorMap (TMA), into this CTA only.
 __device__ __forceinline__ void tma_load_2d(void *dst, const void *tmap, int x, int y, uint64_t *bar) {
     asm volatile(
         "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "

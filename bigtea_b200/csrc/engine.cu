@@ -6,7 +6,9 @@
 // forward_cached (core/arch/src/stream.rs:586, 1793, 1933) and KvCache (core/arch/src/kv.rs).
 #include <cuda.h>
 #include <cuda_runtime.h>
+#include <dlfcn.h>
 #include <math.h>
+#include <nccl.h>  // types of the NCCL calls; the library itself is opened at run time
 #include <string.h>
 
 #include <chrono>
@@ -14,6 +16,7 @@
 #include <memory>
 #include <mutex>
 #include <string>
+#include <thread>
 #include <vector>
 
 #include "../../include/bigtea_decode.h"
@@ -111,6 +114,13 @@ struct bt_engine {
     int max_out = 0;
     DevBuf x, ffn_in, fn, qkv, qbuf, att, rlog, rcnt, sel_ids, sel_w, act, part, acnt;
     DevBuf g_count, g_off, g_list, g_active, g_nactive, dpart;  // grouped experts of batched steps
+    // expert parallelism (bt_engine_enable_ep): this rank computes experts [rank*NE/n, (rank+1)*NE/n)
+    bool ep = false;
+    int ep_rank = 0, ep_n = 1;
+    ncclComm_t ep_comm = nullptr;
+    int ep_timeout_ms = 60000;  // a host wait on an expert-parallel step longer than this aborts the exchange
+    bool ep_aborted = false;
+    DevBuf ep_send_meta, ep_send_rows, ep_recv_meta, ep_recv_rows, ep_act, ep_dpart, ep_ret;
     DevBuf dbg_ids, dbg_w;  // [n_layer][TB][K]
     DevBuf tokens, seq_of, local_idx, pos_of, single, x_rows;
     DevBuf st_seq, st_ntok, st_lrow, next_tok, gen_out, gen_count, logits, amax;
@@ -307,6 +317,86 @@ static int validate_desc(const bt_model_desc *d) {
     if (d->n_embd % 256 || d->n_ff_exp % 256 || (d->n_head * d->head_dim) % 256)
         return fail(BT_ERR_UNSUPPORTED, "n_embd, n_ff_exp and n_head*head_dim must be multiples of 256");
     return BT_OK;
+}
+
+// ------------------------------------------------------------------ NCCL, opened at run time
+// Only expert parallelism needs NCCL, so the library is opened on first use (in a process that
+// already holds torch's NCCL, dlopen returns that one).
+struct NcclApi {
+    ncclResult_t (*GetUniqueId)(ncclUniqueId *);
+    ncclResult_t (*CommInitRank)(ncclComm_t *, int, ncclUniqueId, int);
+    ncclResult_t (*CommDestroy)(ncclComm_t);
+    ncclResult_t (*CommAbort)(ncclComm_t);
+    ncclResult_t (*CommGetAsyncError)(ncclComm_t, ncclResult_t *);
+    ncclResult_t (*GroupStart)();
+    ncclResult_t (*GroupEnd)();
+    ncclResult_t (*Send)(const void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    ncclResult_t (*Recv)(void *, size_t, ncclDataType_t, int, ncclComm_t, cudaStream_t);
+    const char *(*GetErrorString)(ncclResult_t);
+};
+
+static const NcclApi *nccl_api() {
+    static NcclApi api{};
+    static bool ok = false;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *h = dlopen("libnccl.so.2", RTLD_NOW | RTLD_GLOBAL);
+        if (!h) return;
+        api.GetUniqueId = reinterpret_cast<decltype(api.GetUniqueId)>(dlsym(h, "ncclGetUniqueId"));
+        api.CommInitRank = reinterpret_cast<decltype(api.CommInitRank)>(dlsym(h, "ncclCommInitRank"));
+        api.CommDestroy = reinterpret_cast<decltype(api.CommDestroy)>(dlsym(h, "ncclCommDestroy"));
+        api.CommAbort = reinterpret_cast<decltype(api.CommAbort)>(dlsym(h, "ncclCommAbort"));
+        api.CommGetAsyncError = reinterpret_cast<decltype(api.CommGetAsyncError)>(dlsym(h, "ncclCommGetAsyncError"));
+        api.GroupStart = reinterpret_cast<decltype(api.GroupStart)>(dlsym(h, "ncclGroupStart"));
+        api.GroupEnd = reinterpret_cast<decltype(api.GroupEnd)>(dlsym(h, "ncclGroupEnd"));
+        api.Send = reinterpret_cast<decltype(api.Send)>(dlsym(h, "ncclSend"));
+        api.Recv = reinterpret_cast<decltype(api.Recv)>(dlsym(h, "ncclRecv"));
+        api.GetErrorString = reinterpret_cast<decltype(api.GetErrorString)>(dlsym(h, "ncclGetErrorString"));
+        ok = api.GetUniqueId && api.CommInitRank && api.CommDestroy && api.CommAbort && api.CommGetAsyncError &&
+             api.GroupStart && api.GroupEnd && api.Send && api.Recv && api.GetErrorString;
+    });
+    return ok ? &api : nullptr;
+}
+
+#define NK(call)                                                                                     \
+    do {                                                                                             \
+        ncclResult_t r_ = (call);                                                                    \
+        if (r_ != ncclSuccess) return fail(BT_ERR_CUDA, std::string("NCCL: ") + nccl_api()->GetErrorString(r_)); \
+    } while (0)
+
+// Waits for the engine's stream. Without expert parallelism this is cudaStreamSynchronize. With
+// it, a step can only finish when every rank takes part in the exchange, so the wait is bounded:
+// past ep_timeout_ms (or on an NCCL error) the communicator is aborted, which ends its pending
+// transfers, and the engine refuses further steps (BT_ERR_TIMEOUT).
+static int wait_stream(bt_engine *e) {
+    if (!e->ep || !e->ep_comm) {
+        CK(cudaStreamSynchronize(e->st));
+        return BT_OK;
+    }
+    const auto t0 = std::chrono::steady_clock::now();
+    for (;;) {
+        cudaError_t q = cudaStreamQuery(e->st);
+        if (q == cudaSuccess) return BT_OK;
+        if (q != cudaErrorNotReady) CK(q);
+        ncclResult_t ar = ncclSuccess;
+        nccl_api()->CommGetAsyncError(e->ep_comm, &ar);
+        const double ms = std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now() - t0).count();
+        if ((ar != ncclSuccess && ar != ncclInProgress) || ms > e->ep_timeout_ms) {
+            nccl_api()->CommAbort(e->ep_comm);
+            e->ep_comm = nullptr;
+            e->ep_aborted = true;
+            // the aborted transfers return; the kernels queued after them finish on stale rows
+            const auto t1 = std::chrono::steady_clock::now();
+            while (cudaStreamQuery(e->st) == cudaErrorNotReady &&
+                   std::chrono::steady_clock::now() - t1 < std::chrono::seconds(10))
+                std::this_thread::sleep_for(std::chrono::microseconds(200));
+            return fail(BT_ERR_TIMEOUT, ar != ncclSuccess && ar != ncclInProgress
+                                            ? std::string("expert-parallel exchange failed: ") + nccl_api()->GetErrorString(ar)
+                                            : "expert-parallel exchange timed out (a rank did not take part); the "
+                                              "communicator was aborted");
+        }
+        std::this_thread::sleep_for(std::chrono::microseconds(ms < 5 ? 5 : 100));
+    }
 }
 
 static int alloc_scratch(bt_engine *e) {
@@ -629,6 +719,7 @@ extern "C" void bt_engine_destroy(bt_engine *e) {
     cudaSetDevice(e->device);
     if (e->st) cudaStreamSynchronize(e->st);
     for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
+    if (e->ep_comm && nccl_api()) nccl_api()->CommDestroy(e->ep_comm);
     for (auto &p : e->ev_pool) {
         cudaEventDestroy(p.first);
         cudaEventDestroy(p.second);
@@ -1016,7 +1107,7 @@ static int upload_plan(bt_engine *e, const StepPlan &p) {
 // Can this step run as one persistent kernel? Single-token steps of up to STEP_MAX_T
 // sequences whose activations fit the kernel's shared memory.
 static bool step_eligible(const bt_engine *e, const bt_kv *kv, const StepPlan &p) {
-    if (!e->mega || p.T > STEP_MAX_T || p.out_first != 0 || (int)p.x_rows.size() != p.T) return false;
+    if (!e->mega || e->ep || p.T > STEP_MAX_T || p.out_first != 0 || (int)p.x_rows.size() != p.T) return false;
     for (int t = 0; t < p.T; t++)
         if (!p.single[t] || p.local_idx[t] != 0 || p.x_rows[t] != t || p.st_lrow[t] != t) return false;
     if ((int)p.st_seq.size() != p.T) return false;
@@ -1104,6 +1195,7 @@ static int launch_persistent_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bo
 
 // All kernels of one step on e->st. Capturable: no host synchronisation inside.
 static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) {
+    if (e->ep_aborted) return fail(BT_ERR_TIMEOUT, "the expert-parallel communicator was aborted by an earlier failure");
     if (step_eligible(e, kv, p)) return launch_persistent_step(e, kv, p, greedy);
     const bt_model_desc &d = e->d;
     const int T = p.T, E = d.n_embd, H = d.n_head, HK = d.n_head_kv, D = d.head_dim;
@@ -1241,7 +1333,114 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             CK(launch_router(a, st, pdl));
             timer_end(e);
         }
-        if (T > MAX_T) {  // grouped: each selected expert's weights once per step
+        if (e->ep) {  // expert parallelism: rows to the owning ranks, experts there, rows back
+            const int S = e->TB * K, n = e->ep_n, per = NE / n;
+            const NcclApi *api = nccl_api();
+            EpPackArgs pa{};
+            pa.sel_ids = e->sel_ids.as<int>();
+            pa.fn = e->fn.as<float>();
+            pa.T = T;
+            pa.K = K;
+            pa.E = E;
+            pa.ranks = n;
+            pa.per = per;
+            pa.slots = S;
+            pa.send_meta = e->ep_send_meta.as<int>();
+            pa.send_rows = e->ep_send_rows.as<float>();
+            timer_begin(e, "ep_pack");
+            CK(launch_ep_pack(pa, st, pdl));
+            timer_end(e);
+            timer_begin(e, "ep_dispatch");
+            NK(api->GroupStart());
+            for (int r = 0; r < n; r++) {
+                NK(api->Send(pa.send_meta + (size_t)r * S, S, ncclInt32, r, e->ep_comm, st));
+                NK(api->Send(pa.send_rows + (size_t)r * S * E, (size_t)S * E, ncclFloat32, r, e->ep_comm, st));
+                NK(api->Recv(e->ep_recv_meta.as<int>() + (size_t)r * S, S, ncclInt32, r, e->ep_comm, st));
+                NK(api->Recv(e->ep_recv_rows.as<float>() + (size_t)r * S * E, (size_t)S * E, ncclFloat32, r,
+                             e->ep_comm, st));
+            }
+            NK(api->GroupEnd());
+            timer_end(e);
+            GroupArgs ga{};
+            ga.sel_ids = e->ep_recv_meta.as<int>();
+            ga.T = n * e->TB;
+            ga.K = K;
+            ga.NE = NE;
+            ga.g_count = e->g_count.as<int>();
+            ga.g_off = e->g_off.as<int>();
+            ga.g_list = e->g_list.as<int>();
+            ga.g_active = e->g_active.as<int>();
+            ga.g_nactive = e->g_nactive.as<int>();
+            timer_begin(e, "expert_group");
+            CK(launch_group(ga, st, false));
+            timer_end(e);
+            ExpertArgs a{};
+            a.gate = l.gate.buf.as<uint8_t>();
+            a.up = l.up.buf.as<uint8_t>();
+            a.down = l.down.buf.as<uint8_t>();
+            a.gtype = l.gate.type;
+            a.utype = l.up.type;
+            a.dtype = l.down.type;
+            a.g_nsb = l.gate.g.nsb;
+            a.g_rpt = l.gate.g.rpt;
+            a.g_S = l.gate.g.S;
+            a.g_tile_bytes = l.gate.g.tile_bytes;
+            a.g_n_tiles = (int)l.gate.g.n_tiles;
+            a.u_tile_bytes = l.up.g.tile_bytes;
+            a.g_expert_bytes = l.gate.mat_bytes;
+            a.u_expert_bytes = l.up.mat_bytes;
+            a.d_expert_bytes = l.down.mat_bytes;
+            a.d_nsb = l.down.g.nsb;
+            a.d_tile_bytes = l.down.g.tile_bytes;
+            a.E = E;
+            a.F = F;
+            a.K = K;
+            a.T = T;
+            a.workers = (int)d.expert_workers;
+            a.err = err;
+            a.g_count = ga.g_count;
+            a.g_off = ga.g_off;
+            a.g_list = ga.g_list;
+            a.g_active = ga.g_active;
+            a.g_nactive = ga.g_nactive;
+            a.row_div = 1;  // received rows are indexed by their slot
+            a.fn = e->ep_recv_rows.as<float>();
+            a.act = e->ep_act.as<float>();
+            a.dpart = e->ep_dpart.as<float>();
+            const size_t cap = (size_t)max_dynamic_smem();
+            a.slot_bytes = a.g_tile_bytes + a.u_tile_bytes;
+            a.nst = 1;
+            a.nst = pick_nst_cap(a.slot_bytes, gateup_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
+            timer_begin(e, "expert_gateup");
+            CK(launch_gateup_grouped(a, e->n_sm, st, pdl));
+            timer_end(e);
+            a.slot_bytes = down_group_rows(a) * a.d_tile_bytes;
+            a.nst = 1;
+            a.nst = pick_nst_cap(a.slot_bytes, down_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
+            timer_begin(e, "expert_down");
+            CK(launch_down_grouped(a, e->n_sm, st, pdl));
+            timer_end(e);
+            timer_begin(e, "ep_combine_exchange");
+            NK(api->GroupStart());
+            for (int r = 0; r < n; r++) {
+                NK(api->Send(e->ep_dpart.as<float>() + (size_t)r * S * E, (size_t)S * E, ncclFloat32, r, e->ep_comm, st));
+                NK(api->Recv(e->ep_ret.as<float>() + (size_t)r * S * E, (size_t)S * E, ncclFloat32, r, e->ep_comm, st));
+            }
+            NK(api->GroupEnd());
+            timer_end(e);
+            a.sel_ids = e->sel_ids.as<int>();
+            a.sel_w = e->sel_w.as<float>();
+            a.ffn_in = e->ffn_in.as<float>();
+            a.x_out = e->x.as<float>();
+            a.single = e->single.as<unsigned char>();
+            a.dpart = e->ep_ret.as<float>();
+            a.ep_ranks = n;
+            a.ep_per = per;
+            a.ep_slots = S;
+            timer_begin(e, "expert_combine");
+            CK(launch_down_combine(a, st, false));
+            timer_end(e);
+        } else if (T > MAX_T) {  // grouped: each selected expert's weights once per step
             GroupArgs ga{};
             ga.sel_ids = e->sel_ids.as<int>();
             ga.T = T;
@@ -1292,6 +1491,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.g_active = ga.g_active;
             a.g_nactive = ga.g_nactive;
             a.dpart = e->dpart.as<float>();
+            a.row_div = K;  // list entry t*K + k uses token t's row
             const size_t cap = (size_t)max_dynamic_smem();
             a.slot_bytes = a.g_tile_bytes + a.u_tile_bytes;
             a.nst = 1;
@@ -1309,7 +1509,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             CK(launch_down_combine(a, st, pdl));
             timer_end(e);
         }
-        for (int t0 = 0; T <= MAX_T && t0 < T; t0 += MAX_T) {
+        for (int t0 = 0; !e->ep && T <= MAX_T && t0 < T; t0 += MAX_T) {
             int tg = T - t0 < MAX_T ? T - t0 : MAX_T;
             ExpertArgs a{};
             a.gate = l.gate.buf.as<uint8_t>();
@@ -1407,7 +1607,8 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
 static int check_err(bt_engine *e) {
     int h = 0;
     CK(cudaMemcpyAsync(&h, e->err.p, 4, cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
+    int r = wait_stream(e);
+    if (r) return r;
     if (h) {
         CK(cudaMemsetAsync(e->err.p, 0, 4, e->st));
         CK(cudaStreamSynchronize(e->st));
@@ -1488,7 +1689,7 @@ extern "C" int bt_forward(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, cons
     if ((r = check_err(e))) return r;
     if (logits_out)
         CK(cudaMemcpyAsync(logits_out, e->logits.p, (size_t)n_seqs * e->d.n_vocab * 4, cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
+    if ((r = wait_stream(e))) return r;
     for (uint32_t i = 0; i < n_seqs; i++) {
         uint32_t s = seq_ids[i];
         kv->len[s] += n_tokens[i];
@@ -1549,7 +1750,7 @@ static int greedy_finish(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, uint3
         CK(cudaMemcpyAsync(tokens_out, e->gen_out.p, (size_t)n_steps * n_seqs * 4, cudaMemcpyDeviceToHost, e->st));
     if (last_logits && n_steps)
         CK(cudaMemcpyAsync(last_logits, e->logits.p, (size_t)n_seqs * e->d.n_vocab * 4, cudaMemcpyDeviceToHost, e->st));
-    CK(cudaStreamSynchronize(e->st));
+    if ((r = wait_stream(e))) return r;
     for (uint32_t i = 0; i < n_seqs; i++) {
         uint32_t s = seq_ids[i];
         kv->len[s] += n_steps;
@@ -1588,7 +1789,11 @@ extern "C" int bt_generate_greedy(bt_engine *e, bt_kv *kv, const uint32_t *seq_i
     CK(cudaEventRecord(a, e->st));
     for (uint32_t s = 0; s < n_steps; s++) CK(cudaGraphLaunch(it->second, e->st));
     CK(cudaEventRecord(b, e->st));
-    CK(cudaEventSynchronize(b));
+    if ((r = wait_stream(e))) {
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        return r;
+    }
     float ms = 0;
     cudaEventElapsedTime(&ms, a, b);
     cudaEventDestroy(a);
@@ -1619,7 +1824,7 @@ extern "C" int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_id
     e->pdl = false;  // serialised launches: each event pair brackets one kernel
     for (uint32_t s = 0; s < n_steps && !r; s++) {
         r = launch_step(e, kv, p, true);
-        CK(cudaStreamSynchronize(e->st));
+        if (!r) r = wait_stream(e);
         timer_collect(e);
     }
     e->timing = false;
@@ -1734,6 +1939,61 @@ extern "C" int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_id
     return BT_OK;
 }
 
+// ------------------------------------------------------------------ expert parallelism
+extern "C" int bt_ep_unique_id(void *out, size_t nbytes) {
+    if (!out || nbytes < sizeof(ncclUniqueId)) return fail(BT_ERR_INVALID, "the unique id needs 128 bytes");
+    const NcclApi *api = nccl_api();
+    if (!api) return fail(BT_ERR_UNSUPPORTED, "libnccl.so.2 could not be loaded");
+    ncclUniqueId id;
+    NK(api->GetUniqueId(&id));
+    memcpy(out, &id, sizeof(id));
+    return BT_OK;
+}
+
+extern "C" int bt_engine_enable_ep(bt_engine *e, const void *unique_id, size_t nbytes, int rank, int n_ranks) {
+    if (!e || !unique_id || nbytes < sizeof(ncclUniqueId)) return fail(BT_ERR_INVALID, "bad argument");
+    if (n_ranks < 1 || rank < 0 || rank >= n_ranks) return fail(BT_ERR_INVALID, "rank out of range");
+    if (e->ep) return fail(BT_ERR_INVALID, "expert parallelism is already enabled");
+    const bt_model_desc &d = e->d;
+    if (d.n_expert % (uint32_t)n_ranks) return fail(BT_ERR_UNSUPPORTED, "the expert count must divide by the rank count");
+    const NcclApi *api = nccl_api();
+    if (!api) return fail(BT_ERR_UNSUPPORTED, "libnccl.so.2 could not be loaded");
+    CK(cudaSetDevice(e->device));
+    const size_t S = (size_t)e->TB * d.n_expert_used, E = d.n_embd, F = d.n_ff_exp, n = (size_t)n_ranks;
+    CK(e->ep_send_meta.alloc(n * S * 4));
+    CK(e->ep_recv_meta.alloc(n * S * 4));
+    CK(e->ep_send_rows.alloc(n * S * E * 4));
+    CK(e->ep_recv_rows.alloc(n * S * E * 4));
+    CK(e->ep_act.alloc(n * S * F * 4));
+    CK(e->ep_dpart.alloc(n * S * E * 4));
+    CK(e->ep_ret.alloc(n * S * E * 4));
+    CK(cudaMemsetAsync(e->ep_dpart.p, 0, n * S * E * 4, e->st));
+    CK(cudaMemsetAsync(e->ep_send_meta.p, 0xff, n * S * 4, e->st));
+    CK(e->g_list.alloc(n * S * 4));  // the grouped lists now cover every rank's slots
+    ncclUniqueId id;
+    memcpy(&id, unique_id, sizeof(id));
+    ncclComm_t comm = nullptr;
+    NK(api->CommInitRank(&comm, n_ranks, id, rank));
+    e->ep_comm = comm;
+    e->ep = true;
+    e->ep_rank = rank;
+    e->ep_n = n_ranks;
+    // one exchange of the slot metadata now: NCCL connects the peers on first use, which
+    // then happens outside any graph capture
+    NK(api->GroupStart());
+    for (int r = 0; r < n_ranks; r++) {
+        NK(api->Send(e->ep_send_meta.as<int>() + (size_t)r * S, S, ncclInt32, r, comm, e->st));
+        NK(api->Recv(e->ep_recv_meta.as<int>() + (size_t)r * S, S, ncclInt32, r, comm, e->st));
+    }
+    NK(api->GroupEnd());
+    int wr = wait_stream(e);
+    if (wr) return wr;
+    e->mega = false;  // the expert phase crosses ranks: per-phase kernels
+    for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
+    e->graphs.clear();
+    return BT_OK;
+}
+
 extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
     if (!e || !name) return fail(BT_ERR_INVALID, "null argument");
     if (!strcmp(name, "prefetch")) {
@@ -1746,6 +2006,11 @@ extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
         e->mega = value != 0;
         for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
         e->graphs.clear();
+        return BT_OK;
+    }
+    if (!strcmp(name, "ep_timeout_ms")) {
+        if (value < 1) return fail(BT_ERR_INVALID, "ep_timeout_ms must be positive");
+        e->ep_timeout_ms = value;
         return BT_OK;
     }
     if (!strcmp(name, "pdl")) {

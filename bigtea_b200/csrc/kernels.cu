@@ -634,7 +634,7 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gateup_grouped_kernel(const __g
             if (tid < mc) {
                 const int tk = p.g_list[off + c0 + tid];
                 tk_s[tid] = tk;
-                rows_s[tid] = tk / p.K;
+                rows_s[tid] = tk / p.row_div;
             }
             const int base = r.done;  // this warp's j-th tile of the chunk is copy base + j
             auto issue = [&](int j) {
@@ -820,7 +820,11 @@ __global__ void __launch_bounds__(256) down_combine_kernel(const __grid_constant
     const float *w = p.sel_w + t * p.K;
     for (int row = threadIdx.x; row < p.E; row += blockDim.x) {
         float o[MAX_K];
-        for (int k = 0; k < p.K; k++) o[k] = p.dpart[((long long)t * p.K + k) * p.E + row];
+        for (int k = 0; k < p.K; k++) {
+            const long long slot = (long long)t * p.K + k;
+            const long long src = p.ep_ranks ? (long long)(p.sel_ids[slot] / p.ep_per) * p.ep_slots + slot : slot;
+            o[k] = p.dpart[src * p.E + row];
+        }
         float sum = 0.0f;
         if (p.single[t]) {
             int workers = p.workers < p.K ? p.workers : p.K;
@@ -837,6 +841,26 @@ __global__ void __launch_bounds__(256) down_combine_kernel(const __grid_constant
         p.x_out[(long long)t * p.E + row] = __fadd_rn(p.ffn_in[(long long)t * p.E + row], sum);
     }
     pdl_trigger();
+}
+
+// grid slots (the fixed capacity per rank), 256 threads: slot tk = blockIdx.x goes to the rank
+// owning its expert with the token's row; every other rank's copy of the slot is marked empty.
+__global__ void __launch_bounds__(256) ep_pack_kernel(const __grid_constant__ EpPackArgs p) {
+    const int tk = blockIdx.x;
+    pdl_wait();
+    const int e = tk < p.T * p.K ? p.sel_ids[tk] : -1;
+    const int owner = e >= 0 ? e / p.per : -1;
+    for (int r = threadIdx.x; r < p.ranks; r += blockDim.x) p.send_meta[r * p.slots + tk] = r == owner ? e : -1;
+    if (owner >= 0) {
+        const float *src = p.fn + (long long)(tk / p.K) * p.E;
+        float *dst = p.send_rows + ((long long)owner * p.slots + tk) * p.E;
+        for (int i = threadIdx.x; i < p.E; i += blockDim.x) dst[i] = src[i];
+    }
+    pdl_trigger();
+}
+
+cudaError_t launch_ep_pack(const EpPackArgs &a, cudaStream_t st, bool pdl) {
+    return launch_ex(ep_pack_kernel, dim3(a.slots), dim3(256), 0, st, pdl, a);
 }
 
 size_t gateup_grouped_smem_bytes(const ExpertArgs &a) {

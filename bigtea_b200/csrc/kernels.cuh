@@ -77,6 +77,20 @@ struct ExpertArgs {
     // grouped form (batched steps): the tokens of each selected expert, from group_kernel
     const int *g_count, *g_off, *g_list, *g_active, *g_nactive;
     float *dpart;  // [T][K][E] each (token, expert slot)'s down rows before the expert sum
+    int row_div;   // grouped gate/up: the activation row of list entry i is i / row_div
+    // expert parallelism: the combine reads slot (t, k) of the rank owning expert sel_ids[t*K+k]
+    // from dpart[(owner * ep_slots + t*K + k) * E]; ep_ranks = 0 outside expert parallelism
+    int ep_ranks, ep_per, ep_slots;
+};
+
+// Expert-parallel dispatch: the rows of every (token, slot) pair, packed for the rank that owns
+// the pair's expert (ranks own ep_per consecutive experts each).
+struct EpPackArgs {
+    const int *sel_ids;  // [T][K] global expert ids
+    const float *fn;     // [T][E] the experts' input rows
+    int T, K, E, ranks, per, slots;
+    int *send_meta;      // [ranks][slots] expert id, or -1 where the slot is not for that rank
+    float *send_rows;    // [ranks][slots][E]
 };
 
 // Tokens grouped by expert for the batched expert kernels: for every expert e, the (token,
@@ -169,6 +183,7 @@ int down_group_rows(const ExpertArgs &a);  // output rows of one grouped down un
 cudaError_t launch_gateup_grouped(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_down_grouped(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_down_combine(const ExpertArgs &a, cudaStream_t st, bool pdl);
+cudaError_t launch_ep_pack(const EpPackArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl);
 size_t attn_smem_bytes(int G, int max_chunks);
 cudaError_t launch_attn(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl);

@@ -67,6 +67,21 @@ class Engine:
     def set_option(self, name: str, value: int):
         check(lib.bt_set_option(self.h, name.encode(), int(value)))
 
+    def enable_ep(self, unique_id: bytes, rank: int, n_ranks: int):
+        """Join an expert-parallel group of n_ranks engines, one per GPU and process: this rank
+        computes experts [rank*NE/n, (rank+1)*NE/n) for every rank's tokens, with the rows
+        exchanged over NCCL. Collective: all ranks call it with the same unique_id (from
+        ep_unique_id() on one rank), then run the same sequence of steps."""
+        buf = (C.c_uint8 * len(unique_id)).from_buffer_copy(unique_id)
+        check(lib.bt_engine_enable_ep(self.h, buf, len(unique_id), int(rank), int(n_ranks)))
+
+    def enable_ep_torch(self, group=None):
+        """enable_ep over an initialised torch.distributed process group (any backend): rank 0's
+        unique id is shared through the group, then every rank joins."""
+        import torch.distributed as dist
+
+        self.enable_ep(share_ep_unique_id(group), dist.get_rank(group), dist.get_world_size(group))
+
     def debug_topk(self, layer: int, token: int):
         K = self.cfg.n_expert_used
         ids = np.empty(K, np.int32)
@@ -160,6 +175,22 @@ class KvCache:
         if k.nbytes != v.nbytes:
             raise BtError(_lib.BT_ERR_KV, "k and v differ in size")
         check(lib.bt_kv_import_layer(self.h, seq, layer, _lib.ptr(k), _lib.ptr(v), k.nbytes))
+
+
+def ep_unique_id() -> bytes:
+    """An NCCL unique id for Engine.enable_ep (made on one rank, shared with the others)."""
+    buf = (C.c_uint8 * 128)()
+    check(lib.bt_ep_unique_id(buf, 128))
+    return bytes(buf)
+
+
+def share_ep_unique_id(group=None) -> bytes:
+    """Rank 0 of the torch.distributed group makes the unique id; every rank returns it."""
+    import torch.distributed as dist
+
+    obj = [ep_unique_id() if dist.get_rank(group) == 0 else None]
+    dist.broadcast_object_list(obj, src=0, group=group)
+    return obj[0]
 
 
 def _u32(a) -> np.ndarray:

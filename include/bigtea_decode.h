@@ -149,6 +149,23 @@ int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const ui
  * holds every SM for the whole step, default 1; 0 = one kernel per phase). */
 int bt_set_option(bt_engine *e, const char *name, int value);
 
+/* ---- expert parallelism (batched decode over the GPUs of one node) ----
+ * No counterpart in the reference, which has no distributed code. One engine per GPU, one
+ * process each. With n ranks, rank r computes the experts [r*NE/n, (r+1)*NE/n). Each layer of
+ * a step then runs as follows:
+ *   - every (token, slot) row goes to the rank that owns the slot's expert;
+ *   - that rank runs the expert FFN on the rows it received;
+ *   - the expert outputs come back (NCCL send/recv over NVLink);
+ *   - the token's own rank adds them in the reference's order (stream.rs:1232-1284), so the
+ *     results equal a single-GPU run bit for bit.
+ * Attention, the router and the head stay on each sequence's rank (data parallel). Every
+ * rank must run the same sequence of steps: the exchange has fixed sizes and all ranks take
+ * part in every layer. */
+/* an NCCL unique id for bt_engine_enable_ep (nbytes >= 128); rank 0 makes it and shares it */
+int bt_ep_unique_id(void *out, size_t nbytes);
+/* collective over the n_ranks engines; disables the persistent single-kernel step */
+int bt_engine_enable_ep(bt_engine *e, const void *unique_id, size_t nbytes, int rank, int n_ranks);
+
 /* ---- parity hooks: each runs one device kernel on host buffers ---- */
 /* dequantize() (core/ggml/src/lib.rs:233-290): n values of `type` through the device layout */
 int bt_debug_dequant(uint32_t type, const void *bytes, uint64_t n, float *out);
