@@ -1294,6 +1294,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.layer = (int)il;
             a.n_blocks = kv->n_blocks;
             a.max_chunks = (int)((kv->max_positions + ATTN_CHUNK - 1) / ATTN_CHUNK);
+            a.n_cta = e->n_sm * 3;  // three resident CTAs per SM
             a.scale = 1.0f / sqrtf((float)D);
             a.part = e->part.as<float>();
             a.cnt = e->acnt.as<int>();

@@ -1064,19 +1064,21 @@ cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl) {
 }
 
 // ====================================================================== attention
-// grid (max_chunks, HK, T), 256 threads, one CTA per (token, kv head, chunk of 128 keys);
-// about 73 KB of shared memory, so two or three CTAs share an SM. K and V pages arrive by
-// 2-D TMA (128-byte swizzle, box 64 x 16). Scores: thread (hh, k) owns key k for heads
-// [hh*G/2, hh*G/2+G/2), a sequential fmaf dot over d. P*V: thread (hq, d) owns column d for
-// heads [hq*G/2, hq*G/2+G/2), a sequential fmaf over the chunk's keys. A chunk that is the
-// whole context finalises its heads; otherwise it writes (acc, m, l) to scratch and
-// attn_combine_kernel merges the chunks in order (C8).
+// Persistent: about three 128-thread CTAs per SM (73 KB of shared memory each) walk the step's
+// items, an item being (token, kv head, chunk of 128 keys) in that order; CTA b takes the
+// contiguous range [b*N/grid, (b+1)*N/grid). K and V pages arrive by 2-D TMA (128-byte swizzle,
+// box 64 x 16) into one K and one V buffer: the next item's K is requested as soon as this
+// item's scores are done and its V once P*V is done, so the copies overlap the arithmetic.
+// Scores: thread = key, all G heads, a sequential fmaf dot over d. P*V: thread = two columns,
+// G/2 heads, a sequential fmaf over the chunk's keys. A chunk that is the whole context
+// finalises its heads; otherwise it writes (acc, m, l) to scratch and attn_combine_kernel
+// merges the chunks in order (C8).
 constexpr int ATTN_THREADS = 128;
 constexpr int ATTN_PART_ROW = 132;  // floats per (chunk, head) partial: acc[128], m, l, 2 pad
 
-size_t attn_smem_bytes(int G, int max_chunks) {
-    (void)max_chunks;
-    return 65536 + (size_t)128 * G * 2 + (size_t)ATTN_CHUNK * G * 4 + (32 + 32 + 8 + 8) * 4 + 16 + 1024;
+size_t attn_smem_bytes(int G, int T) {
+    return 65536 + (size_t)128 * G * 2 + (size_t)ATTN_CHUNK * G * 4 + (32 + 32 + 8 + 8) * 4 + 16 +
+           (size_t)(3 * T + 1) * 4 + 1024;
 }
 
 template <int N>
@@ -1130,12 +1132,12 @@ __device__ __forceinline__ void ldw_n(uint32_t (&dst)[N], const uint32_t *src) {
     }
 }
 
-// One CTA of 128 threads per (chunk c, kv head g, token t): the chunk's K/V pages by TMA (one
-// lane per page), q rounded to f16 in shared memory, then
+// The item loop of the attention kernel. Per item (t, g, c): q rounded to f16 in shared memory
+// (when (t, g) changes), then
 //   scores: thread = key, all G heads, dims in order (C8: q.k as f16 x f16 + f32 fmas);
 //   chunk max, exp and the P3 sum (32-key butterflies, the 4 warp sums in order);
 //   P*V: thread = dims 2dp, 2dp+1 and heads hq*G/2 .. +G/2, keys in order;
-// and writes the chunk's partial (acc, m, l), or the output when the context is one chunk.
+// and the chunk's partial (acc, m, l), or the output when the context is one chunk.
 template <int G>
 __global__ void __launch_bounds__(ATTN_THREADS, 3)
     attn_kernel(const __grid_constant__ AttnArgs p, const __grid_constant__ CUtensorMap tmap) {
@@ -1148,169 +1150,250 @@ __global__ void __launch_bounds__(ATTN_THREADS, 3)
     float *red = ps + CH * G;                                         // [4][8]
     float *red2 = red + 32;                                           // [4][8]
     float *s_m = red2 + 32, *s_l = s_m + 8;
-    uint64_t *bar = reinterpret_cast<uint64_t *>(s_l + 8);
+    uint64_t *bars = reinterpret_cast<uint64_t *>(s_l + 8);  // [0] K copies, [1] V copies
+    int *pre = reinterpret_cast<int *>(bars + 2);            // [T + 1] first item of each token
+    int *pos_s = pre + p.T + 1, *seq_s = pos_s + p.T;        // [T] each
 
-    const int c = blockIdx.x, g = blockIdx.y, t = blockIdx.z;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    pdl_wait();
-    const int seq = p.seq_of[t], pos = p.pos_of[t];
-    const int nk = pos + 1, nc = (nk + CH - 1) / CH;
-    if (c >= nc) {
-        pdl_trigger();
-        return;
-    }
-    const int base = c * CH;
-    const int cnt = nk - base < CH ? nk - base : CH;
-    const int npages = (cnt + 15) / 16;
     if (tid == 0) {
-        mbar_init(bar, 1);
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
         fence_mbar_init();
     }
+    pdl_wait();
+    if (warp == 0) {  // items per token: HK * its chunk count; exclusive prefix over the tokens
+        int run = 0;
+        for (int t0 = 0; t0 < p.T; t0 += 32) {
+            const int t = t0 + lane;
+            const int pos = t < p.T ? p.pos_of[t] : 0;
+            const int n = t < p.T ? p.HK * ((pos + CH) / CH) : 0;
+            int incl = n;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(FULL, incl, o);
+                if (lane >= o) incl += v;
+            }
+            if (t < p.T) {
+                pre[t] = run + incl - n;
+                pos_s[t] = pos;
+                seq_s[t] = p.seq_of[t];
+            }
+            run += __shfl_sync(FULL, incl, 31);
+        }
+        if (lane == 0) pre[p.T] = run;
+    }
     __syncthreads();
-    if (warp == 0) {
+    pdl_trigger();
+    const int N = pre[p.T];
+    const int u0 = (int)((long long)blockIdx.x * N / gridDim.x);
+    const int u1 = (int)((long long)(blockIdx.x + 1) * N / gridDim.x);
+    if (u0 >= u1) return;
+
+    // item i -> token t (the last with pre[t] <= i), kv head g, chunk c
+    auto decode = [&](int i, int &t, int &g, int &c) {
+        int lo = 0, hi = p.T - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (pre[mid] <= i) lo = mid;
+            else hi = mid - 1;
+        }
+        t = lo;
+        const int nc = (pos_s[t] + CH) / CH, r = i - pre[t];
+        g = r / nc;
+        c = r - g * nc;
+    };
+    // warp 0: the page rows of item i (lane = page), kept until its K and V copies are issued
+    int nx_pages = 0, nx_row = 0;
+    auto locate = [&](int i) {
+        int t, g, c;
+        decode(i, t, g, c);
+        const int nk = pos_s[t] + 1, base = c * CH;
+        const int cnt = nk - base < CH ? nk - base : CH;
+        nx_pages = (cnt + 15) / 16;
+        nx_row = 0;
+        if (lane < nx_pages) {
+            const int blk = p.block_table[seq_s[t] * p.max_blocks + (base >> 4) + lane];
+            nx_row = (int)(((((long long)p.layer * p.n_blocks + blk) * 2 + 0) * p.HK + g) * 16);
+        }
+    };
+    auto issue = [&](int which) {  // which 0: K pages, 1: V pages (row + HK*16)
         if (lane == 0) {
-            prefetch_tmap(&tmap);
-            mbar_arrive_expect_tx(bar, npages * 8192);
+            fence_proxy_async();
+            mbar_arrive_expect_tx(&bars[which], nx_pages * 4096);
         }
         __syncwarp();
-        for (int pg = lane; pg < npages; pg += 32) {
-            const int blk = p.block_table[seq * p.max_blocks + (base >> 4) + pg];
-            const int rowK = (int)(((((long long)p.layer * p.n_blocks + blk) * 2 + 0) * p.HK + g) * 16);
-            const int rowV = rowK + p.HK * 16;
-            tma_load_2d(K0 + pg * 2048, &tmap, 0, rowK, bar);
-            tma_load_2d(K1 + pg * 2048, &tmap, 64, rowK, bar);
-            tma_load_2d(V0 + pg * 2048, &tmap, 0, rowV, bar);
-            tma_load_2d(V1 + pg * 2048, &tmap, 64, rowV, bar);
+        if (lane < nx_pages) {
+            const int row = which ? nx_row + p.HK * 16 : nx_row;
+            uint8_t *d0 = which ? V0 : K0, *d1 = which ? V1 : K1;
+            tma_load_2d(d0 + lane * 2048, &tmap, 0, row, &bars[which]);
+            tma_load_2d(d1 + lane * 2048, &tmap, 64, row, &bars[which]);
         }
+    };
+    int k_issued = 0, v_issued = 0;  // copies requested per buffer (item j's copy is the j-th)
+    if (warp == 0) {
+        if (lane == 0) prefetch_tmap(&tmap);
+        locate(u0);
+        issue(0);
+        issue(1);
     }
-    pdl_trigger();
-    for (int i = tid; i < D * G; i += ATTN_THREADS) {
-        const int h = i / D, d = i % D;
-        qs[d * G + h] = __half_as_ushort(__float2half_rn(p.q[(long long)t * p.H * D + (g * G + h) * D + d]));
-    }
-    __syncthreads();
-    const bool landed = mbar_wait(bar, 0, p.err);
-    if (__syncthreads_or(!landed)) {  // a wait ran out: give the copies one more bounded wait, then leave
-        if (tid == 0) mbar_wait(bar, 0, nullptr);
-        return;
-    }
-
-    // ---- scores
-    const int k = tid;
-    const bool valid = k < cnt;
-    float sc[G];
-#pragma unroll
-    for (int h = 0; h < G; h++) sc[h] = 0.0f;
-    {
-        const uint8_t *krow = K0 + k * 128;
-        const int ksw = k & 7;
-        const uint32_t *qw = reinterpret_cast<const uint32_t *>(qs);
-#pragma unroll 2
-        for (int c16 = 0; c16 < 16; c16++) {
-            const uint4 w = *reinterpret_cast<const uint4 *>((c16 < 8 ? krow : krow + 16384) + (((c16 & 7) ^ ksw) << 4));
-            const uint32_t kw[4] = {w.x, w.y, w.z, w.w};
-#pragma unroll
-            for (int e = 0; e < 8; e++) {
-                uint32_t q[QWORDS];
-                ldw_n<QWORDS>(q, qw + (c16 * 8 + e) * QWORDS);
-#pragma unroll
-                for (int j = 0; j < QWORDS; j++) {
-                    if (e & 1)
-                        fma_qk<true>(q[j], kw[e >> 1], sc[2 * j], sc[2 * j + 1]);
-                    else
-                        fma_qk<false>(q[j], kw[e >> 1], sc[2 * j], sc[2 * j + 1]);
-                }
+    k_issued = v_issued = 1;
+    const int QW = p.H * D, dp = tid & 63, hq = tid >> 6;
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    int cur_tg = -1;
+    bool ok = true;
+    for (int i = u0, j = 0; i < u1; i++, j++) {
+        int t, g, c;
+        decode(i, t, g, c);
+        const int nk = pos_s[t] + 1, nc = (nk + CH - 1) / CH, base = c * CH;
+        const int cnt = nk - base < CH ? nk - base : CH;
+        if (warp == 0 && i + 1 < u1) locate(i + 1);  // the page ids load under this item's arithmetic
+        if (t * p.HK + g != cur_tg) {  // every thread passed the last item's scores: qs is free
+            cur_tg = t * p.HK + g;
+            for (int x = tid; x < D * G; x += ATTN_THREADS) {
+                const int h = x / D, d = x % D;
+                qs[d * G + h] = __half_as_ushort(__float2half_rn(p.q[(long long)t * QW + (g * G + h) * D + d]));
             }
         }
-    }
-    const float NEG_INF = -__int_as_float(0x7f800000);
+        __syncthreads();
+        if (__syncthreads_or(!mbar_wait(&bars[0], j & 1, p.err))) {
+            ok = false;
+            break;
+        }
+
+        // ---- scores
+        const int k = tid;
+        const bool valid = k < cnt;
+        float sc[G];
 #pragma unroll
-    for (int h = 0; h < G; h++) {
-        sc[h] = valid ? __fmul_rn(sc[h], p.scale) : NEG_INF;
-        const float m = warp_max(sc[h]);
-        if (lane == 0) red[warp * 8 + h] = m;
-    }
-    __syncthreads();
-    if (tid < G) {
-        float m = red[tid];
-        for (int w = 1; w < 4; w++) m = fmaxf(m, red[w * 8 + tid]);
-        s_m[tid] = m;
-    }
-    __syncthreads();
+        for (int h = 0; h < G; h++) sc[h] = 0.0f;
+        {
+            const uint8_t *krow = K0 + k * 128;
+            const int ksw = k & 7;
+            const uint32_t *qw = reinterpret_cast<const uint32_t *>(qs);
+#pragma unroll 2
+            for (int c16 = 0; c16 < 16; c16++) {
+                const uint4 w =
+                    *reinterpret_cast<const uint4 *>((c16 < 8 ? krow : krow + 16384) + (((c16 & 7) ^ ksw) << 4));
+                const uint32_t kw[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-    for (int h = 0; h < G; h++) {
-        const float pr = valid ? bt_exp(__fsub_rn(sc[h], s_m[h])) : 0.0f;
-        sc[h] = pr;
-        const float ws = butterfly_sum(pr);
-        if (lane == 0) red2[warp * 8 + h] = ws;
-    }
-    if constexpr (G % 4 == 0) {
-        float4 *prow = reinterpret_cast<float4 *>(ps + k * G);
+                for (int e = 0; e < 8; e++) {
+                    uint32_t q[QWORDS];
+                    ldw_n<QWORDS>(q, qw + (c16 * 8 + e) * QWORDS);
 #pragma unroll
-        for (int h4 = 0; h4 < G / 4; h4++) prow[h4] = make_float4(sc[4 * h4], sc[4 * h4 + 1], sc[4 * h4 + 2], sc[4 * h4 + 3]);
-    } else {
-#pragma unroll
-        for (int h = 0; h < G; h++) ps[k * G + h] = sc[h];
-    }
-    __syncthreads();
-    if (tid < G) {
-        float l = 0.0f;
-        for (int w = 0; w < CH / 32; w++) l = __fadd_rn(l, red2[w * 8 + tid]);
-        s_l[tid] = l;
-    }
-    // ---- P*V
-    const int dp = tid & 63, hq = tid >> 6;
-    float acc0[HPT], acc1[HPT];
-#pragma unroll
-    for (int h = 0; h < HPT; h++) acc0[h] = acc1[h] = 0.0f;
-    {
-        const int d = 2 * dp, cc = (d & 63) >> 3;
-        const uint8_t *vcol = ((d < 64) ? V0 : V1) + (d & 7) * 2;
-        int off[8];
-#pragma unroll
-        for (int kk = 0; kk < 8; kk++) off[kk] = kk * 128 + ((cc ^ kk) << 4);
-        const float *pb0 = ps + hq * HPT;
-        for (int j0 = 0; j0 < cnt; j0 += 8) {
-            const uint8_t *vb = vcol + j0 * 128;
-            const float *pb = pb0 + j0 * G;
-#pragma unroll
-            for (int kk = 0; kk < 8; kk++) {
-                if (j0 + kk < cnt) {
-                    const float2 vf = h2f2_fma(*reinterpret_cast<const uint32_t *>(vb + off[kk]));
-                    float pj[HPT];
-                    lds_vec<HPT>(pj, pb + kk * G);
-#pragma unroll
-                    for (int h = 0; h < HPT; h++) {
-                        acc0[h] = fmaf(pj[h], vf.x, acc0[h]);
-                        acc1[h] = fmaf(pj[h], vf.y, acc1[h]);
+                    for (int jj = 0; jj < QWORDS; jj++) {
+                        if (e & 1)
+                            fma_qk<true>(q[jj], kw[e >> 1], sc[2 * jj], sc[2 * jj + 1]);
+                        else
+                            fma_qk<false>(q[jj], kw[e >> 1], sc[2 * jj], sc[2 * jj + 1]);
                     }
                 }
             }
         }
-    }
-    __syncthreads();
-    const int QW = p.H * D, d = 2 * dp;
-    if (nc == 1) {
 #pragma unroll
-        for (int h = 0; h < HPT; h++) {
-            const int head = hq * HPT + h;
-            const float f = bt_exp(__fsub_rn(s_m[head], s_m[head]));
-            const float L = fmaf(s_l[head], f, 0.0f);
-            float *o = p.out + (long long)t * QW + (g * G + head) * D + d;
-            o[0] = __fdiv_rn(fmaf(acc0[h], f, 0.0f), L);
-            o[1] = __fdiv_rn(fmaf(acc1[h], f, 0.0f), L);
+        for (int h = 0; h < G; h++) {
+            sc[h] = valid ? __fmul_rn(sc[h], p.scale) : NEG_INF;
+            const float m = warp_max(sc[h]);
+            if (lane == 0) red[warp * 8 + h] = m;
         }
-        return;
-    }
-    const long long pbase = (((long long)t * p.HK + g) * p.max_chunks) * G * ATTN_PART_ROW;
+        __syncthreads();  // K is no longer read: the next item's K pages may land
+        if (warp == 0 && i + 1 < u1) issue(0);
+        k_issued += i + 1 < u1;
+        if (tid < G) {
+            float m = red[tid];
+            for (int w = 1; w < 4; w++) m = fmaxf(m, red[w * 8 + tid]);
+            s_m[tid] = m;
+        }
+        __syncthreads();
 #pragma unroll
-    for (int h = 0; h < HPT; h++) {
-        const int head = hq * HPT + h;
-        float *pp = p.part + pbase + ((long long)c * G + head) * ATTN_PART_ROW;
-        *reinterpret_cast<float2 *>(pp + d) = make_float2(acc0[h], acc1[h]);
-        if (dp == 0) {
-            pp[D] = s_m[head];
-            pp[D + 1] = s_l[head];
+        for (int h = 0; h < G; h++) {
+            const float pr = valid ? bt_exp(__fsub_rn(sc[h], s_m[h])) : 0.0f;
+            sc[h] = pr;
+            const float ws = butterfly_sum(pr);
+            if (lane == 0) red2[warp * 8 + h] = ws;
+        }
+        if constexpr (G % 4 == 0) {
+            float4 *prow = reinterpret_cast<float4 *>(ps + k * G);
+#pragma unroll
+            for (int h4 = 0; h4 < G / 4; h4++)
+                prow[h4] = make_float4(sc[4 * h4], sc[4 * h4 + 1], sc[4 * h4 + 2], sc[4 * h4 + 3]);
+        } else {
+#pragma unroll
+            for (int h = 0; h < G; h++) ps[k * G + h] = sc[h];
+        }
+        __syncthreads();
+        if (tid < G) {
+            float l = 0.0f;
+            for (int w = 0; w < CH / 32; w++) l = __fadd_rn(l, red2[w * 8 + tid]);
+            s_l[tid] = l;
+        }
+        if (__syncthreads_or(!mbar_wait(&bars[1], j & 1, p.err))) {
+            ok = false;
+            break;
+        }
+        // ---- P*V
+        float acc0[HPT], acc1[HPT];
+#pragma unroll
+        for (int h = 0; h < HPT; h++) acc0[h] = acc1[h] = 0.0f;
+        {
+            const int d = 2 * dp, cc = (d & 63) >> 3;
+            const uint8_t *vcol = ((d < 64) ? V0 : V1) + (d & 7) * 2;
+            int off[8];
+#pragma unroll
+            for (int kk = 0; kk < 8; kk++) off[kk] = kk * 128 + ((cc ^ kk) << 4);
+            const float *pb0 = ps + hq * HPT;
+            for (int j0 = 0; j0 < cnt; j0 += 8) {
+                const uint8_t *vb = vcol + j0 * 128;
+                const float *pb = pb0 + j0 * G;
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) {
+                    if (j0 + kk < cnt) {
+                        const float2 vf = h2f2_fma(*reinterpret_cast<const uint32_t *>(vb + off[kk]));
+                        float pj[HPT];
+                        lds_vec<HPT>(pj, pb + kk * G);
+#pragma unroll
+                        for (int h = 0; h < HPT; h++) {
+                            acc0[h] = fmaf(pj[h], vf.x, acc0[h]);
+                            acc1[h] = fmaf(pj[h], vf.y, acc1[h]);
+                        }
+                    }
+                }
+            }
+        }
+        __syncthreads();  // V is no longer read: the next item's V pages may land
+        if (warp == 0 && i + 1 < u1) issue(1);
+        v_issued += i + 1 < u1;
+        const int d = 2 * dp;
+        if (nc == 1) {
+#pragma unroll
+            for (int h = 0; h < HPT; h++) {
+                const int head = hq * HPT + h;
+                const float f = bt_exp(__fsub_rn(s_m[head], s_m[head]));
+                const float L = fmaf(s_l[head], f, 0.0f);
+                float *o = p.out + (long long)t * QW + (g * G + head) * D + d;
+                o[0] = __fdiv_rn(fmaf(acc0[h], f, 0.0f), L);
+                o[1] = __fdiv_rn(fmaf(acc1[h], f, 0.0f), L);
+            }
+        } else {
+            const long long pbase = (((long long)t * p.HK + g) * p.max_chunks) * G * ATTN_PART_ROW;
+#pragma unroll
+            for (int h = 0; h < HPT; h++) {
+                const int head = hq * HPT + h;
+                float *pp = p.part + pbase + ((long long)c * G + head) * ATTN_PART_ROW;
+                *reinterpret_cast<float2 *>(pp + d) = make_float2(acc0[h], acc1[h]);
+                if (dp == 0) {
+                    pp[D] = s_m[head];
+                    pp[D + 1] = s_l[head];
+                }
+            }
+        }
+        if (!ok) break;
+    }
+    if (!ok && tid == 0) {
+        // a wait ran out: give every copy requested (at most one per buffer beyond those
+        // consumed) one more bounded wait before the CTA leaves
+        for (int q = 0; q < 2; q++) {
+            const int n = q ? v_issued : k_issued;
+            mbar_wait(&bars[q], (n - 1) & 1, nullptr);
         }
     }
 }
@@ -1367,9 +1450,9 @@ __global__ void __launch_bounds__(128) attn_combine_kernel(const __grid_constant
 template <int G>
 static cudaError_t launch_attn_g(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.max_chunks, a.HK, a.T);
+    cfg.gridDim = dim3(a.n_cta);
     cfg.blockDim = dim3(ATTN_THREADS);
-    cfg.dynamicSmemBytes = attn_smem_bytes(G, a.max_chunks);
+    cfg.dynamicSmemBytes = attn_smem_bytes(G, a.T);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;

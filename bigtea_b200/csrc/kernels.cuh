@@ -135,6 +135,7 @@ struct AttnArgs {
     int H, HK, D, G, T;
     const int *seq_of, *pos_of, *block_table;
     int max_blocks, layer, n_blocks, max_chunks;
+    int n_cta;  // persistent grid of the attention kernel
     float scale;
     float *part;
     int *cnt;
@@ -185,7 +186,7 @@ cudaError_t launch_down_grouped(const ExpertArgs &a, int grid, cudaStream_t st, 
 cudaError_t launch_down_combine(const ExpertArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_ep_pack(const EpPackArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl);
-size_t attn_smem_bytes(int G, int max_chunks);
+size_t attn_smem_bytes(int G, int T);
 cudaError_t launch_attn(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl);
 cudaError_t launch_embed(const EmbedArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_step_end(const StepEndArgs &a, cudaStream_t st, bool pdl);
