@@ -1143,7 +1143,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, 3)
     attn_kernel(const __grid_constant__ AttnArgs p, const __grid_constant__ CUtensorMap tmap) {
     constexpr int D = 128, HPT = G / 2, CH = ATTN_CHUNK, QWORDS = G / 2;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    // offset from the shared array itself (not through an integer), so loads stay ld.shared
+    uint8_t *smem = smem_raw + ((1024u - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023u)) & 1023u);
     uint8_t *const K0 = smem, *const K1 = smem + 16384, *const V0 = smem + 32768, *const V1 = smem + 49152;
     uint16_t *qs = reinterpret_cast<uint16_t *>(smem + 65536);        // [D][G] f16 bits
     float *ps = reinterpret_cast<float *>(smem + 65536 + D * G * 2);  // [CH][G]

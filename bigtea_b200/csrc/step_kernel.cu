@@ -855,7 +855,8 @@ template <int G>
 __global__ void __launch_bounds__(STEP_THREADS, 1)
     decode_step_kernel(const __grid_constant__ StepArgs p, const __grid_constant__ CUtensorMap tmap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
-    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~(uintptr_t)1023);
+    // offset from the shared array itself (not through an integer), so loads stay ld.shared
+    uint8_t *smem = smem_raw + ((1024u - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023u)) & 1023u);
     StepSmem sm;
     sm.ring_bar = reinterpret_cast<uint64_t *>(smem);  // 8 x 4 x 8 B
     sm.attn_bar = sm.ring_bar + STEP_WARPS * RING_SLOTS;
