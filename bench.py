@@ -10,6 +10,9 @@ of uniform-random token ids into the f16 paged KV cache. A step = one decode tok
   e2e        tok/s through bt_forward with host token in / host logits out every step
   roofline   the expert FFN (gate/up + down kernels) against the measured HBM copy peak
   cpu_baseline  the CPU oracle decoding from the same weights and cache on the host cores
+  batched    64 concurrent sequences, contexts seeded uniform in [512, 16384], paged f16 KV
+             with seeded contents, a log-Zipf(1.1) router bias per layer (expert popularity
+             over a seeded rank permutation); device tok/s of K graph-replayed steps
 
 N>1 (torchrun): replicas -- every rank runs the same batch-1 decode on its own GPU (weak
 scaling; no collective on the batch-1 path); rank 0 reports the sum of tok/s with the step
@@ -230,6 +233,9 @@ def run_ours(args, rank, world, local_rank):
         for sq, c in enumerate(ctxs):
             cache2.set_positions(int(c), sq)
         first2 = rng2.integers(0, cfg.n_vocab, B)
+        if args.zipf > 0:  # skewed routing: a log-Zipf router bias per layer
+            for il in range(cfg.n_layer):
+                engine.set_router_bias(il, bt.models.zipf_router_bias(cfg.n_expert, il, args.seed, args.zipf))
         if world > 1:
             # expert parallelism: each rank computes NE/world experts for every rank's tokens
             engine.enable_ep_torch()
@@ -237,12 +243,16 @@ def run_ours(args, rank, world, local_rank):
         sync_ranks(world)
         runner.generate_greedy(cache2, first2, args.steps)
         ms2 = max_over_ranks(runner.last_device_ms(), world)
+        # distinct experts a layer's last step selected (this rank's tokens)
+        distinct = [len({int(i) for t in range(B) for i in engine.debug_topk(il, t)[0]}) for il in range(cfg.n_layer)]
         batched = {"value": round(world * B * args.steps / (ms2 / 1e3), 1), "unit": "tok/s", "batch": B,
                    "ms_per_step": round(ms2 / args.steps, 3),
                    "context": f"per sequence, seeded uniform in [{args.ctx2_min}, {args.ctx2_max}], "
                               f"mean {float(ctxs.mean()):.0f}",
                    "kv": "paged f16, 16-token blocks, seeded random contents",
-                   "routing": "the synthetic router (no Zipf popularity bias)",
+                   "routing": (f"log-Zipf({args.zipf}) router bias per layer over a seeded permutation of the "
+                               f"expert ranks" if args.zipf > 0 else "the synthetic router (no popularity bias)"),
+                   "distinct_experts_per_layer": round(float(np.mean(distinct)), 1),
                    "path": "per-phase kernels (single-token steps of more than 4 sequences)",
                    "parallelism": (f"expert parallel over {world} GPUs: {B} sequences per rank, experts split "
                                    f"{cfg.n_expert // world} per rank, rows exchanged by NCCL send/recv"
@@ -381,6 +391,8 @@ def main():
     ap.add_argument("--batch2", type=int, default=64, help="sequences of the batched workload (0 skips it)")
     ap.add_argument("--ctx2-min", type=int, default=512)
     ap.add_argument("--ctx2-max", type=int, default=16384)
+    ap.add_argument("--zipf", type=float, default=1.1, help="router-bias Zipf exponent of the batched workload "
+                    "(0: unbiased)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 

@@ -91,6 +91,7 @@ SIGNATURES = {
     "bt_debug_hidden": (C.c_int, [_P, C.c_uint32, _F32P]),
     "bt_op_gemv": (C.c_int, [C.c_uint32, _P, C.c_uint32, C.c_uint32, _F32P, C.c_uint32, _F32P]),
     "bt_ep_unique_id": (C.c_int, [_P, C.c_size_t]),
+    "bt_engine_set_router_bias": (C.c_int, [_P, C.c_uint32, _F32P, C.c_uint32]),
     "bt_engine_enable_ep": (C.c_int, [_P, _P, C.c_size_t, C.c_int, C.c_int]),
     # device pointers and a cudaStream_t, passed as integers
     "bt_op_gemv_noalloc": (C.c_int, [C.c_uint32, _P, C.c_uint32, C.c_uint32, _P, C.c_uint32, _P, _P]),

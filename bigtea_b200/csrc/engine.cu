@@ -86,6 +86,7 @@ struct QMat {
 
 struct Layer {
     DevBuf attn_norm, q_norm, k_norm, ffn_norm, gate_inp;
+    DevBuf gate_bias;  // optional ffn_gate_inp.bias [n_expert], added to the router logits
     QMat q, k, v, o, gate, up, down;
 };
 
@@ -461,7 +462,8 @@ static QMatDev qmat_dev(const QMat &m) {
     return d;
 }
 
-static int finish_create(bt_engine *e) {
+// the per-layer pointer table of the persistent kernel
+static int upload_layer_dev(bt_engine *e) {
     std::vector<LayerDev> ld(e->d.n_layer);
     for (uint32_t il = 0; il < e->d.n_layer; il++) {
         Layer &l = e->L[il];
@@ -471,6 +473,7 @@ static int finish_create(bt_engine *e) {
         x.k_norm = l.k_norm.as<float>();
         x.ffn_norm = l.ffn_norm.as<float>();
         x.gate_inp = l.gate_inp.as<float>();
+        x.gate_bias = l.gate_bias.p ? l.gate_bias.as<float>() : nullptr;
         x.q = qmat_dev(l.q);
         x.k = qmat_dev(l.k);
         x.v = qmat_dev(l.v);
@@ -479,8 +482,14 @@ static int finish_create(bt_engine *e) {
         x.up = qmat_dev(l.up);
         x.down = qmat_dev(l.down);
     }
-    CK(e->layer_dev.alloc(ld.size() * sizeof(LayerDev)));
+    if (!e->layer_dev.p) CK(e->layer_dev.alloc(ld.size() * sizeof(LayerDev)));
     CK(cudaMemcpy(e->layer_dev.p, ld.data(), ld.size() * sizeof(LayerDev), cudaMemcpyHostToDevice));
+    return BT_OK;
+}
+
+static int finish_create(bt_engine *e) {
+    int ur = upload_layer_dev(e);
+    if (ur) return ur;
     e->out_dev = qmat_dev(e->out);
     CK(e->gbar.alloc(64));
     CK(cudaMemset(e->gbar.p, 0, 64));
@@ -582,6 +591,15 @@ static int build_engine(bt_engine *e, const std::map<std::string, SrcTensor> &sr
             if ((r = check_shape(nm, tt, {E, NE}))) return r;
             if (tt->type != T_F32) return fail(BT_ERR_UNSUPPORTED, nm + " must be F32");
             if ((r = ingest_f32(e, l.gate_inp, tt->data, tt->device, E * NE))) return r;
+            // optional: a router bias (not in the reference's qwen3moe tensors; the skewed-routing
+            // workloads carry one)
+            nm = p + "ffn_gate_inp.bias";
+            if (find_src(src, nm, &tt) == BT_OK) {
+                if ((r = check_shape(nm, tt, {NE}))) return r;
+                if (tt->type != T_F32) return fail(BT_ERR_UNSUPPORTED, nm + " must be F32");
+                if ((r = ingest_f32(e, l.gate_bias, tt->data, tt->device, NE))) return r;
+            }
+            g_err.clear();
         }
         if ((r = mat("attn_q.weight", l.q, E, QW, 1, default_rpt(E)))) return r;
         if ((r = mat("attn_k.weight", l.k, E, KW, 1, default_rpt(E)))) return r;
@@ -1319,6 +1337,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.eps = d.rms_eps;
             a.E = E;
             a.Wr = l.gate_inp.as<float>();
+            a.bias = l.gate_bias.p ? l.gate_bias.as<float>() : nullptr;
             a.NE = NE;
             a.K = K;
             a.T = T;
@@ -1940,6 +1959,24 @@ extern "C" int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_id
     return BT_OK;
 }
 
+extern "C" int bt_engine_set_router_bias(bt_engine *e, uint32_t layer, const float *bias, uint32_t n) {
+    if (!e) return fail(BT_ERR_INVALID, "null engine");
+    if (layer >= e->d.n_layer) return fail(BT_ERR_INVALID, "layer out of range");
+    Layer &l = e->L[layer];
+    if (!bias) {
+        l.gate_bias = DevBuf();
+    } else {
+        if (n != e->d.n_expert) return fail(BT_ERR_INVALID, "the bias has one value per expert");
+        CK(cudaSetDevice(e->device));
+        CK(cudaStreamSynchronize(e->st));
+        CK(l.gate_bias.alloc((size_t)n * 4));
+        CK(cudaMemcpy(l.gate_bias.p, bias, (size_t)n * 4, cudaMemcpyHostToDevice));
+    }
+    for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);  // they hold the old pointers
+    e->graphs.clear();
+    return upload_layer_dev(e);
+}
+
 // ------------------------------------------------------------------ expert parallelism
 extern "C" int bt_ep_unique_id(void *out, size_t nbytes) {
     if (!out || nbytes < sizeof(ncclUniqueId)) return fail(BT_ERR_INVALID, "the unique id needs 128 bytes");
@@ -2132,6 +2169,7 @@ extern "C" int bt_engine_tensor_bytes(const bt_engine *ec, const char *name, voi
         else if (s == "attn_k_norm.weight") f = &l.k_norm;
         else if (s == "ffn_norm.weight") f = &l.ffn_norm;
         else if (s == "ffn_gate_inp.weight") f = &l.gate_inp;
+        else if (s == "ffn_gate_inp.bias" && l.gate_bias.p) f = &l.gate_bias;
     }
     if (f) {
         if (nbytes != f->n) return fail(BT_ERR_INVALID, "size mismatch for " + n);

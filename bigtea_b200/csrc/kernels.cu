@@ -922,6 +922,7 @@ __global__ void __launch_bounds__(128) router_kernel(const __grid_constant__ Rou
     const int r = blockIdx.x * ROUTER_ROWS + warp;
     if (r < p.NE) {
         float acc = warp_dot_p2(p.Wr + (long long)r * p.E, s_y, p.E, lane);
+        if (p.bias) acc = __fadd_rn(acc, p.bias[r]);
         if (lane == 0) p.logits[(long long)t * p.NE + r] = acc;
     }
     __threadfence();

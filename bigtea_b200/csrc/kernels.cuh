@@ -108,6 +108,7 @@ struct RouterArgs {
     float eps;
     int E;
     const float *Wr;
+    const float *bias;  // [NE] added to the logits, or null
     int NE, K, T, rows_per_cta;
     float *fn_out, *logits;
     int *cnt;

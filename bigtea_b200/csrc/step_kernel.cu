@@ -1137,7 +1137,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
 #pragma unroll 8
             for (int i = lane; i < E; i += 32) acc = fmaf(wr[i], yt[i], acc);
             acc = butterfly_sum(acc);
-            if (lane == 0) p.rlog[(long long)t * p.NE + blockIdx.x + k * gridDim.x] = acc;
+            const int row = blockIdx.x + k * gridDim.x;
+            if (L.gate_bias) acc = __fadd_rn(acc, L.gate_bias[row]);
+            if (lane == 0) p.rlog[(long long)t * p.NE + row] = acc;
         }
         int d0, d1;
         cta_range(T * E, d0, d1);

@@ -25,6 +25,7 @@ struct QMatDev {
 // memory word by word.
 struct LayerDev {
     const float *attn_norm, *q_norm, *k_norm, *ffn_norm, *gate_inp;
+    const float *gate_bias;  // [NE] added to the router logits, or null
     QMatDev q, k, v, o, gate, up, down;
 };
 

@@ -45,6 +45,9 @@ class Qwen3MoeConfig:
     out_type: int = TYPE_Q6_K
     layer_types: list = field(default_factory=list)  # per layer: 7 ggml types (LAYER_QUANT_TENSORS)
     name: str = "qwen3moe"
+    # > 0: each layer carries an F32 router bias ffn_gate_inp.bias = log-Zipf(router_zipf)
+    # expert popularity over a seeded per-layer permutation of the expert ranks (zipf_router_bias)
+    router_zipf: float = 0.0
 
     def __post_init__(self):
         if not self.layer_types:
@@ -81,6 +84,8 @@ class Qwen3MoeConfig:
                     (p + "ffn_gate_exps.weight", t[4], (E, F, NE), 0.0),
                     (p + "ffn_up_exps.weight", t[5], (E, F, NE), 0.0),
                     (p + "ffn_down_exps.weight", t[6], (F, E, NE), 0.0)]
+            if self.router_zipf > 0:
+                out.append((p + "ffn_gate_inp.bias", TYPE_F32, (NE,), 0.0))
         return out
 
     def weight_bytes(self) -> int:
@@ -164,10 +169,23 @@ def synth_tensor(name: str, ggml_type: int, ne: tuple, mean: float, seed: int, s
     return buf
 
 
+def zipf_router_bias(n_expert: int, layer: int, seed: int, s: float) -> np.ndarray:
+    """A router bias giving expert e of a layer the log-popularity of Zipf(s) at its rank:
+    bias[e] = -s * ln(rank(e)), the ranks 1..n_expert a seeded permutation per layer."""
+    rank = np.random.default_rng([seed, layer, 0x2F1B]).permutation(n_expert) + 1
+    return (-s * np.log(rank.astype(np.float64))).astype(np.float32)
+
+
 def synth_model(cfg: Qwen3MoeConfig, seed: int, sigma: float = 0.02) -> dict:
     """name -> (ggml type, dims, uint8 bytes) for every tensor of `cfg`."""
-    return {name: (ty, ne, synth_tensor(name, ty, ne, mean, seed, sigma))
-            for name, ty, ne, mean in cfg.tensor_specs()}
+    out = {}
+    for name, ty, ne, mean in cfg.tensor_specs():
+        if name.endswith("ffn_gate_inp.bias"):
+            layer = int(name.split(".")[1])
+            out[name] = (ty, ne, zipf_router_bias(cfg.n_expert, layer, seed, cfg.router_zipf).view(np.uint8))
+        else:
+            out[name] = (ty, ne, synth_tensor(name, ty, ne, mean, seed, sigma))
+    return out
 
 
 def write_gguf(path: str, cfg: Qwen3MoeConfig, tensors: dict) -> None:

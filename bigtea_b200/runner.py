@@ -35,6 +35,11 @@ class Engine:
             types = cfg.flat_layer_types()
             check(lib.bt_engine_create_synthetic(C.byref(d), _lib.ptr(types, C.c_uint32), cfg.embd_type,
                                                  cfg.out_type, seed, sigma, device, C.byref(self.h)))
+            if cfg.router_zipf > 0:  # the same bias synth_model puts in the tensor set
+                from .models import zipf_router_bias
+
+                for il in range(cfg.n_layer):
+                    self.set_router_bias(il, zipf_router_bias(cfg.n_expert, il, seed, cfg.router_zipf))
 
     @classmethod
     def synthetic(cls, cfg: Qwen3MoeConfig, seed: int, sigma: float = 0.02, device: int = 0) -> "Engine":
@@ -63,6 +68,15 @@ class Engine:
         out = np.empty(nbytes, dtype=np.uint8)
         check(lib.bt_engine_tensor_bytes(self.h, name.encode(), _lib.ptr(out), nbytes))
         return out
+
+    def set_router_bias(self, layer: int, bias):
+        """Set (or, with None, remove) layer's router bias: one F32 value per expert, added to
+        the router logits before the softmax."""
+        if bias is None:
+            check(lib.bt_engine_set_router_bias(self.h, layer, None, 0))
+            return
+        b = np.ascontiguousarray(bias, dtype=np.float32)
+        check(lib.bt_engine_set_router_bias(self.h, layer, _lib.ptr(b, C.c_float), b.size))
 
     def set_option(self, name: str, value: int):
         check(lib.bt_set_option(self.h, name.encode(), int(value)))

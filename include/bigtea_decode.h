@@ -149,6 +149,13 @@ int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const ui
  * holds every SM for the whole step, default 1; 0 = one kernel per phase). */
 int bt_set_option(bt_engine *e, const char *name, int value);
 
+/* Router bias of one layer: n == n_expert F32 values added to the router logits before the
+ * softmax (a ggml_add after the ffn_gate_inp mul_mat), or bias == NULL to remove it. Not part
+ * of the reference's qwen3moe tensor set (stream.rs:2784-2831 has no bias): the skewed-routing
+ * workloads use it. bt_engine_create also takes it as the optional tensor
+ * blk.N.ffn_gate_inp.bias. */
+int bt_engine_set_router_bias(bt_engine *e, uint32_t layer, const float *bias, uint32_t n);
+
 /* ---- expert parallelism (batched decode over the GPUs of one node) ----
  * No counterpart in the reference, which has no distributed code. One engine per GPU, one
  * process each. With n ranks, rank r computes the experts [r*NE/n, (r+1)*NE/n). Each layer of

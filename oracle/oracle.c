@@ -500,6 +500,7 @@ typedef struct {
 
 typedef struct {
     tref attn_norm, q, k, v, q_norm, k_norm, o, ffn_norm, gate_inp, gate, up, down;
+    tref gate_bias; /* optional ffn_gate_inp.bias: data NULL when absent */
 } layer_w;
 
 struct or_model {
@@ -566,6 +567,8 @@ or_model *or_model_new(const or_config *cfg, const or_tensor *ts, int n) {
         GETW(o, "attn_output.weight");
         GETW(ffn_norm, "ffn_norm.weight");
         GETW(gate_inp, "ffn_gate_inp.weight");
+        snprintf(nm, sizeof nm, "blk.%d.ffn_gate_inp.bias", il);
+        find_tensor(ts, n, nm, &m->L[il].gate_bias, 0);
         GETW(gate, "ffn_gate_exps.weight");
         GETW(up, "ffn_up_exps.weight");
         GETW(down, "ffn_down_exps.weight");
@@ -719,6 +722,8 @@ int or_forward(or_model *m, or_kv *kv, const int32_t *tokens, int T, int pos_sta
             float *fi = ffin + (size_t)t * E, *fn = xn + (size_t)t * E;
             or_rmsnorm(fi, (const float *)w->ffn_norm.data, E, c->rms_eps, fn);
             or_gemv(OR_F32, w->gate_inp.data, NE, E, fn, rl);
+            if (w->gate_bias.data) /* ggml_add of the router bias: one f32 add per logit */
+                for (int i = 0; i < NE; i++) rl[i] = rl[i] + ((const float *)w->gate_bias.data)[i];
             or_softmax(rl, NE, pr);
             or_route(pr, NE, K, ids, wts);
             memcpy(m->dbg_ids + ((size_t)il * T + t) * K, ids, sizeof(int32_t) * K);

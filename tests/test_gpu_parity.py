@@ -98,6 +98,38 @@ def test_forward_prefill_and_decode_match_oracle(tiny_cfg, tiny_weights, tiny_en
     assert cache.is_consistent()
 
 
+@pytest.mark.parametrize("persistent", [1, 0])
+@pytest.mark.parametrize("source", ["tensors", "synthetic"])
+def test_router_bias_matches_oracle(persistent, source):
+    """A log-Zipf router bias, from the tensor set (blk.N.ffn_gate_inp.bias) or set on a
+    synthetic engine: logits, top-k ids and weights of a prefill and greedy steps bit-exact."""
+    cfg = bt.config("tiny", router_zipf=1.1)
+    W = bt.synth_model(cfg, seed=7)
+    e = bt.Engine(cfg, W) if source == "tensors" else bt.Engine.synthetic(cfg, seed=7)
+    e.set_option("persistent", persistent)
+    model = orc.Model(cfg, W)
+    cache = bt.KvCache(e, max_positions=256)
+    runner = bt.StreamingRunner(e)
+    prompt = np.random.default_rng(29).integers(0, cfg.n_vocab, 13)
+    assert_logits(runner.forward_cached(cache, prompt, 0), model.forward(prompt, 0))
+    for il in range(cfg.n_layer):
+        for t in (0, 12):
+            gi, gw = e.debug_topk(il, t)
+            oi, ow = model.topk(il, t)
+            assert np.array_equal(gi, oi) and np.array_equal(bits(gw), bits(ow))
+    tok = 3
+    for _ in range(4):
+        assert_logits(runner.forward_cached(cache, [tok], cache.len()), model.forward([tok], model.len()))
+        gi, _ = e.debug_topk(1, 0)
+        assert np.array_equal(gi, model.topk(1, 0)[0])
+        tok = (tok * 11 + 5) % cfg.n_vocab
+    toks = runner.generate_greedy(cache, [tok], 5)
+    assert list(toks[:, 0]) == model.greedy(tok, 5)
+    compare_kv(cache, model, cfg)
+    cache.close()
+    e.close()
+
+
 def test_long_context_uses_several_attention_chunks(tiny_cfg, tiny_weights, tiny_engine):
     cfg = tiny_cfg
     prompt = np.random.default_rng(22).integers(0, cfg.n_vocab, 600)

@@ -294,6 +294,8 @@ def _f64_forward(cfg, W, tokens):
         x = x + att.reshape(T, H * D) @ deq(p + "attn_output.weight", E, H * D).T
         fn = rms(x, vec(p + "ffn_norm.weight"))
         logits = fn @ deq(p + "ffn_gate_inp.weight", cfg.n_expert, E).T
+        if p + "ffn_gate_inp.bias" in W:
+            logits = logits + vec(p + "ffn_gate_inp.bias")
         pr = np.exp(logits - logits.max(-1, keepdims=True))
         pr /= pr.sum(-1, keepdims=True)
         out = np.zeros_like(x)
@@ -324,6 +326,25 @@ def test_forward_tracks_float64_restatement(tiny_cfg, tiny_weights):
     want = _f64_forward(tiny_cfg, tiny_weights, tokens)
     rel = np.linalg.norm(got - want) / np.linalg.norm(want)
     assert rel < 0.05, rel  # Q8_K activations and the f16 cache are the only differences
+
+
+def test_router_bias_forward_tracks_float64_restatement_and_skews_routing():
+    import bigtea_b200 as bt
+
+    cfg = bt.config("tiny", router_zipf=1.1)
+    W = bt.synth_model(cfg, seed=7)
+    b0 = np.frombuffer(W["blk.0.ffn_gate_inp.bias"][2].tobytes(), np.float32)
+    assert np.array_equal(b0, bt.models.zipf_router_bias(cfg.n_expert, 0, 7, 1.1))
+    assert sorted(np.round(np.exp(-b0 / 1.1)).astype(int)) == list(range(1, cfg.n_expert + 1))
+    tokens = np.random.default_rng(8).integers(0, cfg.n_vocab, 40)
+    m = orc.Model(cfg, W)
+    got = m.forward(tokens, 0).astype(np.float64)
+    want = _f64_forward(cfg, W, tokens)
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) < 0.05
+    # the experts the bias favours are the ones picked most: rank-1 expert in most top-k sets
+    top = int(np.argmax(b0))
+    hits = sum(top in m.topk(0, t)[0] for t in range(len(tokens)))
+    assert hits >= len(tokens) // 2, hits
 
 
 def test_block_prefill_and_token_steps_share_layer0_kv(tiny_cfg, tiny_weights):
