@@ -10,6 +10,9 @@ of uniform-random token ids into the f16 paged KV cache. A step = one decode tok
   e2e        tok/s through bt_forward with host token in / host logits out every step
   roofline   the expert FFN (gate/up + down kernels) against the measured HBM copy peak
   cpu_baseline  the CPU oracle decoding from the same weights and cache on the host cores
+  expert_cache  experts moved to pinned host memory behind a 6.26 GiB HBM cache (the cfg4
+             ratio), batch-1 greedy decode with the router bias; LRU and frequency-gated
+             admission each from a cold cache: tok/s and hit rate
   batched    64 concurrent sequences, contexts seeded uniform in [512, 16384], paged f16 KV
              with seeded contents, a log-Zipf(1.1) router bias per layer (expert popularity
              over a seeded rank permutation); device tok/s of K graph-replayed steps
@@ -109,12 +112,15 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def expert_bytes(cfg):
+def expert_bytes(cfg, per_expert=False):
     """Algorithmic bytes of the expert FFN per token, averaged over layers: top-k experts x
-    (gate + up + down) in each layer's K-quant types."""
+    (gate + up + down) in each layer's K-quant types (per_expert: one expert's bytes)."""
     from bigtea_b200.gguf import tensor_nbytes
 
     E, F, K = cfg.n_embd, cfg.n_ff_exp, cfg.n_expert_used
+    if per_expert:
+        return float(np.mean([tensor_nbytes(t[4], E * F) + tensor_nbytes(t[5], E * F) + tensor_nbytes(t[6], F * E)
+                              for t in cfg.layer_types]))
     gu, dn = [], []
     for t in cfg.layer_types:
         gu.append(K * (tensor_nbytes(t[4], E * F) + tensor_nbytes(t[5], E * F)))
@@ -258,6 +264,7 @@ def run_ours(args, rank, world, local_rank):
                                    f"{cfg.n_expert // world} per rank, rows exchanged by NCCL send/recv"
                                    if world > 1 else "single GPU")}
         cache2.close()
+
     # per-phase kernels: the expert kernels' times; the persistent step: its gate/up and down
     # phases (slowest CTA, from the in-kernel timeline)
     gu = prof.get("expert_gateup", prof.get("ph5_gateup_work", (1, 0.0)))
@@ -268,6 +275,7 @@ def run_ours(args, rank, world, local_rank):
     per_step_launches = 1 if persistent else 1 + cfg.n_layer * 7 + 1 + 1
 
     result = None
+    xcache = None
     if rank == 0:
         cpu = None
         if not args.no_cpu:
@@ -300,9 +308,36 @@ def run_ours(args, rank, world, local_rank):
                          "bytes_per_token_layer": gu_bytes + dn_bytes, "traffic": None},
             "kernels_us": kernel_table,
             "batched": batched,
+            "expert_cache": None,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
+    # the out-of-HBM case at this model's scale: experts in pinned host memory behind an HBM
+    # cache of args.xcache_gib, batch-1 greedy decode with the log-Zipf router bias, each policy
+    # from a cold cache
+    if args.xcache_gib > 0 and world == 1:
+        if args.zipf > 0 and not args.batch2:
+            for il in range(cfg.n_layer):
+                engine.set_router_bias(il, bt.models.zipf_router_bias(cfg.n_expert, il, args.seed, args.zipf))
+        xcache = {"cache_bytes": int(args.xcache_gib * (1 << 30)), "steps": args.xcache_steps, "batch": 1,
+                  "experts_bytes": int(cfg.n_layer * cfg.n_expert * expert_bytes(cfg, per_expert=True)),
+                  "routing": f"log-Zipf({args.zipf}) router bias per layer" if args.zipf > 0 else "unbiased"}
+        try:
+            for policy in ("lru", "freq"):
+                engine.enable_expert_cache(xcache["cache_bytes"], policy)
+                t0 = time.perf_counter()
+                runner.generate_greedy(cache, [nxt], args.xcache_steps)
+                wall = time.perf_counter() - t0
+                st = engine.expert_cache_stats()
+                xcache[policy] = {"tok_s": round(args.xcache_steps / (runner.last_device_ms() / 1e3), 2),
+                                  "hit_rate": round(st["hit_rate"], 4), "evictions": st["evictions"],
+                                  "bypasses": st["bypasses"], "gb_copied": round(st["bytes_copied"] / 1e9, 2),
+                                  "wall_s": round(wall, 2)}
+                xcache["slots"] = st["capacity_slots"]
+        except bt.BtError as err:  # e.g. pinned host memory refused
+            xcache["unavailable"] = str(err)
+    if result is not None:
+        result["expert_cache"] = xcache
     cache.close()
     engine.close()
     return result
@@ -391,6 +426,10 @@ def main():
     ap.add_argument("--batch2", type=int, default=64, help="sequences of the batched workload (0 skips it)")
     ap.add_argument("--ctx2-min", type=int, default=512)
     ap.add_argument("--ctx2-max", type=int, default=16384)
+    ap.add_argument("--xcache-gib", type=float, default=6.26,
+                    help="HBM expert-cache size of the out-of-HBM leg (0 skips it); the default keeps the "
+                         "cfg4 ratio of cache to experts (120 GB of ~311 GB)")
+    ap.add_argument("--xcache-steps", type=int, default=128)
     ap.add_argument("--zipf", type=float, default=1.1, help="router-bias Zipf exponent of the batched workload "
                     "(0: unbiased)")
     args = ap.parse_args()

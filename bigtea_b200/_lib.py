@@ -50,6 +50,14 @@ class Stats(C.Structure):
     ]
 
 
+class XCacheStats(C.Structure):
+    _fields_ = [(n, C.c_uint64) for n in ("hits", "misses", "evictions", "admissions", "bypasses", "bytes_copied",
+                                          "capacity_slots", "slot_bytes")]
+
+
+XCACHE_LRU, XCACHE_FREQ = 0, 1
+
+
 class KernelTime(C.Structure):
     _fields_ = [("name", C.c_char * 32), ("launches", C.c_uint64), ("total_ms", C.c_double)]
 
@@ -92,6 +100,10 @@ SIGNATURES = {
     "bt_op_gemv": (C.c_int, [C.c_uint32, _P, C.c_uint32, C.c_uint32, _F32P, C.c_uint32, _F32P]),
     "bt_ep_unique_id": (C.c_int, [_P, C.c_size_t]),
     "bt_engine_set_router_bias": (C.c_int, [_P, C.c_uint32, _F32P, C.c_uint32]),
+    "bt_engine_enable_expert_cache": (C.c_int, [_P, C.c_uint64, C.c_int]),
+    "bt_expert_cache_stats": (C.c_int, [_P, C.POINTER(XCacheStats)]),
+    "bt_expert_cache_simulate": (C.c_int, [C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _I32P,
+                                           C.c_uint32, C.POINTER(XCacheStats)]),
     "bt_engine_enable_ep": (C.c_int, [_P, _P, C.c_size_t, C.c_int, C.c_int]),
     # device pointers and a cudaStream_t, passed as integers
     "bt_op_gemv_noalloc": (C.c_int, [C.c_uint32, _P, C.c_uint32, C.c_uint32, _P, C.c_uint32, _P, _P]),

@@ -21,6 +21,7 @@
 
 #include "../../include/bigtea_decode.h"
 #include "bt_common.cuh"
+#include "expert_cache.h"
 #include "kernels.cuh"
 #include "step_kernel.cuh"
 
@@ -115,12 +116,25 @@ struct bt_engine {
     int max_out = 0;
     DevBuf x, ffn_in, fn, qkv, qbuf, att, rlog, rcnt, sel_ids, sel_w, act, part, acnt;
     DevBuf g_count, g_off, g_list, g_active, g_nactive, dpart;  // grouped experts of batched steps
+    DevBuf g_chunk_e, g_chunk_r0, g_nchunks;
     // expert parallelism (bt_engine_enable_ep): this rank computes experts [rank*NE/n, (rank+1)*NE/n)
     bool ep = false;
     int ep_rank = 0, ep_n = 1;
     ncclComm_t ep_comm = nullptr;
     int ep_timeout_ms = 60000;  // a host wait on an expert-parallel step longer than this aborts the exchange
     bool ep_aborted = false;
+    // expert cache: experts in pinned host memory, the ones a layer selects copied into slots
+    // of a device pool before its expert kernels (bt_engine_enable_expert_cache)
+    bool xcache = false;
+    ExpertCachePolicy xpol;
+    XCacheStats xstats;
+    int x_bounce = 0;               // bounce slots, after the cache's own
+    long long x_stride = 0;         // bytes of a slot: one expert's gate | up | down
+    DevBuf x_pool, x_slot_dev;      // (capacity + bounce) slots; [n_layer][NE] slot of each expert
+    std::vector<uint8_t *> x_host;  // per layer, pinned: [NE] experts of x_stride bytes
+    int *x_sel_host = nullptr;      // pinned: a step's selections
+    int *x_slot_host = nullptr;     // pinned [n_layer][NE]: staging of x_slot_dev
+    cudaEvent_t x_ev = nullptr;
     DevBuf ep_send_meta, ep_send_rows, ep_recv_meta, ep_recv_rows, ep_act, ep_dpart, ep_ret;
     DevBuf dbg_ids, dbg_w;  // [n_layer][TB][K]
     DevBuf tokens, seq_of, local_idx, pos_of, single, x_rows;
@@ -425,6 +439,9 @@ static int alloc_scratch(bt_engine *e) {
     CK(e->g_list.alloc((size_t)TB * K * 4));
     CK(e->g_active.alloc((size_t)NE * 4));
     CK(e->g_nactive.alloc(4));
+    CK(e->g_nchunks.alloc(4));
+    CK(e->g_chunk_e.alloc((size_t)group_max_chunks(TB * K, NE) * 4));
+    CK(e->g_chunk_r0.alloc((size_t)group_max_chunks(TB * K, NE) * 4));
     CK(e->dpart.alloc((size_t)TB * K * E * 4));
     CK(cudaMemset(e->acnt.p, 0, (size_t)TB * d.n_head_kv * 4));
     CK(e->dbg_ids.alloc((size_t)d.n_layer * TB * K * 4));
@@ -738,6 +755,10 @@ extern "C" void bt_engine_destroy(bt_engine *e) {
     if (e->st) cudaStreamSynchronize(e->st);
     for (auto &kv : e->graphs) cudaGraphExecDestroy(kv.second);
     if (e->ep_comm && nccl_api()) nccl_api()->CommDestroy(e->ep_comm);
+    for (uint8_t *h : e->x_host) cudaFreeHost(h);
+    if (e->x_sel_host) cudaFreeHost(e->x_sel_host);
+    if (e->x_slot_host) cudaFreeHost(e->x_slot_host);
+    if (e->x_ev) cudaEventDestroy(e->x_ev);
     for (auto &p : e->ev_pool) {
         cudaEventDestroy(p.first);
         cudaEventDestroy(p.second);
@@ -1125,7 +1146,7 @@ static int upload_plan(bt_engine *e, const StepPlan &p) {
 // Can this step run as one persistent kernel? Single-token steps of up to STEP_MAX_T
 // sequences whose activations fit the kernel's shared memory.
 static bool step_eligible(const bt_engine *e, const bt_kv *kv, const StepPlan &p) {
-    if (!e->mega || e->ep || p.T > STEP_MAX_T || p.out_first != 0 || (int)p.x_rows.size() != p.T) return false;
+    if (!e->mega || e->ep || e->xcache || p.T > STEP_MAX_T || p.out_first != 0 || (int)p.x_rows.size() != p.T) return false;
     for (int t = 0; t < p.T; t++)
         if (!p.single[t] || p.local_idx[t] != 0 || p.x_rows[t] != t || p.st_lrow[t] != t) return false;
     if ((int)p.st_seq.size() != p.T) return false;
@@ -1212,6 +1233,52 @@ static int launch_persistent_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bo
 }
 
 // All kernels of one step on e->st. Capturable: no host synchronisation inside.
+// Expert cache, one layer: read the layer's selections back, decide hits and misses, copy the
+// missing experts from pinned host memory into their slots (ordered before the expert kernels
+// on the stream) and upload the layer's slot table. Earlier layers' kernels have finished when
+// the selections arrive, so any slot not used by this layer can be overwritten.
+static int xcache_layer(bt_engine *e, int il, int T) {
+    const int K = (int)e->d.n_expert_used, NE = (int)e->d.n_expert, n = T * K;
+    CK(cudaMemcpyAsync(e->x_sel_host, e->sel_ids.p, (size_t)n * 4, cudaMemcpyDeviceToHost, e->st));
+    CK(cudaEventRecord(e->x_ev, e->st));
+    CK(cudaEventSynchronize(e->x_ev));
+    std::vector<int> distinct;
+    std::vector<char> seen(NE, 0);
+    for (int i = 0; i < n; i++) {
+        const int x = e->x_sel_host[i];
+        if (x < 0 || x >= NE) return fail(BT_ERR_INVALID, "expert id out of range");
+        if (!seen[x]) {
+            seen[x] = 1;
+            distinct.push_back(x);
+        }
+    }
+    const int nd = (int)distinct.size();
+    std::vector<int> slot(nd);
+    std::unique_ptr<bool[]> copy(new bool[nd]);
+    e->xpol.lookup(il, distinct.data(), nd, slot.data(), copy.get(), e->xstats);
+    const Layer &l = e->L[il];
+    const size_t bytes = (size_t)(l.gate.mat_bytes + l.up.mat_bytes + l.down.mat_bytes);
+    int *row = e->x_slot_host + (size_t)il * NE;
+    int bounce = 0;
+    for (int i = 0; i < nd; i++) {
+        int s = slot[i];
+        bool c = copy[i];
+        if (s < 0) {
+            if (bounce >= e->x_bounce) return fail(BT_ERR_INVALID, "more distinct experts than bounce slots");
+            s = e->xpol.capacity() + bounce++;
+            c = true;
+        }
+        row[distinct[i]] = s;
+        if (c) {
+            CK(cudaMemcpyAsync(e->x_pool.as<uint8_t>() + (size_t)s * e->x_stride,
+                               e->x_host[il] + (size_t)distinct[i] * e->x_stride, bytes, cudaMemcpyHostToDevice, e->st));
+            e->xstats.bytes_copied += bytes;
+        }
+    }
+    CK(cudaMemcpyAsync(e->x_slot_dev.as<int>() + (size_t)il * NE, row, (size_t)NE * 4, cudaMemcpyHostToDevice, e->st));
+    return BT_OK;
+}
+
 static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) {
     if (e->ep_aborted) return fail(BT_ERR_TIMEOUT, "the expert-parallel communicator was aborted by an earlier failure");
     if (step_eligible(e, kv, p)) return launch_persistent_step(e, kv, p, greedy);
@@ -1353,6 +1420,11 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             CK(launch_router(a, st, pdl));
             timer_end(e);
         }
+        if (e->xcache) {
+            int xr = xcache_layer(e, (int)il, T);
+            if (xr) return xr;
+        }
+        const int *x_slot = e->xcache ? e->x_slot_dev.as<int>() + (size_t)il * NE : nullptr;
         if (e->ep) {  // expert parallelism: rows to the owning ranks, experts there, rows back
             const int S = e->TB * K, n = e->ep_n, per = NE / n;
             const NcclApi *api = nccl_api();
@@ -1391,6 +1463,9 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             ga.g_list = e->g_list.as<int>();
             ga.g_active = e->g_active.as<int>();
             ga.g_nactive = e->g_nactive.as<int>();
+            ga.g_chunk_e = e->g_chunk_e.as<int>();
+            ga.g_chunk_r0 = e->g_chunk_r0.as<int>();
+            ga.g_nchunks = e->g_nchunks.as<int>();
             timer_begin(e, "expert_group");
             CK(launch_group(ga, st, false));
             timer_end(e);
@@ -1423,6 +1498,9 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.g_list = ga.g_list;
             a.g_active = ga.g_active;
             a.g_nactive = ga.g_nactive;
+            a.g_chunk_e = ga.g_chunk_e;
+            a.g_chunk_r0 = ga.g_chunk_r0;
+            a.g_nchunks = ga.g_nchunks;
             a.row_div = 1;  // received rows are indexed by their slot
             a.fn = e->ep_recv_rows.as<float>();
             a.act = e->ep_act.as<float>();
@@ -1471,6 +1549,9 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             ga.g_list = e->g_list.as<int>();
             ga.g_active = e->g_active.as<int>();
             ga.g_nactive = e->g_nactive.as<int>();
+            ga.g_chunk_e = e->g_chunk_e.as<int>();
+            ga.g_chunk_r0 = e->g_chunk_r0.as<int>();
+            ga.g_nchunks = e->g_nchunks.as<int>();
             timer_begin(e, "expert_group");
             CK(launch_group(ga, st, pdl));
             timer_end(e);
@@ -1510,8 +1591,14 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.g_list = ga.g_list;
             a.g_active = ga.g_active;
             a.g_nactive = ga.g_nactive;
+            a.g_chunk_e = ga.g_chunk_e;
+            a.g_chunk_r0 = ga.g_chunk_r0;
+            a.g_nchunks = ga.g_nchunks;
             a.dpart = e->dpart.as<float>();
             a.row_div = K;  // list entry t*K + k uses token t's row
+            a.slot_of = x_slot;
+            a.pool = e->x_pool.as<uint8_t>();
+            a.slot_stride = e->x_stride;
             const size_t cap = (size_t)max_dynamic_smem();
             a.slot_bytes = a.g_tile_bytes + a.u_tile_bytes;
             a.nst = 1;
@@ -1562,6 +1649,9 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.x_out = e->x.as<float>() + (size_t)t0 * E;
             a.single = e->single.as<unsigned char>() + t0;
             a.err = err;
+            a.slot_of = x_slot;
+            a.pool = e->x_pool.as<uint8_t>();
+            a.slot_stride = e->x_stride;
             if (e->prefetch && t0 == 0 && il + 1 < d.n_layer) {  // the next layer's q/k/v weights
                 const Layer &n = e->L[il + 1];
                 a.pf.ptr[0] = n.q.buf.p;
@@ -1788,6 +1878,25 @@ extern "C" int bt_generate_greedy(bt_engine *e, bt_kv *kv, const uint32_t *seq_i
     StepPlan p;
     int r = greedy_prepare(e, kv, seq_ids, first_tokens, n_seqs, n_steps, p);
     if (r) return r;
+    if (e->xcache) {  // a host decision in every layer: plain launches, no graph
+        cudaEvent_t a, b;
+        CK(cudaEventCreate(&a));
+        CK(cudaEventCreate(&b));
+        CK(cudaEventRecord(a, e->st));
+        for (uint32_t s = 0; s < n_steps && !r; s++) r = launch_step(e, kv, p, true);
+        CK(cudaEventRecord(b, e->st));
+        if (!r) r = wait_stream(e);
+        float ms = 0;
+        cudaEventElapsedTime(&ms, a, b);
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        if (r) return r;
+        e->last_device_ms = ms;
+        r = greedy_finish(e, kv, seq_ids, n_seqs, n_steps, tokens_out, last_logits);
+        e->stats.forward_calls++;
+        e->stats.forward_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+        return r;
+    }
     GraphKey key{kv, std::vector<uint32_t>(seq_ids, seq_ids + n_seqs)};
     auto it = e->graphs.find(key);
     if (it == e->graphs.end() && n_steps > 0) {
@@ -1977,6 +2086,135 @@ extern "C" int bt_engine_set_router_bias(bt_engine *e, uint32_t layer, const flo
     return upload_layer_dev(e);
 }
 
+// ------------------------------------------------------------------ expert cache
+extern "C" int bt_engine_enable_expert_cache(bt_engine *e, uint64_t cache_bytes, int policy) {
+    if (!e) return fail(BT_ERR_INVALID, "null engine");
+    if (e->ep) return fail(BT_ERR_UNSUPPORTED, "the expert cache and expert parallelism do not combine");
+    if (policy != BT_XCACHE_LRU && policy != BT_XCACHE_FREQ) return fail(BT_ERR_INVALID, "unknown cache policy");
+    const bt_model_desc &d = e->d;
+    const int NE = (int)d.n_expert, K = (int)d.n_expert_used, L = (int)d.n_layer;
+    if (e->xcache) {  // already host-resident: a new, empty cache of the given size and policy
+        const long long cap = (long long)(cache_bytes / (uint64_t)e->x_stride);
+        if (cap < 2 * K) return fail(BT_ERR_INVALID, "the cache must hold at least two steps' worth of experts (2 * top-k)");
+        const int capacity = (int)(cap < (long long)L * NE ? cap : (long long)L * NE);
+        CK(cudaStreamSynchronize(e->st));
+        if (capacity != e->xpol.capacity()) CK(e->x_pool.alloc((size_t)(capacity + e->x_bounce) * e->x_stride));
+        CK(cudaMemset(e->x_slot_dev.p, 0xff, (size_t)L * NE * 4));
+        memset(e->x_slot_host, 0xff, (size_t)L * NE * 4);
+        e->xpol = ExpertCachePolicy(policy, capacity, L, NE);
+        e->xstats = XCacheStats();
+        return BT_OK;
+    }
+    long long stride = 0;
+    for (int il = 0; il < L; il++) {
+        const Layer &l = e->L[il];
+        const long long b = (long long)(l.gate.mat_bytes + l.up.mat_bytes + l.down.mat_bytes);
+        if (b > stride) stride = b;
+    }
+    stride = (stride + 127) & ~127ll;
+    const long long cap = (long long)(cache_bytes / (uint64_t)stride);
+    if (cap < 2 * K) return fail(BT_ERR_INVALID, "the cache must hold at least two steps' worth of experts (2 * top-k)");
+    const int capacity = (int)(cap < (long long)L * NE ? cap : (long long)L * NE);
+    const int bounce = NE < e->TB * K ? NE : e->TB * K;
+    CK(cudaSetDevice(e->device));
+    CK(cudaStreamSynchronize(e->st));
+    // the experts to pinned host memory, one contiguous gate | up | down block per expert
+    std::vector<uint8_t *> host(L, nullptr);
+    auto undo = [&]() {
+        for (uint8_t *h : host)
+            if (h) cudaFreeHost(h);
+    };
+    for (int il = 0; il < L; il++) {
+        const Layer &l = e->L[il];
+        cudaError_t ce = cudaHostAlloc((void **)&host[il], (size_t)NE * stride, cudaHostAllocDefault);
+        if (ce != cudaSuccess) {
+            undo();
+            return fail(BT_ERR_OOM, std::string("pinned host memory for the experts: ") + cudaGetErrorString(ce));
+        }
+        const QMat *mats[3] = {&l.gate, &l.up, &l.down};
+        size_t off = 0;
+        for (const QMat *m : mats) {
+            ce = cudaMemcpy2D(host[il] + off, (size_t)stride, m->buf.p, (size_t)m->mat_bytes, (size_t)m->mat_bytes,
+                              (size_t)NE, cudaMemcpyDeviceToHost);
+            if (ce != cudaSuccess) {
+                undo();
+                return fail(BT_ERR_CUDA, std::string("expert copy to the host: ") + cudaGetErrorString(ce));
+            }
+            off += (size_t)m->mat_bytes;
+        }
+    }
+    for (int il = 0; il < L; il++) {  // the device copies go: the pool replaces them
+        Layer &l = e->L[il];
+        l.gate.buf = DevBuf();
+        l.up.buf = DevBuf();
+        l.down.buf = DevBuf();
+    }
+    e->x_host = host;
+    CK(e->x_pool.alloc((size_t)(capacity + bounce) * stride));
+    CK(e->x_slot_dev.alloc((size_t)L * NE * 4));
+    CK(cudaMemset(e->x_slot_dev.p, 0xff, (size_t)L * NE * 4));
+    CK(cudaHostAlloc((void **)&e->x_sel_host, (size_t)e->TB * K * 4, cudaHostAllocDefault));
+    CK(cudaHostAlloc((void **)&e->x_slot_host, (size_t)L * NE * 4, cudaHostAllocDefault));
+    memset(e->x_slot_host, 0xff, (size_t)L * NE * 4);
+    CK(cudaEventCreateWithFlags(&e->x_ev, cudaEventDisableTiming));
+    e->xpol = ExpertCachePolicy(policy, capacity, L, NE);
+    e->xstats = XCacheStats();
+    e->x_stride = stride;
+    e->x_bounce = bounce;
+    e->xcache = true;
+    e->mega = false;  // the host decides between the router and the experts: per-phase kernels
+    for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
+    e->graphs.clear();
+    return BT_OK;
+}
+
+static void xcache_fill(const XCacheStats &s, int capacity, long long stride, bt_xcache_stats *out) {
+    out->hits = s.hits;
+    out->misses = s.misses;
+    out->evictions = s.evictions;
+    out->admissions = s.admissions;
+    out->bypasses = s.bypasses;
+    out->bytes_copied = s.bytes_copied;
+    out->capacity_slots = (uint64_t)capacity;
+    out->slot_bytes = (uint64_t)stride;
+}
+
+extern "C" int bt_expert_cache_stats(const bt_engine *e, bt_xcache_stats *out) {
+    if (!e || !out) return fail(BT_ERR_INVALID, "null argument");
+    if (!e->xcache) return fail(BT_ERR_INVALID, "the expert cache is not enabled");
+    xcache_fill(e->xstats, e->xpol.capacity(), e->x_stride, out);
+    return BT_OK;
+}
+
+extern "C" int bt_expert_cache_simulate(int policy, uint32_t capacity, uint32_t n_layer, uint32_t n_expert,
+                                        uint32_t n_sel, const int32_t *trace, uint32_t n_steps, bt_xcache_stats *out) {
+    if (!trace || !out || !capacity || !n_layer || !n_expert || !n_sel)
+        return fail(BT_ERR_INVALID, "bad argument");
+    if (policy != BT_XCACHE_LRU && policy != BT_XCACHE_FREQ) return fail(BT_ERR_INVALID, "unknown cache policy");
+    ExpertCachePolicy pol(policy, (int)capacity, (int)n_layer, (int)n_expert);
+    XCacheStats st;
+    std::vector<int> distinct, slot;
+    std::vector<char> seen;
+    std::unique_ptr<bool[]> copy(new bool[n_sel]);
+    for (uint32_t s = 0; s < n_steps; s++)
+        for (uint32_t il = 0; il < n_layer; il++) {
+            const int32_t *sel = trace + ((size_t)s * n_layer + il) * n_sel;
+            distinct.clear();
+            seen.assign(n_expert, 0);
+            for (uint32_t i = 0; i < n_sel; i++) {
+                if (sel[i] < 0 || (uint32_t)sel[i] >= n_expert) return fail(BT_ERR_INVALID, "expert id out of range");
+                if (!seen[sel[i]]) {
+                    seen[sel[i]] = 1;
+                    distinct.push_back(sel[i]);
+                }
+            }
+            slot.resize(distinct.size());
+            pol.lookup((int)il, distinct.data(), (int)distinct.size(), slot.data(), copy.get(), st);
+        }
+    xcache_fill(st, (int)capacity, 0, out);
+    return BT_OK;
+}
+
 // ------------------------------------------------------------------ expert parallelism
 extern "C" int bt_ep_unique_id(void *out, size_t nbytes) {
     if (!out || nbytes < sizeof(ncclUniqueId)) return fail(BT_ERR_INVALID, "the unique id needs 128 bytes");
@@ -1992,6 +2230,7 @@ extern "C" int bt_engine_enable_ep(bt_engine *e, const void *unique_id, size_t n
     if (!e || !unique_id || nbytes < sizeof(ncclUniqueId)) return fail(BT_ERR_INVALID, "bad argument");
     if (n_ranks < 1 || rank < 0 || rank >= n_ranks) return fail(BT_ERR_INVALID, "rank out of range");
     if (e->ep) return fail(BT_ERR_INVALID, "expert parallelism is already enabled");
+    if (e->xcache) return fail(BT_ERR_UNSUPPORTED, "the expert cache and expert parallelism do not combine");
     const bt_model_desc &d = e->d;
     if (d.n_expert % (uint32_t)n_ranks) return fail(BT_ERR_UNSUPPORTED, "the expert count must divide by the rank count");
     const NcclApi *api = nccl_api();
@@ -2008,6 +2247,8 @@ extern "C" int bt_engine_enable_ep(bt_engine *e, const void *unique_id, size_t n
     CK(cudaMemsetAsync(e->ep_dpart.p, 0, n * S * E * 4, e->st));
     CK(cudaMemsetAsync(e->ep_send_meta.p, 0xff, n * S * 4, e->st));
     CK(e->g_list.alloc(n * S * 4));  // the grouped lists now cover every rank's slots
+    CK(e->g_chunk_e.alloc((size_t)group_max_chunks((int)(n * S), (int)d.n_expert) * 4));
+    CK(e->g_chunk_r0.alloc((size_t)group_max_chunks((int)(n * S), (int)d.n_expert) * 4));
     ncclUniqueId id;
     memcpy(&id, unique_id, sizeof(id));
     ncclComm_t comm = nullptr;
@@ -2177,6 +2418,7 @@ extern "C" int bt_engine_tensor_bytes(const bt_engine *ec, const char *name, voi
         return BT_OK;
     }
     if (!m) return fail(BT_ERR_MISSING_TENSOR, "no tensor " + n);
+    if (!m->buf.p) return fail(BT_ERR_UNSUPPORTED, n + " lives in the host expert cache");
     size_t raw = (size_t)m->n_mats * m->rows * (m->cols / 256) * qk_block_bytes(m->type);
     if (nbytes != raw) return fail(BT_ERR_INVALID, "size mismatch for " + n);
     DevBuf tmp;

@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gateup_kernel(const __grid_cons
     if (p.prefetch_down) {  // the down weights of the selected experts, for the next kernel
         unsigned long long k = 1ull << 40;  // a fresh round-robin start
         for (int q = 0; q < p.T * p.K; q++) {
-            const void *ptr = p.down + p.sel_ids[q] * p.d_expert_bytes;
+            const void *ptr = expert_down(p, p.sel_ids[q]);
             const unsigned long long nb = (unsigned long long)p.d_expert_bytes;
             prefetch_ranges_spread(&ptr, &nb, 1, k);
         }
@@ -374,8 +374,8 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gateup_kernel(const __grid_cons
         int slot = j % p.nst;
         uint8_t *dst = myring + (size_t)slot * p.slot_bytes;
         mbar_arrive_expect_tx(&mybar[slot], p.g_tile_bytes + p.u_tile_bytes);
-        bulk_g2s(dst, p.gate + e * p.g_expert_bytes + (long long)tile * p.g_tile_bytes, p.g_tile_bytes, &mybar[slot]);
-        bulk_g2s(dst + p.g_tile_bytes, p.up + e * p.u_expert_bytes + (long long)tile * p.u_tile_bytes, p.u_tile_bytes,
+        bulk_g2s(dst, expert_gate(p, e) + (long long)tile * p.g_tile_bytes, p.g_tile_bytes, &mybar[slot]);
+        bulk_g2s(dst + p.g_tile_bytes, expert_up(p, e) + (long long)tile * p.u_tile_bytes, p.u_tile_bytes,
                  &mybar[slot]);
     };
     if (lane == 0)
@@ -463,7 +463,7 @@ __global__ void __launch_bounds__(NWARP * 32, 1) down_kernel(const __grid_consta
         mbar_arrive_expect_tx(&mybar[slot], p.K * p.d_tile_bytes);
         for (int k = 0; k < p.K; k++) {
             int e = p.sel_ids[t * p.K + k];
-            bulk_g2s(dst + k * p.d_tile_bytes, p.down + e * p.d_expert_bytes + (long long)row * p.d_tile_bytes,
+            bulk_g2s(dst + k * p.d_tile_bytes, expert_down(p, e) + (long long)row * p.d_tile_bytes,
                      p.d_tile_bytes, &mybar[slot]);
         }
     };
@@ -547,9 +547,11 @@ cudaError_t launch_down(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl
 
 // ====================================================================== grouped experts (batched steps)
 // With many tokens in a step, the per-(token, expert) units above read an expert's weights once
-// for every token that selected it. The grouped kernels read each selected expert's weights
-// once per step: units are (expert, tile), and a CTA stages the activations of that expert's
-// tokens (GROUP_MAXM at a time). The arithmetic per (token, expert, row) is unchanged.
+// for every token that selected it. The grouped kernels split each selected expert's rows into
+// chunks of at most GROUP_MAXM and make units (chunk, tile): every unit has about the same
+// work however skewed the routing, an expert's tile is read from DRAM about once and re-read
+// from L2 by its other chunks, and a CTA (a contiguous unit range) stages each chunk's
+// activations once. The arithmetic per (token, expert, row) is unchanged.
 
 // One CTA: per expert, the (token, slot) indices tk = t*K + k that selected it, ascending.
 __global__ void __launch_bounds__(256) group_kernel(const __grid_constant__ GroupArgs p) {
@@ -566,13 +568,19 @@ __global__ void __launch_bounds__(256) group_kernel(const __grid_constant__ Grou
     }
     __syncthreads();
     if (tid == 0) {
-        int na = 0, o = 0;
+        int na = 0, o = 0, nch = 0;
         for (int e = 0; e < p.NE; e++) {
             off[e] = o;
             o += cnt[e];
             if (cnt[e]) p.g_active[na++] = e;
+            for (int r0 = 0; r0 < cnt[e]; r0 += GROUP_MAXM) {
+                p.g_chunk_e[nch] = e;
+                p.g_chunk_r0[nch] = r0;
+                nch++;
+            }
         }
         *p.g_nactive = na;
+        *p.g_nchunks = nch;
     }
     __syncthreads();
     for (int e = tid; e < p.NE; e += blockDim.x) {
@@ -618,17 +626,17 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gateup_grouped_kernel(const __g
     }
     __syncwarp();
     pdl_wait();  // the groups come from group_kernel, the activations from the router
-    const int total = *p.g_nactive * nt;
+    const int total = *p.g_nchunks * nt;
     const int u0 = (int)((unsigned)blockIdx.x * (unsigned)total / gridDim.x);
     const int u1 = (int)((unsigned)(blockIdx.x + 1) * (unsigned)total / gridDim.x);
     pdl_trigger();
     bool ok = true;
-    for (int a = nt ? u0 / nt : 0; ok && a * nt < u1; a++) {
-        const int e = p.g_active[a], m = p.g_count[e], off = p.g_off[e];
-        const int lo = (u0 > a * nt ? u0 : a * nt) - a * nt;
-        const int hi = (u1 < (a + 1) * nt ? u1 : (a + 1) * nt) - a * nt;
+    for (int ci = nt ? u0 / nt : 0; ok && ci * nt < u1; ci++) {
+        const int e = p.g_chunk_e[ci], c0 = p.g_chunk_r0[ci], m = p.g_count[e], off = p.g_off[e];
+        const int lo = (u0 > ci * nt ? u0 : ci * nt) - ci * nt;
+        const int hi = (u1 < (ci + 1) * nt ? u1 : (ci + 1) * nt) - ci * nt;
         const int ntw = hi - lo > warp ? (hi - lo - warp + NWARP - 1) / NWARP : 0;
-        for (int c0 = 0; ok && c0 < m; c0 += GROUP_MAXM) {
+        {
             const int mc = m - c0 < GROUP_MAXM ? m - c0 : GROUP_MAXM;
             __syncthreads();  // the previous chunk's activations are no longer read
             if (tid < mc) {
@@ -641,9 +649,9 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gateup_grouped_kernel(const __g
                 const int tile = lo + warp + j * NWARP, slot = (base + j) % r.nst;
                 uint8_t *dst = r.base + (size_t)slot * r.slot_bytes;
                 mbar_arrive_expect_tx(&r.bars[slot], p.g_tile_bytes + p.u_tile_bytes);
-                bulk_g2s(dst, p.gate + e * p.g_expert_bytes + (long long)tile * p.g_tile_bytes, p.g_tile_bytes,
+                bulk_g2s(dst, expert_gate(p, e) + (long long)tile * p.g_tile_bytes, p.g_tile_bytes,
                          &r.bars[slot]);
-                bulk_g2s(dst + p.g_tile_bytes, p.up + e * p.u_expert_bytes + (long long)tile * p.u_tile_bytes,
+                bulk_g2s(dst + p.g_tile_bytes, expert_up(p, e) + (long long)tile * p.u_tile_bytes,
                          p.u_tile_bytes, &r.bars[slot]);
             };
             if (lane == 0) {
@@ -738,17 +746,17 @@ __global__ void __launch_bounds__(NWARP * 32, 1) down_grouped_kernel(const __gri
     }
     __syncwarp();
     pdl_wait();
-    const int total = *p.g_nactive * ng;
+    const int total = *p.g_nchunks * ng;
     const int u0 = (int)((unsigned)blockIdx.x * (unsigned)total / gridDim.x);
     const int u1 = (int)((unsigned)(blockIdx.x + 1) * (unsigned)total / gridDim.x);
     pdl_trigger();
     bool ok = true;
-    for (int a = ng ? u0 / ng : 0; ok && a * ng < u1; a++) {
-        const int e = p.g_active[a], m = p.g_count[e], off = p.g_off[e];
-        const int lo = (u0 > a * ng ? u0 : a * ng) - a * ng;
-        const int hi = (u1 < (a + 1) * ng ? u1 : (a + 1) * ng) - a * ng;
+    for (int ci = ng ? u0 / ng : 0; ok && ci * ng < u1; ci++) {
+        const int e = p.g_chunk_e[ci], c0 = p.g_chunk_r0[ci], m = p.g_count[e], off = p.g_off[e];
+        const int lo = (u0 > ci * ng ? u0 : ci * ng) - ci * ng;
+        const int hi = (u1 < (ci + 1) * ng ? u1 : (ci + 1) * ng) - ci * ng;
         const int nuw = hi - lo > warp ? (hi - lo - warp + NWARP - 1) / NWARP : 0;
-        for (int c0 = 0; ok && c0 < m; c0 += GROUP_MAXM) {
+        {
             const int mc = m - c0 < GROUP_MAXM ? m - c0 : GROUP_MAXM;
             __syncthreads();
             if (tid < mc) tk_s[tid] = p.g_list[off + c0 + tid];
@@ -757,7 +765,7 @@ __global__ void __launch_bounds__(NWARP * 32, 1) down_grouped_kernel(const __gri
                 const int gr = lo + warp + j * NWARP, slot = (base + j) % r.nst;
                 const int r0 = gr * RG, nr = p.E - r0 < RG ? p.E - r0 : RG;
                 mbar_arrive_expect_tx(&r.bars[slot], nr * p.d_tile_bytes);
-                bulk_g2s(r.base + (size_t)slot * r.slot_bytes, p.down + e * p.d_expert_bytes + (long long)r0 * p.d_tile_bytes,
+                bulk_g2s(r.base + (size_t)slot * r.slot_bytes, expert_down(p, e) + (long long)r0 * p.d_tile_bytes,
                          nr * p.d_tile_bytes, &r.bars[slot]);
             };
             if (lane == 0) {

@@ -76,12 +76,31 @@ struct ExpertArgs {
     int prefetch_down;  // gate/up: pull the selected experts' down weights into L2
     // grouped form (batched steps): the tokens of each selected expert, from group_kernel
     const int *g_count, *g_off, *g_list, *g_active, *g_nactive;
+    const int *g_chunk_e, *g_chunk_r0, *g_nchunks;  // the chunks of at most GROUP_MAXM rows
     float *dpart;  // [T][K][E] each (token, expert slot)'s down rows before the expert sum
     int row_div;   // grouped gate/up: the activation row of list entry i is i / row_div
     // expert parallelism: the combine reads slot (t, k) of the rank owning expert sel_ids[t*K+k]
     // from dpart[(owner * ep_slots + t*K + k) * E]; ep_ranks = 0 outside expert parallelism
     int ep_ranks, ep_per, ep_slots;
+    // expert cache: expert e's gate | up | down matrices sit in slot slot_of[e] of the pool
+    // (slot_stride bytes each); slot_of = null when every expert is resident
+    const int *slot_of;
+    const uint8_t *pool;
+    long long slot_stride;
 };
+
+// the weights of expert e: its resident matrices, or its slot of the expert cache
+__device__ __forceinline__ const uint8_t *expert_gate(const ExpertArgs &p, int e) {
+    return p.slot_of ? p.pool + (long long)p.slot_of[e] * p.slot_stride : p.gate + e * p.g_expert_bytes;
+}
+__device__ __forceinline__ const uint8_t *expert_up(const ExpertArgs &p, int e) {
+    return p.slot_of ? p.pool + (long long)p.slot_of[e] * p.slot_stride + p.g_expert_bytes
+                     : p.up + e * p.u_expert_bytes;
+}
+__device__ __forceinline__ const uint8_t *expert_down(const ExpertArgs &p, int e) {
+    return p.slot_of ? p.pool + (long long)p.slot_of[e] * p.slot_stride + p.g_expert_bytes + p.u_expert_bytes
+                     : p.down + e * p.d_expert_bytes;
+}
 
 // Expert-parallel dispatch: the rows of every (token, slot) pair, packed for the rank that owns
 // the pair's expert (ranks own ep_per consecutive experts each).
@@ -100,8 +119,11 @@ struct GroupArgs {
     const int *sel_ids;  // [T][K]
     int T, K, NE;
     int *g_count, *g_off, *g_list, *g_active, *g_nactive;
+    int *g_chunk_e, *g_chunk_r0, *g_nchunks;  // chunk i: expert g_chunk_e[i], its rows from g_chunk_r0[i]
 };
 constexpr int GROUP_MAXM = 16;  // tokens of one expert whose activations a CTA stages at a time
+// chunks of a grouped step: at most one partial chunk per expert
+inline int group_max_chunks(int rows, int NE) { return rows / GROUP_MAXM + NE + 1; }
 
 struct RouterArgs {
     const float *x, *norm_w;

@@ -69,6 +69,20 @@ class Engine:
         check(lib.bt_engine_tensor_bytes(self.h, name.encode(), _lib.ptr(out), nbytes))
         return out
 
+    def enable_expert_cache(self, cache_bytes: int, policy: str = "freq"):
+        """Move the experts to pinned host memory and serve them through an HBM cache of
+        cache_bytes ("lru" or "freq": the reference's frequency-gated admission)."""
+        pol = {"lru": _lib.XCACHE_LRU, "freq": _lib.XCACHE_FREQ}[policy]
+        check(lib.bt_engine_enable_expert_cache(self.h, int(cache_bytes), pol))
+
+    def expert_cache_stats(self) -> dict:
+        s = _lib.XCacheStats()
+        check(lib.bt_expert_cache_stats(self.h, C.byref(s)))
+        d = {k: getattr(s, k) for k, _ in s._fields_}
+        n = d["hits"] + d["misses"]
+        d["hit_rate"] = d["hits"] / n if n else 0.0
+        return d
+
     def set_router_bias(self, layer: int, bias):
         """Set (or, with None, remove) layer's router bias: one F32 value per expert, added to
         the router logits before the softmax."""
@@ -189,6 +203,17 @@ class KvCache:
         if k.nbytes != v.nbytes:
             raise BtError(_lib.BT_ERR_KV, "k and v differ in size")
         check(lib.bt_kv_import_layer(self.h, seq, layer, _lib.ptr(k), _lib.ptr(v), k.nbytes))
+
+
+def simulate_expert_cache(policy: str, capacity: int, trace: np.ndarray) -> dict:
+    """The expert-cache policy alone on a selection trace [steps, layers, n_sel] (host only)."""
+    tr = np.ascontiguousarray(trace, dtype=np.int32)
+    steps, n_layer, n_sel = tr.shape
+    s = _lib.XCacheStats()
+    pol = {"lru": _lib.XCACHE_LRU, "freq": _lib.XCACHE_FREQ}[policy]
+    check(lib.bt_expert_cache_simulate(pol, capacity, n_layer, int(tr.max()) + 1, n_sel, _lib.ptr(tr, C.c_int32),
+                                       steps, C.byref(s)))
+    return {k: getattr(s, k) for k, _ in s._fields_}
 
 
 def ep_unique_id() -> bytes:

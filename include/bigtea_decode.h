@@ -156,6 +156,30 @@ int bt_set_option(bt_engine *e, const char *name, int value);
  * blk.N.ffn_gate_inp.bias. */
 int bt_engine_set_router_bias(bt_engine *e, uint32_t layer, const float *bias, uint32_t n);
 
+/* ---- expert cache (models whose experts do not fit in HBM) ----
+ * The experts move to pinned host memory; each step copies the experts a layer selects into
+ * slots of an HBM pool of `cache_bytes` (cudaMemcpyAsync on the engine's stream, ordered
+ * before that layer's expert kernels). The reference streams expert slices from disk into a
+ * host cache instead (core/arch/src/stream.rs:1400-1475, admission stream.rs:1314-1379,
+ * core/arch/src/expert_cache.rs); here the slow tier is host memory and the cache is HBM.
+ * Policies: BT_XCACHE_LRU evicts the least recently used expert; BT_XCACHE_FREQ is the
+ * reference's frequency-gated admission (a newcomer replaces the least-used of 8 sampled
+ * entries only when selected strictly more often; else it is used once from a bounce slot).
+ * Steps run as per-phase kernels with one host round trip per layer; results are the same
+ * bits as with every expert resident. Not combinable with expert parallelism. */
+enum { BT_XCACHE_LRU = 0, BT_XCACHE_FREQ = 1 };
+typedef struct bt_xcache_stats {
+    uint64_t hits, misses, evictions, admissions, bypasses, bytes_copied;
+    uint64_t capacity_slots, slot_bytes;
+} bt_xcache_stats;
+/* a second call starts a new, empty cache of the given size and policy */
+int bt_engine_enable_expert_cache(bt_engine *e, uint64_t cache_bytes, int policy);
+int bt_expert_cache_stats(const bt_engine *e, bt_xcache_stats *out);
+/* the policy alone, on the host: a trace of n_steps x n_layer groups of n_sel expert ids
+ * (layer-major within a step), looked up in order; no device is touched */
+int bt_expert_cache_simulate(int policy, uint32_t capacity, uint32_t n_layer, uint32_t n_expert, uint32_t n_sel,
+                             const int32_t *trace, uint32_t n_steps, bt_xcache_stats *out);
+
 /* ---- expert parallelism (batched decode over the GPUs of one node) ----
  * No counterpart in the reference, which has no distributed code. One engine per GPU, one
  * process each. With n ranks, rank r computes the experts [r*NE/n, (r+1)*NE/n). Each layer of
