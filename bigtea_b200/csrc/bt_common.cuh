@@ -56,6 +56,25 @@ __device__ __forceinline__ float bt_exp(float x) {
 
 // f16 x f16 + f32 with one rounding (sm_100 mixed-precision fma on the FMA pipe). Equal to
 // fmaf((float)a, (float)b, c): the product of two f16 values is exact in f32.
+// Packed pairs of f32 (low half = element 0) and the paired fma of sm_100: each half is one
+// fmaf (a single rounding), exactly as the scalar form.
+typedef unsigned long long f32x2;
+__device__ __forceinline__ f32x2 pk2(float lo, float hi) {
+    f32x2 r;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+    return r;
+}
+__device__ __forceinline__ float2 upk2(f32x2 v) {
+    float2 r;
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
+    return r;
+}
+__device__ __forceinline__ f32x2 ffma2(f32x2 a, f32x2 b, f32x2 c) {
+    f32x2 d;
+    asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+    return d;
+}
+
 __device__ __forceinline__ float fma_f16(uint16_t a, uint16_t b, float c) {
     float d;
     asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(c));

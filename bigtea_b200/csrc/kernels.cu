@@ -237,17 +237,22 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_kernel(const __grid_consta
         const long long tl = u - sg.tile0;
         const bool active = lane < sg.S;
         const int b = active ? lane % sg.nsb : 0;
+        // lane's superblock decoded into registers once; its dots with the tokens' activation
+        // blocks two at a time (independent chains)
+        const uint32_t tile_s = smem_u32(tile), act_b = smem_u32(&act[b]);
+        const uint32_t tok_stride = (uint32_t)(nsbK * sizeof(ActBlock));
+        const int ls = active ? lane : 0;
         // 8 tokens at a time: every lane's superblock partial to shared memory, then one lane
         // per (row, token) adds the row's nsb partials in superblock order (C4)
+        auto run_tokens = [&](auto &&dot) {
         for (int t0 = 0; t0 < p.T; t0 += 8) {
             const int tn = p.T - t0 < 8 ? p.T - t0 : 8;
-            for (int i = 0; i < tn; i++) {
-                float v = 0.0f;
-                if (active) {
-                    const ActBlock &ab = act[(t0 + i) * nsbK + b];
-                    v = (sg.type == T_Q4_K) ? q4k_slot_dot(tile, sg.S, lane, ab) : q6k_slot_dot(tile, sg.S, lane, ab);
-                }
-                red[i * RED_STRIDE + lane] = v;
+            for (int i = 0; i < tn; i += 2) {
+                const int i1 = i + 1 < tn ? i + 1 : i;
+                const float v0 = dot(act_b + (uint32_t)(t0 + i) * tok_stride);
+                const float v1 = dot(act_b + (uint32_t)(t0 + i1) * tok_stride);
+                red[i * RED_STRIDE + lane] = active ? v0 : 0.0f;
+                if (i + 1 < tn) red[(i + 1) * RED_STRIDE + lane] = active ? v1 : 0.0f;
             }
             __syncwarp();
             for (int q = lane; q < sg.rpt * 8; q += 32) {
@@ -271,6 +276,16 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gemv_kernel(const __grid_consta
                 }
             }
             __syncwarp();
+        }
+        };
+        if (sg.type == T_Q4_K) {
+            Q4Reg w;
+            q4k_load_r(w, tile_s, sg.S, ls);
+            run_tokens([&](uint32_t a) { return q4k_dot_r(w, a); });
+        } else {
+            Q6Reg w;
+            q6k_load_r(w, tile_s, sg.S, ls);
+            run_tokens([&](uint32_t a) { return q6k_dot_r(w, a); });
         }
         __syncwarp();
         if (lane == 0 && j + p.nst < nmine) {
@@ -619,7 +634,7 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gateup_grouped_kernel(const __g
     r.bars = reinterpret_cast<uint64_t *>(smem) + warp * p.nst;
     r.issued = r.done = 0;
     float *red = reinterpret_cast<float *>(smem + 1024 + ((act_bytes + 127) & ~(size_t)127) +
-                                           (size_t)NWARP * p.nst * p.slot_bytes) + warp * 2 * RED_WARP_FLOATS;
+                                           (size_t)NWARP * p.nst * p.slot_bytes) + warp * 2 * GROUP_RED_FLOATS;
     if (lane == 0) {
         for (int i = 0; i < p.nst; i++) mbar_init(&r.bars[i], 1);
         fence_mbar_init();
@@ -676,37 +691,47 @@ __global__ void __launch_bounds__(NWARP * 32, 1) gateup_grouped_kernel(const __g
                 const uint8_t *gt = r.base + (size_t)slot * r.slot_bytes, *ut = gt + p.g_tile_bytes;
                 const bool active = lane < p.g_S;
                 const int b = active ? lane % nsb : 0;
-                for (int t0 = 0; t0 < mc; t0 += 8) {  // 8 tokens at a time, reduced as in gemv_kernel
-                    const int tn = mc - t0 < 8 ? mc - t0 : 8;
-#pragma unroll 1
-                    for (int i = 0; i < tn; i++) {
-#pragma unroll 1
-                        for (int which = 0; which < 2; which++) {
-                            const uint8_t *tl = which ? ut : gt;
-                            const int ty = which ? p.utype : p.gtype;
-                            float v = 0.0f;
-                            if (active) {
-                                const ActBlock &ab = act[(t0 + i) * nsb + b];
-                                v = ty == T_Q4_K ? q4k_slot_dot(tl, p.g_S, lane, ab) : q6k_slot_dot(tl, p.g_S, lane, ab);
-                            }
-                            red[which * RED_WARP_FLOATS + i * RED_STRIDE + lane] = v;
-                        }
+                const int ls = active ? lane : 0;
+                const uint32_t act_b = smem_u32(&act[b]), tok_stride = (uint32_t)(nsb * sizeof(ActBlock));
+                // gate then up: the lane's superblock decoded into registers once, its dots with
+                // the chunk's tokens two at a time, every partial to shared memory
+                auto dots = [&](auto &&dot, float *dst) {
+                    for (int i = 0; i < mc; i += 2) {
+                        const int i1 = i + 1 < mc ? i + 1 : i;
+                        const float v0 = dot(act_b + (uint32_t)i * tok_stride);
+                        const float v1 = dot(act_b + (uint32_t)i1 * tok_stride);
+                        dst[i * RED_STRIDE + lane] = active ? v0 : 0.0f;
+                        if (i + 1 < mc) dst[(i + 1) * RED_STRIDE + lane] = active ? v1 : 0.0f;
                     }
-                    __syncwarp();
-                    for (int q = lane; q < p.g_rpt * 8; q += 32) {
-                        const int rr = q >> 3, i = q & 7, rrow = tile * p.g_rpt + rr;
-                        if (i < tn && rrow < p.F) {
-                            const float *gv = red + i * RED_STRIDE + rr * nsb;
-                            const float *uv = gv + RED_WARP_FLOATS;
-                            float ag = 0.0f, au = 0.0f;
-                            for (int b2 = 0; b2 < nsb; b2++) {
-                                ag = __fadd_rn(ag, gv[b2]);
-                                au = __fadd_rn(au, uv[b2]);
-                            }
-                            p.act[(long long)tk_s[t0 + i] * p.F + rrow] = __fmul_rn(bt_silu(ag), au);
-                        }
+                };
+#pragma unroll 1
+                for (int which = 0; which < 2; which++) {
+                    const uint32_t tl = smem_u32(which ? ut : gt);
+                    float *dst = red + which * GROUP_RED_FLOATS;
+                    if ((which ? p.utype : p.gtype) == T_Q4_K) {
+                        Q4Reg w;
+                        q4k_load_r(w, tl, p.g_S, ls);
+                        dots([&](uint32_t a) { return q4k_dot_r(w, a); }, dst);
+                    } else {
+                        Q6Reg w;
+                        q6k_load_r(w, tl, p.g_S, ls);
+                        dots([&](uint32_t a) { return q6k_dot_r(w, a); }, dst);
                     }
-                    __syncwarp();
+                }
+                __syncwarp();
+                // one lane per (row, token): the row's nsb partials in superblock order (C4)
+                for (int q = lane; q < p.g_rpt * GROUP_MAXM; q += 32) {
+                    const int rr = q / GROUP_MAXM, i = q % GROUP_MAXM, rrow = tile * p.g_rpt + rr;
+                    if (i < mc && rrow < p.F) {
+                        const float *gv = red + i * RED_STRIDE + rr * nsb;
+                        const float *uv = gv + GROUP_RED_FLOATS;
+                        float ag = 0.0f, au = 0.0f;
+                        for (int b2 = 0; b2 < nsb; b2++) {
+                            ag = __fadd_rn(ag, gv[b2]);
+                            au = __fadd_rn(au, uv[b2]);
+                        }
+                        p.act[(long long)tk_s[i] * p.F + rrow] = __fmul_rn(bt_silu(ag), au);
+                    }
                 }
                 __syncwarp();
                 if (lane == 0 && r.issued - base < ntw) {
@@ -790,20 +815,35 @@ __global__ void __launch_bounds__(NWARP * 32, 1) down_grouped_kernel(const __gri
                 const int nr = p.E - r0 < RG ? p.E - r0 : RG;
                 const bool active = lane < nr * nsb;
                 const int rr = active ? lane / nsb : 0, b = active ? lane - rr * nsb : 0;
-                const uint8_t *tile = r.base + (size_t)slot * r.slot_bytes + (size_t)rr * p.d_tile_bytes;
-#pragma unroll 1
-                for (int i = 0; i < mc; i++) {
-                    float v = 0.0f;
-                    if (active) {
-                        const ActBlock &ab = act[i * nsb + b];
-                        v = p.dtype == T_Q4_K ? q4k_slot_dot(tile, nsb, b, ab) : q6k_slot_dot(tile, nsb, b, ab);
+                const uint32_t tile = smem_u32(r.base + (size_t)slot * r.slot_bytes + (size_t)rr * p.d_tile_bytes);
+                const uint32_t act_b = smem_u32(&act[b]), tok_stride = (uint32_t)(nsb * sizeof(ActBlock));
+                // the lane's superblock in registers once; two tokens at a time, each row's nsb
+                // partials added in superblock order across its lanes (C4)
+                auto dots = [&](auto &&dot) {
+                    for (int i = 0; i < mc; i += 2) {
+                        const int i1 = i + 1 < mc ? i + 1 : i;
+                        const float v0 = dot(act_b + (uint32_t)i * tok_stride);
+                        const float v1 = dot(act_b + (uint32_t)i1 * tok_stride);
+                        float acc0 = 0.0f, acc1 = 0.0f;
+                        for (int b2 = 0; b2 < nsb; b2++) {
+                            const int srcl = rr * nsb + b2;
+                            acc0 = __fadd_rn(acc0, __shfl_sync(FULL, v0, srcl < 32 ? srcl : 31));
+                            acc1 = __fadd_rn(acc1, __shfl_sync(FULL, v1, srcl < 32 ? srcl : 31));
+                        }
+                        if (active && b == 0) {
+                            p.dpart[(long long)tk_s[i] * p.E + r0 + rr] = acc0;
+                            if (i + 1 < mc) p.dpart[(long long)tk_s[i + 1] * p.E + r0 + rr] = acc1;
+                        }
                     }
-                    float acc = 0.0f;
-                    for (int b2 = 0; b2 < nsb; b2++) {
-                        const int srcl = rr * nsb + b2;
-                        acc = __fadd_rn(acc, __shfl_sync(FULL, v, srcl < 32 ? srcl : 31));
-                    }
-                    if (active && b == 0) p.dpart[(long long)tk_s[i] * p.E + r0 + rr] = acc;
+                };
+                if (p.dtype == T_Q4_K) {
+                    Q4Reg w;
+                    q4k_load_r(w, tile, nsb, b);
+                    dots([&](uint32_t a) { return q4k_dot_r(w, a); });
+                } else {
+                    Q6Reg w;
+                    q6k_load_r(w, tile, nsb, b);
+                    dots([&](uint32_t a) { return q6k_dot_r(w, a); });
                 }
                 __syncwarp();
                 if (lane == 0 && r.issued - base < nuw) {
@@ -874,7 +914,7 @@ cudaError_t launch_ep_pack(const EpPackArgs &a, cudaStream_t st, bool pdl) {
 size_t gateup_grouped_smem_bytes(const ExpertArgs &a) {
     size_t act = (size_t)GROUP_MAXM * a.g_nsb * sizeof(ActBlock);
     return 1024 + ((act + 127) & ~(size_t)127) + (size_t)GEMV_WARPS * a.nst * a.slot_bytes +
-           (size_t)GEMV_WARPS * 2 * RED_WARP_FLOATS * 4;
+           (size_t)GEMV_WARPS * 2 * GROUP_RED_FLOATS * 4;
 }
 size_t down_grouped_smem_bytes(const ExpertArgs &a) {
     size_t act = (size_t)GROUP_MAXM * a.d_nsb * sizeof(ActBlock);
@@ -1086,7 +1126,7 @@ constexpr int ATTN_THREADS = 128;
 constexpr int ATTN_PART_ROW = 132;  // floats per (chunk, head) partial: acc[128], m, l, 2 pad
 
 size_t attn_smem_bytes(int G, int T) {
-    return 65536 + (size_t)128 * G * 2 + (size_t)ATTN_CHUNK * G * 4 + (32 + 32 + 8 + 8) * 4 + 16 +
+    return 65536 + (size_t)128 * G * 4 + (size_t)ATTN_CHUNK * G * 4 + (32 + 32 + 8 + 8) * 4 + 16 +
            (size_t)(3 * T + 1) * 4 + 1024;
 }
 
@@ -1155,8 +1195,8 @@ __global__ void __launch_bounds__(ATTN_THREADS, 3)
     // offset from the shared array itself (not through an integer), so loads stay ld.shared
     uint8_t *smem = smem_raw + ((1024u - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023u)) & 1023u);
     uint8_t *const K0 = smem, *const K1 = smem + 16384, *const V0 = smem + 32768, *const V1 = smem + 49152;
-    uint16_t *qs = reinterpret_cast<uint16_t *>(smem + 65536);        // [D][G] f16 bits
-    float *ps = reinterpret_cast<float *>(smem + 65536 + D * G * 2);  // [CH][G]
+    float *qs = reinterpret_cast<float *>(smem + 65536);              // [D][G] q rounded to f16, as f32
+    float *ps = reinterpret_cast<float *>(smem + 65536 + D * G * 4);  // [CH][G]
     float *red = ps + CH * G;                                         // [4][8]
     float *red2 = red + 32;                                           // [4][8]
     float *s_m = red2 + 32, *s_l = s_m + 8;
@@ -1261,7 +1301,7 @@ __global__ void __launch_bounds__(ATTN_THREADS, 3)
             cur_tg = t * p.HK + g;
             for (int x = tid; x < D * G; x += ATTN_THREADS) {
                 const int h = x / D, d = x % D;
-                qs[d * G + h] = __half_as_ushort(__float2half_rn(p.q[(long long)t * QW + (g * G + h) * D + d]));
+                qs[d * G + h] = __half2float(__float2half_rn(p.q[(long long)t * QW + (g * G + h) * D + d]));
             }
         }
         __syncthreads();
@@ -1274,29 +1314,37 @@ __global__ void __launch_bounds__(ATTN_THREADS, 3)
         const int k = tid;
         const bool valid = k < cnt;
         float sc[G];
-#pragma unroll
-        for (int h = 0; h < G; h++) sc[h] = 0.0f;
         {
+            // heads in pairs: (sc[2j], sc[2j+1]) += (q[d][2j], q[d][2j+1]) * (k[d], k[d]), one
+            // paired fma per pair and dimension, d in order (C8: each an fmaf of two f16 values)
+            f32x2 acc[G / 2];
+#pragma unroll
+            for (int j = 0; j < G / 2; j++) acc[j] = 0ull;
             const uint8_t *krow = K0 + k * 128;
             const int ksw = k & 7;
-            const uint32_t *qw = reinterpret_cast<const uint32_t *>(qs);
 #pragma unroll 2
             for (int c16 = 0; c16 < 16; c16++) {
                 const uint4 w =
                     *reinterpret_cast<const uint4 *>((c16 < 8 ? krow : krow + 16384) + (((c16 & 7) ^ ksw) << 4));
                 const uint32_t kw[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-                for (int e = 0; e < 8; e++) {
-                    uint32_t q[QWORDS];
-                    ldw_n<QWORDS>(q, qw + (c16 * 8 + e) * QWORDS);
+                for (int e2 = 0; e2 < 4; e2++) {
+                    const float2 kf = h2f2_fma(kw[e2]);
 #pragma unroll
-                    for (int jj = 0; jj < QWORDS; jj++) {
-                        if (e & 1)
-                            fma_qk<true>(q[jj], kw[e >> 1], sc[2 * jj], sc[2 * jj + 1]);
-                        else
-                            fma_qk<false>(q[jj], kw[e >> 1], sc[2 * jj], sc[2 * jj + 1]);
+                    for (int hl = 0; hl < 2; hl++) {
+                        const int d = c16 * 8 + 2 * e2 + hl;
+                        const f32x2 kk = hl ? pk2(kf.y, kf.y) : pk2(kf.x, kf.x);
+                        const f32x2 *qd = reinterpret_cast<const f32x2 *>(qs + d * G);
+#pragma unroll
+                        for (int j = 0; j < G / 2; j++) acc[j] = ffma2(qd[j], kk, acc[j]);
                     }
                 }
+            }
+#pragma unroll
+            for (int j = 0; j < G / 2; j++) {
+                const float2 v = upk2(acc[j]);
+                sc[2 * j] = v.x;
+                sc[2 * j + 1] = v.y;
             }
         }
 #pragma unroll
@@ -1342,9 +1390,17 @@ __global__ void __launch_bounds__(ATTN_THREADS, 3)
         }
         // ---- P*V
         float acc0[HPT], acc1[HPT];
-#pragma unroll
-        for (int h = 0; h < HPT; h++) acc0[h] = acc1[h] = 0.0f;
         {
+            // heads in pairs: (acc[d][h], acc[d][h+1]) += (p[h], p[h+1]) * (v[d], v[d]), keys in
+            // order (C8)
+            constexpr bool PAIRS = HPT % 2 == 0;  // else one head at a time (G = 2, 6)
+            constexpr int NP = PAIRS ? HPT / 2 : 1;
+            f32x2 a0[NP], a1[NP];
+            float s0[HPT], s1[HPT];
+#pragma unroll
+            for (int j = 0; j < NP; j++) a0[j] = a1[j] = 0ull;
+#pragma unroll
+            for (int h = 0; h < HPT; h++) s0[h] = s1[h] = 0.0f;
             const int d = 2 * dp, cc = (d & 63) >> 3;
             const uint8_t *vcol = ((d < 64) ? V0 : V1) + (d & 7) * 2;
             int off[8];
@@ -1358,14 +1414,40 @@ __global__ void __launch_bounds__(ATTN_THREADS, 3)
                 for (int kk = 0; kk < 8; kk++) {
                     if (j0 + kk < cnt) {
                         const float2 vf = h2f2_fma(*reinterpret_cast<const uint32_t *>(vb + off[kk]));
-                        float pj[HPT];
-                        lds_vec<HPT>(pj, pb + kk * G);
+                        if constexpr (PAIRS) {
+                            const f32x2 *pp = reinterpret_cast<const f32x2 *>(pb + kk * G);
+                            const f32x2 vx = pk2(vf.x, vf.x), vy = pk2(vf.y, vf.y);
 #pragma unroll
-                        for (int h = 0; h < HPT; h++) {
-                            acc0[h] = fmaf(pj[h], vf.x, acc0[h]);
-                            acc1[h] = fmaf(pj[h], vf.y, acc1[h]);
+                            for (int j = 0; j < NP; j++) {
+                                const f32x2 pj = pp[j];
+                                a0[j] = ffma2(pj, vx, a0[j]);
+                                a1[j] = ffma2(pj, vy, a1[j]);
+                            }
+                        } else {
+#pragma unroll
+                            for (int h = 0; h < HPT; h++) {
+                                const float pj = pb[kk * G + h];
+                                s0[h] = fmaf(pj, vf.x, s0[h]);
+                                s1[h] = fmaf(pj, vf.y, s1[h]);
+                            }
                         }
                     }
+                }
+            }
+            if constexpr (PAIRS) {
+#pragma unroll
+                for (int j = 0; j < NP; j++) {
+                    const float2 x = upk2(a0[j]), y = upk2(a1[j]);
+                    acc0[2 * j] = x.x;
+                    acc0[2 * j + 1] = x.y;
+                    acc1[2 * j] = y.x;
+                    acc1[2 * j + 1] = y.y;
+                }
+            } else {
+#pragma unroll
+                for (int h = 0; h < HPT; h++) {
+                    acc0[h] = s0[h];
+                    acc1[h] = s1[h];
                 }
             }
         }

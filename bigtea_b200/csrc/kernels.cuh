@@ -122,6 +122,7 @@ struct GroupArgs {
     int *g_chunk_e, *g_chunk_r0, *g_nchunks;  // chunk i: expert g_chunk_e[i], its rows from g_chunk_r0[i]
 };
 constexpr int GROUP_MAXM = 16;  // tokens of one expert whose activations a CTA stages at a time
+constexpr int GROUP_RED_FLOATS = GROUP_MAXM * RED_STRIDE;  // a warp's partials of one chunk (gate or up)
 // chunks of a grouped step: at most one partial chunk per expert
 inline int group_max_chunks(int rows, int NE) { return rows / GROUP_MAXM + NE + 1; }
 

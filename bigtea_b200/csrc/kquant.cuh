@@ -421,6 +421,136 @@ __device__ __forceinline__ float q6k_dot_s(uint32_t tile_s, int S, int s, uint32
     return __fmul_rn(__int2float_rn(sumi), __fmul_rn(dw, lds_f32(act_s + ACT_D)));
 }
 
+// Register-resident forms for several tokens against one weight superblock: *_load_r decodes
+// lane s's superblock of the tile once (nibbles masked, 6-bit values assembled, scales
+// unpacked), *_dot_r then computes one token's dot from its activation block. Each is the same
+// integer and float arithmetic, in the same order, as q4k_dot_s / q6k_dot_s.
+struct Q4Reg {
+    uint32_t lo[32], hi[32];  // per 32-value group g: words 8g..8g+7, low and high nibbles in place
+    int sc[8], mn[8];
+    float dw, dminw;
+};
+__device__ __forceinline__ void q4k_load_r(Q4Reg &r, uint32_t tile_s, int S, int s) {
+    const uint32_t base = tile_s + (uint32_t)s * 16u, cstride = (uint32_t)S * 16u;
+    const uint4 h = lds_u4(base);
+    r.dw = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffff)));
+    r.dminw = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+    const uint32_t s03 = h.y, s47 = h.z, s811 = h.w;
+    const uint32_t sc_lo = s03 & 0x3F3F3F3Fu, m_lo = s47 & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (s811 & 0x0F0F0F0Fu) | ((s03 >> 2) & 0x30303030u);
+    const uint32_t m_hi = ((s811 >> 4) & 0x0F0F0F0Fu) | ((s47 >> 2) & 0x30303030u);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        r.sc[j] = byte_u(sc_lo, j);
+        r.sc[j + 4] = byte_u(sc_hi, j);
+        r.mn[j] = byte_u(m_lo, j);
+        r.mn[j + 4] = byte_u(m_hi, j);
+    }
+#pragma unroll
+    for (int g = 0; g < 4; g++) {
+        const uint4 w0 = lds_u4(base + (1 + 2 * g) * cstride), w1 = lds_u4(base + (2 + 2 * g) * cstride);
+        const uint32_t w[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            r.lo[8 * g + i] = w[i] & 0x0F0F0F0Fu;
+            r.hi[8 * g + i] = w[i] & 0xF0F0F0F0u;
+        }
+    }
+}
+__device__ __forceinline__ float q4k_dot_r(const Q4Reg &r, uint32_t act_s) {
+    int dot[8];
+#pragma unroll
+    for (int g = 0; g < 4; g++) {
+        const uint4 al0 = lds_u4(act_s + 64 * g), al1 = lds_u4(act_s + 64 * g + 16);
+        const uint4 ah0 = lds_u4(act_s + 64 * g + 32), ah1 = lds_u4(act_s + 64 * g + 48);
+        const uint32_t al[8] = {al0.x, al0.y, al0.z, al0.w, al1.x, al1.y, al1.z, al1.w};
+        const uint32_t ah[8] = {ah0.x, ah0.y, ah0.z, ah0.w, ah1.x, ah1.y, ah1.z, ah1.w};
+        int dlo = 0, dhi = 0;
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            dlo = dp4a((int)r.lo[8 * g + i], (int)al[i], dlo);
+            dhi = dp4a_us(r.hi[8 * g + i], (int)ah[i], dhi);
+        }
+        dot[2 * g] = dlo;
+        dot[2 * g + 1] = dhi >> 4;
+    }
+    const uint4 b0 = lds_u4(act_s + ACT_BS32), b1 = lds_u4(act_s + ACT_BS32 + 16);
+    const int bs[8] = {(int)b0.x, (int)b0.y, (int)b0.z, (int)b0.w, (int)b1.x, (int)b1.y, (int)b1.z, (int)b1.w};
+    int sumi = 0, summ = 0;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        sumi += r.sc[j] * dot[j];
+        summ += r.mn[j] * bs[j];
+    }
+    const float da = lds_f32(act_s + ACT_D);
+    const float t1 = __fmul_rn(r.dw, da);
+    const float t2 = __fmul_rn(__int2float_rn(sumi), t1);
+    const float t3 = __fmul_rn(r.dminw, da);
+    const float t4 = __fmul_rn(__int2float_rn(summ), t3);
+    return __fsub_rn(t2, t4);
+}
+
+struct Q6Reg {
+    uint32_t u[64];  // [n][hf][i][q]: the 6-bit values q + 32 of sub-blocks 8n + 2q + hf, bytes 4i..4i+3
+    int sc[16];
+    float dw;
+};
+__device__ __forceinline__ void q6k_load_r(Q6Reg &r, uint32_t tile_s, int S, int s) {
+    const uint32_t base = tile_s + (uint32_t)s * 16u, cstride = (uint32_t)S * 16u;
+    r.dw = __half2float(__ushort_as_half(lds_u16(tile_s + 13u * cstride + 2u * (uint32_t)s)));
+    const uint4 scv = lds_u4(base + 12u * cstride);
+    const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+#pragma unroll
+    for (int j = 0; j < 16; j++) r.sc[j] = byte_s(scw[j >> 2], j & 3);
+#pragma unroll
+    for (int n = 0; n < 2; n++) {
+        const uint4 qa0 = lds_u4(base + (4 * n + 0) * cstride), qa1 = lds_u4(base + (4 * n + 1) * cstride);
+        const uint4 qb0 = lds_u4(base + (4 * n + 2) * cstride), qb1 = lds_u4(base + (4 * n + 3) * cstride);
+        const uint4 hh0 = lds_u4(base + (8 + 2 * n) * cstride), hh1 = lds_u4(base + (9 + 2 * n) * cstride);
+        const uint32_t wa[8] = {qa0.x, qa0.y, qa0.z, qa0.w, qa1.x, qa1.y, qa1.z, qa1.w};
+        const uint32_t wb[8] = {qb0.x, qb0.y, qb0.z, qb0.w, qb1.x, qb1.y, qb1.z, qb1.w};
+        const uint32_t wh[8] = {hh0.x, hh0.y, hh0.z, hh0.w, hh1.x, hh1.y, hh1.z, hh1.w};
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++)
+#pragma unroll
+            for (int i = 0; i < 4; i++) {
+                const int l4 = 4 * hf + i;
+                const uint32_t hq = wh[l4];
+                uint32_t *u = r.u + ((n * 2 + hf) * 4 + i) * 4;
+                u[0] = (wa[l4] & 0x0F0F0F0Fu) | ((hq << 4) & 0x30303030u);
+                u[1] = (wb[l4] & 0x0F0F0F0Fu) | ((hq << 2) & 0x30303030u);
+                u[2] = ((wa[l4] >> 4) & 0x0F0F0F0Fu) | (hq & 0x30303030u);
+                u[3] = ((wb[l4] >> 4) & 0x0F0F0F0Fu) | ((hq >> 2) & 0x30303030u);
+            }
+    }
+}
+__device__ __forceinline__ float q6k_dot_r(const Q6Reg &r, uint32_t act_s) {
+    const uint4 bq0 = lds_u4(act_s + ACT_BS16), bq1 = lds_u4(act_s + ACT_BS16 + 16);
+    const uint32_t bsw[8] = {bq0.x, bq0.y, bq0.z, bq0.w, bq1.x, bq1.y, bq1.z, bq1.w};
+    int sumi = 0;
+#pragma unroll
+    for (int n = 0; n < 2; n++)
+#pragma unroll
+        for (int hf = 0; hf < 2; hf++) {
+            const uint4 A0 = lds_u4(act_s + 16 * (8 * n + 0 + hf)), A1 = lds_u4(act_s + 16 * (8 * n + 2 + hf));
+            const uint4 A2 = lds_u4(act_s + 16 * (8 * n + 4 + hf)), A3 = lds_u4(act_s + 16 * (8 * n + 6 + hf));
+            const uint32_t a[4][4] = {{A0.x, A0.y, A0.z, A0.w}, {A1.x, A1.y, A1.z, A1.w}, {A2.x, A2.y, A2.z, A2.w},
+                                      {A3.x, A3.y, A3.z, A3.w}};
+            int acc[4] = {0, 0, 0, 0};
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int q = 0; q < 4; q++) acc[q] = dp4a_us(r.u[((n * 2 + hf) * 4 + i) * 4 + q], (int)a[q][i], acc[q]);
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+                const int sub = 8 * n + 2 * q + hf;
+                const int bs = (int)(int16_t)((bsw[sub >> 1] >> (16 * (sub & 1))) & 0xffffu);
+                sumi += r.sc[sub] * (acc[q] - 32 * bs);
+            }
+        }
+    return __fmul_rn(__int2float_rn(sumi), __fmul_rn(r.dw, lds_f32(act_s + ACT_D)));
+}
+
 // The same dots on generic pointers into shared memory.
 __device__ __forceinline__ float q4k_slot_dot(const uint8_t *tile, int S, int s, const ActBlock &a) {
     return q4k_dot_s((uint32_t)__cvta_generic_to_shared(tile), S, s, (uint32_t)__cvta_generic_to_shared(&a));

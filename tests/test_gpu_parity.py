@@ -355,3 +355,39 @@ def test_long_context_batched_step_matches_oracle(tiny_cfg, tiny_weights, persis
         compare_kv(cache, model, cfg, seq=s)
     cache.close()
     e.close()
+
+
+@pytest.mark.parametrize("n_head", [4, 12, 16])  # GQA groups of 2, 6 and 8 query heads
+def test_batched_step_gqa_groups_match_oracle(n_head):
+    """A batched single-token step (per-phase attention, grouped experts) for each group size the
+    attention kernel is built for: paired heads (2, 8 per kv head -> 1, 4 per thread) and the
+    one-head-at-a-time path (6 -> 3 per thread)."""
+    cfg = bt.config("tiny", n_head=n_head, max_positions=2048)
+    W = bt.synth_model(cfg, seed=5)
+    e = bt.Engine(cfg, W)
+    rng = np.random.default_rng(n_head)
+    ctxs = [int(c) for c in rng.integers(50, 700, 10)]
+    kw = cfg.n_head_kv * cfg.head_dim
+    cache = bt.KvCache(e, max_positions=2048, max_seqs=len(ctxs))
+    kv = []
+    for s_, n in enumerate(ctxs):
+        layers = []
+        for il in range(cfg.n_layer):
+            k = (0.5 * rng.standard_normal(n * kw)).astype(np.float16)
+            v = rng.standard_normal(n * kw).astype(np.float16)
+            cache.restore_layer(il, k, v, seq=s_)
+            layers.append((k, v))
+        cache.set_positions(n, s_)
+        kv.append(layers)
+    toks = [int(t) for t in rng.integers(0, cfg.n_vocab, len(ctxs))]
+    got = bt.StreamingRunner(e).forward_batch(cache, list(range(len(ctxs))), [[t] for t in toks], ctxs)
+    for s_, n in enumerate(ctxs):
+        model = orc.Model(cfg, W)
+        for il in range(cfg.n_layer):
+            model.write_kv_layer(il, kv[s_][il][0], kv[s_][il][1])
+        model.set_len(n)
+        assert_logits(got[s_], model.forward([toks[s_]], n))
+        compare_kv(cache, model, cfg, seq=s_)
+    cache.close()
+    e.close()
+
