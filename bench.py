@@ -11,8 +11,9 @@ of uniform-random token ids into the f16 paged KV cache. A step = one decode tok
   roofline   the expert FFN (gate/up + down kernels) against the measured HBM copy peak
   cpu_baseline  the CPU oracle decoding from the same weights and cache on the host cores
   expert_cache  experts moved to pinned host memory behind a 6.26 GiB HBM cache (the cfg4
-             ratio), batch-1 decode of seeded uniform token ids with the router bias; LRU and
-             frequency-gated admission each from a cold cache: tok/s and hit rate
+             ratio), a fresh sequence: 128-token prefill then 128 batch-1 decode steps of
+             seeded uniform ids with the router bias; LRU and frequency-gated admission, each
+             from a cold cache: decode tok/s and hit rate
   batched    64 concurrent sequences, contexts seeded uniform in [512, 16384], paged f16 KV
              with seeded contents, a log-Zipf(1.1) router bias per layer (expert popularity
              over a seeded rank permutation); device tok/s of K graph-replayed steps
@@ -323,20 +324,30 @@ def run_ours(args, rank, world, local_rank):
                   "experts_bytes": int(cfg.n_layer * cfg.n_expert * expert_bytes(cfg, per_expert=True)),
                   "routing": f"log-Zipf({args.zipf}) router bias per layer" if args.zipf > 0 else "unbiased"}
         try:
+            rngx = np.random.default_rng(args.seed + 3)
+            prompt_x = rngx.integers(0, cfg.n_vocab, args.xcache_prompt)
+            toks_x = rngx.integers(0, cfg.n_vocab, args.xcache_steps)
             for policy in ("lru", "freq"):
                 engine.enable_expert_cache(xcache["cache_bytes"], policy)
-                toks_x = np.random.default_rng(args.seed + 3).integers(0, cfg.n_vocab, args.xcache_steps)
+                cache_x = bt.KvCache(engine, max_positions=args.xcache_prompt + args.xcache_steps + 8)
+                runner.forward_cached(cache_x, prompt_x, 0)  # prefill: warms the cache
+                st0 = engine.expert_cache_stats()
                 t0 = time.perf_counter()
-                for tk in toks_x:  # one token a step, seeded uniform ids: the routing keeps moving
-                    runner.forward_cached(cache, [int(tk)], cache.len())
+                for tk in toks_x:  # one token a step, seeded uniform ids
+                    runner.forward_cached(cache_x, [int(tk)], cache_x.len())
                 wall = time.perf_counter() - t0
                 st = engine.expert_cache_stats()
-                xcache[policy] = {"tok_s": round(args.xcache_steps / wall, 2), "hit_rate": round(st["hit_rate"], 4),
-                                  "evictions": st["evictions"], "bypasses": st["bypasses"],
-                                  "gb_copied": round(st["bytes_copied"] / 1e9, 2), "wall_s": round(wall, 2)}
+                cache_x.close()
+                d = {k: st[k] - st0[k] for k in ("hits", "misses", "evictions", "bypasses", "bytes_copied")}
+                xcache[policy] = {"tok_s": round(args.xcache_steps / wall, 2),
+                                  "hit_rate": round(d["hits"] / max(d["hits"] + d["misses"], 1), 4),
+                                  "evictions": d["evictions"], "bypasses": d["bypasses"],
+                                  "gb_copied": round(d["bytes_copied"] / 1e9, 2), "wall_s": round(wall, 2),
+                                  "prefill_hit_rate": round(st0["hit_rate"], 4)}
                 xcache["slots"] = st["capacity_slots"]
-            xcache["timing"] = ("wall clock of bt_forward per token (host token in, logits out, one host "
-                                "round trip per layer for the cache decisions)")
+            xcache["timing"] = (f"decode steps after a {args.xcache_prompt}-token prefill of seeded uniform ids: "
+                                "wall clock of bt_forward per token (host token in, logits out, one host round "
+                                "trip per layer for the cache decisions); hit rate over the decode steps")
         except bt.BtError as err:  # e.g. pinned host memory refused
             xcache["unavailable"] = str(err)
     if result is not None:
@@ -433,6 +444,7 @@ def main():
                     help="HBM expert-cache size of the out-of-HBM leg (0 skips it); the default keeps the "
                          "cfg4 ratio of cache to experts (120 GB of ~311 GB)")
     ap.add_argument("--xcache-steps", type=int, default=128)
+    ap.add_argument("--xcache-prompt", type=int, default=128)
     ap.add_argument("--zipf", type=float, default=1.1, help="router-bias Zipf exponent of the batched workload "
                     "(0: unbiased)")
     args = ap.parse_args()
