@@ -525,7 +525,7 @@ __device__ __forceinline__ void head_norm_rope(float v[4], const float w[4], con
 // Each half of the CTA (128 threads, warps 4h .. 4h+3, named barrier 1 + h) runs one attention
 // item at a time with its own K/V tile buffer and scratch, so a CTA's first two items run
 // concurrently.
-constexpr int ATTN_SCRATCH = 10240;  // per half: q (D x G f32), p (CH x G f32), reductions, new k/v
+constexpr int ATTN_SCRATCH = 8192;  // per half: q (D x G f16), p (CH x G f32), reductions, new k/v
 static_assert(2 * ATTN_BUF + 2 * ATTN_SCRATCH <= STEP_REGION_BYTES, "attention tiles and scratch fit the region");
 
 __device__ __forceinline__ void half_sync(int h) { asm volatile("bar.sync %0, 128;" ::"r"(1 + h) : "memory"); }
@@ -605,8 +605,8 @@ __device__ bool attn_half(const StepArgs &p, const LayerDev &L, const StepSmem &
     };
     uint8_t *K0 = sm.region + hf * ATTN_BUF, *K1 = K0 + 16384, *V0 = K0 + 32768, *V1 = K0 + 49152;
     uint8_t *scr = sm.region + 2 * ATTN_BUF + hf * ATTN_SCRATCH;
-    float *qs = reinterpret_cast<float *>(scr);                 // [D][G] q rounded to f16, as f32
-    float *ps = reinterpret_cast<float *>(scr + D * G * 4);     // [CH][G]
+    uint16_t *qs = reinterpret_cast<uint16_t *>(scr);           // [D][G] f16 bits
+    float *ps = reinterpret_cast<float *>(scr + D * G * 2);     // [CH][G]
     float *red = ps + CH * G;                                   // [4][8]
     float *red2 = red + 32;                                     // [4][8]
     float *s_m = red2 + 32, *s_l = s_m + 8;
@@ -634,7 +634,7 @@ __device__ bool attn_half(const StepArgs &p, const LayerDev &L, const StepSmem &
             }
             head_norm_rope(v, wn, cs, p.eps);
 #pragma unroll
-            for (int i = 0; i < 4; i++) qs[(lane + 32 * i) * G + u] = __half2float(__float2half_rn(v[i]));
+            for (int i = 0; i < 4; i++) qs[(lane + 32 * i) * G + u] = __half_as_ushort(__float2half_rn(v[i]));
         } else {
             // KvCache::push of this token's head g: k normed and roped, v as is, both to f16
             float vv[4];
@@ -682,36 +682,28 @@ __device__ bool attn_half(const StepArgs &p, const LayerDev &L, const StepSmem &
     const int k = tid;
     const bool valid = k < cnt;
     float sc[G];
-    {
-        // heads in pairs: (sc[2j], sc[2j+1]) += (q[d][2j], q[d][2j+1]) * (k[d], k[d]) as one paired
-        // fma, d in order (C8: each half an fmaf of two f16 values)
-        f32x2 acc[G / 2];
 #pragma unroll
-        for (int j = 0; j < G / 2; j++) acc[j] = 0ull;
+    for (int h = 0; h < G; h++) sc[h] = 0.0f;
+    {
         const uint8_t *krow = K0 + k * 128;
         const int ksw = k & 7;
+        const uint32_t *qw = reinterpret_cast<const uint32_t *>(qs);
 #pragma unroll 2
         for (int c16 = 0; c16 < 16; c16++) {
             const uint4 w = *reinterpret_cast<const uint4 *>((c16 < 8 ? krow : krow + 16384) + (((c16 & 7) ^ ksw) << 4));
             const uint32_t kw[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
-            for (int e2 = 0; e2 < 4; e2++) {
-                const float2 kf = h2f2_fma(kw[e2]);
+            for (int e = 0; e < 8; e++) {
+                uint32_t q[QWORDS];
+                ldw_n<QWORDS>(q, qw + (c16 * 8 + e) * QWORDS);
 #pragma unroll
-                for (int hl = 0; hl < 2; hl++) {
-                    const int d = c16 * 8 + 2 * e2 + hl;
-                    const f32x2 kk = hl ? pk2(kf.y, kf.y) : pk2(kf.x, kf.x);
-                    const f32x2 *qd = reinterpret_cast<const f32x2 *>(qs + d * G);
-#pragma unroll
-                    for (int j = 0; j < G / 2; j++) acc[j] = ffma2(qd[j], kk, acc[j]);
+                for (int j = 0; j < QWORDS; j++) {
+                    if (e & 1)
+                        fma_qk<true>(q[j], kw[e >> 1], sc[2 * j], sc[2 * j + 1]);
+                    else
+                        fma_qk<false>(q[j], kw[e >> 1], sc[2 * j], sc[2 * j + 1]);
                 }
             }
-        }
-#pragma unroll
-        for (int j = 0; j < G / 2; j++) {
-            const float2 v = upk2(acc[j]);
-            sc[2 * j] = v.x;
-            sc[2 * j + 1] = v.y;
         }
     }
     const float NEG_INF = -__int_as_float(0x7f800000);
@@ -754,17 +746,9 @@ __device__ bool attn_half(const StepArgs &p, const LayerDev &L, const StepSmem &
     // ---- P*V: thread = dims 2dp, 2dp+1 and heads hq*HPT .. +HPT
     const int dp = tid & 63, hq = tid >> 6;
     float acc0[HPT], acc1[HPT];
+#pragma unroll
+    for (int h = 0; h < HPT; h++) acc0[h] = acc1[h] = 0.0f;
     {
-        // heads in pairs: (acc[d][h], acc[d][h+1]) += (p[h], p[h+1]) * (v[d], v[d]), keys in order
-        // (C8); one head at a time when a thread has an odd number of heads
-        constexpr bool PAIRS = HPT % 2 == 0;
-        constexpr int NP = PAIRS ? HPT / 2 : 1;
-        f32x2 a0[NP], a1[NP];
-        float s0[HPT], s1[HPT];
-#pragma unroll
-        for (int j = 0; j < NP; j++) a0[j] = a1[j] = 0ull;
-#pragma unroll
-        for (int h = 0; h < HPT; h++) s0[h] = s1[h] = 0.0f;
         const int d = 2 * dp, cc = (d & 63) >> 3;
         const uint8_t *vcol = ((d < 64) ? V0 : V1) + (d & 7) * 2;
         int off[8];
@@ -778,40 +762,14 @@ __device__ bool attn_half(const StepArgs &p, const LayerDev &L, const StepSmem &
             for (int kk = 0; kk < 8; kk++) {
                 if (j0 + kk < cnt) {
                     const float2 vf = h2f2_fma(*reinterpret_cast<const uint32_t *>(vb + off[kk]));
-                    if constexpr (PAIRS) {
-                        const f32x2 *pp = reinterpret_cast<const f32x2 *>(pb + kk * G);
-                        const f32x2 vx = pk2(vf.x, vf.x), vy = pk2(vf.y, vf.y);
+                    float pj[HPT];
+                    lds_n<HPT>(pj, pb + kk * G);
 #pragma unroll
-                        for (int j = 0; j < NP; j++) {
-                            const f32x2 pj = pp[j];
-                            a0[j] = ffma2(pj, vx, a0[j]);
-                            a1[j] = ffma2(pj, vy, a1[j]);
-                        }
-                    } else {
-#pragma unroll
-                        for (int h = 0; h < HPT; h++) {
-                            const float pj = pb[kk * G + h];
-                            s0[h] = fmaf(pj, vf.x, s0[h]);
-                            s1[h] = fmaf(pj, vf.y, s1[h]);
-                        }
+                    for (int h = 0; h < HPT; h++) {
+                        acc0[h] = fmaf(pj[h], vf.x, acc0[h]);
+                        acc1[h] = fmaf(pj[h], vf.y, acc1[h]);
                     }
                 }
-            }
-        }
-        if constexpr (PAIRS) {
-#pragma unroll
-            for (int j = 0; j < NP; j++) {
-                const float2 x = upk2(a0[j]), y = upk2(a1[j]);
-                acc0[2 * j] = x.x;
-                acc0[2 * j + 1] = x.y;
-                acc1[2 * j] = y.x;
-                acc1[2 * j + 1] = y.y;
-            }
-        } else {
-#pragma unroll
-            for (int h = 0; h < HPT; h++) {
-                acc0[h] = s0[h];
-                acc1[h] = s1[h];
             }
         }
     }
