@@ -49,6 +49,14 @@ QWEN3_30B = dict(n_embd=2048, n_head=32, n_head_kv=4, head_dim=128, n_expert=128
                  n_vocab=151936)
 
 
+def shape_name(cfg):
+    if cfg.name in ("cfg0", "cfg1"):
+        return f"Qwen3-30B-A3B shape, {cfg.n_layer} layers" + (", Q4_K_M stand-in" if cfg.name == "cfg1" else ", Q4_K")
+    return (f"{cfg.n_layer} layers, hidden {cfg.n_embd}, {cfg.n_head}/{cfg.n_head_kv} heads, {cfg.n_expert} experts "
+            f"top-{cfg.n_expert_used}" + (f" + a shared expert of {cfg.n_ff_shexp}" if cfg.n_ff_shexp else "")
+            + f", expert width {cfg.n_ff_exp}, vocab {cfg.n_vocab}")
+
+
 def peaks():
     p = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(p):
@@ -293,7 +301,7 @@ def run_ours(args, rank, world, local_rank):
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q4_K/q6_K weights, int8 dot, f32 accumulate",
             "data": "synthetic (seeded N(0,0.02) weights, uniform-random token ids)",
-            "config": {"workload": f"{args.config}: Qwen3-30B-A3B shape, {cfg.n_layer} layers, Q4_K_M stand-in, "
+            "config": {"workload": f"{args.config}: {shape_name(cfg)}, "
                                    f"batch 1 greedy decode after a {args.ctx}-token "
                                    + ("prefill" if args.fill == "prefill" else "seeded cache fill"),
                        "batch": 1, "context": args.ctx, "parallelism": "replicas" if world > 1 else "single GPU",
@@ -394,7 +402,7 @@ def run_reference(args, rank, world):
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "q4_K/q6_K weights, int8 dot, f32 accumulate", "data": "synthetic",
-        "config": {"workload": f"{args.config}: Qwen3-30B-A3B shape, 48 layers, Q4_K_M stand-in, batch 1 greedy "
+        "config": {"workload": f"{args.config}: {shape_name(cfg)}, batch 1 greedy "
                                f"decode at context {args.ctx}", "batch": 1, "context": args.ctx},
         "cpu_baseline": {"value": round(tps, 3), "unit": "tok/s", "cores": threads, "kind": "port",
                          "sample": f"{args.steps} decode tokens at context {args.ctx} (seeded f16 cache)"},

@@ -17,7 +17,7 @@ STATUS_NAMES = {
 }
 TYPE_F32, TYPE_F16, TYPE_Q4_K, TYPE_Q6_K = 0, 1, 12, 14
 KV_F16 = 1
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 class BtError(RuntimeError):
@@ -32,7 +32,7 @@ class ModelDesc(C.Structure):
         ("head_dim", C.c_uint32), ("n_expert", C.c_uint32), ("n_expert_used", C.c_uint32),
         ("n_ff_exp", C.c_uint32), ("n_vocab", C.c_uint32), ("n_rot", C.c_uint32),
         ("rms_eps", C.c_float), ("rope_freq_base", C.c_float),
-        ("expert_workers", C.c_uint32), ("max_positions", C.c_uint32),
+        ("expert_workers", C.c_uint32), ("max_positions", C.c_uint32), ("n_ff_shexp", C.c_uint32),
     ]
 
 

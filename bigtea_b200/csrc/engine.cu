@@ -89,6 +89,7 @@ struct Layer {
     DevBuf attn_norm, q_norm, k_norm, ffn_norm, gate_inp;
     DevBuf gate_bias;  // optional ffn_gate_inp.bias [n_expert], added to the router logits
     QMat q, k, v, o, gate, up, down;
+    QMat gate_sh, up_sh, down_sh;  // the shared expert, when the model has one (n_ff_shexp)
 };
 
 struct GraphKey {
@@ -117,6 +118,7 @@ struct bt_engine {
     DevBuf x, ffn_in, fn, qkv, qbuf, att, rlog, rcnt, sel_ids, sel_w, act, part, acnt;
     DevBuf g_count, g_off, g_list, g_active, g_nactive, dpart;  // grouped experts of batched steps
     DevBuf g_chunk_e, g_chunk_r0, g_nchunks;
+    DevBuf sh_gu, sh_act, sh_out;  // the shared expert: [TB][2F] gate|up, [TB][F] silu*up, [TB][E] rows
     // expert parallelism (bt_engine_enable_ep): this rank computes experts [rank*NE/n, (rank+1)*NE/n)
     bool ep = false;
     int ep_rank = 0, ep_n = 1;
@@ -329,8 +331,8 @@ static int validate_desc(const bt_model_desc *d) {
     if (d->n_expert_used > (uint32_t)MAX_K || d->n_expert_used > d->n_expert)
         return fail(BT_ERR_UNSUPPORTED, "n_expert_used must be at most 16 and at most n_expert");
     if (d->n_expert > 512) return fail(BT_ERR_UNSUPPORTED, "n_expert must be at most 512");
-    if (d->n_embd % 256 || d->n_ff_exp % 256 || (d->n_head * d->head_dim) % 256)
-        return fail(BT_ERR_UNSUPPORTED, "n_embd, n_ff_exp and n_head*head_dim must be multiples of 256");
+    if (d->n_embd % 256 || d->n_ff_exp % 256 || (d->n_head * d->head_dim) % 256 || d->n_ff_shexp % 256)
+        return fail(BT_ERR_UNSUPPORTED, "n_embd, n_ff_exp, n_ff_shexp and n_head*head_dim must be multiples of 256");
     return BT_OK;
 }
 
@@ -443,6 +445,11 @@ static int alloc_scratch(bt_engine *e) {
     CK(e->g_chunk_e.alloc((size_t)group_max_chunks(TB * K, NE) * 4));
     CK(e->g_chunk_r0.alloc((size_t)group_max_chunks(TB * K, NE) * 4));
     CK(e->dpart.alloc((size_t)TB * K * E * 4));
+    if (d.n_ff_shexp) {
+        CK(e->sh_gu.alloc((size_t)TB * 2 * d.n_ff_shexp * 4));
+        CK(e->sh_act.alloc((size_t)TB * d.n_ff_shexp * 4));
+        CK(e->sh_out.alloc((size_t)TB * E * 4));
+    }
     CK(cudaMemset(e->acnt.p, 0, (size_t)TB * d.n_head_kv * 4));
     CK(e->dbg_ids.alloc((size_t)d.n_layer * TB * K * 4));
     CK(e->dbg_w.alloc((size_t)d.n_layer * TB * K * 4));
@@ -625,6 +632,12 @@ static int build_engine(bt_engine *e, const std::map<std::string, SrcTensor> &sr
         if ((r = mat("ffn_gate_exps.weight", l.gate, E, F, NE, default_rpt(E)))) return r;
         if ((r = mat("ffn_up_exps.weight", l.up, E, F, NE, default_rpt(E)))) return r;
         if ((r = mat("ffn_down_exps.weight", l.down, F, E, NE, 1))) return r;
+        if (d.n_ff_shexp) {
+            const uint64_t FS = d.n_ff_shexp;
+            if ((r = mat("ffn_gate_shexp.weight", l.gate_sh, E, FS, 1, default_rpt(E)))) return r;
+            if ((r = mat("ffn_up_shexp.weight", l.up_sh, E, FS, 1, default_rpt(E)))) return r;
+            if ((r = mat("ffn_down_shexp.weight", l.down_sh, FS, E, 1, default_rpt(FS)))) return r;
+        }
         if (l.gate.g.tile_bytes != l.up.g.tile_bytes && l.gate.type == l.up.type)
             return fail(BT_ERR_INVALID, "gate and up experts disagree in shape");
     }
@@ -735,6 +748,12 @@ extern "C" int bt_engine_create_synthetic(const bt_model_desc *desc, const uint3
         if ((r = gen(p + "ffn_gate_exps.weight", (int)ty[4], {E, F, NE}))) return r;
         if ((r = gen(p + "ffn_up_exps.weight", (int)ty[5], {E, F, NE}))) return r;
         if ((r = gen(p + "ffn_down_exps.weight", (int)ty[6], {F, E, NE}))) return r;
+        if (d.n_ff_shexp) {  // the shared expert in the routed experts' types
+            const uint64_t FS = d.n_ff_shexp;
+            if ((r = gen(p + "ffn_gate_shexp.weight", (int)ty[4], {E, FS}))) return r;
+            if ((r = gen(p + "ffn_up_shexp.weight", (int)ty[5], {E, FS}))) return r;
+            if ((r = gen(p + "ffn_down_shexp.weight", (int)ty[6], {FS, E}))) return r;
+        }
         // ingest this layer right away so the raw copies do not pile up
         if (il == 0) continue;
     }
@@ -1146,7 +1165,7 @@ static int upload_plan(bt_engine *e, const StepPlan &p) {
 // Can this step run as one persistent kernel? Single-token steps of up to STEP_MAX_T
 // sequences whose activations fit the kernel's shared memory.
 static bool step_eligible(const bt_engine *e, const bt_kv *kv, const StepPlan &p) {
-    if (!e->mega || e->ep || e->xcache || p.T > STEP_MAX_T || p.out_first != 0 || (int)p.x_rows.size() != p.T) return false;
+    if (!e->mega || e->ep || e->xcache || e->d.n_ff_shexp || p.T > STEP_MAX_T || p.out_first != 0 || (int)p.x_rows.size() != p.T) return false;
     for (int t = 0; t < p.T; t++)
         if (!p.single[t] || p.local_idx[t] != 0 || p.x_rows[t] != t || p.st_lrow[t] != t) return false;
     if ((int)p.st_seq.size() != p.T) return false;
@@ -1425,6 +1444,31 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             if (xr) return xr;
         }
         const int *x_slot = e->xcache ? e->x_slot_dev.as<int>() + (size_t)il * NE : nullptr;
+        const float *shexp = nullptr;
+        if (d.n_ff_shexp) {  // the shared expert on every token: gate|up GEMV, silu*up, down GEMV
+            const int FS = (int)d.n_ff_shexp;
+            const int ch = gemv_chunk(T, E, l.gate_sh.g.tile_bytes > l.up_sh.g.tile_bytes ? l.gate_sh.g.tile_bytes
+                                                                                          : l.up_sh.g.tile_bytes);
+            for (int t0 = 0; t0 < T; t0 += ch) {
+                const int tg = T - t0 < ch ? T - t0 : ch;
+                const QMat *mats[2] = {&l.gate_sh, &l.up_sh};
+                int offs[2] = {0, FS};
+                CK(run_gemv(e, mats, offs, 2, e->fn.as<float>() + (size_t)t0 * E, E, nullptr, nullptr, E, tg,
+                            e->sh_gu.as<float>() + (size_t)t0 * 2 * FS, 2 * FS, nullptr, 0, "shexp_gateup_gemv"));
+            }
+            timer_begin(e, "shexp_act");
+            CK(launch_shexp_act(e->sh_gu.as<float>(), e->sh_act.as<float>(), T, FS, st, pdl));
+            timer_end(e);
+            const int chd = gemv_chunk(T, FS, l.down_sh.g.tile_bytes);
+            for (int t0 = 0; t0 < T; t0 += chd) {
+                const int tg = T - t0 < chd ? T - t0 : chd;
+                const QMat *mats[1] = {&l.down_sh};
+                int offs[1] = {0};
+                CK(run_gemv(e, mats, offs, 1, e->sh_act.as<float>() + (size_t)t0 * FS, FS, nullptr, nullptr, FS, tg,
+                            e->sh_out.as<float>() + (size_t)t0 * E, E, nullptr, 0, "shexp_down_gemv"));
+            }
+            shexp = e->sh_out.as<float>();
+        }
         if (e->ep) {  // expert parallelism: rows to the owning ranks, experts there, rows back
             const int S = e->TB * K, n = e->ep_n, per = NE / n;
             const NcclApi *api = nccl_api();
@@ -1535,6 +1579,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.ep_ranks = n;
             a.ep_per = per;
             a.ep_slots = S;
+            a.shexp = shexp;
             timer_begin(e, "expert_combine");
             CK(launch_down_combine(a, st, false));
             timer_end(e);
@@ -1599,6 +1644,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.slot_of = x_slot;
             a.pool = e->x_pool.as<uint8_t>();
             a.slot_stride = e->x_stride;
+            a.shexp = shexp;
             const size_t cap = (size_t)max_dynamic_smem();
             a.slot_bytes = a.g_tile_bytes + a.u_tile_bytes;
             a.nst = 1;
@@ -1652,6 +1698,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.slot_of = x_slot;
             a.pool = e->x_pool.as<uint8_t>();
             a.slot_stride = e->x_stride;
+            a.shexp = shexp ? shexp + (size_t)t0 * E : nullptr;
             if (e->prefetch && t0 == 0 && il + 1 < d.n_layer) {  // the next layer's q/k/v weights
                 const Layer &n = e->L[il + 1];
                 a.pf.ptr[0] = n.q.buf.p;
@@ -2405,6 +2452,9 @@ extern "C" int bt_engine_tensor_bytes(const bt_engine *ec, const char *name, voi
         else if (s == "ffn_gate_exps.weight") m = &l.gate;
         else if (s == "ffn_up_exps.weight") m = &l.up;
         else if (s == "ffn_down_exps.weight") m = &l.down;
+        else if (s == "ffn_gate_shexp.weight" && e->d.n_ff_shexp) m = &l.gate_sh;
+        else if (s == "ffn_up_shexp.weight" && e->d.n_ff_shexp) m = &l.up_sh;
+        else if (s == "ffn_down_shexp.weight" && e->d.n_ff_shexp) m = &l.down_sh;
         else if (s == "attn_norm.weight") f = &l.attn_norm;
         else if (s == "attn_q_norm.weight") f = &l.q_norm;
         else if (s == "attn_k_norm.weight") f = &l.k_norm;

@@ -531,7 +531,8 @@ __global__ void __launch_bounds__(NWARP * 32, 1) down_kernel(const __grid_consta
             } else {
                 for (int i = 0; i < p.K; i++) sum = __fadd_rn(sum, __fmul_rn(o[i], w[i]));
             }
-            p.x_out[(long long)t * p.E + row] = __fadd_rn(p.ffn_in[(long long)t * p.E + row], sum);
+            const long long xi = (long long)t * p.E + row;
+            p.x_out[xi] = p.shexp ? __fadd_rn(__fadd_rn(sum, p.shexp[xi]), p.ffn_in[xi]) : __fadd_rn(p.ffn_in[xi], sum);
         }
         __syncwarp();
         if (lane == 0 && j + p.nst < nmine) {
@@ -886,7 +887,8 @@ __global__ void __launch_bounds__(256) down_combine_kernel(const __grid_constant
         } else {
             for (int i = 0; i < p.K; i++) sum = __fadd_rn(sum, __fmul_rn(o[i], w[i]));
         }
-        p.x_out[(long long)t * p.E + row] = __fadd_rn(p.ffn_in[(long long)t * p.E + row], sum);
+        const long long xi = (long long)t * p.E + row;
+        p.x_out[xi] = p.shexp ? __fadd_rn(__fadd_rn(sum, p.shexp[xi]), p.ffn_in[xi]) : __fadd_rn(p.ffn_in[xi], sum);
     }
     pdl_trigger();
 }
@@ -905,6 +907,32 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __grid_constant__ Ep
         for (int i = threadIdx.x; i < p.E; i += blockDim.x) dst[i] = src[i];
     }
     pdl_trigger();
+}
+
+__global__ void __launch_bounds__(256) shexp_act_kernel(const float *__restrict__ gu, float *__restrict__ act, int T,
+                                                        int F) {
+    pdl_wait();
+    const long long n = (long long)T * F;
+    for (long long i = blockIdx.x * 256ll + threadIdx.x; i < n; i += (long long)gridDim.x * 256) {
+        const long long t = i / F, j = i - t * F;
+        act[i] = __fmul_rn(bt_silu(gu[t * 2 * F + j]), gu[t * 2 * F + F + j]);
+    }
+    pdl_trigger();
+}
+
+cudaError_t launch_shexp_act(const float *gu, float *act, int T, int F, cudaStream_t st, bool pdl) {
+    const long long n = (long long)T * F;
+    const int grid = (int)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, shexp_act_kernel, gu, act, T, F);
 }
 
 cudaError_t launch_ep_pack(const EpPackArgs &a, cudaStream_t st, bool pdl) {

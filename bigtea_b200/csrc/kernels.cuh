@@ -87,6 +87,8 @@ struct ExpertArgs {
     const int *slot_of;
     const uint8_t *pool;
     long long slot_stride;
+    // the shared expert's output rows [T][E], added to the routed sum before the residual; or null
+    const float *shexp;
 };
 
 // the weights of expert e: its resident matrices, or its slot of the expert cache
@@ -209,6 +211,8 @@ cudaError_t launch_gateup_grouped(const ExpertArgs &a, int grid, cudaStream_t st
 cudaError_t launch_down_grouped(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
 cudaError_t launch_down_combine(const ExpertArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_ep_pack(const EpPackArgs &a, cudaStream_t st, bool pdl);
+// act[t][j] = silu(gu[t][j]) * gu[t][F + j] for the shared expert (C7)
+cudaError_t launch_shexp_act(const float *gu, float *act, int T, int F, cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl);
 size_t attn_smem_bytes(int G, int T);
 cudaError_t launch_attn(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl);

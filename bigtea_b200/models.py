@@ -48,6 +48,9 @@ class Qwen3MoeConfig:
     # > 0: each layer carries an F32 router bias ffn_gate_inp.bias = log-Zipf(router_zipf)
     # expert popularity over a seeded per-layer permutation of the expert ranks (zipf_router_bias)
     router_zipf: float = 0.0
+    # > 0: one shared expert of this width per layer (ffn_{gate,up,down}_shexp, the routed
+    # experts' types), added unweighted to the routed sum (DeepSeek-style models)
+    n_ff_shexp: int = 0
 
     def __post_init__(self):
         if not self.layer_types:
@@ -60,7 +63,8 @@ class Qwen3MoeConfig:
     def desc(self) -> _lib.ModelDesc:
         return _lib.ModelDesc(self.n_layer, self.n_embd, self.n_head, self.n_head_kv, self.head_dim,
                               self.n_expert, self.n_expert_used, self.n_ff_exp, self.n_vocab, self.n_rot,
-                              self.rms_eps, self.rope_freq_base, self.expert_workers, self.max_positions)
+                              self.rms_eps, self.rope_freq_base, self.expert_workers, self.max_positions,
+                              self.n_ff_shexp)
 
     def tensor_specs(self):
         """(name, ggml type, ggml dims innermost-first, mean) for every tensor."""
@@ -86,6 +90,11 @@ class Qwen3MoeConfig:
                     (p + "ffn_down_exps.weight", t[6], (F, E, NE), 0.0)]
             if self.router_zipf > 0:
                 out.append((p + "ffn_gate_inp.bias", TYPE_F32, (NE,), 0.0))
+            if self.n_ff_shexp:
+                FS = self.n_ff_shexp
+                out += [(p + "ffn_gate_shexp.weight", t[4], (E, FS), 0.0),
+                        (p + "ffn_up_shexp.weight", t[5], (E, FS), 0.0),
+                        (p + "ffn_down_shexp.weight", t[6], (FS, E), 0.0)]
         return out
 
     def weight_bytes(self) -> int:
@@ -118,7 +127,9 @@ class Qwen3MoeConfig:
                    rms_eps=float(a("attention.layer_norm_rms_epsilon", 1e-6)),
                    rope_freq_base=float(a("rope.freq_base", 10000.0)),
                    max_positions=max_positions, embd_type=t["token_embd.weight"].type, out_type=out.type,
-                   layer_types=types, name=r.arch())
+                   layer_types=types, name=r.arch(),
+                   n_ff_shexp=int(a("expert_shared_feed_forward_length", 0)) if "blk.0.ffn_gate_shexp.weight" in t else 0,
+                   router_zipf=0.0)
 
 
 def q4km_layer_types(n_layer: int):
@@ -146,6 +157,16 @@ CONFIGS = {
     # the full 48-layer Qwen3-30B-A3B shape, Q4_K_M stand-in
     "cfg1": Qwen3MoeConfig(n_layer=48, max_positions=8192 + 512, layer_types=q4km_layer_types(48),
                            name="cfg1", **QWEN3_30B_A3B),
+    # DeepSeek-style: 43 layers, hidden 4096, 32 heads / 8 KV heads, 256 routed experts top-6
+    # plus one shared expert, expert width 2048, vocab 129280; Q4_K experts, Q6_K attention
+    "cfg3": Qwen3MoeConfig(n_layer=43, n_embd=4096, n_head=32, n_head_kv=8, head_dim=128, n_expert=256,
+                           n_expert_used=6, n_ff_exp=2048, n_vocab=129280, n_ff_shexp=2048,
+                           max_positions=4096 + 512, layer_types=[[TYPE_Q6_K] * 4 + [TYPE_Q4_K] * 3] * 43,
+                           name="cfg3"),
+    # small shapes with a shared expert for parity tests
+    "tiny_sh": Qwen3MoeConfig(n_layer=2, n_embd=512, n_head=8, n_head_kv=2, head_dim=128, n_expert=16,
+                              n_expert_used=4, n_ff_exp=256, n_vocab=1000, max_positions=1024, n_ff_shexp=512,
+                              name="tiny_sh"),
 }
 
 
@@ -201,6 +222,8 @@ def write_gguf(path: str, cfg: Qwen3MoeConfig, tensors: dict) -> None:
                  ("expert_feed_forward_length", cfg.n_ff_exp), ("vocab_size", cfg.n_vocab),
                  ("context_length", cfg.max_positions)]:
         w.add(f"{arch}.{k}", int(v))
+    if cfg.n_ff_shexp:
+        w.add(f"{arch}.expert_shared_feed_forward_length", int(cfg.n_ff_shexp))
     w.add(f"{arch}.rope.freq_base", float(cfg.rope_freq_base))
     w.add(f"{arch}.attention.layer_norm_rms_epsilon", float(cfg.rms_eps))
     for name, (ty, ne, data) in tensors.items():

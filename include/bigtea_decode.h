@@ -19,7 +19,7 @@
 extern "C" {
 #endif
 
-#define BT_ABI_VERSION 1
+#define BT_ABI_VERSION 2
 
 typedef enum {
     BT_OK = 0,
@@ -47,6 +47,11 @@ typedef struct {
     uint32_t expert_workers;
     /* longest sequence the RoPE table covers (positions 0..max_positions-1) */
     uint32_t max_positions;
+    /* width of a shared expert (blk.N.ffn_{gate,up,down}_shexp), 0 = none. Not in the
+     * reference's qwen3moe tensor set: the DeepSeek-style workload has one, added unweighted
+     * to the routed sum before the residual, as llama.cpp's deepseek2 graph does:
+     * x = (moe + shexp(x_n)) + ffn_inp. */
+    uint32_t n_ff_shexp;
 } bt_model_desc;
 
 /* One GGUF tensor as Model::read_tensor returns it (core/model/src/lib.rs:390-470):

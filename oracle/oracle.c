@@ -501,6 +501,9 @@ typedef struct {
 typedef struct {
     tref attn_norm, q, k, v, q_norm, k_norm, o, ffn_norm, gate_inp, gate, up, down;
     tref gate_bias; /* optional ffn_gate_inp.bias: data NULL when absent */
+    /* optional shared expert (ffn_{gate,up,down}_shexp; data NULL when absent), added
+     * unweighted to the routed sum before the residual as llama.cpp's deepseek2 graph does */
+    tref gate_sh, up_sh, down_sh;
 } layer_w;
 
 struct or_model {
@@ -569,6 +572,17 @@ or_model *or_model_new(const or_config *cfg, const or_tensor *ts, int n) {
         GETW(gate_inp, "ffn_gate_inp.weight");
         snprintf(nm, sizeof nm, "blk.%d.ffn_gate_inp.bias", il);
         find_tensor(ts, n, nm, &m->L[il].gate_bias, 0);
+        snprintf(nm, sizeof nm, "blk.%d.ffn_gate_shexp.weight", il);
+        find_tensor(ts, n, nm, &m->L[il].gate_sh, 0);
+        snprintf(nm, sizeof nm, "blk.%d.ffn_up_shexp.weight", il);
+        find_tensor(ts, n, nm, &m->L[il].up_sh, 0);
+        snprintf(nm, sizeof nm, "blk.%d.ffn_down_shexp.weight", il);
+        find_tensor(ts, n, nm, &m->L[il].down_sh, 0);
+        if ((m->L[il].gate_sh.data != NULL) != (m->L[il].down_sh.data != NULL) ||
+            (m->L[il].gate_sh.data != NULL) != (m->L[il].up_sh.data != NULL)) {
+            set_err("a shared expert needs its gate, up and down tensors");
+            bad = 1;
+        }
         GETW(gate, "ffn_gate_exps.weight");
         GETW(up, "ffn_up_exps.weight");
         GETW(down, "ffn_down_exps.weight");
@@ -669,6 +683,12 @@ int or_forward(or_model *m, or_kv *kv, const int32_t *tokens, int T, int pos_sta
     float *eo = (float *)malloc(sizeof(float) * (size_t)K * E);
     float *sum = (float *)malloc(sizeof(float) * (size_t)E);
     float *tot = (float *)malloc(sizeof(float) * (size_t)E);
+    int FS = 0; /* the widest shared expert of the model */
+    for (int il = 0; il < c->n_layer; il++)
+        if (m->L[il].gate_sh.data && (int)m->L[il].gate_sh.ne[1] > FS) FS = (int)m->L[il].gate_sh.ne[1];
+    float *gsh = (float *)malloc(sizeof(float) * (size_t)(FS > 0 ? FS : 1));
+    float *ush = (float *)malloc(sizeof(float) * (size_t)(FS > 0 ? FS : 1));
+    float *sh = (float *)malloc(sizeof(float) * (size_t)E);
     int32_t ids[64];
     float wts[64];
 
@@ -773,7 +793,17 @@ int or_forward(or_model *m, or_kv *kv, const int32_t *tokens, int T, int pos_sta
                 for (int i = 0; i < K; i++)
                     for (int j = 0; j < E; j++) sum[j] = sum[j] + eo[(size_t)i * E + j];
             }
-            for (int j = 0; j < E; j++) x[(size_t)t * E + j] = fi[j] + sum[j];
+            if (w->gate_sh.data) {
+                /* shared expert: down(silu(gate x) * up x), then x = (moe + shexp) + ffn_inp */
+                const int fs = (int)w->gate_sh.ne[1];
+                or_gemv(w->gate_sh.type, w->gate_sh.data, fs, E, fn, gsh);
+                or_gemv(w->up_sh.type, w->up_sh.data, fs, E, fn, ush);
+                for (int j = 0; j < fs; j++) gsh[j] = or_silu(gsh[j]) * ush[j];
+                or_gemv(w->down_sh.type, w->down_sh.data, E, fs, gsh, sh);
+                for (int j = 0; j < E; j++) x[(size_t)t * E + j] = (sum[j] + sh[j]) + fi[j];
+            } else {
+                for (int j = 0; j < E; j++) x[(size_t)t * E + j] = fi[j] + sum[j];
+            }
         }
     }
     kv->len += T;
@@ -785,6 +815,7 @@ int or_forward(or_model *m, or_kv *kv, const int32_t *tokens, int T, int pos_sta
 
     free(x); free(xn); free(q); free(kk); free(vv); free(att); free(ao); free(ffin);
     free(rl); free(pr); free(g); free(u); free(o); free(eo); free(sum); free(tot);
+    free(gsh); free(ush); free(sh);
     return 0;
 }
 

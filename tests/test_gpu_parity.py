@@ -391,3 +391,50 @@ def test_batched_step_gqa_groups_match_oracle(n_head):
     cache.close()
     e.close()
 
+
+@pytest.mark.parametrize("source", ["tensors", "synthetic"])
+def test_shared_expert_matches_oracle(source):
+    """A model with a shared expert (DeepSeek-style, added unweighted to the routed sum): a
+    prefill, single-token steps, the greedy loop and a 12-sequence batched step (grouped
+    experts) give the oracle's bits."""
+    cfg = bt.config("tiny_sh", max_positions=1024)
+    W = bt.synth_model(cfg, seed=7)
+    e = bt.Engine(cfg, W) if source == "tensors" else bt.Engine.synthetic(cfg, seed=7)
+    model = orc.Model(cfg, W)
+    cache = bt.KvCache(e, max_positions=512)
+    runner = bt.StreamingRunner(e)
+    prompt = np.random.default_rng(33).integers(0, cfg.n_vocab, 19)
+    assert_logits(runner.forward_cached(cache, prompt, 0), model.forward(prompt, 0))
+    tok = 9
+    for _ in range(3):
+        assert_logits(runner.forward_cached(cache, [tok], cache.len()), model.forward([tok], model.len()))
+        tok = (tok * 17 + 2) % cfg.n_vocab
+    toks = runner.generate_greedy(cache, [tok], 4)
+    assert list(toks[:, 0]) == model.greedy(tok, 4)
+    compare_kv(cache, model, cfg)
+    cache.close()
+    rng = np.random.default_rng(34)
+    ctxs = [int(c) for c in rng.integers(20, 400, 12)]
+    kw = cfg.n_head_kv * cfg.head_dim
+    cache = bt.KvCache(e, max_positions=512, max_seqs=len(ctxs))
+    kv = []
+    for s_, n in enumerate(ctxs):
+        layers = []
+        for il in range(cfg.n_layer):
+            k = (0.5 * rng.standard_normal(n * kw)).astype(np.float16)
+            v = rng.standard_normal(n * kw).astype(np.float16)
+            cache.restore_layer(il, k, v, seq=s_)
+            layers.append((k, v))
+        cache.set_positions(n, s_)
+        kv.append(layers)
+    toks = [int(t) for t in rng.integers(0, cfg.n_vocab, len(ctxs))]
+    got = runner.forward_batch(cache, list(range(len(ctxs))), [[t] for t in toks], ctxs)
+    for s_, n in enumerate(ctxs):
+        m2 = orc.Model(cfg, W)
+        for il in range(cfg.n_layer):
+            m2.write_kv_layer(il, kv[s_][il][0], kv[s_][il][1])
+        m2.set_len(n)
+        assert_logits(got[s_], m2.forward([toks[s_]], n))
+    cache.close()
+    e.close()
+

@@ -314,6 +314,11 @@ def _f64_forward(cfg, W, tokens):
                 g_ = gw @ fn[t]
                 a = g_ / (1 + np.exp(-g_)) * (uw @ fn[t])
                 out[t] += we * (dw @ a)
+            if p + "ffn_gate_shexp.weight" in W:  # the shared expert, unweighted
+                FS = cfg.n_ff_shexp
+                g_ = deq(p + "ffn_gate_shexp.weight", FS, E) @ fn[t]
+                a = g_ / (1 + np.exp(-g_)) * (deq(p + "ffn_up_shexp.weight", FS, E) @ fn[t])
+                out[t] += deq(p + "ffn_down_shexp.weight", E, FS) @ a
         x = x + out
     xn = rms(x[-1], vec("output_norm.weight"))
     return xn @ deq("output.weight", cfg.n_vocab, E).T
@@ -345,6 +350,23 @@ def test_router_bias_forward_tracks_float64_restatement_and_skews_routing():
     top = int(np.argmax(b0))
     hits = sum(top in m.topk(0, t)[0] for t in range(len(tokens)))
     assert hits >= len(tokens) // 2, hits
+
+
+def test_shared_expert_forward_tracks_float64_restatement():
+    import bigtea_b200 as bt
+
+    cfg = bt.config("tiny_sh")
+    W = bt.synth_model(cfg, seed=7)
+    assert W["blk.1.ffn_down_shexp.weight"][1] == (cfg.n_ff_shexp, cfg.n_embd)
+    tokens = np.random.default_rng(12).integers(0, cfg.n_vocab, 10)
+    got = orc.Model(cfg, W).forward(tokens, 0).astype(np.float64)
+    want = _f64_forward(cfg, W, tokens)
+    assert np.linalg.norm(got - want) / np.linalg.norm(want) < 0.05
+    # and the shared expert matters: without it the logits move
+    W2 = {k: v for k, v in W.items() if "shexp" not in k}
+    cfg2 = bt.config("tiny_sh", n_ff_shexp=0)
+    other = orc.Model(cfg2, W2).forward(tokens, 0).astype(np.float64)
+    assert np.abs(other - got).max() > 1e-3
 
 
 def test_block_prefill_and_token_steps_share_layer0_kv(tiny_cfg, tiny_weights):
