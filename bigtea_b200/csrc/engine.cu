@@ -551,7 +551,10 @@ static int check_shape(const std::string &n, const SrcTensor *t, std::initialize
     return BT_OK;
 }
 
-static int build_engine(bt_engine *e, const std::map<std::string, SrcTensor> &src) {
+// Ingests the tensors in `src`: the embedding and output head when `globals`, layers [l0, l1),
+// then (when `finish`) the per-engine tables. The synthetic path calls it one layer at a time.
+static int build_engine(bt_engine *e, const std::map<std::string, SrcTensor> &src, uint32_t l0, uint32_t l1,
+                        bool globals, bool finish) {
     const bt_model_desc &d = e->d;
     const uint64_t E = d.n_embd, QW = d.n_head * d.head_dim, KW = d.n_head_kv * d.head_dim;
     const uint64_t NE = d.n_expert, F = d.n_ff_exp, V = d.n_vocab, D = d.head_dim;
@@ -561,6 +564,7 @@ static int build_engine(bt_engine *e, const std::map<std::string, SrcTensor> &sr
 #define NEED(name, ...)                                  \
     if ((r = find_src(src, name, &t))) return r;         \
     if ((r = check_shape(name, t, {__VA_ARGS__}))) return r;
+    if (globals) {
     NEED("token_embd.weight", E, V);
     if ((r = ingest_qmat(e, e->embd, t->type, V, E, 1, t->data, t->device, default_rpt(E), true, staging))) return r;
     NEED("output_norm.weight", E);
@@ -579,8 +583,9 @@ static int build_engine(bt_engine *e, const std::map<std::string, SrcTensor> &sr
         if ((r = ingest_qmat(e, e->out, o->type, V, E, 1, o->data, o->device, default_rpt(E), false, staging)))
             return r;
     }
-    e->L.resize(d.n_layer);
-    for (uint32_t il = 0; il < d.n_layer; il++) {
+    }
+    if (e->L.size() != d.n_layer) e->L.resize(d.n_layer);
+    for (uint32_t il = l0; il < l1; il++) {
         Layer &l = e->L[il];
         std::string p = "blk." + std::to_string(il) + ".";
         auto f32 = [&](const char *suffix, DevBuf &b, uint64_t n) -> int {
@@ -642,7 +647,8 @@ static int build_engine(bt_engine *e, const std::map<std::string, SrcTensor> &sr
             return fail(BT_ERR_INVALID, "gate and up experts disagree in shape");
     }
 #undef NEED
-    return finish_create(e);
+    CK(cudaStreamSynchronize(e->st));  // the sources may be freed after this returns
+    return finish ? finish_create(e) : BT_OK;
 }
 
 static int engine_init_device(bt_engine *e, int device) {
@@ -681,7 +687,7 @@ extern "C" int bt_engine_create(const bt_model_desc *desc, const bt_tensor_view 
         s.nbytes = tv.nbytes;
         src[tv.name] = s;
     }
-    if ((r = build_engine(e.get(), src))) {
+    if ((r = build_engine(e.get(), src, 0, e->d.n_layer, true, true))) {
         std::string keep = g_err;
         bt_engine_destroy(e.release());
         g_err = keep;
@@ -705,8 +711,8 @@ extern "C" int bt_engine_create_synthetic(const bt_model_desc *desc, const uint3
     const bt_model_desc &d = e->d;
     const uint64_t E = d.n_embd, QW = d.n_head * d.head_dim, KW = d.n_head_kv * d.head_dim;
     const uint64_t NE = d.n_expert, F = d.n_ff_exp, V = d.n_vocab, D = d.head_dim;
-    // Generate every tensor on the device (synth_kernel), keep the raw bytes alive until the
-    // engine has ingested them. One buffer per tensor: peak memory is the raw model once.
+    // Generate the tensors on the device (synth_kernel), one layer at a time, each layer's raw
+    // bytes freed once the engine has ingested them.
     std::vector<std::unique_ptr<DevBuf>> raws;
     std::map<std::string, SrcTensor> src;
     auto gen = [&](const std::string &name, int type, std::vector<uint64_t> ne) -> int {
@@ -730,9 +736,23 @@ extern "C" int bt_engine_create_synthetic(const bt_model_desc *desc, const uint3
         raws.push_back(std::move(b));
         return BT_OK;
     };
+    auto ingest = [&](uint32_t l0, uint32_t l1, bool globals) -> int {
+        CK(cudaStreamSynchronize(e->st));
+        int rr = build_engine(e.get(), src, l0, l1, globals, false);
+        raws.clear();  // build_engine synchronised: the raw copies go
+        src.clear();
+        return rr;
+    };
+    auto bail = [&](int rr) {
+        std::string keep = g_err;
+        bt_engine_destroy(e.release());
+        g_err = keep;
+        return rr;
+    };
     if ((r = gen("token_embd.weight", (int)embd_type, {E, V}))) return r;
     if ((r = gen("output_norm.weight", T_F32, {E}))) return r;
     if ((r = gen("output.weight", (int)out_type, {E, V}))) return r;
+    if ((r = ingest(0, 0, true))) return bail(r);
     for (uint32_t il = 0; il < d.n_layer; il++) {
         std::string p = "blk." + std::to_string(il) + ".";
         const uint32_t *ty = types + 7 * il;
@@ -754,16 +774,10 @@ extern "C" int bt_engine_create_synthetic(const bt_model_desc *desc, const uint3
             if ((r = gen(p + "ffn_up_shexp.weight", (int)ty[5], {E, FS}))) return r;
             if ((r = gen(p + "ffn_down_shexp.weight", (int)ty[6], {FS, E}))) return r;
         }
-        // ingest this layer right away so the raw copies do not pile up
-        if (il == 0) continue;
+        // ingest this layer right away: peak memory is the engine plus one raw layer
+        if ((r = ingest(il, il + 1, false))) return bail(r);
     }
-    CK(cudaStreamSynchronize(e->st));
-    if ((r = build_engine(e.get(), src))) {
-        std::string keep = g_err;
-        bt_engine_destroy(e.release());
-        g_err = keep;
-        return r;
-    }
+    if ((r = finish_create(e.get()))) return bail(r);
     *out = e.release();
     return BT_OK;
 }
