@@ -1007,7 +1007,8 @@ __global__ void __launch_bounds__(128) router_kernel(const __grid_constant__ Rou
     __syncthreads();
     if (!s_last) return;
     __threadfence();
-    if (warp == 0) {
+    __shared__ int s_key[512];
+    if (warp == 0) {  // soft_max_ext: max, exp and the P2 sum, then the scaling (C5, C6)
         const float *lg = p.logits + (long long)t * p.NE;
         float m = -__int_as_float(0x7f800000);
         for (int i = lane; i < p.NE; i += 32) {
@@ -1024,44 +1025,48 @@ __global__ void __launch_bounds__(128) router_kernel(const __grid_constant__ Rou
         }
         acc = butterfly_sum(acc);
         const float inv = __fdiv_rn(1.0f, acc);
-        for (int i = lane; i < p.NE; i += 32) s_prob[i] = __fmul_rn(s_prob[i], inv);
-        __syncwarp();
         for (int i = lane; i < p.NE; i += 32) {
-            int ki = total_key(s_prob[i]);
-            int rank = 0;
-            for (int jj = 0; jj < p.NE; jj++) {
-                int kj = total_key(s_prob[jj]);
-                rank += (kj > ki) || (kj == ki && jj < i);
-            }
-            if (rank < p.K) {
-                s_rank_id[rank] = i;
-                s_rank_p[rank] = s_prob[i];
-            }
+            s_prob[i] = __fmul_rn(s_prob[i], inv);
+            s_key[i] = total_key(s_prob[i]);
         }
-        __syncwarp();
-        if (lane == 0) {
-            float total = 0.0f;
-            for (int q = 0; q < p.K; q++) total = __fadd_rn(total, s_rank_p[q]);
-            int ids[MAX_K];
-            float ws[MAX_K];
-            for (int q = 0; q < p.K; q++) {
-                float w = total > 0.0f ? __fdiv_rn(s_rank_p[q], total) : s_rank_p[q];
-                ids[q] = s_rank_id[q];
-                ws[q] = w;
-                p.topk_ids[t * p.K + q] = ids[q];
-                p.topk_w[t * p.K + q] = w;
-            }
-            for (int a = 1; a < p.K; a++)
-                for (int b = a; b > 0 && ids[b - 1] > ids[b]; b--) {
-                    int ti = ids[b]; ids[b] = ids[b - 1]; ids[b - 1] = ti;
-                    float tw = ws[b]; ws[b] = ws[b - 1]; ws[b - 1] = tw;
-                }
-            for (int q = 0; q < p.K; q++) {
-                p.sel_ids[t * p.K + q] = ids[q];
-                p.sel_w[t * p.K + q] = ws[q];
-            }
-            p.cnt[t] = 0;
+    }
+    __syncthreads();
+    // route(): the rank of each probability in the stable descending order, all threads
+    for (int i = threadIdx.x; i < p.NE; i += blockDim.x) {
+        const int ki = s_key[i];
+        int rank = 0;
+        for (int jj = 0; jj < p.NE; jj++) {
+            const int kj = s_key[jj];
+            rank += (kj > ki) || (kj == ki && jj < i);
         }
+        if (rank < p.K) {
+            s_rank_id[rank] = i;
+            s_rank_p[rank] = s_prob[i];
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float total = 0.0f;
+        for (int q = 0; q < p.K; q++) total = __fadd_rn(total, s_rank_p[q]);
+        int ids[MAX_K];
+        float ws[MAX_K];
+        for (int q = 0; q < p.K; q++) {
+            float w = total > 0.0f ? __fdiv_rn(s_rank_p[q], total) : s_rank_p[q];
+            ids[q] = s_rank_id[q];
+            ws[q] = w;
+            p.topk_ids[t * p.K + q] = ids[q];
+            p.topk_w[t * p.K + q] = w;
+        }
+        for (int a = 1; a < p.K; a++)
+            for (int b = a; b > 0 && ids[b - 1] > ids[b]; b--) {
+                int ti = ids[b]; ids[b] = ids[b - 1]; ids[b - 1] = ti;
+                float tw = ws[b]; ws[b] = ws[b - 1]; ws[b - 1] = tw;
+            }
+        for (int q = 0; q < p.K; q++) {
+            p.sel_ids[t * p.K + q] = ids[q];
+            p.sel_w[t * p.K + q] = ws[q];
+        }
+        p.cnt[t] = 0;
     }
 }
 
