@@ -100,6 +100,7 @@ SIGNATURES = {
     "bt_op_gemv": (C.c_int, [C.c_uint32, _P, C.c_uint32, C.c_uint32, _F32P, C.c_uint32, _F32P]),
     "bt_ep_unique_id": (C.c_int, [_P, C.c_size_t]),
     "bt_engine_set_router_bias": (C.c_int, [_P, C.c_uint32, _F32P, C.c_uint32]),
+    "bt_op_i8_mma": (C.c_int, [_P, _P, C.c_uint32, C.c_uint32, _I32P]),
     "bt_engine_enable_expert_cache": (C.c_int, [_P, C.c_uint64, C.c_int]),
     "bt_expert_cache_stats": (C.c_int, [_P, C.POINTER(XCacheStats)]),
     "bt_expert_cache_simulate": (C.c_int, [C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _I32P,

@@ -2402,6 +2402,27 @@ extern "C" int bt_debug_dequant(uint32_t type, const void *bytes, uint64_t n, fl
     return BT_OK;
 }
 
+extern "C" int bt_op_i8_mma(const uint8_t *a, const int8_t *b, uint32_t n, uint32_t k, int32_t *d) {
+    if (!a || !b || !d) return fail(BT_ERR_INVALID, "null argument");
+    if ((n != 8 && n != 16 && n != 32) || !k || k % 32 || k > 512) return fail(BT_ERR_INVALID, "n in {8, 16, 32}, k = 32..512");
+    DevBuf ad, bd, dd, err;
+    CK(ad.alloc((size_t)128 * k));
+    CK(bd.alloc((size_t)n * k));
+    CK(dd.alloc((size_t)128 * n * 4));
+    CK(err.alloc(4));
+    CK(cudaMemset(err.p, 0, 4));
+    CK(cudaMemset(dd.p, 0, (size_t)128 * n * 4));
+    CK(cudaMemcpy(ad.p, a, (size_t)128 * k, cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(bd.p, b, (size_t)n * k, cudaMemcpyHostToDevice));
+    CK(launch_i8_mma_probe(ad.as<uint8_t>(), bd.as<int8_t>(), dd.as<int32_t>(), (int)n, (int)k, err.as<int>(), 0));
+    CK(cudaDeviceSynchronize());
+    int h = 0;
+    CK(cudaMemcpy(&h, err.p, 4, cudaMemcpyDeviceToHost));
+    if (h) return fail(BT_ERR_TIMEOUT, "the MMA's completion wait ran out");
+    CK(cudaMemcpy(d, dd.p, (size_t)128 * n * 4, cudaMemcpyDeviceToHost));
+    return BT_OK;
+}
+
 extern "C" int bt_op_gemv(uint32_t type, const void *w_bytes, uint32_t rows, uint32_t cols, const float *x, uint32_t T,
                           float *y) {
     if (!w_bytes || !x || !y || !rows || !cols || !T) return fail(BT_ERR_INVALID, "bad argument");

@@ -1223,7 +1223,7 @@ __device__ __forceinline__ void ldw_n(uint32_t (&dst)[N], const uint32_t *src) {
 template <int G>
 __global__ void __launch_bounds__(ATTN_THREADS, 3)
     attn_kernel(const __grid_constant__ AttnArgs p, const __grid_constant__ CUtensorMap tmap) {
-    constexpr int D = 128, HPT = G / 2, CH = ATTN_CHUNK, QWORDS = G / 2;
+    constexpr int D = 128, HPT = G / 2, CH = ATTN_CHUNK;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // offset from the shared array itself (not through an integer), so loads stay ld.shared
     uint8_t *smem = smem_raw + ((1024u - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023u)) & 1023u);

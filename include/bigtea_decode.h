@@ -215,6 +215,11 @@ int bt_debug_hidden(const bt_engine *e, uint32_t token, float *out);
 int bt_op_gemv(uint32_t type, const void *w_bytes, uint32_t rows, uint32_t cols, const float *x,
                uint32_t T, float *y);
 
+/* parity hook of the tensor-core path (tcgen05.mma kind::i8, the operand layouts and
+ * descriptors of the grouped expert kernel): d[128][n] = a[128][k] . b[n][k]^T in int32, a
+ * unsigned 8-bit, b signed 8-bit, host buffers; n in {8, 16, 32}, k a multiple of 32 up to 512 */
+int bt_op_i8_mma(const uint8_t *a, const int8_t *b, uint32_t n, uint32_t k, int32_t *d);
+
 /* ---- allocation-free GEMV (no counterpart in the reference) ----
  * bt_op_gemv on caller-owned DEVICE buffers that allocates nothing: no cudaMalloc, cudaFree,
  * stream or event creation, and no allocating library call. It is for callers that cannot
