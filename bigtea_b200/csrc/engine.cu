@@ -125,6 +125,7 @@ struct bt_engine {
     ncclComm_t ep_comm = nullptr;
     int ep_timeout_ms = 60000;  // a host wait on an expert-parallel step longer than this aborts the exchange
     bool ep_aborted = false;
+    bool mma = true;  // grouped Q4_K gate/up on tcgen05 (option "mma")
     // expert cache: experts in pinned host memory, the ones a layer selects copied into slots
     // of a device pool before its expert kernels (bt_engine_enable_expert_cache)
     bool xcache = false;
@@ -1312,6 +1313,13 @@ static int xcache_layer(bt_engine *e, int il, int T) {
     return BT_OK;
 }
 
+// The tensor-core gate/up of the grouped path: Q4_K gate and up, whole 128-row blocks, and
+// shared memory for the chunk's operands.
+static bool use_gateup_mma(const bt_engine *e, const Layer &l) {
+    return e->mma && l.gate.type == T_Q4_K && l.up.type == T_Q4_K && e->d.n_ff_exp % 128 == 0 &&
+           gateup_mma_smem_bytes((int)e->d.n_embd) <= (size_t)max_dynamic_smem();
+}
+
 static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) {
     if (e->ep_aborted) return fail(BT_ERR_TIMEOUT, "the expert-parallel communicator was aborted by an earlier failure");
     if (step_eligible(e, kv, p)) return launch_persistent_step(e, kv, p, greedy);
@@ -1568,7 +1576,10 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.nst = 1;
             a.nst = pick_nst_cap(a.slot_bytes, gateup_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
             timer_begin(e, "expert_gateup");
-            CK(launch_gateup_grouped(a, e->n_sm, st, pdl));
+            if (use_gateup_mma(e, l))
+                CK(launch_gateup_mma(a, e->n_sm, st, pdl));
+            else
+                CK(launch_gateup_grouped(a, e->n_sm, st, pdl));
             timer_end(e);
             a.slot_bytes = down_group_rows(a) * a.d_tile_bytes;
             a.nst = 1;
@@ -1664,7 +1675,10 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.nst = 1;
             a.nst = pick_nst_cap(a.slot_bytes, gateup_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
             timer_begin(e, "expert_gateup");
-            CK(launch_gateup_grouped(a, e->n_sm, st, pdl));
+            if (use_gateup_mma(e, l))
+                CK(launch_gateup_mma(a, e->n_sm, st, pdl));
+            else
+                CK(launch_gateup_grouped(a, e->n_sm, st, pdl));
             timer_end(e);
             a.slot_bytes = down_group_rows(a) * a.d_tile_bytes;
             a.nst = 1;
@@ -2344,6 +2358,12 @@ extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
     }
     if (!strcmp(name, "persistent")) {
         e->mega = value != 0;
+        for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
+        e->graphs.clear();
+        return BT_OK;
+    }
+    if (!strcmp(name, "mma")) {
+        e->mma = value != 0;
         for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
         e->graphs.clear();
         return BT_OK;

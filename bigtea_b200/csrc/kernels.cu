@@ -1697,7 +1697,7 @@ cudaError_t init_kernel_attributes() {
         int dyn = optin - (int)fa.sharedSizeBytes;
         if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, dyn))) return e;
     }
-    return cudaSuccess;
+    return init_mma_attributes();
 }
 
 int max_dynamic_smem() {

@@ -214,6 +214,10 @@ cudaError_t launch_ep_pack(const EpPackArgs &a, cudaStream_t st, bool pdl);
 // tcgen05 kind::i8 probe: D[128][N] = A[128][K] . B[N][K]^T (u8 x s8 -> s32)
 cudaError_t launch_i8_mma_probe(const uint8_t *A, const int8_t *B, int32_t *D, int N, int K, int *err,
                                 cudaStream_t st);
+// grouped gate/up on tcgen05 (Q4_K gate and up, F a multiple of 128); one CTA per SM
+size_t gateup_mma_smem_bytes(int E);
+cudaError_t launch_gateup_mma(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
+cudaError_t init_mma_attributes();
 // act[t][j] = silu(gu[t][j]) * gu[t][F + j] for the shared expert (C7)
 cudaError_t launch_shexp_act(const float *gu, float *act, int T, int F, cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl);

@@ -3,6 +3,8 @@
 
 #include "bt_common.cuh"
 #include "kernels.cuh"
+#include "kquant.cuh"
+#include "stage.cuh"
 #include "umma.cuh"
 
 namespace bt {
@@ -55,6 +57,257 @@ __global__ void __launch_bounds__(128) i8_mma_probe_kernel(const uint8_t *__rest
 }
 
 size_t i8_mma_probe_smem(int N, int K) { return (size_t)(128 + N) * K + 16; }
+
+// ====================================================================== grouped gate/up on tcgen05
+// Q4_K gate and up of the grouped batched path. Unit = (chunk of at most 16 rows of one
+// expert, block of 128 output rows); CTA b takes units [b*U/grid, (b+1)*U/grid), chunk-major,
+// so consecutive units share the chunk's staged activations. Per unit, 16 steps (gate then
+// up, superblock 0..7):
+//   - thread r (= output row r of the block, = TMEM lane r) loads its row's 144-byte
+//     superblock (header + 128 bytes of nibbles) straight from the tiled weights, one step
+//     ahead, and unpacks the nibbles into the 8-bit A operand (8 sub-blocks x 128 rows x 32);
+//   - one thread issues 8 MMAs (M = 128, N = 16, K = 32: one per 32-value sub-block, each into
+//     its own 16 TMEM columns) against the chunk's Q8_K activations (the B operand) and
+//     commits them to the step's mbarrier;
+//   - the previous step's epilogue reads its 8 x 16 integer sub-block dots from TMEM and
+//     finishes C4 per (row, token): sumi = sum sc_j dot_j, summ = sum m_j bs32_j, then
+//     (float)sumi * (d * d_a) - (float)summ * (dmin * d_a), added to the row's running sum in
+//     superblock order -- the integers are exact, so the result equals the dp4a kernels' bits.
+// A and TMEM are double-buffered by step parity. Every wait is bounded; on a timeout the CTA
+// waits (bounded) for its MMAs in flight, frees its TMEM and leaves.
+constexpr int MMA_N = 16;                     // tokens per MMA (the chunk, zero-padded)
+constexpr int MMA_A_BYTES = 8 * 128 * 32;     // one superblock of 128 rows, 8 K steps
+constexpr int MMA_TMEM_COLS = 256;            // 2 buffers x 8 sub-blocks x 16 tokens
+
+size_t gateup_mma_smem_bytes(int E) {
+    const size_t nsb = (size_t)E / 256;
+    return 1024 + (size_t)MMA_N * E + 2 * MMA_A_BYTES + (size_t)MMA_N * nsb * sizeof(ActBlock) + 256;
+}
+
+__global__ void __launch_bounds__(128, 1) gateup_mma_kernel(const __grid_constant__ ExpertArgs p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int E = p.E, nsb = E / 256, S = p.g_S;
+    uint8_t *sB = smem;                                                  // [E/32 K steps][16 rows][32]
+    uint8_t *sA = sB + MMA_N * E;                                        // [2][8 K steps][128 rows][32]
+    ActBlock *act = reinterpret_cast<ActBlock *>(sA + 2 * MMA_A_BYTES);  // [16][nsb]
+    int *tk_s = reinterpret_cast<int *>(act + MMA_N * nsb);             // [16]
+    int *rows_s = tk_s + MMA_N;                                          // [16]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(rows_s + MMA_N);      // [2]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(smem_u32(tslot), MMA_TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    pdl_wait();  // the groups come from group_kernel, the activations from the router
+    const int nrb = p.F / 128;
+    const int total = *p.g_nchunks * nrb;
+    const int u0 = (int)((long long)blockIdx.x * total / gridDim.x);
+    const int u1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
+    pdl_trigger();
+    const uint32_t idesc = umma_idesc_u8s8(128, MMA_N);
+    const uint32_t aBase = smem_u32(sA), bBase = smem_u32(sB);
+    int cur_chunk = -1, mc = 0;
+    uint32_t gstep = 0;  // steps issued by this CTA: buffer gstep & 1, its barrier phase (gstep >> 1) & 1
+    bool ok = true;
+    for (int u = u0; ok && u < u1; u++) {
+        const int ci = u / nrb, rb = u - ci * nrb;
+        const int e = p.g_chunk_e[ci];
+        if (ci != cur_chunk) {  // stage the chunk: Q8_K blocks, then the B operand (zero rows past mc)
+            cur_chunk = ci;
+            const int c0 = p.g_chunk_r0[ci], m = p.g_count[e], off = p.g_off[e];
+            mc = m - c0 < MMA_N ? m - c0 : MMA_N;
+            __syncthreads();  // the previous chunk's operands are no longer read
+            if (tid < mc) {
+                const int tk = p.g_list[off + c0 + tid];
+                tk_s[tid] = tk;
+                rows_s[tid] = tk / p.row_div;
+            }
+            __syncthreads();
+            stage_activations<4>(p.fn, p.E, rows_s, nullptr, 0.0f, p.E, mc, act, nullptr);
+            __syncthreads();
+            for (int i = tid; i < MMA_N * E / 16; i += 128) {  // 16-byte pieces of the B operand
+                const int t = i / (E / 16), k = (i - t * (E / 16)) * 16;
+                uint4 v = make_uint4(0, 0, 0, 0);
+                if (t < mc) v = *reinterpret_cast<const uint4 *>(act[t * nsb + k / 256].qs + (k & 255));
+                *reinterpret_cast<uint4 *>(sB + umma_off(t, k, MMA_N)) = v;
+            }
+        }
+        // this thread's row of the block: tile (row / rpt), slot (row % rpt) * nsb + superblock
+        const int row = rb * 128 + tid;
+        const int rpt = p.g_rpt;
+        const uint8_t *gbase = expert_gate(p, e) + (long long)(row / rpt) * p.g_tile_bytes;
+        const uint8_t *ubase = expert_up(p, e) + (long long)(row / rpt) * p.u_tile_bytes;
+        const int slot0 = (row % rpt) * nsb;
+        auto load_raw = [&](int st, uint4 (&w)[9]) {
+            const uint8_t *b = (st < nsb ? gbase : ubase) + (size_t)(slot0 + (st < nsb ? st : st - nsb)) * 16;
+#pragma unroll
+            for (int c = 0; c < 9; c++) w[c] = __ldg(reinterpret_cast<const uint4 *>(b + (size_t)c * S * 16));
+        };
+        float acc_g[MMA_N], acc_u[MMA_N];
+#pragma unroll
+        for (int t = 0; t < MMA_N; t++) acc_g[t] = acc_u[t] = 0.0f;
+        uint4 raw[9], nxt[9];
+        load_raw(0, raw);
+        int sc[8], mn[8];
+        float dw = 0.0f, dminw = 0.0f;
+        int psc[8], pmn[8];
+        float pdw = 0.0f, pdminw = 0.0f;
+        const int nsteps = 2 * nsb;
+        auto epilogue = [&](int st, uint32_t gs) -> bool {  // the integer dots of step st -> the row sums
+            if (!mbar_wait(&bars[gs & 1], (gs >> 1) & 1, p.err)) return false;
+            tc_fence_after();
+            const int sb = st < nsb ? st : st - nsb;
+            int dots[8][MMA_N];
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                uint32_t v[16];
+                tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (gs & 1) * 128 + j * 16, v);
+                tmem_wait_ld();
+#pragma unroll
+                for (int t = 0; t < MMA_N; t++) dots[j][t] = (int)v[t];
+            }
+#pragma unroll
+            for (int t = 0; t < MMA_N; t++) {
+                const ActBlock &ab = act[(t < mc ? t : 0) * nsb + sb];
+                const uint4 b0 = *reinterpret_cast<const uint4 *>(ab.bs32);
+                const uint4 b1 = *reinterpret_cast<const uint4 *>(ab.bs32 + 4);
+                const int bs[8] = {(int)b0.x, (int)b0.y, (int)b0.z, (int)b0.w, (int)b1.x, (int)b1.y, (int)b1.z, (int)b1.w};
+                int sumi = 0, summ = 0;
+#pragma unroll
+                for (int j = 0; j < 8; j++) {
+                    sumi += psc[j] * dots[j][t];
+                    summ += pmn[j] * bs[j];
+                }
+                const float da = ab.d;
+                const float t1 = __fmul_rn(pdw, da);
+                const float t2 = __fmul_rn(__int2float_rn(sumi), t1);
+                const float t3 = __fmul_rn(pdminw, da);
+                const float t4 = __fmul_rn(__int2float_rn(summ), t3);
+                const float v = __fsub_rn(t2, t4);
+                if (st < nsb) acc_g[t] = __fadd_rn(acc_g[t], v);
+                else acc_u[t] = __fadd_rn(acc_u[t], v);
+            }
+            return true;
+        };
+        for (int st = 0; st < nsteps; st++) {
+            const uint32_t gs = gstep++;
+            // header: d, dmin and the 6-bit scales/mins of this row's superblock (get_scale_min_k4)
+            {
+                const uint4 h = raw[0];
+                dw = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffff)));
+                dminw = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+                const uint32_t s03 = h.y, s47 = h.z, s811 = h.w;
+                const uint32_t sc_lo = s03 & 0x3F3F3F3Fu, m_lo = s47 & 0x3F3F3F3Fu;
+                const uint32_t sc_hi = (s811 & 0x0F0F0F0Fu) | ((s03 >> 2) & 0x30303030u);
+                const uint32_t m_hi = ((s811 >> 4) & 0x0F0F0F0Fu) | ((s47 >> 2) & 0x30303030u);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    sc[j] = byte_u(sc_lo, j);
+                    sc[j + 4] = byte_u(sc_hi, j);
+                    mn[j] = byte_u(m_lo, j);
+                    mn[j + 4] = byte_u(m_hi, j);
+                }
+            }
+            // the A operand of this step: sub-block 2g = low nibbles, 2g + 1 = high nibbles of
+            // the 32 bytes of group g; row `tid`, K step j at j * 4096
+            uint8_t *a = sA + (gs & 1) * MMA_A_BYTES;
+#pragma unroll
+            for (int g = 0; g < 4; g++) {
+                const uint4 w0 = raw[1 + 2 * g], w1 = raw[2 + 2 * g];
+                const uint4 lo0 = make_uint4(w0.x & 0x0F0F0F0Fu, w0.y & 0x0F0F0F0Fu, w0.z & 0x0F0F0F0Fu, w0.w & 0x0F0F0F0Fu);
+                const uint4 lo1 = make_uint4(w1.x & 0x0F0F0F0Fu, w1.y & 0x0F0F0F0Fu, w1.z & 0x0F0F0F0Fu, w1.w & 0x0F0F0F0Fu);
+                const uint4 hi0 = make_uint4((w0.x >> 4) & 0x0F0F0F0Fu, (w0.y >> 4) & 0x0F0F0F0Fu, (w0.z >> 4) & 0x0F0F0F0Fu,
+                                             (w0.w >> 4) & 0x0F0F0F0Fu);
+                const uint4 hi1 = make_uint4((w1.x >> 4) & 0x0F0F0F0Fu, (w1.y >> 4) & 0x0F0F0F0Fu, (w1.z >> 4) & 0x0F0F0F0Fu,
+                                             (w1.w >> 4) & 0x0F0F0F0Fu);
+                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g) * 32, 128)) = lo0;
+                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g) * 32 + 16, 128)) = lo1;
+                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g + 1) * 32, 128)) = hi0;
+                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g + 1) * 32 + 16, 128)) = hi1;
+            }
+            fence_proxy_async();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0) {
+                const int sb = st < nsb ? st : st - nsb;
+#pragma unroll 1
+                for (int j = 0; j < 8; j++)
+                    umma_i8(tmem + (gs & 1) * 128 + j * 16,
+                            umma_desc(aBase + (gs & 1) * MMA_A_BYTES + j * 4096, 128, 256),
+                            umma_desc(bBase + (uint32_t)(sb * 8 + j) * MMA_N * 32, 128, 256), idesc, false);
+                umma_commit(smem_u32(&bars[gs & 1]));
+            }
+            if (st + 1 < nsteps) load_raw(st + 1, nxt);
+            if (st > 0 && !__syncthreads_and(epilogue(st - 1, gs - 1))) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                psc[j] = sc[j];
+                pmn[j] = mn[j];
+            }
+            pdw = dw;
+            pdminw = dminw;
+#pragma unroll
+            for (int c = 0; c < 9; c++) raw[c] = nxt[c];
+            tc_fence_before();
+        }
+        if (!ok) break;
+        if (!__syncthreads_and(epilogue(nsteps - 1, gstep - 1))) {
+            ok = false;
+            break;
+        }
+        tc_fence_before();
+        if (row < p.F)
+            for (int t = 0; t < mc; t++) p.act[(long long)tk_s[t] * p.F + row] = __fmul_rn(bt_silu(acc_g[t]), acc_u[t]);
+    }
+    if (!ok && tid == 0) {  // let this CTA's MMAs in flight finish (bounded) before the TMEM goes
+        for (uint32_t b = 0; b < 2; b++) {
+            // the last step issued on buffer b
+            const long long last = gstep == 0 ? -1 : ((long long)((gstep - 1) & 1) == b ? gstep - 1 : (long long)gstep - 2);
+            if (last >= 0) mbar_wait(&bars[b], (uint32_t)(last >> 1) & 1, nullptr);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, MMA_TMEM_COLS);
+}
+
+cudaError_t launch_gateup_mma(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl) {
+    const size_t smem = gateup_mma_smem_bytes(a.E);
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gateup_mma_kernel, a);
+}
+
+cudaError_t init_mma_attributes() {
+    int dev = 0, optin = 0;
+    cudaError_t e;
+    if ((e = cudaGetDevice(&dev))) return e;
+    if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
+    cudaFuncAttributes fa;
+    if ((e = cudaFuncGetAttributes(&fa, gateup_mma_kernel))) return e;
+    return cudaFuncSetAttribute(gateup_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                optin - (int)fa.sharedSizeBytes);
+}
 
 cudaError_t launch_i8_mma_probe(const uint8_t *A, const int8_t *B, int32_t *D, int N, int K, int *err,
                                 cudaStream_t st) {

@@ -438,3 +438,24 @@ def test_shared_expert_matches_oracle(source):
     cache.close()
     e.close()
 
+
+def test_tensor_core_gateup_matches_dp4a_kernel(tiny_cfg, tiny_weights):
+    """The grouped gate/up on tcgen05 (int8 MMA per K-quant sub-block, integer-exact) and the
+    dp4a grouped kernel give the same bits: a 64-token prefill sub-step and a 24-sequence step."""
+    rng = np.random.default_rng(55)
+    prompt = rng.integers(0, tiny_cfg.n_vocab, 70)
+    outs = {}
+    for mma in (1, 0):
+        e = bt.Engine(tiny_cfg, tiny_weights)
+        e.set_option("mma", mma)
+        cache = bt.KvCache(e, max_positions=512, max_seqs=24)
+        runner = bt.StreamingRunner(e)
+        lg = runner.forward_batch(cache, [0], [prompt], [0])
+        steps = runner.forward_batch(cache, list(range(1, 24)), [[int(t)] for t in prompt[:23]], [0] * 23)
+        outs[mma] = (lg, steps, cache.layer_bytes(1, 0))
+        cache.close()
+        e.close()
+    assert np.array_equal(bits(outs[0][0]), bits(outs[1][0]))
+    assert np.array_equal(bits(outs[0][1]), bits(outs[1][1]))
+    assert np.array_equal(outs[0][2][0], outs[1][2][0]) and np.array_equal(outs[0][2][1], outs[1][2][1])
+
