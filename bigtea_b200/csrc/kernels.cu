@@ -1220,17 +1220,10 @@ __device__ __forceinline__ void ldw_n(uint32_t (&dst)[N], const uint32_t *src) {
 //   chunk max, exp and the P3 sum (32-key butterflies, the 4 warp sums in order);
 //   P*V: thread = dims 2dp, 2dp+1 and heads hq*G/2 .. +G/2, keys in order;
 // and the chunk's partial (acc, m, l), or the output when the context is one chunk.
-// threads of the attention kernel: 256 when the heads split evenly into quarters (scores:
-// two threads per key, each half of the heads; P*V: four head groups), else 128
-__host__ __device__ constexpr int attn_threads(int G) { return G % 4 == 0 ? 256 : 128; }
-
 template <int G>
-__global__ void __launch_bounds__(attn_threads(G), 3)
+__global__ void __launch_bounds__(ATTN_THREADS, 3)
     attn_kernel(const __grid_constant__ AttnArgs p, const __grid_constant__ CUtensorMap tmap) {
-    constexpr int NT = attn_threads(G);
-    constexpr int SH = G / (NT / 128);  // heads per scoring thread
-    constexpr int HPT = G / (NT / 64);  // heads per P*V thread
-    constexpr int D = 128, CH = ATTN_CHUNK;
+    constexpr int D = 128, HPT = G / 2, CH = ATTN_CHUNK;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // offset from the shared array itself (not through an integer), so loads stay ld.shared
     uint8_t *smem = smem_raw + ((1024u - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023u)) & 1023u);
@@ -1327,7 +1320,7 @@ __global__ void __launch_bounds__(attn_threads(G), 3)
         issue(1);
     }
     k_issued = v_issued = 1;
-    const int QW = p.H * D, dp = tid & 63, hq = tid >> 6;  // P*V: dims 2dp, 2dp+1; heads hq*HPT ..
+    const int QW = p.H * D, dp = tid & 63, hq = tid >> 6;
     const float NEG_INF = -__int_as_float(0x7f800000);
     int cur_tg = -1;
     bool ok = true;
@@ -1339,7 +1332,7 @@ __global__ void __launch_bounds__(attn_threads(G), 3)
         if (warp == 0 && i + 1 < u1) locate(i + 1);  // the page ids load under this item's arithmetic
         if (t * p.HK + g != cur_tg) {  // every thread passed the last item's scores: qs is free
             cur_tg = t * p.HK + g;
-            for (int x = tid; x < D * G; x += NT) {
+            for (int x = tid; x < D * G; x += ATTN_THREADS) {
                 const int h = x / D, d = x % D;
                 qs[d * G + h] = __half2float(__float2half_rn(p.q[(long long)t * QW + (g * G + h) * D + d]));
             }
@@ -1350,19 +1343,18 @@ __global__ void __launch_bounds__(attn_threads(G), 3)
             break;
         }
 
-        // ---- scores: thread = (key k, head half hh); heads hh*SH .. hh*SH+SH-1
-        const int k = tid & 127, hh = tid >> 7, kw_ = (tid >> 5) & 3;
+        // ---- scores
+        const int k = tid;
         const bool valid = k < cnt;
-        float sc[SH];
+        float sc[G];
         {
             // heads in pairs: (sc[2j], sc[2j+1]) += (q[d][2j], q[d][2j+1]) * (k[d], k[d]), one
             // paired fma per pair and dimension, d in order (C8: each an fmaf of two f16 values)
-            f32x2 acc[SH / 2];
+            f32x2 acc[G / 2];
 #pragma unroll
-            for (int j = 0; j < SH / 2; j++) acc[j] = 0ull;
+            for (int j = 0; j < G / 2; j++) acc[j] = 0ull;
             const uint8_t *krow = K0 + k * 128;
             const int ksw = k & 7;
-            const float *qh = qs + hh * SH;
 #pragma unroll 2
             for (int c16 = 0; c16 < 16; c16++) {
                 const uint4 w =
@@ -1375,24 +1367,24 @@ __global__ void __launch_bounds__(attn_threads(G), 3)
                     for (int hl = 0; hl < 2; hl++) {
                         const int d = c16 * 8 + 2 * e2 + hl;
                         const f32x2 kk = hl ? pk2(kf.y, kf.y) : pk2(kf.x, kf.x);
-                        const f32x2 *qd = reinterpret_cast<const f32x2 *>(qh + d * G);
+                        const f32x2 *qd = reinterpret_cast<const f32x2 *>(qs + d * G);
 #pragma unroll
-                        for (int j = 0; j < SH / 2; j++) acc[j] = ffma2(qd[j], kk, acc[j]);
+                        for (int j = 0; j < G / 2; j++) acc[j] = ffma2(qd[j], kk, acc[j]);
                     }
                 }
             }
 #pragma unroll
-            for (int j = 0; j < SH / 2; j++) {
+            for (int j = 0; j < G / 2; j++) {
                 const float2 v = upk2(acc[j]);
                 sc[2 * j] = v.x;
                 sc[2 * j + 1] = v.y;
             }
         }
 #pragma unroll
-        for (int h = 0; h < SH; h++) {
+        for (int h = 0; h < G; h++) {
             sc[h] = valid ? __fmul_rn(sc[h], p.scale) : NEG_INF;
             const float m = warp_max(sc[h]);
-            if (lane == 0) red[kw_ * 8 + hh * SH + h] = m;
+            if (lane == 0) red[warp * 8 + h] = m;
         }
         __syncthreads();  // K is no longer read: the next item's K pages may land
         if (warp == 0 && i + 1 < u1) issue(0);
@@ -1404,20 +1396,20 @@ __global__ void __launch_bounds__(attn_threads(G), 3)
         }
         __syncthreads();
 #pragma unroll
-        for (int h = 0; h < SH; h++) {
-            const float pr = valid ? bt_exp(__fsub_rn(sc[h], s_m[hh * SH + h])) : 0.0f;
+        for (int h = 0; h < G; h++) {
+            const float pr = valid ? bt_exp(__fsub_rn(sc[h], s_m[h])) : 0.0f;
             sc[h] = pr;
             const float ws = butterfly_sum(pr);
-            if (lane == 0) red2[kw_ * 8 + hh * SH + h] = ws;
+            if (lane == 0) red2[warp * 8 + h] = ws;
         }
-        if constexpr (SH % 4 == 0) {
-            float4 *prow = reinterpret_cast<float4 *>(ps + k * G + hh * SH);
+        if constexpr (G % 4 == 0) {
+            float4 *prow = reinterpret_cast<float4 *>(ps + k * G);
 #pragma unroll
-            for (int h4 = 0; h4 < SH / 4; h4++)
+            for (int h4 = 0; h4 < G / 4; h4++)
                 prow[h4] = make_float4(sc[4 * h4], sc[4 * h4 + 1], sc[4 * h4 + 2], sc[4 * h4 + 3]);
         } else {
 #pragma unroll
-            for (int h = 0; h < SH; h++) ps[k * G + hh * SH + h] = sc[h];
+            for (int h = 0; h < G; h++) ps[k * G + h] = sc[h];
         }
         __syncthreads();
         if (tid < G) {
@@ -1584,7 +1576,7 @@ template <int G>
 static cudaError_t launch_attn_g(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(a.n_cta);
-    cfg.blockDim = dim3(attn_threads(G));
+    cfg.blockDim = dim3(ATTN_THREADS);
     cfg.dynamicSmemBytes = attn_smem_bytes(G, a.T);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
