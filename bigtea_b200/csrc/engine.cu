@@ -1161,6 +1161,62 @@ static cudaError_t run_gemv(bt_engine *e, const QMat *const *mats, const int *ou
     return r;
 }
 
+// A batched GEMV (T > MAX_T tokens): the Q4_K segments of whole 128-row blocks run on tcgen05 in
+// one launch over all tokens; the other segments run through the dp4a kernel in token chunks.
+static int run_gemv_batched(bt_engine *e, const QMat *const *mats, const int *offs, int nseg, const float *x,
+                            long long x_stride, const float *norm_w, int K, int T, float *y, long long y_stride,
+                            const float *res, long long res_stride, const char *name, const PrefetchSpec *pf) {
+    const QMat *mm[3], *dm[3];
+    int mo[3], dof[3], nm = 0, nd = 0;
+    const bool mma_ok = e->mma && gemv_mma_smem_bytes(K) <= (size_t)max_dynamic_smem();
+    for (int i = 0; i < nseg; i++) {
+        if (mma_ok && mats[i]->type == T_Q4_K && mats[i]->rows % 128 == 0) {
+            mm[nm] = mats[i];
+            mo[nm++] = offs[i];
+        } else {
+            dm[nd] = mats[i];
+            dof[nd++] = offs[i];
+        }
+    }
+    if (nm) {
+        GemvArgs a{};
+        int tile0 = 0;
+        for (int i = 0; i < nm; i++) {
+            a.seg[i] = make_seg(*mm[i], tile0, mo[i]);
+            tile0 += a.seg[i].n_tiles;
+        }
+        a.nseg = nm;
+        a.total_tiles = tile0;
+        a.x = x;
+        a.x_stride = x_stride;
+        a.norm_w = norm_w;
+        a.eps = e->d.rms_eps;
+        a.K = K;
+        a.T = T;
+        a.y = y;
+        a.y_stride = y_stride;
+        a.res = res;
+        a.res_stride = res_stride;
+        a.err = e->err.as<int>();
+        timer_begin(e, name);
+        cudaError_t ce = launch_gemv_mma(a, e->n_sm, e->st, e->pdl);
+        timer_end(e);
+        CK(ce);
+    }
+    if (nd) {
+        int slot = 0;
+        for (int i = 0; i < nd; i++) slot = dm[i]->g.tile_bytes > slot ? dm[i]->g.tile_bytes : slot;
+        const int chunk = gemv_chunk(T, K, slot);
+        for (int t0 = 0; t0 < T; t0 += chunk) {
+            const int tg = T - t0 < chunk ? T - t0 : chunk;
+            CK(run_gemv(e, dm, dof, nd, x + (size_t)t0 * x_stride, x_stride, nullptr, norm_w, K, tg,
+                        y + (size_t)t0 * y_stride, y_stride, res ? res + (size_t)t0 * res_stride : nullptr, res_stride,
+                        name, nullptr, t0 == 0 ? pf : nullptr));
+        }
+    }
+    return BT_OK;
+}
+
 static int upload_plan(bt_engine *e, const StepPlan &p) {
     cudaStream_t st = e->st;
     CK(cudaMemcpyAsync(e->tokens.p, p.tokens.data(), p.T * 4, cudaMemcpyHostToDevice, st));
@@ -1372,7 +1428,14 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
         int qslot = l.q.g.tile_bytes > l.k.g.tile_bytes ? l.q.g.tile_bytes : l.k.g.tile_bytes;
         qslot = l.v.g.tile_bytes > qslot ? l.v.g.tile_bytes : qslot;
         const int qchunk = gemv_chunk(T, E, qslot);
-        for (int t0 = 0; t0 < T; t0 += qchunk) {
+        if (T > MAX_T) {
+            const QMat *mats[3] = {&l.q, &l.k, &l.v};
+            int offs[3] = {0, QW, QW + KW};
+            int rr = run_gemv_batched(e, mats, offs, 3, e->x.as<float>(), E, l.attn_norm.as<float>(), E, T,
+                                      e->qkv.as<float>(), QW + 2 * KW, nullptr, 0, "qkv_gemv", &pf_qkv);
+            if (rr) return rr;
+        }
+        for (int t0 = 0; T <= MAX_T && t0 < T; t0 += qchunk) {
             int tg = T - t0 < qchunk ? T - t0 : qchunk;
             const QMat *mats[3] = {&l.q, &l.k, &l.v};
             int offs[3] = {0, QW, QW + KW};
@@ -1431,7 +1494,14 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             timer_end(e);
         }
         const int ochunk = gemv_chunk(T, QW, l.o.g.tile_bytes);
-        for (int t0 = 0; t0 < T; t0 += ochunk) {
+        if (T > MAX_T) {
+            const QMat *mats[1] = {&l.o};
+            int offs[1] = {0};
+            int rr = run_gemv_batched(e, mats, offs, 1, e->att.as<float>(), QW, nullptr, QW, T, e->ffn_in.as<float>(), E,
+                                      e->x.as<float>(), E, "attn_out_gemv", nullptr);
+            if (rr) return rr;
+        }
+        for (int t0 = 0; T <= MAX_T && t0 < T; t0 += ochunk) {
             int tg = T - t0 < ochunk ? T - t0 : ochunk;
             const QMat *mats[1] = {&l.o};
             int offs[1] = {0};

@@ -218,6 +218,9 @@ cudaError_t launch_i8_mma_probe(const uint8_t *A, const int8_t *B, int32_t *D, i
 size_t gateup_mma_smem_bytes(int E);
 cudaError_t launch_gateup_mma(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
 cudaError_t init_mma_attributes();
+// batched GEMV on tcgen05 (Q4_K segments of whole 128-row blocks, no argmax); one CTA per SM
+size_t gemv_mma_smem_bytes(int K);
+cudaError_t launch_gemv_mma(const GemvArgs &a, int grid, cudaStream_t st, bool pdl);
 // act[t][j] = silu(gu[t][j]) * gu[t][F + j] for the shared expert (C7)
 cudaError_t launch_shexp_act(const float *gu, float *act, int T, int F, cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl);

@@ -298,15 +298,273 @@ cudaError_t launch_gateup_mma(const ExpertArgs &a, int grid, cudaStream_t st, bo
     return cudaLaunchKernelEx(&cfg, gateup_mma_kernel, a);
 }
 
+// ====================================================================== batched GEMV on tcgen05
+// y[t][out_off + r] = W[r,:] . x[t,:] (+ res) for Q4_K segments of whole 128-row blocks and T > 8
+// tokens (q/k/v and attn_output of batched steps). Unit = (chunk of 32 tokens, block of 128
+// rows of one segment), token-chunk-major. The activations of a chunk are RMS-normed (q/k/v)
+// and quantised exactly as the dp4a kernel stages them, into the 8-bit B operand plus each
+// block's d and 32-value sums. Per superblock step, thread r unpacks its row's nibbles into A
+// (double-buffered), one thread issues 8 MMAs (M = 128, N = 32, one per sub-block, each into
+// its own 32 TMEM columns; TMEM double-buffered), and the previous step's epilogue turns the
+// integer sub-block dots into the superblock's C4 value per (row, token) and adds it to the
+// row's running sum in superblock order.
+constexpr int GM_N = 32;
+
+size_t gemv_mma_smem_bytes(int K) {
+    const size_t nsb = (size_t)K / 256;
+    return 1024 + (size_t)GM_N * K + (size_t)GM_N * nsb * (4 + 32) + 4 * sizeof(ActBlock) + 2 * MMA_A_BYTES +
+           GM_N * 4 + 256;
+}
+
+__global__ void __launch_bounds__(128, 1) gemv_mma_kernel(const __grid_constant__ GemvArgs p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int K = p.K, nsb = K / 256;
+    uint8_t *sA = smem;                                                  // [2][8 K steps][128 rows][32]
+    uint8_t *sB = sA + 2 * MMA_A_BYTES;                                  // [K/32 steps][32 rows][32]
+    float *dA = reinterpret_cast<float *>(sB + (size_t)GM_N * K);        // [32][nsb]
+    int *bsA = reinterpret_cast<int *>(dA + GM_N * nsb);                 // [32][nsb][8]
+    ActBlock *tmp = reinterpret_cast<ActBlock *>(bsA + GM_N * nsb * 8);  // [4] one per warp
+    float *normS = reinterpret_cast<float *>(tmp + 4);                   // [32]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(normS + GM_N);         // [2]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(smem_u32(tslot), 512);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    pdl_wait();
+    int nrb = 0;  // 128-row blocks over the segments
+    for (int i = 0; i < p.nseg; i++) nrb += p.seg[i].rows / 128;
+    const int ntc = (p.T + GM_N - 1) / GM_N;
+    const int total = ntc * nrb;
+    const int u0 = (int)((long long)blockIdx.x * total / gridDim.x);
+    const int u1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
+    pdl_trigger();
+    const uint32_t idesc = umma_idesc_u8s8(128, GM_N);
+    const uint32_t aBase = smem_u32(sA), bBase = smem_u32(sB);
+    int cur_tc = -1, tn = 0;
+    uint32_t gstep = 0;
+    bool ok = true;
+    for (int u = u0; ok && u < u1; u++) {
+        const int tc = u / nrb;
+        int rb = u - tc * nrb, si = 0;
+        while (rb >= p.seg[si].rows / 128) {
+            rb -= p.seg[si].rows / 128;
+            si++;
+        }
+        const GemvSeg &sg = p.seg[si];
+        if (tc != cur_tc) {  // stage the chunk's 32 token rows (zeros past the last token)
+            cur_tc = tc;
+            const int t0 = tc * GM_N;
+            tn = p.T - t0 < GM_N ? p.T - t0 : GM_N;
+            __syncthreads();  // the previous chunk's operands are no longer read
+            if (p.norm_w) {
+                for (int t = warp; t < tn; t += 4) {
+                    const float *xt = p.x + (long long)(p.x_rows ? p.x_rows[t0 + t] : t0 + t) * p.x_stride;
+                    const float acc = warp_sumsq_p2(xt, K, lane);
+                    if (lane == 0) normS[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)K), p.eps)));
+                }
+                __syncthreads();
+            }
+            for (int blk = warp; blk < GM_N * nsb; blk += 4) {
+                const int t = blk / nsb, b = blk - t * nsb;
+                uint2 q8 = make_uint2(0, 0);
+                float dv = 0.0f;
+                int bsv = 0;
+                if (t < tn) {
+                    const float *xt = p.x + (long long)(p.x_rows ? p.x_rows[t0 + t] : t0 + t) * p.x_stride + b * 256 +
+                                      lane * 8;
+                    float v[8];
+                    const float4 a0 = *reinterpret_cast<const float4 *>(xt), a1 = *reinterpret_cast<const float4 *>(xt + 4);
+                    v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
+                    v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+                    if (p.norm_w) {
+                        const float sN = normS[t];
+                        const float *w = p.norm_w + b * 256 + lane * 8;
+#pragma unroll
+                        for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fmul_rn(v[i], sN), w[i]);
+                    }
+                    quantize_block_warp(v, tmp + warp, lane);
+                    __syncwarp();
+                    q8 = *reinterpret_cast<const uint2 *>(tmp[warp].qs + lane * 8);
+                    dv = tmp[warp].d;
+                    bsv = lane < 8 ? tmp[warp].bs32[lane] : 0;
+                    __syncwarp();  // tmp is read before the warp's next block overwrites it
+                }
+                const int k = b * 256 + lane * 8;
+                *reinterpret_cast<uint2 *>(sB + umma_off(t, k, GM_N)) = q8;
+                if (lane == 0) dA[t * nsb + b] = dv;
+                if (lane < 8) bsA[(t * nsb + b) * 8 + lane] = bsv;
+            }
+        }
+        // this thread's row: tile row / rpt of the segment, slot (row % rpt) * nsb + superblock
+        const int row = rb * 128 + tid;
+        const uint8_t *wbase = sg.w + (long long)(row / sg.rpt) * sg.tile_bytes;
+        const int slot0 = (row % sg.rpt) * nsb, S = sg.S;
+        auto load_raw = [&](int st, uint4 (&w)[9]) {
+            const uint8_t *b = wbase + (size_t)(slot0 + st) * 16;
+#pragma unroll
+            for (int c = 0; c < 9; c++) w[c] = __ldg(reinterpret_cast<const uint4 *>(b + (size_t)c * S * 16));
+        };
+        float acc[GM_N];
+#pragma unroll
+        for (int t = 0; t < GM_N; t++) acc[t] = 0.0f;
+        uint4 raw[9], nxt[9];
+        load_raw(0, raw);
+        int sc[8], mn[8], psc[8], pmn[8];
+        float dw = 0.0f, dminw = 0.0f, pdw = 0.0f, pdminw = 0.0f;
+        auto epilogue = [&](int sb, uint32_t gs) -> bool {
+            if (!mbar_wait(&bars[gs & 1], (gs >> 1) & 1, p.err)) return false;
+            tc_fence_after();
+            int sumi[GM_N];
+#pragma unroll
+            for (int t = 0; t < GM_N; t++) sumi[t] = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+#pragma unroll
+                for (int h = 0; h < GM_N / 16; h++) {
+                    uint32_t v[16];
+                    tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (gs & 1) * 256 + j * GM_N + h * 16, v);
+                    tmem_wait_ld();
+#pragma unroll
+                    for (int t = 0; t < 16; t++) sumi[h * 16 + t] += psc[j] * (int)v[t];
+                }
+            }
+#pragma unroll
+            for (int t = 0; t < GM_N; t++) {
+                const int4 b0 = *reinterpret_cast<const int4 *>(bsA + (t * nsb + sb) * 8);
+                const int4 b1 = *reinterpret_cast<const int4 *>(bsA + (t * nsb + sb) * 8 + 4);
+                const int summ = pmn[0] * b0.x + pmn[1] * b0.y + pmn[2] * b0.z + pmn[3] * b0.w + pmn[4] * b1.x +
+                                 pmn[5] * b1.y + pmn[6] * b1.z + pmn[7] * b1.w;
+                const float da = dA[t * nsb + sb];
+                const float t1 = __fmul_rn(pdw, da);
+                const float t2 = __fmul_rn(__int2float_rn(sumi[t]), t1);
+                const float t3 = __fmul_rn(pdminw, da);
+                const float t4 = __fmul_rn(__int2float_rn(summ), t3);
+                acc[t] = __fadd_rn(acc[t], __fsub_rn(t2, t4));
+            }
+            return true;
+        };
+        for (int st = 0; st < nsb; st++) {
+            const uint32_t gs = gstep++;
+            {
+                const uint4 h = raw[0];
+                dw = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffff)));
+                dminw = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
+                const uint32_t s03 = h.y, s47 = h.z, s811 = h.w;
+                const uint32_t sc_lo = s03 & 0x3F3F3F3Fu, m_lo = s47 & 0x3F3F3F3Fu;
+                const uint32_t sc_hi = (s811 & 0x0F0F0F0Fu) | ((s03 >> 2) & 0x30303030u);
+                const uint32_t m_hi = ((s811 >> 4) & 0x0F0F0F0Fu) | ((s47 >> 2) & 0x30303030u);
+#pragma unroll
+                for (int j = 0; j < 4; j++) {
+                    sc[j] = byte_u(sc_lo, j);
+                    sc[j + 4] = byte_u(sc_hi, j);
+                    mn[j] = byte_u(m_lo, j);
+                    mn[j + 4] = byte_u(m_hi, j);
+                }
+            }
+            uint8_t *a = sA + (gs & 1) * MMA_A_BYTES;
+#pragma unroll
+            for (int g = 0; g < 4; g++) {
+                const uint4 w0 = raw[1 + 2 * g], w1 = raw[2 + 2 * g];
+                const uint4 lo0 = make_uint4(w0.x & 0x0F0F0F0Fu, w0.y & 0x0F0F0F0Fu, w0.z & 0x0F0F0F0Fu, w0.w & 0x0F0F0F0Fu);
+                const uint4 lo1 = make_uint4(w1.x & 0x0F0F0F0Fu, w1.y & 0x0F0F0F0Fu, w1.z & 0x0F0F0F0Fu, w1.w & 0x0F0F0F0Fu);
+                const uint4 hi0 = make_uint4((w0.x >> 4) & 0x0F0F0F0Fu, (w0.y >> 4) & 0x0F0F0F0Fu, (w0.z >> 4) & 0x0F0F0F0Fu,
+                                             (w0.w >> 4) & 0x0F0F0F0Fu);
+                const uint4 hi1 = make_uint4((w1.x >> 4) & 0x0F0F0F0Fu, (w1.y >> 4) & 0x0F0F0F0Fu, (w1.z >> 4) & 0x0F0F0F0Fu,
+                                             (w1.w >> 4) & 0x0F0F0F0Fu);
+                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g) * 32, 128)) = lo0;
+                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g) * 32 + 16, 128)) = lo1;
+                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g + 1) * 32, 128)) = hi0;
+                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g + 1) * 32 + 16, 128)) = hi1;
+            }
+            fence_proxy_async();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0) {
+#pragma unroll 1
+                for (int j = 0; j < 8; j++)
+                    umma_i8(tmem + (gs & 1) * 256 + j * GM_N,
+                            umma_desc(aBase + (gs & 1) * MMA_A_BYTES + j * 4096, 128, 256),
+                            umma_desc(bBase + (uint32_t)(st * 8 + j) * GM_N * 32, 128, 256), idesc, false);
+                umma_commit(smem_u32(&bars[gs & 1]));
+            }
+            if (st + 1 < nsb) load_raw(st + 1, nxt);
+            if (st > 0 && !__syncthreads_and(epilogue(st - 1, gs - 1))) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                psc[j] = sc[j];
+                pmn[j] = mn[j];
+            }
+            pdw = dw;
+            pdminw = dminw;
+#pragma unroll
+            for (int c = 0; c < 9; c++) raw[c] = nxt[c];
+            tc_fence_before();
+        }
+        if (!ok) break;
+        if (!__syncthreads_and(epilogue(nsb - 1, gstep - 1))) {
+            ok = false;
+            break;
+        }
+        tc_fence_before();
+        const int t0 = tc * GM_N;
+        for (int t = 0; t < tn; t++) {
+            const long long yi = (long long)(t0 + t) * p.y_stride + sg.out_off + row;
+            float r = acc[t];
+            if (p.res) r = __fadd_rn(p.res[(long long)(t0 + t) * p.res_stride + sg.out_off + row], acc[t]);
+            p.y[yi] = r;
+        }
+    }
+    if (!ok && tid == 0) {
+        for (uint32_t b = 0; b < 2; b++) {
+            const long long last = gstep == 0 ? -1 : ((long long)((gstep - 1) & 1) == b ? gstep - 1 : (long long)gstep - 2);
+            if (last >= 0) mbar_wait(&bars[b], (uint32_t)(last >> 1) & 1, nullptr);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+cudaError_t launch_gemv_mma(const GemvArgs &a, int grid, cudaStream_t st, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(128);
+    cfg.dynamicSmemBytes = gemv_mma_smem_bytes(a.K);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, gemv_mma_kernel, a);
+}
+
 cudaError_t init_mma_attributes() {
     int dev = 0, optin = 0;
     cudaError_t e;
     if ((e = cudaGetDevice(&dev))) return e;
     if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
-    cudaFuncAttributes fa;
-    if ((e = cudaFuncGetAttributes(&fa, gateup_mma_kernel))) return e;
-    return cudaFuncSetAttribute(gateup_mma_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                optin - (int)fa.sharedSizeBytes);
+    const void *kerns[] = {(const void *)gateup_mma_kernel, (const void *)gemv_mma_kernel};
+    for (const void *k : kerns) {
+        cudaFuncAttributes fa;
+        if ((e = cudaFuncGetAttributes(&fa, k))) return e;
+        if ((e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, optin - (int)fa.sharedSizeBytes)))
+            return e;
+    }
+    return cudaSuccess;
 }
 
 cudaError_t launch_i8_mma_probe(const uint8_t *A, const int8_t *B, int32_t *D, int N, int K, int *err,
