@@ -84,7 +84,7 @@ size_t gateup_mma_smem_bytes(int E) {
     return 1024 + (size_t)MMA_N * E + 2 * MMA_A_BYTES + (size_t)MMA_N * nsb * sizeof(ActBlock) + 256;
 }
 
-__global__ void __launch_bounds__(128, 1) gateup_mma_kernel(const __grid_constant__ ExpertArgs p) {
+__global__ void __launch_bounds__(256, 1) gateup_mma_kernel(const __grid_constant__ ExpertArgs p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int E = p.E, nsb = E / 256, S = p.g_S;
@@ -95,7 +95,10 @@ __global__ void __launch_bounds__(128, 1) gateup_mma_kernel(const __grid_constan
     int *rows_s = tk_s + MMA_N;                                          // [16]
     uint64_t *bars = reinterpret_cast<uint64_t *>(rows_s + MMA_N);      // [2]
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int tid = threadIdx.x, warp = tid >> 5;
+    // thread (row r of the block, half h): h loads and unpacks nibble groups 2h, 2h+1 of the
+    // row and finishes the epilogue of tokens 8h .. 8h+7
+    const int r = tid & 127, h = tid >> 7;
     if (tid == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
@@ -106,6 +109,7 @@ __global__ void __launch_bounds__(128, 1) gateup_mma_kernel(const __grid_constan
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
+    const uint32_t tlane = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM lanes
     pdl_wait();  // the groups come from group_kernel, the activations from the router
     const int nrb = p.F / 128;
     const int total = *p.g_nchunks * nrb;
@@ -131,9 +135,9 @@ __global__ void __launch_bounds__(128, 1) gateup_mma_kernel(const __grid_constan
                 rows_s[tid] = tk / p.row_div;
             }
             __syncthreads();
-            stage_activations<4>(p.fn, p.E, rows_s, nullptr, 0.0f, p.E, mc, act, nullptr);
+            stage_activations<8>(p.fn, p.E, rows_s, nullptr, 0.0f, p.E, mc, act, nullptr);
             __syncthreads();
-            for (int i = tid; i < MMA_N * E / 16; i += 128) {  // 16-byte pieces of the B operand
+            for (int i = tid; i < MMA_N * E / 16; i += 256) {  // 16-byte pieces of the B operand
                 const int t = i / (E / 16), k = (i - t * (E / 16)) * 16;
                 uint4 v = make_uint4(0, 0, 0, 0);
                 if (t < mc) v = *reinterpret_cast<const uint4 *>(act[t * nsb + k / 256].qs + (k & 255));
@@ -141,20 +145,23 @@ __global__ void __launch_bounds__(128, 1) gateup_mma_kernel(const __grid_constan
             }
         }
         // this thread's row of the block: tile (row / rpt), slot (row % rpt) * nsb + superblock
-        const int row = rb * 128 + tid;
+        const int row = rb * 128 + r;
         const int rpt = p.g_rpt;
         const uint8_t *gbase = expert_gate(p, e) + (long long)(row / rpt) * p.g_tile_bytes;
         const uint8_t *ubase = expert_up(p, e) + (long long)(row / rpt) * p.u_tile_bytes;
         const int slot0 = (row % rpt) * nsb;
-        auto load_raw = [&](int st, uint4 (&w)[9]) {
+        // chunk 0 (header) and this half's four nibble chunks 1 + 4h .. 4 + 4h
+        auto load_raw = [&](int st, uint4 (&w)[5]) {
             const uint8_t *b = (st < nsb ? gbase : ubase) + (size_t)(slot0 + (st < nsb ? st : st - nsb)) * 16;
+            w[0] = __ldg(reinterpret_cast<const uint4 *>(b));
 #pragma unroll
-            for (int c = 0; c < 9; c++) w[c] = __ldg(reinterpret_cast<const uint4 *>(b + (size_t)c * S * 16));
+            for (int c = 0; c < 4; c++)
+                w[1 + c] = __ldg(reinterpret_cast<const uint4 *>(b + (size_t)(1 + 4 * h + c) * S * 16));
         };
-        float acc_g[MMA_N], acc_u[MMA_N];
+        float acc_g[8], acc_u[8];
 #pragma unroll
-        for (int t = 0; t < MMA_N; t++) acc_g[t] = acc_u[t] = 0.0f;
-        uint4 raw[9], nxt[9];
+        for (int t = 0; t < 8; t++) acc_g[t] = acc_u[t] = 0.0f;
+        uint4 raw[5], nxt[5];
         load_raw(0, raw);
         int sc[8], mn[8];
         float dw = 0.0f, dminw = 0.0f;
@@ -165,30 +172,28 @@ __global__ void __launch_bounds__(128, 1) gateup_mma_kernel(const __grid_constan
             if (!mbar_wait(&bars[gs & 1], (gs >> 1) & 1, p.err)) return false;
             tc_fence_after();
             const int sb = st < nsb ? st : st - nsb;
-            int dots[8][MMA_N];
+            int sumi[8];
+#pragma unroll
+            for (int t = 0; t < 8; t++) sumi[t] = 0;
 #pragma unroll
             for (int j = 0; j < 8; j++) {
-                uint32_t v[16];
-                tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (gs & 1) * 128 + j * 16, v);
+                uint32_t v[8];
+                tmem_ld8(tmem + tlane + (gs & 1) * 128 + j * 16 + h * 8, v);
                 tmem_wait_ld();
 #pragma unroll
-                for (int t = 0; t < MMA_N; t++) dots[j][t] = (int)v[t];
+                for (int t = 0; t < 8; t++) sumi[t] += psc[j] * (int)v[t];
             }
 #pragma unroll
-            for (int t = 0; t < MMA_N; t++) {
-                const ActBlock &ab = act[(t < mc ? t : 0) * nsb + sb];
-                const uint4 b0 = *reinterpret_cast<const uint4 *>(ab.bs32);
-                const uint4 b1 = *reinterpret_cast<const uint4 *>(ab.bs32 + 4);
-                const int bs[8] = {(int)b0.x, (int)b0.y, (int)b0.z, (int)b0.w, (int)b1.x, (int)b1.y, (int)b1.z, (int)b1.w};
-                int sumi = 0, summ = 0;
-#pragma unroll
-                for (int j = 0; j < 8; j++) {
-                    sumi += psc[j] * dots[j][t];
-                    summ += pmn[j] * bs[j];
-                }
+            for (int t = 0; t < 8; t++) {
+                const int tt = 8 * h + t;
+                const ActBlock &ab = act[(tt < mc ? tt : 0) * nsb + sb];
+                const int4 b0 = *reinterpret_cast<const int4 *>(ab.bs32);
+                const int4 b1 = *reinterpret_cast<const int4 *>(ab.bs32 + 4);
+                const int summ = pmn[0] * b0.x + pmn[1] * b0.y + pmn[2] * b0.z + pmn[3] * b0.w + pmn[4] * b1.x +
+                                 pmn[5] * b1.y + pmn[6] * b1.z + pmn[7] * b1.w;
                 const float da = ab.d;
                 const float t1 = __fmul_rn(pdw, da);
-                const float t2 = __fmul_rn(__int2float_rn(sumi), t1);
+                const float t2 = __fmul_rn(__int2float_rn(sumi[t]), t1);
                 const float t3 = __fmul_rn(pdminw, da);
                 const float t4 = __fmul_rn(__int2float_rn(summ), t3);
                 const float v = __fsub_rn(t2, t4);
@@ -201,10 +206,10 @@ __global__ void __launch_bounds__(128, 1) gateup_mma_kernel(const __grid_constan
             const uint32_t gs = gstep++;
             // header: d, dmin and the 6-bit scales/mins of this row's superblock (get_scale_min_k4)
             {
-                const uint4 h = raw[0];
-                dw = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffff)));
-                dminw = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
-                const uint32_t s03 = h.y, s47 = h.z, s811 = h.w;
+                const uint4 hd = raw[0];
+                dw = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff)));
+                dminw = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+                const uint32_t s03 = hd.y, s47 = hd.z, s811 = hd.w;
                 const uint32_t sc_lo = s03 & 0x3F3F3F3Fu, m_lo = s47 & 0x3F3F3F3Fu;
                 const uint32_t sc_hi = (s811 & 0x0F0F0F0Fu) | ((s03 >> 2) & 0x30303030u);
                 const uint32_t m_hi = ((s811 >> 4) & 0x0F0F0F0Fu) | ((s47 >> 2) & 0x30303030u);
@@ -216,22 +221,22 @@ __global__ void __launch_bounds__(128, 1) gateup_mma_kernel(const __grid_constan
                     mn[j + 4] = byte_u(m_hi, j);
                 }
             }
-            // the A operand of this step: sub-block 2g = low nibbles, 2g + 1 = high nibbles of
-            // the 32 bytes of group g; row `tid`, K step j at j * 4096
+            // the A operand: nibble group g = 2h + gg; sub-block 2g = low nibbles, 2g + 1 = high
             uint8_t *a = sA + (gs & 1) * MMA_A_BYTES;
 #pragma unroll
-            for (int g = 0; g < 4; g++) {
-                const uint4 w0 = raw[1 + 2 * g], w1 = raw[2 + 2 * g];
+            for (int gg = 0; gg < 2; gg++) {
+                const int g = 2 * h + gg;
+                const uint4 w0 = raw[1 + 2 * gg], w1 = raw[2 + 2 * gg];
                 const uint4 lo0 = make_uint4(w0.x & 0x0F0F0F0Fu, w0.y & 0x0F0F0F0Fu, w0.z & 0x0F0F0F0Fu, w0.w & 0x0F0F0F0Fu);
                 const uint4 lo1 = make_uint4(w1.x & 0x0F0F0F0Fu, w1.y & 0x0F0F0F0Fu, w1.z & 0x0F0F0F0Fu, w1.w & 0x0F0F0F0Fu);
                 const uint4 hi0 = make_uint4((w0.x >> 4) & 0x0F0F0F0Fu, (w0.y >> 4) & 0x0F0F0F0Fu, (w0.z >> 4) & 0x0F0F0F0Fu,
                                              (w0.w >> 4) & 0x0F0F0F0Fu);
                 const uint4 hi1 = make_uint4((w1.x >> 4) & 0x0F0F0F0Fu, (w1.y >> 4) & 0x0F0F0F0Fu, (w1.z >> 4) & 0x0F0F0F0Fu,
                                              (w1.w >> 4) & 0x0F0F0F0Fu);
-                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g) * 32, 128)) = lo0;
-                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g) * 32 + 16, 128)) = lo1;
-                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g + 1) * 32, 128)) = hi0;
-                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g + 1) * 32 + 16, 128)) = hi1;
+                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g) * 32, 128)) = lo0;
+                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g) * 32 + 16, 128)) = lo1;
+                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g + 1) * 32, 128)) = hi0;
+                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g + 1) * 32 + 16, 128)) = hi1;
             }
             fence_proxy_async();
             tc_fence_before();
@@ -259,7 +264,7 @@ __global__ void __launch_bounds__(128, 1) gateup_mma_kernel(const __grid_constan
             pdw = dw;
             pdminw = dminw;
 #pragma unroll
-            for (int c = 0; c < 9; c++) raw[c] = nxt[c];
+            for (int c = 0; c < 5; c++) raw[c] = nxt[c];
             tc_fence_before();
         }
         if (!ok) break;
@@ -269,7 +274,9 @@ __global__ void __launch_bounds__(128, 1) gateup_mma_kernel(const __grid_constan
         }
         tc_fence_before();
         if (row < p.F)
-            for (int t = 0; t < mc; t++) p.act[(long long)tk_s[t] * p.F + row] = __fmul_rn(bt_silu(acc_g[t]), acc_u[t]);
+            for (int t = 0; t < 8; t++)
+                if (8 * h + t < mc)
+                    p.act[(long long)tk_s[8 * h + t] * p.F + row] = __fmul_rn(bt_silu(acc_g[t]), acc_u[t]);
     }
     if (!ok && tid == 0) {  // let this CTA's MMAs in flight finish (bounded) before the TMEM goes
         for (uint32_t b = 0; b < 2; b++) {
@@ -287,7 +294,7 @@ cudaError_t launch_gateup_mma(const ExpertArgs &a, int grid, cudaStream_t st, bo
     const size_t smem = gateup_mma_smem_bytes(a.E);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(128);
+    cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
