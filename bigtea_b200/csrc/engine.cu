@@ -1168,7 +1168,13 @@ static int run_gemv_batched(bt_engine *e, const QMat *const *mats, const int *of
                             const float *res, long long res_stride, const char *name, const PrefetchSpec *pf) {
     const QMat *mm[3], *dm[3];
     int mo[3], dof[3], nm = 0, nd = 0;
-    const bool mma_ok = e->mma && gemv_mma_smem_bytes(K) <= (size_t)max_dynamic_smem();
+    // the tensor-core kernel's units are (32 tokens, 128 rows), one CTA per SM: it pays when
+    // they cover at least half of the SMs
+    long long units = 0;
+    for (int i = 0; i < nseg; i++)
+        if (mats[i]->type == T_Q4_K && mats[i]->rows % 128 == 0) units += (long long)(mats[i]->rows / 128);
+    units *= (T + 31) / 32;
+    const bool mma_ok = e->mma && gemv_mma_smem_bytes(K) <= (size_t)max_dynamic_smem() && 2 * units >= e->n_sm;
     for (int i = 0; i < nseg; i++) {
         if (mma_ok && mats[i]->type == T_Q4_K && mats[i]->rows % 128 == 0) {
             mm[nm] = mats[i];

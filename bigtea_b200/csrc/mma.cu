@@ -319,11 +319,11 @@ constexpr int GM_N = 32;
 
 size_t gemv_mma_smem_bytes(int K) {
     const size_t nsb = (size_t)K / 256;
-    return 1024 + (size_t)GM_N * K + (size_t)GM_N * nsb * (4 + 32) + 4 * sizeof(ActBlock) + 2 * MMA_A_BYTES +
+    return 1024 + (size_t)GM_N * K + (size_t)GM_N * nsb * (4 + 32) + 8 * sizeof(ActBlock) + 2 * MMA_A_BYTES +
            GM_N * 4 + 256;
 }
 
-__global__ void __launch_bounds__(128, 1) gemv_mma_kernel(const __grid_constant__ GemvArgs p) {
+__global__ void __launch_bounds__(256, 1) gemv_mma_kernel(const __grid_constant__ GemvArgs p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int K = p.K, nsb = K / 256;
@@ -331,11 +331,15 @@ __global__ void __launch_bounds__(128, 1) gemv_mma_kernel(const __grid_constant_
     uint8_t *sB = sA + 2 * MMA_A_BYTES;                                  // [K/32 steps][32 rows][32]
     float *dA = reinterpret_cast<float *>(sB + (size_t)GM_N * K);        // [32][nsb]
     int *bsA = reinterpret_cast<int *>(dA + GM_N * nsb);                 // [32][nsb][8]
-    ActBlock *tmp = reinterpret_cast<ActBlock *>(bsA + GM_N * nsb * 8);  // [4] one per warp
-    float *normS = reinterpret_cast<float *>(tmp + 4);                   // [32]
+    ActBlock *tmp = reinterpret_cast<ActBlock *>(bsA + GM_N * nsb * 8);  // [8] one per warp
+    float *normS = reinterpret_cast<float *>(tmp + 8);                   // [32]
     uint64_t *bars = reinterpret_cast<uint64_t *>(normS + GM_N);         // [2]
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // thread (row r of the block, half h): h unpacks nibble groups 2h, 2h+1 of the row and
+    // finishes the epilogue of tokens 16h .. 16h+15
+    const int r = tid & 127, h = tid >> 7;
+    const uint32_t tlane = (uint32_t)((warp & 3) * 32) << 16;
     if (tid == 0) {
         mbar_init(&bars[0], 1);
         mbar_init(&bars[1], 1);
@@ -373,14 +377,14 @@ __global__ void __launch_bounds__(128, 1) gemv_mma_kernel(const __grid_constant_
             tn = p.T - t0 < GM_N ? p.T - t0 : GM_N;
             __syncthreads();  // the previous chunk's operands are no longer read
             if (p.norm_w) {
-                for (int t = warp; t < tn; t += 4) {
+                for (int t = warp; t < tn; t += 8) {
                     const float *xt = p.x + (long long)(p.x_rows ? p.x_rows[t0 + t] : t0 + t) * p.x_stride;
                     const float acc = warp_sumsq_p2(xt, K, lane);
                     if (lane == 0) normS[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)K), p.eps)));
                 }
                 __syncthreads();
             }
-            for (int blk = warp; blk < GM_N * nsb; blk += 4) {
+            for (int blk = warp; blk < GM_N * nsb; blk += 8) {
                 const int t = blk / nsb, b = blk - t * nsb;
                 uint2 q8 = make_uint2(0, 0);
                 float dv = 0.0f;
@@ -412,50 +416,51 @@ __global__ void __launch_bounds__(128, 1) gemv_mma_kernel(const __grid_constant_
             }
         }
         // this thread's row: tile row / rpt of the segment, slot (row % rpt) * nsb + superblock
-        const int row = rb * 128 + tid;
+        const int row = rb * 128 + r;
         const uint8_t *wbase = sg.w + (long long)(row / sg.rpt) * sg.tile_bytes;
         const int slot0 = (row % sg.rpt) * nsb, S = sg.S;
-        auto load_raw = [&](int st, uint4 (&w)[9]) {
+        auto load_raw = [&](int st, uint4 (&w)[5]) {  // header and this half's four nibble chunks
             const uint8_t *b = wbase + (size_t)(slot0 + st) * 16;
+            w[0] = __ldg(reinterpret_cast<const uint4 *>(b));
 #pragma unroll
-            for (int c = 0; c < 9; c++) w[c] = __ldg(reinterpret_cast<const uint4 *>(b + (size_t)c * S * 16));
+            for (int c = 0; c < 4; c++)
+                w[1 + c] = __ldg(reinterpret_cast<const uint4 *>(b + (size_t)(1 + 4 * h + c) * S * 16));
         };
-        float acc[GM_N];
+        constexpr int HT = GM_N / 2;  // tokens per half
+        float acc[HT];
 #pragma unroll
-        for (int t = 0; t < GM_N; t++) acc[t] = 0.0f;
-        uint4 raw[9], nxt[9];
+        for (int t = 0; t < HT; t++) acc[t] = 0.0f;
+        uint4 raw[5], nxt[5];
         load_raw(0, raw);
         int sc[8], mn[8], psc[8], pmn[8];
         float dw = 0.0f, dminw = 0.0f, pdw = 0.0f, pdminw = 0.0f;
         auto epilogue = [&](int sb, uint32_t gs) -> bool {
             if (!mbar_wait(&bars[gs & 1], (gs >> 1) & 1, p.err)) return false;
             tc_fence_after();
-            int sumi[GM_N];
+            int sumi[HT];
 #pragma unroll
-            for (int t = 0; t < GM_N; t++) sumi[t] = 0;
+            for (int t = 0; t < HT; t++) sumi[t] = 0;
 #pragma unroll
             for (int j = 0; j < 8; j++) {
+                uint32_t v[16];
+                tmem_ld16(tmem + tlane + (gs & 1) * 256 + j * GM_N + h * HT, v);
+                tmem_wait_ld();
 #pragma unroll
-                for (int h = 0; h < GM_N / 16; h++) {
-                    uint32_t v[16];
-                    tmem_ld16(tmem + ((uint32_t)(warp * 32) << 16) + (gs & 1) * 256 + j * GM_N + h * 16, v);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int t = 0; t < 16; t++) sumi[h * 16 + t] += psc[j] * (int)v[t];
-                }
+                for (int t = 0; t < HT; t++) sumi[t] += psc[j] * (int)v[t];
             }
 #pragma unroll
-            for (int t = 0; t < GM_N; t++) {
+            for (int tt = 0; tt < HT; tt++) {
+                const int t = HT * h + tt;
                 const int4 b0 = *reinterpret_cast<const int4 *>(bsA + (t * nsb + sb) * 8);
                 const int4 b1 = *reinterpret_cast<const int4 *>(bsA + (t * nsb + sb) * 8 + 4);
                 const int summ = pmn[0] * b0.x + pmn[1] * b0.y + pmn[2] * b0.z + pmn[3] * b0.w + pmn[4] * b1.x +
                                  pmn[5] * b1.y + pmn[6] * b1.z + pmn[7] * b1.w;
                 const float da = dA[t * nsb + sb];
                 const float t1 = __fmul_rn(pdw, da);
-                const float t2 = __fmul_rn(__int2float_rn(sumi[t]), t1);
+                const float t2 = __fmul_rn(__int2float_rn(sumi[tt]), t1);
                 const float t3 = __fmul_rn(pdminw, da);
                 const float t4 = __fmul_rn(__int2float_rn(summ), t3);
-                acc[t] = __fadd_rn(acc[t], __fsub_rn(t2, t4));
+                acc[tt] = __fadd_rn(acc[tt], __fsub_rn(t2, t4));
             }
             return true;
         };
@@ -479,18 +484,19 @@ __global__ void __launch_bounds__(128, 1) gemv_mma_kernel(const __grid_constant_
             }
             uint8_t *a = sA + (gs & 1) * MMA_A_BYTES;
 #pragma unroll
-            for (int g = 0; g < 4; g++) {
-                const uint4 w0 = raw[1 + 2 * g], w1 = raw[2 + 2 * g];
+            for (int gg = 0; gg < 2; gg++) {
+                const int g = 2 * h + gg;
+                const uint4 w0 = raw[1 + 2 * gg], w1 = raw[2 + 2 * gg];
                 const uint4 lo0 = make_uint4(w0.x & 0x0F0F0F0Fu, w0.y & 0x0F0F0F0Fu, w0.z & 0x0F0F0F0Fu, w0.w & 0x0F0F0F0Fu);
                 const uint4 lo1 = make_uint4(w1.x & 0x0F0F0F0Fu, w1.y & 0x0F0F0F0Fu, w1.z & 0x0F0F0F0Fu, w1.w & 0x0F0F0F0Fu);
                 const uint4 hi0 = make_uint4((w0.x >> 4) & 0x0F0F0F0Fu, (w0.y >> 4) & 0x0F0F0F0Fu, (w0.z >> 4) & 0x0F0F0F0Fu,
                                              (w0.w >> 4) & 0x0F0F0F0Fu);
                 const uint4 hi1 = make_uint4((w1.x >> 4) & 0x0F0F0F0Fu, (w1.y >> 4) & 0x0F0F0F0Fu, (w1.z >> 4) & 0x0F0F0F0Fu,
                                              (w1.w >> 4) & 0x0F0F0F0Fu);
-                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g) * 32, 128)) = lo0;
-                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g) * 32 + 16, 128)) = lo1;
-                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g + 1) * 32, 128)) = hi0;
-                *reinterpret_cast<uint4 *>(a + umma_off(tid, (2 * g + 1) * 32 + 16, 128)) = hi1;
+                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g) * 32, 128)) = lo0;
+                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g) * 32 + 16, 128)) = lo1;
+                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g + 1) * 32, 128)) = hi0;
+                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g + 1) * 32 + 16, 128)) = hi1;
             }
             fence_proxy_async();
             tc_fence_before();
@@ -517,7 +523,7 @@ __global__ void __launch_bounds__(128, 1) gemv_mma_kernel(const __grid_constant_
             pdw = dw;
             pdminw = dminw;
 #pragma unroll
-            for (int c = 0; c < 9; c++) raw[c] = nxt[c];
+            for (int c = 0; c < 5; c++) raw[c] = nxt[c];
             tc_fence_before();
         }
         if (!ok) break;
@@ -526,12 +532,12 @@ __global__ void __launch_bounds__(128, 1) gemv_mma_kernel(const __grid_constant_
             break;
         }
         tc_fence_before();
-        const int t0 = tc * GM_N;
-        for (int t = 0; t < tn; t++) {
+        const int t0 = tc * GM_N + HT * h;
+        for (int t = 0; t < HT && HT * h + t < tn; t++) {
             const long long yi = (long long)(t0 + t) * p.y_stride + sg.out_off + row;
-            float r = acc[t];
-            if (p.res) r = __fadd_rn(p.res[(long long)(t0 + t) * p.res_stride + sg.out_off + row], acc[t]);
-            p.y[yi] = r;
+            float y = acc[t];
+            if (p.res) y = __fadd_rn(p.res[(long long)(t0 + t) * p.res_stride + sg.out_off + row], acc[t]);
+            p.y[yi] = y;
         }
     }
     if (!ok && tid == 0) {
@@ -548,7 +554,7 @@ __global__ void __launch_bounds__(128, 1) gemv_mma_kernel(const __grid_constant_
 cudaError_t launch_gemv_mma(const GemvArgs &a, int grid, cudaStream_t st, bool pdl) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(128);
+    cfg.blockDim = dim3(256);
     cfg.dynamicSmemBytes = gemv_mma_smem_bytes(a.K);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
