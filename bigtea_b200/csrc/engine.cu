@@ -116,6 +116,8 @@ struct bt_engine {
     int TB = 64;
     int max_out = 0;
     DevBuf x, ffn_in, fn, qkv, qbuf, att, rlog, rcnt, sel_ids, sel_w, act, part, acnt;
+    DevBuf q8_qs, q8_d, q8_bs;  // activation rows as Q8_K for the tensor-core kernels (q8_rows x q8_k)
+    size_t q8_rows = 0, q8_k = 0;
     DevBuf g_count, g_off, g_list, g_active, g_nactive, dpart;  // grouped experts of batched steps
     DevBuf g_chunk_e, g_chunk_r0, g_nchunks;
     DevBuf sh_gu, sh_act, sh_out;  // the shared expert: [TB][2F] gate|up, [TB][F] silu*up, [TB][E] rows
@@ -126,6 +128,8 @@ struct bt_engine {
     int ep_timeout_ms = 60000;  // a host wait on an expert-parallel step longer than this aborts the exchange
     bool ep_aborted = false;
     bool mma = true;  // grouped Q4_K gate/up on tcgen05 (option "mma")
+    int mma_min_units = 32;  // batched GEMVs on tcgen05 from this many (tokens, rows) units on (option)
+    int mma_grid = 0;        // CTAs of the tensor-core kernels (0: one per SM; option, for tests)
     // expert cache: experts in pinned host memory, the ones a layer selects copied into slots
     // of a device pool before its expert kernels (bt_engine_enable_expert_cache)
     bool xcache = false;
@@ -417,12 +421,27 @@ static int wait_stream(bt_engine *e) {
     }
 }
 
+// Q8_K activation rows for the tensor-core kernels: `rows` rows of up to max(hidden, heads x
+// head_dim) values.
+static cudaError_t alloc_q8(bt_engine *e, size_t rows) {
+    const size_t K = std::max<size_t>(e->d.n_embd, (size_t)e->d.n_head * e->d.head_dim), nsb = K / 256;
+    if (rows <= e->q8_rows && K <= e->q8_k) return cudaSuccess;
+    cudaError_t r;
+    if ((r = e->q8_qs.alloc(rows * K))) return r;
+    if ((r = e->q8_d.alloc(rows * nsb * 4))) return r;
+    if ((r = e->q8_bs.alloc(rows * nsb * 8 * 4))) return r;
+    e->q8_rows = rows;
+    e->q8_k = K;
+    return cudaSuccess;
+}
+
 static int alloc_scratch(bt_engine *e) {
     const bt_model_desc &d = e->d;
     const int TB = e->TB, E = d.n_embd, QW = d.n_head * d.head_dim, KW = d.n_head_kv * d.head_dim;
     const int K = d.n_expert_used, NE = d.n_expert, F = d.n_ff_exp, G = d.n_head / d.n_head_kv;
     e->part_chunks = (int)((d.max_positions + ATTN_CHUNK - 1) / ATTN_CHUNK);
     e->max_out = 256;
+    CK(alloc_q8(e, (size_t)TB));
     CK(e->x.alloc((size_t)TB * E * 4));
     CK(e->ffn_in.alloc((size_t)TB * E * 4));
     CK(e->fn.alloc((size_t)TB * E * 4));
@@ -1168,13 +1187,15 @@ static int run_gemv_batched(bt_engine *e, const QMat *const *mats, const int *of
                             const float *res, long long res_stride, const char *name, const PrefetchSpec *pf) {
     const QMat *mm[3], *dm[3];
     int mo[3], dof[3], nm = 0, nd = 0;
-    // the tensor-core kernel's units are (32 tokens, 128 rows), one CTA per SM: it pays when
-    // they cover at least half of the SMs
+    // the tensor-core kernel's units are (N tokens, 128 rows), one CTA per SM: it pays once
+    // they cover mma_min_units CTAs
+    const int gn = gemv_mma_tokens(K);
     long long units = 0;
     for (int i = 0; i < nseg; i++)
         if (mats[i]->type == T_Q4_K && mats[i]->rows % 128 == 0) units += (long long)(mats[i]->rows / 128);
-    units *= (T + 31) / 32;
-    const bool mma_ok = e->mma && gemv_mma_smem_bytes(K) <= (size_t)max_dynamic_smem() && 2 * units >= e->n_sm;
+    units *= gn ? (T + gn - 1) / gn : 0;
+    const bool mma_ok = e->mma && gn && gemv_mma_smem_bytes(K) <= (size_t)max_dynamic_smem() &&
+                        units >= e->mma_min_units && (size_t)T <= e->q8_rows;
     for (int i = 0; i < nseg; i++) {
         if (mma_ok && mats[i]->type == T_Q4_K && mats[i]->rows % 128 == 0) {
             mm[nm] = mats[i];
@@ -1204,8 +1225,15 @@ static int run_gemv_batched(bt_engine *e, const QMat *const *mats, const int *of
         a.res = res;
         a.res_stride = res_stride;
         a.err = e->err.as<int>();
+        a.q8_qs = e->q8_qs.as<int8_t>();
+        a.q8_d = e->q8_d.as<float>();
+        a.q8_bs = e->q8_bs.as<int>();
         timer_begin(e, name);
-        cudaError_t ce = launch_gemv_mma(a, e->n_sm, e->st, e->pdl);
+        cudaError_t ce = (size_t)T > e->q8_rows ? cudaErrorInvalidValue
+                                                : launch_q8_stage(x, x_stride, nullptr, norm_w, e->d.rms_eps, K, T,
+                                                                  e->q8_qs.as<int8_t>(), e->q8_d.as<float>(),
+                                                                  e->q8_bs.as<int>(), e->st, e->pdl);
+        if (ce == cudaSuccess) ce = launch_gemv_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, e->st, e->pdl);
         timer_end(e);
         CK(ce);
     }
@@ -1377,9 +1405,18 @@ static int xcache_layer(bt_engine *e, int il, int T) {
 
 // The tensor-core gate/up of the grouped path: Q4_K gate and up, whole 128-row blocks, and
 // shared memory for the chunk's operands.
-static bool use_gateup_mma(const bt_engine *e, const Layer &l) {
+// The gate/up input rows (a.fn, `rows` of them) as Q8_K rows for the tensor-core gate/up.
+static cudaError_t stage_gateup_q8(bt_engine *e, ExpertArgs &a, int rows, cudaStream_t st, bool pdl) {
+    a.q8_qs = e->q8_qs.as<int8_t>();
+    a.q8_d = e->q8_d.as<float>();
+    a.q8_bs = e->q8_bs.as<int>();
+    return launch_q8_stage(a.fn, a.E, nullptr, nullptr, 0.0f, a.E, rows, e->q8_qs.as<int8_t>(), e->q8_d.as<float>(),
+                           e->q8_bs.as<int>(), st, pdl);
+}
+
+static bool use_gateup_mma(const bt_engine *e, const Layer &l, size_t rows) {
     return e->mma && l.gate.type == T_Q4_K && l.up.type == T_Q4_K && e->d.n_ff_exp % 128 == 0 &&
-           gateup_mma_smem_bytes((int)e->d.n_embd) <= (size_t)max_dynamic_smem();
+           gateup_mma_smem_bytes((int)e->d.n_embd) <= (size_t)max_dynamic_smem() && rows <= e->q8_rows;
 }
 
 static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) {
@@ -1652,8 +1689,10 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.nst = 1;
             a.nst = pick_nst_cap(a.slot_bytes, gateup_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
             timer_begin(e, "expert_gateup");
-            if (use_gateup_mma(e, l))
-                CK(launch_gateup_mma(a, e->n_sm, st, pdl));
+            if (use_gateup_mma(e, l, (size_t)n * S)) {
+                CK(stage_gateup_q8(e, a, n * S, st, pdl));
+                CK(launch_gateup_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, st, pdl));
+            }
             else
                 CK(launch_gateup_grouped(a, e->n_sm, st, pdl));
             timer_end(e);
@@ -1751,8 +1790,10 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.nst = 1;
             a.nst = pick_nst_cap(a.slot_bytes, gateup_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
             timer_begin(e, "expert_gateup");
-            if (use_gateup_mma(e, l))
-                CK(launch_gateup_mma(a, e->n_sm, st, pdl));
+            if (use_gateup_mma(e, l, (size_t)T)) {
+                CK(stage_gateup_q8(e, a, T, st, pdl));
+                CK(launch_gateup_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, st, pdl));
+            }
             else
                 CK(launch_gateup_grouped(a, e->n_sm, st, pdl));
             timer_end(e);
@@ -2392,6 +2433,7 @@ extern "C" int bt_engine_enable_ep(bt_engine *e, const void *unique_id, size_t n
     CK(e->ep_recv_meta.alloc(n * S * 4));
     CK(e->ep_send_rows.alloc(n * S * E * 4));
     CK(e->ep_recv_rows.alloc(n * S * E * 4));
+    CK(alloc_q8(e, (size_t)n * S));
     CK(e->ep_act.alloc(n * S * F * 4));
     CK(e->ep_dpart.alloc(n * S * E * 4));
     CK(e->ep_ret.alloc(n * S * E * 4));
@@ -2440,6 +2482,20 @@ extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
     }
     if (!strcmp(name, "mma")) {
         e->mma = value != 0;
+        for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
+        e->graphs.clear();
+        return BT_OK;
+    }
+    if (!strcmp(name, "mma_grid")) {
+        if (value < 0) return fail(BT_ERR_INVALID, "mma_grid must be >= 0");
+        e->mma_grid = value;
+        for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
+        e->graphs.clear();
+        return BT_OK;
+    }
+    if (!strcmp(name, "mma_min_units")) {
+        if (value < 1) return fail(BT_ERR_INVALID, "mma_min_units must be positive");
+        e->mma_min_units = value;
         for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
         e->graphs.clear();
         return BT_OK;

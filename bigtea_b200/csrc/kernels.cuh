@@ -53,6 +53,11 @@ struct GemvArgs {
     int slot_bytes, nst;
     unsigned long long *amax;  // optional: per token, max of (total_cmp key, row) over the output
     PrefetchSpec pf;
+    // the activations as Q8_K rows (q8_stage_kernel): [T][K] values, [T][K/256] scales,
+    // [T][K/256][8] 32-value sums; read by the tensor-core GEMV
+    const int8_t *q8_qs;
+    const float *q8_d;
+    const int *q8_bs;
 };
 
 struct ExpertArgs {
@@ -79,6 +84,9 @@ struct ExpertArgs {
     const int *g_chunk_e, *g_chunk_r0, *g_nchunks;  // the chunks of at most GROUP_MAXM rows
     float *dpart;  // [T][K][E] each (token, expert slot)'s down rows before the expert sum
     int row_div;   // grouped gate/up: the activation row of list entry i is i / row_div
+    const int8_t *q8_qs;  // fn as Q8_K rows (q8_stage_kernel), read by the tensor-core gate/up
+    const float *q8_d;
+    const int *q8_bs;
     // expert parallelism: the combine reads slot (t, k) of the rank owning expert sel_ids[t*K+k]
     // from dpart[(owner * ep_slots + t*K + k) * E]; ep_ranks = 0 outside expert parallelism
     int ep_ranks, ep_per, ep_slots;
@@ -220,6 +228,11 @@ cudaError_t launch_gateup_mma(const ExpertArgs &a, int grid, cudaStream_t st, bo
 cudaError_t init_mma_attributes();
 // batched GEMV on tcgen05 (Q4_K segments of whole 128-row blocks, no argmax); one CTA per SM
 size_t gemv_mma_smem_bytes(int K);
+int gemv_mma_tokens(int K);
+// T rows of K activations (row t = x_rows[t] or t; RMSNorm first when norm_w) as Q8_K rows:
+// qs [T][K], d [T][K/256], bs [T][K/256][8] (C3/C6, the dp4a kernels' staging bit for bit)
+cudaError_t launch_q8_stage(const float *x, long long x_stride, const int *x_rows, const float *norm_w, float eps, int K,
+                            int T, int8_t *qs, float *d, int *bs, cudaStream_t st, bool pdl);  // tokens per unit of the batched tensor-core GEMV (32 or 16; 0: does not fit)
 cudaError_t launch_gemv_mma(const GemvArgs &a, int grid, cudaStream_t st, bool pdl);
 // act[t][j] = silu(gu[t][j]) * gu[t][F + j] for the shared expert (C7)
 cudaError_t launch_shexp_act(const float *gu, float *act, int T, int F, cudaStream_t st, bool pdl);

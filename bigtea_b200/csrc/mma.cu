@@ -63,9 +63,9 @@ size_t i8_mma_probe_smem(int N, int K) { return (size_t)(128 + N) * K + 16; }
 // expert, block of 128 output rows); CTA b takes units [b*U/grid, (b+1)*U/grid), chunk-major,
 // so consecutive units share the chunk's staged activations. Per unit, 16 steps (gate then
 // up, superblock 0..7):
-//   - thread r (= output row r of the block, = TMEM lane r) loads its row's 144-byte
-//     superblock (header + 128 bytes of nibbles) straight from the tiled weights, one step
-//     ahead, and unpacks the nibbles into the 8-bit A operand (8 sub-blocks x 128 rows x 32);
+//   - thread r (= output row r of the block, = TMEM lane r) takes its row's 144-byte
+//     superblock (header + 128 bytes of nibbles) from the raw-weight ring and unpacks the
+//     nibbles into the 8-bit A operand (8 sub-blocks x 128 rows x 32);
 //   - one thread issues 8 MMAs (M = 128, N = 16, K = 32: one per 32-value sub-block, each into
 //     its own 16 TMEM columns) against the chunk's Q8_K activations (the B operand) and
 //     commits them to the step's mbarrier;
@@ -73,15 +73,101 @@ size_t i8_mma_probe_smem(int N, int K) { return (size_t)(128 + N) * K + 16; }
 //     finishes C4 per (row, token): sumi = sum sc_j dot_j, summ = sum m_j bs32_j, then
 //     (float)sumi * (d * d_a) - (float)summ * (dmin * d_a), added to the row's running sum in
 //     superblock order -- the integers are exact, so the result equals the dp4a kernels' bits.
-// A and TMEM are double-buffered by step parity. Every wait is bounded; on a timeout the CTA
-// waits (bounded) for its MMAs in flight, frees its TMEM and leaves.
+// The raw-weight ring: each thread copies its own 5 x 16 bytes of a step (the header and the
+// four nibble chunks of its half) with cp.async RAW_D steps ahead, across unit boundaries, so
+// the weight stream does not wait for a DRAM round trip per step. The chunk's activations come
+// as Q8_K rows quantised once per step by q8_stage_kernel and are copied in with cp.async. A and
+// TMEM are double-buffered by step parity. Every wait is bounded; on a timeout the CTA waits
+// (bounded) for its MMAs in flight, frees its TMEM and leaves.
 constexpr int MMA_N = 16;                     // tokens per MMA (the chunk, zero-padded)
 constexpr int MMA_A_BYTES = 8 * 128 * 32;     // one superblock of 128 rows, 8 K steps
 constexpr int MMA_TMEM_COLS = 256;            // 2 buffers x 8 sub-blocks x 16 tokens
+constexpr int RAW_D = 3, RAW_R = RAW_D + 1;   // ring: steps in flight ahead, stages
+constexpr int RAW_CHUNK = 256 * 16;           // one 16-byte piece per thread
+constexpr int RAW_STAGE = 5 * RAW_CHUNK;      // header + four nibble chunks per thread
+constexpr size_t MMA_SMEM_LIMIT = 230400;     // sm_100 opt-in per block less the engine's 2 KB headroom
 
 size_t gateup_mma_smem_bytes(int E) {
     const size_t nsb = (size_t)E / 256;
-    return 1024 + (size_t)MMA_N * E + 2 * MMA_A_BYTES + (size_t)MMA_N * nsb * sizeof(ActBlock) + 256;
+    return 1024 + (size_t)MMA_N * E + 2 * MMA_A_BYTES + (size_t)RAW_R * RAW_STAGE + (size_t)MMA_N * nsb * (4 + 32) +
+           2 * MMA_N * 4 + 256;
+}
+
+// 8 or 16 consecutive TMEM columns of this warp's lanes
+template <int HT>
+__device__ __forceinline__ void tmem_ld_cols(uint32_t taddr, uint32_t (&v)[HT]) {
+    if constexpr (HT == 16) tmem_ld16(taddr, v);
+    else tmem_ld8(taddr, v);
+}
+
+// The C4 epilogue of one step for HT tokens of this thread's row: the 8 sub-block integer
+// dots of token t at TMEM column col0 + j * jstride + t, loaded JB sub-blocks per wait.
+template <int HT>
+__device__ __forceinline__ void tmem_sumi(uint32_t col0, int jstride, const int (&psc)[8], int (&sumi)[HT]) {
+    constexpr int JB = HT == 16 ? 2 : 4;
+#pragma unroll
+    for (int t = 0; t < HT; t++) sumi[t] = 0;
+#pragma unroll
+    for (int j0 = 0; j0 < 8; j0 += JB) {
+        uint32_t v[JB][HT];
+#pragma unroll
+        for (int jj = 0; jj < JB; jj++) tmem_ld_cols<HT>(col0 + (uint32_t)((j0 + jj) * jstride), v[jj]);
+        tmem_wait_ld();
+#pragma unroll
+        for (int jj = 0; jj < JB; jj++) tmem_pin(v[jj]);
+#pragma unroll
+        for (int jj = 0; jj < JB; jj++)
+#pragma unroll
+            for (int t = 0; t < HT; t++) sumi[t] += psc[j0 + jj] * (int)v[jj][t];
+    }
+}
+
+// Header of a Q4_K superblock (get_scale_min_k4): d, dmin and the 6-bit scales and mins.
+__device__ __forceinline__ void q4k_header(const uint4 hd, float &dw, float &dminw, int (&sc)[8], int (&mn)[8]) {
+    dw = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff)));
+    dminw = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
+    const uint32_t s03 = hd.y, s47 = hd.z, s811 = hd.w;
+    const uint32_t sc_lo = s03 & 0x3F3F3F3Fu, m_lo = s47 & 0x3F3F3F3Fu;
+    const uint32_t sc_hi = (s811 & 0x0F0F0F0Fu) | ((s03 >> 2) & 0x30303030u);
+    const uint32_t m_hi = ((s811 >> 4) & 0x0F0F0F0Fu) | ((s47 >> 2) & 0x30303030u);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+        sc[j] = byte_u(sc_lo, j);
+        sc[j + 4] = byte_u(sc_hi, j);
+        mn[j] = byte_u(m_lo, j);
+        mn[j + 4] = byte_u(m_hi, j);
+    }
+}
+
+// The A operand of one step: nibble groups 2h, 2h+1 of row r (sub-block 2g = low nibbles,
+// 2g + 1 = high) from the four 16-byte chunks raw[1..4].
+__device__ __forceinline__ void q4k_unpack_a(uint8_t *a, const uint4 (&raw)[5], int r, int h) {
+#pragma unroll
+    for (int gg = 0; gg < 2; gg++) {
+        const int g = 2 * h + gg;
+        const uint4 w0 = raw[1 + 2 * gg], w1 = raw[2 + 2 * gg];
+        const uint4 lo0 = make_uint4(w0.x & 0x0F0F0F0Fu, w0.y & 0x0F0F0F0Fu, w0.z & 0x0F0F0F0Fu, w0.w & 0x0F0F0F0Fu);
+        const uint4 lo1 = make_uint4(w1.x & 0x0F0F0F0Fu, w1.y & 0x0F0F0F0Fu, w1.z & 0x0F0F0F0Fu, w1.w & 0x0F0F0F0Fu);
+        const uint4 hi0 = make_uint4((w0.x >> 4) & 0x0F0F0F0Fu, (w0.y >> 4) & 0x0F0F0F0Fu, (w0.z >> 4) & 0x0F0F0F0Fu,
+                                     (w0.w >> 4) & 0x0F0F0F0Fu);
+        const uint4 hi1 = make_uint4((w1.x >> 4) & 0x0F0F0F0Fu, (w1.y >> 4) & 0x0F0F0F0Fu, (w1.z >> 4) & 0x0F0F0F0Fu,
+                                     (w1.w >> 4) & 0x0F0F0F0Fu);
+        *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g) * 32, 128)) = lo0;
+        *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g) * 32 + 16, 128)) = lo1;
+        *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g + 1) * 32, 128)) = hi0;
+        *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g + 1) * 32 + 16, 128)) = hi1;
+    }
+}
+
+// Step q's 5 x 16 bytes of this thread: from the ring (after waiting for its copies), then the
+// copies of step q + RAW_D go out into the stage step q - 1 used.
+template <typename IssueFn>
+__device__ __forceinline__ void ring_take(const uint8_t *ring_t, int q, uint4 (&raw)[5], IssueFn &&issue) {
+    cp_async_wait<RAW_D - 1>();
+    const uint8_t *src = ring_t + (size_t)(q % RAW_R) * RAW_STAGE;
+#pragma unroll
+    for (int c = 0; c < 5; c++) raw[c] = *reinterpret_cast<const uint4 *>(src + c * RAW_CHUNK);
+    issue(q + RAW_D);
 }
 
 __global__ void __launch_bounds__(256, 1) gateup_mma_kernel(const __grid_constant__ ExpertArgs p) {
@@ -90,8 +176,10 @@ __global__ void __launch_bounds__(256, 1) gateup_mma_kernel(const __grid_constan
     const int E = p.E, nsb = E / 256, S = p.g_S;
     uint8_t *sB = smem;                                                  // [E/32 K steps][16 rows][32]
     uint8_t *sA = sB + MMA_N * E;                                        // [2][8 K steps][128 rows][32]
-    ActBlock *act = reinterpret_cast<ActBlock *>(sA + 2 * MMA_A_BYTES);  // [16][nsb]
-    int *tk_s = reinterpret_cast<int *>(act + MMA_N * nsb);             // [16]
+    uint8_t *ring = sA + 2 * MMA_A_BYTES;                                // [RAW_R][5][256 threads][16]
+    float *dA = reinterpret_cast<float *>(ring + RAW_R * RAW_STAGE);     // [16][nsb] activation scales
+    int *bsA = reinterpret_cast<int *>(dA + MMA_N * nsb);                // [16][nsb][8] 32-value sums
+    int *tk_s = bsA + MMA_N * nsb * 8;                                   // [16]
     int *rows_s = tk_s + MMA_N;                                          // [16]
     uint64_t *bars = reinterpret_cast<uint64_t *>(rows_s + MMA_N);      // [2]
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2);
@@ -118,13 +206,47 @@ __global__ void __launch_bounds__(256, 1) gateup_mma_kernel(const __grid_constan
     pdl_trigger();
     const uint32_t idesc = umma_idesc_u8s8(128, MMA_N);
     const uint32_t aBase = smem_u32(sA), bBase = smem_u32(sB);
-    int cur_chunk = -1, mc = 0;
+    const int rpt = p.g_rpt, nsteps = 2 * nsb;
+    // this thread's row of unit u: tile (row / rpt), slot (row % rpt) * nsb + superblock
+    auto unit_src = [&](int u, const uint8_t *&gb, const uint8_t *&ub, int &s0) {
+        const int ci = u / nrb, rb = u - ci * nrb;
+        const int e = p.g_chunk_e[ci];
+        const int row = rb * 128 + r;
+        gb = expert_gate(p, e) + (long long)(row / rpt) * p.g_tile_bytes;
+        ub = expert_up(p, e) + (long long)(row / rpt) * p.u_tile_bytes;
+        s0 = (row % rpt) * nsb;
+    };
+    // ring: step q of this CTA is (unit u0 + q / nsteps, step q % nsteps)
+    const int Q = u1 > u0 ? (u1 - u0) * nsteps : 0;
+    const uint8_t *ring_t = ring + tid * 16;
+    const uint32_t ring_s = smem_u32(ring) + (uint32_t)tid * 16;
+    int pf_u = -1, pf_s0 = 0;
+    const uint8_t *pf_g = nullptr, *pf_up = nullptr;
+    auto issue = [&](int q) {
+        if (q < Q) {
+            const int qu = q / nsteps, sq = q - qu * nsteps;
+            if (u0 + qu != pf_u) {
+                pf_u = u0 + qu;
+                unit_src(pf_u, pf_g, pf_up, pf_s0);
+            }
+            const bool g = sq < nsb;
+            const uint8_t *b = (g ? pf_g : pf_up) + (size_t)(pf_s0 + (g ? sq : sq - nsb)) * 16;
+            const uint32_t dst = ring_s + (uint32_t)(q % RAW_R) * RAW_STAGE;
+            cp_async16(dst, b);
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                cp_async16(dst + (uint32_t)(1 + c) * RAW_CHUNK, b + (size_t)(1 + 4 * h + c) * S * 16);
+        }
+        cp_async_commit();
+    };
+    for (int q = 0; q < RAW_D; q++) issue(q);
+    int cur_chunk = -1, mc = 0, q = 0;
     uint32_t gstep = 0;  // steps issued by this CTA: buffer gstep & 1, its barrier phase (gstep >> 1) & 1
     bool ok = true;
     for (int u = u0; ok && u < u1; u++) {
         const int ci = u / nrb, rb = u - ci * nrb;
         const int e = p.g_chunk_e[ci];
-        if (ci != cur_chunk) {  // stage the chunk: Q8_K blocks, then the B operand (zero rows past mc)
+        if (ci != cur_chunk) {  // the chunk's Q8_K rows: B operand (zero rows past mc), scales, sums
             cur_chunk = ci;
             const int c0 = p.g_chunk_r0[ci], m = p.g_count[e], off = p.g_off[e];
             mc = m - c0 < MMA_N ? m - c0 : MMA_N;
@@ -135,63 +257,48 @@ __global__ void __launch_bounds__(256, 1) gateup_mma_kernel(const __grid_constan
                 rows_s[tid] = tk / p.row_div;
             }
             __syncthreads();
-            stage_activations<8>(p.fn, p.E, rows_s, nullptr, 0.0f, p.E, mc, act, nullptr);
-            __syncthreads();
+            const uint32_t sB_s = smem_u32(sB);
             for (int i = tid; i < MMA_N * E / 16; i += 256) {  // 16-byte pieces of the B operand
                 const int t = i / (E / 16), k = (i - t * (E / 16)) * 16;
-                uint4 v = make_uint4(0, 0, 0, 0);
-                if (t < mc) v = *reinterpret_cast<const uint4 *>(act[t * nsb + k / 256].qs + (k & 255));
-                *reinterpret_cast<uint4 *>(sB + umma_off(t, k, MMA_N)) = v;
+                if (t < mc) cp_async16(sB_s + umma_off(t, k, MMA_N), p.q8_qs + (long long)rows_s[t] * E + k);
+                else *reinterpret_cast<uint4 *>(sB + umma_off(t, k, MMA_N)) = make_uint4(0, 0, 0, 0);
             }
+            for (int i = tid; i < MMA_N * nsb * 2; i += 256) {  // 32-value sums, two 16-byte halves per block
+                const int t = i / (nsb * 2), j = i - t * nsb * 2;
+                if (t < mc) cp_async16(smem_u32(bsA + t * nsb * 8 + j * 4), p.q8_bs + (long long)rows_s[t] * nsb * 8 + j * 4);
+                else *reinterpret_cast<int4 *>(bsA + t * nsb * 8 + j * 4) = make_int4(0, 0, 0, 0);
+            }
+            for (int i = tid; i < MMA_N * nsb; i += 256) {
+                const int t = i / nsb, b = i - t * nsb;
+                dA[i] = t < mc ? p.q8_d[(long long)rows_s[t] * nsb + b] : 0.0f;
+            }
+            cp_async_commit();
+            cp_async_wait<0>();  // (the ring's copies in flight complete here too)
+            __syncthreads();
         }
-        // this thread's row of the block: tile (row / rpt), slot (row % rpt) * nsb + superblock
         const int row = rb * 128 + r;
-        const int rpt = p.g_rpt;
-        const uint8_t *gbase = expert_gate(p, e) + (long long)(row / rpt) * p.g_tile_bytes;
-        const uint8_t *ubase = expert_up(p, e) + (long long)(row / rpt) * p.u_tile_bytes;
-        const int slot0 = (row % rpt) * nsb;
-        // chunk 0 (header) and this half's four nibble chunks 1 + 4h .. 4 + 4h
-        auto load_raw = [&](int st, uint4 (&w)[5]) {
-            const uint8_t *b = (st < nsb ? gbase : ubase) + (size_t)(slot0 + (st < nsb ? st : st - nsb)) * 16;
-            w[0] = __ldg(reinterpret_cast<const uint4 *>(b));
-#pragma unroll
-            for (int c = 0; c < 4; c++)
-                w[1 + c] = __ldg(reinterpret_cast<const uint4 *>(b + (size_t)(1 + 4 * h + c) * S * 16));
-        };
         float acc_g[8], acc_u[8];
 #pragma unroll
         for (int t = 0; t < 8; t++) acc_g[t] = acc_u[t] = 0.0f;
-        uint4 raw[5], nxt[5];
-        load_raw(0, raw);
+        uint4 raw[5];
         int sc[8], mn[8];
         float dw = 0.0f, dminw = 0.0f;
         int psc[8], pmn[8];
         float pdw = 0.0f, pdminw = 0.0f;
-        const int nsteps = 2 * nsb;
         auto epilogue = [&](int st, uint32_t gs) -> bool {  // the integer dots of step st -> the row sums
             if (!mbar_wait(&bars[gs & 1], (gs >> 1) & 1, p.err)) return false;
             tc_fence_after();
             const int sb = st < nsb ? st : st - nsb;
             int sumi[8];
-#pragma unroll
-            for (int t = 0; t < 8; t++) sumi[t] = 0;
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                uint32_t v[8];
-                tmem_ld8(tmem + tlane + (gs & 1) * 128 + j * 16 + h * 8, v);
-                tmem_wait_ld();
-#pragma unroll
-                for (int t = 0; t < 8; t++) sumi[t] += psc[j] * (int)v[t];
-            }
+            tmem_sumi<8>(tmem + tlane + (gs & 1) * 128 + h * 8, 16, psc, sumi);
 #pragma unroll
             for (int t = 0; t < 8; t++) {
                 const int tt = 8 * h + t;
-                const ActBlock &ab = act[(tt < mc ? tt : 0) * nsb + sb];
-                const int4 b0 = *reinterpret_cast<const int4 *>(ab.bs32);
-                const int4 b1 = *reinterpret_cast<const int4 *>(ab.bs32 + 4);
+                const int4 b0 = *reinterpret_cast<const int4 *>(bsA + (tt * nsb + sb) * 8);
+                const int4 b1 = *reinterpret_cast<const int4 *>(bsA + (tt * nsb + sb) * 8 + 4);
                 const int summ = pmn[0] * b0.x + pmn[1] * b0.y + pmn[2] * b0.z + pmn[3] * b0.w + pmn[4] * b1.x +
                                  pmn[5] * b1.y + pmn[6] * b1.z + pmn[7] * b1.w;
-                const float da = ab.d;
+                const float da = dA[tt * nsb + sb];
                 const float t1 = __fmul_rn(pdw, da);
                 const float t2 = __fmul_rn(__int2float_rn(sumi[t]), t1);
                 const float t3 = __fmul_rn(pdminw, da);
@@ -202,42 +309,11 @@ __global__ void __launch_bounds__(256, 1) gateup_mma_kernel(const __grid_constan
             }
             return true;
         };
-        for (int st = 0; st < nsteps; st++) {
+        for (int st = 0; st < nsteps; st++, q++) {
             const uint32_t gs = gstep++;
-            // header: d, dmin and the 6-bit scales/mins of this row's superblock (get_scale_min_k4)
-            {
-                const uint4 hd = raw[0];
-                dw = __half2float(__ushort_as_half((unsigned short)(hd.x & 0xffff)));
-                dminw = __half2float(__ushort_as_half((unsigned short)(hd.x >> 16)));
-                const uint32_t s03 = hd.y, s47 = hd.z, s811 = hd.w;
-                const uint32_t sc_lo = s03 & 0x3F3F3F3Fu, m_lo = s47 & 0x3F3F3F3Fu;
-                const uint32_t sc_hi = (s811 & 0x0F0F0F0Fu) | ((s03 >> 2) & 0x30303030u);
-                const uint32_t m_hi = ((s811 >> 4) & 0x0F0F0F0Fu) | ((s47 >> 2) & 0x30303030u);
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    sc[j] = byte_u(sc_lo, j);
-                    sc[j + 4] = byte_u(sc_hi, j);
-                    mn[j] = byte_u(m_lo, j);
-                    mn[j + 4] = byte_u(m_hi, j);
-                }
-            }
-            // the A operand: nibble group g = 2h + gg; sub-block 2g = low nibbles, 2g + 1 = high
-            uint8_t *a = sA + (gs & 1) * MMA_A_BYTES;
-#pragma unroll
-            for (int gg = 0; gg < 2; gg++) {
-                const int g = 2 * h + gg;
-                const uint4 w0 = raw[1 + 2 * gg], w1 = raw[2 + 2 * gg];
-                const uint4 lo0 = make_uint4(w0.x & 0x0F0F0F0Fu, w0.y & 0x0F0F0F0Fu, w0.z & 0x0F0F0F0Fu, w0.w & 0x0F0F0F0Fu);
-                const uint4 lo1 = make_uint4(w1.x & 0x0F0F0F0Fu, w1.y & 0x0F0F0F0Fu, w1.z & 0x0F0F0F0Fu, w1.w & 0x0F0F0F0Fu);
-                const uint4 hi0 = make_uint4((w0.x >> 4) & 0x0F0F0F0Fu, (w0.y >> 4) & 0x0F0F0F0Fu, (w0.z >> 4) & 0x0F0F0F0Fu,
-                                             (w0.w >> 4) & 0x0F0F0F0Fu);
-                const uint4 hi1 = make_uint4((w1.x >> 4) & 0x0F0F0F0Fu, (w1.y >> 4) & 0x0F0F0F0Fu, (w1.z >> 4) & 0x0F0F0F0Fu,
-                                             (w1.w >> 4) & 0x0F0F0F0Fu);
-                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g) * 32, 128)) = lo0;
-                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g) * 32 + 16, 128)) = lo1;
-                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g + 1) * 32, 128)) = hi0;
-                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g + 1) * 32 + 16, 128)) = hi1;
-            }
+            ring_take(ring_t, q, raw, issue);
+            q4k_header(raw[0], dw, dminw, sc, mn);
+            q4k_unpack_a(sA + (gs & 1) * MMA_A_BYTES, raw, r, h);
             fence_proxy_async();
             tc_fence_before();
             __syncthreads();
@@ -251,7 +327,6 @@ __global__ void __launch_bounds__(256, 1) gateup_mma_kernel(const __grid_constan
                             umma_desc(bBase + (uint32_t)(sb * 8 + j) * MMA_N * 32, 128, 256), idesc, false);
                 umma_commit(smem_u32(&bars[gs & 1]));
             }
-            if (st + 1 < nsteps) load_raw(st + 1, nxt);
             if (st > 0 && !__syncthreads_and(epilogue(st - 1, gs - 1))) {
                 ok = false;
                 break;
@@ -263,8 +338,6 @@ __global__ void __launch_bounds__(256, 1) gateup_mma_kernel(const __grid_constan
             }
             pdw = dw;
             pdminw = dminw;
-#pragma unroll
-            for (int c = 0; c < 5; c++) raw[c] = nxt[c];
             tc_fence_before();
         }
         if (!ok) break;
@@ -278,6 +351,7 @@ __global__ void __launch_bounds__(256, 1) gateup_mma_kernel(const __grid_constan
                 if (8 * h + t < mc)
                     p.act[(long long)tk_s[8 * h + t] * p.F + row] = __fmul_rn(bt_silu(acc_g[t]), acc_u[t]);
     }
+    cp_async_wait_all();  // no copy into this CTA's shared memory outlives it
     if (!ok && tid == 0) {  // let this CTA's MMAs in flight finish (bounded) before the TMEM goes
         for (uint32_t b = 0; b < 2; b++) {
             // the last step issued on buffer b
@@ -291,11 +365,10 @@ __global__ void __launch_bounds__(256, 1) gateup_mma_kernel(const __grid_constan
 }
 
 cudaError_t launch_gateup_mma(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl) {
-    const size_t smem = gateup_mma_smem_bytes(a.E);
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(256);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = gateup_mma_smem_bytes(a.E);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -305,39 +378,112 @@ cudaError_t launch_gateup_mma(const ExpertArgs &a, int grid, cudaStream_t st, bo
     return cudaLaunchKernelEx(&cfg, gateup_mma_kernel, a);
 }
 
-// ====================================================================== batched GEMV on tcgen05
-// y[t][out_off + r] = W[r,:] . x[t,:] (+ res) for Q4_K segments of whole 128-row blocks and T > 8
-// tokens (q/k/v and attn_output of batched steps). Unit = (chunk of 32 tokens, block of 128
-// rows of one segment), token-chunk-major. The activations of a chunk are RMS-normed (q/k/v)
-// and quantised exactly as the dp4a kernel stages them, into the 8-bit B operand plus each
-// block's d and 32-value sums. Per superblock step, thread r unpacks its row's nibbles into A
-// (double-buffered), one thread issues 8 MMAs (M = 128, N = 32, one per sub-block, each into
-// its own 32 TMEM columns; TMEM double-buffered), and the previous step's epilogue turns the
-// integer sub-block dots into the superblock's C4 value per (row, token) and adds it to the
-// row's running sum in superblock order.
-constexpr int GM_N = 32;
-
-size_t gemv_mma_smem_bytes(int K) {
-    const size_t nsb = (size_t)K / 256;
-    return 1024 + (size_t)GM_N * K + (size_t)GM_N * nsb * (4 + 32) + 8 * sizeof(ActBlock) + 2 * MMA_A_BYTES +
-           GM_N * 4 + 256;
+// ====================================================================== Q8_K activation rows
+// One CTA per row: the row's RMSNorm factor (warp 0, C5/C6) when norm_w, then the 256-value
+// blocks quantised (C3) by the warps in turn, written as the tensor-core kernels read them: the
+// 8-bit values in row order, each block's scale and its eight 32-value sums. The arithmetic is
+// the dp4a kernels' staging, so both paths see the same bits.
+__global__ void __launch_bounds__(256) q8_stage_kernel(const float *x, long long xs, const int *x_rows,
+                                                       const float *norm_w, float eps, int K, int8_t *qs, float *dq,
+                                                       int *bs) {
+    __shared__ ActBlock tmp[8];
+    __shared__ float s_norm;
+    const int t = blockIdx.x, warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nsb = K / 256;
+    pdl_wait();
+    const float *xt = x + (long long)(x_rows ? x_rows[t] : t) * xs;
+    if (norm_w) {
+        if (warp == 0) {
+            const float acc = warp_sumsq_p2(xt, K, lane);
+            if (lane == 0) s_norm = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)K), eps)));
+        }
+        __syncthreads();
+    }
+    pdl_trigger();
+    for (int b = warp; b < nsb; b += 8) {
+        const float *src = xt + b * 256 + lane * 8;
+        float v[8];
+        const float4 a0 = *reinterpret_cast<const float4 *>(src), a1 = *reinterpret_cast<const float4 *>(src + 4);
+        v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
+        v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+        if (norm_w) {
+            const float sN = s_norm;
+            const float *w = norm_w + b * 256 + lane * 8;
+#pragma unroll
+            for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fmul_rn(v[i], sN), w[i]);
+        }
+        quantize_block_warp(v, tmp + warp, lane);
+        __syncwarp();
+        *reinterpret_cast<uint2 *>(qs + (long long)t * K + b * 256 + lane * 8) =
+            *reinterpret_cast<const uint2 *>(tmp[warp].qs + lane * 8);
+        if (lane == 0) dq[(long long)t * nsb + b] = tmp[warp].d;
+        if (lane < 8) bs[((long long)t * nsb + b) * 8 + lane] = tmp[warp].bs32[lane];
+        __syncwarp();  // tmp is read before the warp's next block overwrites it
+    }
 }
 
+cudaError_t launch_q8_stage(const float *x, long long x_stride, const int *x_rows, const float *norm_w, float eps, int K,
+                            int T, int8_t *qs, float *d, int *bs, cudaStream_t st, bool pdl) {
+    if (T <= 0) return cudaSuccess;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(T);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, q8_stage_kernel, x, x_stride, x_rows, norm_w, eps, K, qs, d, bs);
+}
+
+// ====================================================================== batched GEMV on tcgen05
+// y[t][out_off + r] = W[r,:] . x[t,:] (+ res) for Q4_K segments of whole 128-row blocks and T > 8
+// tokens (q/k/v and attn_output of batched steps). Unit = (chunk of N tokens, block of 128
+// rows of one segment), token-chunk-major; N = 32 where the operands fit beside the raw-weight
+// ring, else 16 (K of 4096). The activations come as Q8_K rows, RMS-normed (q/k/v) and quantised
+// once per step by q8_stage_kernel exactly as the dp4a kernel stages them; a chunk copies its
+// rows into the 8-bit B operand plus each block's d and 32-value sums. Per superblock step, thread r takes its row's superblock from the ring
+// (cp.async, RAW_D steps ahead across units) and unpacks its nibbles into A (double-buffered),
+// one thread issues 8 MMAs (M = 128, one per sub-block, each into its own N TMEM columns; TMEM
+// double-buffered), and the previous step's epilogue turns the integer sub-block dots into the
+// superblock's C4 value per (row, token) and adds it to the row's running sum in superblock
+// order.
+template <int N>
+static size_t gemv_mma_bytes(int K) {
+    const size_t nsb = (size_t)K / 256;
+    return 1024 + (size_t)N * K + (size_t)N * nsb * (4 + 32) + 2 * MMA_A_BYTES + (size_t)RAW_R * RAW_STAGE + 256;
+}
+
+int gemv_mma_tokens(int K) {
+    if (K % 256) return 0;
+    if (gemv_mma_bytes<32>(K) <= MMA_SMEM_LIMIT) return 32;
+    if (gemv_mma_bytes<16>(K) <= MMA_SMEM_LIMIT) return 16;
+    return 0;
+}
+
+size_t gemv_mma_smem_bytes(int K) {
+    const int n = gemv_mma_tokens(K);
+    return n == 32 ? gemv_mma_bytes<32>(K) : n == 16 ? gemv_mma_bytes<16>(K) : (size_t)-1;
+}
+
+template <int N>
 __global__ void __launch_bounds__(256, 1) gemv_mma_kernel(const __grid_constant__ GemvArgs p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int K = p.K, nsb = K / 256;
     uint8_t *sA = smem;                                                  // [2][8 K steps][128 rows][32]
-    uint8_t *sB = sA + 2 * MMA_A_BYTES;                                  // [K/32 steps][32 rows][32]
-    float *dA = reinterpret_cast<float *>(sB + (size_t)GM_N * K);        // [32][nsb]
-    int *bsA = reinterpret_cast<int *>(dA + GM_N * nsb);                 // [32][nsb][8]
-    ActBlock *tmp = reinterpret_cast<ActBlock *>(bsA + GM_N * nsb * 8);  // [8] one per warp
-    float *normS = reinterpret_cast<float *>(tmp + 8);                   // [32]
-    uint64_t *bars = reinterpret_cast<uint64_t *>(normS + GM_N);         // [2]
+    uint8_t *ring = sA + 2 * MMA_A_BYTES;                                // [RAW_R][5][256 threads][16]
+    uint8_t *sB = ring + RAW_R * RAW_STAGE;                              // [K/32 steps][N rows][32]
+    float *dA = reinterpret_cast<float *>(sB + (size_t)N * K);           // [N][nsb]
+    int *bsA = reinterpret_cast<int *>(dA + N * nsb);                    // [N][nsb][8]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(bsA + N * nsb * 8);    // [2]
     uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    constexpr int HT = N / 2;                // tokens per half
+    constexpr uint32_t TCOLS = 2 * 8 * N;    // 2 buffers x 8 sub-blocks x N tokens
+    const int tid = threadIdx.x, warp = tid >> 5;
     // thread (row r of the block, half h): h unpacks nibble groups 2h, 2h+1 of the row and
-    // finishes the epilogue of tokens 16h .. 16h+15
+    // finishes the epilogue of tokens HT*h .. HT*h + HT-1
     const int r = tid & 127, h = tid >> 7;
     const uint32_t tlane = (uint32_t)((warp & 3) * 32) << 16;
     if (tid == 0) {
@@ -345,109 +491,102 @@ __global__ void __launch_bounds__(256, 1) gemv_mma_kernel(const __grid_constant_
         mbar_init(&bars[1], 1);
         fence_mbar_init();
     }
-    if (warp == 0) tmem_alloc(smem_u32(tslot), 512);
+    if (warp == 0) tmem_alloc(smem_u32(tslot), TCOLS);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = *tslot;
-    pdl_wait();
     int nrb = 0;  // 128-row blocks over the segments
     for (int i = 0; i < p.nseg; i++) nrb += p.seg[i].rows / 128;
-    const int ntc = (p.T + GM_N - 1) / GM_N;
+    const int ntc = (p.T + N - 1) / N;
     const int total = ntc * nrb;
     const int u0 = (int)((long long)blockIdx.x * total / gridDim.x);
     const int u1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
-    pdl_trigger();
-    const uint32_t idesc = umma_idesc_u8s8(128, GM_N);
-    const uint32_t aBase = smem_u32(sA), bBase = smem_u32(sB);
-    int cur_tc = -1, tn = 0;
-    uint32_t gstep = 0;
-    bool ok = true;
-    for (int u = u0; ok && u < u1; u++) {
-        const int tc = u / nrb;
-        int rb = u - tc * nrb, si = 0;
+    // this thread's row of unit u: the segment, tile (row / rpt), slot (row % rpt) * nsb
+    auto unit_src = [&](int u, const uint8_t *&wb, int &s0, int &S, int &si, int &row) {
+        int rb = u - (u / nrb) * nrb;
+        si = 0;
         while (rb >= p.seg[si].rows / 128) {
             rb -= p.seg[si].rows / 128;
             si++;
         }
-        const GemvSeg &sg = p.seg[si];
-        if (tc != cur_tc) {  // stage the chunk's 32 token rows (zeros past the last token)
-            cur_tc = tc;
-            const int t0 = tc * GM_N;
-            tn = p.T - t0 < GM_N ? p.T - t0 : GM_N;
-            __syncthreads();  // the previous chunk's operands are no longer read
-            if (p.norm_w) {
-                for (int t = warp; t < tn; t += 8) {
-                    const float *xt = p.x + (long long)(p.x_rows ? p.x_rows[t0 + t] : t0 + t) * p.x_stride;
-                    const float acc = warp_sumsq_p2(xt, K, lane);
-                    if (lane == 0) normS[t] = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(__fdiv_rn(acc, (float)K), p.eps)));
-                }
-                __syncthreads();
+        row = rb * 128 + r;
+        wb = p.seg[si].w + (long long)(row / p.seg[si].rpt) * p.seg[si].tile_bytes;
+        s0 = (row % p.seg[si].rpt) * nsb;
+        S = p.seg[si].S;
+    };
+    const int Q = u1 > u0 ? (u1 - u0) * nsb : 0;
+    const uint8_t *ring_t = ring + tid * 16;
+    const uint32_t ring_s = smem_u32(ring) + (uint32_t)tid * 16;
+    int pf_u = -1, pf_s0 = 0, pf_S = 0;
+    const uint8_t *pf_w = nullptr;
+    auto issue = [&](int q) {
+        if (q < Q) {
+            const int qu = q / nsb, sq = q - qu * nsb;
+            if (u0 + qu != pf_u) {
+                int si_, row_;
+                pf_u = u0 + qu;
+                unit_src(pf_u, pf_w, pf_s0, pf_S, si_, row_);
             }
-            for (int blk = warp; blk < GM_N * nsb; blk += 8) {
-                const int t = blk / nsb, b = blk - t * nsb;
-                uint2 q8 = make_uint2(0, 0);
-                float dv = 0.0f;
-                int bsv = 0;
-                if (t < tn) {
-                    const float *xt = p.x + (long long)(p.x_rows ? p.x_rows[t0 + t] : t0 + t) * p.x_stride + b * 256 +
-                                      lane * 8;
-                    float v[8];
-                    const float4 a0 = *reinterpret_cast<const float4 *>(xt), a1 = *reinterpret_cast<const float4 *>(xt + 4);
-                    v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
-                    v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
-                    if (p.norm_w) {
-                        const float sN = normS[t];
-                        const float *w = p.norm_w + b * 256 + lane * 8;
-#pragma unroll
-                        for (int i = 0; i < 8; i++) v[i] = __fmul_rn(__fmul_rn(v[i], sN), w[i]);
-                    }
-                    quantize_block_warp(v, tmp + warp, lane);
-                    __syncwarp();
-                    q8 = *reinterpret_cast<const uint2 *>(tmp[warp].qs + lane * 8);
-                    dv = tmp[warp].d;
-                    bsv = lane < 8 ? tmp[warp].bs32[lane] : 0;
-                    __syncwarp();  // tmp is read before the warp's next block overwrites it
-                }
-                const int k = b * 256 + lane * 8;
-                *reinterpret_cast<uint2 *>(sB + umma_off(t, k, GM_N)) = q8;
-                if (lane == 0) dA[t * nsb + b] = dv;
-                if (lane < 8) bsA[(t * nsb + b) * 8 + lane] = bsv;
-            }
-        }
-        // this thread's row: tile row / rpt of the segment, slot (row % rpt) * nsb + superblock
-        const int row = rb * 128 + r;
-        const uint8_t *wbase = sg.w + (long long)(row / sg.rpt) * sg.tile_bytes;
-        const int slot0 = (row % sg.rpt) * nsb, S = sg.S;
-        auto load_raw = [&](int st, uint4 (&w)[5]) {  // header and this half's four nibble chunks
-            const uint8_t *b = wbase + (size_t)(slot0 + st) * 16;
-            w[0] = __ldg(reinterpret_cast<const uint4 *>(b));
+            const uint8_t *b = pf_w + (size_t)(pf_s0 + sq) * 16;
+            const uint32_t dst = ring_s + (uint32_t)(q % RAW_R) * RAW_STAGE;
+            cp_async16(dst, b);
 #pragma unroll
             for (int c = 0; c < 4; c++)
-                w[1 + c] = __ldg(reinterpret_cast<const uint4 *>(b + (size_t)(1 + 4 * h + c) * S * 16));
-        };
-        constexpr int HT = GM_N / 2;  // tokens per half
+                cp_async16(dst + (uint32_t)(1 + c) * RAW_CHUNK, b + (size_t)(1 + 4 * h + c) * pf_S * 16);
+        }
+        cp_async_commit();
+    };
+    // the weights do not depend on the previous kernel: their first copies go out before the wait
+    for (int q = 0; q < RAW_D; q++) issue(q);
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t idesc = umma_idesc_u8s8(128, N);
+    const uint32_t aBase = smem_u32(sA), bBase = smem_u32(sB);
+    int cur_tc = -1, tn = 0, q = 0;
+    uint32_t gstep = 0;
+    bool ok = true;
+    for (int u = u0; ok && u < u1; u++) {
+        const int tc = u / nrb;
+        const uint8_t *wb_;
+        int s0_, S_, si, row;
+        unit_src(u, wb_, s0_, S_, si, row);
+        const GemvSeg &sg = p.seg[si];
+        if (tc != cur_tc) {  // the chunk's N token rows as Q8_K: B operand (zeros past the last token), scales, sums
+            cur_tc = tc;
+            const int t0 = tc * N;
+            tn = p.T - t0 < N ? p.T - t0 : N;
+            __syncthreads();  // the previous chunk's operands are no longer read
+            const uint32_t sB_s = smem_u32(sB);
+            for (int i = tid; i < N * K / 16; i += 256) {  // 16-byte pieces of the B operand
+                const int t = i / (K / 16), k = (i - t * (K / 16)) * 16;
+                if (t < tn) cp_async16(sB_s + umma_off(t, k, N), p.q8_qs + (long long)(t0 + t) * K + k);
+                else *reinterpret_cast<uint4 *>(sB + umma_off(t, k, N)) = make_uint4(0, 0, 0, 0);
+            }
+            for (int i = tid; i < N * nsb * 2; i += 256) {  // 32-value sums, two 16-byte halves per block
+                const int t = i / (nsb * 2), j = i - t * nsb * 2;
+                if (t < tn) cp_async16(smem_u32(bsA + t * nsb * 8 + j * 4), p.q8_bs + (long long)(t0 + t) * nsb * 8 + j * 4);
+                else *reinterpret_cast<int4 *>(bsA + t * nsb * 8 + j * 4) = make_int4(0, 0, 0, 0);
+            }
+            for (int i = tid; i < N * nsb; i += 256) {
+                const int t = i / nsb, b = i - t * nsb;
+                dA[i] = t < tn ? p.q8_d[(long long)(t0 + t) * nsb + b] : 0.0f;
+            }
+            cp_async_commit();
+            cp_async_wait<0>();  // (the ring's copies in flight complete here too)
+            __syncthreads();
+        }
         float acc[HT];
 #pragma unroll
         for (int t = 0; t < HT; t++) acc[t] = 0.0f;
-        uint4 raw[5], nxt[5];
-        load_raw(0, raw);
+        uint4 raw[5];
         int sc[8], mn[8], psc[8], pmn[8];
         float dw = 0.0f, dminw = 0.0f, pdw = 0.0f, pdminw = 0.0f;
         auto epilogue = [&](int sb, uint32_t gs) -> bool {
             if (!mbar_wait(&bars[gs & 1], (gs >> 1) & 1, p.err)) return false;
             tc_fence_after();
             int sumi[HT];
-#pragma unroll
-            for (int t = 0; t < HT; t++) sumi[t] = 0;
-#pragma unroll
-            for (int j = 0; j < 8; j++) {
-                uint32_t v[16];
-                tmem_ld16(tmem + tlane + (gs & 1) * 256 + j * GM_N + h * HT, v);
-                tmem_wait_ld();
-#pragma unroll
-                for (int t = 0; t < HT; t++) sumi[t] += psc[j] * (int)v[t];
-            }
+            tmem_sumi<HT>(tmem + tlane + (gs & 1) * 8 * N + h * HT, N, psc, sumi);
 #pragma unroll
             for (int tt = 0; tt < HT; tt++) {
                 const int t = HT * h + tt;
@@ -464,40 +603,11 @@ __global__ void __launch_bounds__(256, 1) gemv_mma_kernel(const __grid_constant_
             }
             return true;
         };
-        for (int st = 0; st < nsb; st++) {
+        for (int st = 0; st < nsb; st++, q++) {
             const uint32_t gs = gstep++;
-            {
-                const uint4 h = raw[0];
-                dw = __half2float(__ushort_as_half((unsigned short)(h.x & 0xffff)));
-                dminw = __half2float(__ushort_as_half((unsigned short)(h.x >> 16)));
-                const uint32_t s03 = h.y, s47 = h.z, s811 = h.w;
-                const uint32_t sc_lo = s03 & 0x3F3F3F3Fu, m_lo = s47 & 0x3F3F3F3Fu;
-                const uint32_t sc_hi = (s811 & 0x0F0F0F0Fu) | ((s03 >> 2) & 0x30303030u);
-                const uint32_t m_hi = ((s811 >> 4) & 0x0F0F0F0Fu) | ((s47 >> 2) & 0x30303030u);
-#pragma unroll
-                for (int j = 0; j < 4; j++) {
-                    sc[j] = byte_u(sc_lo, j);
-                    sc[j + 4] = byte_u(sc_hi, j);
-                    mn[j] = byte_u(m_lo, j);
-                    mn[j + 4] = byte_u(m_hi, j);
-                }
-            }
-            uint8_t *a = sA + (gs & 1) * MMA_A_BYTES;
-#pragma unroll
-            for (int gg = 0; gg < 2; gg++) {
-                const int g = 2 * h + gg;
-                const uint4 w0 = raw[1 + 2 * gg], w1 = raw[2 + 2 * gg];
-                const uint4 lo0 = make_uint4(w0.x & 0x0F0F0F0Fu, w0.y & 0x0F0F0F0Fu, w0.z & 0x0F0F0F0Fu, w0.w & 0x0F0F0F0Fu);
-                const uint4 lo1 = make_uint4(w1.x & 0x0F0F0F0Fu, w1.y & 0x0F0F0F0Fu, w1.z & 0x0F0F0F0Fu, w1.w & 0x0F0F0F0Fu);
-                const uint4 hi0 = make_uint4((w0.x >> 4) & 0x0F0F0F0Fu, (w0.y >> 4) & 0x0F0F0F0Fu, (w0.z >> 4) & 0x0F0F0F0Fu,
-                                             (w0.w >> 4) & 0x0F0F0F0Fu);
-                const uint4 hi1 = make_uint4((w1.x >> 4) & 0x0F0F0F0Fu, (w1.y >> 4) & 0x0F0F0F0Fu, (w1.z >> 4) & 0x0F0F0F0Fu,
-                                             (w1.w >> 4) & 0x0F0F0F0Fu);
-                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g) * 32, 128)) = lo0;
-                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g) * 32 + 16, 128)) = lo1;
-                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g + 1) * 32, 128)) = hi0;
-                *reinterpret_cast<uint4 *>(a + umma_off(r, (2 * g + 1) * 32 + 16, 128)) = hi1;
-            }
+            ring_take(ring_t, q, raw, issue);
+            q4k_header(raw[0], dw, dminw, sc, mn);
+            q4k_unpack_a(sA + (gs & 1) * MMA_A_BYTES, raw, r, h);
             fence_proxy_async();
             tc_fence_before();
             __syncthreads();
@@ -505,12 +615,11 @@ __global__ void __launch_bounds__(256, 1) gemv_mma_kernel(const __grid_constant_
             if (tid == 0) {
 #pragma unroll 1
                 for (int j = 0; j < 8; j++)
-                    umma_i8(tmem + (gs & 1) * 256 + j * GM_N,
+                    umma_i8(tmem + (gs & 1) * 8 * N + j * N,
                             umma_desc(aBase + (gs & 1) * MMA_A_BYTES + j * 4096, 128, 256),
-                            umma_desc(bBase + (uint32_t)(st * 8 + j) * GM_N * 32, 128, 256), idesc, false);
+                            umma_desc(bBase + (uint32_t)(st * 8 + j) * N * 32, 128, 256), idesc, false);
                 umma_commit(smem_u32(&bars[gs & 1]));
             }
-            if (st + 1 < nsb) load_raw(st + 1, nxt);
             if (st > 0 && !__syncthreads_and(epilogue(st - 1, gs - 1))) {
                 ok = false;
                 break;
@@ -522,8 +631,6 @@ __global__ void __launch_bounds__(256, 1) gemv_mma_kernel(const __grid_constant_
             }
             pdw = dw;
             pdminw = dminw;
-#pragma unroll
-            for (int c = 0; c < 5; c++) raw[c] = nxt[c];
             tc_fence_before();
         }
         if (!ok) break;
@@ -532,7 +639,7 @@ __global__ void __launch_bounds__(256, 1) gemv_mma_kernel(const __grid_constant_
             break;
         }
         tc_fence_before();
-        const int t0 = tc * GM_N + HT * h;
+        const int t0 = tc * N + HT * h;
         for (int t = 0; t < HT && HT * h + t < tn; t++) {
             const long long yi = (long long)(t0 + t) * p.y_stride + sg.out_off + row;
             float y = acc[t];
@@ -540,6 +647,7 @@ __global__ void __launch_bounds__(256, 1) gemv_mma_kernel(const __grid_constant_
             p.y[yi] = y;
         }
     }
+    cp_async_wait_all();  // no copy into this CTA's shared memory outlives it
     if (!ok && tid == 0) {
         for (uint32_t b = 0; b < 2; b++) {
             const long long last = gstep == 0 ? -1 : ((long long)((gstep - 1) & 1) == b ? gstep - 1 : (long long)gstep - 2);
@@ -548,10 +656,12 @@ __global__ void __launch_bounds__(256, 1) gemv_mma_kernel(const __grid_constant_
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tmem_dealloc(tmem, 512);
+    if (warp == 0) tmem_dealloc(tmem, TCOLS);
 }
 
 cudaError_t launch_gemv_mma(const GemvArgs &a, int grid, cudaStream_t st, bool pdl) {
+    const int n = gemv_mma_tokens(a.K);
+    if (!n) return cudaErrorInvalidValue;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
     cfg.blockDim = dim3(256);
@@ -562,7 +672,7 @@ cudaError_t launch_gemv_mma(const GemvArgs &a, int grid, cudaStream_t st, bool p
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, gemv_mma_kernel, a);
+    return n == 32 ? cudaLaunchKernelEx(&cfg, gemv_mma_kernel<32>, a) : cudaLaunchKernelEx(&cfg, gemv_mma_kernel<16>, a);
 }
 
 cudaError_t init_mma_attributes() {
@@ -570,7 +680,8 @@ cudaError_t init_mma_attributes() {
     cudaError_t e;
     if ((e = cudaGetDevice(&dev))) return e;
     if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
-    const void *kerns[] = {(const void *)gateup_mma_kernel, (const void *)gemv_mma_kernel};
+    const void *kerns[] = {(const void *)gateup_mma_kernel, (const void *)gemv_mma_kernel<32>,
+                           (const void *)gemv_mma_kernel<16>};
     for (const void *k : kerns) {
         cudaFuncAttributes fa;
         if ((e = cudaFuncGetAttributes(&fa, k))) return e;

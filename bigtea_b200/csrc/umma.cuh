@@ -85,6 +85,27 @@ __device__ __forceinline__ void tmem_ld8(uint32_t taddr, uint32_t (&v)[8]) {
                  : "memory");
 }
 
+// After tcgen05.wait::ld: makes every later use of v depend on this point, so the compiler
+// cannot read a loaded register before the wait.
+template <int N>
+__device__ __forceinline__ void tmem_pin(uint32_t (&v)[N]) {
+#pragma unroll
+    for (int i = 0; i < N; i++) asm volatile("" : "+r"(v[i]));
+}
+
+// Per-thread asynchronous 16-byte copies global -> shared (L1 bypassed), grouped by
+// commit_group; wait_group<N> returns once at most N of this thread's newest groups are still
+// in flight, and the data of the completed ones is then visible to this thread.
+__device__ __forceinline__ void cp_async16(uint32_t dst_smem, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst_smem), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+    asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
 // Byte offset of (row, k) in a K-major, no-swizzle operand tile of 32-byte K steps:
 // K step s = k / 32 at s * rows * 32; inside it, core matrix (row / 8, (k % 32) / 16).
 __host__ __device__ constexpr uint32_t umma_off(int row, int k, int rows) {

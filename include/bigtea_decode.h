@@ -151,7 +151,10 @@ int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const ui
 /* Engine switches: "pdl" (programmatic dependent launch between the step's kernels, default 1),
  * "prefetch" (L2 bulk prefetch of the next kernels' weights and KV pages, default 0),
  * "persistent" (run single-token steps of up to 4 sequences as one cooperative kernel that
- * holds every SM for the whole step, default 1; 0 = one kernel per phase). */
+ * holds every SM for the whole step, default 1; 0 = one kernel per phase), "mma" (Q4_K
+ * contractions of batched steps on the tensor cores, default 1), "mma_min_units" (the batched
+ * GEMV goes to the tensor cores from this many 128-row x token-chunk units, default 32),
+ * "mma_grid" (CTAs of the tensor-core kernels, default 0 = one per SM). */
 int bt_set_option(bt_engine *e, const char *name, int value);
 
 /* Router bias of one layer: n == n_expert F32 values added to the router logits before the

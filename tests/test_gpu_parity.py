@@ -439,6 +439,41 @@ def test_shared_expert_matches_oracle(source):
     e.close()
 
 
+def test_tensor_core_gemv_matches_dp4a_and_oracle():
+    """The batched GEMVs on tcgen05 give the dp4a kernels' bits and the oracle's: q/k/v at
+    K = 512 (32-token units) and attn_output at K = 4096 (32 heads of 128: 16-token units), on a
+    4-CTA grid so every CTA streams many (token chunk, row block) units, and gate/up many chunks,
+    through its weight ring (prefetch across units and chunks)."""
+    cfg = bt.config("tiny", n_head=32, n_head_kv=4)
+    W = bt.synth_model(cfg, seed=11)
+    rng = np.random.default_rng(56)
+    prompt = rng.integers(0, cfg.n_vocab, 100)
+    outs = {}
+    for mode in ("mma", "dp4a"):
+        e = bt.Engine(cfg, W)
+        if mode == "mma":
+            e.set_option("mma_min_units", 1)
+            e.set_option("mma_grid", 4)
+        else:
+            e.set_option("mma", 0)
+        cache = bt.KvCache(e, max_positions=256, max_seqs=40)
+        runner = bt.StreamingRunner(e)
+        lg = runner.forward_batch(cache, [0], [prompt], [0])
+        steps = runner.forward_batch(cache, list(range(1, 40)), [[int(t)] for t in prompt[:39]], [0] * 39)
+        outs[mode] = (lg, steps, cache.layer_bytes(1, 0))
+        cache.close()
+        e.close()
+    assert np.array_equal(bits(outs["mma"][0]), bits(outs["dp4a"][0]))
+    assert np.array_equal(bits(outs["mma"][1]), bits(outs["dp4a"][1]))
+    assert np.array_equal(outs["mma"][2][0], outs["dp4a"][2][0])
+    assert np.array_equal(outs["mma"][2][1], outs["dp4a"][2][1])
+    model = orc.Model(cfg, W)
+    assert_logits(outs["mma"][0][0], model.forward(list(prompt), 0))
+    for i in (0, 17, 38):
+        m1 = orc.Model(cfg, W)
+        assert_logits(outs["mma"][1][i], m1.forward([int(prompt[i])], 0))
+
+
 def test_tensor_core_gateup_matches_dp4a_kernel(tiny_cfg, tiny_weights):
     """The grouped gate/up on tcgen05 (int8 MMA per K-quant sub-block, integer-exact) and the
     dp4a grouped kernel give the same bits: a 64-token prefill sub-step and a 24-sequence step."""
