@@ -130,6 +130,7 @@ struct bt_engine {
     bool mma = true;  // grouped Q4_K gate/up on tcgen05 (option "mma")
     int mma_min_units = 32;  // batched GEMVs on tcgen05 from this many (tokens, rows) units on (option)
     int mma_grid = 0;        // CTAs of the tensor-core kernels (0: one per SM; option, for tests)
+    bool attn_warp = true;   // batched attention with one warp per 128-key chunk (option "attn_warp")
     // expert cache: experts in pinned host memory, the ones a layer selects copied into slots
     // of a device pool before its expert kernels (bt_engine_enable_expert_cache)
     bool xcache = false;
@@ -1526,14 +1527,17 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.layer = (int)il;
             a.n_blocks = kv->n_blocks;
             a.max_chunks = (int)((kv->max_positions + ATTN_CHUNK - 1) / ATTN_CHUNK);
-            a.n_cta = e->n_sm * 3;  // three resident CTAs per SM
+            a.n_cta = e->n_sm * (e->attn_warp ? 2 : 3);  // resident CTAs per SM
             a.scale = 1.0f / sqrtf((float)D);
             a.part = e->part.as<float>();
             a.cnt = e->acnt.as<int>();
             a.out = e->att.as<float>();
             a.err = err;
             timer_begin(e, "attention");
-            CK(launch_attn(a, kv->tmap, st, pdl));
+            if (e->attn_warp)
+                CK(launch_attn_warp(a, kv->tmap, st, pdl));
+            else
+                CK(launch_attn(a, kv->tmap, st, pdl));
             timer_end(e);
         }
         const int ochunk = gemv_chunk(T, QW, l.o.g.tile_bytes);
@@ -2482,6 +2486,12 @@ extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
     }
     if (!strcmp(name, "mma")) {
         e->mma = value != 0;
+        for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
+        e->graphs.clear();
+        return BT_OK;
+    }
+    if (!strcmp(name, "attn_warp")) {
+        e->attn_warp = value != 0;
         for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
         e->graphs.clear();
         return BT_OK;

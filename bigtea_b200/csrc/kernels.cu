@@ -1523,6 +1523,342 @@ __global__ void __launch_bounds__(ATTN_THREADS, 3)
     }
 }
 
+// ====================================================================== attention, one warp per item
+// Batched steps. CTAs of four warps, two per SM, walk groups (token t, kv head g, four
+// consecutive 128-key chunks), CTA b a contiguous range of them; warp w takes chunk 4 cg + w of
+// group (t, g, cg). The warps of a CTA share the group's q values. Each warp streams its chunk's
+// K and then V in pieces of 32 keys (8 KB: two 16-row pages in two 128-byte-swizzled column
+// halves) through its own two-slot TMA ring, requesting the next piece -- also the first piece
+// of its next chunk -- as it takes the current one. Lane l owns keys l, l + 32, l + 64, l + 96
+// for the scores (per head a sequential dot over d in mixed-precision f16 x f16 + f32 fmas, one
+// independent chain per head, q as f16 so one load brings a dimension's G values) and dims
+// 4l .. 4l + 3 for P*V (every head; dims in f32x2 pairs against probabilities stored twice,
+// so a pair operand is one load). The arithmetic is attn_kernel's (C8): piece j's keys sit on
+// the lanes as warp j's keys do there, so the 32-key butterfly sums are the same, and every
+// score and P*V sum runs in the same order.
+constexpr int AW_WARPS = 4;
+constexpr int AW_PIECE_BYTES = 32 * 256;  // 32 keys of one kv head, f16
+
+size_t attn_warp_smem_bytes(int G, int T) {
+    return 1024 + (size_t)AW_WARPS * (2 * AW_PIECE_BYTES + (size_t)ATTN_CHUNK * G * 8) + (size_t)128 * G * 4 +
+           AW_WARPS * 2 * 8 + (size_t)(3 * T + 1) * 4 + 64;
+}
+
+// both halves of w as one f32x2 of exact f32 values (FMA pipe)
+__device__ __forceinline__ f32x2 h2_f32x2(uint32_t w) {
+    f32x2 r;
+    asm("{\n\t.reg .b16 l, h;\n\t.reg .f32 a, b;\n\tmov.b32 {l, h}, %1;\n\tadd.rn.f32.f16 a, l, %2;\n\t"
+        "add.rn.f32.f16 b, h, %2;\n\tmov.b64 %0, {a, b};\n\t}"
+        : "=l"(r)
+        : "r"(w), "f"(-0.0f));
+    return r;
+}
+
+template <int G>
+__global__ void __launch_bounds__(AW_WARPS * 32, 2)
+    attn_warp_kernel(const __grid_constant__ AttnArgs p, const __grid_constant__ CUtensorMap tmap) {
+    constexpr int D = 128, CH = ATTN_CHUNK, HP = G / 2;
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023u)) & 1023u);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    uint8_t *ring = smem + warp * 2 * AW_PIECE_BYTES;                                 // [2 slots][piece]
+    float *fbase = reinterpret_cast<float *>(smem + AW_WARPS * 2 * AW_PIECE_BYTES);
+    float *pb = fbase + warp * CH * G * 2;                                            // [CH][G][2] P twice
+    __half *qh = reinterpret_cast<__half *>(fbase + AW_WARPS * CH * G * 2);           // [D][G] q rounded to f16
+    uint64_t *bars = reinterpret_cast<uint64_t *>(fbase + AW_WARPS * CH * G * 2 + D * G);  // [warps][2]
+    int *pre = reinterpret_cast<int *>(bars + AW_WARPS * 2);                          // [T + 1] first group of t
+    int *pos_s = pre + p.T + 1, *seq_s = pos_s + p.T;                                 // [T] each
+    uint64_t *wb = bars + warp * 2;
+    if (lane == 0) {
+        mbar_init(&wb[0], 1);
+        mbar_init(&wb[1], 1);
+        fence_mbar_init();
+    }
+    pdl_wait();
+    if (warp == 0) {  // groups per token: HK * ceil(chunks / 4); exclusive prefix over the tokens
+        int run = 0;
+        for (int t0 = 0; t0 < p.T; t0 += 32) {
+            const int t = t0 + lane;
+            const int pos = t < p.T ? p.pos_of[t] : 0;
+            const int n = t < p.T ? p.HK * (((pos + CH) / CH + AW_WARPS - 1) / AW_WARPS) : 0;
+            int incl = n;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(FULL, incl, o);
+                if (lane >= o) incl += v;
+            }
+            if (t < p.T) {
+                pre[t] = run + incl - n;
+                pos_s[t] = pos;
+                seq_s[t] = p.seq_of[t];
+            }
+            run += __shfl_sync(FULL, incl, 31);
+        }
+        if (lane == 0) pre[p.T] = run;
+    }
+    __syncthreads();
+    pdl_trigger();
+    const int NG = pre[p.T];
+    const int g0 = (int)((long long)blockIdx.x * NG / gridDim.x);
+    const int g1 = (int)((long long)(blockIdx.x + 1) * NG / gridDim.x);
+    if (g0 >= g1) return;
+    if (warp == 0 && lane == 0) prefetch_tmap(&tmap);
+
+    // group i -> token t (the last with pre[t] <= i), kv head g, chunk group cg
+    auto decode = [&](int i, int &t, int &g, int &cg) {
+        int lo = 0, hi = p.T - 1;
+        while (lo < hi) {
+            const int mid = (lo + hi + 1) >> 1;
+            if (pre[mid] <= i) lo = mid;
+            else hi = mid - 1;
+        }
+        t = lo;
+        const int ngc = ((pos_s[t] + CH) / CH + AW_WARPS - 1) / AW_WARPS, r = i - pre[t];
+        g = r / ngc;
+        cg = r - g * ngc;
+    };
+    // this warp's item in group i: chunk c of (t, g) with nk keys, or none
+    struct Item {
+        int grp, t, g, c, nk, cnt, np;
+    };
+    auto item_at = [&](int i, Item &it) -> bool {
+        int t, g, cg;
+        decode(i, t, g, cg);
+        const int nk = pos_s[t] + 1, c = cg * AW_WARPS + warp;
+        if (c * CH >= nk) return false;
+        it.grp = i;
+        it.t = t;
+        it.g = g;
+        it.c = c;
+        it.nk = nk;
+        it.cnt = nk - c * CH < CH ? nk - c * CH : CH;
+        it.np = (it.cnt + 31) >> 5;
+        return true;
+    };
+    auto next_item = [&](int from, Item &it) -> bool {
+        for (int i = from; i < g1; i++)
+            if (item_at(i, it)) return true;
+        return false;
+    };
+    // lane < 8: block id of page `lane` of the item's chunk (pages past the keys are not read)
+    auto load_pages = [&](const Item &it) -> int {
+        const int pg = it.c * (CH / 16) + lane;
+        return lane < 8 && pg * 16 < it.nk ? p.block_table[seq_s[it.t] * p.max_blocks + pg] : 0;
+    };
+    // piece q of item it (K pieces 0 .. np-1, then V pieces) into slot `slot`
+    auto issue = [&](int slot, const Item &it, int q, int pages) {
+        const int kv = q >= it.np ? 1 : 0, j = kv ? q - it.np : q;
+        const int keys = it.cnt - 32 * j < 32 ? it.cnt - 32 * j : 32;
+        const int npg = (keys + 15) >> 4;
+        const int blk = __shfl_sync(FULL, pages, (2 * j + (lane >> 1)) & 7);
+        if (lane == 0) {
+            fence_proxy_async();
+            mbar_arrive_expect_tx(&wb[slot], npg * 4096);
+        }
+        __syncwarp();
+        if (lane < 2 * npg) {
+            const int row = (int)(((((long long)p.layer * p.n_blocks + blk) * 2 + kv) * p.HK + it.g) * 16);
+            tma_load_2d(ring + slot * AW_PIECE_BYTES + (lane & 1) * 4096 + (lane >> 1) * 2048, &tmap, (lane & 1) * 64,
+                        row, &wb[slot]);
+        }
+    };
+
+    const int QW = p.H * D;
+    const float NEG_INF = -__int_as_float(0x7f800000);
+    Item cur, nxt;
+    bool have = next_item(g0, cur);
+    int pg_cur = have ? load_pages(cur) : 0;
+    bool have_n = have && next_item(cur.grp + 1, nxt);
+    int pg_nxt = have_n ? load_pages(nxt) : 0;
+    int issued = 0, pc = 0;  // pieces requested and taken by this warp (piece k: slot k & 1)
+    if (have) issue(0, cur, 0, pg_cur);
+    issued = have ? 1 : 0;
+    bool ok = true;
+    int cur_tg = -1;
+    // wait for piece pc after requesting the one after it (in this item or the next)
+    auto take = [&](int q) -> bool {
+        if (q + 1 < 2 * cur.np) {
+            issue(issued & 1, cur, q + 1, pg_cur);
+            issued++;
+        } else if (have_n) {
+            issue(issued & 1, nxt, 0, pg_nxt);
+            issued++;
+        }
+        return mbar_wait(&wb[pc & 1], (pc >> 1) & 1, p.err);
+    };
+    for (int i = g0; i < g1; i++) {
+        int t, g, cg;
+        decode(i, t, g, cg);
+        if (t * p.HK + g != cur_tg) {  // every warp is past its scores of the previous (t, g)
+            __syncthreads();
+            cur_tg = t * p.HK + g;
+            for (int x = tid; x < D * G; x += AW_WARPS * 32) {
+                const int h = x / D, d = x % D;
+                qh[d * G + h] = __float2half_rn(p.q[(long long)t * QW + (g * G + h) * D + d]);
+            }
+            __syncthreads();
+        }
+        if (!ok || !have || cur.grp != i) continue;
+        // ---- scores, piece by piece: lane = key 32 j + lane
+        float sc[4][G];
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            if (j < cur.np) {
+                if (!take(j)) {
+                    ok = false;
+                    break;
+                }
+                // per dimension one load of the G q values (f16) and G mixed-precision fmas, one
+                // independent chain per head (C8: an fmaf of two f16 values per term, d in order)
+                float acc[G];
+#pragma unroll
+                for (int h = 0; h < G; h++) acc[h] = 0.0f;
+                const uint8_t *krow = ring + (pc & 1) * AW_PIECE_BYTES + lane * 128;
+                const int ksw = lane & 7;
+                const uint32_t *qw = reinterpret_cast<const uint32_t *>(qh);
+#pragma unroll 2
+                for (int c16 = 0; c16 < 16; c16++) {
+                    const uint4 w =
+                        *reinterpret_cast<const uint4 *>((c16 < 8 ? krow : krow + 4096) + (((c16 & 7) ^ ksw) << 4));
+                    const uint32_t kw[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                    for (int e2 = 0; e2 < 4; e2++) {
+#pragma unroll
+                        for (int hl = 0; hl < 2; hl++) {
+                            const int d = c16 * 8 + 2 * e2 + hl;
+                            uint32_t qv[HP];
+                            ldw_n<HP>(qv, qw + d * HP);
+#pragma unroll
+                            for (int i2 = 0; i2 < HP; i2++) {
+                                if (hl) fma_qk<true>(qv[i2], kw[e2], acc[2 * i2], acc[2 * i2 + 1]);
+                                else fma_qk<false>(qv[i2], kw[e2], acc[2 * i2], acc[2 * i2 + 1]);
+                            }
+                        }
+                    }
+                }
+                const bool valid = 32 * j + lane < cur.cnt;
+#pragma unroll
+                for (int h = 0; h < G; h++) sc[j][h] = valid ? __fmul_rn(acc[h], p.scale) : NEG_INF;
+                __syncwarp();  // every lane is done with the piece: its slot may be refilled
+                pc++;
+            } else {
+#pragma unroll
+                for (int h = 0; h < G; h++) sc[j][h] = NEG_INF;
+            }
+        }
+        if (!ok) continue;
+        // ---- softmax over the chunk: max, p = exp(s - m), l = the four 32-key butterfly sums in order
+        float m[G], l[G];
+#pragma unroll
+        for (int h = 0; h < G; h++) {
+            float x = fmaxf(fmaxf(sc[0][h], sc[1][h]), fmaxf(sc[2][h], sc[3][h]));
+            m[h] = warp_max(x);
+            l[h] = 0.0f;
+        }
+#pragma unroll
+        for (int j = 0; j < 4; j++) {
+            const bool valid = 32 * j + lane < cur.cnt;
+            float pr[G];
+#pragma unroll
+            for (int h = 0; h < G; h++) {
+                pr[h] = valid ? bt_exp(__fsub_rn(sc[j][h], m[h])) : 0.0f;
+                l[h] = __fadd_rn(l[h], butterfly_sum(pr[h]));
+            }
+            if (j < cur.np) {
+                float4 *prow = reinterpret_cast<float4 *>(pb + (32 * j + lane) * G * 2);
+#pragma unroll
+                for (int h2 = 0; h2 < HP; h2++) prow[h2] = make_float4(pr[2 * h2], pr[2 * h2], pr[2 * h2 + 1], pr[2 * h2 + 1]);
+            }
+        }
+        __syncwarp();
+        // ---- P*V, piece by piece: lane = dims 4 lane .. 4 lane + 3, keys in order
+        f32x2 o01[G], o23[G];
+#pragma unroll
+        for (int h = 0; h < G; h++) o01[h] = o23[h] = 0ull;
+        const int vhalf = lane < 16 ? 0 : 4096, vcc = (lane & 15) >> 1, vsub = (lane & 1) * 8;
+#pragma unroll 1
+        for (int j = 0; j < cur.np; j++) {
+            if (!take(cur.np + j)) {
+                ok = false;
+                break;
+            }
+            const uint8_t *vb = ring + (pc & 1) * AW_PIECE_BYTES + vhalf + vsub;
+            const int kmax = cur.cnt - 32 * j < 32 ? cur.cnt - 32 * j : 32;
+            const float *pj = pb + 32 * j * G * 2;
+#pragma unroll 4
+            for (int kk = 0; kk < 32; kk++) {
+                if (kk < kmax) {
+                    const uint2 v = *reinterpret_cast<const uint2 *>(vb + kk * 128 + ((vcc ^ (kk & 7)) << 4));
+                    const f32x2 v01 = h2_f32x2(v.x), v23 = h2_f32x2(v.y);
+                    const f32x2 *pr = reinterpret_cast<const f32x2 *>(pj + kk * G * 2);  // (p_h, p_h)
+#pragma unroll
+                    for (int h = 0; h < G; h++) {
+                        const f32x2 ph = pr[h];
+                        o01[h] = ffma2(ph, v01, o01[h]);
+                        o23[h] = ffma2(ph, v23, o23[h]);
+                    }
+                }
+            }
+            __syncwarp();
+            pc++;
+        }
+        if (!ok) continue;
+        // ---- the chunk's partial (acc, m, l), or the output when the context is one chunk
+        const int nc = (cur.nk + CH - 1) / CH;
+#pragma unroll
+        for (int h = 0; h < G; h++) {
+            const float2 a01 = upk2(o01[h]), a23 = upk2(o23[h]);
+            if (nc == 1) {
+                const float f = bt_exp(__fsub_rn(m[h], m[h]));
+                const float L = fmaf(l[h], f, 0.0f);
+                float4 o;
+                o.x = __fdiv_rn(fmaf(a01.x, f, 0.0f), L);
+                o.y = __fdiv_rn(fmaf(a01.y, f, 0.0f), L);
+                o.z = __fdiv_rn(fmaf(a23.x, f, 0.0f), L);
+                o.w = __fdiv_rn(fmaf(a23.y, f, 0.0f), L);
+                *reinterpret_cast<float4 *>(p.out + (long long)cur.t * QW + (cur.g * G + h) * D + 4 * lane) = o;
+            } else {
+                float *pp = p.part + ((((long long)cur.t * p.HK + cur.g) * p.max_chunks + cur.c) * G + h) * ATTN_PART_ROW;
+                *reinterpret_cast<float4 *>(pp + 4 * lane) = make_float4(a01.x, a01.y, a23.x, a23.y);
+                if (lane == 0) {
+                    pp[D] = m[h];
+                    pp[D + 1] = l[h];
+                }
+            }
+        }
+        // ---- the next item: its first piece is already requested
+        cur = nxt;
+        pg_cur = pg_nxt;
+        have = have_n;
+        have_n = have && next_item(cur.grp + 1, nxt);
+        pg_nxt = have_n ? load_pages(nxt) : 0;
+    }
+    if (!ok && lane == 0) {
+        // a wait ran out: give the copies still requested one more bounded wait before leaving
+        for (int s2 = 0; s2 < 2; s2++) {
+            long long last = -1;
+            for (long long k = issued - 1; k >= 0 && k >= issued - 2; k--)
+                if ((k & 1) == s2) last = k;
+            if (last >= pc) mbar_wait(&wb[s2], (uint32_t)(last >> 1) & 1, nullptr);
+        }
+    }
+}
+
+template <int G>
+static cudaError_t launch_attn_warp_g(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(a.n_cta);
+    cfg.blockDim = dim3(AW_WARPS * 32);
+    cfg.dynamicSmemBytes = attn_warp_smem_bytes(G, a.T);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, attn_warp_kernel<G>, a, tmap);
+}
+
 // grid (H, T), 128 threads: merges the chunk partials of one query head in chunk order
 // (C8): M = max m_c, f_c = exp(m_c - M), L = fmaf(l_c, f_c, L), O = fmaf(acc_c, f_c, O).
 __global__ void __launch_bounds__(128) attn_combine_kernel(const __grid_constant__ AttnArgs p) {
@@ -1585,6 +1921,19 @@ static cudaError_t launch_attn_g(const AttnArgs &a, const CUtensorMap &tmap, cud
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
     return cudaLaunchKernelEx(&cfg, attn_kernel<G>, a, tmap);
+}
+
+cudaError_t launch_attn_warp(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl) {
+    cudaError_t e;
+    switch (a.G) {
+    case 2: e = launch_attn_warp_g<2>(a, tmap, st, pdl); break;
+    case 4: e = launch_attn_warp_g<4>(a, tmap, st, pdl); break;
+    case 6: e = launch_attn_warp_g<6>(a, tmap, st, pdl); break;
+    case 8: e = launch_attn_warp_g<8>(a, tmap, st, pdl); break;
+    default: return cudaErrorInvalidValue;
+    }
+    if (e != cudaSuccess) return e;
+    return launch_ex(attn_combine_kernel, dim3(a.H, a.T), dim3(128), (size_t)3 * a.max_chunks * 4, st, pdl, a);
 }
 
 cudaError_t launch_attn(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl) {
@@ -1690,7 +2039,9 @@ cudaError_t init_kernel_attributes() {
                            (const void *)down_grouped_kernel<GEMV_WARPS>, (const void *)group_kernel,
                            (const void *)attn_kernel<2>,
                            (const void *)attn_kernel<4>,          (const void *)attn_kernel<6>,
-                           (const void *)attn_kernel<8>};
+                           (const void *)attn_kernel<8>,          (const void *)attn_warp_kernel<2>,
+                           (const void *)attn_warp_kernel<4>,     (const void *)attn_warp_kernel<6>,
+                           (const void *)attn_warp_kernel<8>};
     for (const void *k : kerns) {
         cudaFuncAttributes fa;
         if ((e = cudaFuncGetAttributes(&fa, k))) return e;

@@ -239,6 +239,9 @@ cudaError_t launch_shexp_act(const float *gu, float *act, int T, int F, cudaStre
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl);
 size_t attn_smem_bytes(int G, int T);
 cudaError_t launch_attn(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl);
+// the batched steps' attention with one warp per 128-key chunk (attn_warp_kernel), then the combine
+cudaError_t launch_attn_warp(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl);
+size_t attn_warp_smem_bytes(int G, int T);
 cudaError_t launch_embed(const EmbedArgs &a, cudaStream_t st, bool pdl);
 cudaError_t launch_step_end(const StepEndArgs &a, cudaStream_t st, bool pdl);
 

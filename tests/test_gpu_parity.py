@@ -439,6 +439,41 @@ def test_shared_expert_matches_oracle(source):
     e.close()
 
 
+def test_warp_attention_matches_cta_attention_and_oracle(tiny_cfg, tiny_weights):
+    """Batched attention with one warp per 128-key chunk gives the per-CTA kernel's bits and the
+    oracle's: 40 sequences whose contexts cover one-chunk finalisation, partial 32-key pieces,
+    a last page of one key and up to 63 chunks (the combine): enough chunk groups that every
+    CTA walks several and its warps prefetch across their items."""
+    cfg = bt.config("tiny", max_positions=8192)
+    rng = np.random.default_rng(57)
+    ctxs = [1, 15, 16, 17, 31, 32, 33, 127, 128, 129, 255, 256, 257, 511, 700] + \
+        [int(c) for c in rng.integers(1, 8000, 25)]
+    kw = cfg.n_head_kv * cfg.head_dim
+    kv = [[((0.5 * rng.standard_normal(n * kw)).astype(np.float16), rng.standard_normal(n * kw).astype(np.float16))
+           for _ in range(cfg.n_layer)] for n in ctxs]
+    toks = [int(t) for t in rng.integers(0, cfg.n_vocab, len(ctxs))]
+    outs = {}
+    for mode in (1, 0):
+        e = bt.Engine(cfg, tiny_weights)
+        e.set_option("attn_warp", mode)
+        cache = bt.KvCache(e, max_positions=8192, max_seqs=len(ctxs))
+        for s_, n in enumerate(ctxs):
+            for il in range(cfg.n_layer):
+                cache.restore_layer(il, kv[s_][il][0], kv[s_][il][1], seq=s_)
+            cache.set_positions(n, s_)
+        runner = bt.StreamingRunner(e)
+        outs[mode] = runner.forward_batch(cache, list(range(len(ctxs))), [[t] for t in toks], ctxs)
+        cache.close()
+        e.close()
+    assert np.array_equal(bits(outs[0]), bits(outs[1]))
+    for s_ in (0, 3, 7, 9, 14, 15, 20):
+        m2 = orc.Model(cfg, tiny_weights)
+        for il in range(cfg.n_layer):
+            m2.write_kv_layer(il, kv[s_][il][0], kv[s_][il][1])
+        m2.set_len(ctxs[s_])
+        assert_logits(outs[1][s_], m2.forward([toks[s_]], ctxs[s_]))
+
+
 def test_tensor_core_gemv_matches_dp4a_and_oracle():
     """The batched GEMVs on tcgen05 give the dp4a kernels' bits and the oracle's: q/k/v at
     K = 512 (32-token units) and attn_output at K = 4096 (32 heads of 128: 16-token units), on a
