@@ -1527,7 +1527,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.layer = (int)il;
             a.n_blocks = kv->n_blocks;
             a.max_chunks = (int)((kv->max_positions + ATTN_CHUNK - 1) / ATTN_CHUNK);
-            a.n_cta = e->n_sm * (e->attn_warp ? 2 : 3);  // resident CTAs per SM
+            a.n_cta = e->n_sm * (e->attn_warp ? 4 : 3);  // resident CTAs per SM
             a.scale = 1.0f / sqrtf((float)D);
             a.part = e->part.as<float>();
             a.cnt = e->acnt.as<int>();

@@ -1523,25 +1523,26 @@ __global__ void __launch_bounds__(ATTN_THREADS, 3)
     }
 }
 
-// ====================================================================== attention, one warp per item
-// Batched steps. CTAs of four warps, two per SM, walk groups (token t, kv head g, four
-// consecutive 128-key chunks), CTA b a contiguous range of them; warp w takes chunk 4 cg + w of
-// group (t, g, cg). The warps of a CTA share the group's q values. Each warp streams its chunk's
-// K and then V in pieces of 32 keys (8 KB: two 16-row pages in two 128-byte-swizzled column
-// halves) through its own two-slot TMA ring, requesting the next piece -- also the first piece
-// of its next chunk -- as it takes the current one. Lane l owns keys l, l + 32, l + 64, l + 96
-// for the scores (per head a sequential dot over d in mixed-precision f16 x f16 + f32 fmas, one
-// independent chain per head, q as f16 so one load brings a dimension's G values) and dims
-// 4l .. 4l + 3 for P*V (every head; dims in f32x2 pairs against probabilities stored twice,
-// so a pair operand is one load). The arithmetic is attn_kernel's (C8): piece j's keys sit on
-// the lanes as warp j's keys do there, so the 32-key butterfly sums are the same, and every
-// score and P*V sum runs in the same order.
-constexpr int AW_WARPS = 4;
+// ====================================================================== attention, one warp pair per chunk
+// Batched steps. CTAs of two warp pairs, four CTAs per SM, walk groups (token t, kv head g, two
+// consecutive 128-key chunks), CTA b a contiguous range of them; pair pi takes chunk 2 cg + pi of
+// group (t, g, cg), and warp hp of the pair takes heads hp*G/2 .. (hp+1)*G/2 - 1. The CTA shares
+// the group's q (f16). A pair streams its chunk's K, then V, in pieces of 32 keys (8 KB: two
+// 16-row pages in two 128-byte-swizzled column halves) through its own two-slot TMA ring; per
+// piece both warps wait for it, meet at a pair barrier (so the slot of the piece before is free)
+// and warp 0 requests the next piece -- also the first piece of the pair's next chunk. Lane l
+// owns keys l, l + 32, l + 64, l + 96 for the scores (per head a sequential fmaf dot over d;
+// heads in f32x2 pairs against each k value converted twice into both halves of a pair) and
+// dims 4l .. 4l + 3 for P*V (the warp's heads; dims in f32x2 pairs against probabilities
+// stored twice, so a pair operand is one load; full 32-key pieces run without per-key tests). The arithmetic is attn_kernel's (C8): piece j's keys sit on the lanes as
+// warp j's keys do there, so the 32-key butterfly sums are the same, and every score and P*V
+// sum runs in the same order.
+constexpr int AW_PAIRS = 2, AW_WARPS = 2 * AW_PAIRS;
 constexpr int AW_PIECE_BYTES = 32 * 256;  // 32 keys of one kv head, f16
 
 size_t attn_warp_smem_bytes(int G, int T) {
-    return 1024 + (size_t)AW_WARPS * (2 * AW_PIECE_BYTES + (size_t)ATTN_CHUNK * G * 8) + (size_t)128 * G * 4 +
-           AW_WARPS * 2 * 8 + (size_t)(3 * T + 1) * 4 + 64;
+    return 1024 + (size_t)AW_PAIRS * 2 * AW_PIECE_BYTES + (size_t)AW_WARPS * ATTN_CHUNK * (G / 2) * 8 +
+           (size_t)128 * G * 4 + AW_PAIRS * 2 * 8 + (size_t)(3 * T + 1) * 4 + 64;
 }
 
 // both halves of w as one f32x2 of exact f32 values (FMA pipe)
@@ -1553,34 +1554,53 @@ __device__ __forceinline__ f32x2 h2_f32x2(uint32_t w) {
         : "r"(w), "f"(-0.0f));
     return r;
 }
+// (lo, lo) and (hi, hi) of w as two f32x2 of exact f32 values, each half converted twice so the
+// pairs need no register moves (FMA pipe)
+__device__ __forceinline__ void h2_bcast2(uint32_t w, f32x2 &lo, f32x2 &hi) {
+    asm("{\n\t.reg .b16 l, h;\n\t.reg .f32 a, b, c, d;\n\tmov.b32 {l, h}, %2;\n\t"
+        "add.rn.f32.f16 a, l, %3;\n\tadd.rn.f32.f16 b, l, %3;\n\tadd.rn.f32.f16 c, h, %3;\n\t"
+        "add.rn.f32.f16 d, h, %3;\n\tmov.b64 %0, {a, b};\n\tmov.b64 %1, {c, d};\n\t}"
+        : "=l"(lo), "=l"(hi)
+        : "r"(w), "f"(-0.0f));
+}
+// barrier of one warp pair (64 threads, named barrier 1 + pair) that also ANDs v over it
+__device__ __forceinline__ bool pair_sync_and(int pair, bool v) {
+    int r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.s32 p, %1, 0;\n\tbar.red.and.pred q, %2, 64, p;\n\tselp.s32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"((int)v), "r"(1 + pair)
+        : "memory");
+    return r != 0;
+}
 
 template <int G>
-__global__ void __launch_bounds__(AW_WARPS * 32, 2)
+__global__ void __launch_bounds__(AW_WARPS * 32, 4)
     attn_warp_kernel(const __grid_constant__ AttnArgs p, const __grid_constant__ CUtensorMap tmap) {
-    constexpr int D = 128, CH = ATTN_CHUNK, HP = G / 2;
+    constexpr int D = 128, CH = ATTN_CHUNK, HH = G / 2;
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - ((uint32_t)__cvta_generic_to_shared(smem_raw) & 1023u)) & 1023u);
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    uint8_t *ring = smem + warp * 2 * AW_PIECE_BYTES;                                 // [2 slots][piece]
-    float *fbase = reinterpret_cast<float *>(smem + AW_WARPS * 2 * AW_PIECE_BYTES);
-    float *pb = fbase + warp * CH * G * 2;                                            // [CH][G][2] P twice
-    __half *qh = reinterpret_cast<__half *>(fbase + AW_WARPS * CH * G * 2);           // [D][G] q rounded to f16
-    uint64_t *bars = reinterpret_cast<uint64_t *>(fbase + AW_WARPS * CH * G * 2 + D * G);  // [warps][2]
-    int *pre = reinterpret_cast<int *>(bars + AW_WARPS * 2);                          // [T + 1] first group of t
-    int *pos_s = pre + p.T + 1, *seq_s = pos_s + p.T;                                 // [T] each
-    uint64_t *wb = bars + warp * 2;
-    if (lane == 0) {
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, pair = warp >> 1, hp = warp & 1;
+    uint8_t *ring = smem + pair * 2 * AW_PIECE_BYTES;                                  // [2 slots][piece]
+    float *fbase = reinterpret_cast<float *>(smem + AW_PAIRS * 2 * AW_PIECE_BYTES);
+    float *pb = fbase + warp * CH * HH * 2;                                            // [CH][HH][2] P twice
+    float *qf = fbase + AW_WARPS * CH * HH * 2;                                        // [D][G] q's f16 rounding, as f32
+    uint64_t *bars = reinterpret_cast<uint64_t *>(qf + D * G);                         // [pairs][2]
+    int *pre = reinterpret_cast<int *>(bars + AW_PAIRS * 2);                           // [T + 1] first group of t
+    int *pos_s = pre + p.T + 1, *seq_s = pos_s + p.T;                                  // [T] each
+    uint64_t *wb = bars + pair * 2;
+    if (hp == 0 && lane == 0) {
         mbar_init(&wb[0], 1);
         mbar_init(&wb[1], 1);
         fence_mbar_init();
     }
     pdl_wait();
-    if (warp == 0) {  // groups per token: HK * ceil(chunks / 4); exclusive prefix over the tokens
+    if (warp == 0) {  // groups per token: HK * ceil(chunks / 2); exclusive prefix over the tokens
         int run = 0;
         for (int t0 = 0; t0 < p.T; t0 += 32) {
             const int t = t0 + lane;
             const int pos = t < p.T ? p.pos_of[t] : 0;
-            const int n = t < p.T ? p.HK * (((pos + CH) / CH + AW_WARPS - 1) / AW_WARPS) : 0;
+            const int n = t < p.T ? p.HK * (((pos + CH) / CH + AW_PAIRS - 1) / AW_PAIRS) : 0;
             int incl = n;
 #pragma unroll
             for (int o = 1; o < 32; o <<= 1) {
@@ -1613,18 +1633,18 @@ __global__ void __launch_bounds__(AW_WARPS * 32, 2)
             else hi = mid - 1;
         }
         t = lo;
-        const int ngc = ((pos_s[t] + CH) / CH + AW_WARPS - 1) / AW_WARPS, r = i - pre[t];
+        const int ngc = ((pos_s[t] + CH) / CH + AW_PAIRS - 1) / AW_PAIRS, r = i - pre[t];
         g = r / ngc;
         cg = r - g * ngc;
     };
-    // this warp's item in group i: chunk c of (t, g) with nk keys, or none
+    // this pair's chunk in group i: chunk c of (t, g) with nk keys, or none
     struct Item {
         int grp, t, g, c, nk, cnt, np;
     };
     auto item_at = [&](int i, Item &it) -> bool {
         int t, g, cg;
         decode(i, t, g, cg);
-        const int nk = pos_s[t] + 1, c = cg * AW_WARPS + warp;
+        const int nk = pos_s[t] + 1, c = cg * AW_PAIRS + pair;
         if (c * CH >= nk) return false;
         it.grp = i;
         it.t = t;
@@ -1643,9 +1663,9 @@ __global__ void __launch_bounds__(AW_WARPS * 32, 2)
     // lane < 8: block id of page `lane` of the item's chunk (pages past the keys are not read)
     auto load_pages = [&](const Item &it) -> int {
         const int pg = it.c * (CH / 16) + lane;
-        return lane < 8 && pg * 16 < it.nk ? p.block_table[seq_s[it.t] * p.max_blocks + pg] : 0;
+        return hp == 0 && lane < 8 && pg * 16 < it.nk ? p.block_table[seq_s[it.t] * p.max_blocks + pg] : 0;
     };
-    // piece q of item it (K pieces 0 .. np-1, then V pieces) into slot `slot`
+    // (warp 0 of the pair) piece q of item it (K pieces 0 .. np-1, then V pieces) into slot `slot`
     auto issue = [&](int slot, const Item &it, int q, int pages) {
         const int kv = q >= it.np ? 1 : 0, j = kv ? q - it.np : q;
         const int keys = it.cnt - 32 * j < 32 ? it.cnt - 32 * j : 32;
@@ -1670,21 +1690,24 @@ __global__ void __launch_bounds__(AW_WARPS * 32, 2)
     int pg_cur = have ? load_pages(cur) : 0;
     bool have_n = have && next_item(cur.grp + 1, nxt);
     int pg_nxt = have_n ? load_pages(nxt) : 0;
-    int issued = 0, pc = 0;  // pieces requested and taken by this warp (piece k: slot k & 1)
-    if (have) issue(0, cur, 0, pg_cur);
+    int issued = 0, pc = 0;  // pieces requested and taken by this pair (piece k: slot k & 1)
+    if (have && hp == 0) issue(0, cur, 0, pg_cur);
     issued = have ? 1 : 0;
     bool ok = true;
     int cur_tg = -1;
-    // wait for piece pc after requesting the one after it (in this item or the next)
+    // piece q of the current item: wait for it; at the pair barrier both warps are past the
+    // piece before, so warp 0 may refill that slot with the piece after this one
     auto take = [&](int q) -> bool {
+        const bool landed = mbar_wait(&wb[pc & 1], (pc >> 1) & 1, p.err);
+        if (!pair_sync_and(pair, landed)) return false;
         if (q + 1 < 2 * cur.np) {
-            issue(issued & 1, cur, q + 1, pg_cur);
+            if (hp == 0) issue(issued & 1, cur, q + 1, pg_cur);
             issued++;
         } else if (have_n) {
-            issue(issued & 1, nxt, 0, pg_nxt);
+            if (hp == 0) issue(issued & 1, nxt, 0, pg_nxt);
             issued++;
         }
-        return mbar_wait(&wb[pc & 1], (pc >> 1) & 1, p.err);
+        return true;
     };
     for (int i = g0; i < g1; i++) {
         int t, g, cg;
@@ -1694,13 +1717,13 @@ __global__ void __launch_bounds__(AW_WARPS * 32, 2)
             cur_tg = t * p.HK + g;
             for (int x = tid; x < D * G; x += AW_WARPS * 32) {
                 const int h = x / D, d = x % D;
-                qh[d * G + h] = __float2half_rn(p.q[(long long)t * QW + (g * G + h) * D + d]);
+                qf[d * G + h] = __half2float(__float2half_rn(p.q[(long long)t * QW + (g * G + h) * D + d]));
             }
             __syncthreads();
         }
         if (!ok || !have || cur.grp != i) continue;
-        // ---- scores, piece by piece: lane = key 32 j + lane
-        float sc[4][G];
+        // ---- scores, piece by piece: lane = key 32 j + lane, this warp's HH heads
+        float sc[4][HH];
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             if (j < cur.np) {
@@ -1708,14 +1731,15 @@ __global__ void __launch_bounds__(AW_WARPS * 32, 2)
                     ok = false;
                     break;
                 }
-                // per dimension one load of the G q values (f16) and G mixed-precision fmas, one
-                // independent chain per head (C8: an fmaf of two f16 values per term, d in order)
-                float acc[G];
+                // heads in f32x2 pairs: (s_h, s_h+1) += (q_h, q_h+1) * (k_d, k_d), d in order (C8:
+                // each an fmaf of two f16 values); k_d converted twice into both halves of its pair
+                constexpr int NP = (HH + 1) / 2;
+                f32x2 acc[NP];
 #pragma unroll
-                for (int h = 0; h < G; h++) acc[h] = 0.0f;
+                for (int jp = 0; jp < NP; jp++) acc[jp] = 0ull;
                 const uint8_t *krow = ring + (pc & 1) * AW_PIECE_BYTES + lane * 128;
                 const int ksw = lane & 7;
-                const uint32_t *qw = reinterpret_cast<const uint32_t *>(qh);
+                const float *qb = qf + hp * HH;
 #pragma unroll 2
                 for (int c16 = 0; c16 < 16; c16++) {
                     const uint4 w =
@@ -1723,58 +1747,70 @@ __global__ void __launch_bounds__(AW_WARPS * 32, 2)
                     const uint32_t kw[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                     for (int e2 = 0; e2 < 4; e2++) {
+                        f32x2 kb[2];
+                        h2_bcast2(kw[e2], kb[0], kb[1]);
 #pragma unroll
                         for (int hl = 0; hl < 2; hl++) {
                             const int d = c16 * 8 + 2 * e2 + hl;
-                            uint32_t qv[HP];
-                            ldw_n<HP>(qv, qw + d * HP);
+                            if constexpr (HH % 2 == 0) {
+                                const f32x2 *qd = reinterpret_cast<const f32x2 *>(qb + d * G);
 #pragma unroll
-                            for (int i2 = 0; i2 < HP; i2++) {
-                                if (hl) fma_qk<true>(qv[i2], kw[e2], acc[2 * i2], acc[2 * i2 + 1]);
-                                else fma_qk<false>(qv[i2], kw[e2], acc[2 * i2], acc[2 * i2 + 1]);
+                                for (int jp = 0; jp < NP; jp++) acc[jp] = ffma2(qd[jp], kb[hl], acc[jp]);
+                            } else {  // odd head count: the last pair's upper half is unused
+#pragma unroll
+                                for (int jp = 0; jp < NP; jp++) {
+                                    const float q0 = qb[d * G + 2 * jp], q1 = 2 * jp + 1 < HH ? qb[d * G + 2 * jp + 1] : 0.0f;
+                                    acc[jp] = ffma2(pk2(q0, q1), kb[hl], acc[jp]);
+                                }
                             }
                         }
                     }
                 }
+                float accs[2 * NP];
+#pragma unroll
+                for (int jp = 0; jp < NP; jp++) {
+                    const float2 v = upk2(acc[jp]);
+                    accs[2 * jp] = v.x;
+                    accs[2 * jp + 1] = v.y;
+                }
                 const bool valid = 32 * j + lane < cur.cnt;
 #pragma unroll
-                for (int h = 0; h < G; h++) sc[j][h] = valid ? __fmul_rn(acc[h], p.scale) : NEG_INF;
-                __syncwarp();  // every lane is done with the piece: its slot may be refilled
+                for (int h = 0; h < HH; h++) sc[j][h] = valid ? __fmul_rn(accs[h], p.scale) : NEG_INF;
                 pc++;
             } else {
 #pragma unroll
-                for (int h = 0; h < G; h++) sc[j][h] = NEG_INF;
+                for (int h = 0; h < HH; h++) sc[j][h] = NEG_INF;
             }
         }
         if (!ok) continue;
         // ---- softmax over the chunk: max, p = exp(s - m), l = the four 32-key butterfly sums in order
-        float m[G], l[G];
+        float m[HH], l[HH];
 #pragma unroll
-        for (int h = 0; h < G; h++) {
-            float x = fmaxf(fmaxf(sc[0][h], sc[1][h]), fmaxf(sc[2][h], sc[3][h]));
+        for (int h = 0; h < HH; h++) {
+            const float x = fmaxf(fmaxf(sc[0][h], sc[1][h]), fmaxf(sc[2][h], sc[3][h]));
             m[h] = warp_max(x);
             l[h] = 0.0f;
         }
 #pragma unroll
         for (int j = 0; j < 4; j++) {
             const bool valid = 32 * j + lane < cur.cnt;
-            float pr[G];
+            float pr[HH];
 #pragma unroll
-            for (int h = 0; h < G; h++) {
+            for (int h = 0; h < HH; h++) {
                 pr[h] = valid ? bt_exp(__fsub_rn(sc[j][h], m[h])) : 0.0f;
                 l[h] = __fadd_rn(l[h], butterfly_sum(pr[h]));
             }
             if (j < cur.np) {
-                float4 *prow = reinterpret_cast<float4 *>(pb + (32 * j + lane) * G * 2);
+                f32x2 *prow = reinterpret_cast<f32x2 *>(pb + (32 * j + lane) * HH * 2);
 #pragma unroll
-                for (int h2 = 0; h2 < HP; h2++) prow[h2] = make_float4(pr[2 * h2], pr[2 * h2], pr[2 * h2 + 1], pr[2 * h2 + 1]);
+                for (int h = 0; h < HH; h++) prow[h] = pk2(pr[h], pr[h]);
             }
         }
         __syncwarp();
         // ---- P*V, piece by piece: lane = dims 4 lane .. 4 lane + 3, keys in order
-        f32x2 o01[G], o23[G];
+        f32x2 o01[HH], o23[HH];
 #pragma unroll
-        for (int h = 0; h < G; h++) o01[h] = o23[h] = 0ull;
+        for (int h = 0; h < HH; h++) o01[h] = o23[h] = 0ull;
         const int vhalf = lane < 16 ? 0 : 4096, vcc = (lane & 15) >> 1, vsub = (lane & 1) * 8;
 #pragma unroll 1
         for (int j = 0; j < cur.np; j++) {
@@ -1784,33 +1820,37 @@ __global__ void __launch_bounds__(AW_WARPS * 32, 2)
             }
             const uint8_t *vb = ring + (pc & 1) * AW_PIECE_BYTES + vhalf + vsub;
             const int kmax = cur.cnt - 32 * j < 32 ? cur.cnt - 32 * j : 32;
-            const float *pj = pb + 32 * j * G * 2;
-#pragma unroll 4
-            for (int kk = 0; kk < 32; kk++) {
-                if (kk < kmax) {
-                    const uint2 v = *reinterpret_cast<const uint2 *>(vb + kk * 128 + ((vcc ^ (kk & 7)) << 4));
-                    const f32x2 v01 = h2_f32x2(v.x), v23 = h2_f32x2(v.y);
-                    const f32x2 *pr = reinterpret_cast<const f32x2 *>(pj + kk * G * 2);  // (p_h, p_h)
+            const float *pj = pb + 32 * j * HH * 2;
+            auto pv_key = [&](int kk) {
+                const uint2 v = *reinterpret_cast<const uint2 *>(vb + kk * 128 + ((vcc ^ (kk & 7)) << 4));
+                const f32x2 v01 = h2_f32x2(v.x), v23 = h2_f32x2(v.y);
+                const f32x2 *pr = reinterpret_cast<const f32x2 *>(pj + kk * HH * 2);  // (p_h, p_h)
 #pragma unroll
-                    for (int h = 0; h < G; h++) {
-                        const f32x2 ph = pr[h];
-                        o01[h] = ffma2(ph, v01, o01[h]);
-                        o23[h] = ffma2(ph, v23, o23[h]);
-                    }
+                for (int h = 0; h < HH; h++) {
+                    const f32x2 ph = pr[h];
+                    o01[h] = ffma2(ph, v01, o01[h]);
+                    o23[h] = ffma2(ph, v23, o23[h]);
                 }
+            };
+            if (kmax == 32) {
+#pragma unroll 8
+                for (int kk = 0; kk < 32; kk++) pv_key(kk);
+            } else {
+#pragma unroll 1
+                for (int kk = 0; kk < kmax; kk++) pv_key(kk);
             }
-            __syncwarp();
             pc++;
         }
         if (!ok) continue;
         // ---- the chunk's partial (acc, m, l), or the output when the context is one chunk
         const int nc = (cur.nk + CH - 1) / CH;
 #pragma unroll
-        for (int h = 0; h < G; h++) {
-            const float2 a01 = upk2(o01[h]), a23 = upk2(o23[h]);
+        for (int hh = 0; hh < HH; hh++) {
+            const int h = hp * HH + hh;
+            const float2 a01 = upk2(o01[hh]), a23 = upk2(o23[hh]);
             if (nc == 1) {
-                const float f = bt_exp(__fsub_rn(m[h], m[h]));
-                const float L = fmaf(l[h], f, 0.0f);
+                const float f = bt_exp(__fsub_rn(m[hh], m[hh]));
+                const float L = fmaf(l[hh], f, 0.0f);
                 float4 o;
                 o.x = __fdiv_rn(fmaf(a01.x, f, 0.0f), L);
                 o.y = __fdiv_rn(fmaf(a01.y, f, 0.0f), L);
@@ -1821,8 +1861,8 @@ __global__ void __launch_bounds__(AW_WARPS * 32, 2)
                 float *pp = p.part + ((((long long)cur.t * p.HK + cur.g) * p.max_chunks + cur.c) * G + h) * ATTN_PART_ROW;
                 *reinterpret_cast<float4 *>(pp + 4 * lane) = make_float4(a01.x, a01.y, a23.x, a23.y);
                 if (lane == 0) {
-                    pp[D] = m[h];
-                    pp[D + 1] = l[h];
+                    pp[D] = m[hh];
+                    pp[D + 1] = l[hh];
                 }
             }
         }
@@ -1833,7 +1873,7 @@ __global__ void __launch_bounds__(AW_WARPS * 32, 2)
         have_n = have && next_item(cur.grp + 1, nxt);
         pg_nxt = have_n ? load_pages(nxt) : 0;
     }
-    if (!ok && lane == 0) {
+    if (!ok && hp == 0 && lane == 0) {
         // a wait ran out: give the copies still requested one more bounded wait before leaving
         for (int s2 = 0; s2 < 2; s2++) {
             long long last = -1;
@@ -1846,10 +1886,16 @@ __global__ void __launch_bounds__(AW_WARPS * 32, 2)
 
 template <int G>
 static cudaError_t launch_attn_warp_g(const AttnArgs &a, const CUtensorMap &tmap, cudaStream_t st, bool pdl) {
+    // a.n_cta = 4 CTAs per SM; fewer when the token tables make the CTA too large for four
+    const size_t smem = attn_warp_smem_bytes(G, a.T);
+    int per = 0;
+    cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per, attn_warp_kernel<G>, AW_WARPS * 32, smem);
+    if (oe != cudaSuccess) return oe;
+    if (per < 1) return cudaErrorInvalidConfiguration;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(a.n_cta);
+    cfg.gridDim = dim3(per < 4 ? a.n_cta / 4 * per : a.n_cta);
     cfg.blockDim = dim3(AW_WARPS * 32);
-    cfg.dynamicSmemBytes = attn_warp_smem_bytes(G, a.T);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
