@@ -572,39 +572,70 @@ cudaError_t launch_down(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl
 // One CTA: per expert, the (token, slot) indices tk = t*K + k that selected it, ascending.
 __global__ void __launch_bounds__(256) group_kernel(const __grid_constant__ GroupArgs p) {
     extern __shared__ int gsm[];
-    const int n = p.T * p.K, tid = threadIdx.x;
-    int *sel = gsm, *cnt = sel + n, *off = cnt + p.NE;
+    const int n = p.T * p.K, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    int *sel = gsm, *cnt = sel + n, *fill = cnt + p.NE;
+    for (int e = tid; e < p.NE; e += blockDim.x) cnt[e] = 0;
     pdl_wait();  // the selections come from the router
     for (int i = tid; i < n; i += blockDim.x) sel[i] = p.sel_ids[i];
     __syncthreads();
-    for (int e = tid; e < p.NE; e += blockDim.x) {
-        int c = 0;
-        for (int i = 0; i < n; i++) c += sel[i] == e;
-        cnt[e] = c;
+    for (int i = tid; i < n; i += blockDim.x) {  // counts (order-free); ids outside [0, NE) are empty slots
+        const int e = sel[i];
+        if (e >= 0 && e < p.NE) atomicAdd(&cnt[e], 1);
     }
     __syncthreads();
-    if (tid == 0) {
-        int na = 0, o = 0, nch = 0;
-        for (int e = 0; e < p.NE; e++) {
-            off[e] = o;
-            o += cnt[e];
-            if (cnt[e]) p.g_active[na++] = e;
-            for (int r0 = 0; r0 < cnt[e]; r0 += GROUP_MAXM) {
-                p.g_chunk_e[nch] = e;
-                p.g_chunk_r0[nch] = r0;
-                nch++;
+    if (warp == 0) {
+        // experts in ascending order: list offsets, the active list and the chunks of at most
+        // GROUP_MAXM rows, by warp-wide exclusive scans
+        int run = 0, crun = 0, arun = 0;
+        for (int e0 = 0; e0 < p.NE; e0 += 32) {
+            const int e = e0 + lane;
+            const int c = e < p.NE ? cnt[e] : 0;
+            const int ch = (c + GROUP_MAXM - 1) / GROUP_MAXM, a = c > 0 ? 1 : 0;
+            int ic = c, ich = ch, ia = a;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int v = __shfl_up_sync(FULL, ic, o), w = __shfl_up_sync(FULL, ich, o),
+                          x = __shfl_up_sync(FULL, ia, o);
+                if (lane >= o) {
+                    ic += v;
+                    ich += w;
+                    ia += x;
+                }
             }
+            if (e < p.NE) {
+                const int off = run + ic - c;
+                fill[e] = off;
+                p.g_count[e] = c;
+                p.g_off[e] = off;
+                if (a) p.g_active[arun + ia - 1] = e;
+                for (int k = 0; k < ch; k++) {
+                    p.g_chunk_e[crun + ich - ch + k] = e;
+                    p.g_chunk_r0[crun + ich - ch + k] = k * GROUP_MAXM;
+                }
+            }
+            run += __shfl_sync(FULL, ic, 31);
+            crun += __shfl_sync(FULL, ich, 31);
+            arun += __shfl_sync(FULL, ia, 31);
         }
-        *p.g_nactive = na;
-        *p.g_nchunks = nch;
-    }
-    __syncthreads();
-    for (int e = tid; e < p.NE; e += blockDim.x) {
-        int o = off[e];
-        for (int i = 0; i < n; i++)
-            if (sel[i] == e) p.g_list[o++] = i;
-        p.g_count[e] = cnt[e];
-        p.g_off[e] = off[e];
+        if (lane == 0) {
+            *p.g_nactive = arun;
+            *p.g_nchunks = crun;
+        }
+        __syncwarp();
+        // each expert's list in ascending selection order: 32 selections at a time, a lane's
+        // place = the lanes before it with the same expert
+        for (int i0 = 0; i0 < n; i0 += 32) {
+            const int i = i0 + lane;
+            const int e = i < n ? sel[i] : -1;
+            const bool valid = e >= 0 && e < p.NE;
+            const unsigned m = __match_any_sync(FULL, valid ? e : -1);
+            const int rank = __popc(m & ((1u << lane) - 1u));
+            const int base = valid ? fill[e] : 0;
+            if (valid) p.g_list[base + rank] = i;
+            __syncwarp();
+            if (valid && lane == __ffs(m) - 1) fill[e] = base + __popc(m);
+            __syncwarp();
+        }
     }
     pdl_trigger();
 }
@@ -861,13 +892,13 @@ __global__ void __launch_bounds__(NWARP * 32, 1) down_grouped_kernel(const __gri
         for (int g = r.done; g < r.issued; g++) mbar_wait(&r.bars[g % r.nst], (g / r.nst) & 1, nullptr);
 }
 
-// grid T: x = ffn_in + the K expert rows scaled by their weights and summed in the reference's
+// grid (T, E / 256): x = ffn_in + the K expert rows scaled by their weights and summed in the reference's
 // order (the single-token pairs of expert_ffn_single, or the block path's sequential sum).
 __global__ void __launch_bounds__(256) down_combine_kernel(const __grid_constant__ ExpertArgs p) {
     const int t = blockIdx.x;
     pdl_wait();
     const float *w = p.sel_w + t * p.K;
-    for (int row = threadIdx.x; row < p.E; row += blockDim.x) {
+    for (int row = blockIdx.y * blockDim.x + threadIdx.x; row < p.E; row += gridDim.y * blockDim.x) {
         float o[MAX_K];
         for (int k = 0; k < p.K; k++) {
             const long long slot = (long long)t * p.K + k;
@@ -951,7 +982,7 @@ size_t down_grouped_smem_bytes(const ExpertArgs &a) {
 int down_group_rows(const ExpertArgs &a) { return 32 / a.d_nsb; }
 
 cudaError_t launch_group(const GroupArgs &a, cudaStream_t st, bool pdl) {
-    const size_t smem = ((size_t)a.T * a.K + 2 * (size_t)a.NE + 1) * 4;
+    const size_t smem = ((size_t)a.T * a.K + 2 * (size_t)a.NE + 1) * 4;  // selections, counts, fill
     return launch_ex(group_kernel, dim3(1), dim3(256), smem, st, pdl, a);
 }
 cudaError_t launch_gateup_grouped(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl) {
@@ -963,7 +994,7 @@ cudaError_t launch_down_grouped(const ExpertArgs &a, int grid, cudaStream_t st, 
                      pdl, a);
 }
 cudaError_t launch_down_combine(const ExpertArgs &a, cudaStream_t st, bool pdl) {
-    return launch_ex(down_combine_kernel, dim3(a.T), dim3(256), 0, st, pdl, a);
+    return launch_ex(down_combine_kernel, dim3(a.T, (a.E + 255) / 256), dim3(256), 0, st, pdl, a);
 }
 
 // ====================================================================== router
