@@ -74,6 +74,15 @@ __device__ __forceinline__ f32x2 ffma2(f32x2 a, f32x2 b, f32x2 c) {
     asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
     return d;
 }
+// (lo, lo) and (hi, hi) of w as two f32x2 of exact f32 values, each half converted twice so the
+// pairs need no register moves (FMA pipe)
+__device__ __forceinline__ void h2_bcast2(uint32_t w, f32x2 &lo, f32x2 &hi) {
+    asm("{\n\t.reg .b16 l, h;\n\t.reg .f32 a, b, c, d;\n\tmov.b32 {l, h}, %2;\n\t"
+        "add.rn.f32.f16 a, l, %3;\n\tadd.rn.f32.f16 b, l, %3;\n\tadd.rn.f32.f16 c, h, %3;\n\t"
+        "add.rn.f32.f16 d, h, %3;\n\tmov.b64 %0, {a, b};\n\tmov.b64 %1, {c, d};\n\t}"
+        : "=l"(lo), "=l"(hi)
+        : "r"(w), "f"(-0.0f));
+}
 
 __device__ __forceinline__ float fma_f16(uint16_t a, uint16_t b, float c) {
     float d;

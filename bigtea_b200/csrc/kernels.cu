@@ -1585,15 +1585,6 @@ __device__ __forceinline__ f32x2 h2_f32x2(uint32_t w) {
         : "r"(w), "f"(-0.0f));
     return r;
 }
-// (lo, lo) and (hi, hi) of w as two f32x2 of exact f32 values, each half converted twice so the
-// pairs need no register moves (FMA pipe)
-__device__ __forceinline__ void h2_bcast2(uint32_t w, f32x2 &lo, f32x2 &hi) {
-    asm("{\n\t.reg .b16 l, h;\n\t.reg .f32 a, b, c, d;\n\tmov.b32 {l, h}, %2;\n\t"
-        "add.rn.f32.f16 a, l, %3;\n\tadd.rn.f32.f16 b, l, %3;\n\tadd.rn.f32.f16 c, h, %3;\n\t"
-        "add.rn.f32.f16 d, h, %3;\n\tmov.b64 %0, {a, b};\n\tmov.b64 %1, {c, d};\n\t}"
-        : "=l"(lo), "=l"(hi)
-        : "r"(w), "f"(-0.0f));
-}
 // barrier of one warp pair (64 threads, named barrier 1 + pair) that also ANDs v over it
 __device__ __forceinline__ bool pair_sync_and(int pair, bool v) {
     int r;

@@ -755,21 +755,56 @@ __device__ bool attn_half(const StepArgs &p, const LayerDev &L, const StepSmem &
 #pragma unroll
         for (int kk = 0; kk < 8; kk++) off[kk] = kk * 128 + ((cc ^ kk) << 4);
         const float *pb0 = ps + hq * HPT;
-        for (int j0 = 0; j0 < cnt; j0 += 8) {
-            const uint8_t *vb = vcol + j0 * 128;
-            const float *pb = pb0 + j0 * G;
+        // heads in f32x2 pairs when HPT is even: (acc_d[h], acc_d[h+1]) += (p_h, p_h+1) *
+        // (v_d, v_d), each v converted twice into both halves of its pair (C8: one fmaf a term)
+        constexpr int NPR = HPT % 2 == 0 ? HPT / 2 : 1;
+        f32x2 pa0[NPR], pa1[NPR];
 #pragma unroll
-            for (int kk = 0; kk < 8; kk++) {
-                if (j0 + kk < cnt) {
-                    const float2 vf = h2f2_fma(*reinterpret_cast<const uint32_t *>(vb + off[kk]));
-                    float pj[HPT];
-                    lds_n<HPT>(pj, pb + kk * G);
+        for (int j = 0; j < NPR; j++) pa0[j] = pa1[j] = 0ull;
+        auto pv_key = [&](const uint8_t *vb, const float *pb, int kk) {
+            const uint32_t vw = *reinterpret_cast<const uint32_t *>(vb + off[kk]);
+            if constexpr (HPT % 2 == 0) {
+                f32x2 vx, vy;
+                h2_bcast2(vw, vx, vy);
+                const f32x2 *pp = reinterpret_cast<const f32x2 *>(pb + kk * G);
 #pragma unroll
-                    for (int h = 0; h < HPT; h++) {
-                        acc0[h] = fmaf(pj[h], vf.x, acc0[h]);
-                        acc1[h] = fmaf(pj[h], vf.y, acc1[h]);
-                    }
+                for (int j = 0; j < NPR; j++) {
+                    const f32x2 pj = pp[j];
+                    pa0[j] = ffma2(pj, vx, pa0[j]);
+                    pa1[j] = ffma2(pj, vy, pa1[j]);
                 }
+            } else {
+                const float2 vf = h2f2_fma(vw);
+                float pj[HPT];
+                lds_n<HPT>(pj, pb + kk * G);
+#pragma unroll
+                for (int h = 0; h < HPT; h++) {
+                    acc0[h] = fmaf(pj[h], vf.x, acc0[h]);
+                    acc1[h] = fmaf(pj[h], vf.y, acc1[h]);
+                }
+            }
+        };
+        if (cnt == CH) {  // a full chunk: no per-key tests, loads free to run ahead
+#pragma unroll 2
+            for (int j0 = 0; j0 < CH; j0 += 8) {
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++) pv_key(vcol + j0 * 128, pb0 + j0 * G, kk);
+            }
+        } else {
+            for (int j0 = 0; j0 < cnt; j0 += 8) {
+#pragma unroll
+                for (int kk = 0; kk < 8; kk++)
+                    if (j0 + kk < cnt) pv_key(vcol + j0 * 128, pb0 + j0 * G, kk);
+            }
+        }
+        if constexpr (HPT % 2 == 0) {
+#pragma unroll
+            for (int j = 0; j < NPR; j++) {
+                const float2 a = upk2(pa0[j]), b = upk2(pa1[j]);
+                acc0[2 * j] = a.x;
+                acc0[2 * j + 1] = a.y;
+                acc1[2 * j] = b.x;
+                acc1[2 * j + 1] = b.y;
             }
         }
     }
