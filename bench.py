@@ -212,11 +212,15 @@ def run_ours(args, rank, world, local_rank):
     ms = max_over_ranks(dev_ms, world)
     value = world * args.steps / (ms / 1e3)
 
-    # e2e: bt_forward with a host token in and host logits out every step
-    e2e_steps = max(4, args.steps // 4)
+    # e2e: bt_forward with a host token in and host logits out every step, after its own
+    # untimed warm-up calls (the first direct launches after the graph replays cost a few ms)
+    e2e_steps = max(16, args.steps)
+    nxt = int(toks[-1, 0])
+    for _ in range(max(3, args.warmup)):
+        lg = runner.forward_cached(cache, [nxt], cache.len())
+        nxt = int(np.argmax(lg))
     sync_ranks(world)
     t0 = time.perf_counter()
-    nxt = int(toks[-1, 0])
     for _ in range(e2e_steps):
         lg = runner.forward_cached(cache, [nxt], cache.len())
         nxt = int(np.argmax(lg))

@@ -148,6 +148,16 @@ struct bt_engine {
     DevBuf tokens, seq_of, local_idx, pos_of, single, x_rows;
     DevBuf st_seq, st_ntok, st_lrow, next_tok, gen_out, gen_count, logits, amax;
     DevBuf err;
+    // pinned host staging of a call's small transfers: the step plan's vectors go up from
+    // plan_host without a host wait (plan_ev marks when its last copies have been read), and a
+    // call of up to STEP_MAX_T sequences brings its error word and logits back through err_host
+    // and logits_host behind one stream wait
+    uint8_t *plan_host = nullptr;
+    size_t plan_seg = 0;  // bytes of one plan vector's slot in plan_host (8 slots)
+    cudaEvent_t plan_ev = nullptr;
+    bool plan_ev_live = false;
+    int *err_host = nullptr;
+    float *logits_host = nullptr;
     int part_chunks = 0;
     size_t gen_cap = 0;
     uint64_t weight_bytes = 0;
@@ -490,6 +500,13 @@ static int alloc_scratch(bt_engine *e) {
     CK(cudaMemset(e->amax.p, 0, (size_t)e->max_out * 8));
     CK(e->err.alloc(4));
     CK(cudaMemset(e->err.p, 0, 4));
+    const int plan_rows = TB > e->max_out ? TB : e->max_out;
+    e->plan_seg = ((size_t)plan_rows * 4 + 255) & ~(size_t)255;
+    if (!e->plan_host) CK(cudaHostAlloc((void **)&e->plan_host, 8 * e->plan_seg, cudaHostAllocDefault));
+    if (!e->plan_ev) CK(cudaEventCreateWithFlags(&e->plan_ev, cudaEventDisableTiming));
+    if (!e->err_host) CK(cudaHostAlloc((void **)&e->err_host, 4, cudaHostAllocDefault));
+    if (!e->logits_host)
+        CK(cudaHostAlloc((void **)&e->logits_host, (size_t)STEP_MAX_T * d.n_vocab * 4, cudaHostAllocDefault));
     return BT_OK;
 }
 
@@ -813,6 +830,10 @@ extern "C" void bt_engine_destroy(bt_engine *e) {
     if (e->x_sel_host) cudaFreeHost(e->x_sel_host);
     if (e->x_slot_host) cudaFreeHost(e->x_slot_host);
     if (e->x_ev) cudaEventDestroy(e->x_ev);
+    if (e->plan_host) cudaFreeHost(e->plan_host);
+    if (e->plan_ev) cudaEventDestroy(e->plan_ev);
+    if (e->err_host) cudaFreeHost(e->err_host);
+    if (e->logits_host) cudaFreeHost(e->logits_host);
     for (auto &p : e->ev_pool) {
         cudaEventDestroy(p.first);
         cudaEventDestroy(p.second);
@@ -1252,19 +1273,34 @@ static int run_gemv_batched(bt_engine *e, const QMat *const *mats, const int *of
     return BT_OK;
 }
 
+// The plan's vectors are copied into the engine's pinned staging and sent from there, so the
+// host does not wait for the device here. The staging is rewritten only once the previous
+// plan's copies have run (plan_ev); in stream order those copies also follow every kernel of
+// the step before, so no step reads a plan vector that a later plan overwrites.
 static int upload_plan(bt_engine *e, const StepPlan &p) {
     cudaStream_t st = e->st;
-    CK(cudaMemcpyAsync(e->tokens.p, p.tokens.data(), p.T * 4, cudaMemcpyHostToDevice, st));
-    CK(cudaMemcpyAsync(e->seq_of.p, p.seq_of.data(), p.T * 4, cudaMemcpyHostToDevice, st));
-    CK(cudaMemcpyAsync(e->local_idx.p, p.local_idx.data(), p.T * 4, cudaMemcpyHostToDevice, st));
-    CK(cudaMemcpyAsync(e->single.p, p.single.data(), p.T, cudaMemcpyHostToDevice, st));
-    CK(cudaMemcpyAsync(e->st_seq.p, p.st_seq.data(), p.st_seq.size() * 4, cudaMemcpyHostToDevice, st));
-    CK(cudaMemcpyAsync(e->st_ntok.p, p.st_ntok.data(), p.st_ntok.size() * 4, cudaMemcpyHostToDevice, st));
-    CK(cudaMemcpyAsync(e->st_lrow.p, p.st_lrow.data(), p.st_lrow.size() * 4, cudaMemcpyHostToDevice, st));
-    if (!p.x_rows.empty())
-        CK(cudaMemcpyAsync(e->x_rows.p, p.x_rows.data(), p.x_rows.size() * 4, cudaMemcpyHostToDevice, st));
-    // plan vectors are host locals of the caller: wait before they go out of scope
-    CK(cudaStreamSynchronize(st));
+    if (e->plan_ev_live) {
+        CK(cudaEventSynchronize(e->plan_ev));
+        e->plan_ev_live = false;
+    }
+    int slot = 0;
+    auto put = [&](DevBuf &dst, const void *src, size_t n) -> cudaError_t {
+        if (n == 0) return cudaSuccess;
+        if (n > e->plan_seg) return cudaErrorInvalidValue;
+        uint8_t *h = e->plan_host + (size_t)slot++ * e->plan_seg;
+        memcpy(h, src, n);
+        return cudaMemcpyAsync(dst.p, h, n, cudaMemcpyHostToDevice, st);
+    };
+    CK(put(e->tokens, p.tokens.data(), (size_t)p.T * 4));
+    CK(put(e->seq_of, p.seq_of.data(), (size_t)p.T * 4));
+    CK(put(e->local_idx, p.local_idx.data(), (size_t)p.T * 4));
+    CK(put(e->single, p.single.data(), (size_t)p.T));
+    CK(put(e->st_seq, p.st_seq.data(), p.st_seq.size() * 4));
+    CK(put(e->st_ntok, p.st_ntok.data(), p.st_ntok.size() * 4));
+    CK(put(e->st_lrow, p.st_lrow.data(), p.st_lrow.size() * 4));
+    CK(put(e->x_rows, p.x_rows.data(), p.x_rows.size() * 4));
+    CK(cudaEventRecord(e->plan_ev, st));
+    e->plan_ev_live = true;
     return BT_OK;
 }
 
@@ -1910,11 +1946,9 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
     return BT_OK;
 }
 
-static int check_err(bt_engine *e) {
-    int h = 0;
-    CK(cudaMemcpyAsync(&h, e->err.p, 4, cudaMemcpyDeviceToHost, e->st));
-    int r = wait_stream(e);
-    if (r) return r;
+// The device error word `h`, read back after the stream was waited for: nonzero clears it and
+// fails the call.
+static int err_word(bt_engine *e, int h) {
     if (h) {
         CK(cudaMemsetAsync(e->err.p, 0, 4, e->st));
         CK(cudaStreamSynchronize(e->st));
@@ -1922,6 +1956,15 @@ static int check_err(bt_engine *e) {
         return fail(BT_ERR_INVALID, "a kernel rejected an index (token id out of range?)");
     }
     return BT_OK;
+}
+
+static int check_err(bt_engine *e) {
+    int local = 0;
+    int *h = e->err_host ? e->err_host : &local;  // the single-op engines have no pinned staging
+    CK(cudaMemcpyAsync(h, e->err.p, 4, cudaMemcpyDeviceToHost, e->st));
+    int r = wait_stream(e);
+    if (r) return r;
+    return err_word(e, *h);
 }
 
 extern "C" int bt_forward(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const uint32_t *tokens,
@@ -1992,10 +2035,19 @@ extern "C" int bt_forward(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, cons
         e->last_T = p.T;
         e->last_first = g - p.T;
     }
-    if ((r = check_err(e))) return r;
-    if (logits_out)
-        CK(cudaMemcpyAsync(logits_out, e->logits.p, (size_t)n_seqs * e->d.n_vocab * 4, cudaMemcpyDeviceToHost, e->st));
-    if ((r = wait_stream(e))) return r;
+    const size_t lbytes = (size_t)n_seqs * e->d.n_vocab * 4;
+    if (logits_out && n_seqs <= (uint32_t)STEP_MAX_T) {
+        // error word and logits through pinned staging, behind one wait
+        CK(cudaMemcpyAsync(e->err_host, e->err.p, 4, cudaMemcpyDeviceToHost, e->st));
+        CK(cudaMemcpyAsync(e->logits_host, e->logits.p, lbytes, cudaMemcpyDeviceToHost, e->st));
+        if ((r = wait_stream(e))) return r;
+        if ((r = err_word(e, *e->err_host))) return r;
+        memcpy(logits_out, e->logits_host, lbytes);
+    } else {
+        if ((r = check_err(e))) return r;
+        if (logits_out) CK(cudaMemcpyAsync(logits_out, e->logits.p, lbytes, cudaMemcpyDeviceToHost, e->st));
+        if ((r = wait_stream(e))) return r;
+    }
     for (uint32_t i = 0; i < n_seqs; i++) {
         uint32_t s = seq_ids[i];
         kv->len[s] += n_tokens[i];

@@ -840,48 +840,77 @@ __device__ bool attn_half(const StepArgs &p, const LayerDev &L, const StepSmem &
     return true;
 }
 
-// One head's merge of its chunk partials (C8): M = max m_c, f_c = exp(m_c - M),
-// L = sum_c l_c f_c and O = sum_c acc_c f_c in chunk order, out = O / L. Threads < 128 load
-// their dimension's first 64 partials in the same round trip as the m/l loads of threads >= 128.
-__device__ void combine_head(const float *part, int cstride, int nc, float *out, float *cbuf, float *misc) {
+// One slice of one head's merge of its chunk partials (C8): M = max m_c, f_c = exp(m_c - M),
+// L = sum_c l_c f_c and O = sum_c acc_c f_c in chunk order, out = O / L, for the `nd` output
+// dimensions starting at `part` (a head's row plus the slice offset; m and l sit at
+// `ml[c * cstride]` and one float later). The slice's partials come into `stage` (shared memory,
+// STEP_ACT_BYTES) by 16-byte cp.async copies issued from a rolled loop, in the same round trip as
+// the m/l loads, so the code stays small (the phase runs from a cold instruction cache every
+// layer) and a head split over several CTAs still reads each partial once.
+__device__ __forceinline__ void cp_async16_s(uint32_t dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ void combine_slice(const float *part, const float *ml, int cstride, int nc, int nd, float *out,
+                              float *cbuf, float *stage, float *misc) {
     const int tid = threadIdx.x;
     float *cm = cbuf, *cl = cm + nc, *cf = cl + nc;
-    constexpr int B = 64;
-    const float *pd = part + tid;
-    float a[B];
-    auto load = [&](int c0) {
-#pragma unroll
-        for (int kk = 0; kk < B; kk++) a[kk] = c0 + kk < nc ? __ldcg(pd + (c0 + kk) * cstride) : 0.0f;
-    };
-    if (tid < 128) {
-        load(0);
-    } else {
-        for (int cc = tid - 128; cc < nc; cc += STEP_THREADS - 128) {
-            cm[cc] = __ldcg(part + cc * cstride + 128);
-            cl[cc] = __ldcg(part + cc * cstride + 129);
+    const int vpc = nd / 4;                            // 16-byte vectors per chunk row of the slice
+    const int pc = (STEP_ACT_BYTES / 4) / nd;          // chunks per staged piece
+    const uint32_t st_s = smem_u32(stage);
+    auto issue = [&](int c0) {
+        const int n = (nc - c0 < pc ? nc - c0 : pc) * vpc;
+#pragma unroll 1
+        for (int e = tid; e < n; e += STEP_THREADS) {
+            const int c = e / vpc, v = e - c * vpc;
+            cp_async16_s(st_s + (uint32_t)e * 16u, part + (long long)(c0 + c) * cstride + 4 * v);
         }
+        asm volatile("cp.async.commit_group;" ::: "memory");
+    };
+    float m0 = 0.0f, l0 = 0.0f;
+    const bool has_ml = tid < nc;
+    if (has_ml) {
+        m0 = __ldcg(ml + (long long)tid * cstride);
+        l0 = __ldcg(ml + (long long)tid * cstride + 1);
+    }
+    issue(0);
+    for (int c = tid + STEP_THREADS; c < nc; c += STEP_THREADS) {
+        cm[c] = __ldcg(ml + (long long)c * cstride);
+        cl[c] = __ldcg(ml + (long long)c * cstride + 1);
+    }
+    if (has_ml) {
+        cm[tid] = m0;
+        cl[tid] = l0;
     }
     __syncthreads();
     float M = -__int_as_float(0x7f800000);
-    for (int cc = 0; cc < nc; cc++) M = fmaxf(M, cm[cc]);
-    for (int cc = tid; cc < nc; cc += STEP_THREADS) cf[cc] = bt_exp(__fsub_rn(cm[cc], M));
+#pragma unroll 4
+    for (int c = 0; c < nc; c++) M = fmaxf(M, cm[c]);
+    for (int c = tid; c < nc; c += STEP_THREADS) cf[c] = bt_exp(__fsub_rn(cm[c], M));
     __syncthreads();
-    float O = 0.0f;
-    if (tid < 128) {
-#pragma unroll 1
-        for (int c0 = 0; c0 < nc; c0 += B) {
-            if (c0) load(c0);
-#pragma unroll
-            for (int kk = 0; kk < B; kk++)
-                if (c0 + kk < nc) O = fmaf(a[kk], cf[c0 + kk], O);
-        }
-    } else if (tid == 128) {
+    if (tid == STEP_THREADS - 1) {  // nd <= 128: never one of the dimension threads
         float Lh = 0.0f;
-        for (int cc = 0; cc < nc; cc++) Lh = fmaf(cl[cc], cf[cc], Lh);
+#pragma unroll 4
+        for (int c = 0; c < nc; c++) Lh = fmaf(cl[c], cf[c], Lh);
         misc[1] = Lh;
     }
+    float O = 0.0f;
+#pragma unroll 1
+    for (int c0 = 0; c0 < nc; c0 += pc) {
+        if (c0) {
+            __syncthreads();  // the previous piece has been read
+            issue(c0);
+        }
+        asm volatile("cp.async.wait_all;" ::: "memory");
+        __syncthreads();
+        const int n = nc - c0 < pc ? nc - c0 : pc;
+        if (tid < nd) {
+            const float *col = stage + tid;
+#pragma unroll 4
+            for (int c = 0; c < n; c++) O = fmaf(col[c * nd], cf[c0 + c], O);
+        }
+    }
     __syncthreads();
-    if (tid < 128) out[tid] = __fdiv_rn(O, misc[1]);
+    if (tid < nd) out[tid] = __fdiv_rn(O, misc[1]);
     __syncthreads();
 }
 
@@ -1125,16 +1154,21 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             int multi = 0;
             for (int t = 0; t < T; t++) multi += (sm.pos[t] + 1 > ATTN_CHUNK);
             if (multi) {
-                const int n_ci = T * p.H;
+                // each head in `split` slices of 128 / split dimensions, as many as the grid covers
+                const int split = T * p.H * 4 <= (int)gridDim.x ? 4 : T * p.H * 2 <= (int)gridDim.x ? 2 : 1;
+                const int nd = 128 / split;
+                const int n_ci = T * p.H * split;
                 for (int ci = blockIdx.x; ci < n_ci; ci += gridDim.x) {
-                    const int t = ci / p.H, hd = ci - t * p.H;
+                    const int th = ci / split, q = ci - th * split;
+                    const int t = th / p.H, hd = th - t * p.H;
                     const int nc = (sm.pos[t] + 1 + ATTN_CHUNK - 1) / ATTN_CHUNK;
                     if (nc == 1) continue;
                     const int g = hd / G, h = hd % G;
-                    const float *part =
+                    const float *row =
                         p.part + (((long long)t * p.HK + g) * p.max_chunks) * G * PART_ROW + (long long)h * PART_ROW;
-                    combine_head(part, G * PART_ROW, nc, p.att + (long long)t * QW + hd * 128, sm.cbuf,
-                                 sm.misc);
+                    combine_slice(row + q * nd, row + 128, G * PART_ROW, nc, nd,
+                                  p.att + (long long)t * QW + hd * 128 + q * nd, sm.cbuf,
+                                  reinterpret_cast<float *>(sm.act), sm.misc);
                 }
                 if (!grid_sync(p.bar, epoch, p.err, TR(il, 2))) return;
             }
