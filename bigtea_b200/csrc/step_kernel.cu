@@ -766,12 +766,24 @@ __device__ bool attn_half(const StepArgs &p, const LayerDev &L, const StepSmem &
             if constexpr (HPT % 2 == 0) {
                 f32x2 vx, vy;
                 h2_bcast2(vw, vx, vy);
-                const f32x2 *pp = reinterpret_cast<const f32x2 *>(pb + kk * G);
+                if constexpr (NPR % 2 == 0) {  // two head pairs per 16-byte load (row offsets are 16-byte multiples)
+                    const ulonglong2 *pq = reinterpret_cast<const ulonglong2 *>(pb + kk * G);
 #pragma unroll
-                for (int j = 0; j < NPR; j++) {
-                    const f32x2 pj = pp[j];
-                    pa0[j] = ffma2(pj, vx, pa0[j]);
-                    pa1[j] = ffma2(pj, vy, pa1[j]);
+                    for (int j2 = 0; j2 < NPR / 2; j2++) {
+                        const ulonglong2 w = pq[j2];
+                        pa0[2 * j2] = ffma2(w.x, vx, pa0[2 * j2]);
+                        pa1[2 * j2] = ffma2(w.x, vy, pa1[2 * j2]);
+                        pa0[2 * j2 + 1] = ffma2(w.y, vx, pa0[2 * j2 + 1]);
+                        pa1[2 * j2 + 1] = ffma2(w.y, vy, pa1[2 * j2 + 1]);
+                    }
+                } else {
+                    const f32x2 *pp = reinterpret_cast<const f32x2 *>(pb + kk * G);
+#pragma unroll
+                    for (int j = 0; j < NPR; j++) {
+                        const f32x2 pj = pp[j];
+                        pa0[j] = ffma2(pj, vx, pa0[j]);
+                        pa1[j] = ffma2(pj, vy, pa1[j]);
+                    }
                 }
             } else {
                 const float2 vf = h2f2_fma(vw);
