@@ -81,29 +81,39 @@ __device__ __forceinline__ unsigned long long global_ns() {
 // One monotonic arrival counter, zeroed before each launch: barrier n of a launch completes
 // when the counter reaches n * gridDim.x. Thread 0 arrives with a release-add after the CTA's
 // __syncthreads and waits with relaxed polls followed by one acquire fence. The wait is
-// bounded: a timeout sets the engine's error word, after which every CTA leaves at its next
-// barrier.
+// bounded: a timeout sets the engine's error word and BAR_POISON in the counter. A CTA that
+// finds BAR_POISON leaves, so every CTA leaves at its next barrier; the poll that ends the
+// wait brings the poison with it, and no other global read follows the barrier. The error
+// word itself is read once, at the first barrier, for an error an earlier launch left.
+constexpr unsigned BAR_POISON = 0x80000000u;  // arrivals stay far below bit 31
+__device__ __forceinline__ void poison_barrier(unsigned *bar) { atomicOr(bar, BAR_POISON); }
+
 __device__ __noinline__ bool grid_sync(unsigned *bar, unsigned &epoch, int *err, unsigned long long *trace_row = nullptr) {
     __syncthreads();
     epoch += 1;
+    bool bad = false;
     if (threadIdx.x == 0) {
         if (trace_row) trace_row[blockIdx.x] = global_ns();
         const unsigned target = epoch * gridDim.x;
         asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(bar), "r"(1u) : "memory");
-        if (ld_relaxed_gpu(bar) < target) {
+        unsigned v = ld_relaxed_gpu(bar);
+        if (v < target) {
             const long long t0 = clock64();
-            while (ld_relaxed_gpu(bar) < target) {
+            while ((v = ld_relaxed_gpu(bar)) < target) {
                 if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
                     atomicOr(err, ERR_WAIT_TIMEOUT);
+                    poison_barrier(bar);
+                    v = BAR_POISON;
                     break;
                 }
             }
         }
         asm volatile("fence.acq_rel.gpu;" ::: "memory");
+        bad = v >= BAR_POISON;
+        if (epoch == 1) bad |= *reinterpret_cast<volatile int *>(err) != 0;
         if (trace_row && blockIdx.x == 0) trace_row[gridDim.x] = global_ns();
     }
-    __syncthreads();
-    return *reinterpret_cast<volatile int *>(err) == 0;
+    return !__syncthreads_or(bad);
 }
 
 // ------------------------------------------------------------------ per-warp TMA ring
@@ -1074,7 +1084,10 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             yv = okt ? yv : 0.0f;
             x0[i] = yv;
             if (blockIdx.x == 0) p.x[i] = yv;
-            if (!okt && e == 0) atomicOr(p.err, ERR_BAD_INDEX);
+            if (!okt && e == 0) {
+                atomicOr(p.err, ERR_BAD_INDEX);
+                poison_barrier(p.bar);
+            }
         }
         if (blockIdx.x == 0 && tid < T) p.pos_of[tid] = sm.pos[tid];
         __syncthreads();
