@@ -66,9 +66,9 @@ struct StepSmem {
 };
 
 // ------------------------------------------------------------------ grid barrier
-__device__ __forceinline__ unsigned ld_relaxed_gpu(const unsigned *p) {
+__device__ __forceinline__ unsigned ld_acquire_gpu(const unsigned *p) {
     unsigned v;
-    asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
     return v;
 }
 
@@ -80,11 +80,12 @@ __device__ __forceinline__ unsigned long long global_ns() {
 
 // One monotonic arrival counter, zeroed before each launch: barrier n of a launch completes
 // when the counter reaches n * gridDim.x. Thread 0 arrives with a release-add after the CTA's
-// __syncthreads and waits with relaxed polls followed by one acquire fence. The wait is
-// bounded: a timeout sets the engine's error word and BAR_POISON in the counter. A CTA that
-// finds BAR_POISON leaves, so every CTA leaves at its next barrier; the poll that ends the
-// wait brings the poison with it, and no other global read follows the barrier. The error
-// word itself is read once, at the first barrier, for an error an earlier launch left.
+// __syncthreads and waits with acquire polls: the poll that sees the count complete orders the
+// CTA's later reads after every arrival's writes (the adds form one release sequence). The
+// wait is bounded: a timeout sets the engine's error word and BAR_POISON in the counter. A CTA
+// that finds BAR_POISON leaves, so every CTA leaves at its next barrier; the poll that ends the
+// wait brings the poison with it, and no other global read follows the barrier. The error word
+// itself is read once, at the first barrier, for an error an earlier launch left.
 constexpr unsigned BAR_POISON = 0x80000000u;  // arrivals stay far below bit 31
 __device__ __forceinline__ void poison_barrier(unsigned *bar) { atomicOr(bar, BAR_POISON); }
 
@@ -96,19 +97,19 @@ __device__ __noinline__ bool grid_sync(unsigned *bar, unsigned &epoch, int *err,
         if (trace_row) trace_row[blockIdx.x] = global_ns();
         const unsigned target = epoch * gridDim.x;
         asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(bar), "r"(1u) : "memory");
-        unsigned v = ld_relaxed_gpu(bar);
+        unsigned v = ld_acquire_gpu(bar);
         if (v < target) {
             const long long t0 = clock64();
-            while ((v = ld_relaxed_gpu(bar)) < target) {
+            while ((v = ld_acquire_gpu(bar)) < target) {
                 if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
                     atomicOr(err, ERR_WAIT_TIMEOUT);
                     poison_barrier(bar);
                     v = BAR_POISON;
+                    asm volatile("fence.acq_rel.gpu;" ::: "memory");
                     break;
                 }
             }
         }
-        asm volatile("fence.acq_rel.gpu;" ::: "memory");
         bad = v >= BAR_POISON;
         if (epoch == 1) bad |= *reinterpret_cast<volatile int *>(err) != 0;
         if (trace_row && blockIdx.x == 0) trace_row[gridDim.x] = global_ns();
