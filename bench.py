@@ -137,11 +137,58 @@ def expert_bytes(cfg, per_expert=False):
     return float(np.mean(gu)), float(np.mean(dn))
 
 
-def cpu_baseline_from_engine(engine, cache, cfg, ctx, n_tokens, threads, seed):
-    """Time the CPU oracle decoding n_tokens from the same weights (copied back from HBM)
-    and the same KV cache; the first token's logits are checked against the GPU's."""
+def workload_config(config_name, cfg, shape, ctx, world):
+    """The `config` dict of both arms' JSON lines (identical for the same workload and N)."""
+    resident = sum(_kq_bytes(ty, int(np.prod(ne))) for _, ty, ne, _ in cfg.tensor_specs())
+    return {"workload": f"{config_name}: {shape}, batch 1 greedy decode at context {ctx}", "batch": 1,
+            "context": ctx, "parallelism": "replicas" if world > 1 else "single GPU",
+            "l2": f"inputs larger than L2: {decode_bytes_per_token(cfg, ctx) / 1e9:.2f} GB of weights and KV read "
+                  f"per step ({resident / 1e9:.1f} GB of weights resident)"}
+
+
+def _kq_bytes(ty, n):
+    return n * 4 if ty == 0 else n * 2 if ty == 1 else n // 256 * (144 if ty == 12 else 210)
+
+
+def decode_bytes_per_token(cfg, ctx):
+    """Algorithmic bytes one batch-1 decode token reads at context ctx: the attention weights,
+    norms and router of every layer, the K selected experts' gate/up/down, the output head, and
+    the K/V of ctx + 1 positions (the new one included); the embedding row is negligible."""
+    tot = 0
+    for name, ty, ne, _ in cfg.tensor_specs():
+        n = 1
+        for d in ne:
+            n *= d
+        if name == "token_embd.weight":
+            continue
+        b = _kq_bytes(ty, n)
+        if "_exps." in name:
+            b = b // cfg.n_expert * cfg.n_expert_used
+        tot += b
+    return tot + cfg.n_layer * 2 * cfg.n_head_kv * cfg.head_dim * 2 * (ctx + 1)
+
+
+def host_info(threads):
+    """CPU model, the threads used, and the host's STREAM-style copy bandwidth (read + write)."""
     from oracle import pyoracle as orc
-    import bigtea_b200 as bt
+
+    model = "unknown"
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                model = line.split(":", 1)[1].strip()
+                break
+    except OSError:
+        pass
+    gbs = orc.lib().or_copy_gbs(1 << 30, threads, 3)
+    return {"cpu_model": model, "cores": threads, "host_copy_gbs": round(gbs, 1)}
+
+
+def cpu_baseline_from_engine(engine, cache, cfg, ctx, n_tokens, threads, tok0):
+    """The CPU oracle decoding n_tokens from the same weights (copied back from HBM) and the same
+    first ctx cache positions, starting with token tok0 at position ctx. Returns the tok/s and the
+    logits of that first step, which the caller compares with the GPU's for the same position."""
+    from oracle import pyoracle as orc
     from bigtea_b200.gguf import tensor_nbytes
 
     W = {}
@@ -156,7 +203,7 @@ def cpu_baseline_from_engine(engine, cache, cfg, ctx, n_tokens, threads, seed):
         model.write_kv_layer(il, k, v)
     model.set_len(ctx)
     orc.lib().or_set_threads(threads)
-    tok = int(np.random.default_rng(seed).integers(0, cfg.n_vocab))
+    tok = tok0
     t0 = time.perf_counter()
     first = None
     for i in range(n_tokens):
@@ -201,6 +248,12 @@ def run_ours(args, rank, world, local_rank):
         cache.set_positions(args.ctx)
         tok = int(rng.integers(0, cfg.n_vocab))
     prefill_s = time.perf_counter() - t0
+    # the first decode position: one bt_forward step (the persistent kernel at batch 1) whose
+    # logits the CPU oracle reproduces below from the same weights and the same first ctx cache
+    # positions -- the parity check of the measured path
+    tok0 = tok
+    logits0 = runner.forward_cached(cache, [tok0], args.ctx)
+    tok = int(np.argmax(logits0))
     # warm-up (also captures the step graph), then K timed graph replays
     runner.generate_greedy(cache, [tok], args.warmup)
     sync_ranks(world)
@@ -295,28 +348,37 @@ def run_ours(args, rank, world, local_rank):
     result = None
     xcache = None
     if rank == 0:
-        cpu = None
+        cpu, parity = None, {"status": "not checked (--no-cpu)"}
         if not args.no_cpu:
             threads = os.cpu_count() or 1
-            ctx_now = cache.len()
-            cpu_tps, _ = cpu_baseline_from_engine(engine, cache, cfg, args.ctx, args.cpu_tokens, threads, args.seed)
+            cpu_tps, first = cpu_baseline_from_engine(engine, cache, cfg, args.ctx, args.cpu_tokens, threads, tok0)
+            host = host_info(threads)
+            bpt = decode_bytes_per_token(cfg, args.ctx)
             cpu = {"value": round(cpu_tps, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-                   "sample": f"{args.cpu_tokens} greedy decode tokens of the same 48-layer model from the same "
-                             f"ctx-{args.ctx} KV cache (weights and cache copied back from HBM)"}
-            del ctx_now
+                   "sample": f"{args.cpu_tokens} greedy decode tokens of the same {cfg.n_layer}-layer model from the "
+                             f"same ctx-{args.ctx} KV cache (weights and cache copied back from HBM)",
+                   "cpu_model": host["cpu_model"], "host_copy_gbs": host["host_copy_gbs"],
+                   "bytes_per_token": bpt,
+                   "host_ceiling_tok_s": round(host["host_copy_gbs"] * 1e9 / bpt, 2),
+                   "ceiling_note": "host copy GB/s (read + write bytes) / algorithmic bytes a decode token reads"}
+            diff = np.abs(first.astype(np.float64) - logits0.astype(np.float64))
+            exact = bool(np.array_equal(first.view(np.uint32), logits0.view(np.uint32)))
+            parity = {"status": "bit-exact" if exact else "MISMATCH", "max_abs": float(diff.max()),
+                      "tolerance": 1e-2, "argmax_equal": int(np.argmax(first)) == int(np.argmax(logits0)),
+                      "what": f"logits of the first decode step (position {args.ctx}, the persistent step kernel) "
+                              "against the CPU oracle from the same weights and cache"}
         kernel_table = {k: {"launches": v[0], "avg_us": round(1e3 * v[1] / max(v[0], 1), 2)} for k, v in prof.items()}
+        bpt_all = decode_bytes_per_token(cfg, args.ctx)
         result = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q4_K/q6_K weights, int8 dot, f32 accumulate",
             "data": "synthetic (seeded N(0,0.02) weights, uniform-random token ids)",
-            "config": {"workload": f"{args.config}: {shape_name(cfg)}, "
-                                   f"batch 1 greedy decode after a {args.ctx}-token "
-                                   + ("prefill" if args.fill == "prefill" else "seeded cache fill"),
-                       "batch": 1, "context": args.ctx, "parallelism": "replicas" if world > 1 else "single GPU",
-                       "l2": "inputs larger than L2: about 2.6 GB of weights and KV read per step "
-                             "(17 GB of weights resident)",
-                       "prefill_seconds": round(prefill_s, 2), "setup_seconds": round(time.perf_counter() - t_setup, 1)},
+            "config": workload_config(args.config, cfg, shape_name(cfg), args.ctx, world),
+            "setup": {"context_fill": f"{args.ctx}-token prefill of uniform-random ids" if args.fill == "prefill"
+                      else "seeded f16 cache fill", "prefill_seconds": round(prefill_s, 2),
+                      "setup_seconds": round(time.perf_counter() - t_setup, 1)},
+            "parity": parity,
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": 4 * 7 + 1,
                     "d2h_bytes_per_step": 4 * cfg.n_vocab + 4},
             "gpu_launches": per_step_launches * args.steps,
@@ -325,8 +387,10 @@ def run_ours(args, rank, world, local_rank):
                          "frac": round(achieved / peak, 4) if achieved else None, "peak_kind": peak_kind,
                          "bytes_per_token_layer": gu_bytes + dn_bytes, "traffic": None,
                          "traffic_note": "the expert FFN is two phases of the one persistent step kernel and ncu "
-                                         "counts DRAM bytes per kernel: a 4-layer launch read 462.2 MB for 460 MB "
-                                         "of algorithmic bytes (no re-reads)"},
+                                         "counts DRAM bytes per kernel: see step.traffic for the whole kernel"},
+            "step": {"kernel": "decode_step_kernel (the whole batch-1 step)", "bytes_per_step": bpt_all,
+                     "achieved_gbs": round(bpt_all / (ms / args.steps / 1e3) / 1e9, 1),
+                     "frac": round(bpt_all / (ms / args.steps / 1e3) / 1e9 / peak, 4)},
             "kernels_us": kernel_table,
             "batched": batched,
             "expert_cache": None,
@@ -378,15 +442,20 @@ def run_ours(args, rank, world, local_rank):
 
 
 def run_reference(args, rank, world):
-    """The CPU restatement of the reference's decode path on the host cores, same config."""
+    """The CPU restatement of the reference's decode path on the host cores, same workload and
+    config dict as the GPU arm. The model comes from the oracle's own seeded generator and
+    workload description (oracle/workloads.py), so this arm never loads the product library."""
     if rank != 0:
         return None
-    import bigtea_b200 as bt
     from oracle import pyoracle as orc
+    from oracle import workloads
 
-    cfg = bt.config(args.config, max_positions=args.ctx + args.steps + args.warmup + 8)
+    try:
+        cfg = workloads.workload(args.config, max_positions=args.ctx + args.steps + args.warmup + 8)
+    except KeyError as err:
+        return {"impl": "reference", "unavailable": f"no CPU-arm description of {args.config}: {err}"}
     threads = os.cpu_count() or 1
-    W = bt.synth_model(cfg, seed=args.seed)
+    W = orc.synth_model(cfg.tensor_specs(), seed=args.seed)
     model = orc.Model(cfg, W)
     # the decode cost does not depend on the cache contents: seeded f16 values stand in for
     # the prefilled context
@@ -406,15 +475,20 @@ def run_reference(args, rank, world):
         tok = orc.argmax(model.forward([tok], model.len()))
     dt = time.perf_counter() - t0
     tps = args.steps / dt
+    host = host_info(threads)
+    bpt = decode_bytes_per_token(cfg, args.ctx)
     return {
         "impl": "reference", "metric": METRIC, "value": round(tps, 3), "unit": "tok/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(1e3 * dt / args.steps, 2),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "q4_K/q6_K weights, int8 dot, f32 accumulate", "data": "synthetic",
-        "config": {"workload": f"{args.config}: {shape_name(cfg)}, batch 1 greedy "
-                               f"decode at context {args.ctx}", "batch": 1, "context": args.ctx},
+        "config": workload_config(args.config, cfg, cfg.shape_name(), args.ctx, world),
         "cpu_baseline": {"value": round(tps, 3), "unit": "tok/s", "cores": threads, "kind": "port",
-                         "sample": f"{args.steps} decode tokens at context {args.ctx} (seeded f16 cache)"},
+                         "sample": f"{args.steps} decode tokens at context {args.ctx} (seeded f16 cache)",
+                         "cpu_model": host["cpu_model"], "host_copy_gbs": host["host_copy_gbs"],
+                         "bytes_per_token": bpt, "host_ceiling_tok_s": round(host["host_copy_gbs"] * 1e9 / bpt, 2),
+                         "ceiling_note": "host copy GB/s (read + write bytes) / algorithmic bytes a decode token "
+                                         "reads"},
         "e2e": {"value": round(tps, 3), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
 
@@ -492,6 +566,9 @@ def main():
         _dist.destroy_process_group()
     if rank == 0 and out is not None:
         print(json.dumps(out), flush=True)
+        if out.get("parity", {}).get("status") == "MISMATCH":
+            print("bench: the measured step's logits differ from the CPU oracle's", file=sys.stderr)
+            sys.exit(3)
 
 
 if __name__ == "__main__":

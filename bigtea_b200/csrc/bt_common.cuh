@@ -212,18 +212,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
     return ok != 0;
 }
 
-// Bounded wait: returns false (and sets ERR_WAIT_TIMEOUT) if the phase does not complete
-// within WAIT_LIMIT_CYCLES.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+// Bounded wait: returns false (and sets ERR_WAIT_TIMEOUT when err is given) if the phase does
+// not complete within `limit` SM cycles.
+__device__ __forceinline__ bool mbar_wait_l(uint64_t *bar, uint32_t parity, int *err, long long limit) {
     if (mbar_try_wait(bar, parity)) return true;
     long long t0 = clock64();
     while (!mbar_try_wait(bar, parity)) {
-        if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
+        if (clock64() - t0 > limit) {
             if (err) atomicOr(err, ERR_WAIT_TIMEOUT);
             return false;
         }
     }
     return true;
+}
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+    return mbar_wait_l(bar, parity, err, WAIT_LIMIT_CYCLES);
 }
 
 // 1-D bulk copy global -> shared (TMA, no tensor map). dst/src 16-byte aligned, bytes % 16 == 0.

@@ -131,6 +131,12 @@ struct bt_engine {
     int mma_min_units = 32;  // batched GEMVs on tcgen05 from this many (tokens, rows) units on (option)
     int mma_grid = 0;        // CTAs of the tensor-core kernels (0: one per SM; option, for tests)
     bool attn_warp = true;   // batched attention with one warp per 128-key chunk (option "attn_warp")
+    // the persistent step's bounded waits, in microseconds (option "wait_limit_us"; 0 = about 1 s)
+    int wait_limit_us = 0;
+    // failure drill of the persistent step (options "fault_cta", "fault_barrier"; off at 0):
+    // CTA fault_cta leaves at its grid barrier number fault_barrier without arriving
+    int fault_cta = 0, fault_barrier = 0;
+    int fault_copy = 0;  // option "fault_copy": in layer fault_copy - 1, CTA fault_cta requests no expert tiles
     // expert cache: experts in pinned host memory, the ones a layer selects copied into slots
     // of a device pool before its expert kernels (bt_engine_enable_expert_cache)
     bool xcache = false;
@@ -1384,6 +1390,15 @@ static int launch_persistent_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bo
     a.n_out = p.T;
     a.bar = e->gbar.as<unsigned>();
     a.err = e->err.as<int>();
+    a.wait_limit = WAIT_LIMIT_CYCLES;
+    if (e->wait_limit_us > 0) {
+        int clk_khz = 0;
+        CK(cudaDeviceGetAttribute(&clk_khz, cudaDevAttrClockRate, e->device));
+        a.wait_limit = (long long)e->wait_limit_us * (clk_khz > 0 ? clk_khz : 1965000) / 1000;
+    }
+    a.fault_cta = e->fault_cta;
+    a.fault_barrier = e->fault_barrier;
+    a.fault_copy = e->fault_copy;
     a.trace = e->tracing ? e->trace.as<unsigned long long>() : nullptr;
     // the barrier's arrival count starts from zero even if an earlier launch stopped early
     CK(cudaMemsetAsync(e->gbar.p, 0, 8, e->st));
@@ -1951,6 +1966,8 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
 static int err_word(bt_engine *e, int h) {
     if (h) {
         CK(cudaMemsetAsync(e->err.p, 0, 4, e->st));
+        // a step that stopped early leaves its partial argmax keys behind (the step end clears them)
+        CK(cudaMemsetAsync(e->amax.p, 0, (size_t)e->max_out * 8, e->st));
         CK(cudaStreamSynchronize(e->st));
         if (h & ERR_WAIT_TIMEOUT) return fail(BT_ERR_TIMEOUT, "a device wait ran out of time");
         return fail(BT_ERR_INVALID, "a kernel rejected an index (token id out of range?)");
@@ -2565,6 +2582,17 @@ extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
     if (!strcmp(name, "ep_timeout_ms")) {
         if (value < 1) return fail(BT_ERR_INVALID, "ep_timeout_ms must be positive");
         e->ep_timeout_ms = value;
+        return BT_OK;
+    }
+    if (!strcmp(name, "wait_limit_us") || !strcmp(name, "fault_cta") || !strcmp(name, "fault_barrier") ||
+        !strcmp(name, "fault_copy")) {
+        if (value < 0) return fail(BT_ERR_INVALID, std::string(name) + " must be >= 0");
+        (!strcmp(name, "wait_limit_us")   ? e->wait_limit_us
+         : !strcmp(name, "fault_cta")     ? e->fault_cta
+         : !strcmp(name, "fault_barrier") ? e->fault_barrier
+                                          : e->fault_copy) = value;
+        for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);  // the values are baked into captured launches
+        e->graphs.clear();
         return BT_OK;
     }
     if (!strcmp(name, "pdl")) {

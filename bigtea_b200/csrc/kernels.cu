@@ -2,7 +2,7 @@
 //
 // Reference call sites each kernel replaces (Chaos tree, core/arch/src/stream.rs unless noted):
 //   embed_kernel      get_rows on token_embd                           2192-2231
-//   gemv_kernel       rms_norm+mul then mul_mat (q/k/v, attn_output, output head)
+//   kq_rows_kernel    rms_norm+mul then mul_mat (q/k/v, attn_output, output head)
 //                                                                      2265-2330, 2669, 2853-2914
 //   qkv_post_kernel   q/k head RMSNorm, rope_ext NEOX, KvCache::push  2390-2474, 2545-2552; kv.rs:171-205
 //   attn_kernel       flash_attn_ext over the cached history          2554-2703; qwen3.rs:1186-1227
@@ -178,7 +178,7 @@ __device__ void run_prefetch(const PrefetchSpec &pf) {
 // bulk copies (weights do not depend on the previous kernel, so the first slots are
 // requested before griddepcontrol.wait), and lane s decodes slot s in registers.
 template <int NWARP>
-__global__ void __launch_bounds__(NWARP * 32, 1) gemv_kernel(const __grid_constant__ GemvArgs p) {
+__global__ void __launch_bounds__(NWARP * 32, 1) kq_rows_kernel(const __grid_constant__ GemvArgs p) {
     extern __shared__ __align__(1024) uint8_t smem[];
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     uint64_t *bars = reinterpret_cast<uint64_t *>(smem);
@@ -342,7 +342,7 @@ static cudaError_t launch_ex(Kern k, dim3 grid, dim3 block, size_t smem, cudaStr
 
 cudaError_t launch_gemv(const GemvArgs &a, int grid, cudaStream_t st, bool pdl) {
     size_t smem = gemv_smem_bytes(a);
-    return launch_ex(gemv_kernel<GEMV_WARPS>, dim3(grid), dim3(GEMV_WARPS * 32), smem, st, pdl, a);
+    return launch_ex(kq_rows_kernel<GEMV_WARPS>, dim3(grid), dim3(GEMV_WARPS * 32), smem, st, pdl, a);
 }
 
 // ====================================================================== experts
@@ -2102,7 +2102,7 @@ cudaError_t init_kernel_attributes() {
     cudaError_t e;
     if ((e = cudaGetDevice(&dev))) return e;
     if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
-    const void *kerns[] = {(const void *)gemv_kernel<GEMV_WARPS>, (const void *)gateup_kernel<GEMV_WARPS>,
+    const void *kerns[] = {(const void *)kq_rows_kernel<GEMV_WARPS>, (const void *)gateup_kernel<GEMV_WARPS>,
                            (const void *)down_kernel<GEMV_WARPS>, (const void *)gateup_grouped_kernel<GEMV_WARPS>,
                            (const void *)down_grouped_kernel<GEMV_WARPS>, (const void *)group_kernel,
                            (const void *)attn_kernel<2>,

@@ -468,7 +468,7 @@ size_t gemv_mma_smem_bytes(int K) {
 }
 
 template <int N>
-__global__ void __launch_bounds__(256, 1) gemv_mma_kernel(const __grid_constant__ GemvArgs p) {
+__global__ void __launch_bounds__(256, 1) kq_rows_mma_kernel(const __grid_constant__ GemvArgs p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int K = p.K, nsb = K / 256;
@@ -672,7 +672,7 @@ cudaError_t launch_gemv_mma(const GemvArgs &a, int grid, cudaStream_t st, bool p
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 1 : 0;
-    return n == 32 ? cudaLaunchKernelEx(&cfg, gemv_mma_kernel<32>, a) : cudaLaunchKernelEx(&cfg, gemv_mma_kernel<16>, a);
+    return n == 32 ? cudaLaunchKernelEx(&cfg, kq_rows_mma_kernel<32>, a) : cudaLaunchKernelEx(&cfg, kq_rows_mma_kernel<16>, a);
 }
 
 cudaError_t init_mma_attributes() {
@@ -680,8 +680,8 @@ cudaError_t init_mma_attributes() {
     cudaError_t e;
     if ((e = cudaGetDevice(&dev))) return e;
     if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
-    const void *kerns[] = {(const void *)gateup_mma_kernel, (const void *)gemv_mma_kernel<32>,
-                           (const void *)gemv_mma_kernel<16>};
+    const void *kerns[] = {(const void *)gateup_mma_kernel, (const void *)kq_rows_mma_kernel<32>,
+                           (const void *)kq_rows_mma_kernel<16>};
     for (const void *k : kerns) {
         cudaFuncAttributes fa;
         if ((e = cudaFuncGetAttributes(&fa, k))) return e;

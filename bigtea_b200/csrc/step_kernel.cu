@@ -10,8 +10,9 @@
 //
 // At batch 1 a layer moves ~40 MB in a few microseconds, so the step is bound by global round
 // trips more than by bandwidth, and the kernel is organised around them:
-//  * phases are separated by a one-counter grid barrier (release-add, relaxed polls, one
-//    acquire fence; bounded);
+//  * phases are separated by a one-counter grid barrier (release-add arrival, ld.acquire.gpu
+//    polls and no trailing fence; bounded, with a poison bit in the counter that releases every
+//    CTA at its next barrier once one CTA has failed);
 //  * whatever is static in a phase is requested before the barrier that precedes it: weight
 //    tiles into the warps' TMA rings, the K/V pages of a CTA's first attention item, the
 //    router rows, the norm vector of the next staging (into shared memory), and the residual
@@ -89,21 +90,23 @@ __device__ __forceinline__ unsigned long long global_ns() {
 constexpr unsigned BAR_POISON = 0x80000000u;  // arrivals stay far below bit 31
 __device__ __forceinline__ void poison_barrier(unsigned *bar) { atomicOr(bar, BAR_POISON); }
 
-__device__ __noinline__ bool grid_sync(unsigned *bar, unsigned &epoch, int *err, unsigned long long *trace_row = nullptr) {
+__device__ __noinline__ bool grid_sync(const StepArgs &p, unsigned &epoch, unsigned long long *trace_row = nullptr) {
     __syncthreads();
     epoch += 1;
+    // the failure drill: this CTA leaves without arriving, as one that died would
+    if (p.fault_barrier == (int)epoch && p.fault_cta == (int)blockIdx.x) return false;
     bool bad = false;
     if (threadIdx.x == 0) {
         if (trace_row) trace_row[blockIdx.x] = global_ns();
         const unsigned target = epoch * gridDim.x;
-        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(bar), "r"(1u) : "memory");
-        unsigned v = ld_acquire_gpu(bar);
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p.bar), "r"(1u) : "memory");
+        unsigned v = ld_acquire_gpu(p.bar);
         if (v < target) {
             const long long t0 = clock64();
-            while ((v = ld_acquire_gpu(bar)) < target) {
-                if (clock64() - t0 > WAIT_LIMIT_CYCLES) {
-                    atomicOr(err, ERR_WAIT_TIMEOUT);
-                    poison_barrier(bar);
+            while ((v = ld_acquire_gpu(p.bar)) < target) {
+                if (clock64() - t0 > p.wait_limit) {
+                    atomicOr(p.err, ERR_WAIT_TIMEOUT);
+                    poison_barrier(p.bar);
                     v = BAR_POISON;
                     asm volatile("fence.acq_rel.gpu;" ::: "memory");
                     break;
@@ -111,7 +114,7 @@ __device__ __noinline__ bool grid_sync(unsigned *bar, unsigned &epoch, int *err,
             }
         }
         bad = v >= BAR_POISON;
-        if (epoch == 1) bad |= *reinterpret_cast<volatile int *>(err) != 0;
+        if (epoch == 1) bad |= *reinterpret_cast<volatile int *>(p.err) != 0;
         if (trace_row && blockIdx.x == 0) trace_row[gridDim.x] = global_ns();
     }
     return !__syncthreads_or(bad);
@@ -140,11 +143,12 @@ struct WarpRing {
     __device__ uint8_t *slot_ptr(int j) const { return base + (size_t)(j % nst) * slot_bytes; }
     __device__ uint64_t *slot_bar(int j) const { return bars + (j % nst); }
     __device__ bool can_issue() const { return issued - done < nst; }
-    // wait for unit j (== done); false if the bounded wait ran out
-    __device__ bool wait(int j, int *err) {
+    // wait for unit j (== done); false if the bounded wait ran out, in which case the slot's
+    // parity stays, so that a later wait (the failure drain) waits for the same copy
+    __device__ bool wait(int j, int *err, long long limit) {
         const int s = j % nst;
-        const bool ok = __all_sync(FULL, mbar_wait(bars + s, (par >> s) & 1u, err));
-        par ^= 1u << s;
+        const bool ok = __all_sync(FULL, mbar_wait_l(bars + s, (par >> s) & 1u, err, limit));
+        if (ok) par ^= 1u << s;
         return ok;
     }
 };
@@ -332,7 +336,7 @@ __device__ void gemv_preissue(WarpRing &r, const SegList &s, int warp, int lane)
 // over the written rows (output head). The segments' parameters are read once into registers.
 __device__ __forceinline__ bool gemv_run(WarpRing &r, const SegList &s, const ActBlock *act, int nsbK, int T,
                                          float *y, long long ys, const float *res, int res_row0, int res_ld,
-                                         unsigned long long *amax, int *err, int warp, int lane,
+                                         unsigned long long *amax, int *err, long long lim, int warp, int lane,
                                          unsigned long long *cyc = nullptr) {
     long long cw = 0, cc0 = clock64();
     int u0, u1;
@@ -357,7 +361,7 @@ __device__ __forceinline__ bool gemv_run(WarpRing &r, const SegList &s, const Ac
     for (int j = 0; j < n; j++) {
         while (r.issued < n && r.can_issue()) gemv_issue(r, s, u0, warp, lane);
         const long long w0 = clock64();
-        if (!r.wait(j, err)) {
+        if (!r.wait(j, err, lim)) {
             ok = false;
             break;
         }
@@ -424,8 +428,12 @@ __device__ __forceinline__ bool gemv_run(WarpRing &r, const SegList &s, const Ac
 
 // ------------------------------------------------------------------ expert phases
 __device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int u0, int warp,
-                             int lane) {
+                             int lane, bool drill) {
     const int j = r.issued;
+    if (drill) {  // the failure drill: the slot is counted as requested, but nothing will land
+        r.issued++;
+        return;
+    }
     const int u = u0 + warp + j * STEP_WARPS;
     const int tk = u / L.gate.n_tiles, tile = u - tk * L.gate.n_tiles;
     const int e = sm.sel_ids[(tk / K) * MAX_K + tk % K];
@@ -607,7 +615,7 @@ __device__ __forceinline__ void ldw_n(uint32_t (&dst)[N], const uint32_t *src) {
 // order).
 template <int G>
 __device__ bool attn_half(const StepArgs &p, const LayerDev &L, const StepSmem &sm, const AttnItem &it, int layer,
-                          int hf, uint32_t &apar, unsigned long long *tp) {
+                          int hf, uint32_t &apar, uint32_t &apend, unsigned long long *tp) {
     constexpr int D = 128, HPT = G / 2, CH = ATTN_CHUNK, QWORDS = G / 2;
     const int tid = threadIdx.x & 127, warp = tid >> 5, lane = tid & 31;
     const long long tps = gridDim.x + 1;
@@ -670,8 +678,11 @@ __device__ bool attn_half(const StepArgs &p, const LayerDev &L, const StepSmem &
     }
     half_sync(hf);
     PT(0);
-    const bool landed = mbar_wait(sm.attn_bar + hf, (apar >> hf) & 1u, p.err);
-    apar ^= 1u << hf;
+    const bool landed = mbar_wait_l(sm.attn_bar + hf, (apar >> hf) & 1u, p.err, p.wait_limit);
+    if (landed) {  // else the failure drain waits for the same copies
+        apar ^= 1u << hf;
+        apend &= ~(1u << hf);
+    }
     if (half_sync_or(hf, !landed)) return false;
     PT(1);
     if (last) {  // the new position's row of the tiles is the value just computed
@@ -937,6 +948,27 @@ __device__ void combine_slice(const float *part, const float *ml, int cstride, i
     __syncthreads();
 }
 
+// ------------------------------------------------------------------ the failure exit
+// Taken by the whole CTA together: every path here comes through a CTA-wide vote or a
+// CTA-uniform condition, so no warp leaves while others still wait at a barrier of the CTA.
+// With `poison` (this CTA's own wait ran out and already set the error word), the grid barrier
+// is poisoned so that every other CTA leaves at its next barrier instead of waiting out its own
+// limit. Then the CTA waits, bounded, for its own bulk copies still in flight -- the warps' ring
+// slots, the attention tile buffers (apend) and the aux copies (xpend) -- so that none of them
+// lands in shared memory after the CTA has gone.
+__device__ __noinline__ void step_fail_exit(const StepArgs &p, WarpRing &ring, const StepSmem &sm, uint32_t apend,
+                                            uint32_t apar, uint32_t xpend, uint32_t xpar, bool poison) {
+    const int tid = threadIdx.x;
+    if (poison && tid == 0) poison_barrier(p.bar);
+    for (int j = ring.done; j < ring.issued; j++) ring.wait(j, nullptr, p.wait_limit);
+    const int hf = tid >> 7;
+    if ((tid & 127) == 0 && ((apend >> hf) & 1u)) mbar_wait_l(sm.attn_bar + hf, (apar >> hf) & 1u, nullptr, p.wait_limit);
+    if (tid == 0)
+        for (int i = 0; i < 2; i++)
+            if ((xpend >> i) & 1u) mbar_wait_l(sm.aux_bar + i, (xpar >> i) & 1u, nullptr, p.wait_limit);
+    __syncthreads();
+}
+
 // ------------------------------------------------------------------ the kernel
 template <int G>
 __global__ void __launch_bounds__(STEP_THREADS, 1)
@@ -1015,6 +1047,14 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
     fence_mbar_init();
     __syncthreads();
     uint32_t apar = 0, xpar = 0;  // next parities of attn_bar[0..1] and aux_bar[0..1]
+    // copies in flight that no wait has consumed yet, per attention buffer and aux barrier (what
+    // the failure exit waits for); aux 1 (layer 0's attn_norm) is requested below
+    uint32_t apend = 0, xpend = 2u;
+#define STEP_FAIL(poison)                                                       \
+    do {                                                                        \
+        step_fail_exit(p, ring, sm, apend, apar, xpend, xpar, poison);          \
+        return;                                                                 \
+    } while (0)
     {
         // the page ids of this CTA's first two attention items: the same in every layer
         constexpr int PPI = ATTN_CHUNK / 16;
@@ -1041,8 +1081,11 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
     }
     // wait for aux copy i (all threads); false if the bounded wait ran out anywhere in the CTA
     auto wait_aux = [&](int i) -> bool {
-        const bool ok = mbar_wait(sm.aux_bar + i, (xpar >> i) & 1u, p.err);
-        xpar ^= 1u << i;
+        const bool ok = mbar_wait_l(sm.aux_bar + i, (xpar >> i) & 1u, p.err, p.wait_limit);
+        if (ok) {
+            xpar ^= 1u << i;
+            xpend &= ~(1u << i);
+        }
         return !__syncthreads_or(!ok);
     };
 
@@ -1098,6 +1141,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
 
     for (int il = 0; il < p.n_layer; il++) {
         const LayerDev &L = sm.ldesc[il & 1];
+        bool bad = false;  // this thread's warp saw a bounded wait run out in the current phase
         const bool has_next = il + 1 < p.n_layer;
         // the next layer's descriptor: loaded now, stored to shared memory after the attention
         uint32_t ld_next = 0;
@@ -1106,22 +1150,21 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         const SegList sq = make_segs(&L.q, 0, &L.k, QW, &L.v, QW + KW);
         {
             const float *xs = il == 0 ? x0 : p.x;
-            if (!wait_aux(1)) return;  // attn_norm in cbuf
+            if (!wait_aux(1)) STEP_FAIL(true);  // attn_norm in cbuf
             step_stage(xs, E, E, T, sm.cbuf, p.eps, sm.act, sm.normS, nullptr);
             __syncthreads();
             POINT(il, 0);
             if (il == 0) gemv_preissue(ring, sq, warp, lane);  // the region held the embedding rows
             CYC_RESET();
-            if (!gemv_run(ring, sq, sm.act, nsbE, T, p.qkv, QW + 2 * KW, nullptr, 0, 0, nullptr, p.err, warp, lane,
-                          p.trace ? cycv : nullptr))
-                return;
+            bad = !gemv_run(ring, sq, sm.act, nsbE, T, p.qkv, QW + 2 * KW, nullptr, 0, 0, nullptr, p.err, p.wait_limit,
+                            warp, lane, p.trace ? cycv : nullptr);
             CYC_WRITE(il, 7, 0);
             CYC_WRITE(il, 8, 1);
         }
         // the K/V pages of this CTA's first two attention items, requested before the barrier
         const int it0 = blockIdx.x;
         const int n_items = attn_items(p, sm.pos);
-        __syncthreads();
+        if (__syncthreads_or(bad)) STEP_FAIL(true);
         if (warp < 2) {  // warp k issues item k's pages
             const int i = it0 + warp * gridDim.x;
             if (i < n_items) {
@@ -1130,7 +1173,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                 attn_issue_warp(p, &tmap, sm, it, il, warp, sm.iblk + warp * (ATTN_CHUNK / 16), lane);
             }
         }
-        if (!grid_sync(p.bar, epoch, p.err, TR(il, 0))) return;
+        apend = (it0 < n_items ? 1u : 0u) | (it0 + (int)gridDim.x < n_items ? 2u : 0u);
+        if (!grid_sync(p, epoch, TR(il, 0))) STEP_FAIL(false);
         // ================= ATTN: items it0 + k * grid; half hf of the CTA runs k = hf, hf + 2, ...
         {
             const int hf = warp >> 2;
@@ -1140,15 +1184,18 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                 if (i >= n_items) break;
                 AttnItem it;
                 attn_item(p, sm.pos, i, it);
-                if (k >= 2 && (tid & 127) < 32) attn_issue_warp(p, &tmap, sm, it, il, hf, nullptr, lane);
+                if (k >= 2) {
+                    if ((tid & 127) < 32) attn_issue_warp(p, &tmap, sm, it, il, hf, nullptr, lane);
+                    apend |= 1u << hf;
+                }
                 unsigned long long *tp =
                     (p.trace && k == 0) ? p.trace + ((long long)il * STEP_PHASES + 8 + 16) * (gridDim.x + 1) : nullptr;
-                if (!attn_half<G>(p, L, sm, it, il, hf, apar, tp)) {
+                if (!attn_half<G>(p, L, sm, it, il, hf, apar, apend, tp)) {
                     ok = false;
                     break;
                 }
             }
-            if (__syncthreads_or(!ok)) return;
+            if (__syncthreads_or(!ok)) STEP_FAIL(true);
         }
         if (has_next && tid < LD_WORDS) reinterpret_cast<uint32_t *>(sm.ldesc + ((il + 1) & 1))[tid] = ld_next;
         // attn_output tiles are static: request this CTA's first ones now. Its residual rows (x)
@@ -1165,7 +1212,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             res_pre = __ldcg(p.x + (long long)(tid / orows) * E + orow0 + tid % orows);
         __syncthreads();
         gemv_preissue(ring, so, warp, lane);
-        if (!grid_sync(p.bar, epoch, p.err, TR(il, 1))) return;
+        if (!grid_sync(p, epoch, TR(il, 1))) STEP_FAIL(false);
         if (tid < T * orows) sm.res[tid] = res_pre;
         // the next layer's small vectors, towards L2
         if (has_next && blockIdx.x < 3) {
@@ -1196,20 +1243,20 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                                   p.att + (long long)t * QW + hd * 128 + q * nd, sm.cbuf,
                                   reinterpret_cast<float *>(sm.act), sm.misc);
                 }
-                if (!grid_sync(p.bar, epoch, p.err, TR(il, 2))) return;
+                if (!grid_sync(p, epoch, TR(il, 2))) STEP_FAIL(false);
             }
         }
         // ================= O: ffn_in = x + W_o * att
         step_stage(p.att, QW, QW, T, nullptr, 0.0f, sm.act, nullptr, nullptr);
         __syncthreads();
         POINT(il, 2);
-        if (!gemv_run(ring, so, sm.act, nsbQ, T, p.ffn_in, E, sm.res, orow0, orows, nullptr, p.err, warp, lane))
-            return;
+        bad = !gemv_run(ring, so, sm.act, nsbQ, T, p.ffn_in, E, sm.res, orow0, orows, nullptr, p.err, p.wait_limit, warp,
+                        lane);
         // this CTA's router rows and the ffn norm vector, requested before the barrier
         const int nrr = (int)blockIdx.x < p.NE ? (p.NE - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
         float *rrows = reinterpret_cast<float *>(sm.region);
         float *ynorm = rrows + STEP_ROUTER_ROWS * E;
-        __syncthreads();
+        if (__syncthreads_or(bad)) STEP_FAIL(true);
         if (tid == 0) {
             fence_proxy_async();
             mbar_arrive_expect_tx(sm.aux_bar + 0, nrr * E * 4);
@@ -1219,11 +1266,12 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             mbar_arrive_expect_tx(sm.aux_bar + 1, E * 4);
             bulk_g2s(sm.cbuf, L.ffn_norm, E * 4, sm.aux_bar + 1);
         }
-        if (!grid_sync(p.bar, epoch, p.err, TR(il, 3))) return;
+        xpend |= 3u;
+        if (!grid_sync(p, epoch, TR(il, 3))) STEP_FAIL(false);
         // ================= ROUTER: ffn RMSNorm (staged for the experts too) and router rows
-        if (!wait_aux(1)) return;
+        if (!wait_aux(1)) STEP_FAIL(true);
         step_stage(p.ffn_in, E, E, T, sm.cbuf, p.eps, sm.act, sm.normS, ynorm);
-        if (!wait_aux(0)) return;  // its __syncthreads also completes ynorm
+        if (!wait_aux(0)) STEP_FAIL(true);  // its __syncthreads also completes ynorm
         POINT(il, 3);
         for (int q = warp; q < nrr * T; q += STEP_WARPS) {  // (router row k, token t) per warp, C5
             const int k = q / T, t = q % T;
@@ -1238,7 +1286,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         }
         int d0, d1;
         cta_range(T * E, d0, d1);
-        if (!grid_sync(p.bar, epoch, p.err, TR(il, 4))) return;
+        if (!grid_sync(p, epoch, TR(il, 4))) STEP_FAIL(false);
         // ================= GATEUP: soft_max + route() in every CTA (C5, C7; stable descending
         // by total_cmp, top K, renormalised), then the experts
         {
@@ -1315,13 +1363,17 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             const int nsb = L.gate.nsb, gS = L.gate.S, grpt = L.gate.rpt, gnt = L.gate.n_tiles;
             const bool gq4 = L.gate.type == T_Q4_K, uq4 = L.up.type == T_Q4_K;
             const int gtb = L.gate.tile_bytes;
-            while (ring.issued < n && ring.can_issue()) gateup_issue(ring, L, sm, K, u0, warp, lane);
+            const bool drill = p.fault_copy == il + 1 && p.fault_cta == (int)blockIdx.x;
+            while (ring.issued < n && ring.can_issue()) gateup_issue(ring, L, sm, K, u0, warp, lane, drill);
             CYC_RESET();
             long long gcw = 0, gc0 = clock64();
             for (int j = 0; j < n; j++) {
-                while (ring.issued < n && ring.can_issue()) gateup_issue(ring, L, sm, K, u0, warp, lane);
+                while (ring.issued < n && ring.can_issue()) gateup_issue(ring, L, sm, K, u0, warp, lane, drill);
                 const long long w0 = clock64();
-                if (!ring.wait(j, p.err)) return;
+                if (!ring.wait(j, p.err, p.wait_limit)) {
+                    bad = true;
+                    break;
+                }
                 gcw += clock64() - w0;
                 const int u = u0 + warp + j * STEP_WARPS;
                 const int tk = u / gnt, tile = u - tk * gnt;
@@ -1355,6 +1407,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                 atomicMax(cycv + 4, (unsigned long long)gcw);
                 atomicMax(cycv + 5, (unsigned long long)(clock64() - gc0 - gcw));
             }
+            if (__syncthreads_or(bad)) STEP_FAIL(true);
             CYC_WRITE(il, 11, 4);
             CYC_WRITE(il, 12, 5);
             POINT(il, 5);
@@ -1366,7 +1419,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         // the down phase's residual rows (ffn_in, final since the O barrier)
         float dres_pre = 0.0f;
         if (tid < d1 - d0) dres_pre = __ldcg(p.ffn_in + d0 + tid);
-        if (!grid_sync(p.bar, epoch, p.err, TR(il, 5))) return;
+        if (!grid_sync(p, epoch, TR(il, 5))) STEP_FAIL(false);
         if (tid < d1 - d0) sm.res[tid] = dres_pre;
         // ================= DOWN: the experts' down rows, their sum in the reference's order, residual
         step_stage(p.act, F, F, T * K, nullptr, 0.0f, sm.act, nullptr, nullptr);
@@ -1386,7 +1439,10 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             for (int j = 0; j < n; j++) {
                 while (ring.issued < n && ring.can_issue()) down_issue(ring, L, sm, K, E, d0, warp, lane);
                 const long long w0 = clock64();
-                if (!ring.wait(j, p.err)) return;
+                if (!ring.wait(j, p.err, p.wait_limit)) {
+                    bad = true;
+                    break;
+                }
                 dcw += clock64() - w0;
                 const int u = d0 + warp + j * STEP_WARPS;
                 const int t = u / E;
@@ -1433,13 +1489,14 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         }
         // the next layer's q/k/v tiles (or the output head's) and its norm vector are static:
         // request them now
-        __syncthreads();
+        if (__syncthreads_or(bad)) STEP_FAIL(true);
         if (tid == 0) {
             const float *nv = has_next ? sm.ldesc[(il + 1) & 1].attn_norm : p.out_norm;
             fence_proxy_async();
             mbar_arrive_expect_tx(sm.aux_bar + 1, E * 4);
             bulk_g2s(sm.cbuf, nv, E * 4, sm.aux_bar + 1);
         }
+        xpend |= 2u;
         if (has_next) {
             const LayerDev &Ln = sm.ldesc[(il + 1) & 1];
             const SegList sqn = make_segs(&Ln.q, 0, &Ln.k, QW, &Ln.v, QW + KW);
@@ -1448,22 +1505,22 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             const SegList sout = make_segs(sm.outd, 0, nullptr, 0, nullptr, 0);
             gemv_preissue(ring, sout, warp, lane);
         }
-        if (!grid_sync(p.bar, epoch, p.err, TR(il, 6))) return;
+        if (!grid_sync(p, epoch, TR(il, 6))) STEP_FAIL(false);
     }
     // ================= output head with the fused argmax
     {
         const SegList sout = make_segs(sm.outd, 0, nullptr, 0, nullptr, 0);
-        if (!wait_aux(1)) return;  // out_norm in cbuf
+        if (!wait_aux(1)) STEP_FAIL(true);  // out_norm in cbuf
         step_stage(p.x, E, E, T, sm.cbuf, p.eps, sm.act, sm.normS, nullptr);
         __syncthreads();
         CYC_RESET();
-        if (!gemv_run(ring, sout, sm.act, nsbE, T, p.logits, p.V, nullptr, 0, 0, p.amax, p.err, warp, lane,
-                      p.trace ? cycv : nullptr))
-            return;
+        bool hbad = !gemv_run(ring, sout, sm.act, nsbE, T, p.logits, p.V, nullptr, 0, 0, p.amax, p.err, p.wait_limit,
+                              warp, lane, p.trace ? cycv : nullptr);
+        if (__syncthreads_or(hbad)) STEP_FAIL(true);
         CYC_WRITE(p.n_layer, 13, 0);
         CYC_WRITE(p.n_layer, 14, 1);
     }
-    if (!grid_sync(p.bar, epoch, p.err, TR(p.n_layer, 0))) return;
+    if (!grid_sync(p, epoch, TR(p.n_layer, 0))) STEP_FAIL(false);
     // ================= step end: argmax out, lengths advance, greedy feed-back
     if (blockIdx.x == 0 && tid < T) {
         const int t = tid;
@@ -1479,6 +1536,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         p.dev_len[p.seq_of[t]] += 1;
     }
 }
+
+#undef STEP_FAIL
 
 size_t step_smem_bytes(int max_chunks) {
     (void)max_chunks;

@@ -55,6 +55,15 @@ struct StepArgs {
     int n_out;
     unsigned *bar;  // grid barrier arrival counter, zeroed before each launch
     int *err;
+    // every bounded wait of the step gives up after this many SM cycles (about 1 s by default)
+    long long wait_limit;
+    // failure drill, off when fault_barrier is 0: CTA fault_cta leaves at its grid barrier number
+    // fault_barrier (1-based, counted from the start of the launch) without arriving, as a CTA
+    // that died would; the others' bounded waits then run out
+    int fault_cta, fault_barrier;
+    // second drill, off at 0: in layer fault_copy - 1, CTA fault_cta requests none of its expert
+    // gate/up tiles, so its own bounded ring waits run out (the failure exit with copies missing)
+    int fault_copy;
     // optional timeline: per barrier, every CTA's arrival time and CTA 0's departure time
     // (%globaltimer ns), rows of gridDim.x + 1 at trace[(layer * STEP_PHASES + phase) * (grid + 1)]
     unsigned long long *trace;

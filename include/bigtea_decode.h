@@ -154,7 +154,14 @@ int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const ui
  * holds every SM for the whole step, default 1; 0 = one kernel per phase), "mma" (Q4_K
  * contractions of batched steps on the tensor cores, default 1), "mma_min_units" (the batched
  * GEMV goes to the tensor cores from this many 128-row x token-chunk units, default 32),
- * "mma_grid" (CTAs of the tensor-core kernels, default 0 = one per SM). */
+ * "mma_grid" (CTAs of the tensor-core kernels, default 0 = one per SM), "wait_limit_us" (every
+ * bounded wait of the persistent step gives up after this long, default 0 = about 1 s), and the
+ * failure drill "fault_cta" / "fault_barrier" (off at 0): in each persistent step, CTA fault_cta
+ * leaves at its grid barrier number fault_barrier (1-based) without arriving, as a CTA that died
+ * would; the other CTAs' waits run out, the first one poisons the barrier, every CTA leaves at its
+ * next barrier, and the call returns BT_ERR_TIMEOUT after about one wait limit; "fault_copy" (off
+ * at 0): in layer fault_copy - 1, CTA fault_cta requests none of its expert tiles, so its own
+ * waits run out and it takes the failure exit (barrier poisoned, its copies drained). */
 int bt_set_option(bt_engine *e, const char *name, int value);
 
 /* Router bias of one layer: n == n_expert F32 values added to the router logits before the

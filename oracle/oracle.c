@@ -247,26 +247,52 @@ void or_quantize_q8k(const float *x, int64_t n, or_block_q8k *y) {
 }
 
 /* ------------------------------------------------------------------ C4 dots */
+/* The integer part of a K-quant dot is exact, so the blocks are first unpacked to signed bytes
+ * (as ggml's generic dot does into aux8) and the integer sums run over plain arrays, which the
+ * compiler vectorises; the float combination keeps the contract's order. */
+static void unpack_q4k(const uint8_t *blk, int8_t q[256], int sc[8], int mn[8]) {
+    const uint8_t *qs = blk + 16;
+    for (int g = 0; g < 4; g++) {
+        q4k_scale_min(blk + 4, 2 * g, &sc[2 * g], &mn[2 * g]);
+        q4k_scale_min(blk + 4, 2 * g + 1, &sc[2 * g + 1], &mn[2 * g + 1]);
+        for (int l = 0; l < 32; l++) {
+            q[64 * g + l] = (int8_t)(qs[32 * g + l] & 0xF);
+            q[64 * g + 32 + l] = (int8_t)(qs[32 * g + l] >> 4);
+        }
+    }
+}
+
+static void unpack_q6k(const uint8_t *blk, int8_t q[256]) {
+    const uint8_t *ql = blk, *qh = blk + 128;
+    for (int n = 0; n < 2; n++)
+        for (int l = 0; l < 32; l++) {
+            const uint8_t a = ql[64 * n + l], b = ql[64 * n + 32 + l], h = qh[32 * n + l];
+            q[128 * n + l] = (int8_t)(((a & 0xF) | (((h >> 0) & 3) << 4)) - 32);
+            q[128 * n + 32 + l] = (int8_t)(((b & 0xF) | (((h >> 2) & 3) << 4)) - 32);
+            q[128 * n + 64 + l] = (int8_t)(((a >> 4) | (((h >> 4) & 3) << 4)) - 32);
+            q[128 * n + 96 + l] = (int8_t)(((b >> 4) | (((h >> 6) & 3) << 4)) - 32);
+        }
+}
+
+static inline int32_t idot(const int8_t *a, const int8_t *b, int n) {
+    int32_t s = 0;
+    for (int i = 0; i < n; i++) s += (int32_t)a[i] * (int32_t)b[i];
+    return s;
+}
+
 static float dot_q4k_row(const uint8_t *row, const or_block_q8k *a, int nsb) {
     float acc = 0.0f;
     for (int b = 0; b < nsb; b++) {
         const uint8_t *blk = row + 144 * b;
         const or_block_q8k *ab = a + b;
+        int8_t q[256];
+        int sc[8], mn[8];
+        unpack_q4k(blk, q, sc, mn);
         float dw = or_f16_to_f32(rd16(blk)), dminw = or_f16_to_f32(rd16(blk + 2));
-        const uint8_t *sc = blk + 4, *qs = blk + 16;
         int32_t sumi = 0, summ = 0;
-        for (int g = 0; g < 4; g++) {
-            int s0, m0, s1, m1;
-            q4k_scale_min(sc, 2 * g, &s0, &m0);
-            q4k_scale_min(sc, 2 * g + 1, &s1, &m1);
-            int32_t dlo = 0, dhi = 0;
-            for (int l = 0; l < 32; l++) {
-                dlo += (qs[32 * g + l] & 0xF) * ab->qs[64 * g + l];
-                dhi += (qs[32 * g + l] >> 4) * ab->qs[64 * g + 32 + l];
-            }
-            sumi += s0 * dlo + s1 * dhi;
-            summ += m0 * (ab->bsums[4 * g] + ab->bsums[4 * g + 1]);
-            summ += m1 * (ab->bsums[4 * g + 2] + ab->bsums[4 * g + 3]);
+        for (int j = 0; j < 8; j++) {
+            sumi += sc[j] * idot(q + 32 * j, ab->qs + 32 * j, 32);
+            summ += mn[j] * (ab->bsums[2 * j] + ab->bsums[2 * j + 1]);
         }
         float t1 = dw * ab->d;
         float t2 = (float)sumi * t1;
@@ -283,13 +309,11 @@ static float dot_q6k_row(const uint8_t *row, const or_block_q8k *a, int nsb) {
         const uint8_t *blk = row + 210 * b;
         const or_block_q8k *ab = a + b;
         const int8_t *sc = (const int8_t *)(blk + 192);
+        int8_t q[256];
+        unpack_q6k(blk, q);
         float dw = or_f16_to_f32(rd16(blk + 208));
         int32_t sumi = 0;
-        for (int s = 0; s < 16; s++) {
-            int32_t d = 0;
-            for (int i = 0; i < 16; i++) d += q6k_value(blk, 16 * s + i) * ab->qs[16 * s + i];
-            sumi += sc[s] * d;
-        }
+        for (int s = 0; s < 16; s++) sumi += sc[s] * idot(q + 16 * s, ab->qs + 16 * s, 16);
         acc = acc + (float)sumi * (dw * ab->d);
     }
     return acc;
@@ -438,6 +462,29 @@ uint32_t or_argmax(const float *logits, int64_t n) {
 }
 
 /* ------------------------------------------------------------------ C8 attention */
+/* f16 -> f32 by F16C (vcvtph2ps): exact for every finite value and infinity, as or_f16_to_f32;
+ * a signalling NaN comes out quiet, which changes no non-NaN result. */
+#include <immintrin.h>
+/* 8x8 transpose of eight f32 vectors (r[i] lane j -> r[j] lane i) */
+static inline void transpose8(__m256 r[8]) {
+    __m256 t0 = _mm256_unpacklo_ps(r[0], r[1]), t1 = _mm256_unpackhi_ps(r[0], r[1]);
+    __m256 t2 = _mm256_unpacklo_ps(r[2], r[3]), t3 = _mm256_unpackhi_ps(r[2], r[3]);
+    __m256 t4 = _mm256_unpacklo_ps(r[4], r[5]), t5 = _mm256_unpackhi_ps(r[4], r[5]);
+    __m256 t6 = _mm256_unpacklo_ps(r[6], r[7]), t7 = _mm256_unpackhi_ps(r[6], r[7]);
+    __m256 u0 = _mm256_shuffle_ps(t0, t2, 0x44), u1 = _mm256_shuffle_ps(t0, t2, 0xEE);
+    __m256 u2 = _mm256_shuffle_ps(t1, t3, 0x44), u3 = _mm256_shuffle_ps(t1, t3, 0xEE);
+    __m256 u4 = _mm256_shuffle_ps(t4, t6, 0x44), u5 = _mm256_shuffle_ps(t4, t6, 0xEE);
+    __m256 u6 = _mm256_shuffle_ps(t5, t7, 0x44), u7 = _mm256_shuffle_ps(t5, t7, 0xEE);
+    r[0] = _mm256_permute2f128_ps(u0, u4, 0x20);
+    r[1] = _mm256_permute2f128_ps(u1, u5, 0x20);
+    r[2] = _mm256_permute2f128_ps(u2, u6, 0x20);
+    r[3] = _mm256_permute2f128_ps(u3, u7, 0x20);
+    r[4] = _mm256_permute2f128_ps(u0, u4, 0x31);
+    r[5] = _mm256_permute2f128_ps(u1, u5, 0x31);
+    r[6] = _mm256_permute2f128_ps(u2, u6, 0x31);
+    r[7] = _mm256_permute2f128_ps(u3, u7, 0x31);
+}
+
 void or_attn_head(const float *q, const uint16_t *k, const uint16_t *v, int64_t ld, int nk,
                   int head_dim, float scale, int chunk, float *out) {
     float qf[512];
@@ -451,12 +498,26 @@ void or_attn_head(const float *q, const uint16_t *k, const uint16_t *v, int64_t 
     for (int c = 0; c < nc; c++) {
         int base = c * chunk, cnt = nk - base < chunk ? nk - base : chunk;
         float m = -INFINITY;
-        for (int j = 0; j < cnt; j++) {
-            const uint16_t *kr = k + (int64_t)(base + j) * ld;
-            float acc = 0.0f;
-            for (int d = 0; d < head_dim; d++) acc = fmaf(qf[d], or_f16_to_f32(kr[d]), acc);
-            s[j] = acc * scale;
-            m = s[j] > m ? s[j] : m;
+        /* eight keys at a time: each key's dot is its own in-order fmaf chain over d (one lane
+         * of a fused multiply-add), the eight chains only run side by side */
+        for (int j0 = 0; j0 < cnt; j0 += 8) {
+            const int nj = cnt - j0 < 8 ? cnt - j0 : 8;
+            __m256 acc = _mm256_setzero_ps();
+            for (int d0 = 0; d0 < head_dim; d0 += 8) {
+                __m256 r[8];
+                for (int jj = 0; jj < 8; jj++) {
+                    const uint16_t *kr = k + (int64_t)(base + j0 + (jj < nj ? jj : 0)) * ld + d0;
+                    r[jj] = _mm256_cvtph_ps(_mm_loadu_si128((const __m128i *)kr));
+                }
+                transpose8(r); /* r[e] = element d0 + e of the eight keys */
+                for (int e = 0; e < 8; e++) acc = _mm256_fmadd_ps(_mm256_set1_ps(qf[d0 + e]), r[e], acc);
+            }
+            float av[8];
+            _mm256_storeu_ps(av, acc);
+            for (int jj = 0; jj < nj; jj++) {
+                s[j0 + jj] = av[jj] * scale;
+                m = s[j0 + jj] > m ? s[j0 + jj] : m;
+            }
         }
         for (int j = 0; j < chunk; j++) p[j] = j < cnt ? or_exp(s[j] - m) : 0.0f;
         float l = 0.0f;
@@ -467,9 +528,13 @@ void or_attn_head(const float *q, const uint16_t *k, const uint16_t *v, int64_t 
             l = l + lane[0];
         }
         float *a = ac + (size_t)c * head_dim;
-        for (int j = 0; j < cnt; j++) {
+        for (int j = 0; j < cnt; j++) { /* a[d] = fmaf(p_j, v_jd, a[d]) in key order */
             const uint16_t *vr = v + (int64_t)(base + j) * ld;
-            for (int d = 0; d < head_dim; d++) a[d] = fmaf(p[j], or_f16_to_f32(vr[d]), a[d]);
+            const __m256 pj = _mm256_set1_ps(p[j]);
+            for (int d0 = 0; d0 < head_dim; d0 += 8) {
+                const __m256 vv = _mm256_cvtph_ps(_mm_loadu_si128((const __m128i *)(vr + d0)));
+                _mm256_storeu_ps(a + d0, _mm256_fmadd_ps(pj, vv, _mm256_loadu_ps(a + d0)));
+            }
         }
         mc[c] = m;
         lc[c] = l;
@@ -831,4 +896,205 @@ int or_debug_hidden(const or_model *m, int t, float *out) {
     if (!m->dbg_hidden || t >= m->dbg_tokens) return -1;
     memcpy(out, m->dbg_hidden + (size_t)t * m->c.n_embd, sizeof(float) * m->c.n_embd);
     return 0;
+}
+
+/* ------------------------------------------------------------------ seeded synthetic weights
+ * The synthetic-weight generator the tests and the bench's CPU arm use, restated here so that
+ * the CPU arm builds the same model bytes without loading the product library. Each
+ * 256-element block of a tensor is a function of (seed, tensor id, element index) only:
+ * values are an Irwin-Hall(4) approximation of N(mean, sigma) from one splitmix64 hash per
+ * element, quantised by a simple K-quant quantiser (per 32-value sub-block min/max with 6-bit
+ * scales and mins for Q4_K; per 16-value sub-block absolute max with int8 scales for Q6_K).
+ * tests/test_oracle.py checks the bytes against the product's bt_synth_tensor. */
+static uint64_t sy_mix(uint64_t z) {
+    z += 0x9E3779B97F4A7C15ull;
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+static float sy_value(uint64_t key, uint64_t idx, float mean, float scale) {
+    uint64_t h = sy_mix(key + idx * 0xD1B54A32D192ED03ull);
+    int s = (int)(h & 0xffffu) + (int)((h >> 16) & 0xffffu) + (int)((h >> 32) & 0xffffu) + (int)(h >> 48);
+    float z = (float)(s - 131070) * scale;
+    return mean + z;
+}
+
+static int sy_clamp(int v, int lo, int hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+static void sy_q4k(const float *x, uint8_t *out) {
+    float scl[8], mns[8];
+    for (int j = 0; j < 8; j++) {
+        float lo = x[32 * j], hi = x[32 * j];
+        for (int l = 1; l < 32; l++) {
+            float v = x[32 * j + l];
+            if (v < lo) lo = v;
+            if (v > hi) hi = v;
+        }
+        if (lo > 0.0f) lo = 0.0f;
+        scl[j] = (hi - lo) / 15.0f;
+        mns[j] = -lo;
+    }
+    float ms = 0.0f, mm = 0.0f;
+    for (int j = 0; j < 8; j++) {
+        if (scl[j] > ms) ms = scl[j];
+        if (mns[j] > mm) mm = mns[j];
+    }
+    uint16_t dh = or_f32_to_f16(ms / 63.0f), dmh = or_f32_to_f16(mm / 63.0f);
+    float df = or_f16_to_f32(dh), dmf = or_f16_to_f32(dmh);
+    int sc[8], m[8];
+    for (int j = 0; j < 8; j++) {
+        sc[j] = df > 0.0f ? sy_clamp((int)rintf(scl[j] / df), 0, 63) : 0;
+        m[j] = dmf > 0.0f ? sy_clamp((int)rintf(mns[j] / dmf), 0, 63) : 0;
+    }
+    out[0] = (uint8_t)(dh & 0xff);
+    out[1] = (uint8_t)(dh >> 8);
+    out[2] = (uint8_t)(dmh & 0xff);
+    out[3] = (uint8_t)(dmh >> 8);
+    for (int j = 0; j < 4; j++) { /* the 12 packed scale bytes of the Q4_K format */
+        out[4 + j] = (uint8_t)((sc[j] & 63) | ((sc[j + 4] >> 4) << 6));
+        out[8 + j] = (uint8_t)((m[j] & 63) | ((m[j + 4] >> 4) << 6));
+        out[12 + j] = (uint8_t)((sc[j + 4] & 0xF) | ((m[j + 4] & 0xF) << 4));
+    }
+    for (int g = 0; g < 4; g++) {
+        float d0 = df * (float)sc[2 * g], m0 = dmf * (float)m[2 * g];
+        float d1 = df * (float)sc[2 * g + 1], m1 = dmf * (float)m[2 * g + 1];
+        for (int l = 0; l < 32; l++) {
+            int q0 = d0 > 0.0f ? sy_clamp((int)rintf((x[64 * g + l] + m0) / d0), 0, 15) : 0;
+            int q1 = d1 > 0.0f ? sy_clamp((int)rintf((x[64 * g + 32 + l] + m1) / d1), 0, 15) : 0;
+            out[16 + 32 * g + l] = (uint8_t)(q0 | (q1 << 4));
+        }
+    }
+}
+
+static void sy_q6k(const float *x, uint8_t *out) {
+    float ds[16];
+    for (int s = 0; s < 16; s++) {
+        float amax = 0.0f, mx = 0.0f;
+        for (int i = 0; i < 16; i++) {
+            float v = x[16 * s + i];
+            if (fabsf(v) > amax) {
+                amax = fabsf(v);
+                mx = v;
+            }
+        }
+        ds[s] = amax == 0.0f ? 0.0f : mx / -32.0f;
+    }
+    float amax = 0.0f, smax = 0.0f;
+    for (int s = 0; s < 16; s++)
+        if (fabsf(ds[s]) > amax) {
+            amax = fabsf(ds[s]);
+            smax = ds[s];
+        }
+    int L[256];
+    int8_t sc[16];
+    uint16_t dh = 0;
+    if (amax == 0.0f) {
+        for (int i = 0; i < 256; i++) L[i] = 32;
+        memset(sc, 0, sizeof sc);
+    } else {
+        float iscale = -128.0f / smax;
+        dh = or_f32_to_f16(1.0f / iscale);
+        float df = or_f16_to_f32(dh);
+        for (int s = 0; s < 16; s++) {
+            sc[s] = (int8_t)sy_clamp((int)rintf(iscale * ds[s]), -128, 127);
+            float den = df * (float)sc[s];
+            for (int i = 0; i < 16; i++)
+                L[16 * s + i] = (den != 0.0f ? sy_clamp((int)rintf(x[16 * s + i] / den), -32, 31) : 0) + 32;
+        }
+    }
+    for (int n = 0; n < 2; n++)
+        for (int l = 0; l < 32; l++) {
+            int a = L[128 * n + l], b = L[128 * n + 32 + l], c = L[128 * n + 64 + l], d = L[128 * n + 96 + l];
+            out[64 * n + l] = (uint8_t)((a & 0xF) | ((c & 0xF) << 4));
+            out[64 * n + 32 + l] = (uint8_t)((b & 0xF) | ((d & 0xF) << 4));
+            out[128 + 32 * n + l] = (uint8_t)((a >> 4) | ((b >> 4) << 2) | ((c >> 4) << 4) | ((d >> 4) << 6));
+        }
+    memcpy(out + 192, sc, 16);
+    out[208] = (uint8_t)(dh & 0xff);
+    out[209] = (uint8_t)(dh >> 8);
+}
+
+uint64_t or_tensor_id(const char *name) { /* FNV-1a, 64-bit */
+    uint64_t h = 1469598103934665603ull;
+    for (; *name; name++) {
+        h ^= (uint8_t)*name;
+        h *= 1099511628211ull;
+    }
+    return h;
+}
+
+int or_synth_tensor(int type, int64_t rows, int64_t cols, uint64_t seed, uint64_t tensor_id, float mean,
+                    float sigma, void *out) {
+    const int64_t n = rows * cols;
+    if (type != OR_F32 && type != OR_F16 && type != OR_Q4_K && type != OR_Q6_K) return -1;
+    if ((type == OR_Q4_K || type == OR_Q6_K) && cols % 256) return -1;
+    const uint64_t key = sy_mix(seed ^ sy_mix(tensor_id));
+    const float scale = sigma * 2.64296052e-05f; /* sigma * sqrt(3) / 65536 */
+    const int eb = type == OR_F32 ? 4 : type == OR_F16 ? 2 : 0;
+    const int bb = type == OR_Q4_K ? 144 : type == OR_Q6_K ? 210 : 256 * eb;
+    const int64_t nblk = (n + 255) / 256;
+    uint8_t *o = (uint8_t *)out;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < nblk; i++) {
+        float x[256];
+        uint8_t blk[1024];
+        for (int k = 0; k < 256; k++) x[k] = sy_value(key, (uint64_t)i * 256u + (uint64_t)k, mean, scale);
+        if (type == OR_Q4_K) sy_q4k(x, blk);
+        else if (type == OR_Q6_K) sy_q6k(x, blk);
+        else if (type == OR_F32) memcpy(blk, x, sizeof x);
+        else
+            for (int k = 0; k < 256; k++) {
+                uint16_t h = or_f32_to_f16(x[k]);
+                blk[2 * k] = (uint8_t)(h & 0xff);
+                blk[2 * k + 1] = (uint8_t)(h >> 8);
+            }
+        int64_t left = n - i * 256;
+        int nb = (eb && left < 256) ? (int)left * eb : bb;
+        memcpy(o + (eb ? i * 256 * eb : i * bb), blk, (size_t)nb);
+    }
+    return 0;
+}
+
+/* ------------------------------------------------------------------ host memory bandwidth
+ * A STREAM-style copy of `bytes` over `threads` OpenMP threads, best of `reps`: GB/s counting
+ * the bytes read and written (the figure the CPU decode's bandwidth ceiling is quoted on). */
+double or_copy_gbs(int64_t bytes, int threads, int reps) {
+    const int64_t n = bytes / 8;
+    double *a = (double *)malloc((size_t)n * 8), *b = (double *)malloc((size_t)n * 8);
+    if (!a || !b) {
+        free(a);
+        free(b);
+        return 0.0;
+    }
+#ifdef _OPENMP
+    if (threads > 0) omp_set_num_threads(threads);
+#endif
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; i++) {
+        a[i] = (double)i;
+        b[i] = 0.0;
+    }
+    double best = 0.0;
+    for (int r = 0; r < reps; r++) {
+#ifdef _OPENMP
+        double t0 = omp_get_wtime();
+#else
+        double t0 = 0.0;
+#endif
+#pragma omp parallel for schedule(static)
+        for (int64_t i = 0; i < n; i++) b[i] = a[i];
+#ifdef _OPENMP
+        double dt = omp_get_wtime() - t0;
+#else
+        double dt = 1.0;
+#endif
+        double gbs = 2.0 * (double)n * 8.0 / dt / 1e9;
+        if (gbs > best) best = gbs;
+    }
+    volatile double sink = b[n / 2];
+    (void)sink;
+    free(a);
+    free(b);
+    return best;
 }

@@ -114,6 +114,16 @@ int or_debug_topk(const or_model *m, int layer, int t, int32_t *ids, float *weig
 int or_debug_hidden(const or_model *m, int t, float *out);
 int or_set_threads(int n);
 
+/* ---- seeded synthetic weights (the tests' and the CPU arm's model bytes) ---- */
+/* FNV-1a of a tensor name: the tensor id of the generator */
+uint64_t or_tensor_id(const char *name);
+/* rows x cols values of N(mean, sigma) (Irwin-Hall(4)) quantised to `type`, GGUF row-major */
+int or_synth_tensor(int type, int64_t rows, int64_t cols, uint64_t seed, uint64_t tensor_id, float mean,
+                    float sigma, void *out);
+
+/* STREAM-style host copy bandwidth (read + write bytes), best of reps, GB/s */
+double or_copy_gbs(int64_t bytes, int threads, int reps);
+
 #ifdef __cplusplus
 }
 #endif

@@ -77,6 +77,9 @@ def lib() -> C.CDLL:
             "or_debug_topk": (I, [P, I, I, C.POINTER(C.c_int32), F]),
             "or_debug_hidden": (I, [P, I, F]),
             "or_set_threads": (I, [I]),
+            "or_tensor_id": (C.c_uint64, [C.c_char_p]),
+            "or_synth_tensor": (I, [I, C.c_int64, C.c_int64, C.c_uint64, C.c_uint64, C.c_float, C.c_float, P]),
+            "or_copy_gbs": (C.c_double, [C.c_int64, I, I]),
         }
         for n, (r, a) in sig.items():
             fn = getattr(L, n)
@@ -120,6 +123,29 @@ def gemv(ggml_type: int, w: np.ndarray, rows: int, cols: int, x: np.ndarray) -> 
             raise ValueError("or_gemv rejected the input")
         y[t] = yt
     return y
+
+
+def row_bytes(ggml_type: int, n: int) -> int:
+    return int(lib().or_row_bytes(ggml_type, n))
+
+
+def synth_tensor(name: str, ggml_type: int, ne: tuple, mean: float, seed: int, sigma: float = 0.02) -> np.ndarray:
+    """The seeded synthetic tensor `name` (ggml dims `ne`, innermost first) as GGUF bytes."""
+    n = 1
+    for d in ne:
+        n *= d
+    cols = ne[0]
+    nbytes = (n // cols) * row_bytes(ggml_type, cols) if ggml_type in (OR_Q4_K, OR_Q6_K) else n * (4 if ggml_type == OR_F32 else 2)
+    buf = np.empty(nbytes, np.uint8)
+    if lib().or_synth_tensor(ggml_type, n // cols, cols, seed, lib().or_tensor_id(name.encode()), mean, sigma,
+                             buf.ctypes.data_as(C.c_void_p)):
+        raise ValueError(f"or_synth_tensor rejected {name}")
+    return buf
+
+
+def synth_model(specs, seed: int, sigma: float = 0.02) -> dict:
+    """name -> (type, dims, bytes) for (name, type, dims, mean) specs, without the product library."""
+    return {name: (ty, ne, synth_tensor(name, ty, ne, mean, seed, sigma)) for name, ty, ne, mean in specs}
 
 
 def exp(x: float) -> float:

@@ -385,3 +385,33 @@ def test_forward_refuses_a_wrong_position(tiny_cfg, tiny_weights):
     m = orc.Model(tiny_cfg, tiny_weights)
     with pytest.raises(ValueError):
         m.forward([1, 2], 3)
+
+
+@pytest.mark.parametrize("ty,ne,mean", [(orc.OR_Q4_K, (2048, 96), 0.0), (orc.OR_Q6_K, (768, 40), 0.0),
+                                        (orc.OR_F32, (2048,), 1.0), (orc.OR_F32, (1000, 3), 0.0),
+                                        (orc.OR_F16, (300,), 0.5)])
+def test_oracle_synthetic_weights_equal_the_libraries(ty, ne, mean):
+    """The CPU arm builds its model with the oracle's generator (it never loads the product
+    library); the bytes must be the product generator's for the same seed and tensor name."""
+    import bigtea_b200 as bt
+
+    name = f"blk.3.synth_check_{ty}.weight"
+    got = orc.synth_tensor(name, ty, ne, mean, seed=77)
+    want = bt.models.synth_tensor(name, ty, ne, mean, seed=77)
+    assert got.dtype == np.uint8 and np.array_equal(got, want)
+
+
+@pytest.mark.parametrize("name", ["cfg0", "cfg1"])
+def test_cpu_arm_workloads_equal_the_products(name):
+    """The CPU arm's description of the benchmark models (oracle/workloads.py) has the product's
+    hyper-parameters and exactly its tensor list, types, dims and means."""
+    import bigtea_b200 as bt
+    from oracle import workloads
+
+    w = workloads.workload(name)
+    c = bt.config(name)
+    for f in ("n_layer", "n_embd", "n_head", "n_head_kv", "head_dim", "n_expert", "n_expert_used", "n_ff_exp",
+              "n_vocab", "rms_eps", "rope_freq_base", "expert_workers", "max_positions", "embd_type", "out_type",
+              "layer_types"):
+        assert getattr(w, f) == getattr(c, f), f
+    assert w.tensor_specs() == c.tensor_specs()
