@@ -556,6 +556,200 @@ void or_attn_head(const float *q, const uint16_t *k, const uint16_t *v, int64_t 
     free(p);
 }
 
+/* ------------------------------------------------------------------ ggml-cpu's generic algorithms
+ * A second set of numerics, chosen per op by the bits of or_config.numerics (OR_NUM_*), that
+ * restates the scalar ("generic", no SIMD) code paths of ggml's CPU backend for the calls the
+ * reference makes on this path. It is not what the device computes: it measures how far the
+ * arithmetic contract above lies from ggml's own results on the same model and tokens.
+ * ggml is llama.cpp's tensor library (MIT), unpinned in the reference (git HEAD, CI); these are
+ * restatements of its published algorithms, cited by function:
+ *  - rms_norm (ggml_compute_forward_rms_norm_f32; call site graph.rs:705): sum of the f32
+ *    squares in ggml_float (double), in order; mean = (float)(sum / n); scale = 1.0f /
+ *    sqrtf(mean + eps); y = x * scale, then ggml_mul by the weight;
+ *  - mul_mat of a K-quant matrix (graph.rs:690): activations to Q8_K (quantize_row_q8_K_ref, the
+ *    contract's C3), then ggml_vec_dot_q{4,6}_K_q8_K_generic: eight int32 lanes per superblock
+ *    (lane l collects positions l mod 8), float lanes sums[l] += d * aux32[l] over superblocks,
+ *    the Q4_K min term subtracted from a separate float sumf per superblock, lanes added at end;
+ *  - mul_mat of an F32 matrix (the router): ggml_vec_dot_f32 generic, products in f32, sum in
+ *    double, in order;
+ *  - soft_max_ext(logits, no mask, scale 1, max_bias 0) (graph.rs:1616-1630): max in order,
+ *    val = expf(x - max) (libm), sum in double, y = val * (float)(1.0 / sum);
+ *  - silu (graph.rs:731): x / (1.0f + expf(-x)) (libm), then ggml_mul by up and ggml_scale by
+ *    the route weight;
+ *  - flash_attn_ext (graph.rs:1220-1247; ggml_compute_forward_flash_attn_ext_f16_one_chunk): q
+ *    converted to f16; per key in order: s = ggml_vec_dot_f16 (f16 products in f32, summed in
+ *    double) * scale; online softmax: a new maximum M rescales the accumulator by
+ *    ms = expf(Mold - M) (ggml_vec_scale_f16), else vs = expf(s - M); the value row is added
+ *    with weight vs (ggml_vec_mad_f16: y = f16(f32(y) + f32(v) * vs)); S = S * ms + vs; at the
+ *    end out = f32(acc) * (1.0f / S). With f16 values ggml keeps that accumulator in f16 (the
+ *    VKQ16 buffer); OR_NUM_ATTN_F32V keeps it in f32 instead, the accumulation of ggml's
+ *    f32-value branch, to show how much of the distance the f16 accumulator accounts for.
+ * Multiplications and additions are separately rounded (ggml's generic C is compiled as ISO C,
+ * where GCC does not contract them). OR_NUM_FMA contracts the multiply-adds of the K-quant dot
+ * lanes and of the attention accumulator into fmaf, as a GNU-C build of the same generic code
+ * would: another build of ggml, to show how far two builds of ggml lie from each other. */
+static float gg_sumsq_scale(const float *x, int n, float eps) {
+    double sum = 0.0;
+    for (int i = 0; i < n; i++) sum += (double)(x[i] * x[i]);
+    const float mean = (float)(sum / n);
+    return 1.0f / sqrtf(mean + eps);
+}
+
+static void gg_rmsnorm(const float *x, const float *w, int n, float eps, float *y) {
+    const float sc = gg_sumsq_scale(x, n, eps);
+    for (int i = 0; i < n; i++) y[i] = (x[i] * sc) * w[i];
+}
+
+static float gg_dot_q4k_row(const uint8_t *row, const or_block_q8k *a, int nsb, int fma) {
+    float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0}, sumf = 0.0f;
+    for (int b = 0; b < nsb; b++) {
+        const uint8_t *blk = row + 144 * b;
+        const or_block_q8k *ab = a + b;
+        int8_t q[256];
+        int sc[8], mn[8];
+        unpack_q4k(blk, q, sc, mn);
+        int32_t aux32[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int j = 0; j < 8; j++)         /* sub-blocks of 32 */
+            for (int k = 0; k < 4; k++)     /* four groups of 8 */
+                for (int l = 0; l < 8; l++) aux32[l] += sc[j] * (q[32 * j + 8 * k + l] * ab->qs[32 * j + 8 * k + l]);
+        int32_t summ = 0;
+        for (int j = 0; j < 16; j++) summ += ab->bsums[j] * mn[j / 2];
+        const float d = or_f16_to_f32(rd16(blk)) * ab->d;
+        for (int l = 0; l < 8; l++) sums[l] = fma ? fmaf(d, (float)aux32[l], sums[l]) : sums[l] + d * (float)aux32[l];
+        const float dmin = or_f16_to_f32(rd16(blk + 2)) * ab->d;
+        sumf = fma ? fmaf(-dmin, (float)summ, sumf) : sumf - dmin * (float)summ;
+    }
+    for (int l = 0; l < 8; l++) sumf += sums[l];
+    return sumf;
+}
+
+static float gg_dot_q6k_row(const uint8_t *row, const or_block_q8k *a, int nsb, int fma) {
+    float sums[8] = {0, 0, 0, 0, 0, 0, 0, 0}, sumf = 0.0f;
+    for (int b = 0; b < nsb; b++) {
+        const uint8_t *blk = row + 210 * b;
+        const or_block_q8k *ab = a + b;
+        const int8_t *sc = (const int8_t *)(blk + 192);
+        int8_t q[256];
+        unpack_q6k(blk, q);
+        int32_t aux32[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        for (int j = 0; j < 16; j++)        /* sub-blocks of 16 */
+            for (int k = 0; k < 2; k++)
+                for (int l = 0; l < 8; l++) aux32[l] += sc[j] * (q[16 * j + 8 * k + l] * ab->qs[16 * j + 8 * k + l]);
+        const float d = or_f16_to_f32(rd16(blk + 208)) * ab->d;
+        for (int l = 0; l < 8; l++) sums[l] = fma ? fmaf(d, (float)aux32[l], sums[l]) : sums[l] + d * (float)aux32[l];
+    }
+    for (int l = 0; l < 8; l++) sumf += sums[l];
+    return sumf;
+}
+
+static float gg_dot_f32(const float *a, const float *b, int n) {
+    double sum = 0.0;
+    for (int i = 0; i < n; i++) sum += (double)(a[i] * b[i]);
+    return (float)sum;
+}
+
+static int gg_gemv(int type, const void *W, int64_t rows, int64_t cols, const float *x, float *y, int fma) {
+    const uint8_t *w = (const uint8_t *)W;
+    if (type == OR_F32) {
+#pragma omp parallel for schedule(static)
+        for (int64_t r = 0; r < rows; r++) y[r] = gg_dot_f32((const float *)(w + r * cols * 4), x, (int)cols);
+        return 0;
+    }
+    if ((type != OR_Q4_K && type != OR_Q6_K) || cols % 256) return -1;
+    const int nsb = (int)(cols / 256);
+    or_block_q8k *a = (or_block_q8k *)malloc(sizeof(or_block_q8k) * (size_t)nsb);
+    or_quantize_q8k(x, cols, a);
+    const int64_t rb = or_row_bytes(type, cols);
+#pragma omp parallel for schedule(static)
+    for (int64_t r = 0; r < rows; r++)
+        y[r] = (type == OR_Q4_K) ? gg_dot_q4k_row(w + r * rb, a, nsb, fma) : gg_dot_q6k_row(w + r * rb, a, nsb, fma);
+    free(a);
+    return 0;
+}
+
+static void gg_softmax(const float *x, int n, float *y) {
+    float mx = -INFINITY;
+    for (int i = 0; i < n; i++) mx = x[i] > mx ? x[i] : mx;
+    double sum = 0.0;
+    for (int i = 0; i < n; i++) {
+        const float v = expf(x[i] - mx);
+        sum += (double)v;
+        y[i] = v;
+    }
+    const float inv = (float)(1.0 / sum);
+    for (int i = 0; i < n; i++) y[i] *= inv;
+}
+
+static float gg_silu(float x) { return x / (1.0f + expf(-x)); }
+
+static void gg_attn_head(const float *q, const uint16_t *k, const uint16_t *v, int64_t ld, int nk, int head_dim,
+                         float scale, int f32_acc, int fma, float *out) {
+    float qf[512], acc32[512];
+    uint16_t acc16[512];
+    for (int d = 0; d < head_dim; d++) {
+        qf[d] = or_f16_to_f32(or_f32_to_f16(q[d]));
+        acc32[d] = 0.0f;
+        acc16[d] = 0;
+    }
+    float S = 0.0f, M = -INFINITY;
+    for (int j = 0; j < nk; j++) {
+        const uint16_t *kr = k + (int64_t)j * ld, *vr = v + (int64_t)j * ld;
+        double dot = 0.0;
+        for (int d = 0; d < head_dim; d++) dot += (double)(or_f16_to_f32(kr[d]) * qf[d]);
+        float s = (float)dot;
+        s = s * scale;
+        s += 0.0f; /* the causal mask: 0 for every visible key */
+        const float Mold = M;
+        float ms = 1.0f, vs = 1.0f;
+        if (s > M) {
+            M = s;
+            ms = expf(Mold - M);
+            for (int d = 0; d < head_dim; d++) {
+                if (f32_acc) acc32[d] *= ms;
+                else acc16[d] = or_f32_to_f16(or_f16_to_f32(acc16[d]) * ms);
+            }
+        } else {
+            vs = expf(s - M);
+        }
+        for (int d = 0; d < head_dim; d++) {
+            const float a0 = f32_acc ? acc32[d] : or_f16_to_f32(acc16[d]), vv = or_f16_to_f32(vr[d]);
+            const float a1 = fma ? fmaf(vv, vs, a0) : a0 + vv * vs;
+            if (f32_acc) acc32[d] = a1;
+            else acc16[d] = or_f32_to_f16(a1);
+        }
+        S = S * ms + vs;
+    }
+    const float S_inv = S == 0.0f ? 0.0f : 1.0f / S;
+    for (int d = 0; d < head_dim; d++) out[d] = (f32_acc ? acc32[d] : or_f16_to_f32(acc16[d])) * S_inv;
+}
+
+/* the per-op dispatch the model uses: each op takes ggml's algorithm when its bit is set */
+static int num_gemv(int mode, int type, const void *W, int64_t rows, int64_t cols, const float *x, float *y) {
+    const int bit = type == OR_F32 ? OR_NUM_FDOT : OR_NUM_QDOT;
+    return (mode & bit) ? gg_gemv(type, W, rows, cols, x, y, (mode & OR_NUM_FMA) != 0)
+                        : or_gemv(type, W, rows, cols, x, y);
+}
+static void num_rmsnorm(int mode, const float *x, const float *w, int n, float eps, float *y) {
+    if (mode & OR_NUM_NORM) gg_rmsnorm(x, w, n, eps, y);
+    else or_rmsnorm(x, w, n, eps, y);
+}
+static void num_softmax(int mode, const float *x, int n, float *y) {
+    if (mode & OR_NUM_SOFTMAX) gg_softmax(x, n, y);
+    else or_softmax(x, n, y);
+}
+static float num_silu(int mode, float x) { return (mode & OR_NUM_SILU) ? gg_silu(x) : or_silu(x); }
+
+/* single ops of the ggml mode, for the tests' independent numpy restatement */
+void or_ggml_rmsnorm(const float *x, const float *w, int n, float eps, float *y) { gg_rmsnorm(x, w, n, eps, y); }
+int or_ggml_gemv(int type, const void *W, int64_t rows, int64_t cols, const float *x, float *y) {
+    return gg_gemv(type, W, rows, cols, x, y, 0);
+}
+void or_ggml_softmax(const float *x, int n, float *y) { gg_softmax(x, n, y); }
+void or_ggml_attn_head(const float *q, const uint16_t *k, const uint16_t *v, int64_t ld, int nk, int head_dim,
+                       float scale, int f32_acc, float *out) {
+    gg_attn_head(q, k, v, ld, nk, head_dim, scale, f32_acc, 0, out);
+}
+
 /* ------------------------------------------------------------------ model */
 typedef struct {
     int type;
@@ -581,6 +775,11 @@ struct or_model {
     int32_t *dbg_ids;   /* [n_layer][T][k] */
     float *dbg_w;       /* [n_layer][T][k] */
     float *dbg_hidden;  /* [T][E] */
+    float *dbg_gap;     /* [n_layer][T]: the K-th largest router probability minus the (K+1)-th */
+    /* when set: route() is replaced by that model's choice for the same layer and token in its
+     * last forward (the weights still come from this model's own probabilities), so that two
+     * numerics can be compared without the discontinuity of a different expert set */
+    const struct or_model *route_from;
 };
 
 struct or_kv {
@@ -669,7 +868,16 @@ void or_model_free(or_model *m) {
     free(m->dbg_ids);
     free(m->dbg_w);
     free(m->dbg_hidden);
+    free(m->dbg_gap);
     free(m);
+}
+
+void or_model_route_from(or_model *m, const or_model *src) { m->route_from = src; }
+
+int or_debug_route_gap(const or_model *m, int layer, int t, float *gap) {
+    if (!m->dbg_gap || t >= m->dbg_tokens || layer >= m->c.n_layer) return -1;
+    *gap = m->dbg_gap[(size_t)layer * m->dbg_tokens + t];
+    return 0;
 }
 
 or_kv *or_kv_new(const or_model *m) {
@@ -718,6 +926,7 @@ int or_forward(or_model *m, or_kv *kv, const int32_t *tokens, int T, int pos_sta
     const int E = c->n_embd, H = c->n_head, HK = c->n_head_kv, D = c->head_dim;
     const int NE = c->n_expert, K = c->n_expert_used, F = c->n_ff_exp;
     const int QW = H * D, KW = HK * D;
+    const int mode = c->numerics;
     if (T <= 0) { set_err("no tokens"); return -1; }
     if (pos_start != kv->len) { set_err("pos_start must equal the cache length"); return -1; }
     if (pos_start + T > c->max_positions) { set_err("context exceeds max_positions"); return -1; }
@@ -727,6 +936,8 @@ int or_forward(or_model *m, or_kv *kv, const int32_t *tokens, int T, int pos_sta
     free(m->dbg_ids);
     free(m->dbg_w);
     free(m->dbg_hidden);
+    free(m->dbg_gap);
+    m->dbg_gap = (float *)calloc((size_t)c->n_layer * T, sizeof(float));
     m->dbg_tokens = T;
     m->dbg_ids = (int32_t *)calloc((size_t)c->n_layer * T * K, sizeof(int32_t));
     m->dbg_w = (float *)calloc((size_t)c->n_layer * T * K, sizeof(float));
@@ -767,19 +978,19 @@ int or_forward(or_model *m, or_kv *kv, const int32_t *tokens, int T, int pos_sta
         /* phase 1: attn norm, q/k/v, q/k head norms, rope (stream.rs:2265-2474) */
         for (int t = 0; t < T; t++) {
             float *xt = x + (size_t)t * E, *xnt = xn + (size_t)t * E;
-            or_rmsnorm(xt, (const float *)w->attn_norm.data, E, c->rms_eps, xnt);
-            or_gemv(w->q.type, w->q.data, QW, E, xnt, q + (size_t)t * QW);
-            or_gemv(w->k.type, w->k.data, KW, E, xnt, kk + (size_t)t * KW);
-            or_gemv(w->v.type, w->v.data, KW, E, xnt, vv + (size_t)t * KW);
+            num_rmsnorm(mode, xt, (const float *)w->attn_norm.data, E, c->rms_eps, xnt);
+            num_gemv(mode, w->q.type, w->q.data, QW, E, xnt, q + (size_t)t * QW);
+            num_gemv(mode, w->k.type, w->k.data, KW, E, xnt, kk + (size_t)t * KW);
+            num_gemv(mode, w->v.type, w->v.data, KW, E, xnt, vv + (size_t)t * KW);
             const float *cs = m->rope + (size_t)(pos_start + t) * c->n_rot;
             for (int h = 0; h < H; h++) {
                 float *qh = q + (size_t)t * QW + h * D;
-                or_rmsnorm(qh, (const float *)w->q_norm.data, D, c->rms_eps, qh);
+                num_rmsnorm(mode, qh, (const float *)w->q_norm.data, D, c->rms_eps, qh);
                 or_rope_neox(qh, c->n_rot, cs);
             }
             for (int h = 0; h < HK; h++) {
                 float *kh = kk + (size_t)t * KW + h * D;
-                or_rmsnorm(kh, (const float *)w->k_norm.data, D, c->rms_eps, kh);
+                num_rmsnorm(mode, kh, (const float *)w->k_norm.data, D, c->rms_eps, kh);
                 or_rope_neox(kh, c->n_rot, cs);
             }
             /* KvCache::push: f32 -> f16 (kv.rs:184-192) */
@@ -795,22 +1006,46 @@ int or_forward(or_model *m, or_kv *kv, const int32_t *tokens, int T, int pos_sta
         for (int t = 0; t < T; t++)
             for (int h = 0; h < H; h++) {
                 int g2 = h / (H / HK);
-                or_attn_head(q + (size_t)t * QW + h * D, kv->k[il] + g2 * D, kv->v[il] + g2 * D, KW,
-                             pos_start + t + 1, D, scale, c->attn_chunk, att + (size_t)t * QW + h * D);
+                if (mode & (OR_NUM_ATTN | OR_NUM_ATTN_F32V))
+                    gg_attn_head(q + (size_t)t * QW + h * D, kv->k[il] + g2 * D, kv->v[il] + g2 * D, KW,
+                                 pos_start + t + 1, D, scale, (mode & OR_NUM_ATTN_F32V) != 0, (mode & OR_NUM_FMA) != 0,
+                                 att + (size_t)t * QW + h * D);
+                else
+                    or_attn_head(q + (size_t)t * QW + h * D, kv->k[il] + g2 * D, kv->v[il] + g2 * D, KW,
+                                 pos_start + t + 1, D, scale, c->attn_chunk, att + (size_t)t * QW + h * D);
             }
         for (int t = 0; t < T; t++) {
-            or_gemv(w->o.type, w->o.data, E, QW, att + (size_t)t * QW, ao + (size_t)t * E);
+            num_gemv(mode, w->o.type, w->o.data, E, QW, att + (size_t)t * QW, ao + (size_t)t * E);
             for (int i = 0; i < E; i++) ffin[(size_t)t * E + i] = x[(size_t)t * E + i] + ao[(size_t)t * E + i];
         }
         /* phase 3: ffn norm, router, softmax (stream.rs:2784-2831) and experts */
         for (int t = 0; t < T; t++) {
             float *fi = ffin + (size_t)t * E, *fn = xn + (size_t)t * E;
-            or_rmsnorm(fi, (const float *)w->ffn_norm.data, E, c->rms_eps, fn);
-            or_gemv(OR_F32, w->gate_inp.data, NE, E, fn, rl);
+            num_rmsnorm(mode, fi, (const float *)w->ffn_norm.data, E, c->rms_eps, fn);
+            num_gemv(mode, OR_F32, w->gate_inp.data, NE, E, fn, rl);
             if (w->gate_bias.data) /* ggml_add of the router bias: one f32 add per logit */
                 for (int i = 0; i < NE; i++) rl[i] = rl[i] + ((const float *)w->gate_bias.data)[i];
-            or_softmax(rl, NE, pr);
+            num_softmax(mode, rl, NE, pr);
             or_route(pr, NE, K, ids, wts);
+            {
+                float next = -INFINITY; /* the largest probability route() did not take */
+                for (int e = 0; e < NE; e++) {
+                    int taken = 0;
+                    for (int i = 0; i < K; i++) taken |= ids[i] == e;
+                    if (!taken && pr[e] > next) next = pr[e];
+                }
+                m->dbg_gap[(size_t)il * T + t] = pr[ids[K - 1]] - next;
+            }
+            if (m->route_from && m->route_from->dbg_ids && m->route_from->dbg_tokens == T) {
+                float total = 0.0f;
+                for (int i = 0; i < K; i++) {
+                    ids[i] = m->route_from->dbg_ids[((size_t)il * T + t) * K + i];
+                    wts[i] = pr[ids[i]];
+                    total = total + wts[i];
+                }
+                if (total > 0.0f)
+                    for (int i = 0; i < K; i++) wts[i] = wts[i] / total;
+            }
             memcpy(m->dbg_ids + ((size_t)il * T + t) * K, ids, sizeof(int32_t) * K);
             memcpy(m->dbg_w + ((size_t)il * T + t) * K, wts, sizeof(float) * K);
             /* ascending expert order (BTreeMap in expert_ffn_block, stream.rs:916-926) */
@@ -831,10 +1066,10 @@ int or_forward(or_model *m, or_kv *kv, const int32_t *tokens, int T, int pos_sta
                 }
             for (int i = 0; i < K; i++) {
                 int e = sid[i];
-                or_gemv(w->gate.type, expert_slice(&w->gate, e, F, E), F, E, fn, g);
-                or_gemv(w->up.type, expert_slice(&w->up, e, F, E), F, E, fn, u);
-                for (int j = 0; j < F; j++) g[j] = or_silu(g[j]) * u[j];
-                or_gemv(w->down.type, expert_slice(&w->down, e, E, F), E, F, g, o);
+                num_gemv(mode, w->gate.type, expert_slice(&w->gate, e, F, E), F, E, fn, g);
+                num_gemv(mode, w->up.type, expert_slice(&w->up, e, F, E), F, E, fn, u);
+                for (int j = 0; j < F; j++) g[j] = num_silu(mode, g[j]) * u[j];
+                num_gemv(mode, w->down.type, expert_slice(&w->down, e, E, F), E, F, g, o);
                 for (int j = 0; j < E; j++) eo[(size_t)i * E + j] = o[j] * sw[i];
             }
             if (T == 1) {
@@ -861,10 +1096,10 @@ int or_forward(or_model *m, or_kv *kv, const int32_t *tokens, int T, int pos_sta
             if (w->gate_sh.data) {
                 /* shared expert: down(silu(gate x) * up x), then x = (moe + shexp) + ffn_inp */
                 const int fs = (int)w->gate_sh.ne[1];
-                or_gemv(w->gate_sh.type, w->gate_sh.data, fs, E, fn, gsh);
-                or_gemv(w->up_sh.type, w->up_sh.data, fs, E, fn, ush);
-                for (int j = 0; j < fs; j++) gsh[j] = or_silu(gsh[j]) * ush[j];
-                or_gemv(w->down_sh.type, w->down_sh.data, E, fs, gsh, sh);
+                num_gemv(mode, w->gate_sh.type, w->gate_sh.data, fs, E, fn, gsh);
+                num_gemv(mode, w->up_sh.type, w->up_sh.data, fs, E, fn, ush);
+                for (int j = 0; j < fs; j++) gsh[j] = num_silu(mode, gsh[j]) * ush[j];
+                num_gemv(mode, w->down_sh.type, w->down_sh.data, E, fs, gsh, sh);
                 for (int j = 0; j < E; j++) x[(size_t)t * E + j] = (sum[j] + sh[j]) + fi[j];
             } else {
                 for (int j = 0; j < E; j++) x[(size_t)t * E + j] = fi[j] + sum[j];
@@ -875,8 +1110,8 @@ int or_forward(or_model *m, or_kv *kv, const int32_t *tokens, int T, int pos_sta
     memcpy(m->dbg_hidden, x, sizeof(float) * (size_t)T * E);
 
     /* output head on the last position (stream.rs:2853-2914) */
-    or_rmsnorm(x + (size_t)(T - 1) * E, (const float *)m->out_norm.data, E, c->rms_eps, xn);
-    or_gemv(m->out.type, m->out.data, c->n_vocab, E, xn, logits);
+    num_rmsnorm(mode, x + (size_t)(T - 1) * E, (const float *)m->out_norm.data, E, c->rms_eps, xn);
+    num_gemv(mode, m->out.type, m->out.data, c->n_vocab, E, xn, logits);
 
     free(x); free(xn); free(q); free(kk); free(vv); free(att); free(ao); free(ffin);
     free(rl); free(pr); free(g); free(u); free(o); free(eo); free(sum); free(tot);

@@ -81,7 +81,30 @@ typedef struct {
     int expert_workers; /* reference default 4 (stream.rs:1305-1312) */
     int attn_chunk;     /* attention contract chunk, 128 */
     int max_positions;  /* RoPE table / KV capacity */
+    /* 0 (OR_NUM_CONTRACT): the arithmetic contract the device implements -- the parity oracle.
+     * Otherwise a set of OR_NUM_* bits: each op whose bit is set computes with ggml-cpu's
+     * generic algorithm instead (OR_NUM_GGML: all of them), to measure the distance. */
+    int numerics;
 } or_config;
+
+enum {
+    OR_NUM_CONTRACT = 0,
+    OR_NUM_NORM = 1,       /* rms_norm: squares summed in double */
+    OR_NUM_QDOT = 2,       /* K-quant x Q8_K dots: the generic eight-lane sums */
+    OR_NUM_FDOT = 4,       /* F32 dots (the router): products summed in double */
+    OR_NUM_SOFTMAX = 8,    /* soft_max: libm expf, double sum */
+    OR_NUM_SILU = 16,      /* silu: libm expf */
+    OR_NUM_ATTN = 32,      /* flash_attn_ext: serial online softmax, f16 accumulator */
+    OR_NUM_ATTN_F32V = 64, /* the same with an f32 accumulator */
+    OR_NUM_FMA = 128,      /* the dot lanes and the attention accumulator contracted into fmaf */
+    OR_NUM_GGML = 63
+};
+/* single ops of the ggml mode */
+void or_ggml_rmsnorm(const float *x, const float *w, int n, float eps, float *y);
+int or_ggml_gemv(int type, const void *W, int64_t rows, int64_t cols, const float *x, float *y);
+void or_ggml_softmax(const float *x, int n, float *y);
+void or_ggml_attn_head(const float *q, const uint16_t *k, const uint16_t *v, int64_t ld, int nk, int head_dim,
+                       float scale, int f32_acc, float *out);
 
 typedef struct {
     const char *name;
@@ -113,6 +136,10 @@ int or_debug_topk(const or_model *m, int layer, int t, int32_t *ids, float *weig
 /* the residual stream after the last layer for token t of the last forward */
 int or_debug_hidden(const or_model *m, int t, float *out);
 int or_set_threads(int n);
+/* route() replaced by src's choice for the same layer and token of src's last forward (NULL: off) */
+void or_model_route_from(or_model *m, const or_model *src);
+/* the K-th largest router probability minus the (K+1)-th, for token t of the last forward */
+int or_debug_route_gap(const or_model *m, int layer, int t, float *gap);
 
 /* ---- seeded synthetic weights (the tests' and the CPU arm's model bytes) ---- */
 /* FNV-1a of a tensor name: the tensor id of the generator */

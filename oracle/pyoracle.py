@@ -26,7 +26,15 @@ class Config(C.Structure):
     _fields_ = [(n, C.c_int) for n in ("n_layer", "n_embd", "n_head", "n_head_kv", "head_dim", "n_expert",
                                         "n_expert_used", "n_ff_exp", "n_vocab", "n_rot")] + \
                [("rms_eps", C.c_float), ("rope_base", C.c_float), ("expert_workers", C.c_int),
-                ("attn_chunk", C.c_int), ("max_positions", C.c_int)]
+                ("attn_chunk", C.c_int), ("max_positions", C.c_int), ("numerics", C.c_int)]
+
+
+# numerics of an oracle model: 0 = the device's arithmetic contract; else a set of bits, each op
+# whose bit is set computing with ggml-cpu's generic algorithm (NUM_GGML: all of them)
+NUM_CONTRACT, NUM_NORM, NUM_QDOT, NUM_FDOT, NUM_SOFTMAX, NUM_SILU, NUM_ATTN, NUM_ATTN_F32V, NUM_FMA = \
+    0, 1, 2, 4, 8, 16, 32, 64, 128
+NUM_GGML = 63
+NUM_GGML_F32V = NUM_GGML & ~NUM_ATTN | NUM_ATTN_F32V
 
 
 class Tensor(C.Structure):
@@ -80,6 +88,13 @@ def lib() -> C.CDLL:
             "or_tensor_id": (C.c_uint64, [C.c_char_p]),
             "or_synth_tensor": (I, [I, C.c_int64, C.c_int64, C.c_uint64, C.c_uint64, C.c_float, C.c_float, P]),
             "or_copy_gbs": (C.c_double, [C.c_int64, I, I]),
+            "or_model_route_from": (None, [P, P]),
+            "or_debug_route_gap": (I, [P, I, I, F]),
+            "or_ggml_rmsnorm": (None, [F, F, I, C.c_float, F]),
+            "or_ggml_gemv": (I, [I, P, C.c_int64, C.c_int64, F, F]),
+            "or_ggml_softmax": (None, [F, I, F]),
+            "or_ggml_attn_head": (None, [F, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), C.c_int64, I, I, C.c_float,
+                                         I, F]),
         }
         for n, (r, a) in sig.items():
             fn = getattr(L, n)
@@ -171,6 +186,41 @@ def route(probs, k):
     return ids, w
 
 
+def ggml_rmsnorm(x, w, eps):
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w, np.float32)
+    out = np.empty_like(x)
+    lib().or_ggml_rmsnorm(_f(x), _f(w), x.size, eps, _f(out))
+    return out
+
+
+def ggml_gemv(ggml_type: int, w: np.ndarray, rows: int, cols: int, x: np.ndarray) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    w = np.ascontiguousarray(w).view(np.uint8)
+    y = np.empty(rows, np.float32)
+    if lib().or_ggml_gemv(ggml_type, w.ctypes.data_as(C.c_void_p), rows, cols, _f(x), _f(y)):
+        raise ValueError("or_ggml_gemv rejected the input")
+    return y
+
+
+def ggml_softmax(x) -> np.ndarray:
+    x = np.ascontiguousarray(x, np.float32)
+    out = np.empty_like(x)
+    lib().or_ggml_softmax(_f(x), x.size, _f(out))
+    return out
+
+
+def ggml_attn_head(q, k16, v16, nk, scale, f32_acc=False):
+    q = np.ascontiguousarray(q, np.float32)
+    k16 = np.ascontiguousarray(k16, np.uint16)
+    v16 = np.ascontiguousarray(v16, np.uint16)
+    out = np.empty(q.size, np.float32)
+    u16 = C.POINTER(C.c_uint16)
+    lib().or_ggml_attn_head(_f(q), k16.ctypes.data_as(u16), v16.ctypes.data_as(u16), k16.shape[1], nk, q.size, scale,
+                            int(f32_acc), _f(out))
+    return out
+
+
 def argmax(logits) -> int:
     x = np.ascontiguousarray(logits, np.float32)
     return int(lib().or_argmax(_f(x), x.size))
@@ -205,10 +255,10 @@ def attn_head(q, k16, v16, nk, scale, chunk=128):
 class Model:
     """The whole qwen3moe decode path on the CPU: forward_cached over a contiguous f16 cache."""
 
-    def __init__(self, cfg, tensors: dict):
+    def __init__(self, cfg, tensors: dict, numerics: int = NUM_CONTRACT):
         c = Config(cfg.n_layer, cfg.n_embd, cfg.n_head, cfg.n_head_kv, cfg.head_dim, cfg.n_expert,
                    cfg.n_expert_used, cfg.n_ff_exp, cfg.n_vocab, cfg.head_dim, cfg.rms_eps, cfg.rope_freq_base,
-                   cfg.expert_workers, ATTN_CHUNK, cfg.max_positions)
+                   cfg.expert_workers, ATTN_CHUNK, cfg.max_positions, numerics)
         self.cfg = cfg
         self._keep = []
         arr = (Tensor * len(tensors))()
@@ -275,6 +325,17 @@ class Model:
         if lib().or_debug_topk(self.h, layer, t, ids.ctypes.data_as(C.POINTER(C.c_int32)), _f(w)):
             raise ValueError("no top-k capture")
         return ids, w
+
+    def route_from(self, other):
+        """take route()'s expert choice from `other`'s last forward (None: route itself)"""
+        self._route_src = other
+        lib().or_model_route_from(self.h, other.h if other is not None else None)
+
+    def route_gap(self, layer: int, t: int) -> float:
+        g = C.c_float()
+        if lib().or_debug_route_gap(self.h, layer, t, C.byref(g)):
+            raise ValueError("no route capture")
+        return g.value
 
     def hidden(self, t: int) -> np.ndarray:
         out = np.empty(self.cfg.n_embd, np.float32)
