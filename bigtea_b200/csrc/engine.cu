@@ -124,6 +124,9 @@ struct bt_engine {
     // expert parallelism (bt_engine_enable_ep): this rank computes experts [rank*NE/n, (rank+1)*NE/n)
     bool ep = false;
     int ep_rank = 0, ep_n = 1;
+    // sharded expert memory under expert parallelism: the resident routed experts are
+    // [ep_e0, ep_e0 + ep_ne) of every layer (ep_ne = 0: all of them)
+    int ep_e0 = 0, ep_ne = 0;
     ncclComm_t ep_comm = nullptr;
     int ep_timeout_ms = 60000;  // a host wait on an expert-parallel step longer than this aborts the exchange
     bool ep_aborted = false;
@@ -1736,6 +1739,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.g_chunk_r0 = ga.g_chunk_r0;
             a.g_nchunks = ga.g_nchunks;
             a.row_div = 1;  // received rows are indexed by their slot
+            a.expert_base = e->ep_e0;  // this rank's experts only are resident
             a.fn = e->ep_recv_rows.as<float>();
             a.act = e->ep_act.as<float>();
             a.dpart = e->ep_dpart.as<float>();
@@ -2533,6 +2537,25 @@ extern "C" int bt_engine_enable_ep(bt_engine *e, const void *unique_id, size_t n
     NK(api->GroupEnd());
     int wr = wait_stream(e);
     if (wr) return wr;
+    // keep only this rank's experts in HBM (stream.rs:1422-1429 slices an expert tensor the same
+    // way: expert e is bytes [e, e + 1) * size / n_expert): one layer at a time, so the extra
+    // memory is one layer's share
+    const int per = (int)(d.n_expert / (uint32_t)n_ranks), e0 = rank * per;
+    for (uint32_t il = 0; il < d.n_layer; il++) {
+        for (QMat *m : {&e->L[il].gate, &e->L[il].up, &e->L[il].down}) {
+            DevBuf nb;
+            CK(nb.alloc((size_t)per * m->mat_bytes));
+            CK(cudaMemcpyAsync(nb.p, m->buf.as<uint8_t>() + (size_t)e0 * m->mat_bytes, (size_t)per * m->mat_bytes,
+                               cudaMemcpyDeviceToDevice, e->st));
+            CK(cudaStreamSynchronize(e->st));
+            e->weight_bytes -= (uint64_t)(m->n_mats - per) * m->mat_bytes;
+            std::swap(m->buf, nb);
+            m->n_mats = per;
+        }
+    }
+    e->ep_e0 = e0;
+    e->ep_ne = per;
+    e->stats.weight_bytes = e->weight_bytes;
     e->mega = false;  // the expert phase crosses ranks: per-phase kernels
     for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
     e->graphs.clear();
@@ -2726,9 +2749,10 @@ extern "C" int bt_engine_tensor_bytes(const bt_engine *ec, const char *name, voi
         else if (s == "attn_k.weight") m = &l.k;
         else if (s == "attn_v.weight") m = &l.v;
         else if (s == "attn_output.weight") m = &l.o;
-        else if (s == "ffn_gate_exps.weight") m = &l.gate;
-        else if (s == "ffn_up_exps.weight") m = &l.up;
-        else if (s == "ffn_down_exps.weight") m = &l.down;
+        else if (s == "ffn_gate_exps.weight" || s == "ffn_up_exps.weight" || s == "ffn_down_exps.weight") {
+            if (e->ep_ne) return fail(BT_ERR_INVALID, "the engine holds only its own experts' share of " + n);
+            m = s == "ffn_gate_exps.weight" ? &l.gate : s == "ffn_up_exps.weight" ? &l.up : &l.down;
+        }
         else if (s == "ffn_gate_shexp.weight" && e->d.n_ff_shexp) m = &l.gate_sh;
         else if (s == "ffn_up_shexp.weight" && e->d.n_ff_shexp) m = &l.up_sh;
         else if (s == "ffn_down_shexp.weight" && e->d.n_ff_shexp) m = &l.down_sh;

@@ -94,6 +94,9 @@ struct ExpertArgs {
     // (slot_stride bytes each); slot_of = null when every expert is resident
     const int *slot_of;
     const uint8_t *pool;
+    // expert parallelism with sharded expert memory: the resident matrices are those of the
+    // experts [expert_base, expert_base + per), expert e at position e - expert_base
+    int expert_base;
     long long slot_stride;
     // the shared expert's output rows [T][E], added to the routed sum before the residual; or null
     const float *shexp;
@@ -101,15 +104,15 @@ struct ExpertArgs {
 
 // the weights of expert e: its resident matrices, or its slot of the expert cache
 __device__ __forceinline__ const uint8_t *expert_gate(const ExpertArgs &p, int e) {
-    return p.slot_of ? p.pool + (long long)p.slot_of[e] * p.slot_stride : p.gate + e * p.g_expert_bytes;
+    return p.slot_of ? p.pool + (long long)p.slot_of[e] * p.slot_stride : p.gate + (e - p.expert_base) * p.g_expert_bytes;
 }
 __device__ __forceinline__ const uint8_t *expert_up(const ExpertArgs &p, int e) {
     return p.slot_of ? p.pool + (long long)p.slot_of[e] * p.slot_stride + p.g_expert_bytes
-                     : p.up + e * p.u_expert_bytes;
+                     : p.up + (e - p.expert_base) * p.u_expert_bytes;
 }
 __device__ __forceinline__ const uint8_t *expert_down(const ExpertArgs &p, int e) {
     return p.slot_of ? p.pool + (long long)p.slot_of[e] * p.slot_stride + p.g_expert_bytes + p.u_expert_bytes
-                     : p.down + e * p.d_expert_bytes;
+                     : p.down + (e - p.expert_base) * p.d_expert_bytes;
 }
 
 // Expert-parallel dispatch: the rows of every (token, slot) pair, packed for the rank that owns

@@ -68,8 +68,11 @@ def main():
     cfg = bt.config("tiny", max_positions=2048)
     engine = bt.Engine(cfg, bt.synth_model(cfg, seed=7), device=local)
     engine.set_option("ep_timeout_ms", 30000)
+    before = engine.stats()["weight_bytes"]
     engine.enable_ep_torch()
+    after = engine.stats()["weight_bytes"]
     res = rank_workload(bt, engine, cfg, rank)
+    res["weight_bytes"] = np.array([before, after], np.int64)
     np.savez(os.path.join(args.out, f"rank{rank}.npz"), **res)
     engine.close()
     dist.barrier()

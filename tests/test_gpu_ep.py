@@ -1,6 +1,7 @@
 """Expert parallelism on 2 or more GPUs: every rank's logits, greedy tokens and KV bytes equal a
 single-GPU engine's on the same workload, bit for bit (the expert FFN of each (token, slot)
-row runs on the rank owning the expert and comes back in the reference's summation order).
+row runs on the rank owning the expert and comes back in the reference's summation order), and
+every rank holds only its own 1/n of the routed experts' weights in HBM.
 
 Runs the ranks as child processes (tests/ep_worker.py under torchrun, bounded by `timeout`);
 skipped with fewer than two GPUs."""
@@ -51,4 +52,9 @@ def test_expert_parallel_matches_single_gpu(tmp_path, n):
             assert np.array_equal(bits(got[key]), bits(want[key])), (rank, key)
         assert np.array_equal(got["greedy"], want["greedy"]), rank
         assert np.array_equal(got["kv_k"], want["kv_k"]) and np.array_equal(got["kv_v"], want["kv_v"]), rank
+        # each rank keeps only its 1/n of the routed experts in HBM
+        before, after = (int(x) for x in got["weight_bytes"])
+        expert = sum(bt.gguf.tensor_nbytes(ty, int(np.prod(ne))) for name, ty, ne, _ in cfg.tensor_specs()
+                     if name.endswith("_exps.weight"))
+        assert before - after == expert - expert // n, (rank, before, after, expert)
     engine.close()
