@@ -10,10 +10,15 @@ of uniform-random token ids into the f16 paged KV cache. A step = one decode tok
   e2e        tok/s through bt_forward with host token in / host logits out every step
   roofline   the expert FFN (gate/up + down kernels) against the measured HBM copy peak
   cpu_baseline  the CPU oracle decoding from the same weights and cache on the host cores
-  expert_cache  experts moved to pinned host memory behind a 6.26 GiB HBM cache (the cfg4
-             ratio), a fresh sequence: 128-token prefill then 128 batch-1 decode steps of
-             seeded uniform ids with the router bias; LRU and frequency-gated admission, each
-             from a cold cache: decode tok/s and hit rate
+  parity     the first measured decode step's logits against the CPU oracle from the same
+             weights and cache, bit for bit (a mismatch fails the run)
+  expert_gemv  the routed experts' kernels alone, every layer in turn (bt_bench_experts), at
+             batch 1 and at the batched leg's batch: HBM GB/s of the distinct expert weights
+  expert_cache  experts moved to pinned host memory behind an HBM cache, a fresh sequence:
+             128-token prefill then 128 batch-1 decode steps of seeded uniform ids; LRU and
+             frequency-gated admission, each from a cold cache: decode tok/s and hit rate, for
+             the log-Zipf router bias at the cfg4 ratio of cache to experts (6.26 GiB), the same
+             bias with a third of that cache, and no bias at 6.26 GiB
   batched    64 concurrent sequences, contexts seeded uniform in [512, 16384], paged f16 KV
              with seeded contents, a log-Zipf(1.1) router bias per layer (expert popularity
              over a seeded rank permutation); device tok/s of K graph-replayed steps
@@ -21,8 +26,9 @@ of uniform-random token ids into the f16 paged KV cache. A step = one decode tok
 N>1 (torchrun): replicas -- every rank runs the same batch-1 decode on its own GPU (weak
 scaling; no collective on the batch-1 path); rank 0 reports the sum of tok/s with the step
 time taken as the max over ranks. The batched workload then runs expert parallel: each rank
-holds its own batch of sequences and computes 1/N of the experts for every rank's tokens, the
-rows exchanged over NCCL (weak scaling: global batch = N x batch).
+holds its own batch of sequences and keeps only 1/N of the experts in HBM, computing them for
+every rank's tokens, the rows exchanged over NCCL (weak scaling: global batch = N x batch);
+rank 0 checks one expert-parallel step against a one-GPU engine holding every expert.
 
 --impl reference: the reference's CPU implementation of the path is not buildable here (Rust,
 no toolchain; ggml absent), so this arm times the CPU oracle restatement (`kind: "port"`) on
@@ -287,6 +293,22 @@ def run_ours(args, rank, world, local_rank):
     gu_bytes, dn_bytes = expert_bytes(cfg)
     persistent = "decode_step" in prof
 
+    # the routed experts' kernels alone (bt_bench_experts): every layer in turn, a seeded selection
+    # of K distinct experts per token, at batch 1 (1.02 GB of distinct expert weights a pass over
+    # the 48 layers) and at the batched leg's batch; HBM GB/s of the distinct weights read
+    expert_gemv = None
+    if args.expert_iters:
+        peak_gbs, _ = peaks()
+        expert_gemv = {"what": "the routed experts' gate/up and down kernels alone, every layer in turn (one CUDA "
+                               "graph), seeded selections of K distinct experts per token; bytes = the distinct "
+                               "selected experts' weights of a pass", "peak_gbs": peak_gbs}
+        for T in sorted({1, args.batch2 or 64}):
+            ms_x, nb_x = engine.bench_experts(T, n_iters=args.expert_iters, seed=args.seed)
+            gbs = nb_x / (ms_x / 1e3) / 1e9
+            expert_gemv[f"batch{T}"] = {"ms_per_pass": round(ms_x, 4), "gb_per_pass": round(nb_x / 1e9, 3),
+                                        "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak_gbs, 4),
+                                        "path": "per-token kernels" if T <= 8 else "grouped kernels (tcgen05 gate/up)"}
+
     # the batched workload: batch2 concurrent sequences, per-sequence contexts seeded uniform in
     # [ctx2_min, ctx2_max], paged f16 KV
     batched = None
@@ -301,20 +323,49 @@ def run_ours(args, rank, world, local_rank):
         # random buffer per layer, its prefixes shared by the sequences
         kw = cfg.n_head_kv * cfg.head_dim
         cmax = int(ctxs.max())
+        # N > 1: rank 0 also builds a one-GPU engine with every expert resident and the first NREF
+        # sequences' caches, to check the expert-parallel step's logits against it
+        NREF = min(4, B)
+        ref_engine = ref_cache = None
+        if world > 1 and rank == 0 and args.ep_check:
+            ref_engine = bt.Engine.synthetic(cfg, seed=args.seed, device=local_rank)
+            ref_cache = bt.KvCache(ref_engine, max_positions=int(ctxs[:NREF].max()) + 8, max_seqs=NREF)
         for il in range(cfg.n_layer):
             k = rng2.standard_normal(cmax * kw).astype(np.float16)
             v = rng2.standard_normal(cmax * kw).astype(np.float16)
             for sq, c in enumerate(ctxs):
                 cache2.restore_layer(il, k[:int(c) * kw], v[:int(c) * kw], seq=sq)
+                if ref_cache is not None and sq < NREF:
+                    ref_cache.restore_layer(il, k[:int(c) * kw], v[:int(c) * kw], seq=sq)
         for sq, c in enumerate(ctxs):
             cache2.set_positions(int(c), sq)
+            if ref_cache is not None and sq < NREF:
+                ref_cache.set_positions(int(c), sq)
         first2 = rng2.integers(0, cfg.n_vocab, B)
         if args.zipf > 0:  # skewed routing: a log-Zipf router bias per layer
             for il in range(cfg.n_layer):
-                engine.set_router_bias(il, bt.models.zipf_router_bias(cfg.n_expert, il, args.seed, args.zipf))
+                bias = bt.models.zipf_router_bias(cfg.n_expert, il, args.seed, args.zipf)
+                engine.set_router_bias(il, bias)
+                if ref_engine is not None:
+                    ref_engine.set_router_bias(il, bias)
+        ep_parity = None
         if world > 1:
             # expert parallelism: each rank computes NE/world experts for every rank's tokens
             engine.enable_ep_torch()
+            # one single-token step of every sequence (a collective: every rank runs it); rank 0
+            # compares its first NREF sequences with the one-GPU engine
+            lg_ep = runner.forward_batch(cache2, list(range(B)), [[int(t)] for t in first2], [int(c) for c in ctxs])
+            if ref_engine is not None:
+                lg_ref = bt.StreamingRunner(ref_engine).forward_batch(
+                    ref_cache, list(range(NREF)), [[int(t)] for t in first2[:NREF]], [int(c) for c in ctxs[:NREF]])
+                same = bool(np.array_equal(lg_ep[:NREF].view(np.uint32), lg_ref.view(np.uint32)))
+                ep_parity = {"status": "bit-exact" if same else "MISMATCH",
+                             "max_abs": float(np.abs(lg_ep[:NREF] - lg_ref).max()),
+                             "what": f"rank 0's first {NREF} sequences: logits of one expert-parallel step against "
+                                     "a one-GPU engine holding every expert"}
+                ref_cache.close()
+                ref_engine.close()
+            first2 = np.argmax(lg_ep, axis=1)
         runner.generate_greedy(cache2, first2, args.warmup)
         sync_ranks(world)
         runner.generate_greedy(cache2, first2, args.steps)
@@ -332,8 +383,9 @@ def run_ours(args, rank, world, local_rank):
                    "distinct_experts_per_layer": round(float(np.mean(distinct)), 1),
                    "path": "per-phase kernels (single-token steps of more than 4 sequences)",
                    "parallelism": (f"expert parallel over {world} GPUs: {B} sequences per rank, experts split "
-                                   f"{cfg.n_expert // world} per rank, rows exchanged by NCCL send/recv"
-                                   if world > 1 else "single GPU")}
+                                   f"{cfg.n_expert // world} per rank (only those resident in each GPU's HBM), "
+                                   f"rows exchanged by NCCL send/recv" if world > 1 else "single GPU"),
+                   "comm_nranks": world, "ep_parity": ep_parity}
         cache2.close()
 
     # per-phase kernels: the expert kernels' times; the persistent step: its gate/up and down
@@ -392,46 +444,76 @@ def run_ours(args, rank, world, local_rank):
                      "achieved_gbs": round(bpt_all / (ms / args.steps / 1e3) / 1e9, 1),
                      "frac": round(bpt_all / (ms / args.steps / 1e3) / 1e9 / peak, 4)},
             "kernels_us": kernel_table,
+            "expert_gemv": expert_gemv,
             "batched": batched,
             "expert_cache": None,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
     # the out-of-HBM case at this model's scale: experts in pinned host memory behind an HBM
-    # cache of args.xcache_gib, batch-1 greedy decode with the log-Zipf router bias, each policy
-    # from a cold cache
+    # cache, batch-1 greedy decode, each policy from a cold cache, in three workloads: the
+    # log-Zipf router bias with the cfg4 ratio of cache to experts (args.xcache_gib; the biased
+    # working set about fits), the same bias with a cache a third that size, and no bias at the
+    # cfg4 ratio (every expert in use: the working set is three times the cache)
     if args.xcache_gib > 0 and world == 1:
-        if args.zipf > 0 and not args.batch2:
-            for il in range(cfg.n_layer):
-                engine.set_router_bias(il, bt.models.zipf_router_bias(cfg.n_expert, il, args.seed, args.zipf))
-        xcache = {"cache_bytes": int(args.xcache_gib * (1 << 30)), "steps": args.xcache_steps, "batch": 1,
+        xcache = {"steps": args.xcache_steps, "batch": 1,
                   "experts_bytes": int(cfg.n_layer * cfg.n_expert * expert_bytes(cfg, per_expert=True)),
-                  "routing": f"log-Zipf({args.zipf}) router bias per layer" if args.zipf > 0 else "unbiased"}
+                  "timing": (f"decode steps after a {args.xcache_prompt}-token prefill of seeded uniform ids: wall "
+                             "clock of bt_forward per token (host token in, logits out, one host round trip per "
+                             "layer for the cache decisions); hit rate over the decode steps")}
+        rngx = np.random.default_rng(args.seed + 3)
+        prompt_x = rngx.integers(0, cfg.n_vocab, args.xcache_prompt)
+        toks_x = rngx.integers(0, cfg.n_vocab, args.xcache_steps)
+        cases = [("zipf", args.xcache_gib), ("zipf_small_cache", args.xcache_gib / 3), ("unbiased", args.xcache_gib),
+                 ("zipf_trace", args.xcache_gib)]
+        zs = args.zipf if args.zipf > 0 else 1.1
         try:
-            rngx = np.random.default_rng(args.seed + 3)
-            prompt_x = rngx.integers(0, cfg.n_vocab, args.xcache_prompt)
-            toks_x = rngx.integers(0, cfg.n_vocab, args.xcache_steps)
-            for policy in ("lru", "freq"):
-                engine.enable_expert_cache(xcache["cache_bytes"], policy)
-                cache_x = bt.KvCache(engine, max_positions=args.xcache_prompt + args.xcache_steps + 8)
-                runner.forward_cached(cache_x, prompt_x, 0)  # prefill: warms the cache
-                st0 = engine.expert_cache_stats()
-                t0 = time.perf_counter()
-                for tk in toks_x:  # one token a step, seeded uniform ids
-                    runner.forward_cached(cache_x, [int(tk)], cache_x.len())
-                wall = time.perf_counter() - t0
-                st = engine.expert_cache_stats()
-                cache_x.close()
-                d = {k: st[k] - st0[k] for k in ("hits", "misses", "evictions", "bypasses", "bytes_copied")}
-                xcache[policy] = {"tok_s": round(args.xcache_steps / wall, 2),
-                                  "hit_rate": round(d["hits"] / max(d["hits"] + d["misses"], 1), 4),
-                                  "evictions": d["evictions"], "bypasses": d["bypasses"],
-                                  "gb_copied": round(d["bytes_copied"] / 1e9, 2), "wall_s": round(wall, 2),
-                                  "prefill_hit_rate": round(st0["hit_rate"], 4)}
-                xcache["slots"] = st["capacity_slots"]
-            xcache["timing"] = (f"decode steps after a {args.xcache_prompt}-token prefill of seeded uniform ids: "
-                                "wall clock of bt_forward per token (host token in, logits out, one host round "
-                                "trip per layer for the cache decisions); hit rate over the decode steps")
+            for name, gib in cases:
+                biased = name.startswith("zipf") and name != "zipf_trace" and args.zipf > 0
+                for il in range(cfg.n_layer):
+                    engine.set_router_bias(il, bt.models.zipf_router_bias(cfg.n_expert, il, args.seed, args.zipf)
+                                           if biased else None)
+                case = {"cache_bytes": int(gib * (1 << 30)),
+                        "routing": (f"log-Zipf({args.zipf}) router bias per layer" if biased else
+                                    f"a routing trace: each decode step's K experts per layer drawn from Zipf({zs}) "
+                                    "over a seeded per-layer rank permutation, forced by a router bias (+30 on the "
+                                    "drawn experts)" if name == "zipf_trace" else "unbiased")}
+                trace = None
+                if name == "zipf_trace":  # per step and layer, K distinct experts drawn from Zipf(zs)
+                    rt = np.random.default_rng(args.seed + 4)
+                    K_, NE_ = cfg.n_expert_used, cfg.n_expert
+                    pz = np.arange(1, NE_ + 1, dtype=np.float64) ** -zs
+                    pz /= pz.sum()
+                    perms = [np.random.default_rng([args.seed, il, 0x2F1B]).permutation(NE_) for il in range(cfg.n_layer)]
+                    trace = [[perms[il][rt.choice(NE_, K_, replace=False, p=pz)] for il in range(cfg.n_layer)]
+                             for _ in range(args.xcache_steps)]
+                for policy in ("lru", "freq"):
+                    engine.enable_expert_cache(case["cache_bytes"], policy)
+                    cache_x = bt.KvCache(engine, max_positions=args.xcache_prompt + args.xcache_steps + 8)
+                    runner.forward_cached(cache_x, prompt_x, 0)  # prefill: warms the cache
+                    st0 = engine.expert_cache_stats()
+                    t0 = time.perf_counter()
+                    wall_bias = 0.0
+                    for si, tk in enumerate(toks_x):  # one token a step, seeded uniform ids
+                        if trace is not None:
+                            tb = time.perf_counter()
+                            for il in range(cfg.n_layer):
+                                b = np.zeros(cfg.n_expert, np.float32)
+                                b[trace[si][il]] = 30.0
+                                engine.set_router_bias(il, b)
+                            wall_bias += time.perf_counter() - tb
+                        runner.forward_cached(cache_x, [int(tk)], cache_x.len())
+                    wall = time.perf_counter() - t0 - wall_bias
+                    st = engine.expert_cache_stats()
+                    cache_x.close()
+                    d = {k: st[k] - st0[k] for k in ("hits", "misses", "evictions", "bypasses", "bytes_copied")}
+                    case[policy] = {"tok_s": round(args.xcache_steps / wall, 2),
+                                    "hit_rate": round(d["hits"] / max(d["hits"] + d["misses"], 1), 4),
+                                    "evictions": d["evictions"], "bypasses": d["bypasses"],
+                                    "gb_copied": round(d["bytes_copied"] / 1e9, 2), "wall_s": round(wall, 2),
+                                    "prefill_hit_rate": round(st0["hit_rate"], 4)}
+                    case["slots"] = st["capacity_slots"]
+                xcache[name] = case
         except bt.BtError as err:  # e.g. pinned host memory refused
             xcache["unavailable"] = str(err)
     if result is not None:
@@ -538,6 +620,10 @@ def main():
                     help="HBM expert-cache size of the out-of-HBM leg (0 skips it); the default keeps the "
                          "cfg4 ratio of cache to experts (120 GB of ~311 GB)")
     ap.add_argument("--xcache-steps", type=int, default=128)
+    ap.add_argument("--expert-iters", type=int, default=20, help="passes of the isolated expert-kernel timing "
+                    "(0 skips it)")
+    ap.add_argument("--ep-check", type=int, default=1, help="N > 1: rank 0 checks one expert-parallel step against a "
+                    "one-GPU engine (needs the model twice in rank 0's HBM)")
     ap.add_argument("--xcache-prompt", type=int, default=128)
     ap.add_argument("--zipf", type=float, default=1.1, help="router-bias Zipf exponent of the batched workload "
                     "(0: unbiased)")
@@ -568,6 +654,9 @@ def main():
         print(json.dumps(out), flush=True)
         if out.get("parity", {}).get("status") == "MISMATCH":
             print("bench: the measured step's logits differ from the CPU oracle's", file=sys.stderr)
+            sys.exit(3)
+        if ((out.get("batched") or {}).get("ep_parity") or {}).get("status") == "MISMATCH":
+            print("bench: the expert-parallel step's logits differ from the one-GPU engine's", file=sys.stderr)
             sys.exit(3)
 
 

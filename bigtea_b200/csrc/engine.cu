@@ -11,6 +11,7 @@
 #include <nccl.h>  // types of the NCCL calls; the library itself is opened at run time
 #include <string.h>
 
+#include <algorithm>
 #include <chrono>
 #include <map>
 #include <memory>
@@ -1474,6 +1475,172 @@ static bool use_gateup_mma(const bt_engine *e, const Layer &l, size_t rows) {
            gateup_mma_smem_bytes((int)e->d.n_embd) <= (size_t)max_dynamic_smem() && rows <= e->q8_rows;
 }
 
+// The routed experts of layer il for the T tokens of a step, on one GPU: the grouped kernels
+// (T > MAX_T: each selected expert's weights once per step) or the per-token ones. Each token's
+// selection comes from sel_ids / sel_w ([T][K], ascending ids) and its normalised row from e->fn;
+// the weighted expert sum plus e->ffn_in (and the shared expert's rows, when given) goes to e->x.
+static int launch_layer_experts(bt_engine *e, int il, int T, const int *sel_ids, const float *sel_w, const int *x_slot,
+                                const float *shexp, cudaStream_t st, bool pdl) {
+    const bt_model_desc &d = e->d;
+    const int E = d.n_embd, K = d.n_expert_used, F = d.n_ff_exp, NE = d.n_expert;
+    int *err = e->err.as<int>();
+    const Layer &l = e->L[il];
+    (void)F;
+    (void)NE;
+    if (T > MAX_T) {
+            GroupArgs ga{};
+            ga.sel_ids = sel_ids;
+            ga.T = T;
+            ga.K = K;
+            ga.NE = NE;
+            ga.g_count = e->g_count.as<int>();
+            ga.g_off = e->g_off.as<int>();
+            ga.g_list = e->g_list.as<int>();
+            ga.g_active = e->g_active.as<int>();
+            ga.g_nactive = e->g_nactive.as<int>();
+            ga.g_chunk_e = e->g_chunk_e.as<int>();
+            ga.g_chunk_r0 = e->g_chunk_r0.as<int>();
+            ga.g_nchunks = e->g_nchunks.as<int>();
+            timer_begin(e, "expert_group");
+            CK(launch_group(ga, st, pdl));
+            timer_end(e);
+            ExpertArgs a{};
+            a.gate = l.gate.buf.as<uint8_t>();
+            a.up = l.up.buf.as<uint8_t>();
+            a.down = l.down.buf.as<uint8_t>();
+            a.gtype = l.gate.type;
+            a.utype = l.up.type;
+            a.dtype = l.down.type;
+            a.g_nsb = l.gate.g.nsb;
+            a.g_rpt = l.gate.g.rpt;
+            a.g_S = l.gate.g.S;
+            a.g_tile_bytes = l.gate.g.tile_bytes;
+            a.g_n_tiles = (int)l.gate.g.n_tiles;
+            a.u_tile_bytes = l.up.g.tile_bytes;
+            a.g_expert_bytes = l.gate.mat_bytes;
+            a.u_expert_bytes = l.up.mat_bytes;
+            a.d_expert_bytes = l.down.mat_bytes;
+            a.d_nsb = l.down.g.nsb;
+            a.d_tile_bytes = l.down.g.tile_bytes;
+            a.E = E;
+            a.F = F;
+            a.K = K;
+            a.T = T;
+            a.workers = (int)d.expert_workers;
+            a.sel_ids = sel_ids;
+            a.sel_w = sel_w;
+            a.fn = e->fn.as<float>();
+            a.act = e->act.as<float>();
+            a.ffn_in = e->ffn_in.as<float>();
+            a.x_out = e->x.as<float>();
+            a.single = e->single.as<unsigned char>();
+            a.err = err;
+            a.g_count = ga.g_count;
+            a.g_off = ga.g_off;
+            a.g_list = ga.g_list;
+            a.g_active = ga.g_active;
+            a.g_nactive = ga.g_nactive;
+            a.g_chunk_e = ga.g_chunk_e;
+            a.g_chunk_r0 = ga.g_chunk_r0;
+            a.g_nchunks = ga.g_nchunks;
+            a.dpart = e->dpart.as<float>();
+            a.row_div = K;  // list entry t*K + k uses token t's row
+            a.slot_of = x_slot;
+            a.pool = e->x_pool.as<uint8_t>();
+            a.slot_stride = e->x_stride;
+            a.shexp = shexp;
+            const size_t cap = (size_t)max_dynamic_smem();
+            a.slot_bytes = a.g_tile_bytes + a.u_tile_bytes;
+            a.nst = 1;
+            a.nst = pick_nst_cap(a.slot_bytes, gateup_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
+            timer_begin(e, "expert_gateup");
+            if (use_gateup_mma(e, l, (size_t)T)) {
+                CK(stage_gateup_q8(e, a, T, st, pdl));
+                CK(launch_gateup_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, st, pdl));
+            }
+            else
+                CK(launch_gateup_grouped(a, e->n_sm, st, pdl));
+            timer_end(e);
+            a.slot_bytes = down_group_rows(a) * a.d_tile_bytes;
+            a.nst = 1;
+            a.nst = pick_nst_cap(a.slot_bytes, down_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
+            timer_begin(e, "expert_down");
+            CK(launch_down_grouped(a, e->n_sm, st, pdl));
+            timer_end(e);
+            timer_begin(e, "expert_combine");
+            CK(launch_down_combine(a, st, pdl));
+            timer_end(e);
+            }
+        for (int t0 = 0; T <= MAX_T && t0 < T; t0 += MAX_T) {
+            int tg = T - t0 < MAX_T ? T - t0 : MAX_T;
+            ExpertArgs a{};
+            a.gate = l.gate.buf.as<uint8_t>();
+            a.up = l.up.buf.as<uint8_t>();
+            a.down = l.down.buf.as<uint8_t>();
+            a.gtype = l.gate.type;
+            a.utype = l.up.type;
+            a.dtype = l.down.type;
+            a.g_nsb = l.gate.g.nsb;
+            a.g_rpt = l.gate.g.rpt;
+            a.g_S = l.gate.g.S;
+            a.g_tile_bytes = l.gate.g.tile_bytes;
+            a.g_n_tiles = (int)l.gate.g.n_tiles;
+            a.u_tile_bytes = l.up.g.tile_bytes;
+            a.g_expert_bytes = l.gate.mat_bytes;
+            a.u_expert_bytes = l.up.mat_bytes;
+            a.d_expert_bytes = l.down.mat_bytes;
+            a.d_nsb = l.down.g.nsb;
+            a.d_tile_bytes = l.down.g.tile_bytes;
+            a.E = E;
+            a.F = F;
+            a.K = K;
+            a.T = tg;
+            a.workers = (int)d.expert_workers;
+            a.sel_ids = sel_ids + (size_t)t0 * K;
+            a.sel_w = sel_w + (size_t)t0 * K;
+            a.fn = e->fn.as<float>() + (size_t)t0 * E;
+            a.act = e->act.as<float>() + (size_t)t0 * K * F;
+            a.ffn_in = e->ffn_in.as<float>() + (size_t)t0 * E;
+            a.x_out = e->x.as<float>() + (size_t)t0 * E;
+            a.single = e->single.as<unsigned char>() + t0;
+            a.err = err;
+            a.slot_of = x_slot;
+            a.pool = e->x_pool.as<uint8_t>();
+            a.slot_stride = e->x_stride;
+            a.shexp = shexp ? shexp + (size_t)t0 * E : nullptr;
+            if (e->prefetch && t0 == 0 && il + 1 < d.n_layer) {  // the next layer's q/k/v weights
+                const Layer &n = e->L[il + 1];
+                a.pf.ptr[0] = n.q.buf.p;
+                a.pf.bytes[0] = n.q.buf.n;
+                a.pf.ptr[1] = n.k.buf.p;
+                a.pf.bytes[1] = n.k.buf.n;
+                a.pf.ptr[2] = n.v.buf.p;
+                a.pf.bytes[2] = n.v.buf.n;
+                a.pf.n = 3;
+            } else if (e->prefetch && t0 == 0) {  // the output head
+                a.pf.ptr[0] = e->out.buf.p;
+                a.pf.bytes[0] = e->out.buf.n < (64ull << 20) ? e->out.buf.n : (64ull << 20);
+                a.pf.n = 1;
+            }
+            a.prefetch_down = e->prefetch ? 1 : 0;
+            a.slot_bytes = a.g_tile_bytes + a.u_tile_bytes;
+            a.nst = 1;
+            a.nst = pick_nst(a.slot_bytes, gateup_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes);
+            timer_begin(e, "expert_gateup");
+            CK(launch_gateup(a, grid_for(e, (long long)tg * K * a.g_n_tiles), st, pdl));
+            timer_end(e);
+            a.slot_bytes = K * a.d_tile_bytes;
+            a.nst = 1;
+            a.nst = pick_nst(a.slot_bytes, down_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes);
+            a.pf = PrefetchSpec{};
+            a.prefetch_down = 0;
+            timer_begin(e, "expert_down");
+            CK(launch_down(a, grid_for(e, (long long)tg * E), st, pdl));
+            timer_end(e);
+        }
+    return BT_OK;
+}
+
 static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) {
     if (e->ep_aborted) return fail(BT_ERR_TIMEOUT, "the expert-parallel communicator was aborted by an earlier failure");
     if (step_eligible(e, kv, p)) return launch_persistent_step(e, kv, p, greedy);
@@ -1782,156 +1949,9 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             timer_begin(e, "expert_combine");
             CK(launch_down_combine(a, st, false));
             timer_end(e);
-        } else if (T > MAX_T) {  // grouped: each selected expert's weights once per step
-            GroupArgs ga{};
-            ga.sel_ids = e->sel_ids.as<int>();
-            ga.T = T;
-            ga.K = K;
-            ga.NE = NE;
-            ga.g_count = e->g_count.as<int>();
-            ga.g_off = e->g_off.as<int>();
-            ga.g_list = e->g_list.as<int>();
-            ga.g_active = e->g_active.as<int>();
-            ga.g_nactive = e->g_nactive.as<int>();
-            ga.g_chunk_e = e->g_chunk_e.as<int>();
-            ga.g_chunk_r0 = e->g_chunk_r0.as<int>();
-            ga.g_nchunks = e->g_nchunks.as<int>();
-            timer_begin(e, "expert_group");
-            CK(launch_group(ga, st, pdl));
-            timer_end(e);
-            ExpertArgs a{};
-            a.gate = l.gate.buf.as<uint8_t>();
-            a.up = l.up.buf.as<uint8_t>();
-            a.down = l.down.buf.as<uint8_t>();
-            a.gtype = l.gate.type;
-            a.utype = l.up.type;
-            a.dtype = l.down.type;
-            a.g_nsb = l.gate.g.nsb;
-            a.g_rpt = l.gate.g.rpt;
-            a.g_S = l.gate.g.S;
-            a.g_tile_bytes = l.gate.g.tile_bytes;
-            a.g_n_tiles = (int)l.gate.g.n_tiles;
-            a.u_tile_bytes = l.up.g.tile_bytes;
-            a.g_expert_bytes = l.gate.mat_bytes;
-            a.u_expert_bytes = l.up.mat_bytes;
-            a.d_expert_bytes = l.down.mat_bytes;
-            a.d_nsb = l.down.g.nsb;
-            a.d_tile_bytes = l.down.g.tile_bytes;
-            a.E = E;
-            a.F = F;
-            a.K = K;
-            a.T = T;
-            a.workers = (int)d.expert_workers;
-            a.sel_ids = e->sel_ids.as<int>();
-            a.sel_w = e->sel_w.as<float>();
-            a.fn = e->fn.as<float>();
-            a.act = e->act.as<float>();
-            a.ffn_in = e->ffn_in.as<float>();
-            a.x_out = e->x.as<float>();
-            a.single = e->single.as<unsigned char>();
-            a.err = err;
-            a.g_count = ga.g_count;
-            a.g_off = ga.g_off;
-            a.g_list = ga.g_list;
-            a.g_active = ga.g_active;
-            a.g_nactive = ga.g_nactive;
-            a.g_chunk_e = ga.g_chunk_e;
-            a.g_chunk_r0 = ga.g_chunk_r0;
-            a.g_nchunks = ga.g_nchunks;
-            a.dpart = e->dpart.as<float>();
-            a.row_div = K;  // list entry t*K + k uses token t's row
-            a.slot_of = x_slot;
-            a.pool = e->x_pool.as<uint8_t>();
-            a.slot_stride = e->x_stride;
-            a.shexp = shexp;
-            const size_t cap = (size_t)max_dynamic_smem();
-            a.slot_bytes = a.g_tile_bytes + a.u_tile_bytes;
-            a.nst = 1;
-            a.nst = pick_nst_cap(a.slot_bytes, gateup_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
-            timer_begin(e, "expert_gateup");
-            if (use_gateup_mma(e, l, (size_t)T)) {
-                CK(stage_gateup_q8(e, a, T, st, pdl));
-                CK(launch_gateup_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, st, pdl));
-            }
-            else
-                CK(launch_gateup_grouped(a, e->n_sm, st, pdl));
-            timer_end(e);
-            a.slot_bytes = down_group_rows(a) * a.d_tile_bytes;
-            a.nst = 1;
-            a.nst = pick_nst_cap(a.slot_bytes, down_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
-            timer_begin(e, "expert_down");
-            CK(launch_down_grouped(a, e->n_sm, st, pdl));
-            timer_end(e);
-            timer_begin(e, "expert_combine");
-            CK(launch_down_combine(a, st, pdl));
-            timer_end(e);
-        }
-        for (int t0 = 0; !e->ep && T <= MAX_T && t0 < T; t0 += MAX_T) {
-            int tg = T - t0 < MAX_T ? T - t0 : MAX_T;
-            ExpertArgs a{};
-            a.gate = l.gate.buf.as<uint8_t>();
-            a.up = l.up.buf.as<uint8_t>();
-            a.down = l.down.buf.as<uint8_t>();
-            a.gtype = l.gate.type;
-            a.utype = l.up.type;
-            a.dtype = l.down.type;
-            a.g_nsb = l.gate.g.nsb;
-            a.g_rpt = l.gate.g.rpt;
-            a.g_S = l.gate.g.S;
-            a.g_tile_bytes = l.gate.g.tile_bytes;
-            a.g_n_tiles = (int)l.gate.g.n_tiles;
-            a.u_tile_bytes = l.up.g.tile_bytes;
-            a.g_expert_bytes = l.gate.mat_bytes;
-            a.u_expert_bytes = l.up.mat_bytes;
-            a.d_expert_bytes = l.down.mat_bytes;
-            a.d_nsb = l.down.g.nsb;
-            a.d_tile_bytes = l.down.g.tile_bytes;
-            a.E = E;
-            a.F = F;
-            a.K = K;
-            a.T = tg;
-            a.workers = (int)d.expert_workers;
-            a.sel_ids = e->sel_ids.as<int>() + (size_t)t0 * K;
-            a.sel_w = e->sel_w.as<float>() + (size_t)t0 * K;
-            a.fn = e->fn.as<float>() + (size_t)t0 * E;
-            a.act = e->act.as<float>() + (size_t)t0 * K * F;
-            a.ffn_in = e->ffn_in.as<float>() + (size_t)t0 * E;
-            a.x_out = e->x.as<float>() + (size_t)t0 * E;
-            a.single = e->single.as<unsigned char>() + t0;
-            a.err = err;
-            a.slot_of = x_slot;
-            a.pool = e->x_pool.as<uint8_t>();
-            a.slot_stride = e->x_stride;
-            a.shexp = shexp ? shexp + (size_t)t0 * E : nullptr;
-            if (e->prefetch && t0 == 0 && il + 1 < d.n_layer) {  // the next layer's q/k/v weights
-                const Layer &n = e->L[il + 1];
-                a.pf.ptr[0] = n.q.buf.p;
-                a.pf.bytes[0] = n.q.buf.n;
-                a.pf.ptr[1] = n.k.buf.p;
-                a.pf.bytes[1] = n.k.buf.n;
-                a.pf.ptr[2] = n.v.buf.p;
-                a.pf.bytes[2] = n.v.buf.n;
-                a.pf.n = 3;
-            } else if (e->prefetch && t0 == 0) {  // the output head
-                a.pf.ptr[0] = e->out.buf.p;
-                a.pf.bytes[0] = e->out.buf.n < (64ull << 20) ? e->out.buf.n : (64ull << 20);
-                a.pf.n = 1;
-            }
-            a.prefetch_down = e->prefetch ? 1 : 0;
-            a.slot_bytes = a.g_tile_bytes + a.u_tile_bytes;
-            a.nst = 1;
-            a.nst = pick_nst(a.slot_bytes, gateup_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes);
-            timer_begin(e, "expert_gateup");
-            CK(launch_gateup(a, grid_for(e, (long long)tg * K * a.g_n_tiles), st, pdl));
-            timer_end(e);
-            a.slot_bytes = K * a.d_tile_bytes;
-            a.nst = 1;
-            a.nst = pick_nst(a.slot_bytes, down_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes);
-            a.pf = PrefetchSpec{};
-            a.prefetch_down = 0;
-            timer_begin(e, "expert_down");
-            CK(launch_down(a, grid_for(e, (long long)tg * E), st, pdl));
-            timer_end(e);
+        } else {
+            int r_ = launch_layer_experts(e, il, T, e->sel_ids.as<int>(), e->sel_w.as<float>(), x_slot, shexp, st, pdl);
+            if (r_) return r_;
         }
     }
     const int n_out = (int)p.x_rows.size();
@@ -2202,6 +2222,103 @@ extern "C" int bt_generate_greedy(bt_engine *e, bt_kv *kv, const uint32_t *seq_i
     e->stats.forward_calls++;
     e->stats.forward_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
     return r;
+}
+
+// ------------------------------------------------------------------ isolated expert-FFN timing
+// The routed experts' kernels alone, layer after layer over the whole model: T tokens a layer
+// with a seeded selection of K distinct experts per token (ascending ids, random positive
+// weights summing to 1) and seeded activation rows, through launch_layer_experts -- the kernels a
+// decode step of T single tokens runs. Captured once as a CUDA graph of every layer, replayed
+// once to warm up, then n_iters times between CUDA events.
+extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint64_t seed, double *ms_per_pass,
+                                uint64_t *bytes_per_pass) {
+    if (!e || !ms_per_pass || !bytes_per_pass) return fail(BT_ERR_INVALID, "null argument");
+    if (e->ep || e->xcache) return fail(BT_ERR_UNSUPPORTED, "the expert timing needs every expert resident on one GPU");
+    if (T == 0 || (int)T > e->TB || n_iters == 0) return fail(BT_ERR_INVALID, "T must be 1..the step capacity, n_iters >= 1");
+    CK(cudaSetDevice(e->device));
+    const bt_model_desc &d = e->d;
+    const int L = (int)d.n_layer, K = (int)d.n_expert_used, NE = (int)d.n_expert, E = (int)d.n_embd;
+    uint64_t st = seed ^ 0x5DEECE66Dull;
+    auto next = [&st]() {  // splitmix64
+        uint64_t z = (st += 0x9E3779B97F4A7C15ull);
+        z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+        z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+        return z ^ (z >> 31);
+    };
+    std::vector<int> sel((size_t)L * T * K);
+    std::vector<float> w((size_t)L * T * K), fn((size_t)T * E);
+    uint64_t bytes = 0;
+    std::vector<int> perm(NE);
+    for (int il = 0; il < L; il++) {
+        std::vector<char> used(NE, 0);
+        for (uint32_t t = 0; t < T; t++) {
+            for (int i = 0; i < NE; i++) perm[i] = i;
+            for (int k = 0; k < K; k++) {  // partial Fisher-Yates: K distinct experts
+                const int j = k + (int)(next() % (uint64_t)(NE - k));
+                std::swap(perm[k], perm[j]);
+            }
+            std::sort(perm.begin(), perm.begin() + K);
+            float tot = 0.0f;
+            for (int k = 0; k < K; k++) {
+                const size_t o = ((size_t)il * T + t) * K + k;
+                sel[o] = perm[k];
+                used[perm[k]] = 1;
+                w[o] = 0.05f + (float)(next() >> 40) / (float)(1ull << 24);
+                tot += w[o];
+            }
+            for (int k = 0; k < K; k++) w[((size_t)il * T + t) * K + k] /= tot;
+        }
+        const Layer &l = e->L[il];
+        for (int x = 0; x < NE; x++)
+            if (used[x]) bytes += (uint64_t)(l.gate.mat_bytes + l.up.mat_bytes + l.down.mat_bytes);
+    }
+    for (auto &v : fn) v = (float)((int64_t)(next() >> 40) - (1ll << 23)) / (float)(1ll << 23);
+    DevBuf dsel, dw;
+    CK(dsel.alloc(sel.size() * 4));
+    CK(dw.alloc(w.size() * 4));
+    CK(cudaMemcpyAsync(dsel.p, sel.data(), sel.size() * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(dw.p, w.data(), w.size() * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemcpyAsync(e->fn.p, fn.data(), fn.size() * 4, cudaMemcpyHostToDevice, e->st));
+    CK(cudaMemsetAsync(e->ffn_in.p, 0, (size_t)T * E * 4, e->st));
+    CK(cudaMemsetAsync(e->single.p, 1, T, e->st));
+    CK(cudaStreamSynchronize(e->st));
+    const bool timing = e->timing;
+    e->timing = false;
+    cudaGraph_t g = nullptr;
+    cudaGraphExec_t ge = nullptr;
+    CK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
+    int r = BT_OK;
+    for (int il = 0; il < L && r == BT_OK; il++)
+        r = launch_layer_experts(e, il, (int)T, dsel.as<int>() + (size_t)il * T * K, dw.as<float>() + (size_t)il * T * K,
+                                 nullptr, nullptr, e->st, e->pdl);
+    cudaError_t ce = cudaStreamEndCapture(e->st, &g);
+    e->timing = timing;
+    if (r) {
+        if (g) cudaGraphDestroy(g);
+        return r;
+    }
+    CK(ce);
+    ce = cudaGraphInstantiate(&ge, g, 0);
+    cudaGraphDestroy(g);
+    CK(ce);
+    cudaEvent_t e0, e1;
+    CK(cudaEventCreate(&e0));
+    CK(cudaEventCreate(&e1));
+    ce = cudaGraphLaunch(ge, e->st);
+    if (ce == cudaSuccess) ce = cudaEventRecord(e0, e->st);
+    for (uint32_t i = 0; i < n_iters && ce == cudaSuccess; i++) ce = cudaGraphLaunch(ge, e->st);
+    if (ce == cudaSuccess) ce = cudaEventRecord(e1, e->st);
+    if (ce == cudaSuccess) ce = cudaEventSynchronize(e1);
+    float ms = 0.0f;
+    if (ce == cudaSuccess) ce = cudaEventElapsedTime(&ms, e0, e1);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cudaGraphExecDestroy(ge);
+    CK(ce);
+    if ((r = check_err(e))) return r;
+    *ms_per_pass = (double)ms / n_iters;
+    *bytes_per_pass = bytes;
+    return BT_OK;
 }
 
 extern "C" int bt_last_device_ms(const bt_engine *e, double *ms) {

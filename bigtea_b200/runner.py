@@ -92,6 +92,13 @@ class Engine:
         b = np.ascontiguousarray(bias, dtype=np.float32)
         check(lib.bt_engine_set_router_bias(self.h, layer, _lib.ptr(b, C.c_float), b.size))
 
+    def bench_experts(self, T: int, n_iters: int = 20, seed: int = 1) -> tuple:
+        """(ms per pass over every layer, weight bytes per pass) of the routed experts' kernels
+        alone at T tokens a layer (bt_bench_experts)"""
+        ms, nb = C.c_double(), C.c_uint64()
+        check(lib.bt_bench_experts(self.h, T, n_iters, seed, C.byref(ms), C.byref(nb)))
+        return ms.value, nb.value
+
     def set_option(self, name: str, value: int):
         check(lib.bt_set_option(self.h, name.encode(), int(value)))
 

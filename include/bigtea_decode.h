@@ -121,6 +121,19 @@ int bt_kv_export_layer(const bt_kv *kv, uint32_t seq, uint32_t layer, void *k_ou
 int bt_kv_import_layer(bt_kv *kv, uint32_t seq, uint32_t layer, const void *k, const void *v,
                        uint64_t bytes);
 
+/* ---- isolated expert-FFN timing (no counterpart in the reference) ----
+ * The routed experts' kernels alone, layer after layer over every layer of the model, with T
+ * tokens a layer (1..64): a seeded selection of K distinct experts per token, seeded weights and
+ * activation rows, the same kernels a decode step of T single tokens runs (the per-token ones up
+ * to 8 tokens, the grouped ones above). Captured as one CUDA graph, replayed once to warm up and
+ * then n_iters times between CUDA events: *ms_per_pass is the mean device time of one pass over
+ * the layers, *bytes_per_pass the weight bytes one pass reads (every layer's distinct selected
+ * experts' gate, up and down matrices), so bytes / time is the kernels' HBM bandwidth with the
+ * routing and the rest of the step taken away. Overwrites the engine's step scratch; not for an
+ * expert-parallel engine or one with the expert cache. */
+int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint64_t seed, double *ms_per_pass,
+                     uint64_t *bytes_per_pass);
+
 /* StreamingRunner::forward_cached (stream.rs:1933-1975), batched over sequences.
  * Sequence i appends n_tokens[i] tokens (tokens are concatenated in `tokens`) at
  * pos_start[i], which must equal that sequence's cache length. Writes the logits of

@@ -529,3 +529,23 @@ def test_tensor_core_gateup_matches_dp4a_kernel(tiny_cfg, tiny_weights):
     assert np.array_equal(bits(outs[0][1]), bits(outs[1][1]))
     assert np.array_equal(outs[0][2][0], outs[1][2][0]) and np.array_equal(outs[0][2][1], outs[1][2][1])
 
+
+
+def test_isolated_expert_timing_reports_the_selected_bytes(tiny_cfg, tiny_weights):
+    """bt_bench_experts: the routed experts' kernels over every layer at 1 and 24 tokens a layer
+    report a positive device time and the distinct selected experts' bytes (K distinct experts at
+    one token: exactly K per layer), and leave the engine usable."""
+    e = bt.Engine(tiny_cfg, tiny_weights)
+    per_expert = sum(bt.gguf.tensor_nbytes(tiny_cfg.layer_types[0][i], tiny_cfg.n_embd * tiny_cfg.n_ff_exp)
+                     for i in (4, 5, 6))
+    ms1, b1 = e.bench_experts(1, n_iters=3)
+    assert ms1 > 0 and b1 == tiny_cfg.n_layer * tiny_cfg.n_expert_used * per_expert
+    ms24, b24 = e.bench_experts(24, n_iters=3)
+    assert ms24 > 0 and b1 < b24 <= tiny_cfg.n_layer * tiny_cfg.n_expert * per_expert
+    model = orc.Model(tiny_cfg, tiny_weights)
+    cache = bt.KvCache(e, max_positions=64)
+    prompt = [3, 1, 4, 1, 5]
+    assert_logits(bt.StreamingRunner(e).forward_cached(cache, prompt, 0), model.forward(prompt, 0))
+    cache.close()
+    model.close()
+    e.close()
