@@ -90,23 +90,27 @@ __device__ __forceinline__ unsigned long long global_ns() {
 constexpr unsigned BAR_POISON = 0x80000000u;  // arrivals stay far below bit 31
 __device__ __forceinline__ void poison_barrier(unsigned *bar) { atomicOr(bar, BAR_POISON); }
 
-__device__ __noinline__ bool grid_sync(const StepArgs &p, unsigned &epoch, unsigned long long *trace_row = nullptr) {
-    __syncthreads();
-    epoch += 1;
+// Arguments by value (the counter, the error word, the wait limit, the drill, this barrier's
+// number): a reference would give the caller's variable an address and move it to memory.
+// Returns 0 when every CTA arrived, 2 when a thread of this CTA brings a failed wait of its own
+// (`bad`: the CTA poisons the barrier and leaves), 1 when the barrier failed or was poisoned.
+__device__ __noinline__ int grid_sync(unsigned *bar, int *err, long long limit, int fault_cta, int fault_barrier,
+                                     unsigned epoch, bool bad_here, unsigned long long *trace_row) {
+    if (__syncthreads_or(bad_here)) return 2;
     // the failure drill: this CTA leaves without arriving, as one that died would
-    if (p.fault_barrier == (int)epoch && p.fault_cta == (int)blockIdx.x) return false;
+    if (fault_barrier == (int)epoch && fault_cta == (int)blockIdx.x) return 1;
     bool bad = false;
     if (threadIdx.x == 0) {
         if (trace_row) trace_row[blockIdx.x] = global_ns();
         const unsigned target = epoch * gridDim.x;
-        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p.bar), "r"(1u) : "memory");
-        unsigned v = ld_acquire_gpu(p.bar);
+        asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(bar), "r"(1u) : "memory");
+        unsigned v = ld_acquire_gpu(bar);
         if (v < target) {
             const long long t0 = clock64();
-            while ((v = ld_acquire_gpu(p.bar)) < target) {
-                if (clock64() - t0 > p.wait_limit) {
-                    atomicOr(p.err, ERR_WAIT_TIMEOUT);
-                    poison_barrier(p.bar);
+            while ((v = ld_acquire_gpu(bar)) < target) {
+                if (clock64() - t0 > limit) {
+                    atomicOr(err, ERR_WAIT_TIMEOUT);
+                    poison_barrier(bar);
                     v = BAR_POISON;
                     asm volatile("fence.acq_rel.gpu;" ::: "memory");
                     break;
@@ -114,10 +118,10 @@ __device__ __noinline__ bool grid_sync(const StepArgs &p, unsigned &epoch, unsig
             }
         }
         bad = v >= BAR_POISON;
-        if (epoch == 1) bad |= *reinterpret_cast<volatile int *>(p.err) != 0;
+        if (epoch == 1) bad |= *reinterpret_cast<volatile int *>(err) != 0;
         if (trace_row && blockIdx.x == 0) trace_row[gridDim.x] = global_ns();
     }
-    return !__syncthreads_or(bad);
+    return __syncthreads_or(bad) ? 1 : 0;
 }
 
 // ------------------------------------------------------------------ per-warp TMA ring
@@ -956,16 +960,23 @@ __device__ void combine_slice(const float *part, const float *ml, int cstride, i
 // limit. Then the CTA waits, bounded, for its own bulk copies still in flight -- the warps' ring
 // slots, the attention tile buffers (apend) and the aux copies (xpend) -- so that none of them
 // lands in shared memory after the CTA has gone.
-__device__ __noinline__ void step_fail_exit(const StepArgs &p, WarpRing &ring, const StepSmem &sm, uint32_t apend,
-                                            uint32_t apar, uint32_t xpend, uint32_t xpar, bool poison) {
+// Everything arrives by value: a reference to the ring or to the shared-memory map would give
+// those structs an address and move them out of registers for the whole kernel.
+__device__ __noinline__ void step_fail_exit(unsigned *bar, long long limit, uint64_t *ring_bars, uint32_t ring_par,
+                                            int ring_nst, int ring_done, int ring_issued, uint64_t *attn_bar,
+                                            uint64_t *aux_bar, uint32_t apend, uint32_t apar, uint32_t xpend,
+                                            uint32_t xpar, bool poison) {
     const int tid = threadIdx.x;
-    if (poison && tid == 0) poison_barrier(p.bar);
-    for (int j = ring.done; j < ring.issued; j++) ring.wait(j, nullptr, p.wait_limit);
+    if (poison && tid == 0) poison_barrier(bar);
+    for (int j = ring_done; j < ring_issued; j++) {  // this warp's ring copies in flight
+        const int s = j % ring_nst;
+        if (__all_sync(FULL, mbar_wait_l(ring_bars + s, (ring_par >> s) & 1u, nullptr, limit))) ring_par ^= 1u << s;
+    }
     const int hf = tid >> 7;
-    if ((tid & 127) == 0 && ((apend >> hf) & 1u)) mbar_wait_l(sm.attn_bar + hf, (apar >> hf) & 1u, nullptr, p.wait_limit);
+    if ((tid & 127) == 0 && ((apend >> hf) & 1u)) mbar_wait_l(attn_bar + hf, (apar >> hf) & 1u, nullptr, limit);
     if (tid == 0)
         for (int i = 0; i < 2; i++)
-            if ((xpend >> i) & 1u) mbar_wait_l(sm.aux_bar + i, (xpar >> i) & 1u, nullptr, p.wait_limit);
+            if ((xpend >> i) & 1u) mbar_wait_l(aux_bar + i, (xpar >> i) & 1u, nullptr, limit);
     __syncthreads();
 }
 
@@ -1052,7 +1063,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
     uint32_t apend = 0, xpend = 2u;
 #define STEP_FAIL(poison)                                                       \
     do {                                                                        \
-        step_fail_exit(p, ring, sm, apend, apar, xpend, xpar, poison);          \
+        step_fail_exit(p.bar, p.wait_limit, ring.bars, ring.par, ring.nst, ring.done, ring.issued, sm.attn_bar, \
+                       sm.aux_bar, apend, apar, xpend, xpar, poison);                                    \
         return;                                                                 \
     } while (0)
     {
@@ -1164,7 +1176,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         // the K/V pages of this CTA's first two attention items, requested before the barrier
         const int it0 = blockIdx.x;
         const int n_items = attn_items(p, sm.pos);
-        if (__syncthreads_or(bad)) STEP_FAIL(true);
+        __syncthreads();  // every warp is done with its ring slots: the region takes attention tiles
         if (warp < 2) {  // warp k issues item k's pages
             const int i = it0 + warp * gridDim.x;
             if (i < n_items) {
@@ -1174,7 +1186,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             }
         }
         apend = (it0 < n_items ? 1u : 0u) | (it0 + (int)gridDim.x < n_items ? 2u : 0u);
-        if (!grid_sync(p, epoch, TR(il, 0))) STEP_FAIL(false);
+        if (const int gs_ = grid_sync(p.bar, p.err, p.wait_limit, p.fault_cta, p.fault_barrier, ++epoch, bad,
+                                      TR(il, 0)))
+            STEP_FAIL(gs_ == 2);
         // ================= ATTN: items it0 + k * grid; half hf of the CTA runs k = hf, hf + 2, ...
         {
             const int hf = warp >> 2;
@@ -1212,7 +1226,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             res_pre = __ldcg(p.x + (long long)(tid / orows) * E + orow0 + tid % orows);
         __syncthreads();
         gemv_preissue(ring, so, warp, lane);
-        if (!grid_sync(p, epoch, TR(il, 1))) STEP_FAIL(false);
+        if (const int gs_ = grid_sync(p.bar, p.err, p.wait_limit, p.fault_cta, p.fault_barrier, ++epoch, bad,
+                                      TR(il, 1)))
+            STEP_FAIL(gs_ == 2);
         if (tid < T * orows) sm.res[tid] = res_pre;
         // the next layer's small vectors, towards L2
         if (has_next && blockIdx.x < 3) {
@@ -1243,7 +1259,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                                   p.att + (long long)t * QW + hd * 128 + q * nd, sm.cbuf,
                                   reinterpret_cast<float *>(sm.act), sm.misc);
                 }
-                if (!grid_sync(p, epoch, TR(il, 2))) STEP_FAIL(false);
+                if (const int gs_ = grid_sync(p.bar, p.err, p.wait_limit, p.fault_cta, p.fault_barrier, ++epoch, bad,
+                                              TR(il, 2)))
+                    STEP_FAIL(gs_ == 2);
             }
         }
         // ================= O: ffn_in = x + W_o * att
@@ -1256,7 +1274,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         const int nrr = (int)blockIdx.x < p.NE ? (p.NE - 1 - (int)blockIdx.x) / (int)gridDim.x + 1 : 0;
         float *rrows = reinterpret_cast<float *>(sm.region);
         float *ynorm = rrows + STEP_ROUTER_ROWS * E;
-        if (__syncthreads_or(bad)) STEP_FAIL(true);
+        __syncthreads();  // every warp is done with its ring slots: the region takes router rows
         if (tid == 0) {
             fence_proxy_async();
             mbar_arrive_expect_tx(sm.aux_bar + 0, nrr * E * 4);
@@ -1267,7 +1285,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             bulk_g2s(sm.cbuf, L.ffn_norm, E * 4, sm.aux_bar + 1);
         }
         xpend |= 3u;
-        if (!grid_sync(p, epoch, TR(il, 3))) STEP_FAIL(false);
+        if (const int gs_ = grid_sync(p.bar, p.err, p.wait_limit, p.fault_cta, p.fault_barrier, ++epoch, bad,
+                                      TR(il, 3)))
+            STEP_FAIL(gs_ == 2);
         // ================= ROUTER: ffn RMSNorm (staged for the experts too) and router rows
         if (!wait_aux(1)) STEP_FAIL(true);
         step_stage(p.ffn_in, E, E, T, sm.cbuf, p.eps, sm.act, sm.normS, ynorm);
@@ -1286,7 +1306,9 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         }
         int d0, d1;
         cta_range(T * E, d0, d1);
-        if (!grid_sync(p, epoch, TR(il, 4))) STEP_FAIL(false);
+        if (const int gs_ = grid_sync(p.bar, p.err, p.wait_limit, p.fault_cta, p.fault_barrier, ++epoch, bad,
+                                      TR(il, 4)))
+            STEP_FAIL(gs_ == 2);
         // ================= GATEUP: soft_max + route() in every CTA (C5, C7; stable descending
         // by total_cmp, top K, renormalised), then the experts
         {
@@ -1407,19 +1429,22 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                 atomicMax(cycv + 4, (unsigned long long)gcw);
                 atomicMax(cycv + 5, (unsigned long long)(clock64() - gc0 - gcw));
             }
-            if (__syncthreads_or(bad)) STEP_FAIL(true);
             CYC_WRITE(il, 11, 4);
             CYC_WRITE(il, 12, 5);
             POINT(il, 5);
             // the down rows of this CTA: request the first ones before the barrier
-            const int dn = warp_units(d0, d1, warp);
-            ring.configure(K * L.down.tile_bytes);
-            while (ring.issued < dn && ring.can_issue()) down_issue(ring, L, sm, K, E, d0, warp, lane);
+            if (!bad) {  // a warp whose wait ran out keeps its ring as it is, for the failure drain
+                const int dn = warp_units(d0, d1, warp);
+                ring.configure(K * L.down.tile_bytes);
+                while (ring.issued < dn && ring.can_issue()) down_issue(ring, L, sm, K, E, d0, warp, lane);
+            }
         }
         // the down phase's residual rows (ffn_in, final since the O barrier)
         float dres_pre = 0.0f;
         if (tid < d1 - d0) dres_pre = __ldcg(p.ffn_in + d0 + tid);
-        if (!grid_sync(p, epoch, TR(il, 5))) STEP_FAIL(false);
+        if (const int gs_ = grid_sync(p.bar, p.err, p.wait_limit, p.fault_cta, p.fault_barrier, ++epoch, bad,
+                                      TR(il, 5)))
+            STEP_FAIL(gs_ == 2);
         if (tid < d1 - d0) sm.res[tid] = dres_pre;
         // ================= DOWN: the experts' down rows, their sum in the reference's order, residual
         step_stage(p.act, F, F, T * K, nullptr, 0.0f, sm.act, nullptr, nullptr);
@@ -1489,7 +1514,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         }
         // the next layer's q/k/v tiles (or the output head's) and its norm vector are static:
         // request them now
-        if (__syncthreads_or(bad)) STEP_FAIL(true);
+        __syncthreads();
         if (tid == 0) {
             const float *nv = has_next ? sm.ldesc[(il + 1) & 1].attn_norm : p.out_norm;
             fence_proxy_async();
@@ -1497,7 +1522,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             bulk_g2s(sm.cbuf, nv, E * 4, sm.aux_bar + 1);
         }
         xpend |= 2u;
-        if (has_next) {
+        if (bad) {
+        } else if (has_next) {  // (a warp whose wait ran out keeps its ring for the drain)
             const LayerDev &Ln = sm.ldesc[(il + 1) & 1];
             const SegList sqn = make_segs(&Ln.q, 0, &Ln.k, QW, &Ln.v, QW + KW);
             gemv_preissue(ring, sqn, warp, lane);
@@ -1505,22 +1531,26 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             const SegList sout = make_segs(sm.outd, 0, nullptr, 0, nullptr, 0);
             gemv_preissue(ring, sout, warp, lane);
         }
-        if (!grid_sync(p, epoch, TR(il, 6))) STEP_FAIL(false);
+        if (const int gs_ = grid_sync(p.bar, p.err, p.wait_limit, p.fault_cta, p.fault_barrier, ++epoch, bad,
+                                      TR(il, 6)))
+            STEP_FAIL(gs_ == 2);
     }
     // ================= output head with the fused argmax
+    bool hbad = false;
     {
         const SegList sout = make_segs(sm.outd, 0, nullptr, 0, nullptr, 0);
         if (!wait_aux(1)) STEP_FAIL(true);  // out_norm in cbuf
         step_stage(p.x, E, E, T, sm.cbuf, p.eps, sm.act, sm.normS, nullptr);
         __syncthreads();
         CYC_RESET();
-        bool hbad = !gemv_run(ring, sout, sm.act, nsbE, T, p.logits, p.V, nullptr, 0, 0, p.amax, p.err, p.wait_limit,
-                              warp, lane, p.trace ? cycv : nullptr);
-        if (__syncthreads_or(hbad)) STEP_FAIL(true);
+        hbad = !gemv_run(ring, sout, sm.act, nsbE, T, p.logits, p.V, nullptr, 0, 0, p.amax, p.err, p.wait_limit, warp,
+                         lane, p.trace ? cycv : nullptr);
         CYC_WRITE(p.n_layer, 13, 0);
         CYC_WRITE(p.n_layer, 14, 1);
     }
-    if (!grid_sync(p, epoch, TR(p.n_layer, 0))) STEP_FAIL(false);
+    if (const int gs_ = grid_sync(p.bar, p.err, p.wait_limit, p.fault_cta, p.fault_barrier, ++epoch, hbad,
+                                  TR(p.n_layer, 0)))
+        STEP_FAIL(gs_ == 2);
     // ================= step end: argmax out, lengths advance, greedy feed-back
     if (blockIdx.x == 0 && tid < T) {
         const int t = tid;
