@@ -308,6 +308,17 @@ def run_ours(args, rank, world, local_rank):
             expert_gemv[f"batch{T}"] = {"ms_per_pass": round(ms_x, 4), "gb_per_pass": round(nb_x / 1e9, 3),
                                         "achieved_gbs": round(gbs, 1), "frac": round(gbs / peak_gbs, 4),
                                         "path": "per-token kernels" if T <= 8 else "grouped kernels (tcgen05 gate/up)"}
+        # the same arithmetic as one persistent kernel over every layer, given the selections up
+        # front: the weight stream runs on across the gate/up -> down dependency of each layer
+        ms_s, nb_s, out_s = engine.bench_experts(1, n_iters=args.expert_iters, seed=args.seed, kernel=1, out=True)
+        _, _, out_k = engine.bench_experts(1, n_iters=1, seed=args.seed, kernel=0, out=True)
+        gbs = nb_s / (ms_s / 1e3) / 1e9
+        expert_gemv["batch1_stream"] = {
+            "ms_per_pass": round(ms_s, 4), "gb_per_pass": round(nb_s / 1e9, 3), "achieved_gbs": round(gbs, 1),
+            "frac": round(gbs / peak_gbs, 4),
+            "path": "one persistent kernel over the layers: a producer warp per CTA streams the selected experts' "
+                    "tiles through a CTA-wide TMA ring; layer s's gate/up and layer s-1's down share a stage",
+            "bit_exact_vs_per_layer_kernels": bool(np.array_equal(out_s.view(np.uint32), out_k.view(np.uint32)))}
 
     # the batched workload: batch2 concurrent sequences, per-sequence contexts seeded uniform in
     # [ctx2_min, ctx2_max], paged f16 KV
@@ -657,6 +668,9 @@ def main():
             sys.exit(3)
         if ((out.get("batched") or {}).get("ep_parity") or {}).get("status") == "MISMATCH":
             print("bench: the expert-parallel step's logits differ from the one-GPU engine's", file=sys.stderr)
+            sys.exit(3)
+        if ((out.get("expert_gemv") or {}).get("batch1_stream") or {}).get("bit_exact_vs_per_layer_kernels") is False:
+            print("bench: the expert stream kernel's sums differ from the per-layer kernels'", file=sys.stderr)
             sys.exit(3)
 
 

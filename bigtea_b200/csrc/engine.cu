@@ -25,6 +25,7 @@
 #include "expert_cache.h"
 #include "kernels.cuh"
 #include "step_kernel.cuh"
+#include "expert_stream.cuh"
 
 using namespace bt;
 
@@ -137,6 +138,10 @@ struct bt_engine {
     bool attn_warp = true;   // batched attention with one warp per 128-key chunk (option "attn_warp")
     // the persistent step's bounded waits, in microseconds (option "wait_limit_us"; 0 = about 1 s)
     int wait_limit_us = 0;
+    // ring slots of the expert stream kernel (option "stream_slots"; 0 = as many as fit in
+    // 160 KB of shared memory with the staging buffers, which leaves the SM about 90 KB of L1
+    // for the prefetched activation rows)
+    int stream_slots = 0;
     // failure drill of the persistent step (options "fault_cta", "fault_barrier"; off at 0):
     // CTA fault_cta leaves at its grid barrier number fault_barrier without arriving
     int fault_cta = 0, fault_barrier = 0;
@@ -2230,14 +2235,17 @@ extern "C" int bt_generate_greedy(bt_engine *e, bt_kv *kv, const uint32_t *seq_i
 // weights summing to 1) and seeded activation rows, through launch_layer_experts -- the kernels a
 // decode step of T single tokens runs. Captured once as a CUDA graph of every layer, replayed
 // once to warm up, then n_iters times between CUDA events.
-extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint64_t seed, double *ms_per_pass,
-                                uint64_t *bytes_per_pass) {
+extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint64_t seed, uint32_t kernel,
+                                double *ms_per_pass, uint64_t *bytes_per_pass, float *out_last) {
     if (!e || !ms_per_pass || !bytes_per_pass) return fail(BT_ERR_INVALID, "null argument");
     if (e->ep || e->xcache) return fail(BT_ERR_UNSUPPORTED, "the expert timing needs every expert resident on one GPU");
     if (T == 0 || (int)T > e->TB || n_iters == 0) return fail(BT_ERR_INVALID, "T must be 1..the step capacity, n_iters >= 1");
+    if (kernel > 1) return fail(BT_ERR_INVALID, "kernel must be 0 (per-layer launches) or 1 (the stream kernel)");
+    if (kernel == 1 && (int)T > STEP_MAX_T) return fail(BT_ERR_INVALID, "the stream kernel carries at most 4 tokens");
     CK(cudaSetDevice(e->device));
     const bt_model_desc &d = e->d;
     const int L = (int)d.n_layer, K = (int)d.n_expert_used, NE = (int)d.n_expert, E = (int)d.n_embd;
+    const int F = (int)d.n_ff_exp;
     uint64_t st = seed ^ 0x5DEECE66Dull;
     auto next = [&st]() {  // splitmix64
         uint64_t z = (st += 0x9E3779B97F4A7C15ull);
@@ -2273,7 +2281,7 @@ extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint
             if (used[x]) bytes += (uint64_t)(l.gate.mat_bytes + l.up.mat_bytes + l.down.mat_bytes);
     }
     for (auto &v : fn) v = (float)((int64_t)(next() >> 40) - (1ll << 23)) / (float)(1ll << 23);
-    DevBuf dsel, dw;
+    DevBuf dsel, dw, act_all, out_all;
     CK(dsel.alloc(sel.size() * 4));
     CK(dw.alloc(w.size() * 4));
     CK(cudaMemcpyAsync(dsel.p, sel.data(), sel.size() * 4, cudaMemcpyHostToDevice, e->st));
@@ -2281,6 +2289,56 @@ extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint
     CK(cudaMemcpyAsync(e->fn.p, fn.data(), fn.size() * 4, cudaMemcpyHostToDevice, e->st));
     CK(cudaMemsetAsync(e->ffn_in.p, 0, (size_t)T * E * 4, e->st));
     CK(cudaMemsetAsync(e->single.p, 1, T, e->st));
+    ExpertStreamArgs xa{};
+    if (kernel == 1) {
+        if (!e->layer_dev.p) return fail(BT_ERR_UNSUPPORTED, "the stream kernel needs the device layer table");
+        int slot = 0;
+        for (int il = 0; il < L; il++) {
+            const Layer &l = e->L[il];
+            slot = std::max(slot, l.gate.g.tile_bytes + l.up.g.tile_bytes);
+            slot = std::max(slot, K * l.down.g.tile_bytes);
+            if (l.gate.g.rpt * l.gate.g.nsb > 32 || l.down.g.nsb > 32 || F % 256)
+                return fail(BT_ERR_UNSUPPORTED, "the stream kernel needs 32-slot gate/up tiles and F % 256 == 0");
+        }
+        if ((int)((T * (uint32_t)E + (uint32_t)e->n_sm - 1) / (uint32_t)e->n_sm) > expert_stream_max_rows())
+            return fail(BT_ERR_UNSUPPORTED, "the stream kernel's CTAs would own too many down rows");
+        const size_t fixed = expert_stream_fixed_smem((int)T, E, K, F);
+        const size_t cap = e->stream_slots ? (size_t)max_dynamic_smem() : std::min<size_t>(160 * 1024, max_dynamic_smem());
+        int nslot = cap > fixed ? (int)std::min<size_t>((cap - fixed) / (size_t)slot, (size_t)expert_stream_max_slots()) : 0;
+        if (e->stream_slots) {
+            if (e->stream_slots > nslot) return fail(BT_ERR_INVALID, "stream_slots: that many slots do not fit");
+            nslot = e->stream_slots;
+        }
+        if (nslot < 2) return fail(BT_ERR_UNSUPPORTED, "the stream kernel's ring does not fit in shared memory");
+        CK(act_all.alloc((size_t)L * T * K * F * 4));
+        CK(out_all.alloc((size_t)L * T * E * 4));
+        xa.layers = e->layer_dev.as<LayerDev>();
+        xa.n_layer = L;
+        xa.T = (int)T;
+        xa.K = K;
+        xa.E = E;
+        xa.F = F;
+        xa.workers = (int)d.expert_workers;
+        xa.sel = dsel.as<int>();
+        xa.wts = dw.as<float>();
+        xa.xin = e->fn.as<float>();
+        xa.xin_stride = 0;
+        xa.act = act_all.as<float>();
+        xa.out = out_all.as<float>();
+        xa.bar = e->gbar.as<unsigned>();
+        xa.err = e->err.as<int>();
+        xa.wait_limit = WAIT_LIMIT_CYCLES;
+        xa.nslot = nslot;
+        xa.slot_bytes = slot;
+        int per_sm = 0;
+        CK(prepare_expert_stream(xa, &per_sm));
+        if (per_sm < 1)
+            return fail(BT_ERR_UNSUPPORTED, "the stream kernel does not fit an SM: " +
+                                                std::to_string(expert_stream_fixed_smem((int)T, E, K, F) +
+                                                               (size_t)nslot * slot) +
+                                                " B of shared memory, " + std::to_string(expert_stream_regs()) +
+                                                " registers per thread");
+    }
     CK(cudaStreamSynchronize(e->st));
     const bool timing = e->timing;
     e->timing = false;
@@ -2288,9 +2346,15 @@ extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint
     cudaGraphExec_t ge = nullptr;
     CK(cudaStreamBeginCapture(e->st, cudaStreamCaptureModeThreadLocal));
     int r = BT_OK;
-    for (int il = 0; il < L && r == BT_OK; il++)
-        r = launch_layer_experts(e, il, (int)T, dsel.as<int>() + (size_t)il * T * K, dw.as<float>() + (size_t)il * T * K,
-                                 nullptr, nullptr, e->st, e->pdl);
+    if (kernel == 1) {
+        cudaError_t le = cudaMemsetAsync(xa.bar, 0, 4, e->st);
+        if (le == cudaSuccess) le = launch_expert_stream(xa, e->n_sm, e->st);
+        if (le != cudaSuccess) r = fail(BT_ERR_CUDA, cudaGetErrorString(le));
+    } else {
+        for (int il = 0; il < L && r == BT_OK; il++)
+            r = launch_layer_experts(e, il, (int)T, dsel.as<int>() + (size_t)il * T * K,
+                                     dw.as<float>() + (size_t)il * T * K, nullptr, nullptr, e->st, e->pdl);
+    }
     cudaError_t ce = cudaStreamEndCapture(e->st, &g);
     e->timing = timing;
     if (r) {
@@ -2316,6 +2380,10 @@ extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint
     cudaGraphExecDestroy(ge);
     CK(ce);
     if ((r = check_err(e))) return r;
+    if (out_last) {
+        const float *src = kernel == 1 ? out_all.as<float>() + (size_t)(L - 1) * T * E : e->x.as<float>();
+        CK(cudaMemcpy(out_last, src, (size_t)T * E * 4, cudaMemcpyDeviceToHost));
+    }
     *ms_per_pass = (double)ms / n_iters;
     *bytes_per_pass = bytes;
     return BT_OK;
@@ -2733,6 +2801,11 @@ extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
                                           : e->fault_copy) = value;
         for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);  // the values are baked into captured launches
         e->graphs.clear();
+        return BT_OK;
+    }
+    if (!strcmp(name, "stream_slots")) {
+        if (value < 0) return fail(BT_ERR_INVALID, "stream_slots must be >= 0");
+        e->stream_slots = value;
         return BT_OK;
     }
     if (!strcmp(name, "pdl")) {

@@ -92,12 +92,16 @@ class Engine:
         b = np.ascontiguousarray(bias, dtype=np.float32)
         check(lib.bt_engine_set_router_bias(self.h, layer, _lib.ptr(b, C.c_float), b.size))
 
-    def bench_experts(self, T: int, n_iters: int = 20, seed: int = 1) -> tuple:
-        """(ms per pass over every layer, weight bytes per pass) of the routed experts' kernels
-        alone at T tokens a layer (bt_bench_experts)"""
+    def bench_experts(self, T: int, n_iters: int = 20, seed: int = 1, kernel: int = 0, out: bool = False):
+        """(ms per pass over every layer, weight bytes per pass) of the routed experts' arithmetic
+        alone at T tokens a layer (bt_bench_experts): kernel 0 the decode step's per-layer
+        kernels, kernel 1 the multi-layer stream kernel. With out=True a third element is the last
+        layer's expert sum, [T][n_embd] f32."""
         ms, nb = C.c_double(), C.c_uint64()
-        check(lib.bt_bench_experts(self.h, T, n_iters, seed, C.byref(ms), C.byref(nb)))
-        return ms.value, nb.value
+        o = np.empty((T, self.cfg.n_embd), np.float32) if out else None
+        check(lib.bt_bench_experts(self.h, T, n_iters, seed, kernel, C.byref(ms), C.byref(nb),
+                                   _lib.ptr(o, C.c_float) if out else None))
+        return (ms.value, nb.value, o) if out else (ms.value, nb.value)
 
     def set_option(self, name: str, value: int):
         check(lib.bt_set_option(self.h, name.encode(), int(value)))

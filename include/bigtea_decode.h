@@ -122,17 +122,22 @@ int bt_kv_import_layer(bt_kv *kv, uint32_t seq, uint32_t layer, const void *k, c
                        uint64_t bytes);
 
 /* ---- isolated expert-FFN timing (no counterpart in the reference) ----
- * The routed experts' kernels alone, layer after layer over every layer of the model, with T
- * tokens a layer (1..64): a seeded selection of K distinct experts per token, seeded weights and
- * activation rows, the same kernels a decode step of T single tokens runs (the per-token ones up
- * to 8 tokens, the grouped ones above). Captured as one CUDA graph, replayed once to warm up and
- * then n_iters times between CUDA events: *ms_per_pass is the mean device time of one pass over
- * the layers, *bytes_per_pass the weight bytes one pass reads (every layer's distinct selected
- * experts' gate, up and down matrices), so bytes / time is the kernels' HBM bandwidth with the
- * routing and the rest of the step taken away. Overwrites the engine's step scratch; not for an
- * expert-parallel engine or one with the expert cache. */
-int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint64_t seed, double *ms_per_pass,
-                     uint64_t *bytes_per_pass);
+ * The routed experts' arithmetic alone, over every layer of the model, with T tokens a layer:
+ * a seeded selection of K distinct experts per token, seeded weights and activation rows.
+ * kernel 0: the kernels a decode step of T single tokens runs, layer after layer (the
+ *   per-token ones up to 8 tokens, the grouped ones above; T = 1..the step capacity);
+ * kernel 1: one persistent kernel that is given every layer's selections up front and streams
+ *   the experts' tiles through a CTA-wide TMA ring, layer s's gate/up and layer s-1's down in
+ *   one stage (T = 1..4); the same arithmetic as kernel 0, bit for bit.
+ * Captured as one CUDA graph, replayed once to warm up and then n_iters times between CUDA
+ * events: *ms_per_pass is the mean device time of one pass over the layers, *bytes_per_pass the
+ * weight bytes one pass reads (every layer's distinct selected experts' gate, up and down
+ * matrices), so bytes / time is the kernels' HBM bandwidth with the routing and the rest of the
+ * step taken away. out_last (optional, host, [T][n_embd] f32) receives the last layer's expert
+ * sum. Overwrites the engine's step scratch; not for an expert-parallel engine or one with the
+ * expert cache. */
+int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint64_t seed, uint32_t kernel,
+                     double *ms_per_pass, uint64_t *bytes_per_pass, float *out_last);
 
 /* StreamingRunner::forward_cached (stream.rs:1933-1975), batched over sequences.
  * Sequence i appends n_tokens[i] tokens (tokens are concatenated in `tokens`) at
@@ -174,7 +179,9 @@ int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const ui
  * would; the other CTAs' waits run out, the first one poisons the barrier, every CTA leaves at its
  * next barrier, and the call returns BT_ERR_TIMEOUT after about one wait limit; "fault_copy" (off
  * at 0): in layer fault_copy - 1, CTA fault_cta requests none of its expert tiles, so its own
- * waits run out and it takes the failure exit (barrier poisoned, its copies drained). */
+ * waits run out and it takes the failure exit (barrier poisoned, its copies drained);
+ * "stream_slots" (ring slots of bt_bench_experts' stream kernel, default 0 = as many as fit in
+ * 160 KB of shared memory). */
 int bt_set_option(bt_engine *e, const char *name, int value);
 
 /* Router bias of one layer: n == n_expert F32 values added to the router logits before the

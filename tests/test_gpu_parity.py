@@ -287,6 +287,14 @@ def test_cfg0_prefill_128_then_64_greedy_steps():
         want = model.greedy(first, 64)
         assert list(toks[:, 0]) == want
         compare_kv(cache, model, cfg)
+        # the same 64 steps twice more from the prefilled cache: the grid barrier's ordering of
+        # each phase's inputs is exercised 64 x 15 times per run, so a missed ordering would show
+        # as a repeatable mismatch rather than a rare one
+        for _ in range(2):
+            cache.truncate_to(128)
+            toks = runner.generate_greedy(cache, [first], 64)
+            assert list(toks[:, 0]) == want
+            compare_kv(cache, model, cfg)
     finally:
         e.close()
 

@@ -154,3 +154,26 @@ def test_q4km_persistent_g8_at_long_context(q4km):
     finally:
         model.close()
         e.close()
+
+
+def test_expert_stream_kernel_matches_per_layer_kernels(q4km):
+    """bt_bench_experts kernel 1 (every layer's experts in one persistent kernel, a producer warp
+    streaming the tiles) gives the per-layer expert kernels' sums bit for bit, with the Q6_K down
+    layers of the mix, at 1, 3 and 4 tokens a layer; the engine stays usable afterwards."""
+    cfg, W = q4km
+    e = bt.Engine(cfg, W)
+    try:
+        for T in (1, 3, 4):
+            ms0, b0, o0 = e.bench_experts(T, n_iters=2, seed=40 + T, kernel=0, out=True)
+            ms1, b1, o1 = e.bench_experts(T, n_iters=2, seed=40 + T, kernel=1, out=True)
+            assert ms0 > 0 and ms1 > 0 and b0 == b1
+            assert np.abs(o1).max() > 0
+            assert np.array_equal(bits(o0), bits(o1)), f"T={T}"
+        model = orc.Model(cfg, W)
+        cache = bt.KvCache(e, max_positions=64)
+        prompt = [3, 1, 4, 1, 5]
+        assert_logits(bt.StreamingRunner(e).forward_cached(cache, prompt, 0), model.forward(prompt, 0))
+        cache.close()
+        model.close()
+    finally:
+        e.close()

@@ -85,3 +85,24 @@ def test_noalloc_rejects_a_matrix_larger_than_its_scratch():
                                        small.data_ptr(), None) == _lib.BT_ERR_UNSUPPORTED
     assert _lib.lib.bt_op_gemv_noalloc(_lib.TYPE_Q4_K, small.data_ptr(), 16, 200, small.data_ptr(), 1,
                                        small.data_ptr(), None) == _lib.BT_ERR_UNSUPPORTED
+
+
+def test_noalloc_on_its_own_stream_with_a_partial_last_chunk():
+    """17 tokens (two full launches of 8 and a 1-token tail) on a stream that is not torch's
+    current one, for a Q6_K shape the other test does not use: the call orders itself on the
+    given stream, and the tail chunk's offsets are right."""
+    ty, rows, cols, T = _lib.TYPE_Q6_K, 1536, 2048, 17
+    rng = np.random.default_rng(12)
+    w = _synth(ty, rows, cols, seed=300)
+    x = rng.standard_normal((T, cols)).astype(np.float32)
+    ref = gemv(ty, w, rows, cols, x)
+    s = torch.cuda.Stream()
+    with torch.cuda.stream(s):
+        w_dev = torch.from_numpy(w).to("cuda", non_blocking=False)
+        x_dev = torch.from_numpy(x).to("cuda", non_blocking=False)
+        y_dev = torch.full((T, rows), float("nan"), dtype=torch.float32, device="cuda")
+    rc = _lib.lib.bt_op_gemv_noalloc(ty, w_dev.data_ptr(), rows, cols, x_dev.data_ptr(), T, y_dev.data_ptr(),
+                                     s.cuda_stream)
+    assert rc == 0, _lib.lib.bt_last_error()
+    s.synchronize()
+    np.testing.assert_array_equal(y_dev.cpu().numpy(), ref)
