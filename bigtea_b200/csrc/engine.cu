@@ -1331,6 +1331,8 @@ static bool step_eligible(const bt_engine *e, const bt_kv *kv, const StepPlan &p
     int blocks = nsbE > nsbQ ? nsbE : nsbQ;
     blocks = (int)d.n_expert_used * nsbF > blocks ? (int)d.n_expert_used * nsbF : blocks;
     if ((size_t)p.T * blocks * sizeof(ActBlock) > (size_t)STEP_ACT_BYTES) return false;
+    // the down phase: each warp stages one expert's products, and a CTA's rows fit its table
+    if (nsbF > STEP_MAX_NSB_F || (p.T * (int)d.n_embd + e->n_sm - 1) / e->n_sm > STEP_DOWN_ROWS) return false;
     if ((long long)e->L[0].gate.g.nsb * 1 > 32 || 32 / nsbF < 1) return false;
     const int max_chunks = (int)((kv->max_positions + ATTN_CHUNK - 1) / ATTN_CHUNK);
     if (3 * max_chunks * 4 > STEP_CBUF_BYTES || d.n_expert > 512) return false;

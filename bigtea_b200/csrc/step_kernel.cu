@@ -192,6 +192,26 @@ __device__ __noinline__ void quantize_block_nl(F8 x, uint32_t dst_s, int lane) {
     quantize_block_warp(x.v, reinterpret_cast<ActBlock *>(__cvta_shared_to_generic(dst_s)), lane);
 }
 
+// One warp stages nblk 256-value blocks of a row written by other CTAs (C3), the loads of up
+// to three blocks issued before the first is quantised.
+__device__ __noinline__ void stage_blocks_warp(const float *x, int nblk, uint32_t act_s, int lane) {
+    for (int b0 = 0; b0 < nblk; b0 += 3) {
+        F8 v[3];
+#pragma unroll
+        for (int i = 0; i < 3; i++) {
+            if (b0 + i < nblk) {
+                const float4 *src = reinterpret_cast<const float4 *>(x + (b0 + i) * 256 + lane * 8);
+                const float4 a0 = __ldcg(src), a1 = __ldcg(src + 1);
+                v[i].v[0] = a0.x; v[i].v[1] = a0.y; v[i].v[2] = a0.z; v[i].v[3] = a0.w;
+                v[i].v[4] = a1.x; v[i].v[5] = a1.y; v[i].v[6] = a1.z; v[i].v[7] = a1.w;
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 3; i++)
+            if (b0 + i < nblk) quantize_block_nl(v[i], act_s + (uint32_t)((b0 + i) * sizeof(ActBlock)), lane);
+    }
+}
+
 // ------------------------------------------------------------------ activation staging
 __device__ __forceinline__ float4 ld_f4(const float *p, bool global) {
     return global ? __ldcg(reinterpret_cast<const float4 *>(p)) : *reinterpret_cast<const float4 *>(p);
@@ -452,22 +472,59 @@ __device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm,
     r.issued++;
 }
 
-// one unit of the down phase: output row `row` of token t from every selected expert (lane k
-// issues expert k's row)
-__device__ void down_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int E, int u0, int warp,
-                           int lane) {
-    const int j = r.issued;
-    const int u = u0 + warp + j * STEP_WARPS;
-    const int t = u / E, row = u - t * E;
-    uint8_t *dst = r.slot_ptr(j);
-    if (lane == 0) mbar_arrive_expect_tx(r.slot_bar(j), K * L.down.tile_bytes);
-    __syncwarp();
-    if (lane < K) {
-        const int e = sm.sel_ids[t * MAX_K + lane];
-        bulk_g2s_hint(dst + lane * L.down.tile_bytes,
-                      L.down.w + e * L.down.mat_bytes + (long long)row * L.down.tile_bytes, L.down.tile_bytes,
-                      r.slot_bar(j), l2_evict_first_policy());
+// The down phase's units. A CTA owns the output rows [d0, d1) of T * E; they are cut at token
+// boundaries and into pieces of at most maxr rows, and unit i = (piece i / K, expert i % K):
+// the piece's rows of one selected expert. A down row of the tiled layout is one tile, so a
+// unit is one contiguous copy (one copy per row and expert kept the copy engine far below the
+// SM's share of HBM). Piece q -> token t, first row r0 (0..E-1), rows nr, offset of its first
+// row in [d0, d1); returns the piece count when q is past the end, -1 otherwise.
+__device__ __forceinline__ int down_piece(int d0, int d1, int E, int maxr, int q, int &t, int &r0, int &nr,
+                                          int &off) {
+    int n = 0;
+    for (int tt = d0 / E; tt * E < d1; tt++) {
+        const int a = d0 > tt * E ? d0 : tt * E, b = d1 < (tt + 1) * E ? d1 : (tt + 1) * E;
+        if (a >= b) continue;
+        const int pieces = (b - a + maxr - 1) / maxr;
+        if (q < n + pieces) {
+            const int k = q - n;
+            t = tt;
+            r0 = a + k * maxr - tt * E;
+            nr = (b - a - k * maxr) < maxr ? (b - a - k * maxr) : maxr;
+            off = a + k * maxr - d0;
+            return -1;
+        }
+        n += pieces;
     }
+    return n;
+}
+
+// each expert's values of the CTA's down rows, [MAX_K][STEP_DOWN_ROWS], after the warps' staged
+// products in the activation area
+__device__ __forceinline__ float *step_down_part(const StepSmem &sm) {
+    return reinterpret_cast<float *>(reinterpret_cast<uint8_t *>(sm.act) +
+                                     STEP_WARPS * STEP_MAX_NSB_F * sizeof(ActBlock));
+}
+static_assert(STEP_WARPS * STEP_MAX_NSB_F * sizeof(ActBlock) + MAX_K * STEP_DOWN_ROWS * 4 <= STEP_ACT_BYTES,
+              "the down phase's staged products and row values fit the activation area");
+
+// rows of one down unit's copy: half of a warp's ring share, so two units can be in flight
+__device__ __forceinline__ int down_max_rows(int dtb) { return (STEP_REGION_BYTES / STEP_WARPS / 2) / dtb; }
+
+// this warp's j-th down unit (unit warp + j * STEP_WARPS): lane 0 requests it
+__device__ void down_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int E, int d0, int d1,
+                           int maxr, int warp, int lane) {
+    const int j = r.issued;
+    const int i = warp + j * STEP_WARPS, q = i / K, k = i - q * K;
+    int t, r0, nr, off;
+    down_piece(d0, d1, E, maxr, q, t, r0, nr, off);
+    if (lane == 0) {
+        const int e = sm.sel_ids[t * MAX_K + k];
+        const int dtb = L.down.tile_bytes;
+        mbar_arrive_expect_tx(r.slot_bar(j), nr * dtb);
+        bulk_g2s_hint(r.slot_ptr(j), L.down.w + e * L.down.mat_bytes + (long long)r0 * dtb, nr * dtb, r.slot_bar(j),
+                      l2_evict_first_policy());
+    }
+    __syncwarp();
     r.issued++;
 }
 
@@ -1434,9 +1491,13 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             POINT(il, 5);
             // the down rows of this CTA: request the first ones before the barrier
             if (!bad) {  // a warp whose wait ran out keeps its ring as it is, for the failure drain
-                const int dn = warp_units(d0, d1, warp);
-                ring.configure(K * L.down.tile_bytes);
-                while (ring.issued < dn && ring.can_issue()) down_issue(ring, L, sm, K, E, d0, warp, lane);
+                const int maxr = down_max_rows(L.down.tile_bytes);
+                int t_, r_, n_, o_;
+                const int nt = K * down_piece(d0, d1, E, maxr, 1 << 30, t_, r_, n_, o_);
+                const int dn = nt > warp ? (nt - warp + STEP_WARPS - 1) / STEP_WARPS : 0;
+                ring.configure(maxr * L.down.tile_bytes);
+                while (ring.issued < dn && ring.can_issue())
+                    down_issue(ring, L, sm, K, E, d0, d1, maxr, warp, lane);
             }
         }
         // the down phase's residual rows (ffn_in, final since the O barrier)
@@ -1446,61 +1507,51 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                                       TR(il, 5)))
             STEP_FAIL(gs_ == 2);
         if (tid < d1 - d0) sm.res[tid] = dres_pre;
-        // ================= DOWN: the experts' down rows, their sum in the reference's order, residual
-        step_stage(p.act, F, F, T * K, nullptr, 0.0f, sm.act, nullptr, nullptr);
-        __syncthreads();
-        POINT(il, 6);
+        // ================= DOWN: unit (row piece, expert) per warp in turn: the warp stages that
+        // expert's SiLU products (C3) and writes its rows' values to shared memory; then one
+        // thread per output row adds the experts in the reference's order, and the residual
         {
-            const int n = warp_units(d0, d1, warp);
-            const int nsb = nsbF, epp = 32 / nsb;
             const int dtb = L.down.tile_bytes;
             const bool dq4 = L.down.type == T_Q4_K;
-            float *wv = sm.wv + warp * MAX_K;  // this warp's expert row values
-            int workers = p.workers < K ? p.workers : K;
-            if (workers < 1) workers = 1;
-            const int wchunk = (K + workers - 1) / workers;
+            const int maxr = down_max_rows(dtb);
+            int t_, r_, n_, o_;
+            const int nt = K * down_piece(d0, d1, E, maxr, 1 << 30, t_, r_, n_, o_);
+            const int n = nt > warp ? (nt - warp + STEP_WARPS - 1) / STEP_WARPS : 0;
+            ActBlock *mine = sm.act + warp * nsbF;  // this warp's expert's products
+            float *part = step_down_part(sm);       // [MAX_K][STEP_DOWN_ROWS] the rows' values
+            const int rpp = 32 / nsbF;              // rows per pass of the warp
+            int staged = -1;                        // (token, expert) in `mine`
             CYC_RESET();
             long long dcw = 0, dc0 = clock64();
             for (int j = 0; j < n; j++) {
-                while (ring.issued < n && ring.can_issue()) down_issue(ring, L, sm, K, E, d0, warp, lane);
+                while (ring.issued < n && ring.can_issue()) down_issue(ring, L, sm, K, E, d0, d1, maxr, warp, lane);
+                const int i = warp + j * STEP_WARPS, q = i / K, k = i - q * K;
+                int t, r0, nr, off;
+                down_piece(d0, d1, E, maxr, q, t, r0, nr, off);
+                if (t * K + k != staged) {
+                    staged = t * K + k;
+                    __syncwarp();
+                    stage_blocks_warp(p.act + (long long)staged * F, nsbF, smem_u32(mine), lane);
+                    __syncwarp();
+                }
                 const long long w0 = clock64();
                 if (!ring.wait(j, p.err, p.wait_limit)) {
                     bad = true;
                     break;
                 }
                 dcw += clock64() - w0;
-                const int u = d0 + warp + j * STEP_WARPS;
-                const int t = u / E;
-                const uint8_t *base = ring.slot_ptr(j);
-                const int kk = lane / nsb, b = lane - kk * nsb;
-                for (int k0 = 0; k0 < K; k0 += epp) {
-                    const int k = k0 + kk;
-                    const bool valid = kk < epp && k < K;
+                const uint8_t *tb = ring.slot_ptr(j);
+                for (int rb = 0; rb < nr; rb += rpp) {
+                    const int ri = lane / nsbF, b = lane - ri * nsbF, r = rb + ri;
+                    const bool valid = ri < rpp && r < nr;
                     float v = 0.0f;
-                    if (valid) {
-                        const ActBlock &ab = sm.act[(t * K + k) * nsb + b];
-                        const uint8_t *tile = base + k * dtb;
-                        v = slot_dot(dq4, tile, nsb, b, &ab);
-                    }
+                    if (valid) v = slot_dot(dq4, tb + r * dtb, nsbF, b, mine + b);
                     float acc = 0.0f;
-                    for (int b2 = 0; b2 < nsb; b2++) {
-                        const int srcl = kk * nsb + b2;
+                    for (int b2 = 0; b2 < nsbF; b2++) {
+                        const int srcl = ri * nsbF + b2;
                         acc = __fadd_rn(acc, __shfl_sync(FULL, v, srcl < 32 ? srcl : 31));
                     }
-                    if (valid && b == 0) wv[k] = acc;
-                }
-                __syncwarp();
-                if (lane == 0) {
-                    // expert_ffn_single order: chunks of ceil(K/workers) summed by ggml_add, partials
-                    // added to a zero vector (stream.rs:1232-1284)
-                    const float *w = sm.sel_w + t * MAX_K;
-                    float sum = 0.0f;
-                    for (int s0 = 0; s0 < K; s0 += wchunk) {
-                        float tot = __fmul_rn(wv[s0], w[s0]);
-                        for (int q = s0 + 1; q < K && q < s0 + wchunk; q++) tot = __fadd_rn(tot, __fmul_rn(wv[q], w[q]));
-                        sum = workers <= 1 ? tot : __fadd_rn(sum, tot);
-                    }
-                    p.x[u] = __fadd_rn(sm.res[u - d0], sum);
+                    if (valid && b == 0) part[k * STEP_DOWN_ROWS + off + r] = acc;
                 }
                 __syncwarp();
                 ring.done++;
@@ -1511,6 +1562,25 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             }
             CYC_WRITE(il, 9, 2);
             CYC_WRITE(il, 10, 3);
+            POINT(il, 6);
+            __syncthreads();
+            if (tid < d1 - d0) {
+                // expert_ffn_single order: chunks of ceil(K/workers) summed by ggml_add, partials
+                // added to a zero vector (stream.rs:1232-1284), then the residual
+                int workers = p.workers < K ? p.workers : K;
+                if (workers < 1) workers = 1;
+                const int wchunk = (K + workers - 1) / workers;
+                const int u = d0 + tid, t = u / E;
+                const float *w = sm.sel_w + t * MAX_K;
+                float sum = 0.0f;
+                for (int s0 = 0; s0 < K; s0 += wchunk) {
+                    float tot = __fmul_rn(part[s0 * STEP_DOWN_ROWS + tid], w[s0]);
+                    for (int q = s0 + 1; q < K && q < s0 + wchunk; q++)
+                        tot = __fadd_rn(tot, __fmul_rn(part[q * STEP_DOWN_ROWS + tid], w[q]));
+                    sum = workers <= 1 ? tot : __fadd_rn(sum, tot);
+                }
+                p.x[u] = __fadd_rn(sm.res[tid], sum);
+            }
         }
         // the next layer's q/k/v tiles (or the output head's) and its norm vector are static:
         // request them now

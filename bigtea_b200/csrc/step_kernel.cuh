@@ -13,6 +13,8 @@ constexpr int STEP_ACT_BYTES = 32 * 1024;        // Q8_K activation blocks
 constexpr int STEP_CBUF_BYTES = 16 * 1024;       // norm vector, router probabilities, combine scratch
 constexpr int STEP_ROUTER_ROWS = 4;              // router rows one CTA computes
 constexpr int STEP_RES = 256;                    // residual values one CTA prefetches for a phase
+constexpr int STEP_DOWN_ROWS = 128;              // down rows one CTA owns per layer: T * E / grid, rounded up
+constexpr int STEP_MAX_NSB_F = 8;                // expert width F / 256 the down phase stages per warp
 
 // A quantised matrix in the tiled layout, as the device reads it.
 struct QMatDev {
