@@ -2437,7 +2437,7 @@ extern "C" int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_id
                                 "ph5_gateup", "ph6_down", "ph7_unused"};
         // points inside phases: slowest CTA, measured from the departure of the barrier before
         const char *pnames[8] = {"pt_qkv_staged", "pt_attn_item1", "pt_o_staged", "pt_router_staged",
-                                 "pt_gateup_routed", "pt_gateup_units", "pt_down_staged", "pt_unused"};
+                                 "pt_gateup_routed", "pt_gateup_units", "pt_down_units", "pt_unused"};
         const int point_after[8] = {-1, 0, 2, 3, -1, 4, 5, -1};  // barrier whose departure starts each point
         // cycle counters inside phases (max over warps, then over CTAs), as microseconds at the
         // SM clock the device reports
