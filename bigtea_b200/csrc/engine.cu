@@ -92,6 +92,9 @@ struct Layer {
     DevBuf gate_bias;  // optional ffn_gate_inp.bias [n_expert], added to the router logits
     QMat q, k, v, o, gate, up, down;
     QMat gate_sh, up_sh, down_sh;  // the shared expert, when the model has one (n_ff_shexp)
+    // the shared expert's down matrix again with one row per tile, for the persistent step's
+    // down units (a layout copy: not counted in the weight bytes)
+    QMat down_sh1;
 };
 
 struct GraphKey {
@@ -558,6 +561,13 @@ static int upload_layer_dev(bt_engine *e) {
         x.gate = qmat_dev(l.gate);
         x.up = qmat_dev(l.up);
         x.down = qmat_dev(l.down);
+        if (e->d.n_ff_shexp) {
+            x.sgate = qmat_dev(l.gate_sh);
+            x.sup = qmat_dev(l.up_sh);
+            x.sdown = qmat_dev(l.down_sh1);
+        } else {
+            x.sgate = x.sup = x.sdown = QMatDev{};
+        }
     }
     if (!e->layer_dev.p) CK(e->layer_dev.alloc(ld.size() * sizeof(LayerDev)));
     CK(cudaMemcpy(e->layer_dev.p, ld.data(), ld.size() * sizeof(LayerDev), cudaMemcpyHostToDevice));
@@ -695,6 +705,9 @@ static int build_engine(bt_engine *e, const std::map<std::string, SrcTensor> &sr
             if ((r = mat("ffn_gate_shexp.weight", l.gate_sh, E, FS, 1, default_rpt(E)))) return r;
             if ((r = mat("ffn_up_shexp.weight", l.up_sh, E, FS, 1, default_rpt(E)))) return r;
             if ((r = mat("ffn_down_shexp.weight", l.down_sh, FS, E, 1, default_rpt(FS)))) return r;
+            const uint64_t wb = e->weight_bytes;
+            if ((r = mat("ffn_down_shexp.weight", l.down_sh1, FS, E, 1, 1))) return r;
+            e->weight_bytes = wb;
         }
         if (l.gate.g.tile_bytes != l.up.g.tile_bytes && l.gate.type == l.up.type)
             return fail(BT_ERR_INVALID, "gate and up experts disagree in shape");
@@ -1322,7 +1335,7 @@ static int upload_plan(bt_engine *e, const StepPlan &p) {
 // Can this step run as one persistent kernel? Single-token steps of up to STEP_MAX_T
 // sequences whose activations fit the kernel's shared memory.
 static bool step_eligible(const bt_engine *e, const bt_kv *kv, const StepPlan &p) {
-    if (!e->mega || e->ep || e->xcache || e->d.n_ff_shexp || p.T > STEP_MAX_T || p.out_first != 0 || (int)p.x_rows.size() != p.T) return false;
+    if (!e->mega || e->ep || e->xcache || p.T > STEP_MAX_T || p.out_first != 0 || (int)p.x_rows.size() != p.T) return false;
     for (int t = 0; t < p.T; t++)
         if (!p.single[t] || p.local_idx[t] != 0 || p.x_rows[t] != t || p.st_lrow[t] != t) return false;
     if ((int)p.st_seq.size() != p.T) return false;
@@ -1333,6 +1346,11 @@ static bool step_eligible(const bt_engine *e, const bt_kv *kv, const StepPlan &p
     if ((size_t)p.T * blocks * sizeof(ActBlock) > (size_t)STEP_ACT_BYTES) return false;
     // the down phase: each warp stages one expert's products, and a CTA's rows fit its table
     if (nsbF > STEP_MAX_NSB_F || (p.T * (int)d.n_embd + e->n_sm - 1) / e->n_sm > STEP_DOWN_ROWS) return false;
+    // the shared expert is expert index K of the down units
+    // (a shared expert: only the kernel with 4 query heads per KV head carries it)
+    if (d.n_ff_shexp && ((int)d.n_ff_shexp / 256 > STEP_MAX_NSB_F || (int)d.n_expert_used + 1 > MAX_K ||
+                         d.n_head != 4 * d.n_head_kv))
+        return false;
     if ((long long)e->L[0].gate.g.nsb * 1 > 32 || 32 / nsbF < 1) return false;
     const int max_chunks = (int)((kv->max_positions + ATTN_CHUNK - 1) / ATTN_CHUNK);
     if (3 * max_chunks * 4 > STEP_CBUF_BYTES || d.n_expert > 512) return false;
@@ -1399,6 +1417,8 @@ static int launch_persistent_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bo
     a.gen_out = greedy ? e->gen_out.as<int>() : nullptr;
     a.gen_count = e->gen_count.as<int>();
     a.n_out = p.T;
+    a.FS = (int)e->d.n_ff_shexp;
+    a.shact = e->d.n_ff_shexp ? e->sh_act.as<float>() : nullptr;
     a.bar = e->gbar.as<unsigned>();
     a.err = e->err.as<int>();
     a.wait_limit = WAIT_LIMIT_CYCLES;

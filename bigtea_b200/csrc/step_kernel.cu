@@ -41,7 +41,11 @@ constexpr int RING_SLOTS = 4;
 constexpr int PART_ROW = 132;    // floats per (chunk, head) partial: acc[128], m, l, pad
 constexpr int ATTN_BUF = 65536;  // one attention item's K and V tiles (128 keys x 128 dims x f16 x 2)
 constexpr int LD_WORDS = sizeof(LayerDev) / 4;
-static_assert(sizeof(LayerDev) % 4 == 0 && sizeof(LayerDev) <= 384, "layer descriptor size");
+// barriers and small tables (1 KB), then two layer descriptors and the head's, then the region
+// (1024-byte aligned: the attention tiles' 128-byte swizzle)
+constexpr int STEP_HDR_BYTES = 1024 + ((2 * (int)sizeof(LayerDev) + (int)sizeof(QMatDev) + 1023) / 1024) * 1024;
+static_assert(LD_WORDS <= 256, "a layer descriptor is copied by one thread per word");
+static_assert(sizeof(LayerDev) % 4 == 0, "layer descriptors are copied word by word");
 static_assert(STEP_RES == STEP_THREADS, "one residual value per thread");
 
 // ------------------------------------------------------------------ shared memory map
@@ -451,7 +455,10 @@ __device__ __forceinline__ bool gemv_run(WarpRing &r, const SegList &s, const Ac
 }
 
 // ------------------------------------------------------------------ expert phases
-__device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int u0, int warp,
+// unit u of the gate/up phase: units below nr are (token, slot, tile) of the routed experts,
+// the rest (token, tile) of the shared expert
+template <bool SH>
+__device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int nr, int u0, int warp,
                              int lane, bool drill) {
     const int j = r.issued;
     if (drill) {  // the failure drill: the slot is counted as requested, but nothing will land
@@ -459,14 +466,22 @@ __device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm,
         return;
     }
     const int u = u0 + warp + j * STEP_WARPS;
-    const int tk = u / L.gate.n_tiles, tile = u - tk * L.gate.n_tiles;
-    const int e = sm.sel_ids[(tk / K) * MAX_K + tk % K];
+    const bool sh = SH && u >= nr;
+    const QMatDev &G = sh ? L.sgate : L.gate, &U = sh ? L.sup : L.up;
+    int e = 0, tile;
+    if (sh) {
+        tile = (u - nr) % G.n_tiles;
+    } else {
+        const int tk = u / G.n_tiles;
+        tile = u - tk * G.n_tiles;
+        e = sm.sel_ids[(tk / K) * MAX_K + tk % K];
+    }
     uint8_t *dst = r.slot_ptr(j);
-    if (lane == 0) mbar_arrive_expect_tx(r.slot_bar(j), L.gate.tile_bytes + L.up.tile_bytes);
+    if (lane == 0) mbar_arrive_expect_tx(r.slot_bar(j), G.tile_bytes + U.tile_bytes);
     __syncwarp();
     if (lane < 2) {  // lane 0 the gate tile, lane 1 the up tile
-        const QMatDev &m = lane ? L.up : L.gate;
-        bulk_g2s_hint(dst + lane * L.gate.tile_bytes, m.w + e * m.mat_bytes + (long long)tile * m.tile_bytes,
+        const QMatDev &m = lane ? U : G;
+        bulk_g2s_hint(dst + lane * G.tile_bytes, m.w + e * m.mat_bytes + (long long)tile * m.tile_bytes,
                       m.tile_bytes, r.slot_bar(j), l2_evict_first_policy());
     }
     r.issued++;
@@ -507,22 +522,30 @@ __device__ __forceinline__ float *step_down_part(const StepSmem &sm) {
 static_assert(STEP_WARPS * STEP_MAX_NSB_F * sizeof(ActBlock) + MAX_K * STEP_DOWN_ROWS * 4 <= STEP_ACT_BYTES,
               "the down phase's staged products and row values fit the activation area");
 
-// rows of one down unit's copy: half of a warp's ring share, so two units can be in flight
+// rows of one down unit's copy: half of a warp's ring share, so two units can be in flight (dtb:
+// the largest row of the layer's down matrices)
 __device__ __forceinline__ int down_max_rows(int dtb) { return (STEP_REGION_BYTES / STEP_WARPS / 2) / dtb; }
+template <bool SH>
+__device__ __forceinline__ int down_row_bytes(const LayerDev &L) {
+    return SH && L.sdown.tile_bytes > L.down.tile_bytes ? L.sdown.tile_bytes : L.down.tile_bytes;
+}
 
-// this warp's j-th down unit (unit warp + j * STEP_WARPS): lane 0 requests it
-__device__ void down_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int E, int d0, int d1,
+// this warp's j-th down unit (unit warp + j * STEP_WARPS of nk experts per piece; expert index K
+// is the shared expert): lane 0 requests it
+template <bool SH>
+__device__ void down_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int nk, int E, int d0, int d1,
                            int maxr, int warp, int lane) {
     const int j = r.issued;
-    const int i = warp + j * STEP_WARPS, q = i / K, k = i - q * K;
+    const int i = warp + j * STEP_WARPS, q = i / nk, k = i - q * nk;
     int t, r0, nr, off;
     down_piece(d0, d1, E, maxr, q, t, r0, nr, off);
     if (lane == 0) {
-        const int e = sm.sel_ids[t * MAX_K + k];
-        const int dtb = L.down.tile_bytes;
-        mbar_arrive_expect_tx(r.slot_bar(j), nr * dtb);
-        bulk_g2s_hint(r.slot_ptr(j), L.down.w + e * L.down.mat_bytes + (long long)r0 * dtb, nr * dtb, r.slot_bar(j),
-                      l2_evict_first_policy());
+        const bool shx = SH && k == K;
+        const QMatDev &m = shx ? L.sdown : L.down;
+        const int e = shx ? 0 : sm.sel_ids[t * MAX_K + k];
+        mbar_arrive_expect_tx(r.slot_bar(j), nr * m.tile_bytes);
+        bulk_g2s_hint(r.slot_ptr(j), m.w + e * m.mat_bytes + (long long)r0 * m.tile_bytes, nr * m.tile_bytes,
+                      r.slot_bar(j), l2_evict_first_policy());
     }
     __syncwarp();
     r.issued++;
@@ -1038,7 +1061,7 @@ __device__ __noinline__ void step_fail_exit(unsigned *bar, long long limit, uint
 }
 
 // ------------------------------------------------------------------ the kernel
-template <int G>
+template <int G, bool SH>
 __global__ void __launch_bounds__(STEP_THREADS, 1)
     decode_step_kernel(const __grid_constant__ StepArgs p, const __grid_constant__ CUtensorMap tmap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1056,7 +1079,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
     sm.iblk = sm.seq + STEP_MAX_T;
     sm.ldesc = reinterpret_cast<LayerDev *>(smem + 1024);
     sm.outd = reinterpret_cast<QMatDev *>(smem + 1024 + 2 * sizeof(LayerDev));
-    sm.region = smem + 2048;
+    sm.region = smem + STEP_HDR_BYTES;
     sm.act = reinterpret_cast<ActBlock *>(sm.region + STEP_REGION_BYTES);
     sm.sel_ids = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(sm.act) + STEP_ACT_BYTES);
     sm.sel_w = reinterpret_cast<float *>(sm.sel_ids + STEP_MAX_T * MAX_K);
@@ -1435,19 +1458,26 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         }
         POINT(il, 4);
         {
+            // routed units (token, slot, tile), then the shared expert's (token, tile)
+            const int nr = T * K * L.gate.n_tiles, ns = SH ? T * L.sgate.n_tiles : 0;
             int u0, u1;
-            cta_range(T * K * L.gate.n_tiles, u0, u1);
+            cta_range(nr + ns, u0, u1);
             const int n = warp_units(u0, u1, warp);
-            ring.configure(L.gate.tile_bytes + L.up.tile_bytes);
-            const int nsb = L.gate.nsb, gS = L.gate.S, grpt = L.gate.rpt, gnt = L.gate.n_tiles;
-            const bool gq4 = L.gate.type == T_Q4_K, uq4 = L.up.type == T_Q4_K;
-            const int gtb = L.gate.tile_bytes;
+            const int sgb = SH ? L.sgate.tile_bytes + L.sup.tile_bytes : 0;
+            ring.configure(L.gate.tile_bytes + L.up.tile_bytes > sgb ? L.gate.tile_bytes + L.up.tile_bytes : sgb);
+            const int nsb = L.gate.nsb;  // gate and up have E columns: the same tile shape throughout
+            // both kinds' tile geometry in registers: a unit picks one with selects
+            const int rnt = L.gate.n_tiles, rS = L.gate.S, rrpt = L.gate.rpt, rtb = L.gate.tile_bytes;
+            const int snt = L.sgate.n_tiles, sS = L.sgate.S, srpt = L.sgate.rpt, stb = L.sgate.tile_bytes;
+            const bool rgq4 = L.gate.type == T_Q4_K, ruq4 = L.up.type == T_Q4_K;
+            const bool sgq4 = L.sgate.type == T_Q4_K, suq4 = L.sup.type == T_Q4_K;
             const bool drill = p.fault_copy == il + 1 && p.fault_cta == (int)blockIdx.x;
-            while (ring.issued < n && ring.can_issue()) gateup_issue(ring, L, sm, K, u0, warp, lane, drill);
+            while (ring.issued < n && ring.can_issue()) gateup_issue<SH>(ring, L, sm, K, nr, u0, warp, lane, drill);
             CYC_RESET();
             long long gcw = 0, gc0 = clock64();
             for (int j = 0; j < n; j++) {
-                while (ring.issued < n && ring.can_issue()) gateup_issue(ring, L, sm, K, u0, warp, lane, drill);
+                while (ring.issued < n && ring.can_issue())
+                    gateup_issue<SH>(ring, L, sm, K, nr, u0, warp, lane, drill);
                 const long long w0 = clock64();
                 if (!ring.wait(j, p.err, p.wait_limit)) {
                     bad = true;
@@ -1455,8 +1485,23 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                 }
                 gcw += clock64() - w0;
                 const int u = u0 + warp + j * STEP_WARPS;
-                const int tk = u / gnt, tile = u - tk * gnt;
-                const int t = tk / K;
+                const bool sh = SH && u >= nr;
+                const int gnt = sh ? snt : rnt, gS = sh ? sS : rS, grpt = sh ? srpt : rrpt, gtb = sh ? stb : rtb;
+                const bool gq4 = sh ? sgq4 : rgq4, uq4 = sh ? suq4 : ruq4;
+                int t, tile, width;
+                float *out;
+                if (sh) {
+                    t = (u - nr) / gnt;
+                    tile = (u - nr) - t * gnt;
+                    width = p.FS;
+                    out = p.shact + (long long)t * p.FS;
+                } else {
+                    const int tk = u / gnt;
+                    tile = u - tk * gnt;
+                    t = tk / K;
+                    width = F;
+                    out = p.act + (long long)tk * F;
+                }
                 const uint8_t *gt = ring.slot_ptr(j), *ut = gt + gtb;
                 const bool active = lane < gS;
                 const int rit = active ? lane / nsb : 0, b = active ? lane - rit * nsb : 0;
@@ -1478,7 +1523,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                     }
                     rowv[which] = rr;
                 }
-                if (active && b == 0 && row < F) p.act[(long long)tk * F + row] = __fmul_rn(bt_silu(rowv[0]), rowv[1]);
+                if (active && b == 0 && row < width) out[row] = __fmul_rn(bt_silu(rowv[0]), rowv[1]);
                 __syncwarp();
                 ring.done++;
             }
@@ -1491,13 +1536,13 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             POINT(il, 5);
             // the down rows of this CTA: request the first ones before the barrier
             if (!bad) {  // a warp whose wait ran out keeps its ring as it is, for the failure drain
-                const int maxr = down_max_rows(L.down.tile_bytes);
+                const int dtb = down_row_bytes<SH>(L), maxr = down_max_rows(dtb), nk = K + (SH ? 1 : 0);
                 int t_, r_, n_, o_;
-                const int nt = K * down_piece(d0, d1, E, maxr, 1 << 30, t_, r_, n_, o_);
+                const int nt = nk * down_piece(d0, d1, E, maxr, 1 << 30, t_, r_, n_, o_);
                 const int dn = nt > warp ? (nt - warp + STEP_WARPS - 1) / STEP_WARPS : 0;
-                ring.configure(maxr * L.down.tile_bytes);
+                ring.configure(maxr * dtb);
                 while (ring.issued < dn && ring.can_issue())
-                    down_issue(ring, L, sm, K, E, d0, d1, maxr, warp, lane);
+                    down_issue<SH>(ring, L, sm, K, nk, E, d0, d1, maxr, warp, lane);
             }
         }
         // the down phase's residual rows (ffn_in, final since the O barrier)
@@ -1509,29 +1554,33 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
         if (tid < d1 - d0) sm.res[tid] = dres_pre;
         // ================= DOWN: unit (row piece, expert) per warp in turn: the warp stages that
         // expert's SiLU products (C3) and writes its rows' values to shared memory; then one
-        // thread per output row adds the experts in the reference's order, and the residual
+        // thread per output row adds the experts in the reference's order (the shared expert's
+        // value after them, C10), and the residual
         {
-            const int dtb = L.down.tile_bytes;
-            const bool dq4 = L.down.type == T_Q4_K;
-            const int maxr = down_max_rows(dtb);
+            const int dtb = down_row_bytes<SH>(L), maxr = down_max_rows(dtb), nk = K + (SH ? 1 : 0);
             int t_, r_, n_, o_;
-            const int nt = K * down_piece(d0, d1, E, maxr, 1 << 30, t_, r_, n_, o_);
+            const int nt = nk * down_piece(d0, d1, E, maxr, 1 << 30, t_, r_, n_, o_);
             const int n = nt > warp ? (nt - warp + STEP_WARPS - 1) / STEP_WARPS : 0;
-            ActBlock *mine = sm.act + warp * nsbF;  // this warp's expert's products
-            float *part = step_down_part(sm);       // [MAX_K][STEP_DOWN_ROWS] the rows' values
-            const int rpp = 32 / nsbF;              // rows per pass of the warp
-            int staged = -1;                        // (token, expert) in `mine`
+            ActBlock *mine = sm.act + warp * STEP_MAX_NSB_F;  // this warp's expert's products
+            float *part = step_down_part(sm);                 // [MAX_K][STEP_DOWN_ROWS] the rows' values
+            int staged = -1;                                  // (token, expert) in `mine`
             CYC_RESET();
             long long dcw = 0, dc0 = clock64();
             for (int j = 0; j < n; j++) {
-                while (ring.issued < n && ring.can_issue()) down_issue(ring, L, sm, K, E, d0, d1, maxr, warp, lane);
-                const int i = warp + j * STEP_WARPS, q = i / K, k = i - q * K;
+                while (ring.issued < n && ring.can_issue())
+                    down_issue<SH>(ring, L, sm, K, nk, E, d0, d1, maxr, warp, lane);
+                const int i = warp + j * STEP_WARPS, q = i / nk, k = i - q * nk;
                 int t, r0, nr, off;
                 down_piece(d0, d1, E, maxr, q, t, r0, nr, off);
-                if (t * K + k != staged) {
-                    staged = t * K + k;
+                const bool shx = SH && k == K;
+                const int nsbX = shx ? p.FS / 256 : nsbF;
+                const int mtb = shx ? L.sdown.tile_bytes : L.down.tile_bytes;
+                const bool dq4 = (shx ? L.sdown.type : L.down.type) == T_Q4_K;
+                if (t * nk + k != staged) {
+                    staged = t * nk + k;
                     __syncwarp();
-                    stage_blocks_warp(p.act + (long long)staged * F, nsbF, smem_u32(mine), lane);
+                    stage_blocks_warp(shx ? p.shact + (long long)t * p.FS : p.act + (long long)(t * K + k) * F, nsbX,
+                                      smem_u32(mine), lane);
                     __syncwarp();
                 }
                 const long long w0 = clock64();
@@ -1541,14 +1590,15 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                 }
                 dcw += clock64() - w0;
                 const uint8_t *tb = ring.slot_ptr(j);
+                const int rpp = 32 / nsbX;  // rows per pass of the warp
                 for (int rb = 0; rb < nr; rb += rpp) {
-                    const int ri = lane / nsbF, b = lane - ri * nsbF, r = rb + ri;
+                    const int ri = lane / nsbX, b = lane - ri * nsbX, r = rb + ri;
                     const bool valid = ri < rpp && r < nr;
                     float v = 0.0f;
-                    if (valid) v = slot_dot(dq4, tb + r * dtb, nsbF, b, mine + b);
+                    if (valid) v = slot_dot(dq4, tb + r * mtb, nsbX, b, mine + b);
                     float acc = 0.0f;
-                    for (int b2 = 0; b2 < nsbF; b2++) {
-                        const int srcl = ri * nsbF + b2;
+                    for (int b2 = 0; b2 < nsbX; b2++) {
+                        const int srcl = ri * nsbX + b2;
                         acc = __fadd_rn(acc, __shfl_sync(FULL, v, srcl < 32 ? srcl : 31));
                     }
                     if (valid && b == 0) part[k * STEP_DOWN_ROWS + off + r] = acc;
@@ -1566,7 +1616,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             __syncthreads();
             if (tid < d1 - d0) {
                 // expert_ffn_single order: chunks of ceil(K/workers) summed by ggml_add, partials
-                // added to a zero vector (stream.rs:1232-1284), then the residual
+                // added to a zero vector (stream.rs:1232-1284), then the shared expert and the residual
                 int workers = p.workers < K ? p.workers : K;
                 if (workers < 1) workers = 1;
                 const int wchunk = (K + workers - 1) / workers;
@@ -1579,7 +1629,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                         tot = __fadd_rn(tot, __fmul_rn(part[q * STEP_DOWN_ROWS + tid], w[q]));
                     sum = workers <= 1 ? tot : __fadd_rn(sum, tot);
                 }
-                p.x[u] = __fadd_rn(sm.res[tid], sum);
+                if (SH) sum = __fadd_rn(sum, part[K * STEP_DOWN_ROWS + tid]);
+                p.x[u] = __fadd_rn(sum, sm.res[tid]);
             }
         }
         // the next layer's q/k/v tiles (or the output head's) and its norm vector are static:
@@ -1641,7 +1692,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
 
 size_t step_smem_bytes(int max_chunks) {
     (void)max_chunks;
-    return 1024 + 2048 + STEP_REGION_BYTES + STEP_ACT_BYTES + (size_t)STEP_MAX_T * MAX_K * 8 +
+    return 1024 + STEP_HDR_BYTES + STEP_REGION_BYTES + STEP_ACT_BYTES + (size_t)STEP_MAX_T * MAX_K * 8 +
            (size_t)STEP_WARPS * MAX_K * 4 + STEP_CBUF_BYTES + (size_t)STEP_RES * 4;
 }
 
@@ -1650,8 +1701,9 @@ cudaError_t init_step_kernel_attributes() {
     cudaError_t e;
     if ((e = cudaGetDevice(&dev))) return e;
     if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
-    const void *kerns[] = {(const void *)decode_step_kernel<2>, (const void *)decode_step_kernel<4>,
-                           (const void *)decode_step_kernel<6>, (const void *)decode_step_kernel<8>};
+    const void *kerns[] = {(const void *)decode_step_kernel<2, false>, (const void *)decode_step_kernel<4, false>,
+                           (const void *)decode_step_kernel<6, false>, (const void *)decode_step_kernel<8, false>,
+                           (const void *)decode_step_kernel<4, true>};
     for (const void *k : kerns) {
         cudaFuncAttributes fa;
         if ((e = cudaFuncGetAttributes(&fa, k))) return e;
@@ -1661,7 +1713,7 @@ cudaError_t init_step_kernel_attributes() {
     return cudaSuccess;
 }
 
-template <int G>
+template <int G, bool SH>
 static cudaError_t launch_step_g(const StepArgs &a, const CUtensorMap &tmap, int grid, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -1673,15 +1725,15 @@ static cudaError_t launch_step_g(const StepArgs &a, const CUtensorMap &tmap, int
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, decode_step_kernel<G>, a, tmap);
+    return cudaLaunchKernelEx(&cfg, decode_step_kernel<G, SH>, a, tmap);
 }
 
 cudaError_t launch_decode_step(const StepArgs &a, const CUtensorMap &tmap, int grid, cudaStream_t st) {
     switch (a.G) {
-    case 2: return launch_step_g<2>(a, tmap, grid, st);
-    case 4: return launch_step_g<4>(a, tmap, grid, st);
-    case 6: return launch_step_g<6>(a, tmap, grid, st);
-    case 8: return launch_step_g<8>(a, tmap, grid, st);
+    case 2: return a.FS ? cudaErrorInvalidValue : launch_step_g<2, false>(a, tmap, grid, st);
+    case 4: return a.FS ? launch_step_g<4, true>(a, tmap, grid, st) : launch_step_g<4, false>(a, tmap, grid, st);
+    case 6: return a.FS ? cudaErrorInvalidValue : launch_step_g<6, false>(a, tmap, grid, st);
+    case 8: return a.FS ? cudaErrorInvalidValue : launch_step_g<8, false>(a, tmap, grid, st);
     default: return cudaErrorInvalidValue;
     }
 }

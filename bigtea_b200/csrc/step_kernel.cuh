@@ -29,6 +29,9 @@ struct LayerDev {
     const float *attn_norm, *q_norm, *k_norm, *ffn_norm, *gate_inp;
     const float *gate_bias;  // [NE] added to the router logits, or null
     QMatDev q, k, v, o, gate, up, down;
+    // the shared expert (C10), when the model has one (sgate.w != null): gate and up in the
+    // GEMV layout, down with one row per tile like the routed experts' down matrices
+    QMatDev sgate, sup, sdown;
 };
 
 struct StepArgs {
@@ -48,6 +51,8 @@ struct StepArgs {
     const int *block_table;
     int max_blocks, n_blocks, max_chunks;
     float *x, *ffn_in, *qkv, *att, *part, *rlog, *act;
+    int FS;         // shared expert width (0: none)
+    float *shact;   // [T][FS] SiLU(gate) * up of the shared expert
     int *dbg_ids;
     float *dbg_w;
     int TB;

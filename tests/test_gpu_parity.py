@@ -300,14 +300,20 @@ def test_cfg0_prefill_128_then_64_greedy_steps():
 
 
 # ------------------------------------------------------------------ the persistent step against the per-phase kernels
-def test_persistent_and_per_phase_steps_agree(tiny_cfg, tiny_weights):
+@pytest.mark.parametrize("shape", ["tiny", "tiny_sh"])
+def test_persistent_and_per_phase_steps_agree(tiny_cfg, tiny_weights, shape):
     """Single-token steps run as one cooperative kernel by default; the per-phase kernels
-    are the other implementation of the same contract. Both must equal the oracle."""
-    cfg = tiny_cfg
+    are the other implementation of the same contract. Both must equal the oracle (with and
+    without a shared expert)."""
+    if shape == "tiny":
+        cfg, weights = tiny_cfg, tiny_weights
+    else:
+        cfg = bt.config("tiny_sh", max_positions=1024)
+        weights = bt.synth_model(cfg, seed=8)
     prompt = np.random.default_rng(31).integers(0, cfg.n_vocab, 300)  # three attention chunks
     runs = {}
     for persistent in (1, 0):
-        e = bt.Engine(cfg, tiny_weights)
+        e = bt.Engine(cfg, weights)
         e.set_option("persistent", persistent)
         cache = bt.KvCache(e, max_positions=512, max_seqs=3)
         runner = bt.StreamingRunner(e)
@@ -320,7 +326,7 @@ def test_persistent_and_per_phase_steps_agree(tiny_cfg, tiny_weights):
     assert np.array_equal(bits(runs[0][1]), bits(runs[1][1]))
     for a, b in zip(runs[0][2], runs[1][2]):
         assert np.array_equal(a[0], b[0]) and np.array_equal(a[1], b[1])
-    model = orc.Model(cfg, tiny_weights)
+    model = orc.Model(cfg, weights)
     model.forward(prompt, 0)
     assert list(runs[1][0][:, 0]) == model.greedy(7, 5)
 
@@ -400,14 +406,16 @@ def test_batched_step_gqa_groups_match_oracle(n_head):
     e.close()
 
 
-@pytest.mark.parametrize("source", ["tensors", "synthetic"])
-def test_shared_expert_matches_oracle(source):
+@pytest.mark.parametrize("source,persistent", [("tensors", 1), ("tensors", 0), ("synthetic", 1)])
+def test_shared_expert_matches_oracle(source, persistent):
     """A model with a shared expert (DeepSeek-style, added unweighted to the routed sum): a
-    prefill, single-token steps, the greedy loop and a 12-sequence batched step (grouped
-    experts) give the oracle's bits."""
+    prefill, single-token steps (the persistent kernel, whose down units carry the shared
+    expert as one more expert, or the per-phase kernels), the greedy loop and a 12-sequence
+    batched step (grouped experts) give the oracle's bits."""
     cfg = bt.config("tiny_sh", max_positions=1024)
     W = bt.synth_model(cfg, seed=7)
     e = bt.Engine(cfg, W) if source == "tensors" else bt.Engine.synthetic(cfg, seed=7)
+    e.set_option("persistent", persistent)
     model = orc.Model(cfg, W)
     cache = bt.KvCache(e, max_positions=512)
     runner = bt.StreamingRunner(e)
