@@ -107,6 +107,8 @@ SIGNATURES = {
     "bt_expert_cache_stats": (C.c_int, [_P, C.POINTER(XCacheStats)]),
     "bt_expert_cache_simulate": (C.c_int, [C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _I32P,
                                            C.c_uint32, C.POINTER(XCacheStats)]),
+    "bt_expert_cache_simulate_device": (C.c_int, [C.c_int, C.c_uint32, C.c_uint32, C.c_uint32, C.c_uint32, _I32P,
+                                           C.c_uint32, C.POINTER(XCacheStats)]),
     "bt_engine_enable_ep": (C.c_int, [_P, _P, C.c_size_t, C.c_int, C.c_int]),
     # device pointers and a cudaStream_t, passed as integers
     "bt_op_gemv_noalloc": (C.c_int, [C.c_uint32, _P, C.c_uint32, C.c_uint32, _P, C.c_uint32, _P, _P]),

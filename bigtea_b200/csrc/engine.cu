@@ -26,6 +26,7 @@
 #include "kernels.cuh"
 #include "step_kernel.cuh"
 #include "expert_stream.cuh"
+#include "xcache_dev.cuh"
 
 using namespace bt;
 
@@ -161,6 +162,12 @@ struct bt_engine {
     int *x_sel_host = nullptr;      // pinned: a step's selections
     int *x_slot_host = nullptr;     // pinned [n_layer][NE]: staging of x_slot_dev
     cudaEvent_t x_ev = nullptr;
+    // the policy on the device (option "xcache_device", default 1): no host round trip per layer
+    bool xdev = true;
+    XcDev xd{};
+    DevBuf xd_buf;                            // the device policy's arrays
+    DevBuf x_copies, x_ncopies;               // a layer's slot copies
+    std::vector<const uint8_t *> x_host_dev;  // device addresses of x_host
     DevBuf ep_send_meta, ep_send_rows, ep_recv_meta, ep_recv_rows, ep_act, ep_dpart, ep_ret;
     DevBuf dbg_ids, dbg_w;  // [n_layer][TB][K]
     DevBuf tokens, seq_of, local_idx, pos_of, single, x_rows;
@@ -1486,6 +1493,63 @@ static int xcache_layer(bt_engine *e, int il, int T) {
     return BT_OK;
 }
 
+// The device policy's state for a new, empty cache: the same initial state as
+// ExpertCachePolicy (every slot free, popped in ascending order; the xorshift seed).
+static int xdev_init(DevBuf &buf, XcDev &x, int policy, int capacity, int n_layer, int n_expert, cudaStream_t st) {
+    const size_t LN = (size_t)n_layer * n_expert, C = (size_t)capacity;
+    x = XcDev{};
+    x.policy = policy;
+    x.cap = capacity;
+    x.NE = n_expert;
+    x.keycap = (int)(4 * LN);
+    const size_t bytes = LN * 4 + LN * 4 + C * 4 + C * 8 + C * 8 + C * 4 + (size_t)x.keycap * 4 + XC_NCTR * 4 +
+                         XC_N * 8 + 64;
+    CK(buf.alloc(bytes));
+    uint8_t *p = buf.as<uint8_t>();
+    auto take = [&p](size_t n) {
+        uint8_t *q = p;
+        p += (n + 7) & ~(size_t)7;
+        return q;
+    };
+    x.st = reinterpret_cast<unsigned long long *>(take(XC_N * 8));
+    x.last = reinterpret_cast<unsigned long long *>(take(C * 8));
+    x.inuse = reinterpret_cast<unsigned long long *>(take(C * 8));
+    x.slot_of = reinterpret_cast<int *>(take(LN * 4));
+    x.freq = reinterpret_cast<unsigned *>(take(LN * 4));
+    x.key_of = reinterpret_cast<int *>(take(C * 4));
+    x.free_list = reinterpret_cast<int *>(take(C * 4));
+    x.keys = reinterpret_cast<int *>(take((size_t)x.keycap * 4));
+    x.ctr = reinterpret_cast<int *>(take(XC_NCTR * 4));
+    CK(cudaMemsetAsync(buf.p, 0, bytes, st));
+    CK(cudaMemsetAsync(x.slot_of, 0xff, LN * 4, st));
+    CK(cudaMemsetAsync(x.key_of, 0xff, C * 4, st));
+    std::vector<int> fl(C);
+    for (size_t i = 0; i < C; i++) fl[i] = (int)(C - 1 - i);
+    const int ctr[XC_NCTR] = {capacity, 0, 0, 0};
+    const unsigned long long st0[XC_N] = {0, 0x9E3779B97F4A7C15ull, 0, 0, 0, 0, 0, 0};
+    CK(cudaMemcpyAsync(x.free_list, fl.data(), C * 4, cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(x.ctr, ctr, sizeof(ctr), cudaMemcpyHostToDevice, st));
+    CK(cudaMemcpyAsync(x.st, st0, sizeof(st0), cudaMemcpyHostToDevice, st));
+    CK(cudaStreamSynchronize(st));
+    return BT_OK;
+}
+
+// one layer of the device policy: lookup, then the slot copies from pinned host memory
+static int xcache_layer_dev(bt_engine *e, int il, int T, cudaStream_t st) {
+    const int K = (int)e->d.n_expert_used, NE = (int)e->d.n_expert;
+    const Layer &l = e->L[il];
+    const long long bytes = (long long)(l.gate.mat_bytes + l.up.mat_bytes + l.down.mat_bytes);
+    timer_begin(e, "xcache_lookup");
+    CK(launch_xcache_lookup(e->xd, il, e->sel_ids.as<int>(), T * K, e->x_slot_dev.as<int>() + (size_t)il * NE,
+                            e->x_host_dev[il], e->x_pool.as<uint8_t>(), e->x_stride, bytes, e->x_bounce,
+                            e->x_copies.as<XcCopy>(), e->x_ncopies.as<int>(), e->err.as<int>(), st));
+    timer_end(e);
+    timer_begin(e, "xcache_copy");
+    CK(launch_xcache_copy(e->x_copies.as<XcCopy>(), e->x_ncopies.as<int>(), bytes, 2 * e->n_sm, st));
+    timer_end(e);
+    return BT_OK;
+}
+
 // The tensor-core gate/up of the grouped path: Q4_K gate and up, whole 128-row blocks, and
 // shared memory for the chunk's operands.
 // The gate/up input rows (a.fn, `rows` of them) as Q8_K rows for the tensor-core gate/up.
@@ -1827,7 +1891,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             timer_end(e);
         }
         if (e->xcache) {
-            int xr = xcache_layer(e, (int)il, T);
+            int xr = e->xdev ? xcache_layer_dev(e, (int)il, T, st) : xcache_layer(e, (int)il, T);
             if (xr) return xr;
         }
         const int *x_slot = e->xcache ? e->x_slot_dev.as<int>() + (size_t)il * NE : nullptr;
@@ -1977,7 +2041,10 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             CK(launch_down_combine(a, st, false));
             timer_end(e);
         } else {
-            int r_ = launch_layer_experts(e, il, T, e->sel_ids.as<int>(), e->sel_w.as<float>(), x_slot, shexp, st, pdl);
+            // (with the device cache the weights come from the copy kernel just before: the expert
+            // kernels, which request weight tiles before their PDL wait, must not start early)
+            int r_ = launch_layer_experts(e, il, T, e->sel_ids.as<int>(), e->sel_w.as<float>(), x_slot, shexp, st,
+                                          pdl && !(e->xcache && e->xdev));
             if (r_) return r_;
         }
     }
@@ -2579,7 +2646,7 @@ extern "C" int bt_engine_enable_expert_cache(bt_engine *e, uint64_t cache_bytes,
         memset(e->x_slot_host, 0xff, (size_t)L * NE * 4);
         e->xpol = ExpertCachePolicy(policy, capacity, L, NE);
         e->xstats = XCacheStats();
-        return BT_OK;
+        return xdev_init(e->xd_buf, e->xd, policy, capacity, L, NE, e->st);
     }
     long long stride = 0;
     for (int il = 0; il < L; il++) {
@@ -2637,6 +2704,17 @@ extern "C" int bt_engine_enable_expert_cache(bt_engine *e, uint64_t cache_bytes,
     e->xstats = XCacheStats();
     e->x_stride = stride;
     e->x_bounce = bounce;
+    e->x_host_dev.assign(L, nullptr);
+    for (int il = 0; il < L; il++) {
+        void *dp = nullptr;
+        CK(cudaHostGetDevicePointer(&dp, host[il], 0));
+        e->x_host_dev[il] = reinterpret_cast<const uint8_t *>(dp);
+    }
+    CK(e->x_copies.alloc((size_t)(e->TB * K + bounce) * sizeof(XcCopy)));
+    CK(e->x_ncopies.alloc(16));
+    CK(cudaMemset(e->x_ncopies.p, 0, 16));
+    if (NE > XC_MAX_NE || e->TB * K > XC_MAX_SEL) e->xdev = false;  // beyond the device lookup's tables
+    if (int xr = xdev_init(e->xd_buf, e->xd, policy, capacity, L, NE, e->st)) return xr;
     e->xcache = true;
     e->mega = false;  // the host decides between the router and the experts: per-phase kernels
     for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
@@ -2655,10 +2733,70 @@ static void xcache_fill(const XCacheStats &s, int capacity, long long stride, bt
     out->slot_bytes = (uint64_t)stride;
 }
 
+static int xdev_stats(const XcDev &x, XCacheStats &s) {
+    unsigned long long v[XC_N];
+    CK(cudaMemcpy(v, x.st, sizeof(v), cudaMemcpyDeviceToHost));
+    s.hits = v[XC_HITS];
+    s.misses = v[XC_MISSES];
+    s.evictions = v[XC_EVICTIONS];
+    s.admissions = v[XC_ADMISSIONS];
+    s.bypasses = v[XC_BYPASSES];
+    s.bytes_copied = v[XC_BYTES];
+    return BT_OK;
+}
+
 extern "C" int bt_expert_cache_stats(const bt_engine *e, bt_xcache_stats *out) {
     if (!e || !out) return fail(BT_ERR_INVALID, "null argument");
     if (!e->xcache) return fail(BT_ERR_INVALID, "the expert cache is not enabled");
-    xcache_fill(e->xstats, e->xpol.capacity(), e->x_stride, out);
+    XCacheStats s = e->xstats;
+    if (e->xdev) {
+        CK(cudaSetDevice(e->device));
+        CK(cudaStreamSynchronize(e->st));
+        if (int r = xdev_stats(e->xd, s)) return r;
+    }
+    xcache_fill(s, e->xpol.capacity(), e->x_stride, out);
+    return BT_OK;
+}
+
+extern "C" int bt_expert_cache_simulate_device(int policy, uint32_t capacity, uint32_t n_layer, uint32_t n_expert,
+                                               uint32_t n_sel, const int32_t *trace, uint32_t n_steps,
+                                               bt_xcache_stats *out) {
+    if (!trace || !out || !capacity || !n_layer || !n_expert || !n_sel)
+        return fail(BT_ERR_INVALID, "bad argument");
+    if (policy != BT_XCACHE_LRU && policy != BT_XCACHE_FREQ) return fail(BT_ERR_INVALID, "unknown cache policy");
+    if (n_expert > (uint32_t)XC_MAX_NE || n_sel > (uint32_t)XC_MAX_SEL)
+        return fail(BT_ERR_UNSUPPORTED, "more experts or selections than the device lookup takes");
+    const size_t nt = (size_t)n_steps * n_layer * n_sel;
+    for (size_t i = 0; i < nt; i++)
+        if (trace[i] < 0 || (uint32_t)trace[i] >= n_expert) return fail(BT_ERR_INVALID, "expert id out of range");
+    cudaStream_t st;
+    CK(cudaStreamCreateWithFlags(&st, cudaStreamNonBlocking));
+    struct StreamGuard {
+        cudaStream_t s;
+        ~StreamGuard() { cudaStreamDestroy(s); }
+    } guard{st};
+    DevBuf buf, dtrace, rows, copies, nc, err;
+    XcDev x;
+    if (int r = xdev_init(buf, x, policy, (int)capacity, (int)n_layer, (int)n_expert, st)) return r;
+    CK(dtrace.alloc(nt * 4 + 4));
+    CK(rows.alloc((size_t)n_layer * n_expert * 4));
+    CK(copies.alloc((size_t)n_sel * sizeof(XcCopy)));
+    CK(nc.alloc(16));
+    CK(err.alloc(16));
+    CK(cudaMemsetAsync(err.p, 0, 16, st));
+    CK(cudaMemcpyAsync(dtrace.p, trace, nt * 4, cudaMemcpyHostToDevice, st));
+    for (uint32_t s = 0; s < n_steps; s++)
+        for (uint32_t il = 0; il < n_layer; il++)
+            CK(launch_xcache_lookup(x, (int)il, dtrace.as<int>() + ((size_t)s * n_layer + il) * n_sel, (int)n_sel,
+                                    rows.as<int>() + (size_t)il * n_expert, nullptr, nullptr, 0, 0, (int)n_sel,
+                                    copies.as<XcCopy>(), nc.as<int>(), err.as<int>(), st));
+    CK(cudaStreamSynchronize(st));
+    int herr = 0;
+    CK(cudaMemcpy(&herr, err.p, 4, cudaMemcpyDeviceToHost));
+    if (herr) return fail(BT_ERR_INVALID, "the device lookup rejected the trace");
+    XCacheStats sres;
+    if (int r = xdev_stats(x, sres)) return r;
+    xcache_fill(sres, (int)capacity, 0, out);
     return BT_OK;
 }
 
@@ -2824,6 +2962,13 @@ extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
         for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);  // the values are baked into captured launches
         e->graphs.clear();
         return BT_OK;
+    }
+    if (!strcmp(name, "xcache_device")) {
+        e->xdev = value != 0;
+        if (!e->xcache) return BT_OK;
+        if (e->d.n_expert > (uint32_t)XC_MAX_NE || e->TB * (int)e->d.n_expert_used > XC_MAX_SEL) e->xdev = false;
+        // the two policies keep separate state: switching starts a new, empty cache
+        return bt_engine_enable_expert_cache(e, (uint64_t)e->xpol.capacity() * (uint64_t)e->x_stride, e->xd.policy);
     }
     if (!strcmp(name, "stream_slots")) {
         if (value < 0) return fail(BT_ERR_INVALID, "stream_slots must be >= 0");

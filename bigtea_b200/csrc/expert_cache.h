@@ -13,6 +13,9 @@
 //           the newcomer has strictly more uses; otherwise the expert is served from a
 //           transient bounce slot and not cached.
 // Entries the current layer uses are never evicted while it runs (their slots are being read).
+// The list of admitted keys holds at most 4 * n_layer * n_expert entries: a push onto a full
+// list first drops its stale keys, keeping the order. xcache.cu makes the same decisions on the
+// device.
 #pragma once
 
 #include <stdint.h>
@@ -31,7 +34,8 @@ class ExpertCachePolicy {
     ExpertCachePolicy() = default;
     ExpertCachePolicy(int policy, int capacity, int n_layer, int n_expert)
         : policy_(policy), cap_(capacity), NE_(n_expert), slot_of_((size_t)n_layer * n_expert, -1),
-          freq_((size_t)n_layer * n_expert, 0), key_of_(capacity, -1), last_(capacity, 0), inuse_(capacity, 0) {
+          freq_((size_t)n_layer * n_expert, 0), key_of_(capacity, -1), last_(capacity, 0), inuse_(capacity, 0),
+          keycap_((size_t)4 * n_layer * n_expert) {
         for (int s = capacity - 1; s >= 0; s--) free_.push_back(s);
     }
 
@@ -66,7 +70,15 @@ class ExpertCachePolicy {
             key_of_[s] = key;
             last_[s] = tick_;
             inuse_[s] = tick_;
-            keys_.push_back(key);
+            if (policy_ == FREQ) {  // (only the admission sample reads the list)
+                if (keys_.size() == keycap_) {  // full: drop the stale keys, in order
+                    size_t m = 0;
+                    for (size_t q = 0; q < keys_.size(); q++)
+                        if (slot_of_[keys_[q]] >= 0) keys_[m++] = keys_[q];
+                    keys_.resize(m);
+                }
+                keys_.push_back(key);
+            }
             st.admissions++;
             out_slot[i] = s;
             copy_needed[i] = true;
@@ -141,7 +153,8 @@ class ExpertCachePolicy {
     std::vector<uint64_t> last_;  // slot -> tick of its last use
     std::vector<uint64_t> inuse_; // slot -> tick of the layer using it
     std::vector<int> free_;       // never-used slots
-    std::vector<int> keys_;       // admitted keys (may hold stale ones)
+    std::vector<int> keys_;       // admitted keys (may hold stale ones), at most keycap_
+    size_t keycap_ = 0;
     uint64_t tick_ = 0, rng_ = 0x9E3779B97F4A7C15ull;
 };
 

@@ -216,14 +216,17 @@ class KvCache:
         check(lib.bt_kv_import_layer(self.h, seq, layer, _lib.ptr(k), _lib.ptr(v), k.nbytes))
 
 
-def simulate_expert_cache(policy: str, capacity: int, trace: np.ndarray) -> dict:
-    """The expert-cache policy alone on a selection trace [steps, layers, n_sel] (host only)."""
+def simulate_expert_cache(policy: str, capacity: int, trace: np.ndarray, device: bool = False,
+                          n_expert: int | None = None) -> dict:
+    """The expert-cache policy alone on a selection trace [steps, layers, n_sel]: on the host
+    (bt_expert_cache_simulate), or through the device lookup kernel (device=True)."""
     tr = np.ascontiguousarray(trace, dtype=np.int32)
     steps, n_layer, n_sel = tr.shape
     s = _lib.XCacheStats()
     pol = {"lru": _lib.XCACHE_LRU, "freq": _lib.XCACHE_FREQ}[policy]
-    check(lib.bt_expert_cache_simulate(pol, capacity, n_layer, int(tr.max()) + 1, n_sel, _lib.ptr(tr, C.c_int32),
-                                       steps, C.byref(s)))
+    fn = lib.bt_expert_cache_simulate_device if device else lib.bt_expert_cache_simulate
+    ne = n_expert if n_expert is not None else int(tr.max()) + 1
+    check(fn(pol, capacity, n_layer, ne, n_sel, _lib.ptr(tr, C.c_int32), steps, C.byref(s)))
     return {k: getattr(s, k) for k, _ in s._fields_}
 
 

@@ -181,7 +181,10 @@ int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const ui
  * at 0): in layer fault_copy - 1, CTA fault_cta requests none of its expert tiles, so its own
  * waits run out and it takes the failure exit (barrier poisoned, its copies drained);
  * "stream_slots" (ring slots of bt_bench_experts' stream kernel, default 0 = as many as fit in
- * 160 KB of shared memory). */
+ * 160 KB of shared memory); "xcache_device" (the expert cache's policy runs on the device after
+ * each layer's router and fills missed slots from the pinned host copies with a kernel, so a
+ * step needs no host round trip per layer; default 1; 0 = the host decides each layer; a
+ * change starts a new, empty cache). */
 int bt_set_option(bt_engine *e, const char *name, int value);
 
 /* Router bias of one layer: n == n_expert F32 values added to the router logits before the
@@ -214,6 +217,11 @@ int bt_expert_cache_stats(const bt_engine *e, bt_xcache_stats *out);
  * (layer-major within a step), looked up in order; no device is touched */
 int bt_expert_cache_simulate(int policy, uint32_t capacity, uint32_t n_layer, uint32_t n_expert, uint32_t n_sel,
                              const int32_t *trace, uint32_t n_steps, bt_xcache_stats *out);
+/* the same trace through the device policy (the lookup kernel an engine with the option
+ * "xcache_device" runs after each layer's router) on the current device: the same counts as
+ * bt_expert_cache_simulate; n_expert <= 1024, n_sel <= 1024 */
+int bt_expert_cache_simulate_device(int policy, uint32_t capacity, uint32_t n_layer, uint32_t n_expert,
+                                    uint32_t n_sel, const int32_t *trace, uint32_t n_steps, bt_xcache_stats *out);
 
 /* ---- expert parallelism (batched decode over the GPUs of one node) ----
  * No counterpart in the reference, which has no distributed code. One engine per GPU, one

@@ -15,10 +15,14 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("policy", ["lru", "freq"])
-def test_expert_cache_matches_oracle(policy):
+@pytest.mark.parametrize("on_device", [1, 0])
+def test_expert_cache_matches_oracle(policy, on_device):
+    """The policy on the device (lookup and copy kernels after each router, no host round trip)
+    or on the host: the oracle's bits either way."""
     cfg = bt.config("tiny", router_zipf=1.1, max_positions=512)
     W = bt.synth_model(cfg, seed=7)
     e = bt.Engine(cfg, W)
+    e.set_option("xcache_device", on_device)
     per_expert = sum(len(W[f"blk.0.{n}.weight"][2]) for n in ("ffn_gate_exps", "ffn_up_exps", "ffn_down_exps"))
     per_expert //= cfg.n_expert
     e.enable_expert_cache(10 * (per_expert + 4096), policy)  # about 10 of the 32 (layer, expert) pairs
@@ -79,3 +83,46 @@ def test_expert_cache_batched_step_matches_oracle():
         assert np.array_equal(bits(got[s]), bits(want))
     cache.close()
     e.close()
+
+
+@pytest.mark.parametrize("policy", ["lru", "freq"])
+def test_device_and_host_policies_decide_alike_in_an_engine(policy):
+    """The same prefill and decode steps under the device policy and the host policy: the same
+    hit, miss, eviction, admission and bypass counts and copied bytes."""
+    cfg = bt.config("tiny", router_zipf=1.1, max_positions=512)
+    W = bt.synth_model(cfg, seed=9)
+    stats = {}
+    for on_device in (1, 0):
+        e = bt.Engine(cfg, W)
+        e.set_option("xcache_device", on_device)
+        e.enable_expert_cache(2 << 20, policy)  # about 9 slots
+        cache = bt.KvCache(e, max_positions=256, max_seqs=3)
+        runner = bt.StreamingRunner(e)
+        rng = np.random.default_rng(5)
+        runner.forward_batch(cache, [0, 1, 2], [rng.integers(0, cfg.n_vocab, n) for n in (17, 9, 30)], [0, 0, 0])
+        runner.generate_greedy(cache, [3, 5, 7], 8, seqs=[0, 1, 2])
+        stats[on_device] = e.expert_cache_stats()
+        cache.close()
+        e.close()
+    assert stats[1] == stats[0]
+    assert stats[1]["misses"] > 0 and stats[1]["evictions"] + stats[1]["bypasses"] > 0
+
+
+def _trace(steps, n_layer, n_expert, n_sel, seed):
+    """seeded skewed selections with repeats inside a layer's group (several tokens)"""
+    rng = np.random.default_rng(seed)
+    p = (rng.permutation(n_expert) + 1.0) ** -1.1
+    return rng.choice(n_expert, size=(steps, n_layer, n_sel), p=p / p.sum()).astype(np.int32)
+
+
+@pytest.mark.parametrize("policy", ["lru", "freq"])
+@pytest.mark.parametrize("capacity,n_sel", [(6, 12), (16, 8), (60, 8), (200, 24)])
+def test_device_policy_equals_host_policy(policy, capacity, n_sel):
+    """bt_expert_cache_simulate_device runs the lookup kernel over a trace: every count equals
+    the host policy's (which a CPU test pins to a Python restatement), including the cases where
+    every slot is pinned by the layer and experts are served from bounce slots."""
+    trace = _trace(50, 6, 48, n_sel, seed=capacity + n_sel)
+    host = bt.runner.simulate_expert_cache(policy, capacity, trace, n_expert=48)
+    dev = bt.runner.simulate_expert_cache(policy, capacity, trace, device=True, n_expert=48)
+    assert dev == host
+    assert host["misses"] > 0 and host["evictions"] + host["bypasses"] > 0
