@@ -470,8 +470,9 @@ def run_ours(args, rank, world, local_rank):
         xcache = {"steps": args.xcache_steps, "batch": 1,
                   "experts_bytes": int(cfg.n_layer * cfg.n_expert * expert_bytes(cfg, per_expert=True)),
                   "timing": (f"decode steps after a {args.xcache_prompt}-token prefill of seeded uniform ids: wall "
-                             "clock of bt_forward per token (host token in, logits out, one host round trip per "
-                             "layer for the cache decisions); hit rate over the decode steps")}
+                             "clock of bt_forward per token (host token in, logits out; the cache policy on the "
+                             "device inside the persistent step: CTA 0 looks each layer's experts up, every CTA "
+                             "fills missed slots from pinned host memory); hit rate over the decode steps")}
         rngx = np.random.default_rng(args.seed + 3)
         prompt_x = rngx.integers(0, cfg.n_vocab, args.xcache_prompt)
         toks_x = rngx.integers(0, cfg.n_vocab, args.xcache_steps)

@@ -168,6 +168,7 @@ struct bt_engine {
     DevBuf xd_buf;                            // the device policy's arrays
     DevBuf x_copies, x_ncopies;               // a layer's slot copies
     std::vector<const uint8_t *> x_host_dev;  // device addresses of x_host
+    DevBuf x_host_devarr;                     // the same, in device memory
     DevBuf ep_send_meta, ep_send_rows, ep_recv_meta, ep_recv_rows, ep_act, ep_dpart, ep_ret;
     DevBuf dbg_ids, dbg_w;  // [n_layer][TB][K]
     DevBuf tokens, seq_of, local_idx, pos_of, single, x_rows;
@@ -1342,7 +1343,11 @@ static int upload_plan(bt_engine *e, const StepPlan &p) {
 // Can this step run as one persistent kernel? Single-token steps of up to STEP_MAX_T
 // sequences whose activations fit the kernel's shared memory.
 static bool step_eligible(const bt_engine *e, const bt_kv *kv, const StepPlan &p) {
-    if (!e->mega || e->ep || e->xcache || p.T > STEP_MAX_T || p.out_first != 0 || (int)p.x_rows.size() != p.T) return false;
+    // (the expert cache: only with the device policy, and without a shared expert)
+    if (e->xcache && (!e->xdev || e->d.n_ff_shexp || (e->d.n_head != 4 * e->d.n_head_kv &&
+                                                     e->d.n_head != 8 * e->d.n_head_kv)))
+        return false;
+    if (!e->mega || e->ep || p.T > STEP_MAX_T || p.out_first != 0 || (int)p.x_rows.size() != p.T) return false;
     for (int t = 0; t < p.T; t++)
         if (!p.single[t] || p.local_idx[t] != 0 || p.x_rows[t] != t || p.st_lrow[t] != t) return false;
     if ((int)p.st_seq.size() != p.T) return false;
@@ -1426,6 +1431,17 @@ static int launch_persistent_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bo
     a.n_out = p.T;
     a.FS = (int)e->d.n_ff_shexp;
     a.shact = e->d.n_ff_shexp ? e->sh_act.as<float>() : nullptr;
+    a.xc_on = e->xcache ? 1 : 0;
+    if (e->xcache) {
+        a.xd = e->xd;
+        a.xc_host = e->x_host_devarr.as<const uint8_t *>();
+        a.xc_pool = e->x_pool.as<uint8_t>();
+        a.xc_stride = e->x_stride;
+        a.xc_bounce = e->x_bounce;
+        a.xc_copies = e->x_copies.as<XcCopy>();
+        a.xc_ncopies = e->x_ncopies.as<int>();
+        a.xc_rows = e->x_slot_dev.as<int>();
+    }
     a.bar = e->gbar.as<unsigned>();
     a.err = e->err.as<int>();
     a.wait_limit = WAIT_LIMIT_CYCLES;
@@ -2710,13 +2726,14 @@ extern "C" int bt_engine_enable_expert_cache(bt_engine *e, uint64_t cache_bytes,
         CK(cudaHostGetDevicePointer(&dp, host[il], 0));
         e->x_host_dev[il] = reinterpret_cast<const uint8_t *>(dp);
     }
+    CK(e->x_host_devarr.alloc((size_t)L * sizeof(void *)));
+    CK(cudaMemcpy(e->x_host_devarr.p, e->x_host_dev.data(), (size_t)L * sizeof(void *), cudaMemcpyHostToDevice));
     CK(e->x_copies.alloc((size_t)(e->TB * K + bounce) * sizeof(XcCopy)));
     CK(e->x_ncopies.alloc(16));
     CK(cudaMemset(e->x_ncopies.p, 0, 16));
     if (NE > XC_MAX_NE || e->TB * K > XC_MAX_SEL) e->xdev = false;  // beyond the device lookup's tables
     if (int xr = xdev_init(e->xd_buf, e->xd, policy, capacity, L, NE, e->st)) return xr;
-    e->xcache = true;
-    e->mega = false;  // the host decides between the router and the experts: per-phase kernels
+    e->xcache = true;  // (the persistent step runs with it when the policy is on the device)
     for (auto &g : e->graphs) cudaGraphExecDestroy(g.second);
     e->graphs.clear();
     return BT_OK;

@@ -33,6 +33,7 @@
 #include "kernels.cuh"
 #include "stage.cuh"
 #include "step_kernel.cuh"
+#include "xcache_cta.cuh"
 
 namespace bt {
 
@@ -47,6 +48,7 @@ constexpr int STEP_HDR_BYTES = 1024 + ((2 * (int)sizeof(LayerDev) + (int)sizeof(
 static_assert(LD_WORDS <= 256, "a layer descriptor is copied by one thread per word");
 static_assert(sizeof(LayerDev) % 4 == 0, "layer descriptors are copied word by word");
 static_assert(STEP_RES == STEP_THREADS, "one residual value per thread");
+static_assert(XC_SCRATCH_BYTES <= STEP_CBUF_BYTES, "the cache lookup's scratch fits the combine buffer");
 
 // ------------------------------------------------------------------ shared memory map
 struct StepSmem {
@@ -65,6 +67,7 @@ struct StepSmem {
     QMatDev *outd;       // the output head's descriptor
     int *sel_ids;        // [STEP_MAX_T][MAX_K]
     float *sel_w;        // [STEP_MAX_T][MAX_K]
+    int *sel_slot;       // [STEP_MAX_T][MAX_K] the selected experts' cache slots (expert cache)
     float *wv;           // [STEP_WARPS][MAX_K] expert row values of the down phase
     float *cbuf;         // norm vector / router probabilities / combine scratch, STEP_CBUF_BYTES
     float *res;          // [STEP_RES] residual values of this CTA's output rows
@@ -457,9 +460,9 @@ __device__ __forceinline__ bool gemv_run(WarpRing &r, const SegList &s, const Ac
 // ------------------------------------------------------------------ expert phases
 // unit u of the gate/up phase: units below nr are (token, slot, tile) of the routed experts,
 // the rest (token, tile) of the shared expert
-template <bool SH>
+template <bool SH, bool XC>
 __device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int nr, int u0, int warp,
-                             int lane, bool drill) {
+                             int lane, bool drill, const uint8_t *pool, long long stride) {
     const int j = r.issued;
     if (drill) {  // the failure drill: the slot is counted as requested, but nothing will land
         r.issued++;
@@ -474,15 +477,17 @@ __device__ void gateup_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm,
     } else {
         const int tk = u / G.n_tiles;
         tile = u - tk * G.n_tiles;
-        e = sm.sel_ids[(tk / K) * MAX_K + tk % K];
+        e = (XC ? sm.sel_slot : sm.sel_ids)[(tk / K) * MAX_K + tk % K];
     }
     uint8_t *dst = r.slot_ptr(j);
     if (lane == 0) mbar_arrive_expect_tx(r.slot_bar(j), G.tile_bytes + U.tile_bytes);
     __syncwarp();
     if (lane < 2) {  // lane 0 the gate tile, lane 1 the up tile
         const QMatDev &m = lane ? U : G;
-        bulk_g2s_hint(dst + lane * G.tile_bytes, m.w + e * m.mat_bytes + (long long)tile * m.tile_bytes,
-                      m.tile_bytes, r.slot_bar(j), l2_evict_first_policy());
+        // resident: expert e of the matrix; cached: slot e of the pool, gate then up
+        const uint8_t *src = XC && !sh ? pool + e * stride + (lane ? G.mat_bytes : 0) : m.w + e * m.mat_bytes;
+        bulk_g2s_hint(dst + lane * G.tile_bytes, src + (long long)tile * m.tile_bytes, m.tile_bytes, r.slot_bar(j),
+                      l2_evict_first_policy());
     }
     r.issued++;
 }
@@ -532,9 +537,9 @@ __device__ __forceinline__ int down_row_bytes(const LayerDev &L) {
 
 // this warp's j-th down unit (unit warp + j * STEP_WARPS of nk experts per piece; expert index K
 // is the shared expert): lane 0 requests it
-template <bool SH>
+template <bool SH, bool XC>
 __device__ void down_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, int K, int nk, int E, int d0, int d1,
-                           int maxr, int warp, int lane) {
+                           int maxr, int warp, int lane, const uint8_t *pool, long long stride) {
     const int j = r.issued;
     const int i = warp + j * STEP_WARPS, q = i / nk, k = i - q * nk;
     int t, r0, nr, off;
@@ -542,10 +547,12 @@ __device__ void down_issue(WarpRing &r, const LayerDev &L, const StepSmem &sm, i
     if (lane == 0) {
         const bool shx = SH && k == K;
         const QMatDev &m = shx ? L.sdown : L.down;
-        const int e = shx ? 0 : sm.sel_ids[t * MAX_K + k];
+        const int e = shx ? 0 : (XC ? sm.sel_slot : sm.sel_ids)[t * MAX_K + k];
+        // resident: expert e of the matrix; cached: slot e of the pool, after its gate and up
+        const uint8_t *src = XC && !shx ? pool + e * stride + L.gate.mat_bytes + L.up.mat_bytes : m.w + e * m.mat_bytes;
         mbar_arrive_expect_tx(r.slot_bar(j), nr * m.tile_bytes);
-        bulk_g2s_hint(r.slot_ptr(j), m.w + e * m.mat_bytes + (long long)r0 * m.tile_bytes, nr * m.tile_bytes,
-                      r.slot_bar(j), l2_evict_first_policy());
+        bulk_g2s_hint(r.slot_ptr(j), src + (long long)r0 * m.tile_bytes, nr * m.tile_bytes, r.slot_bar(j),
+                      l2_evict_first_policy());
     }
     __syncwarp();
     r.issued++;
@@ -1061,7 +1068,7 @@ __device__ __noinline__ void step_fail_exit(unsigned *bar, long long limit, uint
 }
 
 // ------------------------------------------------------------------ the kernel
-template <int G, bool SH>
+template <int G, bool SH, bool XC>
 __global__ void __launch_bounds__(STEP_THREADS, 1)
     decode_step_kernel(const __grid_constant__ StepArgs p, const __grid_constant__ CUtensorMap tmap) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -1083,7 +1090,8 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
     sm.act = reinterpret_cast<ActBlock *>(sm.region + STEP_REGION_BYTES);
     sm.sel_ids = reinterpret_cast<int *>(reinterpret_cast<uint8_t *>(sm.act) + STEP_ACT_BYTES);
     sm.sel_w = reinterpret_cast<float *>(sm.sel_ids + STEP_MAX_T * MAX_K);
-    sm.wv = sm.sel_w + STEP_MAX_T * MAX_K;
+    sm.sel_slot = reinterpret_cast<int *>(sm.sel_w + STEP_MAX_T * MAX_K);
+    sm.wv = reinterpret_cast<float *>(sm.sel_slot + STEP_MAX_T * MAX_K);
     sm.cbuf = sm.wv + STEP_WARPS * MAX_K;
     sm.res = sm.cbuf + STEP_CBUF_BYTES / 4;
 
@@ -1456,6 +1464,36 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             }
             __syncthreads();
         }
+        if constexpr (XC) {
+            // the expert cache: CTA 0 looks the layer's selections up (the device policy); once
+            // every CTA has the slots, each fills its share of the missed ones from the pinned
+            // host blocks, and a second barrier orders those copies before the tile requests
+            const long long xbytes = L.gate.mat_bytes + L.up.mat_bytes + L.down.mat_bytes;
+            if (blockIdx.x == 0)
+                xc_lookup_cta(p.xd, il, sm.sel_ids, T, K, MAX_K, p.xc_rows + (long long)il * p.NE, p.xc_host[il],
+                              p.xc_pool, p.xc_stride, xbytes, p.xc_bounce, p.xc_copies, p.xc_ncopies, p.err,
+                              xc_scratch(sm.cbuf));
+            if (const int gs_ = grid_sync(p.bar, p.err, p.wait_limit, p.fault_cta, p.fault_barrier, ++epoch, false,
+                                          nullptr))
+                STEP_FAIL(gs_ == 2);
+            const int nc = __ldcg(p.xc_ncopies);
+            if (nc > 0) {
+                xc_copy_part(p.xc_copies, nc, xbytes, (long long)blockIdx.x * STEP_THREADS + tid,
+                             (long long)gridDim.x * STEP_THREADS);
+                if (const int gs_ = grid_sync(p.bar, p.err, p.wait_limit, p.fault_cta, p.fault_barrier, ++epoch,
+                                              false, nullptr))
+                    STEP_FAIL(gs_ == 2);
+                // the slots were written through the generic proxy; the tile copies read them
+                // through the async proxy
+                asm volatile("fence.proxy.async.global;" ::: "memory");
+            }
+            if (tid < T * K) {
+                const int t = tid / K, k = tid - t * K;
+                sm.sel_slot[t * MAX_K + k] =
+                    __ldcg(p.xc_rows + (long long)il * p.NE + sm.sel_ids[t * MAX_K + k]);
+            }
+            __syncthreads();
+        }
         POINT(il, 4);
         {
             // routed units (token, slot, tile), then the shared expert's (token, tile)
@@ -1472,12 +1510,13 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             const bool rgq4 = L.gate.type == T_Q4_K, ruq4 = L.up.type == T_Q4_K;
             const bool sgq4 = L.sgate.type == T_Q4_K, suq4 = L.sup.type == T_Q4_K;
             const bool drill = p.fault_copy == il + 1 && p.fault_cta == (int)blockIdx.x;
-            while (ring.issued < n && ring.can_issue()) gateup_issue<SH>(ring, L, sm, K, nr, u0, warp, lane, drill);
+            while (ring.issued < n && ring.can_issue())
+                gateup_issue<SH, XC>(ring, L, sm, K, nr, u0, warp, lane, drill, p.xc_pool, p.xc_stride);
             CYC_RESET();
             long long gcw = 0, gc0 = clock64();
             for (int j = 0; j < n; j++) {
                 while (ring.issued < n && ring.can_issue())
-                    gateup_issue<SH>(ring, L, sm, K, nr, u0, warp, lane, drill);
+                    gateup_issue<SH, XC>(ring, L, sm, K, nr, u0, warp, lane, drill, p.xc_pool, p.xc_stride);
                 const long long w0 = clock64();
                 if (!ring.wait(j, p.err, p.wait_limit)) {
                     bad = true;
@@ -1542,7 +1581,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
                 const int dn = nt > warp ? (nt - warp + STEP_WARPS - 1) / STEP_WARPS : 0;
                 ring.configure(maxr * dtb);
                 while (ring.issued < dn && ring.can_issue())
-                    down_issue<SH>(ring, L, sm, K, nk, E, d0, d1, maxr, warp, lane);
+                    down_issue<SH, XC>(ring, L, sm, K, nk, E, d0, d1, maxr, warp, lane, p.xc_pool, p.xc_stride);
             }
         }
         // the down phase's residual rows (ffn_in, final since the O barrier)
@@ -1568,7 +1607,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
             long long dcw = 0, dc0 = clock64();
             for (int j = 0; j < n; j++) {
                 while (ring.issued < n && ring.can_issue())
-                    down_issue<SH>(ring, L, sm, K, nk, E, d0, d1, maxr, warp, lane);
+                    down_issue<SH, XC>(ring, L, sm, K, nk, E, d0, d1, maxr, warp, lane, p.xc_pool, p.xc_stride);
                 const int i = warp + j * STEP_WARPS, q = i / nk, k = i - q * nk;
                 int t, r0, nr, off;
                 down_piece(d0, d1, E, maxr, q, t, r0, nr, off);
@@ -1692,7 +1731,7 @@ __global__ void __launch_bounds__(STEP_THREADS, 1)
 
 size_t step_smem_bytes(int max_chunks) {
     (void)max_chunks;
-    return 1024 + STEP_HDR_BYTES + STEP_REGION_BYTES + STEP_ACT_BYTES + (size_t)STEP_MAX_T * MAX_K * 8 +
+    return 1024 + STEP_HDR_BYTES + STEP_REGION_BYTES + STEP_ACT_BYTES + (size_t)STEP_MAX_T * MAX_K * 12 +
            (size_t)STEP_WARPS * MAX_K * 4 + STEP_CBUF_BYTES + (size_t)STEP_RES * 4;
 }
 
@@ -1701,9 +1740,13 @@ cudaError_t init_step_kernel_attributes() {
     cudaError_t e;
     if ((e = cudaGetDevice(&dev))) return e;
     if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
-    const void *kerns[] = {(const void *)decode_step_kernel<2, false>, (const void *)decode_step_kernel<4, false>,
-                           (const void *)decode_step_kernel<6, false>, (const void *)decode_step_kernel<8, false>,
-                           (const void *)decode_step_kernel<4, true>};
+    const void *kerns[] = {(const void *)decode_step_kernel<2, false, false>,
+                           (const void *)decode_step_kernel<4, false, false>,
+                           (const void *)decode_step_kernel<6, false, false>,
+                           (const void *)decode_step_kernel<8, false, false>,
+                           (const void *)decode_step_kernel<4, true, false>,
+                           (const void *)decode_step_kernel<4, false, true>,
+                           (const void *)decode_step_kernel<8, false, true>};
     for (const void *k : kerns) {
         cudaFuncAttributes fa;
         if ((e = cudaFuncGetAttributes(&fa, k))) return e;
@@ -1713,7 +1756,7 @@ cudaError_t init_step_kernel_attributes() {
     return cudaSuccess;
 }
 
-template <int G, bool SH>
+template <int G, bool SH, bool XC>
 static cudaError_t launch_step_g(const StepArgs &a, const CUtensorMap &tmap, int grid, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
@@ -1725,15 +1768,22 @@ static cudaError_t launch_step_g(const StepArgs &a, const CUtensorMap &tmap, int
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, decode_step_kernel<G, SH>, a, tmap);
+    return cudaLaunchKernelEx(&cfg, decode_step_kernel<G, SH, XC>, a, tmap);
 }
 
 cudaError_t launch_decode_step(const StepArgs &a, const CUtensorMap &tmap, int grid, cudaStream_t st) {
+    if (a.xc_on && a.FS) return cudaErrorInvalidValue;  // no instantiation carries both
     switch (a.G) {
-    case 2: return a.FS ? cudaErrorInvalidValue : launch_step_g<2, false>(a, tmap, grid, st);
-    case 4: return a.FS ? launch_step_g<4, true>(a, tmap, grid, st) : launch_step_g<4, false>(a, tmap, grid, st);
-    case 6: return a.FS ? cudaErrorInvalidValue : launch_step_g<6, false>(a, tmap, grid, st);
-    case 8: return a.FS ? cudaErrorInvalidValue : launch_step_g<8, false>(a, tmap, grid, st);
+    case 2: return a.FS || a.xc_on ? cudaErrorInvalidValue : launch_step_g<2, false, false>(a, tmap, grid, st);
+    case 4:
+        return a.FS      ? launch_step_g<4, true, false>(a, tmap, grid, st)
+               : a.xc_on ? launch_step_g<4, false, true>(a, tmap, grid, st)
+                         : launch_step_g<4, false, false>(a, tmap, grid, st);
+    case 6: return a.FS || a.xc_on ? cudaErrorInvalidValue : launch_step_g<6, false, false>(a, tmap, grid, st);
+    case 8:
+        return a.FS      ? cudaErrorInvalidValue
+               : a.xc_on ? launch_step_g<8, false, true>(a, tmap, grid, st)
+                         : launch_step_g<8, false, false>(a, tmap, grid, st);
     default: return cudaErrorInvalidValue;
     }
 }

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "xcache_dev.cuh"
+
 namespace bt {
 
 constexpr int STEP_MAX_T = 4;                    // sequences one persistent step carries
@@ -53,6 +55,18 @@ struct StepArgs {
     float *x, *ffn_in, *qkv, *att, *part, *rlog, *act;
     int FS;         // shared expert width (0: none)
     float *shact;   // [T][FS] SiLU(gate) * up of the shared expert
+    // the expert cache with its policy on the device (xc_on): after each layer's routing, CTA 0
+    // looks the selected experts up, every CTA fills missed slots from the pinned host blocks,
+    // and the expert tiles come from the slot pool (slot: gate | up | down of one expert)
+    int xc_on;
+    XcDev xd;
+    const uint8_t *const *xc_host;  // [n_layer] device addresses of the experts' host blocks
+    uint8_t *xc_pool;
+    long long xc_stride;
+    int xc_bounce;
+    XcCopy *xc_copies;
+    int *xc_ncopies;
+    int *xc_rows;  // [n_layer][NE] each expert's slot (rows written by the lookups)
     int *dbg_ids;
     float *dbg_w;
     int TB;

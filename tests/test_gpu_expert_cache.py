@@ -15,14 +15,16 @@ pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("policy", ["lru", "freq"])
-@pytest.mark.parametrize("on_device", [1, 0])
-def test_expert_cache_matches_oracle(policy, on_device):
-    """The policy on the device (lookup and copy kernels after each router, no host round trip)
-    or on the host: the oracle's bits either way."""
+@pytest.mark.parametrize("on_device,persistent", [(1, 1), (1, 0), (0, 1)])
+def test_expert_cache_matches_oracle(policy, on_device, persistent):
+    """The policy on the device -- inside the persistent step (CTA 0 looks up, every CTA copies
+    missed slots) or as lookup and copy kernels between the per-phase kernels -- or on the host
+    (per-phase kernels): the oracle's bits every way."""
     cfg = bt.config("tiny", router_zipf=1.1, max_positions=512)
     W = bt.synth_model(cfg, seed=7)
     e = bt.Engine(cfg, W)
     e.set_option("xcache_device", on_device)
+    e.set_option("persistent", persistent)
     per_expert = sum(len(W[f"blk.0.{n}.weight"][2]) for n in ("ffn_gate_exps", "ffn_up_exps", "ffn_down_exps"))
     per_expert //= cfg.n_expert
     e.enable_expert_cache(10 * (per_expert + 4096), policy)  # about 10 of the 32 (layer, expert) pairs
@@ -94,7 +96,7 @@ def test_device_and_host_policies_decide_alike_in_an_engine(policy):
     stats = {}
     for on_device in (1, 0):
         e = bt.Engine(cfg, W)
-        e.set_option("xcache_device", on_device)
+        e.set_option("xcache_device", on_device)  # (1: the persistent step's lookups)
         e.enable_expert_cache(2 << 20, policy)  # about 9 slots
         cache = bt.KvCache(e, max_positions=256, max_seqs=3)
         runner = bt.StreamingRunner(e)
