@@ -12,13 +12,16 @@ of uniform-random token ids into the f16 paged KV cache. A step = one decode tok
   cpu_baseline  the CPU oracle decoding from the same weights and cache on the host cores
   parity     the first measured decode step's logits against the CPU oracle from the same
              weights and cache, bit for bit (a mismatch fails the run)
-  expert_gemv  the routed experts' kernels alone, every layer in turn (bt_bench_experts), at
-             batch 1 and at the batched leg's batch: HBM GB/s of the distinct expert weights
-  expert_cache  experts moved to pinned host memory behind an HBM cache, a fresh sequence:
-             128-token prefill then 128 batch-1 decode steps of seeded uniform ids; LRU and
-             frequency-gated admission, each from a cold cache: decode tok/s and hit rate, for
-             the log-Zipf router bias at the cfg4 ratio of cache to experts (6.26 GiB), the same
-             bias with a third of that cache, and no bias at 6.26 GiB
+  expert_gemv  the routed experts' arithmetic alone over every layer (bt_bench_experts): the
+             per-layer kernels at batch 1 and at the batched leg's batch, and the multi-layer
+             stream kernel at batch 1 (checked bit for bit against the per-layer kernels): HBM
+             GB/s of the distinct expert weights
+  expert_cache  experts moved to pinned host memory behind an HBM cache (the policy on the
+             device, inside the persistent step), a fresh sequence: 128-token prefill then 128
+             batch-1 decode steps of seeded uniform ids; LRU and frequency-gated admission, each
+             from a cold cache: decode tok/s and hit rate, for the log-Zipf router bias at the cfg4
+             ratio of cache to experts (6.26 GiB), the same bias with a third of that cache, no
+             bias at 6.26 GiB, and a routing trace whose working set exceeds the cache
   batched    64 concurrent sequences, contexts seeded uniform in [512, 16384], paged f16 KV
              with seeded contents, a log-Zipf(1.1) router bias per layer (expert popularity
              over a seeded rank permutation); device tok/s of K graph-replayed steps
