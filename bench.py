@@ -415,7 +415,12 @@ def run_ours(args, rank, world, local_rank):
     xcache = None
     if rank == 0:
         cpu, parity = None, {"status": "not checked (--no-cpu)"}
-        if not args.no_cpu:
+        if world > 1:
+            # the CPU leg runs at N = 1 only: it copies every expert back from HBM, and the
+            # expert-parallel leg has left each rank only its share (ep_parity checks that leg)
+            parity = {"status": "not checked at N > 1 (the batch-1 parity runs at N = 1; batched.ep_parity "
+                                "checks the expert-parallel step)"}
+        elif not args.no_cpu:
             threads = os.cpu_count() or 1
             cpu_tps, first = cpu_baseline_from_engine(engine, cache, cfg, args.ctx, args.cpu_tokens, threads, tok0)
             host = host_info(threads)
