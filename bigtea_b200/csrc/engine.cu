@@ -146,6 +146,7 @@ struct bt_engine {
     // 160 KB of shared memory with the staging buffers, which leaves the SM about 90 KB of L1
     // for the prefetched activation rows)
     int stream_slots = 0;
+    int stream_warps = 8;  // consumer warps per CTA of the stream kernel (option "stream_warps": 4 or 8)
     // failure drill of the persistent step (options "fault_cta", "fault_barrier"; off at 0):
     // CTA fault_cta leaves at its grid barrier number fault_barrier without arriving
     int fault_cta = 0, fault_barrier = 0;
@@ -2395,6 +2396,7 @@ extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint
     CK(cudaMemsetAsync(e->ffn_in.p, 0, (size_t)T * E * 4, e->st));
     CK(cudaMemsetAsync(e->single.p, 1, T, e->st));
     ExpertStreamArgs xa{};
+    int xs_grid = e->n_sm;
     if (kernel == 1) {
         if (!e->layer_dev.p) return fail(BT_ERR_UNSUPPORTED, "the stream kernel needs the device layer table");
         int slot = 0;
@@ -2408,7 +2410,12 @@ extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint
         if ((int)((T * (uint32_t)E + (uint32_t)e->n_sm - 1) / (uint32_t)e->n_sm) > expert_stream_max_rows())
             return fail(BT_ERR_UNSUPPORTED, "the stream kernel's CTAs would own too many down rows");
         const size_t fixed = expert_stream_fixed_smem((int)T, E, K, F);
-        const size_t cap = e->stream_slots ? (size_t)max_dynamic_smem() : std::min<size_t>(160 * 1024, max_dynamic_smem());
+        // four consumer warps: two CTAs per SM, each within half the SM's shared memory; eight:
+        // one CTA, 160 KB (the rest of the SM's memory stays L1 for the prefetched products)
+        const int cons = e->stream_warps;
+        const size_t cap = cons == 4 ? (size_t)112 * 1024
+                           : e->stream_slots ? (size_t)max_dynamic_smem()
+                                             : std::min<size_t>(160 * 1024, max_dynamic_smem());
         int nslot = cap > fixed ? (int)std::min<size_t>((cap - fixed) / (size_t)slot, (size_t)expert_stream_max_slots()) : 0;
         if (e->stream_slots) {
             if (e->stream_slots > nslot) return fail(BT_ERR_INVALID, "stream_slots: that many slots do not fit");
@@ -2435,6 +2442,7 @@ extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint
         xa.wait_limit = WAIT_LIMIT_CYCLES;
         xa.nslot = nslot;
         xa.slot_bytes = slot;
+        xa.consumers = cons;
         int per_sm = 0;
         CK(prepare_expert_stream(xa, &per_sm));
         if (per_sm < 1)
@@ -2443,6 +2451,7 @@ extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint
                                                                (size_t)nslot * slot) +
                                                 " B of shared memory, " + std::to_string(expert_stream_regs()) +
                                                 " registers per thread");
+        xs_grid = per_sm * e->n_sm;
     }
     CK(cudaStreamSynchronize(e->st));
     const bool timing = e->timing;
@@ -2453,7 +2462,7 @@ extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint
     int r = BT_OK;
     if (kernel == 1) {
         cudaError_t le = cudaMemsetAsync(xa.bar, 0, 4, e->st);
-        if (le == cudaSuccess) le = launch_expert_stream(xa, e->n_sm, e->st);
+        if (le == cudaSuccess) le = launch_expert_stream(xa, xs_grid, e->st);
         if (le != cudaSuccess) r = fail(BT_ERR_CUDA, cudaGetErrorString(le));
     } else {
         for (int il = 0; il < L && r == BT_OK; il++)
@@ -2986,6 +2995,11 @@ extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
         if (e->d.n_expert > (uint32_t)XC_MAX_NE || e->TB * (int)e->d.n_expert_used > XC_MAX_SEL) e->xdev = false;
         // the two policies keep separate state: switching starts a new, empty cache
         return bt_engine_enable_expert_cache(e, (uint64_t)e->xpol.capacity() * (uint64_t)e->x_stride, e->xd.policy);
+    }
+    if (!strcmp(name, "stream_warps")) {
+        if (value != 4 && value != 8) return fail(BT_ERR_INVALID, "stream_warps must be 4 or 8");
+        e->stream_warps = value;
+        return BT_OK;
     }
     if (!strcmp(name, "stream_slots")) {
         if (value < 0) return fail(BT_ERR_INVALID, "stream_slots must be >= 0");

@@ -44,8 +44,10 @@ namespace bt {
 
 namespace {
 
-constexpr int XS_CONSUMERS = 8, XS_PRODUCER = XS_CONSUMERS, XS_SYNC = XS_CONSUMERS + 1;
-constexpr int XS_THREADS = (XS_CONSUMERS + 2) * 32;
+// NC consumer warps (4 with two CTAs per SM, or 8 with one), then the producer and the sync warp
+constexpr int XS_MAX_CONSUMERS = 8;
+template <int NC>
+constexpr int xs_threads() { return (NC + 2) * 32; }
 constexpr int XS_MAX_SLOTS = 32;
 constexpr unsigned XS_POISON = 0x80000000u;
 
@@ -56,6 +58,7 @@ __device__ __forceinline__ float xs_slot_dot(bool q4, const uint8_t *tile, int S
 }
 
 // named barrier 1 over the consumer warps, with an OR vote
+template <int NC>
 __device__ __forceinline__ bool consumers_sync_or(bool v) {
     uint32_t r;
     asm volatile(
@@ -64,7 +67,7 @@ __device__ __forceinline__ bool consumers_sync_or(bool v) {
         "bar.red.or.pred q, 1, %2, p;\n\t"
         "selp.u32 %0, 1, 0, q;\n\t}"
         : "=r"(r)
-        : "r"((uint32_t)v), "r"(XS_CONSUMERS * 32)
+        : "r"((uint32_t)v), "r"(NC * 32)
         : "memory");
     return r != 0;
 }
@@ -73,13 +76,14 @@ __device__ __forceinline__ bool consumers_sync_or(bool v) {
 // loaded before the first is quantised. The rows were written before an acquire that orders
 // these loads (the sync warp's, through the ready mbarrier), or are read-only: plain loads, so
 // the lines the sync warp prefetched into L1 serve them.
+template <int NC>
 __device__ void xs_stage(const float *x, int nblk, ActBlock *act, int warp, int lane) {
     constexpr int B = 3;
-    for (int w0 = 0; w0 < nblk; w0 += B * XS_CONSUMERS) {
+    for (int w0 = 0; w0 < nblk; w0 += B * NC) {
         float v[B][8];
 #pragma unroll
         for (int i = 0; i < B; i++) {
-            const int blk = w0 + warp + i * XS_CONSUMERS;
+            const int blk = w0 + warp + i * NC;
             if (blk < nblk) {
                 const float4 *src = reinterpret_cast<const float4 *>(x + (long long)blk * 256 + lane * 8);
                 const float4 a0 = src[0], a1 = src[1];
@@ -89,7 +93,7 @@ __device__ void xs_stage(const float *x, int nblk, ActBlock *act, int warp, int 
         }
 #pragma unroll
         for (int i = 0; i < B; i++) {
-            const int blk = w0 + warp + i * XS_CONSUMERS;
+            const int blk = w0 + warp + i * NC;
             if (blk < nblk) quantize_block_warp(v[i], act + blk, lane);
         }
     }
@@ -144,13 +148,13 @@ __device__ __forceinline__ void xs_range(int total, int &u0, int &u1) {
 
 struct XsSmem {
     uint64_t *full, *empty;
-    uint64_t *gu_done;  // the consumer warps' gate/up units of a stage are done (count XS_CONSUMERS)
+    uint64_t *gu_done;  // the consumer warps' gate/up units of a stage are done (count NC)
     uint64_t *ready;    // the sync warp saw every CTA's gate/up of a layer (count 1)
     int *stop, *gfail;
     float *wts;   // [T][K] the route weights of the layer whose down rows run
     float *part;  // [K][XS_MAX_ROWS] each expert's value of the CTA's down rows
     ActBlock *act_in;  // [T][E / 256] the gate/up input
-    ActBlock *act_dn;  // [XS_CONSUMERS][F / 256] each warp's expert's SiLU products
+    ActBlock *act_dn;  // [XS_MAX_CONSUMERS][F / 256] each warp's expert's SiLU products
     uint8_t *ring;
 };
 
@@ -168,7 +172,7 @@ __device__ __forceinline__ XsSmem xs_smem(uint8_t *smem, const ExpertStreamArgs 
     sm.part = reinterpret_cast<float *>(smem + 2048);
     sm.act_in = reinterpret_cast<ActBlock *>(smem + 2048 + MAX_K * XS_MAX_ROWS * 4);
     sm.act_dn = sm.act_in + p.T * (p.E / 256);
-    sm.ring = reinterpret_cast<uint8_t *>(sm.act_dn + XS_CONSUMERS * (p.F / 256));
+    sm.ring = reinterpret_cast<uint8_t *>(sm.act_dn + XS_MAX_CONSUMERS * (p.F / 256));
     return sm;
 }
 
@@ -196,7 +200,9 @@ __device__ __forceinline__ int xs_piece(int d0, int d1, int E, int maxr, int q, 
 
 }  // namespace
 
+template <int NC>
 __global__ void __maxnreg__(168) expert_stream_kernel(const __grid_constant__ ExpertStreamArgs p) {
+    constexpr int XS_CONSUMERS = NC, XS_PRODUCER = NC, XS_SYNC = NC + 1;
     extern __shared__ __align__(1024) uint8_t smem[];
     const XsSmem sm = xs_smem(smem, p);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -390,7 +396,7 @@ __global__ void __maxnreg__(168) expert_stream_kernel(const __grid_constant__ Ex
     for (int s = 0; s <= L; s++) {
         // every warp is done with the previous stage: its down values are complete, the input
         // buffer is free
-        if (consumers_sync_or(bad)) break;
+        if (consumers_sync_or<NC>(bad)) break;
         if (s >= 2) finish_down(s - 2);
         // ---- gate/up of layer s
         if (s < L) {
@@ -400,8 +406,8 @@ __global__ void __maxnreg__(168) expert_stream_kernel(const __grid_constant__ Ex
             const int gtb = Ld.gate.tile_bytes;
             int u0, u1;
             xs_range(T * K * gnt, u0, u1);
-            xs_stage(p.xin + (long long)s * p.xin_stride, T * (E / 256), sm.act_in, warp, lane);
-            if (consumers_sync_or(false)) break;
+            xs_stage<NC>(p.xin + (long long)s * p.xin_stride, T * (E / 256), sm.act_in, warp, lane);
+            if (consumers_sync_or<NC>(false)) break;
             float *act = p.act + (long long)s * T * K * F;
             for (; j < base + (u1 - u0); j += XS_CONSUMERS) {
                 const int slot = j % nslot;
@@ -450,7 +456,7 @@ __global__ void __maxnreg__(168) expert_stream_kernel(const __grid_constant__ Ex
             bool gbad = !mbar_wait_l(sm.ready, (uint32_t)(il & 1), p.err, p.wait_limit);
             gbad |= *reinterpret_cast<volatile int *>(sm.gfail) != 0;
             if (tid < T * K) sm.wts[tid] = __ldg(p.wts + il * T * K + tid);
-            if (consumers_sync_or(gbad || bad)) break;
+            if (consumers_sync_or<NC>(gbad || bad)) break;
             const float *acts = p.act + (long long)il * T * K * F;
             ActBlock *mine = sm.act_dn + warp * nsbF;
             int staged = -1;  // (token, expert) whose products are in `mine`
@@ -495,7 +501,7 @@ __global__ void __maxnreg__(168) expert_stream_kernel(const __grid_constant__ Ex
     // the last layer's expert sums, unless a failure ended the loop (every thread leaves the
     // loop at the same vote, so `completed` is uniform)
     if (completed) {
-        if (consumers_sync_or(bad)) bad = true;
+        if (consumers_sync_or<NC>(bad)) bad = true;
         else finish_down(L - 1);
     }
     // a failure, or the end: tell the producer and the sync warp to stop waiting
@@ -505,7 +511,7 @@ __global__ void __maxnreg__(168) expert_stream_kernel(const __grid_constant__ Ex
 
 size_t expert_stream_fixed_smem(int T, int E, int K, int F) {
     (void)K;
-    return 2048 + (size_t)MAX_K * XS_MAX_ROWS * 4 + (size_t)(T * (E / 256) + XS_CONSUMERS * (F / 256)) * sizeof(ActBlock);
+    return 2048 + (size_t)MAX_K * XS_MAX_ROWS * 4 + (size_t)(T * (E / 256) + XS_MAX_CONSUMERS * (F / 256)) * sizeof(ActBlock);
 }
 
 int expert_stream_max_rows() { return XS_MAX_ROWS; }
@@ -514,25 +520,32 @@ static size_t xs_smem_bytes(const ExpertStreamArgs &a) {
     return expert_stream_fixed_smem(a.T, a.E, a.K, a.F) + (size_t)a.nslot * a.slot_bytes;
 }
 
-cudaError_t prepare_expert_stream(const ExpertStreamArgs &a, int *blocks_per_sm) {
-    if (a.nslot < 1 || a.nslot > XS_MAX_SLOTS || a.slot_bytes % 16) return cudaErrorInvalidValue;
-    cudaError_t e = cudaFuncSetAttribute(expert_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+template <int NC>
+static cudaError_t xs_prepare(const ExpertStreamArgs &a, int *blocks_per_sm) {
+    cudaError_t e = cudaFuncSetAttribute(expert_stream_kernel<NC>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)xs_smem_bytes(a));
     if (e) return e;
-    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, expert_stream_kernel, XS_THREADS,
+    return cudaOccupancyMaxActiveBlocksPerMultiprocessor(blocks_per_sm, expert_stream_kernel<NC>, xs_threads<NC>(),
                                                          xs_smem_bytes(a));
+}
+
+cudaError_t prepare_expert_stream(const ExpertStreamArgs &a, int *blocks_per_sm) {
+    if (a.nslot < 1 || a.nslot > XS_MAX_SLOTS || a.slot_bytes % 16) return cudaErrorInvalidValue;
+    if (a.consumers == 4) return xs_prepare<4>(a, blocks_per_sm);
+    if (a.consumers == 8) return xs_prepare<8>(a, blocks_per_sm);
+    return cudaErrorInvalidValue;
 }
 
 int expert_stream_regs() {
     cudaFuncAttributes fa;
-    return cudaFuncGetAttributes(&fa, expert_stream_kernel) == cudaSuccess ? fa.numRegs : -1;
+    return cudaFuncGetAttributes(&fa, expert_stream_kernel<8>) == cudaSuccess ? fa.numRegs : -1;
 }
 
-cudaError_t launch_expert_stream(const ExpertStreamArgs &a, int grid, cudaStream_t st) {
-    if (a.nslot < 1 || a.nslot > XS_MAX_SLOTS || a.slot_bytes % 16) return cudaErrorInvalidValue;
+template <int NC>
+static cudaError_t xs_launch(const ExpertStreamArgs &a, int grid, cudaStream_t st) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(XS_THREADS);
+    cfg.blockDim = dim3(xs_threads<NC>());
     cfg.dynamicSmemBytes = xs_smem_bytes(a);
     cfg.stream = st;
     cudaLaunchAttribute attr[1];
@@ -540,7 +553,14 @@ cudaError_t launch_expert_stream(const ExpertStreamArgs &a, int grid, cudaStream
     attr[0].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    return cudaLaunchKernelEx(&cfg, expert_stream_kernel, a);
+    return cudaLaunchKernelEx(&cfg, expert_stream_kernel<NC>, a);
+}
+
+cudaError_t launch_expert_stream(const ExpertStreamArgs &a, int grid, cudaStream_t st) {
+    if (a.nslot < 1 || a.nslot > XS_MAX_SLOTS || a.slot_bytes % 16) return cudaErrorInvalidValue;
+    if (a.consumers == 4) return xs_launch<4>(a, grid, st);
+    if (a.consumers == 8) return xs_launch<8>(a, grid, st);
+    return cudaErrorInvalidValue;
 }
 
 int expert_stream_max_slots() { return XS_MAX_SLOTS; }

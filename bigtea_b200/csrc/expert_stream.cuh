@@ -20,6 +20,7 @@ struct ExpertStreamArgs {
     int *err;
     long long wait_limit;  // SM cycles of every bounded wait
     int nslot, slot_bytes;  // the CTA's ring: nslot slots, each holding the largest unit
+    int consumers;          // consumer warps per CTA: 4 (two CTAs per SM) or 8 (one)
 };
 
 size_t expert_stream_fixed_smem(int T, int E, int K, int F);

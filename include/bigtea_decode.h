@@ -181,7 +181,8 @@ int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const ui
  * at 0): in layer fault_copy - 1, CTA fault_cta requests none of its expert tiles, so its own
  * waits run out and it takes the failure exit (barrier poisoned, its copies drained);
  * "stream_slots" (ring slots of bt_bench_experts' stream kernel, default 0 = as many as fit in
- * 160 KB of shared memory); "xcache_device" (the expert cache's policy runs on the device after
+ * 160 KB of shared memory); "stream_warps" (its consumer warps per CTA: 8, one CTA per SM, the
+ * default; or 4, two CTAs per SM); "xcache_device" (the expert cache's policy runs on the device after
  * each layer's router and fills missed slots from the pinned host copies with a kernel, so a
  * step needs no host round trip per layer; default 1; 0 = the host decides each layer; a
  * change starts a new, empty cache). */
