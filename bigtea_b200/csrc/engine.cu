@@ -26,6 +26,10 @@
 #include "kernels.cuh"
 #include "step_kernel.cuh"
 #include "expert_stream.cuh"
+
+#ifndef BT_STEP_TOKENS
+#define BT_STEP_TOKENS 128  // tokens of one step of the per-phase kernels (longer calls are cut into steps)
+#endif
 #include "xcache_dev.cuh"
 
 using namespace bt;
@@ -119,7 +123,7 @@ struct bt_engine {
     QMat embd, out;
     DevBuf out_norm, rope;
     // per-step scratch, sized for TB tokens and max_seqs outputs
-    int TB = 64;
+    int TB = BT_STEP_TOKENS;
     int max_out = 0;
     DevBuf x, ffn_in, fn, qkv, qbuf, att, rlog, rcnt, sel_ids, sel_w, act, part, acnt;
     DevBuf q8_qs, q8_d, q8_bs;  // activation rows as Q8_K for the tensor-core kernels (q8_rows x q8_k)
@@ -138,6 +142,7 @@ struct bt_engine {
     bool ep_aborted = false;
     bool mma = true;  // grouped Q4_K gate/up on tcgen05 (option "mma")
     int mma_min_units = 32;  // batched GEMVs on tcgen05 from this many (tokens, rows) units on (option)
+    int token_groups = 1;    // batched dp4a GEMVs with few tiles split their tokens into groups (option)
     int mma_grid = 0;        // CTAs of the tensor-core kernels (0: one per SM; option, for tests)
     bool attn_warp = true;   // batched attention with one warp per 128-key chunk (option "attn_warp")
     // the persistent step's bounded waits, in microseconds (option "wait_limit_us"; 0 = about 1 s)
@@ -1205,7 +1210,7 @@ static GemvSeg make_seg(const QMat &m, int tile0, int out_off) {
 static cudaError_t run_gemv(bt_engine *e, const QMat *const *mats, const int *out_offs, int nseg, const float *x,
                             long long x_stride, const int *x_rows, const float *norm_w, int K, int T, float *y,
                             long long y_stride, const float *res, long long res_stride, const char *name,
-                            unsigned long long *amax = nullptr, const PrefetchSpec *pf = nullptr) {
+                            unsigned long long *amax = nullptr, const PrefetchSpec *pf = nullptr, int tgrp = 0) {
     GemvArgs a{};
     a.amax = amax;
     if (pf) a.pf = *pf;
@@ -1230,75 +1235,141 @@ static cudaError_t run_gemv(bt_engine *e, const QMat *const *mats, const int *ou
     a.res_stride = res_stride;
     a.err = e->err.as<int>();
     a.slot_bytes = slot;
+    long long n_units = tile0;
+    if (tgrp > 0 && !amax) {
+        // units (group of tgrp tokens, tile); a CTA's contiguous range of at most upc units
+        // covers at most (upc - 1) / tiles + 2 groups, whose tokens it stages
+        a.tgrp = tgrp;
+        n_units = (long long)tile0 * ((T + tgrp - 1) / tgrp);
+        const long long g = grid_for(e, n_units), upc = (n_units + g - 1) / g;
+        const long long span = ((upc - 1) / tile0 + 2) * tgrp;
+        a.stage_max = (int)(span < T ? span : T);
+        if (a.stage_max > 128) return cudaErrorInvalidValue;  // the RMSNorm scales: 128 floats
+    }
     a.nst = 1;
     size_t fixed = gemv_smem_bytes(a) - (size_t)GEMV_WARPS * slot;
     a.nst = T > MAX_T ? pick_nst_cap(slot, fixed, (size_t)max_dynamic_smem()) : pick_nst(slot, fixed);
+    if (gemv_smem_bytes(a) > (size_t)max_dynamic_smem()) return cudaErrorInvalidValue;
     timer_begin(e, name);
-    cudaError_t r = launch_gemv(a, grid_for(e, tile0), e->st, e->pdl);
+    cudaError_t r = launch_gemv(a, grid_for(e, n_units), e->st, e->pdl);
     timer_end(e);
     return r;
 }
 
+// Q6_K matrices the tensor-core kernel takes: whole 128-row blocks, tiles that start on 16 bytes
+// and a run of superblock scales d that ends on 16 bytes
+static bool mma6_fits(const QMat &m) {
+    return m.type == T_Q6_K && m.rows % 128 == 0 && m.g.tile_bytes % 16 == 0 && (2 * m.g.S) % 16 == 0;
+}
+
+// The arguments of a tensor-core GEMV over n segments (activations from the Q8_K staging)
+static GemvArgs mma_args(bt_engine *e, const QMat *const *m, const int *offs, int n, int K, int T, float *y,
+                         long long y_stride, const float *res, long long res_stride, unsigned long long *amax) {
+    GemvArgs a{};
+    int tile0 = 0;
+    for (int i = 0; i < n; i++) {
+        a.seg[i] = make_seg(*m[i], tile0, offs[i]);
+        tile0 += a.seg[i].n_tiles;
+    }
+    a.nseg = n;
+    a.total_tiles = tile0;
+    a.K = K;
+    a.T = T;
+    a.y = y;
+    a.y_stride = y_stride;
+    a.res = res;
+    a.res_stride = res_stride;
+    a.err = e->err.as<int>();
+    a.amax = amax;
+    a.q8_qs = e->q8_qs.as<int8_t>();
+    a.q8_d = e->q8_d.as<float>();
+    a.q8_bs = e->q8_bs.as<int>();
+    return a;
+}
+
+// T activation rows (x_rows[t] or t) as Q8_K rows for the tensor-core GEMVs, RMS-normed first
+// when norm_w
+static cudaError_t stage_q8(bt_engine *e, const float *x, long long x_stride, const int *x_rows, const float *norm_w,
+                            int K, int T) {
+    if ((size_t)T > e->q8_rows) return cudaErrorInvalidValue;
+    return launch_q8_stage(x, x_stride, x_rows, norm_w, e->d.rms_eps, K, T, e->q8_qs.as<int8_t>(), e->q8_d.as<float>(),
+                           e->q8_bs.as<int>(), e->st, e->pdl);
+}
+
 // A batched GEMV (T > MAX_T tokens): the Q4_K segments of whole 128-row blocks run on tcgen05 in
-// one launch over all tokens; the other segments run through the dp4a kernel in token chunks.
+// one launch over all tokens, the Q6_K ones in another (both from one Q8_K staging), when they
+// cover mma_min_units CTAs; the other segments run through the dp4a kernel.
 static int run_gemv_batched(bt_engine *e, const QMat *const *mats, const int *offs, int nseg, const float *x,
                             long long x_stride, const float *norm_w, int K, int T, float *y, long long y_stride,
                             const float *res, long long res_stride, const char *name, const PrefetchSpec *pf) {
-    const QMat *mm[3], *dm[3];
-    int mo[3], dof[3], nm = 0, nd = 0;
-    // the tensor-core kernel's units are (N tokens, 128 rows), one CTA per SM: it pays once
+    const QMat *mm[3], *m6[3], *dm[3];
+    int mo[3], o6[3], dof[3], nm = 0, n6 = 0, nd = 0;
+    // the tensor-core kernels' units are (N tokens, 128 rows), one CTA per SM: they pay once
     // they cover mma_min_units CTAs
     const int gn = gemv_mma_tokens(K);
-    long long units = 0;
-    for (int i = 0; i < nseg; i++)
+    long long units = 0, units6 = 0;
+    for (int i = 0; i < nseg; i++) {
         if (mats[i]->type == T_Q4_K && mats[i]->rows % 128 == 0) units += (long long)(mats[i]->rows / 128);
+        if (mma6_fits(*mats[i])) units6 += (long long)(mats[i]->rows / 128);
+    }
     units *= gn ? (T + gn - 1) / gn : 0;
+    units6 *= (T + 15) / 16;
     const bool mma_ok = e->mma && gn && gemv_mma_smem_bytes(K) <= (size_t)max_dynamic_smem() &&
                         units >= e->mma_min_units && (size_t)T <= e->q8_rows;
+    const bool mma6_ok = e->mma && gemv_mma6_smem_bytes(K) <= (size_t)max_dynamic_smem() &&
+                         units6 >= e->mma_min_units && (size_t)T <= e->q8_rows;
     for (int i = 0; i < nseg; i++) {
         if (mma_ok && mats[i]->type == T_Q4_K && mats[i]->rows % 128 == 0) {
             mm[nm] = mats[i];
             mo[nm++] = offs[i];
+        } else if (mma6_ok && mma6_fits(*mats[i])) {
+            m6[n6] = mats[i];
+            o6[n6++] = offs[i];
         } else {
             dm[nd] = mats[i];
             dof[nd++] = offs[i];
         }
     }
-    if (nm) {
-        GemvArgs a{};
-        int tile0 = 0;
-        for (int i = 0; i < nm; i++) {
-            a.seg[i] = make_seg(*mm[i], tile0, mo[i]);
-            tile0 += a.seg[i].n_tiles;
-        }
-        a.nseg = nm;
-        a.total_tiles = tile0;
-        a.x = x;
-        a.x_stride = x_stride;
-        a.norm_w = norm_w;
-        a.eps = e->d.rms_eps;
-        a.K = K;
-        a.T = T;
-        a.y = y;
-        a.y_stride = y_stride;
-        a.res = res;
-        a.res_stride = res_stride;
-        a.err = e->err.as<int>();
-        a.q8_qs = e->q8_qs.as<int8_t>();
-        a.q8_d = e->q8_d.as<float>();
-        a.q8_bs = e->q8_bs.as<int>();
+    if (nm || n6) {
         timer_begin(e, name);
-        cudaError_t ce = (size_t)T > e->q8_rows ? cudaErrorInvalidValue
-                                                : launch_q8_stage(x, x_stride, nullptr, norm_w, e->d.rms_eps, K, T,
-                                                                  e->q8_qs.as<int8_t>(), e->q8_d.as<float>(),
-                                                                  e->q8_bs.as<int>(), e->st, e->pdl);
-        if (ce == cudaSuccess) ce = launch_gemv_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, e->st, e->pdl);
+        cudaError_t ce = stage_q8(e, x, x_stride, nullptr, norm_w, K, T);
+        if (ce == cudaSuccess && nm) {
+            const GemvArgs a = mma_args(e, mm, mo, nm, K, T, y, y_stride, res, res_stride, nullptr);
+            ce = launch_gemv_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, e->st, e->pdl);
+        }
+        if (ce == cudaSuccess && n6) {
+            const GemvArgs a = mma_args(e, m6, o6, n6, K, T, y, y_stride, res, res_stride, nullptr);
+            ce = launch_gemv_mma6(a, e->mma_grid ? e->mma_grid : e->n_sm, e->st, e->pdl);
+        }
         timer_end(e);
         CK(ce);
     }
     if (nd) {
         int slot = 0;
-        for (int i = 0; i < nd; i++) slot = dm[i]->g.tile_bytes > slot ? dm[i]->g.tile_bytes : slot;
+        long long tiles = 0;
+        for (int i = 0; i < nd; i++) {
+            slot = dm[i]->g.tile_bytes > slot ? dm[i]->g.tile_bytes : slot;
+            tiles += dm[i]->g.n_tiles;
+        }
+        // fewer tiles than half the grid's warps (a 512-row attn_v: 128 tiles): one launch whose
+        // units are (group of 8k tokens, tile), enough of them for every warp
+        const long long warps = (long long)grid_for(e, 1ll << 30) * GEMV_WARPS;
+        if (e->token_groups && tiles * 2 <= warps) {
+            const int ng = (int)((warps + tiles - 1) / tiles);
+            int tgrp = (T + ng - 1) / ng;
+            tgrp = (tgrp + 7) / 8 * 8;
+            GemvArgs probe{};
+            probe.K = K;
+            probe.tgrp = tgrp;
+            probe.stage_max = 2 * tgrp < T ? 2 * tgrp : T;
+            probe.slot_bytes = slot;
+            probe.nst = 1;
+            if (probe.stage_max <= 128 && gemv_smem_bytes(probe) <= (size_t)max_dynamic_smem()) {
+                CK(run_gemv(e, dm, dof, nd, x, x_stride, nullptr, norm_w, K, T, y, y_stride, res, res_stride, name,
+                            nullptr, pf, tgrp));
+                return BT_OK;
+            }
+        }
         const int chunk = gemv_chunk(T, K, slot);
         for (int t0 = 0; t0 < T; t0 += chunk) {
             const int tg = T - t0 < chunk ? T - t0 : chunk;
@@ -2066,7 +2137,24 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
         }
     }
     const int n_out = (int)p.x_rows.size();
-    for (int o0 = 0; o0 < n_out; o0 += MAX_T) {
+    const bool head_mma = n_out > MAX_T && e->mma && mma6_fits(e->out) &&
+                          gemv_mma6_smem_bytes(E) <= (size_t)max_dynamic_smem() && (size_t)n_out <= e->q8_rows;
+    if (head_mma) {
+        // more outputs than one dp4a launch carries: the Q6_K head on the tensor cores, with the
+        // per-output argmax keys
+        const QMat *mats[1] = {&e->out};
+        int offs[1] = {0};
+        timer_begin(e, "output_gemv");
+        cudaError_t ce = stage_q8(e, e->x.as<float>(), E, e->x_rows.as<int>(), e->out_norm.as<float>(), E, n_out);
+        if (ce == cudaSuccess) {
+            const GemvArgs a = mma_args(e, mats, offs, 1, E, n_out, e->logits.as<float>() + (size_t)p.out_first * d.n_vocab,
+                                        d.n_vocab, nullptr, 0, e->amax.as<unsigned long long>() + p.out_first);
+            ce = launch_gemv_mma6(a, e->mma_grid ? e->mma_grid : e->n_sm, e->st, e->pdl);
+        }
+        timer_end(e);
+        CK(ce);
+    }
+    for (int o0 = 0; !head_mma && o0 < n_out; o0 += MAX_T) {
         int og = n_out - o0 < MAX_T ? n_out - o0 : MAX_T;
         const QMat *mats[1] = {&e->out};
         int offs[1] = {0};
@@ -2215,7 +2303,7 @@ static int greedy_prepare(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, cons
                           uint32_t n_seqs, uint32_t n_steps, StepPlan &p) {
     if (!e || !kv || !seq_ids || !first_tokens) return fail(BT_ERR_INVALID, "null argument");
     if (kv->e != e) return fail(BT_ERR_INVALID, "KV pool belongs to another engine");
-    if (n_seqs == 0 || n_seqs > (uint32_t)e->TB) return fail(BT_ERR_INVALID, "1..64 sequences per greedy batch");
+    if (n_seqs == 0 || n_seqs > (uint32_t)e->TB) return fail(BT_ERR_INVALID, "1..step-capacity sequences per greedy batch");
     CK(cudaSetDevice(e->device));
     std::vector<char> seen(kv->max_seqs, 0);
     for (uint32_t i = 0; i < n_seqs; i++) {
@@ -2966,6 +3054,10 @@ extern "C" int bt_set_option(bt_engine *e, const char *name, int value) {
         e->graphs.clear();
         return BT_OK;
     }
+    if (!strcmp(name, "token_groups")) {
+        e->token_groups = value ? 1 : 0;
+        return BT_OK;
+    }
     if (!strcmp(name, "mma_min_units")) {
         if (value < 1) return fail(BT_ERR_INVALID, "mma_min_units must be positive");
         e->mma_min_units = value;
@@ -3020,7 +3112,7 @@ extern "C" int bt_debug_topk(const bt_engine *e, uint32_t layer, uint32_t token,
     if (!e || !ids || !weights) return fail(BT_ERR_INVALID, "null argument");
     if (layer >= e->d.n_layer) return fail(BT_ERR_INVALID, "layer out of range");
     if (token < e->last_first || token >= e->last_first + e->last_T)
-        return fail(BT_ERR_INVALID, "token is not in the last step of the last forward (the last 64 tokens)");
+        return fail(BT_ERR_INVALID, "token is not in the last step of the last forward");
     const int K = e->d.n_expert_used;
     size_t off = ((size_t)layer * e->TB + (token - e->last_first)) * K;
     CK(cudaMemcpy(ids, e->dbg_ids.as<int>() + off, K * 4, cudaMemcpyDeviceToHost));
@@ -3031,7 +3123,7 @@ extern "C" int bt_debug_topk(const bt_engine *e, uint32_t layer, uint32_t token,
 extern "C" int bt_debug_hidden(const bt_engine *e, uint32_t token, float *out) {
     if (!e || !out) return fail(BT_ERR_INVALID, "null argument");
     if (token < e->last_first || token >= e->last_first + e->last_T)
-        return fail(BT_ERR_INVALID, "token is not in the last step of the last forward (the last 64 tokens)");
+        return fail(BT_ERR_INVALID, "token is not in the last step of the last forward");
     CK(cudaMemcpy(out, e->x.as<float>() + (size_t)(token - e->last_first) * e->d.n_embd, e->d.n_embd * 4, cudaMemcpyDeviceToHost));
     return BT_OK;
 }

@@ -185,15 +185,26 @@ __global__ void __launch_bounds__(NWARP * 32, 1) kq_rows_kernel(const __grid_con
     float *normS = reinterpret_cast<float *>(smem + 512);
     ActBlock *act = reinterpret_cast<ActBlock *>(smem + 1024);
     const int nsbK = p.K / 256;
-    const size_t act_bytes = (size_t)p.T * nsbK * sizeof(ActBlock);
+    const int stage_cap = p.tgrp ? p.stage_max : p.T;
+    const size_t act_bytes = (size_t)stage_cap * nsbK * sizeof(ActBlock);
     uint8_t *ring = smem + 1024 + ((act_bytes + 127) & ~(size_t)127);
     uint8_t *myring = ring + (size_t)warp * p.nst * p.slot_bytes;
     uint64_t *mybar = bars + warp * p.nst;
     float *red = reinterpret_cast<float *>(ring + (size_t)NWARP * p.nst * p.slot_bytes) + warp * RED_WARP_FLOATS;
 
-    const long long u0 = (long long)blockIdx.x * p.total_tiles / gridDim.x;
-    const long long u1 = (long long)(blockIdx.x + 1) * p.total_tiles / gridDim.x;
+    // units: tiles, or (token group, tile) group-major
+    const int tg = p.tgrp ? p.tgrp : (p.T > 0 ? p.T : 1);
+    const long long n_units = (long long)p.total_tiles * ((p.T + tg - 1) / tg);
+    const long long u0 = (long long)blockIdx.x * n_units / gridDim.x;
+    const long long u1 = (long long)(blockIdx.x + 1) * n_units / gridDim.x;
     const int nmine = (u1 - u0 > warp) ? (int)((u1 - u0 - warp + NWARP - 1) / NWARP) : 0;
+    // the tokens this CTA stages: [tA, tB), the groups of units u0 .. u1-1
+    const int tA = u1 > u0 ? (int)(u0 / p.total_tiles) * tg : 0;
+    const int tB = u1 > u0 ? min(p.T, (int)((u1 - 1) / p.total_tiles + 1) * tg) : 0;
+    if (tB - tA > stage_cap) {  // the host sized stage_max too small: nothing is computed
+        if (threadIdx.x == 0) atomicOr(p.err, ERR_BAD_INDEX);
+        return;
+    }
 
     auto seg_of = [&](long long u) -> int {
         int si = 0;
@@ -202,7 +213,7 @@ __global__ void __launch_bounds__(NWARP * 32, 1) kq_rows_kernel(const __grid_con
         return si;
     };
     auto issue = [&](int j) {
-        long long u = u0 + warp + (long long)j * NWARP;
+        const long long u = (u0 + warp + (long long)j * NWARP) % p.total_tiles;
         const GemvSeg &sg = p.seg[seg_of(u)];
         const uint8_t *src = sg.w + (u - sg.tile0) * (long long)sg.tile_bytes;
         int slot = j % p.nst;
@@ -220,7 +231,8 @@ __global__ void __launch_bounds__(NWARP * 32, 1) kq_rows_kernel(const __grid_con
 
     pdl_wait();
     run_prefetch(p.pf);
-    stage_activations<NWARP>(p.x, p.x_stride, p.x_rows, p.norm_w, p.eps, p.K, p.T, act, normS);
+    stage_activations<NWARP>(p.x_rows ? p.x : p.x + (long long)tA * p.x_stride, p.x_stride,
+                             p.x_rows ? p.x_rows + tA : nullptr, p.norm_w, p.eps, p.K, tB - tA, act, normS);
     __syncthreads();
     pdl_trigger();
 
@@ -231,7 +243,10 @@ __global__ void __launch_bounds__(NWARP * 32, 1) kq_rows_kernel(const __grid_con
     for (; j < nmine; j++) {
         const int slot = j % p.nst;
         if (!__all_sync(FULL, mbar_wait(&mybar[slot], (j / p.nst) & 1, p.err))) break;
-        const long long u = u0 + warp + (long long)j * NWARP;
+        const long long ug = u0 + warp + (long long)j * NWARP;
+        const long long u = ug % p.total_tiles;
+        // the unit's tokens [ta, te), staged from token tA on
+        const int ta = (int)(ug / p.total_tiles) * tg, te = min(p.T, ta + tg);
         const GemvSeg &sg = p.seg[seg_of(u)];
         const uint8_t *tile = myring + (size_t)slot * p.slot_bytes;
         const long long tl = u - sg.tile0;
@@ -245,12 +260,12 @@ __global__ void __launch_bounds__(NWARP * 32, 1) kq_rows_kernel(const __grid_con
         // 8 tokens at a time: every lane's superblock partial to shared memory, then one lane
         // per (row, token) adds the row's nsb partials in superblock order (C4)
         auto run_tokens = [&](auto &&dot) {
-        for (int t0 = 0; t0 < p.T; t0 += 8) {
-            const int tn = p.T - t0 < 8 ? p.T - t0 : 8;
+        for (int t0 = ta; t0 < te; t0 += 8) {
+            const int tn = te - t0 < 8 ? te - t0 : 8;
             for (int i = 0; i < tn; i += 2) {
                 const int i1 = i + 1 < tn ? i + 1 : i;
-                const float v0 = dot(act_b + (uint32_t)(t0 + i) * tok_stride);
-                const float v1 = dot(act_b + (uint32_t)(t0 + i1) * tok_stride);
+                const float v0 = dot(act_b + (uint32_t)(t0 - tA + i) * tok_stride);
+                const float v1 = dot(act_b + (uint32_t)(t0 - tA + i1) * tok_stride);
                 red[i * RED_STRIDE + lane] = active ? v0 : 0.0f;
                 if (i + 1 < tn) red[(i + 1) * RED_STRIDE + lane] = active ? v1 : 0.0f;
             }
@@ -320,7 +335,7 @@ __global__ void __launch_bounds__(NWARP * 32, 1) kq_rows_kernel(const __grid_con
 }
 
 size_t gemv_smem_bytes(const GemvArgs &a) {
-    size_t act = (size_t)a.T * (a.K / 256) * sizeof(ActBlock);
+    size_t act = (size_t)(a.tgrp ? a.stage_max : a.T) * (a.K / 256) * sizeof(ActBlock);
     return 1024 + ((act + 127) & ~(size_t)127) + (size_t)GEMV_WARPS * a.nst * a.slot_bytes +
            (size_t)GEMV_WARPS * RED_WARP_FLOATS * 4;
 }

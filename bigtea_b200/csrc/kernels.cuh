@@ -58,6 +58,10 @@ struct GemvArgs {
     const int8_t *q8_qs;
     const float *q8_d;
     const int *q8_bs;
+    // token groups (dp4a kernel, no amax): 0 = every unit carries all T tokens; else the units
+    // are (group of tgrp tokens, tile), group-major, and a CTA stages only the tokens of the
+    // groups its units cover, at most stage_max of them
+    int tgrp, stage_max;
 };
 
 struct ExpertArgs {
@@ -231,12 +235,17 @@ cudaError_t launch_gateup_mma(const ExpertArgs &a, int grid, cudaStream_t st, bo
 cudaError_t init_mma_attributes();
 // batched GEMV on tcgen05 (Q4_K segments of whole 128-row blocks, no argmax); one CTA per SM
 size_t gemv_mma_smem_bytes(int K);
+// tokens per unit of the batched tensor-core GEMV (32 or 16; 0: does not fit)
 int gemv_mma_tokens(int K);
 // T rows of K activations (row t = x_rows[t] or t; RMSNorm first when norm_w) as Q8_K rows:
 // qs [T][K], d [T][K/256], bs [T][K/256][8] (C3/C6, the dp4a kernels' staging bit for bit)
 cudaError_t launch_q8_stage(const float *x, long long x_stride, const int *x_rows, const float *norm_w, float eps, int K,
-                            int T, int8_t *qs, float *d, int *bs, cudaStream_t st, bool pdl);  // tokens per unit of the batched tensor-core GEMV (32 or 16; 0: does not fit)
+                            int T, int8_t *qs, float *d, int *bs, cudaStream_t st, bool pdl);
 cudaError_t launch_gemv_mma(const GemvArgs &a, int grid, cudaStream_t st, bool pdl);
+// Q6_K segments of whole 128-row blocks on tcgen05 (16-token chunks), with optional argmax keys;
+// (size_t)-1 = K does not fit
+size_t gemv_mma6_smem_bytes(int K);
+cudaError_t launch_gemv_mma6(const GemvArgs &a, int grid, cudaStream_t st, bool pdl);
 // act[t][j] = silu(gu[t][j]) * gu[t][F + j] for the shared expert (C7)
 cudaError_t launch_shexp_act(const float *gu, float *act, int T, int F, cudaStream_t st, bool pdl);
 cudaError_t launch_qkv_post(const QkvPostArgs &a, cudaStream_t st, bool pdl);

@@ -659,6 +659,334 @@ __global__ void __launch_bounds__(256, 1) kq_rows_mma_kernel(const __grid_consta
     if (warp == 0) tmem_dealloc(tmem, TCOLS);
 }
 
+// ====================================================================== Q6_K rows on tcgen05
+// The same GEMV for Q6_K segments of whole 128-row blocks, optionally with the output head's
+// per-token argmax keys. Q6_K scales each 16-value sub-block on its own while one MMA of kind::i8
+// covers K = 32, so each K step runs two MMAs against the same A (the row's 6-bit values as
+// unsigned bytes, 0..63): one whose B holds the step's first 16 activation values and zeros for
+// the other 16, one the other way round. Neither B is stored: per K step the chunk's
+// activations lie in shared memory as [first halves][zeros][second halves], 16 token rows x 16
+// bytes each, and the two descriptors start at the first and at the zero block with the K halves
+// one block apart (LBO 256 B, SBO 128 B). 16 MMAs per superblock step write the 16 sub-block
+// dots of 128 rows x 16 tokens into their own TMEM columns (2 x 256 columns, double-buffered); the
+// epilogue finishes C4's Q6_K form per (row, token) -- sumi = sum_j sc_j (dot_j - 32 bs16_j),
+// then (float)sumi * (d * d_a) added to the row's sum in superblock order -- the dp4a kernel's
+// bits. Thread (row r, half h) copies its row's ql and qh of half h (4 + 2 pieces of 16 bytes)
+// and either the 16 scales (h = 0) or the 16 bytes holding the superblock's d (h = 1) with
+// cp.async Q6_RAW_D steps ahead; after the step's barrier each thread reads the other half's
+// piece from the ring, and only then are the next copies requested, so no stage is rewritten
+// while a thread still reads it.
+constexpr int Q6_N = 16, Q6_HT = 8;
+constexpr int Q6_RAW_D = 2, Q6_RAW_R = Q6_RAW_D + 1;
+constexpr int Q6_RAW_STAGE = 7 * RAW_CHUNK;
+constexpr int Q6_B_STEP = 3 * Q6_N * 16;      // one K step of B: first halves, zeros, second halves
+constexpr uint32_t Q6_TCOLS = 2 * 16 * Q6_N;  // 2 buffers x 16 sub-blocks x 16 tokens
+
+size_t gemv_mma6_smem_bytes(int K) {
+    if (K <= 0 || K % 256) return (size_t)-1;
+    const size_t nsb = (size_t)K / 256;
+    const size_t b = 1024 + 2 * MMA_A_BYTES + (size_t)Q6_RAW_R * Q6_RAW_STAGE + (size_t)(K / 32) * Q6_B_STEP +
+                     (size_t)Q6_N * nsb * 4 + (size_t)Q6_N * (K / 16) * 4 + 256;
+    return b <= MMA_SMEM_LIMIT ? b : (size_t)-1;
+}
+
+// The A operand of one step: values 128h .. 128h+127 of row r (low 4 bits from ql, high 2 from
+// qh) as unsigned bytes in natural order, value 128h + 32q + l at K step 4h + q, position l.
+// raw[0..1] = ql[64h .. 64h+31], raw[2..3] = ql[64h+32 .. 64h+63], raw[4..5] = qh[32h .. 32h+31].
+__device__ __forceinline__ void q6k_unpack_a(uint8_t *a, const uint4 (&raw)[6], int r, int h) {
+    const uint32_t lo[8] = {raw[0].x, raw[0].y, raw[0].z, raw[0].w, raw[1].x, raw[1].y, raw[1].z, raw[1].w};
+    const uint32_t hi[8] = {raw[2].x, raw[2].y, raw[2].z, raw[2].w, raw[3].x, raw[3].y, raw[3].z, raw[3].w};
+    const uint32_t qh[8] = {raw[4].x, raw[4].y, raw[4].z, raw[4].w, raw[5].x, raw[5].y, raw[5].z, raw[5].w};
+    uint32_t u[4][8];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        u[0][i] = (lo[i] & 0x0F0F0F0Fu) | ((qh[i] << 4) & 0x30303030u);
+        u[1][i] = (hi[i] & 0x0F0F0F0Fu) | ((qh[i] << 2) & 0x30303030u);
+        u[2][i] = ((lo[i] >> 4) & 0x0F0F0F0Fu) | (qh[i] & 0x30303030u);
+        u[3][i] = ((hi[i] >> 4) & 0x0F0F0F0Fu) | ((qh[i] >> 2) & 0x30303030u);
+    }
+#pragma unroll
+    for (int q = 0; q < 4; q++) {
+        *reinterpret_cast<uint4 *>(a + umma_off(r, (4 * h + q) * 32, 128)) = make_uint4(u[q][0], u[q][1], u[q][2], u[q][3]);
+        *reinterpret_cast<uint4 *>(a + umma_off(r, (4 * h + q) * 32 + 16, 128)) =
+            make_uint4(u[q][4], u[q][5], u[q][6], u[q][7]);
+    }
+}
+
+// byte offset of the 16-byte piece k16 (values 16 k16 .. 16 k16 + 15) of token row t in B
+__device__ __forceinline__ uint32_t q6_b_off(int t, int k16) {
+    return (uint32_t)(k16 >> 1) * Q6_B_STEP + (uint32_t)(k16 & 1) * (2 * Q6_N * 16) + (uint32_t)(t >> 3) * 128 +
+           (uint32_t)(t & 7) * 16;
+}
+
+__global__ void __launch_bounds__(256, 1) kq6_rows_mma_kernel(const __grid_constant__ GemvArgs p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int K = p.K, nsb = K / 256, n16 = K / 16;
+    uint8_t *sA = smem;                                                       // [2][8 K steps][128 rows][32]
+    uint8_t *ring = sA + 2 * MMA_A_BYTES;                                     // [Q6_RAW_R][7][256 threads][16]
+    uint8_t *sB = ring + Q6_RAW_R * Q6_RAW_STAGE;                             // [K/32][3][16 rows][16]
+    float *dA = reinterpret_cast<float *>(sB + (size_t)(K / 32) * Q6_B_STEP);  // [16][nsb]
+    int *bs16 = reinterpret_cast<int *>(dA + Q6_N * nsb);                     // [16][K/16]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(bs16 + Q6_N * n16);         // [2]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // thread (row r of the block, half h): h unpacks values 128h .. 128h+127 of the row and
+    // finishes the epilogue of tokens 8h .. 8h+7
+    const int r = tid & 127, h = tid >> 7;
+    const uint32_t tlane = (uint32_t)((warp & 3) * 32) << 16;
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(smem_u32(tslot), Q6_TCOLS);
+    for (int i = tid; i < (K / 32) * Q6_N; i += 256)  // the zero blocks of B, once
+        *reinterpret_cast<uint4 *>(sB + (size_t)(i / Q6_N) * Q6_B_STEP + Q6_N * 16 + (i % Q6_N) * 16) =
+            make_uint4(0, 0, 0, 0);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    int nrb = 0;  // 128-row blocks over the segments
+    for (int i = 0; i < p.nseg; i++) nrb += p.seg[i].rows / 128;
+    const int ntc = (p.T + Q6_N - 1) / Q6_N;
+    const int total = ntc * nrb;
+    const int u0 = (int)((long long)blockIdx.x * total / gridDim.x);
+    const int u1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
+    // this thread's row of unit u: the segment, its tile, the row's first slot
+    auto unit_src = [&](int u, const uint8_t *&wb, int &s0, int &S, int &si, int &row) {
+        int rb = u - (u / nrb) * nrb;
+        si = 0;
+        while (rb >= p.seg[si].rows / 128) {
+            rb -= p.seg[si].rows / 128;
+            si++;
+        }
+        row = rb * 128 + r;
+        wb = p.seg[si].w + (long long)(row / p.seg[si].rpt) * p.seg[si].tile_bytes;
+        s0 = (row % p.seg[si].rpt) * nsb;
+        S = p.seg[si].S;
+    };
+    const int Q = u1 > u0 ? (u1 - u0) * nsb : 0;
+    const uint8_t *ring_t = ring + tid * 16;
+    const uint32_t ring_s = smem_u32(ring) + (uint32_t)tid * 16;
+    int pf_u = -1, pf_s0 = 0, pf_S = 0;
+    const uint8_t *pf_w = nullptr;
+    auto issue = [&](int q) {
+        if (q < Q) {
+            const int qu = q / nsb, sq = q - qu * nsb;
+            if (u0 + qu != pf_u) {
+                int si_, row_;
+                pf_u = u0 + qu;
+                unit_src(pf_u, pf_w, pf_s0, pf_S, si_, row_);
+            }
+            const int s = pf_s0 + sq;
+            const size_t cs = (size_t)pf_S * 16;
+            const uint8_t *b = pf_w + (size_t)s * 16;
+            const uint32_t dst = ring_s + (uint32_t)(q % Q6_RAW_R) * Q6_RAW_STAGE;
+#pragma unroll
+            for (int c = 0; c < 4; c++) cp_async16(dst + (uint32_t)c * RAW_CHUNK, b + (size_t)(4 * h + c) * cs);
+#pragma unroll
+            for (int c = 0; c < 2; c++) cp_async16(dst + (uint32_t)(4 + c) * RAW_CHUNK, b + (size_t)(8 + 2 * h + c) * cs);
+            if (h == 0) cp_async16(dst + 6u * RAW_CHUNK, b + 12 * cs);                          // the 16 scales
+            else cp_async16(dst + 6u * RAW_CHUNK, pf_w + 13 * cs + (size_t)((2 * s) & ~15));  // d's 16 bytes
+        }
+        cp_async_commit();
+    };
+    // the weights do not depend on the previous kernel: their first copies go out before the wait
+    for (int q = 0; q < Q6_RAW_D; q++) issue(q);
+    pdl_wait();
+    pdl_trigger();
+    const uint32_t idesc = umma_idesc_u8s8(128, Q6_N);
+    const uint32_t aBase = smem_u32(sA), bBase = smem_u32(sB);
+    int cur_tc = -1, tn = 0, q = 0;
+    uint32_t gstep = 0;
+    bool ok = true;
+    unsigned long long best[Q6_HT];
+#pragma unroll
+    for (int t = 0; t < Q6_HT; t++) best[t] = 0ull;
+    // the current chunk's argmax keys: per token, the max over this CTA's rows, one atomic per warp
+    auto flush_best = [&]() {
+        if (!p.amax || cur_tc < 0) return;
+#pragma unroll
+        for (int tt = 0; tt < Q6_HT; tt++) {
+            unsigned long long b = best[tt];
+#pragma unroll
+            for (int o = 16; o >= 1; o >>= 1) {
+                const unsigned long long ob = __shfl_xor_sync(FULL, b, o);
+                b = ob > b ? ob : b;
+            }
+            if (lane == 0 && Q6_HT * h + tt < tn) atomicMax(p.amax + cur_tc * Q6_N + Q6_HT * h + tt, b);
+            best[tt] = 0ull;
+        }
+    };
+    for (int u = u0; ok && u < u1; u++) {
+        const int tc = u / nrb;
+        const uint8_t *wb_;
+        int s0, S_, si, row;
+        unit_src(u, wb_, s0, S_, si, row);
+        const GemvSeg &sg = p.seg[si];
+        if (tc != cur_tc) {  // the chunk's 16 token rows as Q8_K: B (zeros past the last token), scales, 16-value sums
+            flush_best();
+            cur_tc = tc;
+            const int t0 = tc * Q6_N;
+            tn = p.T - t0 < Q6_N ? p.T - t0 : Q6_N;
+            __syncthreads();  // the previous chunk's operands are no longer read
+            const uint32_t sB_s = smem_u32(sB);
+            for (int i = tid; i < Q6_N * n16; i += 256) {
+                const int t = i / n16, k16 = i - t * n16;
+                if (t < tn) cp_async16(sB_s + q6_b_off(t, k16), p.q8_qs + (long long)(t0 + t) * K + k16 * 16);
+                else *reinterpret_cast<uint4 *>(sB + q6_b_off(t, k16)) = make_uint4(0, 0, 0, 0);
+            }
+            for (int i = tid; i < Q6_N * nsb; i += 256) {
+                const int t = i / nsb, b = i - t * nsb;
+                dA[i] = t < tn ? p.q8_d[(long long)(t0 + t) * nsb + b] : 0.0f;
+            }
+            cp_async_commit();
+            cp_async_wait<0>();  // (the ring's copies in flight complete here too)
+            __syncthreads();
+            for (int i = tid; i < Q6_N * n16; i += 256) {  // bs16[t][k16]: the sum of those 16 values
+                const uint4 v = *reinterpret_cast<const uint4 *>(sB + q6_b_off(i / n16, i % n16));
+                int s = __dp4a((int)v.x, 0x01010101, 0);
+                s = __dp4a((int)v.y, 0x01010101, s);
+                s = __dp4a((int)v.z, 0x01010101, s);
+                bs16[i] = __dp4a((int)v.w, 0x01010101, s);
+            }
+            __syncthreads();
+        }
+        float acc[Q6_HT];
+#pragma unroll
+        for (int t = 0; t < Q6_HT; t++) acc[t] = 0.0f;
+        uint4 raw[6];
+        int sc[16], psc[16];
+        float dw = 0.0f, pdw = 0.0f;
+        auto epilogue = [&](int sb, uint32_t gs) -> bool {
+            if (!mbar_wait(&bars[gs & 1], (gs >> 1) & 1, p.err)) return false;
+            tc_fence_after();
+            int sumi[Q6_HT];
+#pragma unroll
+            for (int t = 0; t < Q6_HT; t++) sumi[t] = 0;
+            const uint32_t col0 = tmem + tlane + (gs & 1) * 16 * Q6_N + h * Q6_HT;
+#pragma unroll
+            for (int j0 = 0; j0 < 16; j0 += 4) {
+                uint32_t v[4][8];
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) tmem_ld8(col0 + (uint32_t)((j0 + jj) * Q6_N), v[jj]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) tmem_pin(v[jj]);
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++)
+#pragma unroll
+                    for (int t = 0; t < Q6_HT; t++) sumi[t] += psc[j0 + jj] * (int)v[jj][t];
+            }
+#pragma unroll
+            for (int tt = 0; tt < Q6_HT; tt++) {
+                const int t = Q6_HT * h + tt;
+                const int4 *bq = reinterpret_cast<const int4 *>(bs16 + t * n16 + sb * 16);
+                int corr = 0;
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const int4 b = bq[c];
+                    corr += psc[4 * c] * b.x + psc[4 * c + 1] * b.y + psc[4 * c + 2] * b.z + psc[4 * c + 3] * b.w;
+                }
+                const int si_ = sumi[tt] - 32 * corr;
+                acc[tt] = __fadd_rn(acc[tt], __fmul_rn(__int2float_rn(si_), __fmul_rn(pdw, dA[t * nsb + sb])));
+            }
+            return true;
+        };
+        for (int st = 0; st < nsb; st++, q++) {
+            const uint32_t gs = gstep++;
+            cp_async_wait<Q6_RAW_D - 1>();  // this thread's pieces of step q have landed
+            const uint8_t *stage = ring + (size_t)(q % Q6_RAW_R) * Q6_RAW_STAGE;
+#pragma unroll
+            for (int c = 0; c < 6; c++) raw[c] = *reinterpret_cast<const uint4 *>(stage + c * RAW_CHUNK + tid * 16);
+            q6k_unpack_a(sA + (gs & 1) * MMA_A_BYTES, raw, r, h);
+            fence_proxy_async();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0) {
+                const uint32_t a0 = aBase + (gs & 1) * MMA_A_BYTES;
+#pragma unroll 1
+                for (int j = 0; j < 8; j++) {
+                    const uint64_t ad = umma_desc(a0 + j * 4096, 128, 256);
+                    const uint32_t bj = bBase + (uint32_t)(st * 8 + j) * Q6_B_STEP;
+                    const uint32_t d0 = tmem + (gs & 1) * 16 * Q6_N + (uint32_t)(2 * j) * Q6_N;
+                    umma_i8(d0, ad, umma_desc(bj, 256, 128), idesc, false);
+                    umma_i8(d0 + Q6_N, ad, umma_desc(bj + 2 * 128, 256, 128), idesc, false);
+                }
+                umma_commit(smem_u32(&bars[gs & 1]));
+            }
+            {  // the step's scales and d from both halves' pieces (visible after the barrier)
+                const uint4 scv = *reinterpret_cast<const uint4 *>(stage + 6 * RAW_CHUNK + r * 16);
+                const uint4 dv = *reinterpret_cast<const uint4 *>(stage + 6 * RAW_CHUNK + (128 + r) * 16);
+                const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+#pragma unroll
+                for (int j = 0; j < 16; j++) sc[j] = byte_s(scw[j >> 2], j & 3);
+                const int o = (2 * (s0 + st)) & 15;  // d's byte offset in the piece (even)
+                const unsigned long long dword = o < 8 ? ((unsigned long long)dv.y << 32) | dv.x
+                                                       : ((unsigned long long)dv.w << 32) | dv.z;
+                dw = __half2float(__ushort_as_half((unsigned short)((dword >> (8 * (o & 7))) & 0xffffu)));
+            }
+            issue(q + Q6_RAW_D);  // into the stage of step q - 1, which every thread has finished reading
+            if (st > 0 && !__syncthreads_and(epilogue(st - 1, gs - 1))) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j++) psc[j] = sc[j];
+            pdw = dw;
+            tc_fence_before();
+        }
+        if (!ok) break;
+        if (!__syncthreads_and(epilogue(nsb - 1, gstep - 1))) {
+            ok = false;
+            break;
+        }
+        tc_fence_before();
+        const int t0 = tc * Q6_N + Q6_HT * h;
+#pragma unroll
+        for (int tt = 0; tt < Q6_HT; tt++) {
+            if (Q6_HT * h + tt < tn) {
+                float y = acc[tt];
+                if (p.res) y = __fadd_rn(p.res[(long long)(t0 + tt) * p.res_stride + sg.out_off + row], acc[tt]);
+                p.y[(long long)(t0 + tt) * p.y_stride + sg.out_off + row] = y;
+                const unsigned long long key =
+                    ((unsigned long long)((unsigned)total_key(y) ^ 0x80000000u) << 32) | (unsigned)(sg.out_off + row);
+                best[tt] = key > best[tt] ? key : best[tt];
+            }
+        }
+    }
+    if (ok) flush_best();
+    cp_async_wait_all();  // no copy into this CTA's shared memory outlives it
+    if (!ok && tid == 0) {
+        for (uint32_t b = 0; b < 2; b++) {
+            const long long last = gstep == 0 ? -1 : ((long long)((gstep - 1) & 1) == b ? gstep - 1 : (long long)gstep - 2);
+            if (last >= 0) mbar_wait(&bars[b], (uint32_t)(last >> 1) & 1, nullptr);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, Q6_TCOLS);
+}
+
+cudaError_t launch_gemv_mma6(const GemvArgs &a, int grid, cudaStream_t st, bool pdl) {
+    const size_t smem = gemv_mma6_smem_bytes(a.K);
+    if (smem == (size_t)-1) return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kq6_rows_mma_kernel, a);
+}
+
 cudaError_t launch_gemv_mma(const GemvArgs &a, int grid, cudaStream_t st, bool pdl) {
     const int n = gemv_mma_tokens(a.K);
     if (!n) return cudaErrorInvalidValue;
@@ -681,7 +1009,7 @@ cudaError_t init_mma_attributes() {
     if ((e = cudaGetDevice(&dev))) return e;
     if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
     const void *kerns[] = {(const void *)gateup_mma_kernel, (const void *)kq_rows_mma_kernel<32>,
-                           (const void *)kq_rows_mma_kernel<16>};
+                           (const void *)kq_rows_mma_kernel<16>, (const void *)kq6_rows_mma_kernel};
     for (const void *k : kerns) {
         cudaFuncAttributes fa;
         if ((e = cudaFuncGetAttributes(&fa, k))) return e;

@@ -172,7 +172,10 @@ int bt_profile_decode(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const ui
  * holds every SM for the whole step, default 1; 0 = one kernel per phase), "mma" (Q4_K
  * contractions of batched steps on the tensor cores, default 1), "mma_min_units" (the batched
  * GEMV goes to the tensor cores from this many 128-row x token-chunk units, default 32),
- * "mma_grid" (CTAs of the tensor-core kernels, default 0 = one per SM), "wait_limit_us" (every
+ * "mma_grid" (CTAs of the tensor-core kernels, default 0 = one per SM), "token_groups" (a
+ * batched dp4a GEMV with fewer tiles than half the grid's warps, such as a 512-row Q6_K attn_v,
+ * runs as one launch over units of (token group, tile), default 1; 0 = token chunks whose units
+ * carry every token of the chunk; the results are the same bits), "wait_limit_us" (every
  * bounded wait of the persistent step gives up after this long, default 0 = about 1 s), and the
  * failure drill "fault_cta" / "fault_barrier" (off at 0): in each persistent step, CTA fault_cta
  * leaves at its grid barrier number fault_barrier (1-based) without arriving, as a CTA that died
@@ -246,7 +249,7 @@ int bt_engine_enable_ep(bt_engine *e, const void *unique_id, size_t nbytes, int 
 int bt_debug_dequant(uint32_t type, const void *bytes, uint64_t n, float *out);
 /* route() result for one layer and token (stream.rs:869-888): ids in descending probability,
  * renormalised weights. `token` indexes the token list of the last bt_forward; only its last
- * step (its last 64 tokens) is kept. After bt_generate_greedy, token i is sequence i's last step. */
+ * step (its last 128 tokens at most: a call's tokens run in steps of up to 128) is kept. After bt_generate_greedy, token i is sequence i's last step. */
 int bt_debug_topk(const bt_engine *e, uint32_t layer, uint32_t token, int32_t *ids, float *weights);
 /* residual stream after the last layer for `token`, indexed as for bt_debug_topk (n_embd floats) */
 int bt_debug_hidden(const bt_engine *e, uint32_t token, float *out);

@@ -276,12 +276,12 @@ def test_cfg0_prefill_128_then_64_greedy_steps():
         got0 = runner.forward_cached(cache, prompt, 0)
         assert_logits(got0, want0)
         for il in range(cfg.n_layer):
-            for t in (64, 100, 127):  # the debug hooks keep the last 64-token step
+            for t in (3, 64, 100, 127):  # the debug hooks keep the last step: the whole prompt
                 gi, gw = e.debug_topk(il, t)
                 oi, ow = model.topk(il, t)
                 assert np.array_equal(gi, oi) and np.array_equal(bits(gw), bits(ow))
         with pytest.raises(bt.BtError):
-            e.debug_topk(0, 3)
+            e.debug_topk(0, 128)
         first = orc.argmax(want0)
         toks = runner.generate_greedy(cache, [first], 64)
         want = model.greedy(first, 64)
@@ -525,9 +525,54 @@ def test_tensor_core_gemv_matches_dp4a_and_oracle():
         assert_logits(outs["mma"][1][i], m1.forward([int(prompt[i])], 0))
 
 
+@pytest.mark.parametrize("grid", [4, 0])
+def test_tensor_core_q6k_gemv_and_head_match_dp4a_and_oracle(grid):
+    """Q6_K on tcgen05 (two MMAs per 32-value K step against zero-padded halves of the
+    activations, one per 16-value sub-block): q/k/v all Q6_K (K = 512), and the Q6_K output head
+    with its argmax keys at more than 8 outputs, give the dp4a kernels' bits and the oracle's --
+    a 100-token prefill, a 40-sequence step, then 3 greedy steps of the 40 sequences (the head's
+    keys pick the tokens). grid 4: every CTA streams many (token chunk, row block) units."""
+    types = [[bt._lib.TYPE_Q6_K] * 3 + [bt._lib.TYPE_Q4_K] * 4] * 2
+    cfg = bt.config("tiny", n_head=32, n_head_kv=4, n_vocab=1024, layer_types=types)
+    W = bt.synth_model(cfg, seed=12)
+    rng = np.random.default_rng(57)
+    prompt = rng.integers(0, cfg.n_vocab, 100)
+    outs = {}
+    for mode in ("mma", "dp4a"):
+        e = bt.Engine(cfg, W)
+        if mode == "mma":
+            e.set_option("mma_min_units", 1)
+            e.set_option("mma_grid", grid)
+        else:
+            e.set_option("mma", 0)
+        cache = bt.KvCache(e, max_positions=256, max_seqs=41)
+        runner = bt.StreamingRunner(e)
+        lg = runner.forward_batch(cache, [0], [prompt], [0])
+        steps = runner.forward_batch(cache, list(range(1, 41)), [[int(t)] for t in prompt[:40]], [0] * 40)
+        first = [int(np.argmax(steps[i])) for i in range(40)]
+        toks = runner.generate_greedy(cache, first, 3, seqs=list(range(1, 41)))
+        outs[mode] = (lg, steps, toks, cache.layer_bytes(1, 0))
+        cache.close()
+        e.close()
+    assert np.array_equal(bits(outs["mma"][0]), bits(outs["dp4a"][0]))
+    assert np.array_equal(bits(outs["mma"][1]), bits(outs["dp4a"][1]))
+    assert np.array_equal(outs["mma"][2], outs["dp4a"][2])
+    assert np.array_equal(outs["mma"][3][0], outs["dp4a"][3][0])
+    assert np.array_equal(outs["mma"][3][1], outs["dp4a"][3][1])
+    model = orc.Model(cfg, W)
+    assert_logits(outs["mma"][0][0], model.forward(list(prompt), 0))
+    model.close()
+    for i in (0, 21, 39):
+        m1 = orc.Model(cfg, W)
+        want = m1.forward([int(prompt[i])], 0)
+        assert_logits(outs["mma"][1][i], want)
+        assert list(outs["mma"][2][:, i]) == m1.greedy(orc.argmax(want), 3)
+        m1.close()
+
+
 def test_tensor_core_gateup_matches_dp4a_kernel(tiny_cfg, tiny_weights):
     """The grouped gate/up on tcgen05 (int8 MMA per K-quant sub-block, integer-exact) and the
-    dp4a grouped kernel give the same bits: a 64-token prefill sub-step and a 24-sequence step."""
+    dp4a grouped kernel give the same bits: a 70-token prefill step and a 24-sequence step."""
     rng = np.random.default_rng(55)
     prompt = rng.integers(0, tiny_cfg.n_vocab, 70)
     outs = {}

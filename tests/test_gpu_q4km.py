@@ -5,7 +5,7 @@ and its batch-1 steps run the persistent step kernel at G = 8 query heads per KV
 tests run that mix through every path the benchmark uses, against the CPU oracle, bit for bit:
 
 - a 4-layer slice of the benchmark shape (hidden 2048, 32/4 heads, 128 experts top-8, expert
-  width 768, vocab 151936): prefill through the batched kernels (64-token sub-steps, grouped
+  width 768, vocab 151936): prefill through the batched kernels (128-token steps, grouped
   experts, Q6_K down and attn_v), then batch-1 steps through the persistent kernel (G = 8) and
   through the per-phase kernels, past three attention chunks; and a batched single-token step
   of twelve sequences at contexts up to 1500 (grouped experts, warp-pair attention);
@@ -64,7 +64,7 @@ def test_q4km_prefill_then_single_token_steps(q4km, persistent):
         want = model.forward(prompt, 0)
         assert_logits(runner.forward_cached(cache, prompt, 0), want)
         for il in range(cfg.n_layer):
-            for t in (260, 299):  # the debug hook keeps the last 64-token sub-step (256..299)
+            for t in (260, 299):  # the debug hook keeps the last step (256..299)
                 gi, gw = e.debug_topk(il, t)
                 oi, ow = model.topk(il, t)
                 assert np.array_equal(gi, oi) and np.array_equal(bits(gw), bits(ow))
@@ -177,3 +177,32 @@ def test_expert_stream_kernel_matches_per_layer_kernels(q4km):
         model.close()
     finally:
         e.close()
+
+
+@pytest.mark.parametrize("n_tok", [13, 64, 200])
+def test_token_group_gemv_matches_token_chunks(q4km, n_tok):
+    """The batched dp4a GEMV over few tiles (the Q6_K attn_v of even layers) splits its tokens
+    into groups (option token_groups): prefill logits and cache bytes equal the token-chunk
+    launches' bit for bit, and the oracle's, with a ragged last group."""
+    cfg, W = q4km
+    prompt = np.random.default_rng(50 + n_tok).integers(0, cfg.n_vocab, n_tok)
+    outs = []
+    for groups in (1, 0):
+        e = bt.Engine(cfg, W)
+        e.set_option("token_groups", groups)
+        try:
+            cache = bt.KvCache(e, max_positions=256)
+            logits = bt.StreamingRunner(e).forward_cached(cache, prompt, 0)
+            kv = [cache.layer_bytes(il) for il in range(cfg.n_layer)]
+            outs.append((logits, kv))
+            cache.close()
+        finally:
+            e.close()
+    assert np.array_equal(bits(outs[0][0]), bits(outs[1][0]))
+    for (k0, v0), (k1, v1) in zip(outs[0][1], outs[1][1]):
+        assert np.array_equal(k0, k1) and np.array_equal(v0, v1)
+    model = orc.Model(cfg, W)
+    try:
+        assert_logits(outs[0][0], model.forward(prompt, 0))
+    finally:
+        model.close()
