@@ -27,6 +27,9 @@
 #include "step_kernel.cuh"
 #include "expert_stream.cuh"
 
+// Under expert parallelism every exchange carries a step's full capacity of (token, expert)
+// slots to every rank, so the steps are kept at 64 tokens there.
+constexpr int EP_STEP_TOKENS = 64;
 #ifndef BT_STEP_TOKENS
 #define BT_STEP_TOKENS 128  // tokens of one step of the per-phase kernels (longer calls are cut into steps)
 #endif
@@ -477,6 +480,9 @@ static cudaError_t alloc_q8(bt_engine *e, size_t rows) {
     e->q8_k = K;
     return cudaSuccess;
 }
+
+// tokens of one step: the scratch capacity, or less under expert parallelism
+static int step_cap(const bt_engine *e) { return e->ep && EP_STEP_TOKENS < e->TB ? EP_STEP_TOKENS : e->TB; }
 
 static int alloc_scratch(bt_engine *e) {
     const bt_model_desc &d = e->d;
@@ -2009,7 +2015,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             shexp = e->sh_out.as<float>();
         }
         if (e->ep) {  // expert parallelism: rows to the owning ranks, experts there, rows back
-            const int S = e->TB * K, n = e->ep_n, per = NE / n;
+            const int S = step_cap(e) * K, n = e->ep_n, per = NE / n;
             const NcclApi *api = nccl_api();
             EpPackArgs pa{};
             pa.sel_ids = e->sel_ids.as<int>();
@@ -2038,7 +2044,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             timer_end(e);
             GroupArgs ga{};
             ga.sel_ids = e->ep_recv_meta.as<int>();
-            ga.T = n * e->TB;
+            ga.T = n * step_cap(e);
             ga.K = K;
             ga.NE = NE;
             ga.g_count = e->g_count.as<int>();
@@ -2239,7 +2245,7 @@ extern "C" int bt_forward(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, cons
     while (g < total) {
         StepPlan p;
         std::map<int, int> seq_slot;
-        while (p.T < e->TB && g < total) {
+        while (p.T < step_cap(e) && g < total) {
             uint32_t s = seq_ids[si];
             p.tokens.push_back((int)tokens[g]);
             p.seq_of.push_back((int)s);
@@ -2303,7 +2309,8 @@ static int greedy_prepare(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, cons
                           uint32_t n_seqs, uint32_t n_steps, StepPlan &p) {
     if (!e || !kv || !seq_ids || !first_tokens) return fail(BT_ERR_INVALID, "null argument");
     if (kv->e != e) return fail(BT_ERR_INVALID, "KV pool belongs to another engine");
-    if (n_seqs == 0 || n_seqs > (uint32_t)e->TB) return fail(BT_ERR_INVALID, "1..step-capacity sequences per greedy batch");
+    if (n_seqs == 0 || n_seqs > (uint32_t)step_cap(e))
+        return fail(BT_ERR_INVALID, "1..step-capacity sequences per greedy batch (64 under expert parallelism)");
     CK(cudaSetDevice(e->device));
     std::vector<char> seen(kv->max_seqs, 0);
     for (uint32_t i = 0; i < n_seqs; i++) {
@@ -2964,7 +2971,8 @@ extern "C" int bt_engine_enable_ep(bt_engine *e, const void *unique_id, size_t n
     const NcclApi *api = nccl_api();
     if (!api) return fail(BT_ERR_UNSUPPORTED, "libnccl.so.2 could not be loaded");
     CK(cudaSetDevice(e->device));
-    const size_t S = (size_t)e->TB * d.n_expert_used, E = d.n_embd, F = d.n_ff_exp, n = (size_t)n_ranks;
+    const size_t S = (size_t)(EP_STEP_TOKENS < e->TB ? EP_STEP_TOKENS : e->TB) * d.n_expert_used, E = d.n_embd,
+                 F = d.n_ff_exp, n = (size_t)n_ranks;
     CK(e->ep_send_meta.alloc(n * S * 4));
     CK(e->ep_recv_meta.alloc(n * S * 4));
     CK(e->ep_send_rows.alloc(n * S * E * 4));

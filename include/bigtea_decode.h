@@ -237,8 +237,9 @@ int bt_expert_cache_simulate_device(int policy, uint32_t capacity, uint32_t n_la
  *   - the token's own rank adds them in the reference's order (stream.rs:1232-1284), so the
  *     results equal a single-GPU run bit for bit.
  * Attention, the router and the head stay on each sequence's rank (data parallel). Every
- * rank must run the same sequence of steps: the exchange has fixed sizes and all ranks take
- * part in every layer. */
+ * rank must run the same sequence of steps: the exchange has fixed sizes (64 tokens x
+ * n_expert_used slots per rank pair; a call's tokens run in steps of at most 64 here) and all
+ * ranks take part in every layer. */
 /* an NCCL unique id for bt_engine_enable_ep (nbytes >= 128); rank 0 makes it and shares it */
 int bt_ep_unique_id(void *out, size_t nbytes);
 /* collective over the n_ranks engines; disables the persistent single-kernel step */

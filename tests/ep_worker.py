@@ -22,7 +22,8 @@ sys.path.insert(0, ROOT)
 def rank_workload(bt, engine, cfg, rank: int) -> dict:
     """The steps of one rank: one single-token step of every sequence, a mixed step (two short
     prompts beside single tokens), four greedy graph-replayed steps, one more single-token step.
-    Every call is one engine step (at most 128 tokens), the same count on every rank."""
+    Every call is one engine step (at most 64 tokens under expert parallelism), the same count on
+    every rank."""
     n_seq = 3 + 4 * (rank % 3)
     rng = np.random.default_rng(100 + rank)
     ctxs = [int(c) for c in rng.integers(100, 1500, n_seq)]
