@@ -91,6 +91,8 @@ SIGNATURES = {
     "bt_forward": (C.c_int, [_P, _P, _U32P, _U32P, _U32P, _U32P, C.c_uint32, _F32P]),
     "bt_generate_greedy": (C.c_int, [_P, _P, _U32P, _U32P, C.c_uint32, C.c_uint32, _U32P, _F32P]),
     "bt_last_device_ms": (C.c_int, [_P, C.POINTER(C.c_double)]),
+    "bt_host_alloc": (C.c_int, [C.c_uint64, C.POINTER(C.c_void_p)]),
+    "bt_host_free": (C.c_int, [_P]),
     "bt_bench_experts": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint32, C.POINTER(C.c_double),
                                    C.POINTER(C.c_uint64), C.POINTER(C.c_float)]),
     "bt_profile_decode": (C.c_int, [_P, _P, _U32P, _U32P, C.c_uint32, C.c_uint32, C.POINTER(KernelTime),

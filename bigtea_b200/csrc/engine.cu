@@ -490,7 +490,12 @@ static int alloc_scratch(bt_engine *e) {
     const int K = d.n_expert_used, NE = d.n_expert, F = d.n_ff_exp, G = d.n_head / d.n_head_kv;
     e->part_chunks = (int)((d.max_positions + ATTN_CHUNK - 1) / ATTN_CHUNK);
     e->max_out = 256;
-    CK(alloc_q8(e, (size_t)TB));
+    // Q8_K staging: TB rows of the widest GEMV input, or TB * K rows of SiLU products (the grouped
+    // down's input), whichever needs more
+    {
+        const size_t kd = std::max<size_t>(d.n_embd, (size_t)d.n_head * d.head_dim);
+        CK(alloc_q8(e, std::max<size_t>((size_t)TB, ((size_t)TB * K * F + kd - 1) / kd)));
+    }
     CK(e->x.alloc((size_t)TB * E * 4));
     CK(e->ffn_in.alloc((size_t)TB * E * 4));
     CK(e->fn.alloc((size_t)TB * E * 4));
@@ -1262,10 +1267,11 @@ static cudaError_t run_gemv(bt_engine *e, const QMat *const *mats, const int *ou
     return r;
 }
 
-// Q6_K matrices the tensor-core kernel takes: whole 128-row blocks, tiles that start on 16 bytes
-// and a run of superblock scales d that ends on 16 bytes
+// Q6_K matrices the tensor-core kernel takes: whole 128-row blocks (a tile's run of superblock
+// scales d is padded to 16 bytes, so every tile starts on 16 bytes and each d's 16-byte piece lies
+// inside its tile)
 static bool mma6_fits(const QMat &m) {
-    return m.type == T_Q6_K && m.rows % 128 == 0 && m.g.tile_bytes % 16 == 0 && (2 * m.g.S) % 16 == 0;
+    return m.type == T_Q6_K && m.rows % 128 == 0 && m.g.tile_bytes % 16 == 0;
 }
 
 // The arguments of a tensor-core GEMV over n segments (activations from the Q8_K staging)
@@ -1660,6 +1666,24 @@ static bool use_gateup_mma(const bt_engine *e, const Layer &l, size_t rows) {
            gateup_mma_smem_bytes((int)e->d.n_embd) <= (size_t)max_dynamic_smem() && rows <= e->q8_rows;
 }
 
+// The tensor-core down of the grouped path: a Q4_K down, output rows in whole 128-row blocks, and
+// room in the Q8_K staging for `rows` SiLU-product rows.
+static bool use_down_mma(const bt_engine *e, const Layer &l, size_t rows) {
+    const int F = (int)e->d.n_ff_exp, nsb = F / 256;
+    return e->mma && l.down.type == T_Q4_K && F % 256 == 0 && nsb >= 1 && l.down.g.rpt * nsb <= 32 &&
+           e->d.n_embd % 128 == 0 && down_mma_smem_bytes(F) <= (size_t)max_dynamic_smem() &&
+           rows * (size_t)F <= e->q8_rows * e->q8_k;
+}
+
+// The down input rows (a.act: `rows` (token, slot) rows of F SiLU products) as Q8_K rows.
+static cudaError_t stage_down_q8(bt_engine *e, ExpertArgs &a, int rows, cudaStream_t st, bool pdl) {
+    a.q8_qs = e->q8_qs.as<int8_t>();
+    a.q8_d = e->q8_d.as<float>();
+    a.q8_bs = e->q8_bs.as<int>();
+    return launch_q8_stage(a.act, a.F, nullptr, nullptr, 0.0f, a.F, rows, e->q8_qs.as<int8_t>(), e->q8_d.as<float>(),
+                           e->q8_bs.as<int>(), st, pdl);
+}
+
 // The routed experts of layer il for the T tokens of a step, on one GPU: the grouped kernels
 // (T > MAX_T: each selected expert's weights once per step) or the per-token ones. Each token's
 // selection comes from sel_ids / sel_w ([T][K], ascending ids) and its normalised row from e->fn;
@@ -1707,6 +1731,7 @@ static int launch_layer_experts(bt_engine *e, int il, int T, const int *sel_ids,
             a.d_expert_bytes = l.down.mat_bytes;
             a.d_nsb = l.down.g.nsb;
             a.d_tile_bytes = l.down.g.tile_bytes;
+            a.d_rpt = l.down.g.rpt;
             a.E = E;
             a.F = F;
             a.K = K;
@@ -1750,7 +1775,12 @@ static int launch_layer_experts(bt_engine *e, int il, int T, const int *sel_ids,
             a.nst = 1;
             a.nst = pick_nst_cap(a.slot_bytes, down_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
             timer_begin(e, "expert_down");
-            CK(launch_down_grouped(a, e->n_sm, st, pdl));
+            if (use_down_mma(e, l, (size_t)T * K)) {
+                CK(stage_down_q8(e, a, T * K, st, pdl));
+                CK(launch_down_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, st, pdl));
+            } else {
+                CK(launch_down_grouped(a, e->n_sm, st, pdl));
+            }
             timer_end(e);
             timer_begin(e, "expert_combine");
             CK(launch_down_combine(a, st, pdl));
@@ -1776,6 +1806,7 @@ static int launch_layer_experts(bt_engine *e, int il, int T, const int *sel_ids,
             a.d_expert_bytes = l.down.mat_bytes;
             a.d_nsb = l.down.g.nsb;
             a.d_tile_bytes = l.down.g.tile_bytes;
+            a.d_rpt = l.down.g.rpt;
             a.E = E;
             a.F = F;
             a.K = K;
@@ -2076,6 +2107,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.d_expert_bytes = l.down.mat_bytes;
             a.d_nsb = l.down.g.nsb;
             a.d_tile_bytes = l.down.g.tile_bytes;
+            a.d_rpt = l.down.g.rpt;
             a.E = E;
             a.F = F;
             a.K = K;
@@ -2111,7 +2143,12 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.nst = 1;
             a.nst = pick_nst_cap(a.slot_bytes, down_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
             timer_begin(e, "expert_down");
-            CK(launch_down_grouped(a, e->n_sm, st, pdl));
+            if (use_down_mma(e, l, (size_t)n * S)) {
+                CK(stage_down_q8(e, a, n * S, st, pdl));
+                CK(launch_down_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, st, pdl));
+            } else {
+                CK(launch_down_grouped(a, e->n_sm, st, pdl));
+            }
             timer_end(e);
             timer_begin(e, "ep_combine_exchange");
             NK(api->GroupStart());
@@ -2282,7 +2319,17 @@ extern "C" int bt_forward(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, cons
         e->last_first = g - p.T;
     }
     const size_t lbytes = (size_t)n_seqs * e->d.n_vocab * 4;
-    if (logits_out && n_seqs <= (uint32_t)STEP_MAX_T) {
+    cudaPointerAttributes pa{};
+    const bool out_pinned = logits_out && cudaPointerGetAttributes(&pa, logits_out) == cudaSuccess &&
+                            pa.type == cudaMemoryTypeHost;
+    if (logits_out && !out_pinned) cudaGetLastError();  // (pageable memory: not an error)
+    if (out_pinned) {
+        // page-locked output (bt_host_alloc): the logits go straight into it, behind one wait
+        CK(cudaMemcpyAsync(e->err_host, e->err.p, 4, cudaMemcpyDeviceToHost, e->st));
+        CK(cudaMemcpyAsync(logits_out, e->logits.p, lbytes, cudaMemcpyDeviceToHost, e->st));
+        if ((r = wait_stream(e))) return r;
+        if ((r = err_word(e, *e->err_host))) return r;
+    } else if (logits_out && n_seqs <= (uint32_t)STEP_MAX_T) {
         // error word and logits through pinned staging, behind one wait
         CK(cudaMemcpyAsync(e->err_host, e->err.p, 4, cudaMemcpyDeviceToHost, e->st));
         CK(cudaMemcpyAsync(e->logits_host, e->logits.p, lbytes, cudaMemcpyDeviceToHost, e->st));
@@ -2595,6 +2642,25 @@ extern "C" int bt_bench_experts(bt_engine *e, uint32_t T, uint32_t n_iters, uint
     }
     *ms_per_pass = (double)ms / n_iters;
     *bytes_per_pass = bytes;
+    return BT_OK;
+}
+
+extern "C" int bt_host_alloc(uint64_t bytes, void **out) {
+    if (!out || bytes == 0) return fail(BT_ERR_INVALID, "bad argument");
+    *out = nullptr;
+    if (cudaHostAlloc(out, (size_t)bytes, cudaHostAllocDefault) != cudaSuccess) {
+        cudaGetLastError();
+        *out = nullptr;
+        return fail(BT_ERR_OOM, "page-locked host allocation failed");
+    }
+    return BT_OK;
+}
+
+extern "C" int bt_host_free(void *p) {
+    if (p && cudaFreeHost(p) != cudaSuccess) {
+        cudaGetLastError();
+        return fail(BT_ERR_INVALID, "not a bt_host_alloc block");
+    }
     return BT_OK;
 }
 

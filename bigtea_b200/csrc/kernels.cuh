@@ -70,7 +70,7 @@ struct ExpertArgs {
     int g_nsb, g_rpt, g_S, g_tile_bytes, g_n_tiles;
     int u_tile_bytes;
     long long g_expert_bytes, u_expert_bytes, d_expert_bytes;
-    int d_nsb, d_tile_bytes;
+    int d_nsb, d_tile_bytes, d_rpt;  // down: superblocks per row, tile bytes, rows per tile
     int E, F, K, T, workers;
     const int *sel_ids;        // [T][K] ascending expert ids
     const float *sel_w;        // [T][K] their renormalised weights
@@ -232,6 +232,10 @@ cudaError_t launch_i8_mma_probe(const uint8_t *A, const int8_t *B, int32_t *D, i
 // grouped gate/up on tcgen05 (Q4_K gate and up, F a multiple of 128); one CTA per SM
 size_t gateup_mma_smem_bytes(int E);
 cudaError_t launch_gateup_mma(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
+// grouped down on tcgen05 (Q4_K down, tiles of 32 / nsb rows, E a multiple of 128); its B operand
+// is the SiLU products as Q8_K rows, one per (token, slot); one CTA per SM
+size_t down_mma_smem_bytes(int F);
+cudaError_t launch_down_mma(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
 cudaError_t init_mma_attributes();
 // batched GEMV on tcgen05 (Q4_K segments of whole 128-row blocks, no argmax); one CTA per SM
 size_t gemv_mma_smem_bytes(int K);

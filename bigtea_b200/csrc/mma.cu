@@ -378,6 +378,213 @@ cudaError_t launch_gateup_mma(const ExpertArgs &a, int grid, cudaStream_t st, bo
     return cudaLaunchKernelEx(&cfg, gateup_mma_kernel, a);
 }
 
+// ====================================================================== grouped down on tcgen05
+// Q4_K down of the grouped batched path: the gate/up kernel's scheme with one matrix. Unit =
+// (chunk of at most 16 (token, slot) rows of one expert, block of 128 output rows); K = F, one
+// superblock per step. The B operand is the chunk's SiLU-product rows as Q8_K (staged per
+// (token, slot) row by q8_stage_kernel, as the dp4a kernel stages them); the epilogue writes each
+// (token, slot)'s row sums to dpart for the combine. Thread r reads row r of the block from its
+// tile (d_rpt rows of nsb superblocks each); Q4_K tiles start on 16 bytes.
+size_t down_mma_smem_bytes(int F) {
+    const size_t nsb = (size_t)F / 256;
+    return 1024 + (size_t)MMA_N * F + 2 * MMA_A_BYTES + (size_t)RAW_R * RAW_STAGE + (size_t)MMA_N * nsb * (4 + 32) +
+           2 * MMA_N * 4 + 256;
+}
+
+__global__ void __launch_bounds__(256, 1) down_mma_kernel(const __grid_constant__ ExpertArgs p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int F = p.F, nsb = F / 256, rpt = p.d_rpt, S = rpt * nsb;
+    uint8_t *sB = smem;                                                  // [F/32 K steps][16 rows][32]
+    uint8_t *sA = sB + MMA_N * F;                                        // [2][8 K steps][128 rows][32]
+    uint8_t *ring = sA + 2 * MMA_A_BYTES;                                // [RAW_R][5][256 threads][16]
+    float *dA = reinterpret_cast<float *>(ring + RAW_R * RAW_STAGE);     // [16][nsb] activation scales
+    int *bsA = reinterpret_cast<int *>(dA + MMA_N * nsb);                // [16][nsb][8] 32-value sums
+    int *tk_s = bsA + MMA_N * nsb * 8;                                   // [16]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(tk_s + 2 * MMA_N);    // [2]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    // thread (row r of the block, half h): h loads and unpacks nibble groups 2h, 2h+1 of the
+    // row and finishes the epilogue of rows 8h .. 8h+7 of the chunk
+    const int r = tid & 127, h = tid >> 7;
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(smem_u32(tslot), MMA_TMEM_COLS);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    const uint32_t tlane = (uint32_t)((warp & 3) * 32) << 16;  // this warp's TMEM lanes
+    pdl_wait();  // the groups and the staged products come from the kernels before
+    const int nrb = p.E / 128;
+    const int total = *p.g_nchunks * nrb;
+    const int u0 = (int)((long long)blockIdx.x * total / gridDim.x);
+    const int u1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
+    pdl_trigger();
+    const uint32_t idesc = umma_idesc_u8s8(128, MMA_N);
+    const uint32_t aBase = smem_u32(sA), bBase = smem_u32(sB);
+    // this thread's row of unit u: tile (row / rpt), slot (row % rpt) * nsb + superblock
+    auto unit_src = [&](int u, const uint8_t *&db, int &s0) {
+        const int ci = u / nrb, rb = u - ci * nrb;
+        const int row = rb * 128 + r;
+        db = expert_down(p, p.g_chunk_e[ci]) + (long long)(row / rpt) * p.d_tile_bytes;
+        s0 = (row % rpt) * nsb;
+    };
+    const int Q = u1 > u0 ? (u1 - u0) * nsb : 0;
+    const uint8_t *ring_t = ring + tid * 16;
+    const uint32_t ring_s = smem_u32(ring) + (uint32_t)tid * 16;
+    int pf_u = -1, pf_s0 = 0;
+    const uint8_t *pf_d = nullptr;
+    auto issue = [&](int q) {
+        if (q < Q) {
+            const int qu = q / nsb, sq = q - qu * nsb;
+            if (u0 + qu != pf_u) {
+                pf_u = u0 + qu;
+                unit_src(pf_u, pf_d, pf_s0);
+            }
+            const uint8_t *b = pf_d + (size_t)(pf_s0 + sq) * 16;
+            const uint32_t dst = ring_s + (uint32_t)(q % RAW_R) * RAW_STAGE;
+            cp_async16(dst, b);
+#pragma unroll
+            for (int c = 0; c < 4; c++)
+                cp_async16(dst + (uint32_t)(1 + c) * RAW_CHUNK, b + (size_t)(1 + 4 * h + c) * S * 16);
+        }
+        cp_async_commit();
+    };
+    for (int q = 0; q < RAW_D; q++) issue(q);
+    int cur_chunk = -1, mc = 0, q = 0;
+    uint32_t gstep = 0;  // steps issued by this CTA: buffer gstep & 1, its barrier phase (gstep >> 1) & 1
+    bool ok = true;
+    for (int u = u0; ok && u < u1; u++) {
+        const int ci = u / nrb, rb = u - ci * nrb;
+        if (ci != cur_chunk) {  // the chunk's Q8_K rows: B operand (zero rows past mc), scales, sums
+            cur_chunk = ci;
+            const int e = p.g_chunk_e[ci];
+            const int c0 = p.g_chunk_r0[ci], m = p.g_count[e], off = p.g_off[e];
+            mc = m - c0 < MMA_N ? m - c0 : MMA_N;
+            __syncthreads();  // the previous chunk's operands are no longer read
+            if (tid < mc) tk_s[tid] = p.g_list[off + c0 + tid];
+            __syncthreads();
+            const uint32_t sB_s = smem_u32(sB);
+            for (int i = tid; i < MMA_N * F / 16; i += 256) {  // 16-byte pieces of the B operand
+                const int t = i / (F / 16), k = (i - t * (F / 16)) * 16;
+                if (t < mc) cp_async16(sB_s + umma_off(t, k, MMA_N), p.q8_qs + (long long)tk_s[t] * F + k);
+                else *reinterpret_cast<uint4 *>(sB + umma_off(t, k, MMA_N)) = make_uint4(0, 0, 0, 0);
+            }
+            for (int i = tid; i < MMA_N * nsb * 2; i += 256) {  // 32-value sums, two 16-byte halves per block
+                const int t = i / (nsb * 2), j = i - t * nsb * 2;
+                if (t < mc) cp_async16(smem_u32(bsA + t * nsb * 8 + j * 4), p.q8_bs + (long long)tk_s[t] * nsb * 8 + j * 4);
+                else *reinterpret_cast<int4 *>(bsA + t * nsb * 8 + j * 4) = make_int4(0, 0, 0, 0);
+            }
+            for (int i = tid; i < MMA_N * nsb; i += 256) {
+                const int t = i / nsb, b = i - t * nsb;
+                dA[i] = t < mc ? p.q8_d[(long long)tk_s[t] * nsb + b] : 0.0f;
+            }
+            cp_async_commit();
+            cp_async_wait<0>();  // (the ring's copies in flight complete here too)
+            __syncthreads();
+        }
+        const int row = rb * 128 + r;
+        float acc[8];
+#pragma unroll
+        for (int t = 0; t < 8; t++) acc[t] = 0.0f;
+        uint4 raw[5];
+        int sc[8], mn[8];
+        float dw = 0.0f, dminw = 0.0f;
+        int psc[8], pmn[8];
+        float pdw = 0.0f, pdminw = 0.0f;
+        auto epilogue = [&](int sb, uint32_t gs) -> bool {  // the integer dots of superblock sb -> the row sums
+            if (!mbar_wait(&bars[gs & 1], (gs >> 1) & 1, p.err)) return false;
+            tc_fence_after();
+            int sumi[8];
+            tmem_sumi<8>(tmem + tlane + (gs & 1) * 128 + h * 8, 16, psc, sumi);
+#pragma unroll
+            for (int t = 0; t < 8; t++) {
+                const int tt = 8 * h + t;
+                const int4 b0 = *reinterpret_cast<const int4 *>(bsA + (tt * nsb + sb) * 8);
+                const int4 b1 = *reinterpret_cast<const int4 *>(bsA + (tt * nsb + sb) * 8 + 4);
+                const int summ = pmn[0] * b0.x + pmn[1] * b0.y + pmn[2] * b0.z + pmn[3] * b0.w + pmn[4] * b1.x +
+                                 pmn[5] * b1.y + pmn[6] * b1.z + pmn[7] * b1.w;
+                const float da = dA[tt * nsb + sb];
+                const float t1 = __fmul_rn(pdw, da);
+                const float t2 = __fmul_rn(__int2float_rn(sumi[t]), t1);
+                const float t3 = __fmul_rn(pdminw, da);
+                const float t4 = __fmul_rn(__int2float_rn(summ), t3);
+                acc[t] = __fadd_rn(acc[t], __fsub_rn(t2, t4));
+            }
+            return true;
+        };
+        for (int st = 0; st < nsb; st++, q++) {
+            const uint32_t gs = gstep++;
+            ring_take(ring_t, q, raw, issue);
+            q4k_header(raw[0], dw, dminw, sc, mn);
+            q4k_unpack_a(sA + (gs & 1) * MMA_A_BYTES, raw, r, h);
+            fence_proxy_async();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0) {
+#pragma unroll 1
+                for (int j = 0; j < 8; j++)
+                    umma_i8(tmem + (gs & 1) * 128 + j * 16,
+                            umma_desc(aBase + (gs & 1) * MMA_A_BYTES + j * 4096, 128, 256),
+                            umma_desc(bBase + (uint32_t)(st * 8 + j) * MMA_N * 32, 128, 256), idesc, false);
+                umma_commit(smem_u32(&bars[gs & 1]));
+            }
+            if (st > 0 && !__syncthreads_and(epilogue(st - 1, gs - 1))) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                psc[j] = sc[j];
+                pmn[j] = mn[j];
+            }
+            pdw = dw;
+            pdminw = dminw;
+            tc_fence_before();
+        }
+        if (!ok) break;
+        if (!__syncthreads_and(epilogue(nsb - 1, gstep - 1))) {
+            ok = false;
+            break;
+        }
+        tc_fence_before();
+        for (int t = 0; t < 8; t++)
+            if (8 * h + t < mc) p.dpart[(long long)tk_s[8 * h + t] * p.E + row] = acc[t];
+    }
+    cp_async_wait_all();  // no copy into this CTA's shared memory outlives it
+    if (!ok && tid == 0) {  // let this CTA's MMAs in flight finish (bounded) before the TMEM goes
+        for (uint32_t b = 0; b < 2; b++) {
+            const long long last = gstep == 0 ? -1 : ((long long)((gstep - 1) & 1) == b ? gstep - 1 : (long long)gstep - 2);
+            if (last >= 0) mbar_wait(&bars[b], (uint32_t)(last >> 1) & 1, nullptr);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, MMA_TMEM_COLS);
+}
+
+cudaError_t launch_down_mma(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl) {
+    if (a.F % 256 || a.d_rpt < 1 || a.d_rpt * (a.F / 256) > 32 || a.E % 128 || a.dtype != T_Q4_K || a.d_nsb != a.F / 256 ||
+        a.d_tile_bytes != 9 * 16 * a.d_rpt * (a.F / 256))
+        return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = down_mma_smem_bytes(a.F);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, down_mma_kernel, a);
+}
+
 // ====================================================================== Q8_K activation rows
 // One CTA per row: the row's RMSNorm factor (warp 0, C5/C6) when norm_w, then the 256-value
 // blocks quantised (C3) by the warps in turn, written as the tensor-core kernels read them: the
@@ -1009,7 +1216,8 @@ cudaError_t init_mma_attributes() {
     if ((e = cudaGetDevice(&dev))) return e;
     if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
     const void *kerns[] = {(const void *)gateup_mma_kernel, (const void *)kq_rows_mma_kernel<32>,
-                           (const void *)kq_rows_mma_kernel<16>, (const void *)kq6_rows_mma_kernel};
+                           (const void *)kq_rows_mma_kernel<16>, (const void *)kq6_rows_mma_kernel,
+                           (const void *)down_mma_kernel};
     for (const void *k : kerns) {
         cudaFuncAttributes fa;
         if ((e = cudaFuncGetAttributes(&fa, k))) return e;

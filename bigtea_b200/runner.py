@@ -246,6 +246,19 @@ def share_ep_unique_id(group=None) -> bytes:
     return obj[0]
 
 
+def pinned_empty(shape, dtype=np.float32) -> np.ndarray:
+    """An uninitialised array in page-locked host memory (bt_host_alloc), freed with the array:
+    bt_forward copies logits straight into such an output buffer."""
+    dt = np.dtype(dtype)
+    n = int(np.prod(shape)) * dt.itemsize
+    p = C.c_void_p()
+    check(lib.bt_host_alloc(max(n, 1), C.byref(p)))
+    buf = (C.c_uint8 * max(n, 1)).from_address(p.value)
+    arr = np.frombuffer(buf, dtype=dt, count=int(np.prod(shape))).reshape(shape)
+    weakref.finalize(buf, lib.bt_host_free, C.c_void_p(p.value))
+    return arr
+
+
 def _u32(a) -> np.ndarray:
     return np.ascontiguousarray(np.asarray(a, dtype=np.uint32))
 
@@ -256,17 +269,22 @@ class StreamingRunner:
     def __init__(self, engine: Engine):
         self.engine = engine
 
-    def forward_cached(self, cache: KvCache, tokens, pos_start: int, seq: int = 0) -> np.ndarray:
-        """One step of `tokens` at `pos_start` for sequence `seq`: logits of the last position."""
-        return self.forward_batch(cache, [seq], [list(tokens)], [pos_start])[0]
+    def forward_cached(self, cache: KvCache, tokens, pos_start: int, seq: int = 0, out=None) -> np.ndarray:
+        """One step of `tokens` at `pos_start` for sequence `seq`: logits of the last position
+        (into `out`, shape (1, n_vocab) float32, when given; page-locked from pinned_empty saves
+        a host copy)."""
+        return self.forward_batch(cache, [seq], [list(tokens)], [pos_start], out=out)[0]
 
-    def forward_batch(self, cache: KvCache, seqs, token_lists, pos_starts) -> np.ndarray:
+    def forward_batch(self, cache: KvCache, seqs, token_lists, pos_starts, out=None) -> np.ndarray:
         V = self.engine.cfg.n_vocab
         toks = _u32([t for tl in token_lists for t in tl])
         n = _u32([len(tl) for tl in token_lists])
         s = _u32(seqs)
         ps = _u32(pos_starts)
-        out = np.empty((len(seqs), V), np.float32)
+        if out is None:
+            out = np.empty((len(seqs), V), np.float32)
+        elif out.shape != (len(seqs), V) or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise ValueError(f"out must be a C-contiguous float32 array of shape {(len(seqs), V)}")
         check(lib.bt_forward(self.engine.h, cache.h, _lib.ptr(s, C.c_uint32), _lib.ptr(toks, C.c_uint32),
                              _lib.ptr(n, C.c_uint32), _lib.ptr(ps, C.c_uint32), len(seqs),
                              _lib.ptr(out, C.c_float)))

@@ -156,6 +156,11 @@ int bt_generate_greedy(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const u
 
 /* Device time (CUDA events on the engine stream) of the last bt_generate_greedy replay loop. */
 int bt_last_device_ms(const bt_engine *e, double *ms);
+/* Page-locked host memory (no counterpart in the reference). bt_forward copies logits straight
+ * into an output buffer from here, without the staging copy a pageable buffer takes; the
+ * latency-bound single-token loop is where that shows. bt_host_free releases a block. */
+int bt_host_alloc(uint64_t bytes, void **out);
+int bt_host_free(void *p);
 
 /* StreamStats-style per-kernel timing (stream.rs:134-194): runs n_steps greedy steps with
  * serialised launches, each bracketed by CUDA events; fills one entry per kernel kind. */

@@ -610,3 +610,28 @@ def test_isolated_expert_timing_reports_the_selected_bytes(tiny_cfg, tiny_weight
     cache.close()
     model.close()
     e.close()
+
+
+def test_forward_into_page_locked_logits(tiny_cfg, tiny_weights):
+    """bt_forward into a bt_host_alloc buffer (the logits copied straight into it) gives the bits a
+    pageable buffer gets, for single-token and batched calls, and a wrong-shaped buffer is refused."""
+    e = bt.Engine(tiny_cfg, tiny_weights)
+    try:
+        outs = []
+        for pinned in (False, True):
+            cache = bt.KvCache(e, max_positions=128, max_seqs=12)
+            runner = bt.StreamingRunner(e)
+            buf1 = bt.pinned_empty((1, tiny_cfg.n_vocab)) if pinned else None
+            bufb = bt.pinned_empty((12, tiny_cfg.n_vocab)) if pinned else None
+            a = runner.forward_cached(cache, [3, 1, 4, 1, 5], 0, out=buf1).copy()
+            b = runner.forward_cached(cache, [9], 5, out=buf1).copy()
+            c = runner.forward_batch(cache, list(range(1, 12)), [[t] for t in range(11)], [0] * 11,
+                                     out=None if bufb is None else bufb[:11]).copy()
+            outs.append((a, b, c))
+            cache.close()
+        for x, y in zip(outs[0], outs[1]):
+            assert np.array_equal(bits(x), bits(y))
+        with pytest.raises(ValueError):
+            bt.StreamingRunner(e).forward_cached(None, [1], 0, out=bt.pinned_empty((2, tiny_cfg.n_vocab)))
+    finally:
+        e.close()
