@@ -1666,13 +1666,18 @@ static bool use_gateup_mma(const bt_engine *e, const Layer &l, size_t rows) {
            gateup_mma_smem_bytes((int)e->d.n_embd) <= (size_t)max_dynamic_smem() && rows <= e->q8_rows;
 }
 
-// The tensor-core down of the grouped path: a Q4_K down, output rows in whole 128-row blocks, and
-// room in the Q8_K staging for `rows` SiLU-product rows.
+// The tensor-core down of the grouped path: a Q4_K or Q6_K down, output rows in whole 128-row
+// blocks, and room in the Q8_K staging for `rows` SiLU-product rows.
 static bool use_down_mma(const bt_engine *e, const Layer &l, size_t rows) {
     const int F = (int)e->d.n_ff_exp, nsb = F / 256;
-    return e->mma && l.down.type == T_Q4_K && F % 256 == 0 && nsb >= 1 && l.down.g.rpt * nsb <= 32 &&
-           e->d.n_embd % 128 == 0 && down_mma_smem_bytes(F) <= (size_t)max_dynamic_smem() &&
-           rows * (size_t)F <= e->q8_rows * e->q8_k;
+    const size_t smem = l.down.type == T_Q4_K ? down_mma_smem_bytes(F)
+                        : l.down.type == T_Q6_K ? down6_mma_smem_bytes(F) : (size_t)-1;
+    return e->mma && F % 256 == 0 && nsb >= 1 && l.down.g.rpt * nsb <= 32 && l.down.g.tile_bytes % 16 == 0 &&
+           e->d.n_embd % 128 == 0 && smem <= (size_t)max_dynamic_smem() && rows * (size_t)F <= e->q8_rows * e->q8_k;
+}
+
+static cudaError_t launch_down_tc(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl) {
+    return a.dtype == T_Q6_K ? launch_down6_mma(a, grid, st, pdl) : launch_down_mma(a, grid, st, pdl);
 }
 
 // The down input rows (a.act: `rows` (token, slot) rows of F SiLU products) as Q8_K rows.
@@ -1777,7 +1782,7 @@ static int launch_layer_experts(bt_engine *e, int il, int T, const int *sel_ids,
             timer_begin(e, "expert_down");
             if (use_down_mma(e, l, (size_t)T * K)) {
                 CK(stage_down_q8(e, a, T * K, st, pdl));
-                CK(launch_down_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, st, pdl));
+                CK(launch_down_tc(a, e->mma_grid ? e->mma_grid : e->n_sm, st, pdl));
             } else {
                 CK(launch_down_grouped(a, e->n_sm, st, pdl));
             }
@@ -2145,7 +2150,7 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             timer_begin(e, "expert_down");
             if (use_down_mma(e, l, (size_t)n * S)) {
                 CK(stage_down_q8(e, a, n * S, st, pdl));
-                CK(launch_down_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, st, pdl));
+                CK(launch_down_tc(a, e->mma_grid ? e->mma_grid : e->n_sm, st, pdl));
             } else {
                 CK(launch_down_grouped(a, e->n_sm, st, pdl));
             }

@@ -236,6 +236,9 @@ cudaError_t launch_gateup_mma(const ExpertArgs &a, int grid, cudaStream_t st, bo
 // is the SiLU products as Q8_K rows, one per (token, slot); one CTA per SM
 size_t down_mma_smem_bytes(int F);
 cudaError_t launch_down_mma(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
+// the same for a Q6_K down ((size_t)-1: F does not fit)
+size_t down6_mma_smem_bytes(int F);
+cudaError_t launch_down6_mma(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl);
 cudaError_t init_mma_attributes();
 // batched GEMV on tcgen05 (Q4_K segments of whole 128-row blocks, no argmax); one CTA per SM
 size_t gemv_mma_smem_bytes(int K);

@@ -1178,6 +1178,253 @@ __global__ void __launch_bounds__(256, 1) kq6_rows_mma_kernel(const __grid_const
     if (warp == 0) tmem_dealloc(tmem, Q6_TCOLS);
 }
 
+// Q6_K down of the grouped batched path: kq6_rows_mma_kernel's arithmetic (two MMAs per K step
+// against the halves of the activations, the Q6_K epilogue) over down_mma_kernel's units (chunk of
+// at most 16 (token, slot) rows of one expert, block of 128 output rows), K = F, the rows' sums to
+// dpart for the combine.
+size_t down6_mma_smem_bytes(int F) {
+    if (F <= 0 || F % 256) return (size_t)-1;
+    const size_t nsb = (size_t)F / 256;
+    const size_t b = 1024 + 2 * MMA_A_BYTES + (size_t)Q6_RAW_R * Q6_RAW_STAGE + (size_t)(F / 32) * Q6_B_STEP +
+                     (size_t)Q6_N * nsb * 4 + (size_t)Q6_N * (F / 16) * 4 + 2 * Q6_N * 4 + 256;
+    return b <= MMA_SMEM_LIMIT ? b : (size_t)-1;
+}
+
+__global__ void __launch_bounds__(256, 1) down6_mma_kernel(const __grid_constant__ ExpertArgs p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int F = p.F, nsb = F / 256, n16 = F / 16, rpt = p.d_rpt, S = rpt * nsb;
+    uint8_t *sA = smem;                                                       // [2][8 K steps][128 rows][32]
+    uint8_t *ring = sA + 2 * MMA_A_BYTES;                                     // [Q6_RAW_R][7][256 threads][16]
+    uint8_t *sB = ring + Q6_RAW_R * Q6_RAW_STAGE;                             // [F/32][3][16 rows][16]
+    float *dA = reinterpret_cast<float *>(sB + (size_t)(F / 32) * Q6_B_STEP);  // [16][nsb]
+    int *bs16 = reinterpret_cast<int *>(dA + Q6_N * nsb);                     // [16][F/16]
+    int *tk_s = bs16 + Q6_N * n16;                                            // [16]
+    uint64_t *bars = reinterpret_cast<uint64_t *>(tk_s + 2 * Q6_N);          // [2]
+    uint32_t *tslot = reinterpret_cast<uint32_t *>(bars + 2);
+    const int tid = threadIdx.x, warp = tid >> 5;
+    const int r = tid & 127, h = tid >> 7;
+    const uint32_t tlane = (uint32_t)((warp & 3) * 32) << 16;
+    if (tid == 0) {
+        mbar_init(&bars[0], 1);
+        mbar_init(&bars[1], 1);
+        fence_mbar_init();
+    }
+    if (warp == 0) tmem_alloc(smem_u32(tslot), Q6_TCOLS);
+    for (int i = tid; i < (F / 32) * Q6_N; i += 256)  // the zero blocks of B, once
+        *reinterpret_cast<uint4 *>(sB + (size_t)(i / Q6_N) * Q6_B_STEP + Q6_N * 16 + (i % Q6_N) * 16) =
+            make_uint4(0, 0, 0, 0);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = *tslot;
+    pdl_wait();  // the groups and the staged products come from the kernels before
+    const int nrb = p.E / 128;
+    const int total = *p.g_nchunks * nrb;
+    const int u0 = (int)((long long)blockIdx.x * total / gridDim.x);
+    const int u1 = (int)((long long)(blockIdx.x + 1) * total / gridDim.x);
+    pdl_trigger();
+    // this thread's row of unit u: its tile and first slot
+    auto unit_src = [&](int u, const uint8_t *&db, int &s0) {
+        const int ci = u / nrb, rb = u - ci * nrb;
+        const int row = rb * 128 + r;
+        db = expert_down(p, p.g_chunk_e[ci]) + (long long)(row / rpt) * p.d_tile_bytes;
+        s0 = (row % rpt) * nsb;
+    };
+    const int Q = u1 > u0 ? (u1 - u0) * nsb : 0;
+    const uint32_t ring_s = smem_u32(ring) + (uint32_t)tid * 16;
+    int pf_u = -1, pf_s0 = 0;
+    const uint8_t *pf_w = nullptr;
+    auto issue = [&](int q) {
+        if (q < Q) {
+            const int qu = q / nsb, sq = q - qu * nsb;
+            if (u0 + qu != pf_u) {
+                pf_u = u0 + qu;
+                unit_src(pf_u, pf_w, pf_s0);
+            }
+            const int s = pf_s0 + sq;
+            const size_t cs = (size_t)S * 16;
+            const uint8_t *b = pf_w + (size_t)s * 16;
+            const uint32_t dst = ring_s + (uint32_t)(q % Q6_RAW_R) * Q6_RAW_STAGE;
+#pragma unroll
+            for (int c = 0; c < 4; c++) cp_async16(dst + (uint32_t)c * RAW_CHUNK, b + (size_t)(4 * h + c) * cs);
+#pragma unroll
+            for (int c = 0; c < 2; c++) cp_async16(dst + (uint32_t)(4 + c) * RAW_CHUNK, b + (size_t)(8 + 2 * h + c) * cs);
+            if (h == 0) cp_async16(dst + 6u * RAW_CHUNK, b + 12 * cs);                          // the 16 scales
+            else cp_async16(dst + 6u * RAW_CHUNK, pf_w + 13 * cs + (size_t)((2 * s) & ~15));  // d's 16 bytes
+        }
+        cp_async_commit();
+    };
+    for (int q = 0; q < Q6_RAW_D; q++) issue(q);
+    const uint32_t idesc = umma_idesc_u8s8(128, Q6_N);
+    const uint32_t aBase = smem_u32(sA), bBase = smem_u32(sB);
+    int cur_chunk = -1, mc = 0, q = 0;
+    uint32_t gstep = 0;
+    bool ok = true;
+    for (int u = u0; ok && u < u1; u++) {
+        const int ci = u / nrb, rb = u - ci * nrb;
+        int s0;
+        {
+            const uint8_t *db_;
+            unit_src(u, db_, s0);
+        }
+        if (ci != cur_chunk) {  // the chunk's rows as Q8_K: B (zeros past mc), scales, 16-value sums
+            cur_chunk = ci;
+            const int e = p.g_chunk_e[ci];
+            const int c0 = p.g_chunk_r0[ci], m = p.g_count[e], off = p.g_off[e];
+            mc = m - c0 < Q6_N ? m - c0 : Q6_N;
+            __syncthreads();  // the previous chunk's operands are no longer read
+            if (tid < mc) tk_s[tid] = p.g_list[off + c0 + tid];
+            __syncthreads();
+            const uint32_t sB_s = smem_u32(sB);
+            for (int i = tid; i < Q6_N * n16; i += 256) {
+                const int t = i / n16, k16 = i - t * n16;
+                if (t < mc) cp_async16(sB_s + q6_b_off(t, k16), p.q8_qs + (long long)tk_s[t] * F + k16 * 16);
+                else *reinterpret_cast<uint4 *>(sB + q6_b_off(t, k16)) = make_uint4(0, 0, 0, 0);
+            }
+            for (int i = tid; i < Q6_N * nsb; i += 256) {
+                const int t = i / nsb, b = i - t * nsb;
+                dA[i] = t < mc ? p.q8_d[(long long)tk_s[t] * nsb + b] : 0.0f;
+            }
+            cp_async_commit();
+            cp_async_wait<0>();  // (the ring's copies in flight complete here too)
+            __syncthreads();
+            for (int i = tid; i < Q6_N * n16; i += 256) {  // bs16[t][k16]: the sum of those 16 values
+                const uint4 v = *reinterpret_cast<const uint4 *>(sB + q6_b_off(i / n16, i % n16));
+                int s = __dp4a((int)v.x, 0x01010101, 0);
+                s = __dp4a((int)v.y, 0x01010101, s);
+                s = __dp4a((int)v.z, 0x01010101, s);
+                bs16[i] = __dp4a((int)v.w, 0x01010101, s);
+            }
+            __syncthreads();
+        }
+        const int row = rb * 128 + r;
+        float acc[Q6_HT];
+#pragma unroll
+        for (int t = 0; t < Q6_HT; t++) acc[t] = 0.0f;
+        uint4 raw[6];
+        int sc[16], psc[16];
+        float dw = 0.0f, pdw = 0.0f;
+        auto epilogue = [&](int sb, uint32_t gs) -> bool {
+            if (!mbar_wait(&bars[gs & 1], (gs >> 1) & 1, p.err)) return false;
+            tc_fence_after();
+            int sumi[Q6_HT];
+#pragma unroll
+            for (int t = 0; t < Q6_HT; t++) sumi[t] = 0;
+            const uint32_t col0 = tmem + tlane + (gs & 1) * 16 * Q6_N + h * Q6_HT;
+#pragma unroll
+            for (int j0 = 0; j0 < 16; j0 += 4) {
+                uint32_t v[4][8];
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) tmem_ld8(col0 + (uint32_t)((j0 + jj) * Q6_N), v[jj]);
+                tmem_wait_ld();
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++) tmem_pin(v[jj]);
+#pragma unroll
+                for (int jj = 0; jj < 4; jj++)
+#pragma unroll
+                    for (int t = 0; t < Q6_HT; t++) sumi[t] += psc[j0 + jj] * (int)v[jj][t];
+            }
+#pragma unroll
+            for (int tt = 0; tt < Q6_HT; tt++) {
+                const int t = Q6_HT * h + tt;
+                const int4 *bq = reinterpret_cast<const int4 *>(bs16 + t * n16 + sb * 16);
+                int corr = 0;
+#pragma unroll
+                for (int c = 0; c < 4; c++) {
+                    const int4 b = bq[c];
+                    corr += psc[4 * c] * b.x + psc[4 * c + 1] * b.y + psc[4 * c + 2] * b.z + psc[4 * c + 3] * b.w;
+                }
+                const int si_ = sumi[tt] - 32 * corr;
+                acc[tt] = __fadd_rn(acc[tt], __fmul_rn(__int2float_rn(si_), __fmul_rn(pdw, dA[t * nsb + sb])));
+            }
+            return true;
+        };
+        for (int st = 0; st < nsb; st++, q++) {
+            const uint32_t gs = gstep++;
+            cp_async_wait<Q6_RAW_D - 1>();  // this thread's pieces of step q have landed
+            const uint8_t *stage = ring + (size_t)(q % Q6_RAW_R) * Q6_RAW_STAGE;
+#pragma unroll
+            for (int c = 0; c < 6; c++) raw[c] = *reinterpret_cast<const uint4 *>(stage + c * RAW_CHUNK + tid * 16);
+            q6k_unpack_a(sA + (gs & 1) * MMA_A_BYTES, raw, r, h);
+            fence_proxy_async();
+            tc_fence_before();
+            __syncthreads();
+            tc_fence_after();
+            if (tid == 0) {
+                const uint32_t a0 = aBase + (gs & 1) * MMA_A_BYTES;
+#pragma unroll 1
+                for (int j = 0; j < 8; j++) {
+                    const uint64_t ad = umma_desc(a0 + j * 4096, 128, 256);
+                    const uint32_t bj = bBase + (uint32_t)(st * 8 + j) * Q6_B_STEP;
+                    const uint32_t d0 = tmem + (gs & 1) * 16 * Q6_N + (uint32_t)(2 * j) * Q6_N;
+                    umma_i8(d0, ad, umma_desc(bj, 256, 128), idesc, false);
+                    umma_i8(d0 + Q6_N, ad, umma_desc(bj + 2 * 128, 256, 128), idesc, false);
+                }
+                umma_commit(smem_u32(&bars[gs & 1]));
+            }
+            {  // the step's scales and d from both halves' pieces (visible after the barrier)
+                const uint4 scv = *reinterpret_cast<const uint4 *>(stage + 6 * RAW_CHUNK + r * 16);
+                const uint4 dv = *reinterpret_cast<const uint4 *>(stage + 6 * RAW_CHUNK + (128 + r) * 16);
+                const uint32_t scw[4] = {scv.x, scv.y, scv.z, scv.w};
+#pragma unroll
+                for (int j = 0; j < 16; j++) sc[j] = byte_s(scw[j >> 2], j & 3);
+                const int o = (2 * (s0 + st)) & 15;  // d's byte offset in the piece (even)
+                const unsigned long long dword = o < 8 ? ((unsigned long long)dv.y << 32) | dv.x
+                                                       : ((unsigned long long)dv.w << 32) | dv.z;
+                dw = __half2float(__ushort_as_half((unsigned short)((dword >> (8 * (o & 7))) & 0xffffu)));
+            }
+            issue(q + Q6_RAW_D);  // into the stage of step q - 1, which every thread has finished reading
+            if (st > 0 && !__syncthreads_and(epilogue(st - 1, gs - 1))) {
+                ok = false;
+                break;
+            }
+#pragma unroll
+            for (int j = 0; j < 16; j++) psc[j] = sc[j];
+            pdw = dw;
+            tc_fence_before();
+        }
+        if (!ok) break;
+        if (!__syncthreads_and(epilogue(nsb - 1, gstep - 1))) {
+            ok = false;
+            break;
+        }
+        tc_fence_before();
+#pragma unroll
+        for (int tt = 0; tt < Q6_HT; tt++)
+            if (Q6_HT * h + tt < mc) p.dpart[(long long)tk_s[Q6_HT * h + tt] * p.E + row] = acc[tt];
+    }
+    cp_async_wait_all();  // no copy into this CTA's shared memory outlives it
+    if (!ok && tid == 0) {
+        for (uint32_t b = 0; b < 2; b++) {
+            const long long last = gstep == 0 ? -1 : ((long long)((gstep - 1) & 1) == b ? gstep - 1 : (long long)gstep - 2);
+            if (last >= 0) mbar_wait(&bars[b], (uint32_t)(last >> 1) & 1, nullptr);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tmem_dealloc(tmem, Q6_TCOLS);
+}
+
+cudaError_t launch_down6_mma(const ExpertArgs &a, int grid, cudaStream_t st, bool pdl) {
+    const size_t smem = down6_mma_smem_bytes(a.F);
+    if (smem == (size_t)-1 || a.d_rpt < 1 || a.d_rpt * (a.F / 256) > 32 || a.E % 128 || a.dtype != T_Q6_K ||
+        a.d_nsb != a.F / 256 || a.d_tile_bytes % 16 ||
+        a.d_tile_bytes != 13 * 16 * a.d_rpt * (a.F / 256) + (2 * a.d_rpt * (a.F / 256) + 15) / 16 * 16)
+        return cudaErrorInvalidValue;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(grid);
+    cfg.blockDim = dim3(256);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, down6_mma_kernel, a);
+}
+
 cudaError_t launch_gemv_mma6(const GemvArgs &a, int grid, cudaStream_t st, bool pdl) {
     const size_t smem = gemv_mma6_smem_bytes(a.K);
     if (smem == (size_t)-1) return cudaErrorInvalidValue;
@@ -1217,7 +1464,7 @@ cudaError_t init_mma_attributes() {
     if ((e = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev))) return e;
     const void *kerns[] = {(const void *)gateup_mma_kernel, (const void *)kq_rows_mma_kernel<32>,
                            (const void *)kq_rows_mma_kernel<16>, (const void *)kq6_rows_mma_kernel,
-                           (const void *)down_mma_kernel};
+                           (const void *)down_mma_kernel, (const void *)down6_mma_kernel};
     for (const void *k : kerns) {
         cudaFuncAttributes fa;
         if ((e = cudaFuncGetAttributes(&fa, k))) return e;

@@ -33,7 +33,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-@pytest.mark.parametrize("n", [2, 4])
+@pytest.mark.parametrize("n", [2, 4, 8])
 def test_expert_parallel_matches_single_gpu(tmp_path, n):
     if _gpus() < n:
         pytest.skip(f"needs {n} GPUs")
