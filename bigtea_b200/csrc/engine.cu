@@ -179,6 +179,7 @@ struct bt_engine {
     std::vector<const uint8_t *> x_host_dev;  // device addresses of x_host
     DevBuf x_host_devarr;                     // the same, in device memory
     DevBuf ep_send_meta, ep_send_rows, ep_recv_meta, ep_recv_rows, ep_act, ep_dpart, ep_ret;
+    DevBuf ep_send_qs, ep_send_d, ep_send_bs, ep_recv_qs, ep_recv_d, ep_recv_bs;  // Q8_K dispatch
     DevBuf dbg_ids, dbg_w;  // [n_layer][TB][K]
     DevBuf tokens, seq_of, local_idx, pos_of, single, x_rows;
     DevBuf st_seq, st_ntok, st_lrow, next_tok, gen_out, gen_count, logits, amax;
@@ -2064,17 +2065,42 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             pa.slots = S;
             pa.send_meta = e->ep_send_meta.as<int>();
             pa.send_rows = e->ep_send_rows.as<float>();
+            // the owners' gate/up reads Q8_K rows (tensor-core path): quantise the T token rows
+            // here and send those, a quarter of the f32 bytes; the owner would stage the same bits
+            const bool q8x = use_gateup_mma(e, l, (size_t)n * S) && (size_t)T <= e->q8_rows;
+            const int nsb = E / 256;
             timer_begin(e, "ep_pack");
+            if (q8x) {
+                CK(stage_q8(e, e->fn.as<float>(), E, nullptr, nullptr, E, T));
+                pa.q8_qs = e->q8_qs.as<int8_t>();
+                pa.q8_d = e->q8_d.as<float>();
+                pa.q8_bs = e->q8_bs.as<int>();
+                pa.send_qs = e->ep_send_qs.as<int8_t>();
+                pa.send_d = e->ep_send_d.as<float>();
+                pa.send_bs = e->ep_send_bs.as<int>();
+            }
             CK(launch_ep_pack(pa, st, pdl));
             timer_end(e);
             timer_begin(e, "ep_dispatch");
             NK(api->GroupStart());
             for (int r = 0; r < n; r++) {
                 NK(api->Send(pa.send_meta + (size_t)r * S, S, ncclInt32, r, e->ep_comm, st));
-                NK(api->Send(pa.send_rows + (size_t)r * S * E, (size_t)S * E, ncclFloat32, r, e->ep_comm, st));
                 NK(api->Recv(e->ep_recv_meta.as<int>() + (size_t)r * S, S, ncclInt32, r, e->ep_comm, st));
-                NK(api->Recv(e->ep_recv_rows.as<float>() + (size_t)r * S * E, (size_t)S * E, ncclFloat32, r,
-                             e->ep_comm, st));
+                if (q8x) {
+                    NK(api->Send(pa.send_qs + (size_t)r * S * E, (size_t)S * E, ncclInt8, r, e->ep_comm, st));
+                    NK(api->Send(pa.send_d + (size_t)r * S * nsb, (size_t)S * nsb, ncclFloat32, r, e->ep_comm, st));
+                    NK(api->Send(pa.send_bs + (size_t)r * S * nsb * 8, (size_t)S * nsb * 8, ncclInt32, r, e->ep_comm, st));
+                    NK(api->Recv(e->ep_recv_qs.as<int8_t>() + (size_t)r * S * E, (size_t)S * E, ncclInt8, r, e->ep_comm,
+                                 st));
+                    NK(api->Recv(e->ep_recv_d.as<float>() + (size_t)r * S * nsb, (size_t)S * nsb, ncclFloat32, r,
+                                 e->ep_comm, st));
+                    NK(api->Recv(e->ep_recv_bs.as<int>() + (size_t)r * S * nsb * 8, (size_t)S * nsb * 8, ncclInt32, r,
+                                 e->ep_comm, st));
+                } else {
+                    NK(api->Send(pa.send_rows + (size_t)r * S * E, (size_t)S * E, ncclFloat32, r, e->ep_comm, st));
+                    NK(api->Recv(e->ep_recv_rows.as<float>() + (size_t)r * S * E, (size_t)S * E, ncclFloat32, r,
+                                 e->ep_comm, st));
+                }
             }
             NK(api->GroupEnd());
             timer_end(e);
@@ -2137,7 +2163,12 @@ static int launch_step(bt_engine *e, bt_kv *kv, const StepPlan &p, bool greedy) 
             a.nst = 1;
             a.nst = pick_nst_cap(a.slot_bytes, gateup_grouped_smem_bytes(a) - (size_t)GEMV_WARPS * a.slot_bytes, cap);
             timer_begin(e, "expert_gateup");
-            if (use_gateup_mma(e, l, (size_t)n * S)) {
+            if (q8x) {  // the received Q8_K rows are the B operand as they are
+                a.q8_qs = e->ep_recv_qs.as<int8_t>();
+                a.q8_d = e->ep_recv_d.as<float>();
+                a.q8_bs = e->ep_recv_bs.as<int>();
+                CK(launch_gateup_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, st, pdl));
+            } else if (use_gateup_mma(e, l, (size_t)n * S)) {
                 CK(stage_gateup_q8(e, a, n * S, st, pdl));
                 CK(launch_gateup_mma(a, e->mma_grid ? e->mma_grid : e->n_sm, st, pdl));
             }
@@ -3048,6 +3079,12 @@ extern "C" int bt_engine_enable_ep(bt_engine *e, const void *unique_id, size_t n
     CK(e->ep_recv_meta.alloc(n * S * 4));
     CK(e->ep_send_rows.alloc(n * S * E * 4));
     CK(e->ep_recv_rows.alloc(n * S * E * 4));
+    CK(e->ep_send_qs.alloc(n * S * E));
+    CK(e->ep_recv_qs.alloc(n * S * E));
+    CK(e->ep_send_d.alloc(n * S * (E / 256) * 4));
+    CK(e->ep_recv_d.alloc(n * S * (E / 256) * 4));
+    CK(e->ep_send_bs.alloc(n * S * (E / 256) * 8 * 4));
+    CK(e->ep_recv_bs.alloc(n * S * (E / 256) * 8 * 4));
     CK(alloc_q8(e, (size_t)n * S));
     CK(e->ep_act.alloc(n * S * F * 4));
     CK(e->ep_dpart.alloc(n * S * E * 4));

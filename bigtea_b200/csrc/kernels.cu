@@ -947,7 +947,15 @@ __global__ void __launch_bounds__(256) ep_pack_kernel(const __grid_constant__ Ep
     const int e = tk < p.T * p.K ? p.sel_ids[tk] : -1;
     const int owner = e >= 0 ? e / p.per : -1;
     for (int r = threadIdx.x; r < p.ranks; r += blockDim.x) p.send_meta[r * p.slots + tk] = r == owner ? e : -1;
-    if (owner >= 0) {
+    if (owner >= 0 && p.send_qs) {  // the token's Q8_K row: values, block scales, 32-value sums
+        const long long t = tk / p.K, slot = (long long)owner * p.slots + tk;
+        const int nsb = p.E / 256;
+        const uint4 *qs = reinterpret_cast<const uint4 *>(p.q8_qs + t * p.E);
+        uint4 *dq = reinterpret_cast<uint4 *>(p.send_qs + slot * p.E);
+        for (int i = threadIdx.x; i < p.E / 16; i += blockDim.x) dq[i] = qs[i];
+        for (int i = threadIdx.x; i < nsb; i += blockDim.x) p.send_d[slot * nsb + i] = p.q8_d[t * nsb + i];
+        for (int i = threadIdx.x; i < nsb * 8; i += blockDim.x) p.send_bs[slot * nsb * 8 + i] = p.q8_bs[t * nsb * 8 + i];
+    } else if (owner >= 0) {
         const float *src = p.fn + (long long)(tk / p.K) * p.E;
         float *dst = p.send_rows + ((long long)owner * p.slots + tk) * p.E;
         for (int i = threadIdx.x; i < p.E; i += blockDim.x) dst[i] = src[i];

@@ -127,6 +127,14 @@ struct EpPackArgs {
     int T, K, E, ranks, per, slots;
     int *send_meta;      // [ranks][slots] expert id, or -1 where the slot is not for that rank
     float *send_rows;    // [ranks][slots][E]
+    // Q8_K dispatch (when send_qs is set): the T token rows already quantised by q8_stage_kernel
+    // go to the owner's slot in place of the f32 rows, a quarter of the bytes
+    const int8_t *q8_qs;
+    const float *q8_d;
+    const int *q8_bs;
+    int8_t *send_qs;     // [ranks][slots][E]
+    float *send_d;       // [ranks][slots][E/256]
+    int *send_bs;        // [ranks][slots][E/256][8]
 };
 
 // Tokens grouped by expert for the batched expert kernels: for every expert e, the (token,
