@@ -88,7 +88,9 @@ SIGNATURES = {
     "bt_kv_is_consistent": (C.c_int, [_P, C.c_uint32, C.POINTER(C.c_int)]),
     "bt_kv_export_layer": (C.c_int, [_P, C.c_uint32, C.c_uint32, _P, _P, C.c_uint64]),
     "bt_kv_import_layer": (C.c_int, [_P, C.c_uint32, C.c_uint32, _P, _P, C.c_uint64]),
-    "bt_forward": (C.c_int, [_P, _P, _U32P, _U32P, _U32P, _U32P, C.c_uint32, _F32P]),
+    # (array arguments as plain addresses: the per-token call is latency-bound, and building
+    # typed ctypes pointers costs more host time than the rest of the wrapper)
+    "bt_forward": (C.c_int, [_P, _P, _P, _P, _P, _P, C.c_uint32, _P]),
     "bt_generate_greedy": (C.c_int, [_P, _P, _U32P, _U32P, C.c_uint32, C.c_uint32, _U32P, _F32P]),
     "bt_last_device_ms": (C.c_int, [_P, C.POINTER(C.c_double)]),
     "bt_host_alloc": (C.c_int, [C.c_uint64, C.POINTER(C.c_void_p)]),

@@ -277,17 +277,21 @@ class StreamingRunner:
 
     def forward_batch(self, cache: KvCache, seqs, token_lists, pos_starts, out=None) -> np.ndarray:
         V = self.engine.cfg.n_vocab
-        toks = _u32([t for tl in token_lists for t in tl])
-        n = _u32([len(tl) for tl in token_lists])
-        s = _u32(seqs)
-        ps = _u32(pos_starts)
+        ns = len(seqs)
+        if ns == 1:  # the per-token decode loop: one sequence, no list flattening
+            toks = np.array(token_lists[0], dtype=np.uint32).reshape(-1)
+            n = np.array([toks.size], np.uint32)
+        else:
+            toks = _u32([t for tl in token_lists for t in tl])
+            n = _u32([len(tl) for tl in token_lists])
+        s = np.array(seqs, dtype=np.uint32)
+        ps = np.array(pos_starts, dtype=np.uint32)
         if out is None:
-            out = np.empty((len(seqs), V), np.float32)
-        elif out.shape != (len(seqs), V) or out.dtype != np.float32 or not out.flags.c_contiguous:
-            raise ValueError(f"out must be a C-contiguous float32 array of shape {(len(seqs), V)}")
-        check(lib.bt_forward(self.engine.h, cache.h, _lib.ptr(s, C.c_uint32), _lib.ptr(toks, C.c_uint32),
-                             _lib.ptr(n, C.c_uint32), _lib.ptr(ps, C.c_uint32), len(seqs),
-                             _lib.ptr(out, C.c_float)))
+            out = np.empty((ns, V), np.float32)
+        elif out.shape != (ns, V) or out.dtype != np.float32 or not out.flags.c_contiguous:
+            raise ValueError(f"out must be a C-contiguous float32 array of shape {(ns, V)}")
+        check(lib.bt_forward(self.engine.h, cache.h, s.ctypes.data, toks.ctypes.data, n.ctypes.data, ps.ctypes.data,
+                             ns, out.ctypes.data))
         return out
 
     def generate_greedy(self, cache: KvCache, first_tokens, n_steps: int, seqs=None, want_logits: bool = False):
