@@ -612,6 +612,36 @@ def test_isolated_expert_timing_reports_the_selected_bytes(tiny_cfg, tiny_weight
     e.close()
 
 
+@pytest.mark.parametrize("down_type", ["q4", "q6"])
+def test_tensor_core_down_at_wide_experts(down_type):
+    """The grouped down on tcgen05 at an expert width of 2048 (8 superblocks per row, as the
+    DeepSeek-style shape has) gives the dp4a kernel's bits and the oracle's: a 40-token prefill
+    step and a 20-sequence step, with Q4_K or Q6_K down matrices."""
+    dt = bt._lib.TYPE_Q4_K if down_type == "q4" else bt._lib.TYPE_Q6_K
+    types = [[bt._lib.TYPE_Q4_K] * 6 + [dt]] * 2
+    cfg = bt.config("tiny", n_ff_exp=2048, layer_types=types)
+    W = bt.synth_model(cfg, seed=13)
+    prompt = np.random.default_rng(58).integers(0, cfg.n_vocab, 40)
+    outs = {}
+    for mma in (1, 0):
+        e = bt.Engine(cfg, W)
+        e.set_option("mma", mma)
+        cache = bt.KvCache(e, max_positions=128, max_seqs=21)
+        runner = bt.StreamingRunner(e)
+        lg = runner.forward_batch(cache, [0], [prompt], [0])
+        steps = runner.forward_batch(cache, list(range(1, 21)), [[int(t)] for t in prompt[:20]], [0] * 20)
+        outs[mma] = (lg, steps)
+        cache.close()
+        e.close()
+    assert np.array_equal(bits(outs[1][0]), bits(outs[0][0]))
+    assert np.array_equal(bits(outs[1][1]), bits(outs[0][1]))
+    model = orc.Model(cfg, W)
+    try:
+        assert_logits(outs[1][0][0], model.forward(list(prompt), 0))
+    finally:
+        model.close()
+
+
 def test_forward_into_page_locked_logits(tiny_cfg, tiny_weights):
     """bt_forward into a bt_host_alloc buffer (the logits copied straight into it) gives the bits a
     pageable buffer gets, for single-token and batched calls, and a wrong-shaped buffer is refused."""
