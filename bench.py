@@ -399,7 +399,8 @@ def run_ours(args, rank, world, local_rank):
                    "path": "per-phase kernels (single-token steps of more than 4 sequences)",
                    "parallelism": (f"expert parallel over {world} GPUs: {B} sequences per rank, experts split "
                                    f"{cfg.n_expert // world} per rank (only those resident in each GPU's HBM), "
-                                   f"rows exchanged by NCCL send/recv" if world > 1 else "single GPU"),
+                                   f"rows exchanged by NCCL send/recv (Q8_K rows to the owners, f32 rows back)" if world > 1
+                                   else "single GPU"),
                    "comm_nranks": world, "ep_parity": ep_parity}
         cache2.close()
 
