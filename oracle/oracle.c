@@ -248,8 +248,9 @@ void or_quantize_q8k(const float *x, int64_t n, or_block_q8k *y) {
 
 /* ------------------------------------------------------------------ C4 dots */
 /* The integer part of a K-quant dot is exact, so the blocks are first unpacked to signed bytes
- * (as ggml's generic dot does into aux8) and the integer sums run over plain arrays, which the
- * compiler vectorises; the float combination keeps the contract's order. */
+ * (as ggml's generic dot does into aux8) and the integer sums run over plain arrays; the float
+ * combination keeps the contract's order. or_gemv runs the AVX2 form below (the same integers);
+ * these plain dots are its check (or_gemv_scalar_dots). */
 static void unpack_q4k(const uint8_t *blk, int8_t q[256], int sc[8], int mn[8]) {
     const uint8_t *qs = blk + 16;
     for (int g = 0; g < 4; g++) {
@@ -351,6 +352,9 @@ static float sum_p2(const float *x, int n) {
     return lane[0];
 }
 
+static float dot_q4k_row_avx2(const uint8_t *row, const or_block_q8k *a, int nsb);
+static float dot_q6k_row_avx2(const uint8_t *row, const or_block_q8k *a, int nsb);
+
 int or_gemv(int type, const void *W, int64_t rows, int64_t cols, const float *x, float *y) {
     const uint8_t *w = (const uint8_t *)W;
     if (type == OR_F32) {
@@ -365,7 +369,7 @@ int or_gemv(int type, const void *W, int64_t rows, int64_t cols, const float *x,
     int64_t rb = or_row_bytes(type, cols);
 #pragma omp parallel for schedule(static)
     for (int64_t r = 0; r < rows; r++)
-        y[r] = (type == OR_Q4_K) ? dot_q4k_row(w + r * rb, a, nsb) : dot_q6k_row(w + r * rb, a, nsb);
+        y[r] = (type == OR_Q4_K) ? dot_q4k_row_avx2(w + r * rb, a, nsb) : dot_q6k_row_avx2(w + r * rb, a, nsb);
     free(a);
     return 0;
 }
@@ -483,6 +487,102 @@ static inline void transpose8(__m256 r[8]) {
     r[5] = _mm256_permute2f128_ps(u1, u5, 0x31);
     r[6] = _mm256_permute2f128_ps(u2, u6, 0x31);
     r[7] = _mm256_permute2f128_ps(u3, u7, 0x31);
+}
+
+/* The K-quant row dots with AVX2 integer arithmetic, as ggml's x86 path computes them: the
+ * unsigned weight values times the signed Q8_K values by _mm256_maddubs_epi16 (no pair sum
+ * saturates: |15·128·2| and |63·128·2| are below 2^15), widened by _mm256_madd_epi16 and scaled
+ * per sub-block in int32. The integer sums are exact, so they equal dot_q4k_row's and
+ * dot_q6k_row's; the float combination is the same code in the same order. */
+static inline int32_t hsum_epi32(__m256i v) {
+    __m128i s = _mm_add_epi32(_mm256_castsi256_si128(v), _mm256_extracti128_si256(v, 1));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0x4E));
+    s = _mm_add_epi32(s, _mm_shuffle_epi32(s, 0xB1));
+    return _mm_cvtsi128_si32(s);
+}
+
+static float dot_q4k_row_avx2(const uint8_t *row, const or_block_q8k *a, int nsb) {
+    const __m256i m4 = _mm256_set1_epi8(0x0F), ones = _mm256_set1_epi16(1);
+    float acc = 0.0f;
+    for (int b = 0; b < nsb; b++) {
+        const uint8_t *blk = row + 144 * b;
+        const or_block_q8k *ab = a + b;
+        int sc[8], mn[8];
+        for (int j = 0; j < 8; j++) q4k_scale_min(blk + 4, j, &sc[j], &mn[j]);
+        __m256i vs = _mm256_setzero_si256();
+        for (int g = 0; g < 4; g++) {
+            const __m256i w = _mm256_loadu_si256((const __m256i *)(blk + 16 + 32 * g));
+            const __m256i lo = _mm256_and_si256(w, m4), hi = _mm256_and_si256(_mm256_srli_epi16(w, 4), m4);
+            const __m256i a0 = _mm256_loadu_si256((const __m256i *)(ab->qs + 64 * g));
+            const __m256i a1 = _mm256_loadu_si256((const __m256i *)(ab->qs + 64 * g + 32));
+            const __m256i d0 = _mm256_madd_epi16(_mm256_maddubs_epi16(lo, a0), ones);
+            const __m256i d1 = _mm256_madd_epi16(_mm256_maddubs_epi16(hi, a1), ones);
+            vs = _mm256_add_epi32(vs, _mm256_mullo_epi32(d0, _mm256_set1_epi32(sc[2 * g])));
+            vs = _mm256_add_epi32(vs, _mm256_mullo_epi32(d1, _mm256_set1_epi32(sc[2 * g + 1])));
+        }
+        const int32_t sumi = hsum_epi32(vs);
+        int32_t summ = 0;
+        for (int j = 0; j < 8; j++) summ += mn[j] * (ab->bsums[2 * j] + ab->bsums[2 * j + 1]);
+        float dw = or_f16_to_f32(rd16(blk)), dminw = or_f16_to_f32(rd16(blk + 2));
+        float t1 = dw * ab->d;
+        float t2 = (float)sumi * t1;
+        float t3 = dminw * ab->d;
+        float t4 = (float)summ * t3;
+        acc = acc + (t2 - t4);
+    }
+    return acc;
+}
+
+static float dot_q6k_row_avx2(const uint8_t *row, const or_block_q8k *a, int nsb) {
+    const __m256i m4 = _mm256_set1_epi8(0x0F), m3 = _mm256_set1_epi8(0x03), ones = _mm256_set1_epi16(1);
+    float acc = 0.0f;
+    for (int b = 0; b < nsb; b++) {
+        const uint8_t *blk = row + 210 * b;
+        const or_block_q8k *ab = a + b;
+        const int8_t *sc = (const int8_t *)(blk + 192);
+        __m256i vs = _mm256_setzero_si256();
+        for (int n = 0; n < 2; n++) {
+            const __m256i la = _mm256_loadu_si256((const __m256i *)(blk + 64 * n));
+            const __m256i lb = _mm256_loadu_si256((const __m256i *)(blk + 64 * n + 32));
+            const __m256i h = _mm256_loadu_si256((const __m256i *)(blk + 128 + 32 * n));
+            /* the unsigned 6-bit values q + 32 of values 128n + 32k + l, l = 0..31 */
+            __m256i u[4];
+            u[0] = _mm256_or_si256(_mm256_and_si256(la, m4), _mm256_slli_epi16(_mm256_and_si256(h, m3), 4));
+            u[1] = _mm256_or_si256(_mm256_and_si256(lb, m4),
+                                   _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(h, 2), m3), 4));
+            u[2] = _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(la, 4), m4),
+                                   _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(h, 4), m3), 4));
+            u[3] = _mm256_or_si256(_mm256_and_si256(_mm256_srli_epi16(lb, 4), m4),
+                                   _mm256_slli_epi16(_mm256_and_si256(_mm256_srli_epi16(h, 6), m3), 4));
+            for (int k = 0; k < 4; k++) {
+                const __m256i av = _mm256_loadu_si256((const __m256i *)(ab->qs + 128 * n + 32 * k));
+                const __m256i d = _mm256_madd_epi16(_mm256_maddubs_epi16(u[k], av), ones);
+                /* lanes 0-3: sub-block 8n + 2k (values l < 16), lanes 4-7: sub-block 8n + 2k + 1 */
+                const int s0 = sc[8 * n + 2 * k], s1 = sc[8 * n + 2 * k + 1];
+                vs = _mm256_add_epi32(vs, _mm256_mullo_epi32(d, _mm256_setr_epi32(s0, s0, s0, s0, s1, s1, s1, s1)));
+            }
+        }
+        int32_t corr = 0;  /* the -32 offset: 32 * sum_s sc_s * (sum of the sub-block's 16 activations) */
+        for (int s2 = 0; s2 < 16; s2++) corr += sc[s2] * ab->bsums[s2];
+        const int32_t sumi = hsum_epi32(vs) - 32 * corr;
+        float dw = or_f16_to_f32(rd16(blk + 208));
+        acc = acc + (float)sumi * (dw * ab->d);
+    }
+    return acc;
+}
+
+int or_gemv_scalar_dots(int type, const void *W, int64_t rows, int64_t cols, const float *x, float *y) {
+    /* or_gemv with the plain C dots: the check that the AVX2 dots give the same bits */
+    if ((type != OR_Q4_K && type != OR_Q6_K) || cols % 256) return -1;
+    const int nsb = (int)(cols / 256);
+    or_block_q8k *a = (or_block_q8k *)malloc(sizeof(or_block_q8k) * (size_t)nsb);
+    or_quantize_q8k(x, cols, a);
+    const int64_t rb = or_row_bytes(type, cols);
+    for (int64_t r = 0; r < rows; r++)
+        y[r] = (type == OR_Q4_K) ? dot_q4k_row((const uint8_t *)W + r * rb, a, nsb)
+                                 : dot_q6k_row((const uint8_t *)W + r * rb, a, nsb);
+    free(a);
+    return 0;
 }
 
 void or_attn_head(const float *q, const uint16_t *k, const uint16_t *v, int64_t ld, int nk,

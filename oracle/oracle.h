@@ -59,6 +59,8 @@ void or_quantize_q8k(const float *x, int64_t n, or_block_q8k *y);
 /* ---- ops (each restates one ggml call site of the reference) ---- */
 /* y[r] = W[r,:] . x for rows [0, rows); W in GGUF row-major bytes of `type`. */
 int or_gemv(int type, const void *W, int64_t rows, int64_t cols, const float *x, float *y);
+/* the same with the plain C dots, single-threaded (the check of the AVX2 dots) */
+int or_gemv_scalar_dots(int type, const void *W, int64_t rows, int64_t cols, const float *x, float *y);
 void or_rmsnorm(const float *x, const float *w, int n, float eps, float *y);
 float or_sumsq_p2(const float *x, int n);
 float or_dot_p2(const float *a, const float *b, int n);

@@ -168,6 +168,30 @@ def test_gemv_tracks_float64_dot(ty):
 
 
 # ------------------------------------------------------------------ scalar contract pieces
+@pytest.mark.parametrize("ty", [12, 14])
+def test_simd_kquant_dots_equal_the_plain_dots(ty):
+    """or_gemv's AVX2 integer dots (unsigned weights times signed Q8_K values, widened and
+    scaled in int32) give the plain C dots' bits: the integer sums are exact and the float
+    combination is the same code. Wide value ranges, several shapes, a zero activation block."""
+    import ctypes as C
+    L = orc.lib()
+    L.or_gemv_scalar_dots.restype = C.c_int
+    L.or_gemv_scalar_dots.argtypes = [C.c_int, C.c_void_p, C.c_int64, C.c_int64, C.POINTER(C.c_float),
+                                      C.POINTER(C.c_float)]
+    rng = np.random.default_rng(90 + ty)
+    for rows, cols, seed in ((768, 2048, 1), (2048, 768, 2), (37, 4096, 3), (5, 256, 4)):
+        w = orc.synth_tensor("x", ty, (cols, rows), 0.0, seed, sigma=0.3)
+        for trial in range(3):
+            x = (rng.standard_normal(cols) * (10 ** rng.uniform(-3, 3))).astype(np.float32)
+            if trial == 2:
+                x[:256] = 0.0
+            y1 = orc.gemv(ty, w, rows, cols, x).reshape(-1)
+            y2 = np.empty(rows, np.float32)
+            assert L.or_gemv_scalar_dots(ty, w.ctypes.data, rows, cols, x.ctypes.data_as(C.POINTER(C.c_float)),
+                                         y2.ctypes.data_as(C.POINTER(C.c_float))) == 0
+            assert np.array_equal(bits(y1), bits(y2)), (rows, cols, trial)
+
+
 def test_exp_error_bound():
     rng = np.random.default_rng(0)
     xs = np.concatenate([rng.uniform(-87, 88.7, 20000), rng.uniform(-2, 2, 20000), [0.0, -1e-30, 1e-30]])
