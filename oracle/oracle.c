@@ -628,12 +628,24 @@ void or_attn_head(const float *q, const uint16_t *k, const uint16_t *v, int64_t 
             l = l + lane[0];
         }
         float *a = ac + (size_t)c * head_dim;
-        for (int j = 0; j < cnt; j++) { /* a[d] = fmaf(p_j, v_jd, a[d]) in key order */
-            const uint16_t *vr = v + (int64_t)(base + j) * ld;
-            const __m256 pj = _mm256_set1_ps(p[j]);
-            for (int d0 = 0; d0 < head_dim; d0 += 8) {
-                const __m256 vv = _mm256_cvtph_ps(_mm_loadu_si128((const __m128i *)(vr + d0)));
-                _mm256_storeu_ps(a + d0, _mm256_fmadd_ps(pj, vv, _mm256_loadu_ps(a + d0)));
+        if (head_dim == 128) { /* the 128 sums in 16 registers across the keys: the same chains */
+            __m256 acc8[16];
+            for (int i = 0; i < 16; i++) acc8[i] = _mm256_setzero_ps();
+            for (int j = 0; j < cnt; j++) { /* a[d] = fmaf(p_j, v_jd, a[d]) in key order */
+                const uint16_t *vr = v + (int64_t)(base + j) * ld;
+                const __m256 pj = _mm256_set1_ps(p[j]);
+                for (int i = 0; i < 16; i++)
+                    acc8[i] = _mm256_fmadd_ps(pj, _mm256_cvtph_ps(_mm_loadu_si128((const __m128i *)(vr + 8 * i))), acc8[i]);
+            }
+            for (int i = 0; i < 16; i++) _mm256_storeu_ps(a + 8 * i, acc8[i]);
+        } else {
+            for (int j = 0; j < cnt; j++) { /* a[d] = fmaf(p_j, v_jd, a[d]) in key order */
+                const uint16_t *vr = v + (int64_t)(base + j) * ld;
+                const __m256 pj = _mm256_set1_ps(p[j]);
+                for (int d0 = 0; d0 < head_dim; d0 += 8) {
+                    const __m256 vv = _mm256_cvtph_ps(_mm_loadu_si128((const __m128i *)(vr + d0)));
+                    _mm256_storeu_ps(a + d0, _mm256_fmadd_ps(pj, vv, _mm256_loadu_ps(a + d0)));
+                }
             }
         }
         mc[c] = m;
