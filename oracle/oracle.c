@@ -39,6 +39,7 @@
 static __thread char g_err[512];
 static void set_err(const char *msg) { snprintf(g_err, sizeof g_err, "%s", msg); }
 const char *or_last_error(void) { return g_err; }
+void or_set_error_text(const char *msg) { set_err(msg); }
 
 int or_set_threads(int n) {
 #ifdef _OPENMP

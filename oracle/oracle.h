@@ -153,6 +153,70 @@ int or_synth_tensor(int type, int64_t rows, int64_t cols, uint64_t seed, uint64_
 /* STREAM-style host copy bandwidth (read + write bytes), best of reps, GB/s */
 double or_copy_gbs(int64_t bytes, int threads, int reps);
 
+/* ---- the token sampler (core/arch/src/sample.rs), restated in sample.c ---- */
+/* C10 ln and C11 pow: this library's own functions (sample.c), used by the sampler */
+float or_ln(float x);
+float or_pow(float x, float y);
+
+/* SamplerStage (sample.rs:43-50), in the enum's order */
+enum { OR_STAGE_TOP_K = 0, OR_STAGE_TYPICAL_P, OR_STAGE_TOP_P, OR_STAGE_MIN_P, OR_STAGE_XTC,
+       OR_STAGE_TEMPERATURE };
+
+/* SamplerConfig (sample.rs:84-180); the same layout as bt_sampler_config */
+typedef struct {
+    float temperature;
+    uint32_t top_k;
+    float top_p, min_p, typical_p, top_n_sigma;
+    float xtc_probability, xtc_threshold;
+    float dynatemp_range, dynatemp_exponent;
+    float repeat_penalty, frequency_penalty, presence_penalty;
+    uint32_t repeat_last_n;
+    float dry_multiplier, dry_base;
+    uint32_t dry_allowed_length, dry_penalty_last_n;
+    uint32_t mirostat;
+    float mirostat_tau, mirostat_eta;
+    float adaptive_p, adaptive_decay;
+    int32_t ignore_eos, eos;
+    const int32_t *chain; /* NULL: the default chain */
+    uint32_t n_chain;
+    const uint32_t *bias_ids;
+    const float *bias_values;
+    uint32_t n_bias;
+    const uint32_t *suppress_ids;
+    uint32_t n_suppress;
+    const uint32_t *dry_breakers;
+    uint32_t n_dry_breakers;
+    uint64_t seed;
+} or_sampler_config;
+
+/* the state a Sampler keeps between tokens (sample.rs:306-321) */
+typedef struct {
+    uint64_t rng;
+    float mu, ap_weighted, ap_total;
+} or_sampler_state;
+
+void or_sampler_config_default(or_sampler_config *c);  /* SamplerConfig::default, sample.rs:183-222 */
+void or_sampler_config_llamacpp(or_sampler_config *c); /* llamacpp_defaults, sample.rs:228-268 */
+void or_sampler_init(const or_sampler_config *c, or_sampler_state *st); /* Sampler::new, sample.rs:324-344 */
+float or_sampler_next_f32(or_sampler_state *st);                         /* sample.rs:462-472 */
+/* Sampler::sample (sample.rs:474-680); -1 with or_last_error() on a bad config */
+int64_t or_sample(const or_sampler_config *c, or_sampler_state *st, const float *logits, int64_t n_vocab,
+                  const uint32_t *history, int64_t n_history);
+/* the stage functions on a candidate list (ids, vals; n entries), for the reference's unit tests;
+ * each returns the new length */
+int64_t or_stage_top_p(uint32_t *ids, float *vals, int64_t n, float top_p);
+int64_t or_stage_min_p(uint32_t *ids, float *vals, int64_t n, float min_p);
+int64_t or_stage_typical_p(uint32_t *ids, float *vals, int64_t n, float typical_p);
+int64_t or_stage_top_n_sigma(uint32_t *ids, float *vals, int64_t n, float n_sigma);
+int64_t or_stage_xtc(uint32_t *ids, float *vals, int64_t n, float probability, float threshold, float roll);
+void or_stage_temperature(float *vals, int64_t n, float temperature);
+float or_dynamic_temperature(const float *vals, int64_t n, float temperature, float range, float exponent);
+void or_stage_penalties(const uint32_t *ids, float *vals, int64_t n, const uint32_t *history, int64_t n_history,
+                        float repeat, float frequency, float presence, uint32_t last_n);
+void or_stage_dry(const uint32_t *ids, float *vals, int64_t n, const uint32_t *history, int64_t n_history,
+                  float multiplier, float base, uint32_t allowed_length, uint32_t penalty_last_n,
+                  const uint32_t *breakers, uint32_t n_breakers);
+
 #ifdef __cplusplus
 }
 #endif

@@ -41,8 +41,31 @@ class Tensor(C.Structure):
     _fields_ = [("name", C.c_char_p), ("type", C.c_int), ("ne", C.c_int64 * 4), ("data", C.c_void_p)]
 
 
+class SamplerConfig(C.Structure):
+    """SamplerConfig (core/arch/src/sample.rs:84-180); the layout of bt_sampler_config"""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_uint32), ("top_p", C.c_float), ("min_p", C.c_float),
+                ("typical_p", C.c_float), ("top_n_sigma", C.c_float), ("xtc_probability", C.c_float),
+                ("xtc_threshold", C.c_float), ("dynatemp_range", C.c_float), ("dynatemp_exponent", C.c_float),
+                ("repeat_penalty", C.c_float), ("frequency_penalty", C.c_float), ("presence_penalty", C.c_float),
+                ("repeat_last_n", C.c_uint32), ("dry_multiplier", C.c_float), ("dry_base", C.c_float),
+                ("dry_allowed_length", C.c_uint32), ("dry_penalty_last_n", C.c_uint32), ("mirostat", C.c_uint32),
+                ("mirostat_tau", C.c_float), ("mirostat_eta", C.c_float), ("adaptive_p", C.c_float),
+                ("adaptive_decay", C.c_float), ("ignore_eos", C.c_int32), ("eos", C.c_int32),
+                ("chain", C.POINTER(C.c_int32)), ("n_chain", C.c_uint32),
+                ("bias_ids", C.POINTER(C.c_uint32)), ("bias_values", C.POINTER(C.c_float)), ("n_bias", C.c_uint32),
+                ("suppress_ids", C.POINTER(C.c_uint32)), ("n_suppress", C.c_uint32),
+                ("dry_breakers", C.POINTER(C.c_uint32)), ("n_dry_breakers", C.c_uint32), ("seed", C.c_uint64)]
+
+
+class SamplerState(C.Structure):
+    _fields_ = [("rng", C.c_uint64), ("mu", C.c_float), ("ap_weighted", C.c_float), ("ap_total", C.c_float)]
+
+
+STAGE_TOP_K, STAGE_TYPICAL_P, STAGE_TOP_P, STAGE_MIN_P, STAGE_XTC, STAGE_TEMPERATURE = range(6)
+
+
 def build() -> str:
-    src = [os.path.join(HERE, f) for f in ("oracle.c", "oracle.h", "Makefile")]
+    src = [os.path.join(HERE, f) for f in ("oracle.c", "sample.c", "oracle.h", "Makefile")]
     if not os.path.exists(LIB) or any(os.path.getmtime(s) > os.path.getmtime(LIB) for s in src):
         subprocess.run(["make", "-s", "-C", HERE], check=True)
     return LIB
@@ -95,6 +118,25 @@ def lib() -> C.CDLL:
             "or_ggml_softmax": (None, [F, I, F]),
             "or_ggml_attn_head": (None, [F, C.POINTER(C.c_uint16), C.POINTER(C.c_uint16), C.c_int64, I, I, C.c_float,
                                          I, F]),
+            "or_ln": (C.c_float, [C.c_float]),
+            "or_pow": (C.c_float, [C.c_float, C.c_float]),
+            "or_sampler_config_default": (None, [C.POINTER(SamplerConfig)]),
+            "or_sampler_config_llamacpp": (None, [C.POINTER(SamplerConfig)]),
+            "or_sampler_init": (None, [C.POINTER(SamplerConfig), C.POINTER(SamplerState)]),
+            "or_sampler_next_f32": (C.c_float, [C.POINTER(SamplerState)]),
+            "or_sample": (C.c_int64, [C.POINTER(SamplerConfig), C.POINTER(SamplerState), F, C.c_int64, C.POINTER(C.c_uint32),
+                                      C.c_int64]),
+            "or_stage_top_p": (C.c_int64, [C.POINTER(C.c_uint32), F, C.c_int64, C.c_float]),
+            "or_stage_min_p": (C.c_int64, [C.POINTER(C.c_uint32), F, C.c_int64, C.c_float]),
+            "or_stage_typical_p": (C.c_int64, [C.POINTER(C.c_uint32), F, C.c_int64, C.c_float]),
+            "or_stage_top_n_sigma": (C.c_int64, [C.POINTER(C.c_uint32), F, C.c_int64, C.c_float]),
+            "or_stage_xtc": (C.c_int64, [C.POINTER(C.c_uint32), F, C.c_int64, C.c_float, C.c_float, C.c_float]),
+            "or_stage_temperature": (None, [F, C.c_int64, C.c_float]),
+            "or_dynamic_temperature": (C.c_float, [F, C.c_int64, C.c_float, C.c_float, C.c_float]),
+            "or_stage_penalties": (None, [C.POINTER(C.c_uint32), F, C.c_int64, C.POINTER(C.c_uint32), C.c_int64, C.c_float, C.c_float, C.c_float,
+                                          C.c_uint32]),
+            "or_stage_dry": (None, [C.POINTER(C.c_uint32), F, C.c_int64, C.POINTER(C.c_uint32), C.c_int64, C.c_float, C.c_float, C.c_uint32,
+                                    C.c_uint32, C.POINTER(C.c_uint32), C.c_uint32]),
         }
         for n, (r, a) in sig.items():
             fn = getattr(L, n)
@@ -352,3 +394,101 @@ class Model:
             tok = argmax(logits)
             toks.append(tok)
         return toks
+
+
+# ---------------------------------------------------------------- the token sampler (sample.c)
+_LISTS = {"chain": (C.c_int32, np.int32), "bias_ids": (C.c_uint32, np.uint32),
+          "bias_values": (C.c_float, np.float32), "suppress_ids": (C.c_uint32, np.uint32),
+          "dry_breakers": (C.c_uint32, np.uint32)}
+_COUNTS = {"chain": "n_chain", "bias_ids": "n_bias", "suppress_ids": "n_suppress", "dry_breakers": "n_dry_breakers"}
+
+
+def sampler_config(base: str = "default", **kw):
+    """(SamplerConfig, keep-alive arrays): SamplerConfig::default() or llamacpp_defaults() with the
+    fields in `kw` replaced. List fields (chain, bias_ids, bias_values, suppress_ids, dry_breakers)
+    take sequences; `chain=None` means the default chain."""
+    c = SamplerConfig()
+    (lib().or_sampler_config_llamacpp if base == "llamacpp" else lib().or_sampler_config_default)(C.byref(c))
+    keep = []
+    for k, v in kw.items():
+        if k in _LISTS:
+            if v is None:
+                continue
+            ct, nt = _LISTS[k]
+            a = np.ascontiguousarray(np.asarray(v, dtype=nt))
+            keep.append(a)
+            setattr(c, k, a.ctypes.data_as(C.POINTER(ct)) if a.size else C.cast(C.pointer(ct()), C.POINTER(ct)))
+            if k in _COUNTS:
+                setattr(c, _COUNTS[k], int(a.size))
+        else:
+            setattr(c, k, v)
+    return c, keep
+
+
+def sampler_state(cfg) -> SamplerState:
+    st = SamplerState()
+    lib().or_sampler_init(C.byref(cfg), C.byref(st))
+    return st
+
+
+def sample(cfg, st: SamplerState, logits, history=()) -> int:
+    """Sampler::sample (sample.rs:474-680); advances `st` as the reference's Sampler does"""
+    lg = np.ascontiguousarray(np.asarray(logits, dtype=np.float32))
+    h = np.ascontiguousarray(np.asarray(history, dtype=np.uint32))
+    r = lib().or_sample(C.byref(cfg), C.byref(st), _f(lg), lg.size, h.ctypes.data_as(C.POINTER(C.c_uint32)), h.size)
+    if r < 0:
+        raise ValueError(lib().or_last_error().decode())
+    return int(r)
+
+
+def _cand(c):
+    ids = np.ascontiguousarray(np.array([x[0] for x in c], dtype=np.uint32))
+    vals = np.ascontiguousarray(np.array([x[1] for x in c], dtype=np.float32))
+    return ids, vals
+
+
+def _u32p(a):
+    return a.ctypes.data_as(C.POINTER(C.c_uint32))
+
+
+def stage(name: str, cands, *args):
+    """run one stage function on a list of (id, value) pairs; returns the new list"""
+    ids, vals = _cand(cands)
+    fn = getattr(lib(), "or_stage_" + name)
+    n = fn(_u32p(ids), _f(vals), ids.size, *args)
+    return [(int(i), float(v)) for i, v in zip(ids[:n], vals[:n])]
+
+
+def stage_temperature(cands, t: float):
+    ids, vals = _cand(cands)
+    lib().or_stage_temperature(_f(vals), vals.size, t)
+    return [(int(i), float(v)) for i, v in zip(ids, vals)]
+
+
+def dynamic_temperature(cands, t: float, rng: float, ex: float) -> float:
+    _, vals = _cand(cands)
+    return float(lib().or_dynamic_temperature(_f(vals), vals.size, t, rng, ex))
+
+
+def stage_penalties(cands, history, repeat, frequency, presence, last_n):
+    ids, vals = _cand(cands)
+    h = np.ascontiguousarray(np.asarray(history, dtype=np.uint32))
+    lib().or_stage_penalties(_u32p(ids), _f(vals), ids.size, _u32p(h), h.size, repeat, frequency, presence, last_n)
+    return [(int(i), float(v)) for i, v in zip(ids, vals)]
+
+
+def stage_dry(cands, history, multiplier, base, allowed, last_n, breakers=()):
+    ids, vals = _cand(cands)
+    h = np.ascontiguousarray(np.asarray(history, dtype=np.uint32))
+    b = np.ascontiguousarray(np.asarray(breakers, dtype=np.uint32))
+    lib().or_stage_dry(_u32p(ids), _f(vals), ids.size, _u32p(h), h.size, multiplier, base, allowed, last_n,
+                       _u32p(b), b.size)
+    return [(int(i), float(v)) for i, v in zip(ids, vals)]
+
+
+def ln(x: float) -> float:
+    return float(lib().or_ln(x))
+
+
+def pow_(x: float, y: float) -> float:
+    return float(lib().or_pow(x, y))
