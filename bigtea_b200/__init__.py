@@ -7,7 +7,7 @@ libbigtea_decode.so and fails if it is missing: there is no CPU fallback.
 """
 from ._lib import BtError, lib  # noqa: F401  (loads the library: fails loudly if absent)
 from .models import CONFIGS, Qwen3MoeConfig, config, synth_model, write_gguf, read_gguf  # noqa: F401
-from .runner import Engine, KvCache, StreamingRunner, dequantize, ep_unique_id, gemv, pinned_empty  # noqa: F401
+from .runner import Engine, KvCache, Sampler, StreamingRunner, dequantize, ep_unique_id, gemv, pinned_empty  # noqa: F401
 
-__all__ = ["Engine", "KvCache", "StreamingRunner", "Qwen3MoeConfig", "CONFIGS", "config", "synth_model",
+__all__ = ["Engine", "KvCache", "Sampler", "StreamingRunner", "Qwen3MoeConfig", "CONFIGS", "config", "synth_model",
            "write_gguf", "read_gguf", "dequantize", "gemv", "ep_unique_id", "BtError"]

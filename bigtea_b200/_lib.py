@@ -62,6 +62,27 @@ class KernelTime(C.Structure):
     _fields_ = [("name", C.c_char * 32), ("launches", C.c_uint64), ("total_ms", C.c_double)]
 
 
+class SamplerConfig(C.Structure):
+    """bt_sampler_config: SamplerConfig (core/arch/src/sample.rs:84-180)"""
+    _fields_ = [("temperature", C.c_float), ("top_k", C.c_uint32), ("top_p", C.c_float), ("min_p", C.c_float),
+                ("typical_p", C.c_float), ("top_n_sigma", C.c_float), ("xtc_probability", C.c_float),
+                ("xtc_threshold", C.c_float), ("dynatemp_range", C.c_float), ("dynatemp_exponent", C.c_float),
+                ("repeat_penalty", C.c_float), ("frequency_penalty", C.c_float), ("presence_penalty", C.c_float),
+                ("repeat_last_n", C.c_uint32), ("dry_multiplier", C.c_float), ("dry_base", C.c_float),
+                ("dry_allowed_length", C.c_uint32), ("dry_penalty_last_n", C.c_uint32), ("mirostat", C.c_uint32),
+                ("mirostat_tau", C.c_float), ("mirostat_eta", C.c_float), ("adaptive_p", C.c_float),
+                ("adaptive_decay", C.c_float), ("ignore_eos", C.c_int32), ("eos", C.c_int32),
+                ("chain", C.POINTER(C.c_int32)), ("n_chain", C.c_uint32),
+                ("bias_ids", C.POINTER(C.c_uint32)), ("bias_values", C.POINTER(C.c_float)), ("n_bias", C.c_uint32),
+                ("suppress_ids", C.POINTER(C.c_uint32)), ("n_suppress", C.c_uint32),
+                ("dry_breakers", C.POINTER(C.c_uint32)), ("n_dry_breakers", C.c_uint32), ("seed", C.c_uint64)]
+
+
+class SamplerState(C.Structure):
+    """bt_sampler_state: the state a Sampler carries between tokens (sample.rs:306-321)"""
+    _fields_ = [("rng", C.c_uint64), ("mu", C.c_float), ("ap_weighted", C.c_float), ("ap_total", C.c_float)]
+
+
 _P = C.c_void_p
 _U32P = C.POINTER(C.c_uint32)
 _F32P = C.POINTER(C.c_float)
@@ -93,6 +114,11 @@ SIGNATURES = {
     "bt_forward": (C.c_int, [_P, _P, _P, _P, _P, _P, C.c_uint32, _P]),
     "bt_generate_greedy": (C.c_int, [_P, _P, _U32P, _U32P, C.c_uint32, C.c_uint32, _U32P, _F32P]),
     "bt_last_device_ms": (C.c_int, [_P, C.POINTER(C.c_double)]),
+    "bt_sampler_config_default": (None, [C.POINTER(SamplerConfig)]),
+    "bt_sampler_config_llamacpp": (None, [C.POINTER(SamplerConfig)]),
+    "bt_sampler_init": (C.c_int, [C.POINTER(SamplerConfig), C.POINTER(SamplerState)]),
+    "bt_sample": (C.c_int, [_P, C.POINTER(SamplerConfig), C.POINTER(SamplerState), C.c_uint32, _F32P, _U32P, _U32P,
+                            _U32P]),
     "bt_host_alloc": (C.c_int, [C.c_uint64, C.POINTER(C.c_void_p)]),
     "bt_host_free": (C.c_int, [_P]),
     "bt_bench_experts": (C.c_int, [_P, C.c_uint32, C.c_uint32, C.c_uint64, C.c_uint32, C.POINTER(C.c_double),

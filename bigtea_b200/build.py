@@ -15,8 +15,8 @@ import sys
 PKG = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(PKG, "csrc")
 LIB = os.path.join(PKG, "libbigtea_decode.so")
-SOURCES = ["kernels.cu", "step_kernel.cu", "expert_stream.cu", "xcache.cu", "mma.cu", "engine.cu"]
-DEPS = SOURCES + ["kernels.cuh", "kquant.cuh", "bt_common.cuh", "stage.cuh", "step_kernel.cuh", "expert_stream.cuh", "xcache_dev.cuh", "umma.cuh",
+SOURCES = ["kernels.cu", "step_kernel.cu", "expert_stream.cu", "xcache.cu", "mma.cu", "sampler.cu", "engine.cu"]
+DEPS = SOURCES + ["kernels.cuh", "kquant.cuh", "bt_common.cuh", "stage.cuh", "step_kernel.cuh", "expert_stream.cuh", "xcache_dev.cuh", "umma.cuh", "sampler.cuh",
                   "expert_cache.h"]
 HEADER = os.path.join(os.path.dirname(PKG), "include", "bigtea_decode.h")
 

@@ -34,6 +34,7 @@ constexpr int EP_STEP_TOKENS = 64;
 #define BT_STEP_TOKENS 128  // tokens of one step of the per-phase kernels (longer calls are cut into steps)
 #endif
 #include "xcache_dev.cuh"
+#include "sampler.cuh"
 
 using namespace bt;
 
@@ -201,6 +202,8 @@ struct bt_engine {
     std::map<GraphKey, cudaGraphExec_t> graphs;
     cudaGraph_t graph_objs[64] = {};
     int last_T = 0;        // tokens in the last step of the last bt_forward
+    int last_rows = 0;     // logits rows the last bt_forward / bt_generate_greedy left in `logits`
+    DevBuf samp_scratch, samp_aux, samp_in;  // bt_sample: sort and chain scratch, lists, host logits
     size_t last_first = 0; // index (in that call's token list) of the step's first token
     // profiling
     bool timing = false;
@@ -2382,6 +2385,7 @@ extern "C" int bt_forward(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, cons
         kv->len[s] += n_tokens[i];
         for (auto &c : kv->layer_pos[s]) c = kv->len[s];
     }
+    e->last_rows = (int)n_seqs;
     e->stats.forward_calls++;
     e->stats.tokens += total;
     e->stats.forward_seconds += std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
@@ -2445,6 +2449,7 @@ static int greedy_finish(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, uint3
         for (auto &c : kv->layer_pos[s]) c = kv->len[s];
     }
     e->stats.tokens += (uint64_t)n_steps * n_seqs;
+    if (n_steps) e->last_rows = (int)n_seqs;
     e->last_T = (int)n_seqs;
     e->last_first = 0;
     return BT_OK;
@@ -2697,6 +2702,171 @@ extern "C" int bt_host_free(void *p) {
         cudaGetLastError();
         return fail(BT_ERR_INVALID, "not a bt_host_alloc block");
     }
+    return BT_OK;
+}
+
+// ------------------------------------------------------------------ sampling
+extern "C" void bt_sampler_config_default(bt_sampler_config *c) {
+    if (!c) return;
+    memset(c, 0, sizeof *c);
+    c->adaptive_p = -1.0f;  // SamplerConfig::default (sample.rs:183-222)
+    c->adaptive_decay = 0.95f;
+    c->top_p = 1.0f;
+    c->repeat_penalty = 1.0f;
+    c->repeat_last_n = 64;
+    c->dry_base = 1.75f;
+    c->dry_allowed_length = 2;
+    c->typical_p = 1.0f;
+    c->dynatemp_exponent = 1.0f;
+    c->xtc_threshold = 0.1f;
+    c->mirostat_tau = 5.0f;
+    c->mirostat_eta = 0.1f;
+    c->eos = -1;
+}
+
+extern "C" void bt_sampler_config_llamacpp(bt_sampler_config *c) {
+    if (!c) return;
+    bt_sampler_config_default(c);  // llamacpp_defaults (sample.rs:228-268)
+    c->temperature = 0.8f;
+    c->top_k = 40;
+    c->top_p = 0.95f;
+    c->min_p = 0.05f;
+    c->repeat_penalty = 1.1f;
+}
+
+static float clamp_rs(float v, float lo, float hi) {
+    if (v < lo) v = lo;
+    if (v > hi) v = hi;
+    return v;
+}
+
+extern "C" int bt_sampler_init(const bt_sampler_config *c, bt_sampler_state *st) {
+    if (!c || !st) return fail(BT_ERR_INVALID, "null argument");
+    st->rng = c->seed + 0x9E3779B97F4A7C15ull;  // Sampler::new (sample.rs:324-344)
+    const float decay = clamp_rs(c->adaptive_decay, 0.0f, 0.99f);
+    const float ap = (c->adaptive_p != c->adaptive_p || c->adaptive_p < 0.0f) ? 0.0f : c->adaptive_p;
+    st->ap_weighted = ap / (1.0f - decay);
+    st->ap_total = 1.0f / (1.0f - decay);
+    st->mu = 2.0f * c->mirostat_tau;
+    return BT_OK;
+}
+
+static_assert(sizeof(bt_sampler_state) == sizeof(SampState), "bt_sampler_state and SampState agree");
+
+extern "C" int bt_sample(bt_engine *e, const bt_sampler_config *cfg, bt_sampler_state *states, uint32_t n_seqs,
+                         const float *logits, const uint32_t *history, const uint32_t *history_len,
+                         uint32_t *tokens_out) {
+    if (!e || !cfg || !states || !tokens_out) return fail(BT_ERR_INVALID, "null argument");
+    if (n_seqs == 0 || n_seqs > (uint32_t)e->max_out) return fail(BT_ERR_INVALID, "1..256 sequences per call");
+    if (!logits && (int)n_seqs > e->last_rows)
+        return fail(BT_ERR_INVALID, "no device logits for that many sequences: run bt_forward first or pass logits");
+    if (cfg->chain && cfg->n_chain > (uint32_t)SAMP_MAX_CHAIN) return fail(BT_ERR_INVALID, "at most 32 sampler stages");
+    if ((cfg->n_bias && (!cfg->bias_ids || !cfg->bias_values)) || (cfg->n_suppress && !cfg->suppress_ids) ||
+        (cfg->n_dry_breakers && !cfg->dry_breakers))
+        return fail(BT_ERR_INVALID, "a sampler list has a length but no array");
+    SampParams P{};
+    P.temperature = cfg->temperature;
+    P.top_k = cfg->top_k;
+    P.top_p = cfg->top_p;
+    P.min_p = cfg->min_p;
+    P.typical_p = cfg->typical_p;
+    P.top_n_sigma = cfg->top_n_sigma;
+    P.xtc_probability = cfg->xtc_probability;
+    P.xtc_threshold = cfg->xtc_threshold;
+    P.dynatemp_range = cfg->dynatemp_range;
+    P.dynatemp_exponent = cfg->dynatemp_exponent;
+    P.repeat_penalty = cfg->repeat_penalty;
+    P.frequency_penalty = cfg->frequency_penalty;
+    P.presence_penalty = cfg->presence_penalty;
+    P.repeat_last_n = cfg->repeat_last_n;
+    P.dry_multiplier = cfg->dry_multiplier;
+    P.dry_base = cfg->dry_base;
+    P.dry_allowed_length = cfg->dry_allowed_length;
+    P.dry_penalty_last_n = cfg->dry_penalty_last_n;
+    P.mirostat = cfg->mirostat;
+    P.mirostat_tau = cfg->mirostat_tau;
+    P.mirostat_eta = cfg->mirostat_eta;
+    P.adaptive_p = cfg->adaptive_p;
+    P.adaptive_decay = cfg->adaptive_decay;
+    P.ignore_eos = cfg->ignore_eos;
+    P.eos = cfg->eos;
+    if (cfg->chain) {
+        P.n_chain = (int)cfg->n_chain;
+        for (uint32_t k = 0; k < cfg->n_chain; k++) {
+            if (cfg->chain[k] < BT_STAGE_TOP_K || cfg->chain[k] > BT_STAGE_TEMPERATURE)
+                return fail(BT_ERR_INVALID, "unknown sampler stage");
+            P.chain[k] = cfg->chain[k];
+        }
+    } else {  // SamplerStage::default_chain (sample.rs:70-79)
+        P.n_chain = 6;
+        for (int k = 0; k < 6; k++) P.chain[k] = k;
+    }
+    P.n_bias = (int)cfg->n_bias;
+    P.n_suppress = (int)cfg->n_suppress;
+    P.n_breakers = (int)cfg->n_dry_breakers;
+    P.greedy = cfg->temperature <= 0.0f && cfg->repeat_penalty == 1.0f && cfg->frequency_penalty == 0.0f &&
+               cfg->presence_penalty == 0.0f && cfg->n_bias == 0 && !cfg->ignore_eos && cfg->mirostat == 0 &&
+               cfg->dry_multiplier == 0.0f && cfg->adaptive_p < 0.0f && cfg->n_suppress == 0;
+    const int V = (int)e->d.n_vocab;
+    // the lists, the histories and the states go up in one copy
+    std::vector<uint32_t> off(n_seqs + 1, 0);
+    for (uint32_t i = 0; i < n_seqs; i++) off[i + 1] = off[i] + (history_len ? history_len[i] : 0);
+    if (off[n_seqs] && !history) return fail(BT_ERR_INVALID, "history lengths without a history");
+    size_t at = 0;
+    auto slot = [&](size_t bytes) {
+        const size_t a = (at + 15) & ~(size_t)15;
+        at = a + bytes;
+        return a;
+    };
+    const size_t o_bid = slot(4ull * cfg->n_bias), o_bval = slot(4ull * cfg->n_bias);
+    const size_t o_sup = slot(4ull * cfg->n_suppress), o_brk = slot(4ull * cfg->n_dry_breakers);
+    const size_t o_hist = slot(4ull * off[n_seqs]), o_off = slot(4ull * (n_seqs + 1));
+    const size_t o_st = slot(sizeof(SampState) * n_seqs), o_tok = slot(4ull * n_seqs), o_stat = slot(4ull * n_seqs);
+    std::vector<uint8_t> host(at);
+    auto put = [&](size_t o, const void *src, size_t bytes) {
+        if (bytes) memcpy(host.data() + o, src, bytes);
+    };
+    put(o_bid, cfg->bias_ids, 4ull * cfg->n_bias);
+    put(o_bval, cfg->bias_values, 4ull * cfg->n_bias);
+    put(o_sup, cfg->suppress_ids, 4ull * cfg->n_suppress);
+    put(o_brk, cfg->dry_breakers, 4ull * cfg->n_dry_breakers);
+    put(o_hist, history, 4ull * off[n_seqs]);
+    put(o_off, off.data(), 4ull * (n_seqs + 1));
+    put(o_st, states, sizeof(SampState) * n_seqs);
+    CK(cudaSetDevice(e->device));
+    if (e->samp_aux.n < at) CK(e->samp_aux.alloc(at));
+    const size_t need = sampler_scratch_bytes((int)n_seqs, V);
+    if (e->samp_scratch.n < need) CK(e->samp_scratch.alloc(need));
+    uint8_t *aux = e->samp_aux.as<uint8_t>();
+    CK(cudaMemcpyAsync(aux, host.data(), at, cudaMemcpyHostToDevice, e->st));
+    const float *rows = e->logits.as<float>();
+    if (logits) {
+        const size_t lb = (size_t)n_seqs * V * 4;
+        if (e->samp_in.n < lb) CK(e->samp_in.alloc(lb));
+        CK(cudaMemcpyAsync(e->samp_in.p, logits, lb, cudaMemcpyHostToDevice, e->st));
+        rows = e->samp_in.as<float>();
+    }
+    SampLists L{};
+    L.bias_ids = reinterpret_cast<const uint32_t *>(aux + o_bid);
+    L.bias_values = reinterpret_cast<const float *>(aux + o_bval);
+    L.suppress_ids = reinterpret_cast<const uint32_t *>(aux + o_sup);
+    L.breakers = reinterpret_cast<const uint32_t *>(aux + o_brk);
+    L.hist = reinterpret_cast<const uint32_t *>(aux + o_hist);
+    L.hist_off = reinterpret_cast<const uint32_t *>(aux + o_off);
+    auto *dst = reinterpret_cast<SampState *>(aux + o_st);
+    auto *dtok = reinterpret_cast<uint32_t *>(aux + o_tok);
+    auto *dstat = reinterpret_cast<int *>(aux + o_stat);
+    CK(sampler_launch(e->st, P, L, rows, V, (int)n_seqs, e->samp_scratch.p, e->samp_scratch.n, dst, dtok, dstat));
+    CK(cudaMemcpyAsync(host.data() + o_st, aux + o_st, o_stat + 4ull * n_seqs - o_st, cudaMemcpyDeviceToHost, e->st));
+    int r = wait_stream(e);
+    if (r) return r;
+    const int *stat = reinterpret_cast<const int *>(host.data() + o_stat);
+    for (uint32_t i = 0; i < n_seqs; i++)
+        if (stat[i] == SAMP_ERR_TYPICAL_TOO_MANY)
+            return fail(BT_ERR_UNSUPPORTED,
+                        "typical_p over more than 4096 candidates: set top_k, or put top_p or min_p before it");
+    memcpy(states, host.data() + o_st, sizeof(SampState) * n_seqs);
+    memcpy(tokens_out, host.data() + o_tok, 4ull * n_seqs);
     return BT_OK;
 }
 

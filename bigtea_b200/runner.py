@@ -321,6 +321,62 @@ class StreamingRunner:
         return {arr[i].name.decode(): (arr[i].launches, arr[i].total_ms) for i in range(min(n.value, cap))}
 
 
+_SAMPLER_LISTS = {"chain": (C.c_int32, np.int32, "n_chain"), "bias_ids": (C.c_uint32, np.uint32, "n_bias"),
+                  "bias_values": (C.c_float, np.float32, None), "suppress_ids": (C.c_uint32, np.uint32, "n_suppress"),
+                  "dry_breakers": (C.c_uint32, np.uint32, "n_dry_breakers")}
+STAGES = {"top_k": 0, "typical_p": 1, "top_p": 2, "min_p": 3, "xtc": 4, "temperature": 5}
+
+
+class Sampler:
+    """Sampler (core/arch/src/sample.rs:306-680) for a batch of sequences, on the device.
+
+    `config` fields are SamplerConfig's (`base="llamacpp"` starts from llamacpp_defaults());
+    `chain` takes stage numbers or llama.cpp's names (SamplerStage::parse spellings of the common
+    forms). One state per sequence, advanced as the reference's Sampler is; `sample` returns one
+    token per sequence."""
+
+    def __init__(self, engine: Engine, n_seqs: int = 1, base: str = "default", **config):
+        self.engine = engine
+        self.cfg = _lib.SamplerConfig()
+        (lib.bt_sampler_config_llamacpp if base == "llamacpp" else lib.bt_sampler_config_default)(C.byref(self.cfg))
+        self._keep = []
+        for k, v in config.items():
+            if k in _SAMPLER_LISTS:
+                if v is None:
+                    continue
+                ct, nt, count = _SAMPLER_LISTS[k]
+                if k == "chain":
+                    v = [STAGES[x] if isinstance(x, str) else int(x) for x in v]
+                a = np.ascontiguousarray(np.asarray(v, dtype=nt))
+                if a.size == 0:
+                    a = np.zeros(1, nt)[:0]
+                self._keep.append(a)
+                setattr(self.cfg, k, C.cast(a.ctypes.data, C.POINTER(ct)))
+                if count:
+                    setattr(self.cfg, count, int(a.size))
+            else:
+                setattr(self.cfg, k, v)
+        self.states = (_lib.SamplerState * n_seqs)()
+        for i in range(n_seqs):
+            check(lib.bt_sampler_init(C.byref(self.cfg), C.byref(self.states[i])))
+
+    def sample(self, logits=None, histories=None) -> np.ndarray:
+        """One token per sequence. `logits` None samples the engine's logits of its last forward
+        (no copy to the host); else a host array [n_seqs, n_vocab]. `histories`: one token list
+        per sequence (the tokens so far), or None."""
+        n = len(self.states)
+        if logits is not None:
+            logits = np.ascontiguousarray(logits, dtype=np.float32).reshape(n, -1)
+        hl = np.array([len(h) for h in histories] if histories is not None else [0] * n, np.uint32)
+        hist = (np.concatenate([_u32(h) for h in histories]) if histories is not None and hl.sum()
+                else np.zeros(1, np.uint32))
+        out = np.empty(n, np.uint32)
+        check(lib.bt_sample(self.engine.h, C.byref(self.cfg), self.states, n,
+                            _lib.ptr(logits, C.c_float) if logits is not None else None,
+                            _lib.ptr(hist, C.c_uint32), _lib.ptr(hl, C.c_uint32), _lib.ptr(out, C.c_uint32)))
+        return out
+
+
 def dequantize(ggml_type: int, data: np.ndarray, n: int) -> np.ndarray:
     """dequantize() (core/ggml/src/lib.rs:233-290) through the device kernels."""
     out = np.empty(n, np.float32)

@@ -154,6 +154,61 @@ int bt_forward(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const uint32_t 
 int bt_generate_greedy(bt_engine *e, bt_kv *kv, const uint32_t *seq_ids, const uint32_t *first_tokens,
                        uint32_t n_seqs, uint32_t n_steps, uint32_t *tokens_out, float *last_logits);
 
+/* ---- token sampling on the device: Sampler (core/arch/src/sample.rs:306-680) ---- */
+/* SamplerStage (sample.rs:43-50) */
+enum { BT_STAGE_TOP_K = 0, BT_STAGE_TYPICAL_P = 1, BT_STAGE_TOP_P = 2, BT_STAGE_MIN_P = 3, BT_STAGE_XTC = 4,
+       BT_STAGE_TEMPERATURE = 5 };
+/* SamplerConfig (sample.rs:84-180), field for field; the list fields are host arrays. eos < 0 is
+ * None; chain == NULL is the default chain (top_k, typical_p, top_p, min_p, xtc, temperature),
+ * at most 32 stages otherwise. bt_sampler_config_default fills SamplerConfig::default() (greedy)
+ * and bt_sampler_config_llamacpp llamacpp_defaults(). */
+typedef struct bt_sampler_config {
+    float temperature;
+    uint32_t top_k;
+    float top_p, min_p, typical_p, top_n_sigma;
+    float xtc_probability, xtc_threshold;
+    float dynatemp_range, dynatemp_exponent;
+    float repeat_penalty, frequency_penalty, presence_penalty;
+    uint32_t repeat_last_n;
+    float dry_multiplier, dry_base;
+    uint32_t dry_allowed_length, dry_penalty_last_n;
+    uint32_t mirostat;
+    float mirostat_tau, mirostat_eta;
+    float adaptive_p, adaptive_decay;
+    int32_t ignore_eos, eos;
+    const int32_t *chain;
+    uint32_t n_chain;
+    const uint32_t *bias_ids;
+    const float *bias_values;
+    uint32_t n_bias;
+    const uint32_t *suppress_ids; /* infill_suppress */
+    uint32_t n_suppress;
+    const uint32_t *dry_breakers; /* dry_sequence_breakers */
+    uint32_t n_dry_breakers;
+    uint64_t seed;
+} bt_sampler_config;
+/* The state a Sampler carries from token to token (sample.rs:306-321): the SplitMix64 word,
+ * mirostat's mu and adaptive-p's two accumulators. Caller-owned, one per sequence. */
+typedef struct bt_sampler_state {
+    uint64_t rng;
+    float mu, ap_weighted, ap_total;
+} bt_sampler_state;
+void bt_sampler_config_default(bt_sampler_config *c);
+void bt_sampler_config_llamacpp(bt_sampler_config *c);
+/* Sampler::new (sample.rs:324-344): the state of a fresh sampler for `c` (host only). */
+int bt_sampler_init(const bt_sampler_config *c, bt_sampler_state *state);
+/* Sampler::sample (sample.rs:474-680) for n_seqs sequences at once, on the device. `logits` is
+ * NULL for the engine's own logits of the last bt_forward or bt_generate_greedy call (row i is
+ * that call's sequence i; no logits cross to the host), else a host array [n_seqs][n_vocab].
+ * Sequence i's history (the tokens so far, for the penalties and DRY) is
+ * history[sum(history_len[0..i)) ...] of history_len[i] tokens; history_len may be NULL (no
+ * history). states[i] is read and advanced as the reference's Sampler advances. The results
+ * equal the reference's algorithm with this library's exp/ln/pow and tie rules (the smaller id
+ * first among equal logits). typical_p runs on at most 4096 candidates: BT_ERR_UNSUPPORTED
+ * beyond that (set top_k, or put top_p or min_p before it in the chain). */
+int bt_sample(bt_engine *e, const bt_sampler_config *cfg, bt_sampler_state *states, uint32_t n_seqs,
+              const float *logits, const uint32_t *history, const uint32_t *history_len, uint32_t *tokens_out);
+
 /* Device time (CUDA events on the engine stream) of the last bt_generate_greedy replay loop. */
 int bt_last_device_ms(const bt_engine *e, double *ms);
 /* Page-locked host memory (no counterpart in the reference). bt_forward copies logits straight

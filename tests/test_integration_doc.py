@@ -140,7 +140,8 @@ def test_documented_constants_match_the_header():
 def test_documented_structs_match_the_header():
     _, hs, _ = parse_header()
     _, rs, _ = parse_rust(rust_block())
-    for name in ("bt_model_desc", "bt_tensor_view", "bt_stats", "bt_kernel_time", "bt_xcache_stats"):
+    for name in ("bt_model_desc", "bt_tensor_view", "bt_stats", "bt_kernel_time", "bt_xcache_stats",
+                 "bt_sampler_config", "bt_sampler_state"):
         assert name in rs, f"struct {name} is not documented"
         assert rs[name] == hs[name], f"struct {name}: documented {rs[name]}, header {hs[name]}"
 

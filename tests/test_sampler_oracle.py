@@ -9,7 +9,9 @@ independent restatement.
   and sharing only the exp/ln/pow primitives, on random logits, histories and configurations:
   the two must return the same token and the same sampler state, bit for bit.
 """
+import ctypes as C
 import math
+import os
 
 import numpy as np
 import pytest
@@ -415,3 +417,28 @@ def test_c_and_python_restatements_agree(seed):
             assert st.rng == py.rng and np.float32(st.mu) == py.mu
             assert np.float32(st.ap_weighted) == py.apw and np.float32(st.ap_total) == py.apt
             hist = hist + [got]
+
+
+def test_sampler_structs_agree_with_the_header():
+    """bt_sampler_config / bt_sampler_state: the header, the product's ctypes mirror and the
+    oracle's struct have the same fields in the same order (the oracle's functions take the
+    product's structs' bytes in the GPU tests' comparisons)."""
+    import re
+
+    from bigtea_b200 import _lib
+
+    text = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                             "bigtea_decode.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    for cname, prod, orac in (("bt_sampler_config", _lib.SamplerConfig, orc.SamplerConfig),
+                              ("bt_sampler_state", _lib.SamplerState, orc.SamplerState)):
+        body = re.search(r"typedef struct %s \{(.*?)\} %s;" % (cname, cname), text, flags=re.S).group(1)
+        names = []
+        for stmt in body.split(";"):
+            stmt = " ".join(stmt.replace("*", " ").split())
+            if stmt:
+                first, *rest = stmt.split(",")
+                names += [first.split()[-1]] + [r.strip() for r in rest]
+        assert [f[0] for f in prod._fields_] == names
+        assert [f[0] for f in orac._fields_] == names
+        assert C.sizeof(prod) == C.sizeof(orac)
