@@ -13,7 +13,7 @@
 // The arithmetic is the oracle's, bit for bit: every sum the reference accumulates in candidate
 // order is accumulated in that order (staged through shared memory, added by one thread);
 // elementwise work (exp, pow, divisions) runs on all threads, since each element's value does not
-// depend on the order. exp is C7 (bt::bt_exp); ln and pow are C10/C11 below; ties in the sorts go to
+// depend on the order. exp is C7 (bt::bt_exp); ln and pow are S5/S6 below; ties in the sorts go to
 // the smaller token id or the earlier candidate. The library is built with --fmad=false, so no
 // multiply-add is fused unless written as fmaf.
 #include <cub/device/device_radix_sort.cuh>
@@ -38,7 +38,7 @@ __device__ __forceinline__ float key_float(uint32_t k) {
     return __uint_as_float((k & 0x80000000u) ? (k & 0x7fffffffu) : ~k);
 }
 
-// C10: ln x = e ln2 + 2 atanh((m-1)/(m+1)), m in [sqrt(1/2), sqrt(2)), the atanh series to s^11
+// S5: ln x = e ln2 + 2 atanh((m-1)/(m+1)), m in [sqrt(1/2), sqrt(2)), the atanh series to s^11
 __device__ float samp_ln(float x) {
     if (x != x) return x;
     if (x < 0.0f) return f_nan();
@@ -70,7 +70,7 @@ __device__ float samp_ln(float x) {
     return fe * 0.693145751953125f + fmaf(fe, 1.428606765330187045e-06f, lnm);
 }
 
-// C11
+// S6: x^y = exp(y ln x), with the IEEE special cases
 __device__ float samp_pow(float x, float y) {
     if (y == 0.0f || x == 1.0f) return 1.0f;
     if (x != x || y != y) return f_nan();

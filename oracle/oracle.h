@@ -154,7 +154,7 @@ int or_synth_tensor(int type, int64_t rows, int64_t cols, uint64_t seed, uint64_
 double or_copy_gbs(int64_t bytes, int threads, int reps);
 
 /* ---- the token sampler (core/arch/src/sample.rs), restated in sample.c ---- */
-/* C10 ln and C11 pow: this library's own functions (sample.c), used by the sampler */
+/* S5 ln and S6 pow: the sampler's own functions (sample.c) */
 float or_ln(float x);
 float or_pow(float x, float y);
 

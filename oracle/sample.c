@@ -7,13 +7,15 @@
  *
  * Where the reference's result is not fixed by its source, this restatement fixes it (the same
  * rules bind the device sampler):
- *  S1 exp, ln and pow are this library's (C7 or_exp; C10 or_ln; C11 or_pow below), not libm's.
+ *  S1 exp, ln and pow are this library's (C7 or_exp; S5 or_ln and S6 or_pow below), not libm's.
  *     Rust's f32::exp/ln/powf call the platform libm; the two agree to a few ulp.
  *  S2 sort_unstable_by has no tie order. Here ties are broken by the smaller token id (the main
  *     descending sort of logits) or the earlier candidate (typical_p's two sorts).
  *  S3 f32::powi (DRY) is square-and-multiply: r = 1; for each bit of the exponent from the
  *     lowest, r *= a if the bit is set, then a *= a (the compiler runtime's __powisf2).
  *  S4 log2 (mirostat) is or_ln(x) * 1.44269502 (f32).
+ *  S5 ln x = e ln2 + 2 atanh(s), s = (m-1)/(m+1), m in [sqrt(1/2), sqrt(2)), the series to s^11.
+ *  S6 pow x^y = exp(y ln x) (C7, S5), with the IEEE special cases for x = 0, 1, inf and NaN.
  */
 #include "oracle.h"
 
@@ -25,7 +27,7 @@
 const char *or_last_error(void);
 void or_set_error_text(const char *msg);
 
-/* ------------------------------------------------------------------ C10 ln, C11 pow */
+/* ------------------------------------------------------------------ S5 ln, S6 pow */
 static const float LN2_HI = 0.693145751953125f;          /* 16 significant bits: e * LN2_HI is exact */
 static const float LN2_LO = 1.428606765330187045e-06f;   /* ln 2 - LN2_HI */
 

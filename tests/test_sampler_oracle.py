@@ -4,7 +4,7 @@ independent restatement.
 - The cases of core/arch/src/sample.rs:1072-1380 (`mod tests`), restated on the oracle's stage
   functions and Sampler::sample, with the reference's inputs and assertions.
 - SplitMix64 against its published first outputs from state 0.
-- C10 ln and C11 pow against float64 libm within a few ulp.
+- S5 ln and S6 pow against float64 libm within a few ulp.
 - A Python restatement of Sampler::sample (sample.rs:474-680), written separately from the C one
   and sharing only the exp/ln/pow primitives, on random logits, histories and configurations:
   the two must return the same token and the same sampler state, bit for bit.
