@@ -189,6 +189,11 @@ def _sum(vals):
     return t
 
 
+def _fmax(a, b):
+    """f32::max: NaN gives way to the other operand"""
+    return F(np.fmax(F(a), F(b)))
+
+
 def _clamp(v, lo, hi):
     v = F(v)
     if v < lo:
@@ -206,7 +211,7 @@ class PySampler:
         self.c = c
         self.rng = (c["seed"] + 0x9E3779B97F4A7C15) & (2**64 - 1)
         decay = _clamp(c["adaptive_decay"], 0.0, 0.99)
-        self.apw = F(F(max(c["adaptive_p"], 0.0)) / F(F(1.0) - decay))
+        self.apw = F(_fmax(c["adaptive_p"], 0.0) / F(F(1.0) - decay))
         self.apt = F(F(1.0) / F(F(1.0) - decay))
         self.mu = F(F(2.0) * F(c["mirostat_tau"]))
 
@@ -237,7 +242,7 @@ class PySampler:
     def temperature(c, t):
         if abs(F(F(t) - F(1.0))) <= np.finfo(np.float32).eps:
             return c
-        inv = F(F(1.0) / F(max(F(t), F(1e-6))))
+        inv = F(F(1.0) / _fmax(t, 1e-6))
         c = [(i, _pow(v, inv)) for i, v in c]
         return PySampler.renorm(c)
 
@@ -258,6 +263,7 @@ class PySampler:
         c = self.c
         greedy = (c["temperature"] <= 0 and c["repeat_penalty"] == 1 and c["frequency_penalty"] == 0
                   and c["presence_penalty"] == 0 and not c["bias"] and c["mirostat"] == 0
+                  and not c["ignore_eos"] and not c["suppress"]
                   and c["dry_multiplier"] == 0 and c["adaptive_p"] < 0)
         lg = [F(x) for x in logits]
         if greedy:
@@ -265,6 +271,10 @@ class PySampler:
         v = list(lg)
         for i, b in c["bias"]:
             v[i] = F(v[i] + F(b))
+        if c["ignore_eos"] and 0 <= c["eos"] < len(v):
+            v[c["eos"]] = F(-np.inf)
+        for i in c["suppress"]:
+            v[i] = F(-np.inf)
         # penalties (sample.rs:967-1008)
         if c["repeat_last_n"] and hist:
             w = hist[-c["repeat_last_n"]:]
@@ -305,6 +315,18 @@ class PySampler:
         if c["temperature"] <= 0 and c["mirostat"] == 0 and c["adaptive_p"] < 0:
             return max(range(len(v)), key=lambda i: (_key(v[i]), i))
         cand = sorted(((i, v[i]) for i in range(len(v))), key=lambda t: (-_key(t[1]), t[0]))
+        if c["top_n_sigma"] > 0 and len(cand) >= 2:  # sample.rs:820-857
+            mx = F(-np.inf)
+            for _, x in cand:
+                mx = F(np.fmax(mx, x))
+            fin = [x for _, x in cand if np.isfinite(x)]
+            if np.isfinite(mx) and len(fin) >= 2:
+                mean = F(_sum(fin) / F(len(fin)))
+                var = F(_sum(F(F(x - mean) * F(x - mean)) for x in fin) / F(len(fin)))
+                sigma = F(np.sqrt(var))
+                if sigma > 0:
+                    fl = F(mx - F(F(c["top_n_sigma"]) * sigma))
+                    cand = [t for t in cand if t[1] >= fl]
         if c["top_k"] > 0:
             cand = cand[:c["top_k"]]
         cand = self.softmax(cand)
@@ -314,7 +336,7 @@ class PySampler:
             cand = self.temperature(cand[:kept], c["temperature"] if c["temperature"] > 0 else 1.0)
             k = self.draw(cand)
             p = cand[k][1]
-            obs = F(-F(_ln(max(p, F(1e-30))) * F(1.44269502162933349609375)))
+            obs = F(-F(_ln(_fmax(p, 1e-30)) * F(1.44269502162933349609375)))
             self.mu = F(self.mu - F(F(c["mirostat_eta"]) * F(obs - F(c["mirostat_tau"]))))
             self.mu = _clamp(self.mu, 0.0, 100.0)
             return cand[k][0]
@@ -338,7 +360,7 @@ class PySampler:
             elif s == orc.STAGE_TYPICAL_P and c["typical_p"] < 1 and len(cand) >= 2:
                 h = self.entropy(cand)
                 sc = sorted(range(len(cand)),
-                            key=lambda k: (_key(abs(F(-_ln(max(cand[k][1], F(1e-30))) - h))), k))
+                            key=lambda k: (_key(abs(F(-_ln(_fmax(cand[k][1], 1e-30)) - h))), k))
                 cum, keep = F(0.0), 0
                 for k in sc:
                     cum = F(cum + cand[k][1])
@@ -355,7 +377,16 @@ class PySampler:
                     if above >= 2:
                         cand = cand[above - 1:]
             elif s == orc.STAGE_TEMPERATURE:
-                cand = self.temperature(cand, c["temperature"])
+                t = F(c["temperature"])
+                if c["dynatemp_range"] > 0 and len(cand) >= 2:  # sample.rs:878-915
+                    lo = _fmax(F(t - F(c["dynatemp_range"])), 0.0)
+                    hi = F(t + F(c["dynatemp_range"]))
+                    h = self.entropy(cand)
+                    hmax = _ln(F(len(cand)))
+                    if hmax > 0:
+                        nrm = _clamp(F(h / hmax), 0.0, 1.0)
+                        t = F(lo + F(F(hi - lo) * _pow(nrm, _fmax(c["dynatemp_exponent"], 1e-6))))
+                cand = self.temperature(cand, t)
         if c["adaptive_p"] >= 0:  # sample.rs:374-419
             target = _clamp(c["adaptive_p"], 0.0, 1.0)
             mean = target if self.apt == 0 else F(self.apw / self.apt)
@@ -379,6 +410,8 @@ def _random_case(rng):
     logits = (rng.standard_normal(nv) * rng.choice([0.5, 2.0, 6.0])).astype(np.float32)
     if rng.random() < 0.3:  # ties
         logits[rng.integers(0, nv, nv // 3)] = logits[0]
+    if rng.random() < 0.15:  # infinities and NaN among the logits
+        logits[rng.integers(0, nv, 2)] = rng.choice([np.inf, -np.inf, np.nan])
     hist = [int(t) for t in rng.integers(0, min(nv, 12), int(rng.integers(0, 40)))]
     chain = list(rng.permutation(6)[: int(rng.integers(0, 7))]) if rng.random() < 0.4 else [0, 1, 2, 3, 4, 5]
     c = dict(temperature=float(rng.choice([0.0, 0.3, 0.8, 1.0, 1.7])), top_k=int(rng.choice([0, 1, 5, 40])),
@@ -391,11 +424,16 @@ def _random_case(rng):
              mirostat=int(rng.choice([0, 0, 0, 2])), mirostat_tau=5.0, mirostat_eta=0.1,
              adaptive_p=float(rng.choice([-1.0, -1.0, 0.3, 0.7])), adaptive_decay=float(rng.choice([0.95, 0.5])), seed=int(rng.integers(0, 2**63)), chain=chain,
              bias=[(int(rng.integers(0, nv)), float(rng.choice([-5.0, 2.5])))] if rng.random() < 0.3 else [],
-             breakers=[int(rng.integers(0, 12))] if rng.random() < 0.3 else [])
+             breakers=[int(rng.integers(0, 12))] if rng.random() < 0.3 else [],
+             top_n_sigma=float(rng.choice([0.0, 0.0, 1.0, 2.5])),
+             dynatemp_range=float(rng.choice([0.0, 0.0, 0.4])), dynatemp_exponent=float(rng.choice([1.0, 1.7])),
+             ignore_eos=int(rng.random() < 0.2), eos=int(rng.integers(0, nv)),
+             suppress=[int(rng.integers(0, nv))] if rng.random() < 0.2 else [])
     return logits, hist, c
 
 
-@pytest.mark.parametrize("seed", range(6))
+@pytest.mark.filterwarnings("ignore:invalid value")
+@pytest.mark.parametrize("seed", range(10))
 def test_c_and_python_restatements_agree(seed):
     rng = np.random.default_rng(100 + seed)
     for _ in range(40):
@@ -403,10 +441,11 @@ def test_c_and_python_restatements_agree(seed):
         kw = {k: c[k] for k in ("temperature", "top_k", "top_p", "min_p", "typical_p", "xtc_probability",
                                 "xtc_threshold", "repeat_penalty", "frequency_penalty", "presence_penalty",
                                 "repeat_last_n", "dry_multiplier", "dry_base", "mirostat", "mirostat_tau",
-                                "mirostat_eta", "adaptive_p", "adaptive_decay", "seed", "chain")}
+                                "mirostat_eta", "adaptive_p", "adaptive_decay", "seed", "chain", "top_n_sigma",
+                                "dynatemp_range", "dynatemp_exponent", "ignore_eos", "eos")}
         kw.update(dry_allowed_length=c["dry_allowed"], dry_penalty_last_n=c["dry_last_n"],
                   bias_ids=[b[0] for b in c["bias"]], bias_values=[b[1] for b in c["bias"]],
-                  dry_breakers=c["breakers"])
+                  dry_breakers=c["breakers"], suppress_ids=c["suppress"])
         cfg, keep = orc.sampler_config(**kw)
         st = orc.sampler_state(cfg)
         py = PySampler(c)
@@ -414,8 +453,9 @@ def test_c_and_python_restatements_agree(seed):
             want = py.sample(logits, hist)
             got = orc.sample(cfg, st, logits, hist)
             assert got == want, (c, step)
-            assert st.rng == py.rng and np.float32(st.mu) == py.mu
-            assert np.float32(st.ap_weighted) == py.apw and np.float32(st.ap_total) == py.apt
+            assert st.rng == py.rng
+            for a, b in ((st.mu, py.mu), (st.ap_weighted, py.apw), (st.ap_total, py.apt)):
+                assert np.float32(a).view(np.uint32) == np.float32(b).view(np.uint32)
             hist = hist + [got]
 
 
