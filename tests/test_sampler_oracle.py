@@ -482,3 +482,35 @@ def test_sampler_structs_agree_with_the_header():
         assert [f[0] for f in prod._fields_] == names
         assert [f[0] for f in orac._fields_] == names
         assert C.sizeof(prod) == C.sizeof(orac)
+
+
+def test_product_sampler_defaults_and_init_match_the_oracle():
+    """bt_sampler_config_default / _llamacpp and bt_sampler_init are host code in the product
+    library: the same fields and the same initial state as the oracle's Sampler::new."""
+    from bigtea_b200 import _lib
+
+    for base in ("default", "llamacpp"):
+        p = _lib.SamplerConfig()
+        (_lib.lib.bt_sampler_config_llamacpp if base == "llamacpp" else _lib.lib.bt_sampler_config_default)(C.byref(p))
+        o, _ = orc.sampler_config(base)
+        for name, _t in _lib.SamplerConfig._fields_:
+            a, b = getattr(p, name), getattr(o, name)
+            if isinstance(a, (int, float)):
+                assert np.float32(a).tobytes() == np.float32(b).tobytes() if isinstance(a, float) else a == b, name
+            else:
+                assert not a and not b, name  # the list pointers: NULL
+    rng = np.random.default_rng(4)
+    for _ in range(200):
+        kw = dict(seed=int(rng.integers(0, 2**64, dtype=np.uint64)), mirostat_tau=float(rng.uniform(0, 10)),
+                  adaptive_p=float(rng.choice([-1.0, 0.0, 0.3, 1.5, np.nan])),
+                  adaptive_decay=float(rng.choice([0.0, 0.5, 0.95, 0.999, 2.0, -1.0])))
+        o, _ = orc.sampler_config(**kw)
+        p = _lib.SamplerConfig()
+        _lib.lib.bt_sampler_config_default(C.byref(p))
+        for k, v in kw.items():
+            setattr(p, k, v)
+        ps, os_ = _lib.SamplerState(), orc.sampler_state(o)
+        assert _lib.lib.bt_sampler_init(C.byref(p), C.byref(ps)) == 0
+        assert ps.rng == os_.rng
+        for f in ("mu", "ap_weighted", "ap_total"):
+            assert np.float32(getattr(ps, f)).tobytes() == np.float32(getattr(os_, f)).tobytes(), (kw, f)
