@@ -2808,6 +2808,8 @@ extern "C" int bt_sample(bt_engine *e, const bt_sampler_config *cfg, bt_sampler_
                cfg->presence_penalty == 0.0f && cfg->n_bias == 0 && !cfg->ignore_eos && cfg->mirostat == 0 &&
                cfg->dry_multiplier == 0.0f && cfg->adaptive_p < 0.0f && cfg->n_suppress == 0;
     const int V = (int)e->d.n_vocab;
+    if ((uint64_t)n_seqs * (uint64_t)V > (uint64_t)INT32_MAX)
+        return fail(BT_ERR_INVALID, "n_seqs * n_vocab must fit the sort's 31-bit item count");
     // the lists, the histories and the states go up in one copy
     std::vector<uint32_t> off(n_seqs + 1, 0);
     for (uint32_t i = 0; i < n_seqs; i++) off[i + 1] = off[i] + (history_len ? history_len[i] : 0);

@@ -325,15 +325,37 @@ _SAMPLER_LISTS = {"chain": (C.c_int32, np.int32, "n_chain"), "bias_ids": (C.c_ui
                   "bias_values": (C.c_float, np.float32, None), "suppress_ids": (C.c_uint32, np.uint32, "n_suppress"),
                   "dry_breakers": (C.c_uint32, np.uint32, "n_dry_breakers")}
 STAGES = {"top_k": 0, "typical_p": 1, "top_p": 2, "min_p": 3, "xtc": 4, "temperature": 5}
+DEFAULT_CHAIN = [0, 1, 2, 3, 4, 5]  # SamplerStage::default_chain (sample.rs:70-79)
+_STAGE_SPELLINGS = {"top_k": 0, "topk": 0, "typ_p": 1, "typical": 1, "typical_p": 1, "typ": 1, "top_p": 2, "topp": 2,
+                    "min_p": 3, "minp": 3, "xtc": 4, "temperature": 5, "temp": 5}
+
+
+def parse_stage(name: str):
+    """SamplerStage::parse (sample.rs:56-67): llama.cpp's spellings, trimmed, any case; None for
+    anything else, so that a caller can refuse the whole chain."""
+    return _STAGE_SPELLINGS.get(name.strip().lower())
+
+
+def parse_chain(names: str):
+    """a `--samplers`-style list separated by ';' or ','; ValueError on an unknown stage"""
+    out = []
+    for part in names.replace(",", ";").split(";"):
+        if not part.strip():
+            continue
+        st = parse_stage(part)
+        if st is None:
+            raise ValueError(f"unknown sampler stage {part.strip()!r}")
+        out.append(st)
+    return out
 
 
 class Sampler:
     """Sampler (core/arch/src/sample.rs:306-680) for a batch of sequences, on the device.
 
     `config` fields are SamplerConfig's (`base="llamacpp"` starts from llamacpp_defaults());
-    `chain` takes stage numbers or llama.cpp's names (SamplerStage::parse spellings of the common
-    forms). One state per sequence, advanced as the reference's Sampler is; `sample` returns one
-    token per sequence."""
+    `chain` takes stage numbers, llama.cpp's names (SamplerStage::parse) or one string of them
+    separated by ';'. One state per sequence, advanced as the reference's Sampler is; `sample`
+    returns one token per sequence. Construction is host work; `sample` runs on the device."""
 
     def __init__(self, engine: Engine, n_seqs: int = 1, base: str = "default", **config):
         self.engine = engine
@@ -346,7 +368,12 @@ class Sampler:
                     continue
                 ct, nt, count = _SAMPLER_LISTS[k]
                 if k == "chain":
-                    v = [STAGES[x] if isinstance(x, str) else int(x) for x in v]
+                    if isinstance(v, str):
+                        v = parse_chain(v)
+                    else:
+                        v = [x if not isinstance(x, str) else parse_stage(x) for x in v]
+                        if any(x is None for x in v):
+                            raise ValueError("unknown sampler stage in the chain")
                 a = np.ascontiguousarray(np.asarray(v, dtype=nt))
                 if a.size == 0:
                     a = np.zeros(1, nt)[:0]

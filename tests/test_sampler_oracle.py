@@ -514,3 +514,22 @@ def test_product_sampler_defaults_and_init_match_the_oracle():
         assert ps.rng == os_.rng
         for f in ("mu", "ap_weighted", "ap_total"):
             assert np.float32(getattr(ps, f)).tobytes() == np.float32(getattr(os_, f)).tobytes(), (kw, f)
+
+
+def test_stage_names_and_the_default_chain():
+    """sample.rs:1193-1220 (the_default_chain_is_llamacpp_s_order, stage_names_match_llamacpp_s_spelling)
+    on the product's host side, and a chain given by name reaching the C struct"""
+    from bigtea_b200 import runner
+
+    assert runner.DEFAULT_CHAIN == [runner.STAGES[n] for n in ("top_k", "typical_p", "top_p", "min_p", "xtc",
+                                                               "temperature")]
+    assert runner.parse_stage("top_k") == 0 and runner.parse_stage("typ_p") == 1 and runner.parse_stage("min_p") == 3
+    assert runner.parse_stage(" TEMPERATURE ") == 5
+    assert runner.parse_stage("top_q") is None
+    assert runner.parse_chain("temp;top_p") == [5, 2]
+    with pytest.raises(ValueError):
+        runner.parse_chain("top_k;top_q")
+    s = runner.Sampler(None, 2, temperature=1.0, chain="top_p;temperature", seed=9)
+    assert s.cfg.n_chain == 2 and [s.cfg.chain[i] for i in range(2)] == [2, 5]
+    o, _ = orc.sampler_config(temperature=1.0, seed=9)
+    assert all(st.rng == orc.sampler_state(o).rng for st in s.states)
