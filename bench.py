@@ -413,6 +413,26 @@ def run_ours(args, rank, world, local_rank):
     peak, peak_kind = peaks()
     per_step_launches = 1 if persistent else 1 + cfg.n_layer * 7 + 1 + 1
 
+    # the device sampler (bt_sample) on the logits the last step left in HBM: one sequence,
+    # llama.cpp's default chain over the whole vocabulary; host wall time per call
+    sampler_leg = None
+    if rank == 0 and world == 1:
+        try:
+            smp = bt.Sampler(engine, 1, base="llamacpp", seed=args.seed)
+            hist = [list(range(64))]
+            for _ in range(3):
+                smp.sample(None, hist)
+            n_draws = 50
+            t_s = time.perf_counter()
+            for _ in range(n_draws):
+                smp.sample(None, hist)
+            sampler_leg = {"ms_per_draw": round((time.perf_counter() - t_s) / n_draws * 1e3, 4),
+                           "what": "bt_sample wall time per call: 1 sequence, llama.cpp defaults (top_k 40, top_p "
+                                   "0.95, min_p 0.05, temperature 0.8, repeat penalty 1.1 over 64 tokens), "
+                                   f"{cfg.n_vocab} logits already in HBM, 3 launches (prepare, radix sort, chain)"}
+        except Exception as ex:  # a refusal is reported, never fatal to the bench line
+            sampler_leg = {"error": str(ex)[:300]}
+
     result = None
     xcache = None
     if rank == 0:
@@ -468,6 +488,7 @@ def run_ours(args, rank, world, local_rank):
             "expert_gemv": expert_gemv,
             "batched": batched,
             "expert_cache": None,
+            "sampler": sampler_leg,
             "clocks": clk.summary(),
             "cpu_baseline": cpu,
         }
