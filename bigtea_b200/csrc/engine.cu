@@ -2810,9 +2810,21 @@ extern "C" int bt_sample(bt_engine *e, const bt_sampler_config *cfg, bt_sampler_
     const int V = (int)e->d.n_vocab;
     if ((uint64_t)n_seqs * (uint64_t)V > (uint64_t)INT32_MAX)
         return fail(BT_ERR_INVALID, "n_seqs * n_vocab must fit the sort's 31-bit item count");
+    // The kernels count in int. Larger values mean the same as these bounds: a top_k at or
+    // above the vocabulary keeps every candidate, a window longer than any history is the
+    // whole history, and no repeat reaches an allowed length of 2^31 - 1.
+    auto clamp31 = [](uint32_t x) { return x > (uint32_t)INT32_MAX ? (uint32_t)INT32_MAX : x; };
+    P.top_k = P.top_k > (uint32_t)V ? (uint32_t)V : P.top_k;
+    P.repeat_last_n = clamp31(P.repeat_last_n);
+    P.dry_allowed_length = clamp31(P.dry_allowed_length);
+    P.dry_penalty_last_n = clamp31(P.dry_penalty_last_n);
     // the lists, the histories and the states go up in one copy
     std::vector<uint32_t> off(n_seqs + 1, 0);
-    for (uint32_t i = 0; i < n_seqs; i++) off[i + 1] = off[i] + (history_len ? history_len[i] : 0);
+    for (uint32_t i = 0; i < n_seqs; i++) {
+        const uint64_t next = (uint64_t)off[i] + (history_len ? history_len[i] : 0);
+        if (next > (uint64_t)INT32_MAX) return fail(BT_ERR_INVALID, "the histories hold more than 2^31 - 1 tokens");
+        off[i + 1] = (uint32_t)next;
+    }
     if (off[n_seqs] && !history) return fail(BT_ERR_INVALID, "history lengths without a history");
     size_t at = 0;
     auto slot = [&](size_t bytes) {
