@@ -533,3 +533,20 @@ def test_stage_names_and_the_default_chain():
     assert s.cfg.n_chain == 2 and [s.cfg.chain[i] for i in range(2)] == [2, 5]
     o, _ = orc.sampler_config(temperature=1.0, seed=9)
     assert all(st.rng == orc.sampler_state(o).rng for st in s.states)
+
+
+def test_oracle_reproduces_the_sampler_golden_vectors():
+    """tests/golden/sampler_golden.npz (made by gen_sampler_golden.py): every token and state"""
+    import json
+
+    g = np.load(os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "sampler_golden.npz"))
+    for c, (base, kw) in enumerate(json.loads(str(g["configs"]))):
+        cfg, _keep = orc.sampler_config(base, **kw)
+        st = orc.sampler_state(cfg)
+        hist = [int(x) for x in g["history0"]]
+        for s in range(g["tokens"].shape[1]):
+            t = orc.sample(cfg, st, g["logits"][s], hist)
+            assert t == int(g["tokens"][c, s]), (base, kw, s)
+            got = [st.rng] + [int(np.float32(getattr(st, f)).view(np.uint32)) for f in ("mu", "ap_weighted", "ap_total")]
+            assert got == [int(x) for x in g["states"][c, s]], (base, kw, s)
+            hist.append(t)
